@@ -1,0 +1,194 @@
+/*
+ * tabinfer_b200.h -- C ABI of the B200 backend for TabInfer's quantized-GEMV
+ * hot path (int4 G=32 decode GEMV / prefill GEMM, int8-KV split-KV decode
+ * attention, ternary Q2_0_g64 GEMV).
+ *
+ * Conventions
+ *   - every pointer argument named as a tensor is a DEVICE pointer to a
+ *     caller-owned buffer (cudaMalloc / torch / cuMemAlloc), dense row-major;
+ *   - every call is enqueued on the context's stream and returns without
+ *     synchronising; results are valid once that stream reaches the call;
+ *   - the return value is a status (TB_OK = 0); on error, tb_last_error(ctx)
+ *     holds a message and nothing was enqueued;
+ *   - one context per host thread; a context is bound to one CUDA device.
+ * The reference interface each entry point replaces is cited beside it
+ * (paths inside the TabInfer checkout).
+ */
+#ifndef TABINFER_B200_H
+#define TABINFER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TB_API __attribute__((visibility("default")))
+
+enum {
+    TB_OK = 0,
+    TB_ERR_INVALID = 1,     /* bad shape, alignment or argument (reference: JS throw / Rust assert) */
+    TB_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+    TB_ERR_UNSUPPORTED = 3, /* valid request this build does not implement */
+    TB_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up (see tb_ctx_device_error) */
+    TB_ERR_NOMEM = 5
+};
+
+/* Numerics mode of the int4 GEMV, the two decode routes of linearQ
+ * (models/qwen3.js:1597-1602). */
+enum {
+    TB_ACT_F32 = 0,  /* gemvQ: f32 activations, f32 dequant math (qwen3.js:276-321) */
+    TB_ACT_Q8 = 1    /* gemvDP4A: per-32 int8 activations, int32 dot (qwen3.js:332-400) */
+};
+
+typedef struct tb_ctx tb_ctx;
+
+/* ---- context --------------------------------------------------------------
+ * Replaces the engine object of engine/webgpu-engine.js:72 (init) and the
+ * module-level scratch of models/qwen3.js (ensureDp4 :402, ensureDecSplit :2339). */
+TB_API int tb_version(void);
+TB_API int tb_ctx_create(int device, tb_ctx **out);
+TB_API int tb_ctx_destroy(tb_ctx *ctx);
+/* Order all later calls on this stream (a cudaStream_t); NULL = the context's own. */
+TB_API int tb_ctx_set_stream(tb_ctx *ctx, void *cuda_stream);
+TB_API void *tb_ctx_get_stream(tb_ctx *ctx);
+/* 1 = launch kernels with programmatic dependent launch (default), 0 = plain. */
+TB_API int tb_ctx_set_pdl(tb_ctx *ctx, int enable);
+TB_API const char *tb_last_error(tb_ctx *ctx);
+TB_API int tb_ctx_synchronize(tb_ctx *ctx);
+/* Synchronise and read (and clear) the device error word that bounded waits set. */
+TB_API int tb_ctx_device_error(tb_ctx *ctx, int *code);
+
+/* ---- int4 G=32 weight path ------------------------------------------------ */
+
+/* Quant-on-arrival: bf16 [N,K] -> pack u32 [N,K/8] (k=8w+i at bits 4i, nibble
+ * q+8), scales f16 bits [N,K/32].  Bit-exact with quantizeInt4Bf16,
+ * models/qwen3.js:3405-3426 (JS double math, f32ToF16 :3357-3374).  K%32==0. */
+TB_API int tb_quant_int4_g32(tb_ctx *ctx, const uint16_t *w_bf16, uint32_t *pack,
+                             uint16_t *scales, int64_t N, int64_t K);
+
+/* Per-32 int8 activation quantization of T rows: xq int8 [T,K], xs f32
+ * [T,K/32], xsum16 i32 [T,K/16] (may be NULL).  QUANTQ8 qwen3.js:332-358 and
+ * QUANTQ8T qwen3.js:1210-1231 (quantQ8 :414-420). */
+TB_API int tb_quant_q8(tb_ctx *ctx, const float *x, int8_t *xq, float *xs, int32_t *xsum16,
+                       int64_t T, int64_t K);
+
+/* Fused RMSNorm -> per-32 int8: rmsnormQ, models/qwen3.js:569-621.  w16 = f16
+ * norm weight [H].  Outputs as tb_quant_q8.  H%32==0. */
+TB_API int tb_rmsnorm_q8(tb_ctx *ctx, const float *x, const uint16_t *w16, float eps,
+                         int8_t *xq, float *xs, int32_t *xsum16, int64_t T, int64_t H);
+
+/* int8-activation int4 GEMV for `batch` activation rows (1..8):
+ * y[b,n] (+)= sum_g f32(s16[n,g])*xs[b,g] * sum_{k in g} (nib-8)*xq[b,k].
+ * gemvDP4_only, models/qwen3.js:422-427 (GEMVDP4 :359-400).  acc=1 adds to y
+ * (the fused residual).  K%32==0. */
+TB_API int tb_gemv_int4_q8(tb_ctx *ctx, float *y, const int8_t *xq, const float *xs,
+                           const uint32_t *pack, const uint16_t *scales,
+                           int64_t N, int64_t K, int batch, int acc);
+
+/* f32-activation int4 GEMV: y[b,n] (+)= sum_k x[b,k]*(nib-8)*f32(s16).
+ * gemvQ, models/qwen3.js:314-321 (GEMVQ :276-311).  batch 1..8. */
+TB_API int tb_gemv_int4_f32(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
+                            const uint16_t *scales, int64_t N, int64_t K, int batch, int acc);
+
+/* The linearQ router for one int4 matrix, models/qwen3.js:1588-1608:
+ * T==1 and N<16384 -> quantQ8 + gemvDP4; T==1 and N>=16384 -> gemvQ;
+ * 1<T<=8 -> per-token int8 (QUANTQ8T) x int4 math of gemmDP4A (:1397-1407);
+ * T>8 -> TB_ERR_UNSUPPORTED until the prefill GEMM entry point is used.
+ * Uses context-owned scratch for the quantized activation. */
+TB_API int tb_linear_int4(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
+                          const uint16_t *scales, int64_t T, int64_t N, int64_t K, int acc);
+
+/* Fused gate+up+SiLU on int8 activations: swi[b,i] = silu(g)*u,
+ * gateUpSiluDP4_only, models/qwen3.js:861-877 (gateupDP4Wgsl :679-728).
+ * gate/up are int4 [I,H]; batch 1..8. */
+TB_API int tb_gateup_silu_int4_q8(tb_ctx *ctx, float *swi, const int8_t *xq, const float *xs,
+                                  const uint32_t *gpack, const uint16_t *gscales,
+                                  const uint32_t *upack, const uint16_t *uscales,
+                                  int64_t I, int64_t H, int batch);
+
+/* Several int4 matrices that read the SAME int8 activation, in one launch
+ * (the q/k/v projGemv triple of forward(), models/qwen3.js:3981-3984).
+ * ys/packs/scales/Ns are arrays of `count` (<= 4) entries. */
+TB_API int tb_gemv_int4_q8_multi(tb_ctx *ctx, int count, float *const *ys,
+                                 const uint32_t *const *packs, const uint16_t *const *scales,
+                                 const int64_t *Ns, const int8_t *xq, const float *xs,
+                                 int64_t K, int batch, int acc);
+
+/* ---- ternary Q2_0_g64 path (native/crates/n2-kernels) -------------------- */
+
+/* f32 ternary [N,K] -> codes u8 [N,K/4] + f32 scales [N,K/64], bit-exact with
+ * pack_ternary, native/crates/n2-kernels/src/tern.rs:131-160 and
+ * native/tools/pack_bin.py:19-29.  K%64==0. */
+TB_API int tb_pack_tern_q2g64(tb_ctx *ctx, const float *w, uint8_t *codes, float *scales,
+                              int64_t N, int64_t K);
+
+/* Per-vector activation quantization of T rows: act i8 [T,K], xsum i32
+ * [T,K/64], scale f32 [T] (=127/amax, 1 when amax==0).  quantize_act_into,
+ * tern.rs:206-222.  K%64==0. */
+TB_API int tb_quant_act_q8(tb_ctx *ctx, const float *x, int8_t *act, int32_t *xsum,
+                           float *scale, int64_t T, int64_t K);
+
+/* Ternary GEMV for `batch` activation rows (1..8): out[b,n] =
+ * sum_blk s*dot - sum_blk s*xsum, accumulated in block order exactly as
+ * gemv_tern_scalar, tern.rs:79-119 (bit-exact).  Replaces tern::gemv_tern
+ * (tern.rs:56-71), the WASM export gemv_tern (cpu/kernel/src/lib.rs:436-441)
+ * and gemm_tern_b4 (lib.rs:331). */
+TB_API int tb_gemv_tern_q2g64(tb_ctx *ctx, float *out, const uint8_t *codes, const float *scales,
+                              const int8_t *act, const int32_t *xsum, int64_t N, int64_t K, int batch);
+
+/* Model::linear, native/crates/n2-core/src/model.rs:316-339: quantize_act ->
+ * gemv_tern -> out *= 1/scale, for T (1..8) rows.  Context-owned scratch. */
+TB_API int tb_linear_tern(tb_ctx *ctx, float *y, const float *x, const uint8_t *codes,
+                          const float *scales, int64_t T, int64_t N, int64_t K);
+
+/* ---- int8 KV cache + split-KV GQA decode attention ----------------------- */
+
+/* Fused decode attention prep at position `pos` (T=1):
+ * q heads: per-head RMSNorm(qw16) + RoPE -> qr f32 [nHq*hd];
+ * k heads: RMSNorm(kw16) + RoPE -> snorm int8 per-32 into Kq/Ks at row pos;
+ * v heads: raw -> snorm int8 per-32 into Vq/Vs at row pos.
+ * attnPrepQ8, models/qwen3.js:2297-2308 (attnPrepWgsl :2228-2296).
+ * KV layout: Kq/Vq int8 [S_max][nKv*hd], Ks/Vs f32 [S_max][nKv*hd/32].
+ * hd%32==0, hd<=256. */
+TB_API int tb_attn_prep_q8(tb_ctx *ctx, const float *q, const float *k, const float *v,
+                           const uint16_t *qw16, const uint16_t *kw16, float *qr,
+                           int8_t *Kq, float *Ks, int8_t *Vq, float *Vs,
+                           int64_t nHq, int64_t nKv, int64_t hd, int64_t pos,
+                           float theta, float eps);
+
+/* K/V-only quantize-write of T rows at posBase (prefill): KVQW,
+ * models/qwen3.js:2180-2216.  kr/v f32 [T][nKv*hd]. */
+TB_API int tb_kv_quant_write(tb_ctx *ctx, const float *kr, const float *v,
+                             int8_t *Kq, float *Ks, int8_t *Vq, float *Vs,
+                             int64_t T, int64_t nKv, int64_t hd, int64_t posBase);
+
+/* Split-KV streaming decode attention over S cached positions:
+ * attnDecodeStreamQ8 + combine, models/qwen3.js:2165-2173 (kernels :2077-2164,
+ * :2048-2069).  nsplit = 0 picks the reference rule _decNsplit (:2354) scaled
+ * to fill the GPU.  out f32 [nHq*hd].  Context-owned scratch for partials. */
+TB_API int tb_attn_decode_q8(tb_ctx *ctx, float *out, const float *qr,
+                             const int8_t *Kq, const float *Ks, const int8_t *Vq, const float *Vs,
+                             int64_t S, int64_t nHq, int64_t nKv, int64_t hd, int nsplit);
+
+/* ---- decode-step glue ------------------------------------------------------ */
+
+/* Argmax over `rows` rows of n logits -> out_idx[row*stride + offset]
+ * (u32).  argmaxKernel, models/qwen3.js:2681-2690 (one and two-stage).
+ * Lowest index wins on ties. */
+TB_API int tb_argmax(tb_ctx *ctx, const float *x, int64_t n, int64_t rows, uint32_t *out_idx,
+                     int64_t out_offset);
+
+/* y[T,H] = x * rsqrt(mean(x^2)+eps) * f16 w.  rmsnorm, qwen3.js:81-88. */
+TB_API int tb_rmsnorm(tb_ctx *ctx, const float *x, const uint16_t *w16, float *y,
+                      int64_t T, int64_t H, float eps);
+
+/* y[t,:] = f32(embed_f16[ids[idoff+t], :]).  embedGather, qwen3.js:1663-1675. */
+TB_API int tb_embed_gather(tb_ctx *ctx, const uint32_t *ids, int64_t idoff,
+                           const uint16_t *embed_f16, float *y, int64_t T, int64_t H);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TABINFER_B200_H */

@@ -1,0 +1,494 @@
+/*
+ * tb_oracle.c -- CPU restatement of TabInfer's quantized-GEMV hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * product in tabinfer_b200/csrc.  Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / reference legs of bench.py may load it; the product never
+ * calls it and has no CPU fallback.
+ *
+ * Every function restates the reference algorithm in plain C and cites the
+ * reference file:line it follows (paths relative to the TabInfer checkout).
+ * Floating-point semantics follow the reference's own language:
+ *   - the int4 quantizer runs in JavaScript doubles (models/qwen3.js), with
+ *     Float32Array stores and the hand-written f32->f16 rounding;
+ *   - the WGSL kernels compute in f32 (WGSL round() = round-half-to-even,
+ *     pack4x8snorm = floor(0.5 + 127*clamp(v,-1,1)));
+ *   - the ternary kernels follow Rust f32 (no FMA contraction, f32::round =
+ *     half away from zero) in native/crates/n2-kernels/src/tern.rs.
+ * Floating outputs whose reference order is a parallel tree are returned as
+ * f64 "exact-ish" sums; the tests compare those within stated tolerances.
+ *
+ * Parity pins: tests/test_oracle.py checks these functions against the
+ * reference's own golden data (numpy pack_ternary from native/tools/pack_bin.py,
+ * the tern.rs known-answer tests, and the qwen3.js self-test fixtures).
+ *
+ * Built by oracle/build.py with gcc -O2 (no -ffast-math, -ffp-contract=off).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define TBO_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------------ */
+/* f16 / bf16 helpers                                                        */
+/* ------------------------------------------------------------------------ */
+
+static inline uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bits_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* f32 -> f16 bits exactly as models/qwen3.js:3357-3374 (f32ToF16): the value is
+ * first stored to a Float32Array (double->f32 round-to-nearest-even), then the
+ * mantissa is truncated and incremented when the first dropped bit is set
+ * (round-half-up on magnitude, not round-to-even). */
+TBO_API uint16_t tbo_f32_to_f16_js(float val)
+{
+    uint32_t x = f32_bits(val);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t ex = (x >> 23) & 0xffu;
+    uint32_t mant = x & 0x7fffffu;
+    if (ex == 0xffu) return (uint16_t)(sign | (mant ? 0x7e00u : 0x7c00u));
+    int e = (int)ex - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        uint32_t m = mant | 0x800000u;
+        int shift = 14 - e;
+        uint32_t half = m >> shift;
+        if ((m >> (shift - 1)) & 1u) half += 1;
+        return (uint16_t)(sign | half);
+    }
+    uint32_t half = ((uint32_t)e << 10) | (mant >> 13);
+    if ((mant >> 12) & 1u) half += 1;
+    return (uint16_t)(sign | half);
+}
+
+/* f16 bits -> exact value, models/qwen3.js:3397-3400 (f16ToF32scalar, JS double). */
+TBO_API double tbo_f16_to_f64(uint16_t h)
+{
+    int s = (h >> 15) & 1, e = (h >> 10) & 0x1f, f = h & 0x3ff;
+    double sg = s ? -1.0 : 1.0;
+    if (e == 0) return sg * ldexp((double)f, -24);
+    if (e == 31) return f ? NAN : sg * INFINITY;
+    return sg * ldexp(1.0 + f / 1024.0, e - 15);
+}
+
+static inline double bf16_to_f64(uint16_t u) { return (double)bits_f32((uint32_t)u << 16); }
+
+/* JavaScript Math.round: nearest integer, ties toward +infinity; NaN/Inf pass. */
+static inline double js_round(double x)
+{
+    if (isnan(x) || isinf(x)) return x;
+    double f = floor(x);
+    return (x - f) >= 0.5 ? f + 1.0 : f;
+}
+
+/* ------------------------------------------------------------------------ */
+/* int4 G=32 quantizer -- models/qwen3.js:3405-3426 (quantizeInt4Bf16)       */
+/* ------------------------------------------------------------------------ */
+
+/* in: bf16 bits [N,K] row-major.  out: pack u32 [N,K/8] (k=8w+i at bits 4i,
+ * nibble = q+8), scales f16 bits [N,K/32].  K % 32 == 0. */
+TBO_API void tbo_quant_int4_g32(const uint16_t *w, int64_t N, int64_t K,
+                                uint32_t *pack, uint16_t *scales)
+{
+    const int64_t G = 32, wpr = K / 8, gpr = K / G;
+    memset(pack, 0, (size_t)(N * wpr) * sizeof(uint32_t));
+    for (int64_t n = 0; n < N; n++) {
+        for (int64_t g = 0; g < gpr; g++) {
+            const uint16_t *src = w + n * K + g * G;
+            double maxabs = 0.0;
+            for (int j = 0; j < G; j++) {
+                double v = fabs(bf16_to_f64(src[j]));
+                if (v > maxabs) maxabs = v;              /* NaN never wins */
+            }
+            double scale = maxabs > 0 ? maxabs / 7.0 : 1e-8;
+            uint16_t sb = tbo_f32_to_f16_js((float)scale);
+            scales[n * gpr + g] = sb;
+            double inv = 1.0 / tbo_f16_to_f64(sb);      /* 1/0 -> +Inf, as JS */
+            for (int j = 0; j < G; j++) {
+                int64_t k = g * G + j;
+                double q = js_round(bf16_to_f64(src[j]) * inv);
+                if (q < -8) q = -8; else if (q > 7) q = 7;
+                /* (NaN + 8) & 0xF == 0 in JS (ToInt32(NaN) = 0) */
+                uint32_t nib = isnan(q) ? 0u : ((uint32_t)((int)q + 8) & 0xFu);
+                pack[n * wpr + (k >> 3)] |= nib << (4 * (k & 7));
+            }
+        }
+    }
+}
+
+/* Dequantize as the self-test oracle does, models/qwen3.js:3073-3074
+ * (w = (nib-8)*f16ToF32(scale), stored to a Float32Array). */
+TBO_API void tbo_dequant_int4_g32(const uint32_t *pack, const uint16_t *scales,
+                                  int64_t N, int64_t K, float *w)
+{
+    const int64_t wpr = K / 8, gpr = K / 32;
+    for (int64_t n = 0; n < N; n++)
+        for (int64_t k = 0; k < K; k++) {
+            uint32_t word = pack[n * wpr + (k >> 3)];
+            int nib = (int)((word >> (4 * (k & 7))) & 0xFu);
+            w[n * K + k] = (float)((nib - 8) * tbo_f16_to_f64(scales[n * gpr + k / 32]));
+        }
+}
+
+/* f32-activation int4 GEMV oracle: y[b,n] = sum_k x[b,k]*Wdq[n,k], accumulated
+ * in double exactly as the JS self-test reference loop (qwen3.js:3089), which
+ * is the math of gemvQ (qwen3.js:276-321) without its f32 reduction order. */
+TBO_API void tbo_gemv_int4_f32act(const float *x, const uint32_t *pack,
+                                  const uint16_t *scales, int64_t N, int64_t K,
+                                  int64_t batch, double *y)
+{
+    const int64_t wpr = K / 8, gpr = K / 32;
+    for (int64_t n = 0; n < N; n++) {
+        for (int64_t b = 0; b < batch; b++) {
+            double a = 0.0;
+            for (int64_t g = 0; g < gpr; g++) {
+                double s = tbo_f16_to_f64(scales[n * gpr + g]);
+                for (int j = 0; j < 32; j++) {
+                    int64_t k = g * 32 + j;
+                    int nib = (int)((pack[n * wpr + (k >> 3)] >> (4 * (k & 7))) & 0xFu);
+                    float wv = (float)((nib - 8) * s);
+                    a += (double)x[b * K + k] * (double)wv;
+                }
+            }
+            y[b * N + n] = a;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* int8 per-32 activation quantizer -- QUANTQ8 qwen3.js:332-358 (one row),    */
+/* QUANTQ8T qwen3.js:1210-1231 (T rows).  WGSL f32 semantics.                */
+/* ------------------------------------------------------------------------ */
+
+/* x [T,K] f32 -> xq int8 [T,K] (natural k order; the reference packs 4 per
+ * u32 little-endian, which is the same bytes), xs f32 [T,K/32] = maxabs/127,
+ * xsum i32 [T,K/16] (per-16 sums, QUANTQ8 only; may be NULL). */
+TBO_API void tbo_quant_q8(const float *x, int64_t T, int64_t K,
+                          int8_t *xq, float *xs, int32_t *xsum)
+{
+    const int64_t gpr = K / 32;
+    for (int64_t t = 0; t < T; t++)
+        for (int64_t g = 0; g < gpr; g++) {
+            const float *src = x + t * K + g * 32;
+            float m = 0.0f;
+            for (int j = 0; j < 32; j++) m = fmaxf(m, fabsf(src[j]));
+            float scale = m / 127.0f;
+            float inv = scale > 0.0f ? 1.0f / scale : 0.0f;
+            xs[t * gpr + g] = scale;
+            int q[32];
+            for (int j = 0; j < 32; j++) {
+                float r = rintf(src[j] * inv);           /* WGSL round: half to even */
+                int v = (int)r;
+                q[j] = v < -127 ? -127 : (v > 127 ? 127 : v);
+                xq[t * K + g * 32 + j] = (int8_t)q[j];
+            }
+            if (xsum) {
+                int s0 = 0, s1 = 0;
+                for (int j = 0; j < 16; j++) { s0 += q[j]; s1 += q[16 + j]; }
+                xsum[t * (K / 16) + 2 * g] = s0;
+                xsum[t * (K / 16) + 2 * g + 1] = s1;
+            }
+        }
+}
+
+/* Fused RMSNorm -> int8, RMSNORMQ qwen3.js:569-612 (one row per batch entry).
+ * inv = 1/sqrt(mean(x^2)+eps) (sum of squares taken in double here; the WGSL
+ * tree order differs by <1 ulp), then normalized = (x*inv)*w and the group
+ * quantization of QUANTQ8.  Also returns inv per row for diagnostics. */
+TBO_API void tbo_rmsnorm_q8(const float *x, const uint16_t *w16, int64_t T,
+                            int64_t H, float eps, int8_t *xq, float *xs,
+                            int32_t *xsum, float *inv_out)
+{
+    const int64_t ng = H / 32;
+    for (int64_t t = 0; t < T; t++) {
+        const float *xr = x + t * H;
+        double ss = 0.0;
+        for (int64_t i = 0; i < H; i++) ss += (double)xr[i] * (double)xr[i];
+        float inv = 1.0f / sqrtf((float)ss / (float)H + eps);
+        if (inv_out) inv_out[t] = inv;
+        for (int64_t g = 0; g < ng; g++) {
+            float mx = 0.0f;
+            for (int j = 0; j < 32; j++) {
+                int64_t i = g * 32 + j;
+                float v = (xr[i] * inv) * (float)tbo_f16_to_f64(w16[i]);
+                mx = fmaxf(mx, fabsf(v));
+            }
+            float scale = mx / 127.0f;
+            float invs = scale > 0.0f ? 1.0f / scale : 0.0f;
+            xs[t * ng + g] = scale;
+            int s0 = 0, s1 = 0;
+            for (int j = 0; j < 32; j++) {
+                int64_t i = g * 32 + j;
+                float v = ((xr[i] * inv) * (float)tbo_f16_to_f64(w16[i])) * invs;
+                int q = (int)rintf(v);
+                q = q < -127 ? -127 : (q > 127 ? 127 : q);
+                xq[t * H + i] = (int8_t)q;
+                if (j < 16) s0 += q; else s1 += q;
+            }
+            if (xsum) { xsum[t * (H / 16) + 2 * g] = s0; xsum[t * (H / 16) + 2 * g + 1] = s1; }
+        }
+    }
+}
+
+/* int8-activation int4 GEMV/GEMM math, GEMVDP4 qwen3.js:359-400 and
+ * gemmdp4Wgsl qwen3.js:1326-1388: per (row, 32-group) an exact int32 dot of
+ * (nib-8) with the int8 activation, scaled by f32(s16)*xs.  The per-group
+ * products are summed in double (the WGSL order is a workgroup tree). */
+TBO_API void tbo_gemv_int4_q8act(const int8_t *xq, const float *xs,
+                                 const uint32_t *pack, const uint16_t *scales,
+                                 int64_t N, int64_t K, int64_t batch, double *y)
+{
+    const int64_t wpr = K / 8, gpr = K / 32;
+    for (int64_t n = 0; n < N; n++)
+        for (int64_t b = 0; b < batch; b++) {
+            double a = 0.0;
+            for (int64_t g = 0; g < gpr; g++) {
+                int32_t dot = 0;
+                for (int j = 0; j < 32; j++) {
+                    int64_t k = g * 32 + j;
+                    int nib = (int)((pack[n * wpr + (k >> 3)] >> (4 * (k & 7))) & 0xFu);
+                    dot += (nib - 8) * (int32_t)xq[b * K + k];
+                }
+                float s = (float)tbo_f16_to_f64(scales[n * gpr + g]) * xs[b * gpr + g];
+                a += (double)s * (double)dot;
+            }
+            y[b * N + n] = a;
+        }
+}
+
+/* Fused gate+up+SiLU, gateupDP4Wgsl qwen3.js:679-728: swi = silu(g)*u with
+ * g,u from the int8-activation math above.  Returned in double. */
+TBO_API void tbo_gateup_q8act(const int8_t *xq, const float *xs,
+                              const uint32_t *gpack, const uint16_t *gscales,
+                              const uint32_t *upack, const uint16_t *uscales,
+                              int64_t I, int64_t H, int64_t batch, double *swi)
+{
+    double *g = (double *)malloc(sizeof(double) * (size_t)(I * batch));
+    double *u = (double *)malloc(sizeof(double) * (size_t)(I * batch));
+    tbo_gemv_int4_q8act(xq, xs, gpack, gscales, I, H, batch, g);
+    tbo_gemv_int4_q8act(xq, xs, upack, uscales, I, H, batch, u);
+    for (int64_t i = 0; i < I * batch; i++) swi[i] = g[i] / (1.0 + exp(-g[i])) * u[i];
+    free(g); free(u);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Ternary Q2_0_g64 -- native/crates/n2-kernels/src/tern.rs                  */
+/* ------------------------------------------------------------------------ */
+
+/* tern.rs:131-160 (pack_ternary) == native/tools/pack_bin.py:19-29.
+ * s = max|w| per 64; code 1 if |w| < 0.5s, else 0 (negative) / 2 (positive);
+ * code c of a group lives in byte c%16 at bit 2*(c/16). */
+TBO_API void tbo_pack_ternary(const float *w, int64_t N, int64_t K,
+                              uint8_t *codes, float *scales)
+{
+    const int64_t nb = K / 64;
+    memset(codes, 0, (size_t)(N * K / 4));
+    for (int64_t r = 0; r < N; r++)
+        for (int64_t b = 0; b < nb; b++) {
+            const float *g = w + r * K + b * 64;
+            float s = 0.0f;
+            for (int c = 0; c < 64; c++) { float a = fabsf(g[c]); s = a > s ? a : s; }
+            scales[r * nb + b] = s;
+            float thr = s * 0.5f;
+            for (int c = 0; c < 64; c++) {
+                uint8_t code = fabsf(g[c]) < thr ? 1 : (g[c] < 0.0f ? 0 : 2);
+                codes[r * (K / 4) + b * 16 + (c & 15)] |= (uint8_t)(code << (2 * (c >> 4)));
+            }
+        }
+}
+
+/* tern.rs:206-222 (quantize_act_into): per-vector scale = 127/amax (1.0 when
+ * amax == 0), act = round-half-away(x*scale) clamped to +-127, xsum per 64.
+ * Returns the scale.  Applied to each of T rows independently. */
+TBO_API void tbo_quantize_act(const float *x, int64_t T, int64_t K,
+                              int8_t *act, int32_t *xsum, float *scale_out)
+{
+    for (int64_t t = 0; t < T; t++) {
+        const float *xr = x + t * K;
+        float amax = 0.0f;
+        for (int64_t i = 0; i < K; i++) { float a = fabsf(xr[i]); amax = a > amax ? a : amax; }
+        float scale = amax > 0.0f ? 127.0f / amax : 1.0f;
+        for (int64_t i = 0; i < K; i++) {
+            float v = roundf(xr[i] * scale);
+            v = v < -127.0f ? -127.0f : (v > 127.0f ? 127.0f : v);
+            act[t * K + i] = (int8_t)v;
+        }
+        for (int64_t b = 0; b < K / 64; b++) {
+            int32_t s = 0;
+            for (int i = 0; i < 64; i++) s += act[t * K + b * 64 + i];
+            xsum[t * (K / 64) + b] = s;
+        }
+        scale_out[t] = scale;
+    }
+}
+
+/* tern.rs:79-119 (gemv_tern_scalar), the portable reference every backend is
+ * validated against: per row, acc += s*dot and sxs += s*xsum in block order
+ * (f32, separately rounded multiply and add), out = acc - sxs.
+ * Batched form = the same order per column (cpu/kernel/src/lib.rs:299-307). */
+TBO_API void tbo_gemv_tern_scalar(float *out, const uint8_t *codes, const float *scales,
+                                  const int8_t *act, const int32_t *xsum,
+                                  int64_t N, int64_t K, int64_t batch)
+{
+    const int64_t nb = K / 64;
+    for (int64_t t = 0; t < batch; t++) {
+        const int8_t *a = act + t * K;
+        const int32_t *xs = xsum + t * nb;
+        for (int64_t r = 0; r < N; r++) {
+            const uint8_t *rc = codes + r * (K / 4);
+            const float *rs = scales + r * nb;
+            float acc = 0.0f, sxs = 0.0f;   /* -ffp-contract=off keeps each op rounded */
+            for (int64_t b = 0; b < nb; b++) {
+                int32_t dot = 0;
+                for (int j = 0; j < 4; j++)
+                    for (int i = 0; i < 16; i++)
+                        dot += (int32_t)((rc[b * 16 + i] >> (2 * j)) & 3) * (int32_t)a[b * 64 + j * 16 + i];
+                float s = rs[b];
+                float p = s * (float)dot;
+                acc = acc + p;
+                float q = s * (float)xs[b];
+                sxs = sxs + q;
+            }
+            out[t * N + r] = acc - sxs;
+        }
+    }
+}
+
+/* tern.rs:166-189 (gemv_dequant_reference): the independent oracle,
+ * w = (code-1)*s in f32, product in f32, accumulated in f64. */
+TBO_API void tbo_gemv_tern_dequant(float *out, const uint8_t *codes, const float *scales,
+                                   const int8_t *act, int64_t N, int64_t K, int64_t batch)
+{
+    const int64_t nb = K / 64;
+    for (int64_t t = 0; t < batch; t++)
+        for (int64_t r = 0; r < N; r++) {
+            double acc = 0.0;
+            for (int64_t k = 0; k < K; k++) {
+                int64_t b = k / 64, c = k % 64;
+                uint8_t raw = codes[r * (K / 4) + b * 16 + (c % 16)];
+                int code = (raw >> (2 * (c / 16))) & 3;
+                float wv = (float)(code - 1) * scales[r * nb + b];
+                acc += (double)(wv * (float)act[t * K + k]);
+            }
+            out[t * N + r] = (float)acc;
+        }
+}
+
+/* ------------------------------------------------------------------------ */
+/* int8 KV cache and split-KV decode attention                               */
+/* ------------------------------------------------------------------------ */
+
+/* WGSL pack4x8snorm component: floor(0.5 + 127*clamp(v,-1,1)). */
+static inline int8_t snorm8(float v)
+{
+    float c = v < -1.0f ? -1.0f : (v > 1.0f ? 1.0f : v);
+    return (int8_t)floorf(0.5f + 127.0f * c);
+}
+
+/* KVQW qwen3.js:2180-2210 / attnPrep qwen3.js:2277-2295: per 32-element group,
+ * m = max(1e-12, max|x|), q = snorm8(x/m), scale = m.  x [n] with n % 32 == 0. */
+TBO_API void tbo_kv_quant_q8(const float *x, int64_t n, int8_t *q, float *scale)
+{
+    for (int64_t g = 0; g < n / 32; g++) {
+        float m = 1e-12f;
+        for (int j = 0; j < 32; j++) m = fmaxf(m, fabsf(x[g * 32 + j]));
+        for (int j = 0; j < 32; j++) q[g * 32 + j] = snorm8(x[g * 32 + j] / m);
+        scale[g] = m;
+    }
+}
+
+/* Per-head RMSNorm + RoPE split-half, attnPrepWgsl qwen3.js:2257-2275 and
+ * ROPEQK qwen3.js:1722-1761 (T=1 at position pos).  In place on x[nH*hd].
+ * Computed in double (the WGSL pow/cos/sin are not bit-specified). */
+TBO_API void tbo_head_norm_rope(double *x, const uint16_t *w16, int64_t nH, int64_t hd,
+                                int64_t pos, double theta, double eps)
+{
+    double *rk = (double *)malloc(sizeof(double) * (size_t)hd);
+    const int64_t half = hd / 2;
+    for (int64_t h = 0; h < nH; h++) {
+        double *v = x + h * hd;
+        double ss = 0.0;
+        for (int64_t j = 0; j < hd; j++) ss += v[j] * v[j];
+        double inv = 1.0 / sqrt(ss / (double)hd + eps);
+        for (int64_t j = 0; j < hd; j++) rk[j] = v[j] * inv * tbo_f16_to_f64(w16[j]);
+        for (int64_t j = 0; j < hd; j++) {
+            int64_t fi = j < half ? j : j - half;
+            double ang = (double)pos * pow(theta, -2.0 * (double)fi / (double)hd);
+            double partner = j < half ? rk[j + half] : rk[j - half];
+            double rot = j < half ? -partner : partner;
+            v[j] = rk[j] * cos(ang) + rot * sin(ang);
+        }
+    }
+    free(rk);
+}
+
+/* Split-KV streaming decode attention over the int8 KV cache,
+ * attnDecStreamQ8Wgsl qwen3.js:2077-2164 + ATTN_DEC_COMBINE qwen3.js:2048-2069.
+ * The split/online-softmax structure is exact math, so the oracle is a plain
+ * softmax over all S keys in double:
+ *   score_t = sum_g (sum_{j in g} q_j * unpack(K_tj)) * Ks_tg / sqrt(hd)
+ *   out     = sum_t softmax(score)_t * Vs_tg * unpack(V_tj)
+ * with unpack(c) = max(c/127, -1) (WGSL unpack4x8snorm).  GQA: query head hq
+ * reads kv head hq / (nHq/nKv).  Layout: Kq int8 [S][nKv*hd], Ks f32
+ * [S][nKv*hd/32]; q f32 [nHq*hd]; out double [nHq*hd]. */
+TBO_API void tbo_attn_decode_q8(const float *q, const int8_t *Kq, const float *Ks,
+                                const int8_t *Vq, const float *Vs, int64_t S,
+                                int64_t nHq, int64_t nKv, int64_t hd, double *out)
+{
+    const int64_t grp = nHq / nKv, row = nKv * hd, rowg = row / 32;
+    double *sc = (double *)malloc(sizeof(double) * (size_t)(S > 0 ? S : 1));
+    const double scale = 1.0 / sqrt((double)hd);
+    for (int64_t hq = 0; hq < nHq; hq++) {
+        int64_t hk = hq / grp;
+        double mx = -INFINITY;
+        for (int64_t t = 0; t < S; t++) {
+            double s = 0.0;
+            for (int64_t g = 0; g < hd / 32; g++) {
+                double p = 0.0;
+                for (int j = 0; j < 32; j++) {
+                    int64_t d = g * 32 + j;
+                    double kv = fmax((double)Kq[t * row + hk * hd + d] / 127.0, -1.0);
+                    p += (double)q[hq * hd + d] * kv;
+                }
+                s += p * (double)Ks[t * rowg + hk * (hd / 32) + g];
+            }
+            sc[t] = s * scale;
+            if (sc[t] > mx) mx = sc[t];
+        }
+        double l = 0.0;
+        for (int64_t t = 0; t < S; t++) { sc[t] = exp(sc[t] - mx); l += sc[t]; }
+        for (int64_t d = 0; d < hd; d++) {
+            double o = 0.0;
+            for (int64_t t = 0; t < S; t++) {
+                double vv = fmax((double)Vq[t * row + hk * hd + d] / 127.0, -1.0);
+                o += sc[t] * (double)Vs[t * rowg + hk * (hd / 32) + d / 32] * vv;
+            }
+            out[hq * hd + d] = S > 0 ? o / l : 0.0;
+        }
+    }
+    free(sc);
+}
+
+/* Split count rule, _decNsplit qwen3.js:2354 (DEC_TK = 128, max 16 splits). */
+TBO_API int tbo_dec_nsplit(int64_t S)
+{
+    int64_t a = (S + 127) / 128, b = (S + 447) / 448;
+    if (b < 4) b = 4;
+    int64_t n = a < b ? a : b;
+    if (n > 16) n = 16;
+    return n < 1 ? 1 : (int)n;
+}
+
+/* Argmax over x[n]: index of the maximum, lowest index on ties (the WGSL
+ * kernels at qwen3.js:2625-2690 tie-break by thread order; the result on
+ * distinct maxima is the same). */
+TBO_API int64_t tbo_argmax(const float *x, int64_t n)
+{
+    int64_t bi = 0;
+    float bv = -INFINITY;
+    for (int64_t i = 0; i < n; i++) if (x[i] > bv) { bv = x[i]; bi = i; }
+    return bi;
+}

@@ -1,0 +1,16 @@
+"""tabinfer_b200 -- B200 backend for TabInfer's quantized-GEMV hot path.
+
+The product is libtabinfer_b200.so (hand-written sm_100a CUDA behind the C ABI
+in include/tabinfer_b200.h).  This package is the host-side mirror of the
+reference's operator interface for that path (models/qwen3.js linearQ /
+gemvQ / gemvDP4A / rmsnormQ / gateUpSiluDP4 / attnPrepQ8 / attentionQ8 /
+argmaxKernel, and native/crates/n2-kernels tern::{pack_ternary,
+quantize_act, gemv_tern}), taking torch CUDA tensors as device buffers.
+Errors raise TabInferError, as the reference throws.
+"""
+from .ops import (  # noqa: F401
+    TabInferError, Context, default_context,
+    quantize_int4_bf16, quant_q8, rmsnorm_q8, gemv_q, gemv_dp4, gemv_dp4_multi, linear_q,
+    gate_up_silu_dp4, pack_ternary, quantize_act, gemv_tern, linear_tern,
+    attn_prep_q8, kv_quant_write, attention_decode_q8, argmax, rmsnorm, embed_gather,
+)

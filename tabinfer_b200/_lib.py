@@ -1,0 +1,79 @@
+"""ctypes binding of libtabinfer_b200.so (the C ABI in include/tabinfer_b200.h).
+
+The library is loaded from this package directory (built in-tree by
+tabinfer_b200/csrc/build.py).  There is no fallback: if the shared library is
+missing or fails to load, importing this module raises.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtabinfer_b200.so")
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int
+F32 = ctypes.c_float
+
+# name -> argtypes (restype int status unless noted)
+SIGNATURES = {
+    "tb_version": [],
+    "tb_ctx_create": [I32, ctypes.POINTER(P)],
+    "tb_ctx_destroy": [P],
+    "tb_ctx_set_stream": [P, P],
+    "tb_ctx_get_stream": [P],
+    "tb_ctx_set_pdl": [P, I32],
+    "tb_last_error": [P],
+    "tb_ctx_synchronize": [P],
+    "tb_ctx_device_error": [P, ctypes.POINTER(I32)],
+    "tb_quant_int4_g32": [P, P, P, P, I64, I64],
+    "tb_quant_q8": [P, P, P, P, P, I64, I64],
+    "tb_rmsnorm_q8": [P, P, P, F32, P, P, P, I64, I64],
+    "tb_gemv_int4_q8": [P, P, P, P, P, P, I64, I64, I32, I32],
+    "tb_gemv_int4_f32": [P, P, P, P, P, I64, I64, I32, I32],
+    "tb_linear_int4": [P, P, P, P, P, I64, I64, I64, I32],
+    "tb_gateup_silu_int4_q8": [P, P, P, P, P, P, P, P, I64, I64, I32],
+    "tb_gemv_int4_q8_multi": [P, I32, P, P, P, P, P, P, I64, I32, I32],
+    "tb_pack_tern_q2g64": [P, P, P, P, I64, I64],
+    "tb_quant_act_q8": [P, P, P, P, P, I64, I64],
+    "tb_gemv_tern_q2g64": [P, P, P, P, P, P, I64, I64, I32],
+    "tb_linear_tern": [P, P, P, P, P, I64, I64, I64],
+    "tb_attn_prep_q8": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, F32, F32],
+    "tb_kv_quant_write": [P, P, P, P, P, P, P, I64, I64, I64, I64],
+    "tb_attn_decode_q8": [P, P, P, P, P, P, P, I64, I64, I64, I64, I32],
+    "tb_argmax": [P, P, I64, I64, P, I64],
+    "tb_rmsnorm": [P, P, P, P, I64, I64, F32],
+    "tb_embed_gather": [P, P, I64, P, P, I64, I64],
+}
+RESTYPES = {
+    "tb_last_error": ctypes.c_char_p,
+    "tb_ctx_get_stream": P,
+}
+
+
+def load(path=LIB_PATH):
+    if not os.path.exists(path):
+        raise ImportError(
+            "libtabinfer_b200.so not found at %s; build it with "
+            "`python -c 'import __graft_entry__ as g; g.build()'` (nvcc, sm_100a)" % path)
+    lib = ctypes.CDLL(path)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = RESTYPES.get(name, ctypes.c_int)
+    return lib
+
+
+def header_symbols(header=None):
+    """Function names declared TB_API in include/*.h."""
+    import re
+    inc = os.path.join(os.path.dirname(HERE), "include")
+    names = []
+    for fn in sorted(os.listdir(inc)):
+        if fn.endswith(".h"):
+            txt = open(os.path.join(inc, fn)).read()
+            names += re.findall(r"TB_API\s+[\w\s\*]+?\b(tb_\w+)\s*\(", txt)
+    return names
+
+
+LIB = load()

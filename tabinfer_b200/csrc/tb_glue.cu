@@ -1,0 +1,166 @@
+// tb_glue.cu -- decode-step glue: argmax, RMSNorm, embedding gather.
+#include "tb_common.cuh"
+
+namespace {
+
+constexpr int AMAX_THREADS = 256;
+
+// Orderable key: larger value wins, then the LOWER index (ties), NaN never wins
+// (the reference's `if (v > bv)` skips NaN).
+__device__ __forceinline__ unsigned long long amax_key(float v, unsigned idx)
+{
+    if (isnan(v)) v = -INFINITY;
+    uint32_t f = __float_as_uint(v);
+    uint32_t o = (f & 0x80000000u) ? ~f : (f | 0x80000000u);
+    return ((unsigned long long)o << 32) | (0xffffffffu - idx);
+}
+
+__device__ __forceinline__ unsigned long long block_max_key(unsigned long long k)
+{
+    __shared__ unsigned long long sk[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long p = __shfl_xor_sync(0xffffffffu, k, o);
+        k = p > k ? p : k;
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) sk[wid] = k;
+    __syncthreads();
+    if (wid == 0) {
+        k = lane < (int)(blockDim.x >> 5) ? sk[lane] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long p = __shfl_xor_sync(0xffffffffu, k, o);
+            k = p > k ? p : k;
+        }
+    }
+    return k;   // valid in thread 0
+}
+
+// stage 1: blocks (bx, row) reduce an interleaved slice of row `row`
+__global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p1(const float* __restrict__ x, long long n,
+                                                            unsigned long long* __restrict__ part)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int row = blockIdx.y;
+    const float* xr = x + (long long)row * n;
+    unsigned long long best = 0ull;
+    for (long long i = blockIdx.x * (long long)AMAX_THREADS + threadIdx.x; i < n;
+         i += (long long)gridDim.x * AMAX_THREADS) {
+        unsigned long long k = amax_key(xr[i], (unsigned)i);
+        best = k > best ? k : best;
+    }
+    best = block_max_key(best);
+    if (threadIdx.x == 0) part[(long long)row * gridDim.x + blockIdx.x] = best;
+}
+
+__global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p2(const unsigned long long* __restrict__ part, int nparts,
+                                                            uint32_t* __restrict__ out)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int row = blockIdx.x;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < nparts; i += AMAX_THREADS) {
+        unsigned long long k = part[(long long)row * nparts + i];
+        best = k > best ? k : best;
+    }
+    best = block_max_key(best);
+    if (threadIdx.x == 0) out[row] = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+}
+
+// RMSNorm, qwen3.js:60-88: one CTA per row.
+__global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const uint16_t* __restrict__ w16,
+                                                 float* __restrict__ y, int H, float eps)
+{
+    __shared__ float red[32];
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int row = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const float* xr = x + (long long)row * H;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) { float v = xr[i]; ss = fmaf(v, v, ss); }
+    ss = warp_sum(ss);
+    if (lane == 0) red[wid] = ss;
+    __syncthreads();
+    if (wid == 0) {
+        float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)H), eps)));
+    for (int i = threadIdx.x; i < H; i += blockDim.x)
+        y[(long long)row * H + i] = __fmul_rn(__fmul_rn(xr[i], inv), tb_h2f(w16[i]));
+}
+
+// embedGather, qwen3.js:1621-1675: y[t,h] = f32(embed[ids[idoff+t], h])
+__global__ void __launch_bounds__(256) k_embed(const uint32_t* __restrict__ ids, long long idoff,
+                                               const uint16_t* __restrict__ emb, float* __restrict__ y, int T, int H)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * H;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / H), h = (int)(i - (long long)t * H);
+        y[i] = tb_h2f(emb[(long long)ids[idoff + t] * H + h]);
+    }
+}
+
+}  // namespace
+
+int tb_argmax_impl(tb_ctx* ctx, const float* x, int64_t n, int64_t rows, uint32_t* out, unsigned long long* part,
+                   int nparts)
+{
+    cudaError_t e = tb_launch(ctx, k_argmax_p1, dim3(nparts, (unsigned)rows), dim3(AMAX_THREADS), 0, x, (long long)n, part);
+    if (e == cudaSuccess)
+        e = tb_launch(ctx, k_argmax_p2, dim3((unsigned)rows), dim3(AMAX_THREADS), 0,
+                      (const unsigned long long*)part, nparts, out);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "argmax launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+int tb_argmax_parts(tb_ctx* ctx, int64_t n)
+{
+    long long want = (n + AMAX_THREADS * 8 - 1) / (AMAX_THREADS * 8);
+    return (int)std::max(1LL, std::min(want, (long long)ctx->num_sms));
+}
+
+extern "C" {
+
+TB_API int tb_argmax(tb_ctx* ctx, const float* x, int64_t n, int64_t rows, uint32_t* out_idx, int64_t out_offset)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, x && out_idx, "null pointer");
+    TB_REQUIRE(ctx, n > 0 && n < (1LL << 32) - 1 && rows > 0 && rows <= 65535 && out_offset >= 0, "bad shape");
+    int nparts = tb_argmax_parts(ctx, n);
+    auto* part = static_cast<unsigned long long*>(tb_ctx_scratch(ctx, (size_t)rows * nparts * 8));
+    if (!part) return TB_ERR_NOMEM;
+    return tb_argmax_impl(ctx, x, n, rows, out_idx + out_offset, part, nparts);
+}
+
+TB_API int tb_rmsnorm(tb_ctx* ctx, const float* x, const uint16_t* w16, float* y, int64_t T, int64_t H, float eps)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, x && w16 && y, "null pointer");
+    TB_REQUIRE(ctx, T > 0 && T <= 65535 && H > 0, "bad shape");
+    cudaError_t e = tb_launch(ctx, k_rmsnorm, dim3((unsigned)T), dim3(256), 0, x, w16, y, (int)H, eps);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_embed_gather(tb_ctx* ctx, const uint32_t* ids, int64_t idoff, const uint16_t* emb, float* y, int64_t T,
+                           int64_t H)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, ids && emb && y, "null pointer");
+    TB_REQUIRE(ctx, T > 0 && H > 0 && idoff >= 0, "bad shape");
+    long long tot = T * H;
+    int grid = (int)std::min<long long>((tot + 255) / 256, (long long)ctx->num_sms * 8);
+    cudaError_t e = tb_launch(ctx, k_embed, dim3(grid), dim3(256), 0, ids, (long long)idoff, emb, y, (int)T, (int)H);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "embed launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+}  // extern "C"

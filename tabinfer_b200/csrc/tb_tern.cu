@@ -1,0 +1,278 @@
+// tb_tern.cu -- ternary Q2_0_g64 path of the Bonsai engine
+// (native/crates/n2-kernels/src/tern.rs, cpu/kernel/src/lib.rs).
+//
+// Format (native/docs/FORMAT.md:49-112): per row, K/64 groups; group = 16
+// bytes of codes (code c in byte c%16 at bit 2*(c/16), value code-1) and one
+// f32 scale.  out[n] = sum_b s*dot_b - sum_b s*xsum_b, two f32 chains summed
+// in block order and subtracted once (tern.rs:79-119).
+//
+// GEMV design: a warp tile is TR consecutive rows, i.e. one contiguous run of
+// TR*K/4 code bytes and TR*K/64 scales, loaded with perfectly coalesced 16-byte
+// lane loads (phase A).  Each (row, group) item gives an exact int32 dot via
+// 16 dp4a, and the rounded product s*dot is parked in shared memory.  Phase B
+// gives one lane per (row, activation column) and sums the products serially
+// in block order with separately rounded f32 adds, which reproduces
+// gemv_tern_scalar bit for bit while the HBM stream stays fully parallel.
+#include "tb_common.cuh"
+
+namespace {
+
+constexpr int TERN_THREADS = 128;
+constexpr int TERN_WARPS = TERN_THREADS / 32;
+constexpr int TERN_UNROLL = 4;
+
+// ---- pack_ternary (tern.rs:131-160): one warp per (row, 64-group) ----------
+__global__ void __launch_bounds__(256) k_pack_ternary(const float* __restrict__ w, uint8_t* __restrict__ codes,
+                                                      float* __restrict__ scales, long long ngroups)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    for (long long g = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; g < ngroups;
+         g += ((long long)gridDim.x * blockDim.x) >> 5) {
+        const float a = w[g * 64 + lane], b = w[g * 64 + 32 + lane];
+        float s = fmaxf(fabsf(a), fabsf(b));
+        s = warp_max(s);
+        const float thr = s * 0.5f;
+        const uint32_t ca = fabsf(a) < thr ? 1u : (a < 0.0f ? 0u : 2u);   // element lane
+        const uint32_t cb = fabsf(b) < thr ? 1u : (b < 0.0f ? 0u : 2u);   // element 32+lane
+        const uint32_t pa = __shfl_down_sync(0xffffffffu, ca, 16);          // element 16+lane
+        const uint32_t pb = __shfl_down_sync(0xffffffffu, cb, 16);          // element 48+lane
+        if (lane < 16) codes[g * 16 + lane] = (uint8_t)(ca | (pa << 2) | (cb << 4) | (pb << 6));
+        if (lane == 0) scales[g] = s;
+    }
+}
+
+// ---- quantize_act_into (tern.rs:206-222): one CTA per activation row -------
+__global__ void __launch_bounds__(256) k_quant_act(const float* __restrict__ x, int8_t* __restrict__ act,
+                                                   int32_t* __restrict__ xsum, float* __restrict__ scale_out, int K)
+{
+    __shared__ float red[32];
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int row = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const float* xr = x + (long long)row * K;
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) m = fmaxf(m, fabsf(xr[i]));
+    m = warp_max(m);
+    if (lane == 0) red[wid] = m;
+    __syncthreads();
+    if (wid == 0) {
+        float t = lane < nw ? red[lane] : 0.0f;
+        t = warp_max(t);
+        if (lane == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float amax = red[0];
+    const float scale = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 1.0f;
+    if (threadIdx.x == 0) scale_out[row] = scale;
+    for (int g = wid; g < K / 64; g += nw) {
+        int s = 0;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            int i = g * 64 + h * 32 + lane;
+            float v = roundf(__fmul_rn(xr[i], scale));   // half away from zero, as f32::round
+            v = fminf(127.0f, fmaxf(-127.0f, v));
+            int q = (int)v;
+            act[(long long)row * K + i] = (int8_t)q;
+            s += q;
+        }
+        s = (int)warp_sum((float)s);   // |s| <= 64*127: exact in f32
+        if (lane == 0) xsum[(long long)row * (K / 64) + g] = s;
+    }
+}
+
+// ---- ternary GEMV --------------------------------------------------------
+struct TernArgs {
+    float* out;
+    const uint8_t* codes;
+    const float* scales;
+    const int8_t* act;
+    const int32_t* xsum;
+    const float* act_scale;   // optional [B]: out *= 1/act_scale (Model::linear, model.rs:334-337)
+    int N, K, tiles;
+};
+
+// act chunk j (16 bytes = 4 words) of group b lives at slot j ^ ((b>>1)&3),
+// which spreads 8 consecutive groups over 8 bank quads.
+__device__ __forceinline__ int act_slot(int b, int j) { return b * 4 + (j ^ ((b >> 1) & 3)); }
+
+template <int B>
+__global__ void __launch_bounds__(TERN_THREADS) k_gemv_tern(const TernArgs a)
+{
+    constexpr int TR = B <= 4 ? 8 : 32 / B;   // rows per warp tile
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int nb = a.K >> 6;
+    const int ld = nb + 1;                      // padded row stride of the parking area
+    uint4* act_s = reinterpret_cast<uint4*>(smem);                       // [B][nb*4]
+    int* xsum_s = reinterpret_cast<int*>(act_s + B * nb * 4);            // [B][nb]
+    float* park = reinterpret_cast<float*>(xsum_s + B * nb);             // per warp: S[TR][ld], P[B][TR][ld]
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    float* S = park + wid * (B + 1) * TR * ld;
+    float* P = S + TR * ld;
+
+    const int items = TR * nb;                 // (row, group) items per tile
+    const int gw = blockIdx.x * TERN_WARPS + wid, nwarps = gridDim.x * TERN_WARPS;
+
+    // prologue: first items of the first tile, before waiting on the producer
+    uint4 cv[TERN_UNROLL];
+    float sv[TERN_UNROLL];
+    auto load_items = [&](int tile, int i0) {
+        const long long base = (long long)tile * items;   // tile rows are contiguous
+#pragma unroll
+        for (int u = 0; u < TERN_UNROLL; u++) {
+            int i = i0 + u * 32;
+            long long gi = base + i;
+            bool ok = i < items && gi < (long long)a.N * nb;
+            cv[u] = ok ? ldg_stream_v4(a.codes + gi * 16) : make_uint4(0, 0, 0, 0);
+            sv[u] = ok ? __ldg(a.scales + gi) : 0.0f;
+        }
+    };
+    if (gw < a.tiles) load_items(gw, lane);
+
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    for (int i = threadIdx.x; i < B * nb * 4; i += blockDim.x) {
+        int b = i / (nb * 4), r = i - b * nb * 4, g = r >> 2, j = r & 3;
+        act_s[b * nb * 4 + act_slot(g, j)] = reinterpret_cast<const uint4*>(a.act + (long long)b * a.K)[g * 4 + j];
+    }
+    for (int i = threadIdx.x; i < B * nb; i += blockDim.x) xsum_s[i] = a.xsum[i];
+    __syncthreads();
+
+    for (int tile = gw; tile < a.tiles; tile += nwarps) {
+        for (int i0 = lane;; i0 += TERN_UNROLL * 32) {
+            if (tile != gw || i0 != lane) load_items(tile, i0);
+#pragma unroll
+            for (int u = 0; u < TERN_UNROLL; u++) {
+                int i = i0 + u * 32;
+                if (i >= items) break;
+                const int r = i / nb, g = i - r * nb;
+                const uint32_t cw[4] = {cv[u].x, cv[u].y, cv[u].z, cv[u].w};
+#pragma unroll
+                for (int b = 0; b < B; b++) {
+                    const uint4* ab = act_s + b * nb * 4;
+                    int d = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const uint4 av = ab[act_slot(g, j)];
+                        const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+                        for (int w = 0; w < 4; w++)
+                            d = __dp4a((int)((cw[w] >> (2 * j)) & 0x03030303u), (int)aw[w], d);
+                    }
+                    P[(b * TR + r) * ld + g] = __fmul_rn(sv[u], (float)d);
+                }
+                S[r * ld + g] = sv[u];
+            }
+            if (i0 + TERN_UNROLL * 32 >= items) break;
+        }
+        __syncwarp();
+        if (lane < TR * B) {
+            const int r = lane % TR, b = lane / TR;
+            const int row = tile * TR + r;
+            if (row < a.N) {
+                const float* pr = P + (b * TR + r) * ld;
+                const float* sr = S + r * ld;
+                const int* xb = xsum_s + b * nb;
+                float acc = 0.0f, sxs = 0.0f;
+                for (int g = 0; g < nb; g++) {
+                    acc = __fadd_rn(acc, pr[g]);
+                    sxs = __fadd_rn(sxs, __fmul_rn(sr[g], (float)xb[g]));
+                }
+                float v = __fsub_rn(acc, sxs);
+                if (a.act_scale) v = __fmul_rn(v, __fdiv_rn(1.0f, a.act_scale[b]));
+                a.out[(long long)b * a.N + row] = v;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+size_t tern_smem(int B, int nb)
+{
+    const int TR = B <= 4 ? 8 : 32 / B;
+    return (size_t)B * nb * 64 + (size_t)B * nb * 4 + (size_t)TERN_WARPS * (B + 1) * TR * (nb + 1) * 4;
+}
+
+template <int B>
+int launch_tern_B(tb_ctx* ctx, const TernArgs& a)
+{
+    const int nb = a.K >> 6;
+    size_t sm = tern_smem(B, nb);
+    if (sm > 227 * 1024) return tb_fail(ctx, TB_ERR_UNSUPPORTED, "K=%d batch=%d needs %zu bytes of shared memory", a.K, B, sm);
+    if (sm > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemv_tern<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
+    int occ = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemv_tern<B>, TERN_THREADS, sm);
+    if (occ < 1) occ = 1;
+    int grid = std::min(tb_cdiv(a.tiles, TERN_WARPS), ctx->num_sms * occ);
+    cudaError_t e = tb_launch(ctx, k_gemv_tern<B>, dim3(grid), dim3(TERN_THREADS), sm, a);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemv_tern launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+}  // namespace
+
+int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,
+                      const int32_t* xsum, int64_t N, int64_t K, int batch, const float* act_scale)
+{
+    TB_REQUIRE(ctx, out && codes && scales && act && xsum, "null pointer");
+    TB_REQUIRE(ctx, N > 0 && N < (1LL << 31) && K > 0 && K % 64 == 0 && K <= (1 << 18),
+               "bad shape N=%lld K=%lld (K%%64 must be 0)", (long long)N, (long long)K);
+    TB_REQUIRE(ctx, TB_ALIGNED(codes, 16) && TB_ALIGNED(act, 16) && TB_ALIGNED(scales, 4) && TB_ALIGNED(xsum, 4),
+               "codes/act must be 16-byte aligned");
+    TernArgs a{out, codes, scales, act, xsum, act_scale, (int)N, (int)K, 0};
+    const int TR = batch <= 4 ? 8 : 32 / batch;
+    a.tiles = tb_cdiv(N, TR);
+    switch (batch) {
+    case 1: return launch_tern_B<1>(ctx, a);
+    case 2: return launch_tern_B<2>(ctx, a);
+    case 3: return launch_tern_B<3>(ctx, a);
+    case 4: return launch_tern_B<4>(ctx, a);
+    case 5: return launch_tern_B<5>(ctx, a);
+    case 6: return launch_tern_B<6>(ctx, a);
+    case 7: return launch_tern_B<7>(ctx, a);
+    case 8: return launch_tern_B<8>(ctx, a);
+    }
+    return tb_fail(ctx, TB_ERR_INVALID, "batch must be 1..8 (got %d)", batch);
+}
+
+int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K)
+{
+    TB_REQUIRE(ctx, x && act && xsum && scale, "null pointer");
+    TB_REQUIRE(ctx, T > 0 && T <= 65535 && K > 0 && K % 64 == 0, "bad shape T=%lld K=%lld", (long long)T, (long long)K);
+    cudaError_t e = tb_launch(ctx, k_quant_act, dim3((unsigned)T), dim3(256), 0, x, act, xsum, scale, (int)K);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_act launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+extern "C" {
+
+TB_API int tb_pack_tern_q2g64(tb_ctx* ctx, const float* w, uint8_t* codes, float* scales, int64_t N, int64_t K)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, w && codes && scales, "null pointer");
+    TB_REQUIRE(ctx, N > 0 && K > 0 && K % 64 == 0, "bad shape N=%lld K=%lld (K%%64 must be 0)", (long long)N, (long long)K);
+    long long ng = N * (K / 64);
+    int grid = (int)std::min<long long>((ng * 32 + 255) / 256, (long long)ctx->num_sms * 8);
+    cudaError_t e = tb_launch(ctx, k_pack_ternary, dim3(grid), dim3(256), 0, w, codes, scales, ng);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "pack_ternary launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_quant_act_q8(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return tb_quant_act_impl(ctx, x, act, xsum, scale, T, K);
+}
+
+TB_API int tb_gemv_tern_q2g64(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,
+                              const int32_t* xsum, int64_t N, int64_t K, int batch)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return tb_gemv_tern_impl(ctx, out, codes, scales, act, xsum, N, K, batch, nullptr);
+}
+
+}  // extern "C"

@@ -1,0 +1,323 @@
+"""Host-side operator mirror over the C ABI.
+
+Each function follows one reference operator (cited) with the same argument
+meaning; device buffers are torch CUDA tensors (contiguous), outputs are
+allocated when not supplied.  Every call is ordered on the current torch
+stream of the tensor's device.  Shape/alignment errors raise TabInferError
+with the library's message (the reference throws / panics).
+"""
+import ctypes
+import threading
+
+import torch
+
+from ._lib import LIB, P
+
+TB_ACT_F32, TB_ACT_Q8 = 0, 1
+
+
+class TabInferError(RuntimeError):
+    pass
+
+
+class Context:
+    """One tb_ctx per (host thread, device): replaces the engine handle of
+    engine/webgpu-engine.js:72 and the module scratch of models/qwen3.js."""
+
+    def __init__(self, device=0):
+        h = P()
+        rc = LIB.tb_ctx_create(int(device), ctypes.byref(h))
+        if rc != 0:
+            raise TabInferError("tb_ctx_create(%d) failed with status %d" % (device, rc))
+        self.h = h
+        self.device = int(device)
+
+    def check(self, rc, what):
+        if rc != 0:
+            msg = LIB.tb_last_error(self.h)
+            raise TabInferError("%s: status %d: %s" % (what, rc, msg.decode() if msg else ""))
+
+    def bind_stream(self):
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        LIB.tb_ctx_set_stream(self.h, P(s))
+
+    def set_pdl(self, on):
+        LIB.tb_ctx_set_pdl(self.h, 1 if on else 0)
+
+    def synchronize(self):
+        self.check(LIB.tb_ctx_synchronize(self.h), "synchronize")
+
+    def device_error(self):
+        code = ctypes.c_int(0)
+        LIB.tb_ctx_device_error(self.h, ctypes.byref(code))
+        return code.value
+
+    def close(self):
+        if self.h:
+            LIB.tb_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_tls = threading.local()
+
+
+def default_context(device=None):
+    if device is None:
+        device = torch.cuda.current_device()
+    device = int(device)
+    ctxs = getattr(_tls, "ctxs", None)
+    if ctxs is None:
+        ctxs = _tls.ctxs = {}
+    c = ctxs.get(device)
+    if c is None:
+        c = ctxs[device] = Context(device)
+    c.bind_stream()
+    return c
+
+
+def _p(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise TabInferError("tensor must be on a CUDA device")
+    if not t.is_contiguous():
+        raise TabInferError("tensor must be contiguous")
+    return P(t.data_ptr())
+
+
+def _ctx(t):
+    return default_context(t.device.index)
+
+
+def _u16(t):
+    """bf16 / f16 tensors are passed as their 16-bit patterns."""
+    return t
+
+
+# --------------------------------------------------------------------------
+# int4 G=32 path (models/qwen3.js)
+# --------------------------------------------------------------------------
+
+def quantize_int4_bf16(w, pack=None, scales=None):
+    """quantizeInt4Bf16 (qwen3.js:3405-3426): bf16 [N,K] -> (pack u32 [N,K/8] as int32, scales f16 [N,K/32])."""
+    N, K = w.shape
+    if pack is None:
+        pack = torch.empty((N, K // 8), dtype=torch.int32, device=w.device)
+    if scales is None:
+        scales = torch.empty((N, K // 32), dtype=torch.float16, device=w.device)
+    c = _ctx(w)
+    c.check(LIB.tb_quant_int4_g32(c.h, _p(w), _p(pack), _p(scales), N, K), "quant_int4_g32")
+    return pack, scales
+
+
+def quant_q8(x, xq=None, xs=None, xsum16=None):
+    """quantQ8 / QUANTQ8T (qwen3.js:332-358, 1210-1231): f32 [T,K] -> int8, per-32 scales, per-16 sums."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, K = x2.shape
+    xq = xq if xq is not None else torch.empty((T, K), dtype=torch.int8, device=x.device)
+    xs = xs if xs is not None else torch.empty((T, K // 32), dtype=torch.float32, device=x.device)
+    xsum16 = xsum16 if xsum16 is not None else torch.empty((T, K // 16), dtype=torch.int32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_quant_q8(c.h, _p(x2), _p(xq), _p(xs), _p(xsum16), T, K), "quant_q8")
+    return xq, xs, xsum16
+
+
+def rmsnorm_q8(x, w16, eps, xq=None, xs=None, xsum16=None):
+    """rmsnormQ (qwen3.js:569-621): fused RMSNorm -> per-32 int8."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, H = x2.shape
+    xq = xq if xq is not None else torch.empty((T, H), dtype=torch.int8, device=x.device)
+    xs = xs if xs is not None else torch.empty((T, H // 32), dtype=torch.float32, device=x.device)
+    xsum16 = xsum16 if xsum16 is not None else torch.empty((T, H // 16), dtype=torch.int32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_rmsnorm_q8(c.h, _p(x2), _p(w16), float(eps), _p(xq), _p(xs), _p(xsum16), T, H), "rmsnorm_q8")
+    return xq, xs, xsum16
+
+
+def gemv_dp4(xq, xs, pack, scales, y=None, acc=False):
+    """gemvDP4_only (qwen3.js:422-427): int8-activation GEMV, batch = xq rows."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    B, K = xq2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((B, N), dtype=torch.float32, device=xq.device)
+    c = _ctx(xq)
+    c.check(LIB.tb_gemv_int4_q8(c.h, _p(y), _p(xq2), _p(xs), _p(pack), _p(scales), N, K, B, 1 if acc else 0),
+            "gemv_int4_q8")
+    return y
+
+
+def gemv_dp4_multi(xq, xs, mats, ys=None, acc=False):
+    """q/k/v projGemv triple on one quantized activation (qwen3.js:3981-3984), one launch.
+    mats: list of (pack, scales)."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    B, K = xq2.shape
+    n = len(mats)
+    if ys is None:
+        ys = [torch.zeros((B, p.shape[0]), dtype=torch.float32, device=xq.device) for p, _ in mats]
+    arr_y = (P * n)(*[y.data_ptr() for y in ys])
+    arr_p = (P * n)(*[p.data_ptr() for p, _ in mats])
+    arr_s = (P * n)(*[s.data_ptr() for _, s in mats])
+    arr_n = (ctypes.c_int64 * n)(*[p.shape[0] for p, _ in mats])
+    c = _ctx(xq)
+    c.check(LIB.tb_gemv_int4_q8_multi(c.h, n, ctypes.cast(arr_y, P), ctypes.cast(arr_p, P), ctypes.cast(arr_s, P),
+                                      ctypes.cast(arr_n, P), _p(xq2), _p(xs), K, B, 1 if acc else 0),
+            "gemv_int4_q8_multi")
+    return ys
+
+
+def gemv_q(x, pack, scales, y=None, acc=False):
+    """gemvQ (qwen3.js:314-321): f32-activation int4 GEMV, batch = x rows."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((B, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_gemv_int4_f32(c.h, _p(y), _p(x2), _p(pack), _p(scales), N, K, B, 1 if acc else 0),
+            "gemv_int4_f32")
+    return y
+
+
+def linear_q(x, pack, scales, y=None, acc=False):
+    """linearQ (qwen3.js:1588-1608) for T = x rows (1..8)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, K = x2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((T, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_linear_int4(c.h, _p(y), _p(x2), _p(pack), _p(scales), T, N, K, 1 if acc else 0), "linear_int4")
+    return y
+
+
+def gate_up_silu_dp4(xq, xs, gpack, gscales, upack, uscales, swi=None):
+    """gateUpSiluDP4_only (qwen3.js:861-877): swi = silu(W_g x) * (W_u x)."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    B, H = xq2.shape
+    I = gpack.shape[0]
+    if swi is None:
+        swi = torch.empty((B, I), dtype=torch.float32, device=xq.device)
+    c = _ctx(xq)
+    c.check(LIB.tb_gateup_silu_int4_q8(c.h, _p(swi), _p(xq2), _p(xs), _p(gpack), _p(gscales), _p(upack),
+                                       _p(uscales), I, H, B), "gateup_silu_int4_q8")
+    return swi
+
+
+# --------------------------------------------------------------------------
+# ternary Q2_0_g64 (native/crates/n2-kernels/src/tern.rs)
+# --------------------------------------------------------------------------
+
+def pack_ternary(w, codes=None, scales=None):
+    """tern::pack_ternary (tern.rs:131-160): f32 [N,K] -> codes u8 [N,K/4], scales f32 [N,K/64]."""
+    N, K = w.shape
+    codes = codes if codes is not None else torch.empty((N, K // 4), dtype=torch.uint8, device=w.device)
+    scales = scales if scales is not None else torch.empty((N, K // 64), dtype=torch.float32, device=w.device)
+    c = _ctx(w)
+    c.check(LIB.tb_pack_tern_q2g64(c.h, _p(w), _p(codes), _p(scales), N, K), "pack_tern_q2g64")
+    return codes, scales
+
+
+def quantize_act(x, act=None, xsum=None, scale=None):
+    """tern::quantize_act (tern.rs:196-222): returns (act i8, xsum i32 per 64, scale per row)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, K = x2.shape
+    act = act if act is not None else torch.empty((T, K), dtype=torch.int8, device=x.device)
+    xsum = xsum if xsum is not None else torch.empty((T, K // 64), dtype=torch.int32, device=x.device)
+    scale = scale if scale is not None else torch.empty((T,), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_quant_act_q8(c.h, _p(x2), _p(act), _p(xsum), _p(scale), T, K), "quant_act_q8")
+    return act, xsum, scale
+
+
+def gemv_tern(codes, scales, act, xsum, out=None):
+    """tern::gemv_tern (tern.rs:56-71) / WASM gemm_tern_b4 (lib.rs:331): batch = act rows."""
+    a2 = act.reshape(-1, act.shape[-1])
+    B, K = a2.shape
+    N = codes.shape[0]
+    out = out if out is not None else torch.empty((B, N), dtype=torch.float32, device=act.device)
+    c = _ctx(act)
+    c.check(LIB.tb_gemv_tern_q2g64(c.h, _p(out), _p(codes), _p(scales), _p(a2), _p(xsum), N, K, B), "gemv_tern_q2g64")
+    return out
+
+
+def linear_tern(x, codes, scales, y=None):
+    """Model::linear (model.rs:316-339): quantize_act -> gemv_tern -> *= 1/scale."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, K = x2.shape
+    N = codes.shape[0]
+    y = y if y is not None else torch.empty((T, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_linear_tern(c.h, _p(y), _p(x2), _p(codes), _p(scales), T, N, K), "linear_tern")
+    return y
+
+
+# --------------------------------------------------------------------------
+# int8 KV attention (qwen3.js:2048-2308)
+# --------------------------------------------------------------------------
+
+def attn_prep_q8(q, k, v, qw16, kw16, kv, nHq, nKv, hd, pos, theta, eps, qr=None):
+    """attnPrepQ8 (qwen3.js:2297-2308). kv = (Kq, Ks, Vq, Vs) cache tensors."""
+    qr = qr if qr is not None else torch.empty((nHq * hd,), dtype=torch.float32, device=q.device)
+    Kq, Ks, Vq, Vs = kv
+    c = _ctx(q)
+    c.check(LIB.tb_attn_prep_q8(c.h, _p(q), _p(k), _p(v), _p(qw16), _p(kw16), _p(qr), _p(Kq), _p(Ks), _p(Vq),
+                                _p(Vs), nHq, nKv, hd, int(pos), float(theta), float(eps)), "attn_prep_q8")
+    return qr
+
+
+def kv_quant_write(kr, v, kv, T, nKv, hd, pos_base):
+    """kvQuantWrite (qwen3.js:2211-2216)."""
+    Kq, Ks, Vq, Vs = kv
+    c = _ctx(kr)
+    c.check(LIB.tb_kv_quant_write(c.h, _p(kr), _p(v), _p(Kq), _p(Ks), _p(Vq), _p(Vs), T, nKv, hd, int(pos_base)),
+            "kv_quant_write")
+
+
+def attention_decode_q8(qr, kv, S, nHq, nKv, hd, nsplit=0, out=None):
+    """attnDecodeStreamQ8 + combine (qwen3.js:2165-2173)."""
+    out = out if out is not None else torch.empty((nHq * hd,), dtype=torch.float32, device=qr.device)
+    Kq, Ks, Vq, Vs = kv
+    c = _ctx(qr)
+    c.check(LIB.tb_attn_decode_q8(c.h, _p(out), _p(qr), _p(Kq), _p(Ks), _p(Vq), _p(Vs), int(S), nHq, nKv, hd,
+                                  int(nsplit)), "attn_decode_q8")
+    return out
+
+
+# --------------------------------------------------------------------------
+# glue
+# --------------------------------------------------------------------------
+
+def argmax(x, out=None, offset=0):
+    """argmaxKernel (qwen3.js:2681-2690) over each row of x."""
+    x2 = x.reshape(-1, x.shape[-1])
+    R, n = x2.shape
+    out = out if out is not None else torch.empty((R,), dtype=torch.int32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_argmax(c.h, _p(x2), n, R, _p(out), int(offset)), "argmax")
+    return out
+
+
+def rmsnorm(x, w16, eps, y=None):
+    """rmsnorm (qwen3.js:81-88)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, H = x2.shape
+    y = y if y is not None else torch.empty_like(x2)
+    c = _ctx(x)
+    c.check(LIB.tb_rmsnorm(c.h, _p(x2), _p(w16), _p(y), T, H, float(eps)), "rmsnorm")
+    return y
+
+
+def embed_gather(ids, embed_f16, T, idoff=0, y=None):
+    """embedGather (qwen3.js:1663-1675)."""
+    H = embed_f16.shape[1]
+    y = y if y is not None else torch.empty((T, H), dtype=torch.float32, device=ids.device)
+    c = _ctx(ids)
+    c.check(LIB.tb_embed_gather(c.h, _p(ids), int(idoff), _p(embed_f16), _p(y), T, H), "embed_gather")
+    return y
