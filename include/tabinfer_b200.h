@@ -60,6 +60,25 @@ TB_API int tb_ctx_synchronize(tb_ctx *ctx);
 /* Synchronise and read (and clear) the device error word that bounded waits set. */
 TB_API int tb_ctx_device_error(tb_ctx *ctx, int *code);
 
+/* ---- recorded batches (single-submit decode) ------------------------------
+ * Replaces beginBatch / endBatch of engine/webgpu-engine.js:372-386, which the
+ * forward uses to submit a whole decode step as ONE command buffer
+ * (models/qwen3.js:3958).  Here the calls between tb_batch_begin and
+ * tb_batch_end are recorded (CUDA stream capture into a graph) instead of
+ * executed, and tb_batch_submit replays them with one launch.  Recording needs
+ * the context's own stream (tb_ctx_set_stream(ctx, NULL)); the combined calls
+ * that use context scratch must have run once beforehand at the same sizes. */
+typedef struct tb_batch tb_batch;
+TB_API int tb_batch_begin(tb_ctx *ctx);
+TB_API int tb_batch_end(tb_ctx *ctx, tb_batch **out);
+TB_API int tb_batch_submit(tb_ctx *ctx, tb_batch *batch);
+TB_API int tb_batch_destroy(tb_batch *batch);
+/* Stream-ordered copies between host memory and device buffers (pinned host
+ * memory makes them asynchronous), queue.writeBuffer / mapAsync readback of
+ * the reference (qwen3.js:4083). */
+TB_API int tb_copy_h2d(tb_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes);
+TB_API int tb_copy_d2h(tb_ctx *ctx, void *dst_host, const void *src_dev, size_t bytes);
+
 /* ---- int4 G=32 weight path ------------------------------------------------ */
 
 /* Quant-on-arrival: bf16 [N,K] -> pack u32 [N,K/8] (k=8w+i at bits 4i, nibble

@@ -232,3 +232,12 @@ TBR_API void tbr_linear_int4(float *y, const float *x, const uint32_t *pack,
         run_job(&j, threads);
     }
 }
+
+/* gemvQ math (f32 activations) over all N rows, whatever N: the route linearQ
+ * takes for the lm_head (qwen3.js:1602). */
+TBR_API void tbr_gemv_int4_f32(float *y, const float *x, const uint32_t *pack, const uint16_t *scales,
+                               int64_t N, int64_t K, int acc, int threads)
+{
+    job_t j = {JOB_INT4_F32, N, K, acc, y, pack, scales, x, NULL, NULL, 0};
+    run_job(&j, threads);
+}

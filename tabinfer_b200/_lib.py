@@ -26,6 +26,12 @@ SIGNATURES = {
     "tb_last_error": [P],
     "tb_ctx_synchronize": [P],
     "tb_ctx_device_error": [P, ctypes.POINTER(I32)],
+    "tb_batch_begin": [P],
+    "tb_batch_end": [P, ctypes.POINTER(P)],
+    "tb_batch_submit": [P, P],
+    "tb_batch_destroy": [P],
+    "tb_copy_h2d": [P, P, P, ctypes.c_size_t],
+    "tb_copy_d2h": [P, P, P, ctypes.c_size_t],
     "tb_quant_int4_g32": [P, P, P, P, I64, I64],
     "tb_quant_q8": [P, P, P, P, P, I64, I64],
     "tb_rmsnorm_q8": [P, P, P, F32, P, P, P, I64, I64],

@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
             const int8_t* vrow = a.Vq + tr * row_elems + hk * HD;
             const uint32_t vw = DPL == 4 ? __ldg(reinterpret_cast<const uint32_t*>(vrow) + lane)
                                          : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(vrow) + lane);
-            const float vs = __ldg(a.Vs + tr * row_groups + hk * NG + (lane * DPL) / 32);
+            const float vs = __ldg(a.Vs + tr * row_groups + hk * NG + (lane * DPL) / 32) * (1.0f / 127.0f);
 #pragma unroll
             for (int h = 0; h < GRP; h++) {
                 const float pw = __shfl_sync(0xffffffffu, pr[h], kk) * vs;

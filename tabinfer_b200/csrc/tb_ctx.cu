@@ -124,6 +124,71 @@ TB_API int tb_ctx_synchronize(tb_ctx* ctx)
     return TB_OK;
 }
 
+struct tb_batch {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+TB_API int tb_batch_begin(tb_ctx* ctx)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, ctx->stream == ctx->own_stream, "recording needs the context's own stream");
+    cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "begin capture: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_batch_end(tb_ctx* ctx, tb_batch** out)
+{
+    if (!ctx || !out) return TB_ERR_INVALID;
+    *out = nullptr;
+    tb_batch* b = new (std::nothrow) tb_batch();
+    if (!b) return TB_ERR_NOMEM;
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &b->graph);
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&b->exec, b->graph, 0);
+    if (e != cudaSuccess) {
+        if (b->graph) cudaGraphDestroy(b->graph);
+        delete b;
+        cudaGetLastError();
+        return tb_fail(ctx, TB_ERR_CUDA, "end capture: %s", cudaGetErrorString(e));
+    }
+    *out = b;
+    return TB_OK;
+}
+
+TB_API int tb_batch_submit(tb_ctx* ctx, tb_batch* b)
+{
+    if (!ctx || !b) return TB_ERR_INVALID;
+    cudaError_t e = cudaGraphLaunch(b->exec, ctx->stream);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "batch submit: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_batch_destroy(tb_batch* b)
+{
+    if (!b) return TB_OK;
+    if (b->exec) cudaGraphExecDestroy(b->exec);
+    if (b->graph) cudaGraphDestroy(b->graph);
+    delete b;
+    return TB_OK;
+}
+
+TB_API int tb_copy_h2d(tb_ctx* ctx, void* dst, const void* src, size_t bytes)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "h2d copy: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_copy_d2h(tb_ctx* ctx, void* dst, const void* src, size_t bytes)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "d2h copy: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
 TB_API int tb_ctx_device_error(tb_ctx* ctx, int* code)
 {
     if (!ctx || !code) return TB_ERR_INVALID;

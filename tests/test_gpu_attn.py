@@ -3,15 +3,17 @@
 
 Bars: V quantize-write bit-exact (raw input); K (after norm+RoPE) within one
 int8 step, only at rounding ties; q RoPE output within 1e-5 of the f64 oracle;
-attention output within 1e-4 relative per head row of the f64 oracle for every
-split count (uneven and empty splits included); argmax ids exact."""
+attention output of each q head within 1e-4 of that head row's largest
+magnitude (max|got-ref| / max|ref|, f32 accumulation over S keys) against the
+f64 oracle, for every split count (uneven and empty splits included); argmax
+ids exact."""
 import numpy as np
 import pytest
 import torch
 
 import oracle
 import tabinfer_b200 as tb
-from helpers import host, row_rel_err, u16_dev
+from helpers import host, u16_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -35,6 +37,12 @@ def _filled_cache(S, nKv, hd, seed):
 
 def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def head_rel_err(got, ref, hd):
+    got = np.asarray(got, np.float64).reshape(-1, hd)
+    ref = np.asarray(ref, np.float64).reshape(-1, hd)
+    return float(np.max(np.abs(got - ref).max(1) / np.abs(ref).max(1)))
 
 
 @pytest.mark.parametrize("pos", [0, 17, 4095, 32767])
@@ -88,7 +96,7 @@ def test_decode_attention_splits(cuda, S, nsplit):
     q = np.random.default_rng(S + 1).normal(0, 1, nHq * hd).astype(np.float32)
     out = tb.attention_decode_q8(_dev(q), (_dev(Kq), _dev(Ks), _dev(Vq), _dev(Vs)), S, nHq, nKv, hd, nsplit)
     ref = oracle.attn_decode_q8(q, Kq, Ks, Vq, Vs, S, nHq, nKv, hd)
-    assert row_rel_err(host(out), ref) < 1e-4
+    assert head_rel_err(host(out), ref, hd) < 1e-4
 
 
 @pytest.mark.parametrize("nHq,nKv,hd", [(8, 8, 64), (16, 4, 128), (32, 4, 64), (8, 1, 128)])
@@ -98,7 +106,7 @@ def test_decode_attention_head_layouts(cuda, nHq, nKv, hd):
     q = np.random.default_rng(2).normal(0, 1, nHq * hd).astype(np.float32)
     out = tb.attention_decode_q8(_dev(q), (_dev(Kq), _dev(Ks), _dev(Vq), _dev(Vs)), S, nHq, nKv, hd)
     ref = oracle.attn_decode_q8(q, Kq, Ks, Vq, Vs, S, nHq, nKv, hd)
-    assert row_rel_err(host(out), ref) < 1e-4
+    assert head_rel_err(host(out), ref, hd) < 1e-4
 
 
 def test_decode_attention_32k_context(cuda):
@@ -108,7 +116,7 @@ def test_decode_attention_32k_context(cuda):
     q = np.random.default_rng(5).normal(0, 1, nHq * hd).astype(np.float32)
     out = tb.attention_decode_q8(_dev(q), (_dev(Kq), _dev(Ks), _dev(Vq), _dev(Vs)), S, nHq, nKv, hd)
     ref = oracle.attn_decode_q8(q, Kq, Ks, Vq, Vs, S, nHq, nKv, hd)
-    assert row_rel_err(host(out), ref) < 1e-4
+    assert head_rel_err(host(out), ref, hd) < 1e-4
 
 
 def test_argmax_reference_selftests(cuda):
