@@ -161,48 +161,35 @@ class ChainRun:
         self.chain, self.B, self.ctx = chain, B, ctx
         z = lambda *s, dt=torch.float32: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
         self.x = z(B, H)
-        self.xq1, self.xs1, self.xsum1 = z(B, H, dt=torch.int8), z(B, H // 32), z(B, H // 16, dt=torch.int32)
         self.q, self.k, self.v = z(B, NHQ * HD), z(B, NKV * HD), z(B, NKV * HD)
-        self.xq2, self.xs2, self.xsum2 = z(B, NHQ * HD, dt=torch.int8), z(B, NHQ * HD // 32), z(B, NHQ * HD // 16, dt=torch.int32)
         self.swi = z(B, INTER)
-        self.xq3, self.xs3, self.xsum3 = z(B, INTER, dt=torch.int8), z(B, INTER // 32), z(B, INTER // 16, dt=torch.int32)
-        self.normed = z(B, H)
         self.logits = z(B, VOCAB)
         self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
         self.batch = None
         self.launches = 0
 
     def step(self):
-        """Issue one step's calls (eager, or under recording)."""
+        """Issue one step's calls (eager, or under recording): 4 fused launches per layer."""
         import tabinfer_b200 as tb
         c = self.chain
         n = 0
         for L in c.layers:
-            tb.rmsnorm_q8(self.x, L["ln1"], 1e-6, self.xq1, self.xs1, self.xsum1)
-            tb.gemv_dp4_multi(self.xq1, self.xs1, [L["q"], L["k"], L["v"]], ys=[self.q, self.k, self.v])
-            tb.quant_q8(self.q, self.xq2, self.xs2, self.xsum2)
-            tb.gemv_dp4(self.xq2, self.xs2, *L["o"], y=self.x, acc=True)
-            tb.rmsnorm_q8(self.x, L["ln2"], 1e-6, self.xq1, self.xs1, self.xsum1)
-            tb.gate_up_silu_dp4(self.xq1, self.xs1, *L["gate"], *L["up"], swi=self.swi)
-            tb.quant_q8(self.swi, self.xq3, self.xs3, self.xsum3)
-            tb.gemv_dp4(self.xq3, self.xs3, *L["down"], y=self.x, acc=True)
-            n += 8
-        tb.rmsnorm(self.x, c.norm, 1e-6, y=self.normed)
+            tb.gemv_dp4a_multi(self.x, [L["q"], L["k"], L["v"]], norm_w=L["ln1"], eps=1e-6, ys=[self.q, self.k, self.v])
+            tb.gemv_dp4a(self.q, *L["o"], y=self.x, acc=True)
+            tb.gate_up_silu_dp4a(self.x, *L["gate"], *L["up"], norm_w=L["ln2"], eps=1e-6, swi=self.swi)
+            tb.gemv_dp4a(self.swi, *L["down"], y=self.x, acc=True)
+            n += 4
         if self.B == 1:
-            tb.gemv_q(self.normed, *c.lm_head, y=self.logits)
-            n += 2
+            tb.gemv_q_norm(self.x, c.norm, 1e-6, *c.lm_head, y=self.logits)
         else:
-            tb.quant_q8(self.normed, self.xq1, self.xs1, self.xsum1)
-            tb.gemv_dp4(self.xq1, self.xs1, *c.lm_head, y=self.logits)
-            n += 3
+            tb.gemv_dp4a(self.x, *c.lm_head, norm_w=c.norm, eps=1e-6, y=self.logits)
         tb.argmax(self.logits, out=self.tok)
-        n += 2
-        self.launches = n
+        self.launches = n + 3
 
     def record(self):
         import torch
         from tabinfer_b200._lib import LIB, P
-        stream = torch.cuda.ExternalStream(LIB.tb_ctx_get_stream(self.ctx.h), device=self.chain.dev)
+        stream = torch.cuda.ExternalStream(self.ctx.own_stream(), device=self.chain.dev)
         self.stream = stream
         with torch.cuda.stream(stream):
             self.step()                      # eager warm-up (sizes any scratch)
@@ -266,31 +253,30 @@ def dominant_kernel_roofline(chain, ctx, peak, reps=3):
     import tabinfer_b200 as tb
     from tabinfer_b200._lib import LIB
     dev = chain.dev
-    s = torch.cuda.ExternalStream(LIB.tb_ctx_get_stream(ctx.h), device=dev)
+    s = torch.cuda.ExternalStream(ctx.own_stream(), device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     B = 1
     x1 = torch.randn(B, H, device=dev)
     x2 = torch.randn(B, NHQ * HD, device=dev)
     x3 = torch.randn(B, INTER, device=dev)
+    ln = chain.layers[0]["ln1"]
     with torch.cuda.stream(s):
-        q1 = tb.quant_q8(x1)
-        q2 = tb.quant_q8(x2)
-        q3 = tb.quant_q8(x3)
         outs = {n: torch.zeros(B, N, device=dev) for n, N, _ in MATS}
         logits = torch.zeros(B, VOCAB, device=dev)
         swi = torch.zeros(B, INTER, device=dev)
         kinds = {
-            "gemv_int4_q8 qkv (4096x1024)": (lambda L: tb.gemv_dp4_multi(q1[0], q1[1], [L["q"], L["k"], L["v"]],
-                                                                          ys=[outs["q"], outs["k"], outs["v"]]),
-                                             gemv_bytes(4096, H, B, 1.125), LAYERS),
-            "gemv_int4_q8 o (1024x2048)": (lambda L: tb.gemv_dp4(q2[0], q2[1], *L["o"], y=outs["o"]),
-                                           gemv_bytes(H, 2048, B, 1.125), LAYERS),
-            "gemv_int4_q8 gate+up+silu (2x3072x1024)": (lambda L: tb.gate_up_silu_dp4(q1[0], q1[1], *L["gate"], *L["up"], swi=swi),
-                                                        2 * wbytes(INTER, H) + B * H * 1.125 + B * INTER * 4, LAYERS),
-            "gemv_int4_q8 down (1024x3072)": (lambda L: tb.gemv_dp4(q3[0], q3[1], *L["down"], y=outs["down"]),
-                                              gemv_bytes(H, INTER, B, 1.125), LAYERS),
-            "gemv_int4_f32 lm_head (151936x1024)": (lambda L: tb.gemv_q(x1, *chain.lm_head, y=logits),
-                                                    gemv_bytes(VOCAB, H, B, 4), 1),
+            "gemv_dp4a rmsnorm+qkv (4096x1024)": (lambda L: tb.gemv_dp4a_multi(x1, [L["q"], L["k"], L["v"]], norm_w=ln,
+                                                                                ys=[outs["q"], outs["k"], outs["v"]]),
+                                                  gemv_bytes(4096, H, B, 1.125), LAYERS),
+            "gemv_dp4a o (1024x2048)": (lambda L: tb.gemv_dp4a(x2, *L["o"], y=outs["o"]),
+                                        gemv_bytes(H, 2048, B, 1.125), LAYERS),
+            "gemv_dp4a rmsnorm+gate+up+silu (2x3072x1024)": (
+                lambda L: tb.gate_up_silu_dp4a(x1, *L["gate"], *L["up"], norm_w=ln, swi=swi),
+                2 * wbytes(INTER, H) + B * H * 1.125 + B * INTER * 4, LAYERS),
+            "gemv_dp4a down (1024x3072)": (lambda L: tb.gemv_dp4a(x3, *L["down"], y=outs["down"]),
+                                           gemv_bytes(H, INTER, B, 1.125), LAYERS),
+            "gemv_f32 rmsnorm+lm_head (151936x1024)": (lambda L: tb.gemv_q_norm(x1, chain.norm, 1e-6, *chain.lm_head, y=logits),
+                                                       gemv_bytes(VOCAB, H, B, 4), 1),
         }
         res = {}
         for name, (fn, nbytes, per_step) in kinds.items():
@@ -407,7 +393,7 @@ def main():
 
     import tabinfer_b200 as tb
     ctx = tb.default_context(local)
-    tb.ops.LIB.tb_ctx_set_stream(ctx.h, None)
+    ctx.own_stream()
     chain = Chain(dev, seed=1000 + rank)
     run = ChainRun(chain, args.batch, ctx)
     run.record()

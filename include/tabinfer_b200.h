@@ -50,7 +50,8 @@ typedef struct tb_ctx tb_ctx;
 TB_API int tb_version(void);
 TB_API int tb_ctx_create(int device, tb_ctx **out);
 TB_API int tb_ctx_destroy(tb_ctx *ctx);
-/* Order all later calls on this stream (a cudaStream_t); NULL = the context's own. */
+/* Order all later calls on this stream (a cudaStream_t); NULL = the context's own
+ * (non-blocking) stream.  To use the legacy default stream pass cudaStreamLegacy. */
 TB_API int tb_ctx_set_stream(tb_ctx *ctx, void *cuda_stream);
 TB_API void *tb_ctx_get_stream(tb_ctx *ctx);
 /* 1 = launch kernels with programmatic dependent launch (default), 0 = plain. */
@@ -134,6 +135,30 @@ TB_API int tb_gemv_int4_q8_multi(tb_ctx *ctx, int count, float *const *ys,
                                  const uint32_t *const *packs, const uint16_t *const *scales,
                                  const int64_t *Ns, const int8_t *xq, const float *xs,
                                  int64_t K, int batch, int acc);
+
+/* ---- fused activation-prep + GEMV (one launch each) ------------------------
+ * The int8 activation is made inside the GEMV from the f32 rows x [batch,K]:
+ * with norm_w16 == NULL it is QUANTQ8 of x, otherwise RMSNORMQ of x (eps),
+ * bit-identical to tb_quant_q8 / tb_rmsnorm_q8 followed by the _q8 GEMV.
+ *   tb_gemv_int4_dp4a        = gemvDP4A (models/qwen3.js:428-431), or
+ *                              rmsnormQ + gemvDP4_only (forward, :3981-3984)
+ *   tb_gemv_int4_dp4a_multi  = rmsnormQ + the q/k/v projGemv triple
+ *   tb_gateup_silu_int4_dp4a = rmsnormQ + gateUpSiluDP4_only (:4023-4024)
+ *   tb_gemv_int4_f32_norm    = rmsnorm + gemvQ for the lm_head (:4037-4049) */
+TB_API int tb_gemv_int4_dp4a(tb_ctx *ctx, float *y, const float *x, const uint16_t *norm_w16, float eps,
+                             const uint32_t *pack, const uint16_t *scales, int64_t N, int64_t K,
+                             int batch, int acc);
+TB_API int tb_gemv_int4_dp4a_multi(tb_ctx *ctx, int count, float *const *ys,
+                                   const uint32_t *const *packs, const uint16_t *const *scales,
+                                   const int64_t *Ns, const float *x, const uint16_t *norm_w16,
+                                   float eps, int64_t K, int batch, int acc);
+TB_API int tb_gateup_silu_int4_dp4a(tb_ctx *ctx, float *swi, const float *x, const uint16_t *norm_w16,
+                                    float eps, const uint32_t *gpack, const uint16_t *gscales,
+                                    const uint32_t *upack, const uint16_t *uscales,
+                                    int64_t I, int64_t H, int batch);
+TB_API int tb_gemv_int4_f32_norm(tb_ctx *ctx, float *y, const float *x, const uint16_t *norm_w16,
+                                 float eps, const uint32_t *pack, const uint16_t *scales,
+                                 int64_t N, int64_t K, int batch, int acc);
 
 /* ---- ternary Q2_0_g64 path (native/crates/n2-kernels) -------------------- */
 

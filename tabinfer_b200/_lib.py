@@ -40,6 +40,10 @@ SIGNATURES = {
     "tb_linear_int4": [P, P, P, P, P, I64, I64, I64, I32],
     "tb_gateup_silu_int4_q8": [P, P, P, P, P, P, P, P, I64, I64, I32],
     "tb_gemv_int4_q8_multi": [P, I32, P, P, P, P, P, P, I64, I32, I32],
+    "tb_gemv_int4_dp4a": [P, P, P, P, F32, P, P, I64, I64, I32, I32],
+    "tb_gemv_int4_dp4a_multi": [P, I32, P, P, P, P, P, P, F32, I64, I32, I32],
+    "tb_gateup_silu_int4_dp4a": [P, P, P, P, F32, P, P, P, P, I64, I64, I32],
+    "tb_gemv_int4_f32_norm": [P, P, P, P, F32, P, P, I64, I64, I32, I32],
     "tb_pack_tern_q2g64": [P, P, P, P, I64, I64],
     "tb_quant_act_q8": [P, P, P, P, P, I64, I64],
     "tb_gemv_tern_q2g64": [P, P, P, P, P, P, I64, I64, I32],

@@ -1,0 +1,778 @@
+// tb_gemv.cu -- HBM-bound int4 G=32 decode GEMVs for 1..8 activation rows.
+//
+// Weight layout is the reference's (models/qwen3.js:263-270): pack u32 [N][K/8],
+// weight k of row n at bits 4*(k%8) of word k/8 as q+8; f16 scales [N][K/32].
+//
+// B200 design
+//  * Work unit = a row block of RB consecutive rows.  Its packed weights
+//    (RB*K/2 bytes) and scales (RB*K/16 bytes) are each ONE contiguous range,
+//    moved into shared memory by a TMA bulk copy (cp.async.bulk, completion on
+//    an mbarrier).  Small matrices get one row block per CTA and ~1-2 CTAs per
+//    SM, so every SM streams; large ones (lm_head) pipeline NST stages per CTA.
+//  * The first stages are requested BEFORE griddepcontrol.wait: with
+//    programmatic dependent launch the weight stream of this kernel overlaps
+//    the tail of the kernel producing its activation.
+//  * The activation (a few KB) is prepared after the wait, per CTA, straight
+//    from the producer's f32 output: optional RMSNorm, then the per-32 int8
+//    quantization of QUANTQ8, with code shared with the standalone kernels so
+//    the int8 values are bit-identical.  It is stored pre-permuted so the
+//    nibble lanes of a weight word meet dp4a byte lanes directly:
+//       sum (nib-8)*x = dp4a(w & 0x0f0f0f0f, x_even) + dp4a((w>>4) & 0x0f0f0f0f, x_odd) - 8*sum(x).
+//  * f32-activation rows (gemvQ) convert nibbles with a byte permute into the
+//    float 2^23+nib and use Blackwell's packed fma.rn.f32x2.
+//  * A warp owns a row of the staged block, its lanes the row's 16-byte groups
+//    (conflict-free shared-memory reads), reduced with a shuffle tree; lane 0
+//    writes (optionally += y, the fused residual; or silu(g)*u for gate/up).
+#include "tb_act.cuh"
+
+namespace {
+
+constexpr int THREADS = 256;
+constexpr int MAX_NST = 4;
+constexpr int SMEM_HDR = 512;   // mbarriers (64 B) + reduction scratch (>= 72 floats)
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr int ERR_WAIT_TIMEOUT = 0x6d01;
+
+enum Kind { KIND_Q8 = 0, KIND_GATEUP = 1, KIND_F32 = 2 };
+enum ActSrc { ACT_PREQ = 0, ACT_F32 = 1, ACT_RMSNORM = 2 };
+
+struct Mat {
+    const uint32_t* pack;
+    const uint16_t* scales;
+    float* y;
+    int N;
+    int rb_begin;   // first row block of this matrix
+};
+
+struct Args {
+    Mat m[4];
+    int count, nrb, RB, K, acc;
+    int act_src;
+    const float* x;        // f32 [B][K] (ACT_F32 / ACT_RMSNORM)
+    const int8_t* xq;      // int8 [B][K]   (ACT_PREQ)
+    const float* xs;       // f32 [B][K/32] (ACT_PREQ)
+    const uint16_t* normw; // f16 [K]       (ACT_RMSNORM)
+    float eps;
+    int nst;
+    int slot_bytes;        // bytes of one matrix's row block in a stage (weights, then scales)
+    int act_bytes;         // staged activation (Q8 or f32 layout)
+    int xbuf_bytes;        // f32 staging of raw rows for the Q8 prologue
+    int* err;
+};
+
+// ---- mbarrier / bulk-copy primitives ------------------------------------------
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(saddr(dst)), "l"(src), "r"(bytes), "r"(saddr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(saddr(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after WAIT_LIMIT polls (each try_wait may suspend briefly).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
+{
+    for (uint32_t i = 0; i < WAIT_LIMIT; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// ---- packed f32x2 arithmetic (sm_100) ------------------------------------------
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
+{
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n mov.b64 rc, {%6,%7};\n"
+        " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0,%1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b)
+{
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
+        " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0,%1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// ---- row-block bookkeeping --------------------------------------------------
+struct Block {
+    int mi, row0, nrows;
+};
+__device__ __forceinline__ Block block_of(const Args& a, int rb, bool gateup)
+{
+    int mi = 0;
+    if (!gateup) {
+#pragma unroll
+        for (int i = 1; i < 4; i++) if (i < a.count && rb >= a.m[i].rb_begin) mi = i;
+    }
+    const Mat& M = a.m[mi];
+    int row0 = (rb - M.rb_begin) * a.RB;
+    return Block{mi, row0, min(a.RB, M.N - row0)};
+}
+
+// Scales of a block travel by bulk copy when their byte count is a multiple of 16.
+__device__ __forceinline__ bool scales_bulk(int nrows, int G) { return ((nrows * G * 2) & 15) == 0; }
+
+__device__ void issue_block(const Args& a, int rb, unsigned char* stage, uint64_t* bar, bool gateup)
+{
+    const int G = a.K >> 5;
+    const Block bl = block_of(a, rb, gateup);
+    const uint32_t wb = (uint32_t)bl.nrows * (a.K >> 1);
+    const uint32_t sb = (uint32_t)bl.nrows * G * 2;
+    const bool sbulk = scales_bulk(bl.nrows, G);
+    const int nm = gateup ? 2 : 1;
+    mbar_expect_tx(bar, nm * (wb + (sbulk ? sb : 0u)));
+    for (int s = 0; s < nm; s++) {
+        const Mat& M = a.m[gateup ? s : bl.mi];
+        unsigned char* dst = stage + s * a.slot_bytes;
+        bulk_g2s(dst, M.pack + (size_t)bl.row0 * (a.K >> 3), wb, bar);
+        if (sbulk) bulk_g2s(dst + (size_t)a.RB * (a.K >> 1), M.scales + (size_t)bl.row0 * G, sb, bar);
+    }
+}
+
+// ---- activation staging -------------------------------------------------------
+// All of an activation row is requested at once (coalesced float4 loads, many in
+// flight per thread) before any of it is used: the prologue costs one memory
+// round trip, not one per 32-group.
+
+// Sum of squares in block256_sumsq's order, reading element i of a row that is
+// stored in the swizzled f32 layout below.
+__device__ __forceinline__ int swz_index(int G, int b, int i)
+{
+    const int f = i >> 2, g = f >> 3, j = f & 7;
+    return ((b * G + g) * 8 + (j ^ (g & 7))) * 4 + (i & 3);
+}
+
+// Q8 layout per (b, g): lo = (e0,o0,e1,o1), hi = (e2,o2,e3,o3) (e_w / o_w = even /
+// odd k of weight word w, one int8 per byte), s8 = 8*sum(x), sf = scale.
+template <int B>
+__device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbuf_floats, float* red)
+{
+    const int G = a.K >> 5;
+    uint4* xlo = reinterpret_cast<uint4*>(act);
+    uint4* xhi = xlo + B * G;
+    int* xs8 = reinterpret_cast<int*>(xhi + B * G);
+    float* xsf = reinterpret_cast<float*>(xs8 + B * G);
+    const int tid = threadIdx.x;
+    if (a.act_src == ACT_PREQ) {
+        for (int i = tid; i < B * G; i += THREADS) {
+            const int b = i / G, g = i - b * G;
+            const uint4* src = reinterpret_cast<const uint4*>(a.xq + (size_t)b * a.K + g * 32);
+            const uint4 p = src[0], q = src[1];
+            const uint32_t w[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+            uint32_t e[4], o[4];
+            int s = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                e[j] = __byte_perm(w[2 * j], w[2 * j + 1], 0x6420);
+                o[j] = __byte_perm(w[2 * j], w[2 * j + 1], 0x7531);
+                s = __dp4a((int)w[2 * j], 0x01010101, s);
+                s = __dp4a((int)w[2 * j + 1], 0x01010101, s);
+            }
+            xlo[i] = make_uint4(e[0], o[0], e[1], o[1]);
+            xhi[i] = make_uint4(e[2], o[2], e[3], o[3]);
+            xs8[i] = 8 * s;
+            xsf[i] = a.xs[(size_t)b * G + g];
+        }
+        return;
+    }
+    // f32 rows -> swizzled shared copy (one burst of loads) -> one thread per (row, group)
+    const int K4 = a.K >> 2;
+    const int rows_per_chunk = max(1, xbuf_floats / a.K);
+    float4* xb4 = reinterpret_cast<float4*>(xbuf);
+    for (int b0 = 0; b0 < B; b0 += rows_per_chunk) {
+        const int nb = min(rows_per_chunk, B - b0);
+        const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)b0 * a.K);
+#pragma unroll 8
+        for (int i = tid; i < nb * K4; i += THREADS) {
+            const int bb = i / K4, f = i - bb * K4, g = f >> 3, j = f & 7;
+            xb4[bb * K4 + g * 8 + (j ^ (g & 7))] = src[i];
+        }
+        __syncthreads();
+        float inv[B];
+#pragma unroll
+        for (int b = 0; b < B; b++) inv[b] = 1.0f;
+        if (a.act_src == ACT_RMSNORM) {
+            float ss[B];
+            block256_sumsq_rows<B>([&](int bb, int i) {
+                return bb < nb ? xbuf[bb * a.K + swz_index(G, 0, i)] : 0.0f;
+            }, a.K, red, ss);
+#pragma unroll
+            for (int b = 0; b < B; b++) inv[b] = rms_inv(ss[b], a.K, a.eps);
+        }
+        for (int item = tid; item < nb * G; item += THREADS) {
+            const int bb = item / G, g = item - bb * G;
+            const float4* xg = xb4 + bb * K4 + g * 8;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float4 t = xg[j ^ (g & 7)];
+                v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+            }
+            if (a.act_src == ACT_RMSNORM) {
+                float ib = inv[0];
+#pragma unroll
+                for (int b = 1; b < B; b++) if (bb == b) ib = inv[b];
+                const uint4* wq = reinterpret_cast<const uint4*>(a.normw + g * 32);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const uint4 wv = __ldg(wq + j);
+                    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const int k = 8 * j + 2 * h;
+                        v[k] = __fmul_rn(__fmul_rn(v[k], ib), tb_h2f((uint16_t)(ww[h] & 0xffffu)));
+                        v[k + 1] = __fmul_rn(__fmul_rn(v[k + 1], ib), tb_h2f((uint16_t)(ww[h] >> 16)));
+                    }
+                }
+            }
+            float m = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 32; k++) m = fmaxf(m, fabsf(v[k]));
+            const float scale = __fdiv_rn(m, 127.0f);
+            const float is = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+            uint32_t words[8];
+            int sum = 0;
+#pragma unroll
+            for (int wd = 0; wd < 4; wd++) {
+                uint32_t e = 0, o = 0;
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    int qe = max(-127, min(127, __float2int_rn(__fmul_rn(v[8 * wd + 2 * h], is))));
+                    int qo = max(-127, min(127, __float2int_rn(__fmul_rn(v[8 * wd + 2 * h + 1], is))));
+                    sum += qe + qo;
+                    e |= ((uint32_t)qe & 0xffu) << (8 * h);
+                    o |= ((uint32_t)qo & 0xffu) << (8 * h);
+                }
+                words[2 * wd] = e;
+                words[2 * wd + 1] = o;
+            }
+            const int i = (b0 + bb) * G + g;
+            xlo[i] = make_uint4(words[0], words[1], words[2], words[3]);
+            xhi[i] = make_uint4(words[4], words[5], words[6], words[7]);
+            xs8[i] = 8 * sum;
+            xsf[i] = scale;
+        }
+        __syncthreads();   // xbuf is reused by the next chunk
+    }
+}
+
+// F32 layout: per (b, g) 8 float4, float4 index XOR-swizzled by (g & 7).
+template <int B>
+__device__ void stage_f32(const Args& a, unsigned char* act, float* red)
+{
+    const int G = a.K >> 5, K4 = a.K >> 2;
+    float4* xsm = reinterpret_cast<float4*>(act);
+    const float4* src = reinterpret_cast<const float4*>(a.x);
+#pragma unroll 8
+    for (int i = threadIdx.x; i < B * K4; i += THREADS) {
+        const int b = i / K4, f = i - b * K4, g = f >> 3, j = f & 7;
+        xsm[(b * G + g) * 8 + (j ^ (g & 7))] = src[i];
+    }
+    __syncthreads();
+    if (a.act_src != ACT_RMSNORM) return;
+    float* xf = reinterpret_cast<float*>(act);
+    float ss[B];
+    block256_sumsq_rows<B>([&](int b, int i) { return xf[swz_index(G, b, i)]; }, a.K, red, ss);
+    for (int i = threadIdx.x; i < B * a.K; i += THREADS) {
+        const int b = i / a.K, k = i - b * a.K;
+        float inv = rms_inv(ss[0], a.K, a.eps);
+#pragma unroll
+        for (int bb = 1; bb < B; bb++) if (b == bb) inv = rms_inv(ss[bb], a.K, a.eps);
+        float* p = xf + swz_index(G, b, k);
+        *p = __fmul_rn(__fmul_rn(*p, inv), tb_h2f(a.normw[k]));
+    }
+    __syncthreads();
+}
+
+// ---- per-item math ----------------------------------------------------------------
+template <int B>
+__device__ __forceinline__ void item_q8(const uint4 w, const float s, const unsigned char* act, int G, int g, float* acc)
+{
+    const uint4* xlo = reinterpret_cast<const uint4*>(act);
+    const uint4* xhi = xlo + B * G;
+    const int* xs8 = reinterpret_cast<const int*>(xhi + B * G);
+    const float* xsf = reinterpret_cast<const float*>(xs8 + B * G);
+    const uint32_t l0 = w.x & 0x0f0f0f0fu, h0 = (w.x >> 4) & 0x0f0f0f0fu;
+    const uint32_t l1 = w.y & 0x0f0f0f0fu, h1 = (w.y >> 4) & 0x0f0f0f0fu;
+    const uint32_t l2 = w.z & 0x0f0f0f0fu, h2 = (w.z >> 4) & 0x0f0f0f0fu;
+    const uint32_t l3 = w.w & 0x0f0f0f0fu, h3 = (w.w >> 4) & 0x0f0f0f0fu;
+#pragma unroll
+    for (int b = 0; b < B; b++) {
+        const int i = b * G + g;
+        const uint4 xl = xlo[i], xh = xhi[i];
+        int d = -xs8[i];
+        d = __dp4a((int)l0, (int)xl.x, d);
+        d = __dp4a((int)h0, (int)xl.y, d);
+        d = __dp4a((int)l1, (int)xl.z, d);
+        d = __dp4a((int)h1, (int)xl.w, d);
+        d = __dp4a((int)l2, (int)xh.x, d);
+        d = __dp4a((int)h2, (int)xh.y, d);
+        d = __dp4a((int)l3, (int)xh.z, d);
+        d = __dp4a((int)h3, (int)xh.w, d);
+        acc[b] = fmaf(s * xsf[i], (float)d, acc[b]);
+    }
+}
+
+// One weight word (8 nibbles, k = 8wi..8wi+7) against x[k..k+7] = (xa, xb).
+__device__ __forceinline__ float2 word_f32(uint32_t word, float4 xa, float4 xb, float2 d)
+{
+    const float2 M2 = make_float2(-8388616.0f, -8388616.0f);   // -(2^23 + 8)
+    const uint32_t lo = word & 0x0f0f0f0fu, hi = (word >> 4) & 0x0f0f0f0fu;
+    // 0x4B0000nn is the float 2^23 + nn; adding -(2^23+8) leaves nn - 8 exactly
+    const float2 n01 = fadd2(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540)),
+                                         __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540))), M2);
+    const float2 n23 = fadd2(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7541)),
+                                         __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7541))), M2);
+    const float2 n45 = fadd2(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7542)),
+                                         __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7542))), M2);
+    const float2 n67 = fadd2(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7543)),
+                                         __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7543))), M2);
+    d = ffma2(n01, make_float2(xa.x, xa.y), d);
+    d = ffma2(n23, make_float2(xa.z, xa.w), d);
+    d = ffma2(n45, make_float2(xb.x, xb.y), d);
+    d = ffma2(n67, make_float2(xb.z, xb.w), d);
+    return d;
+}
+
+template <int B>
+__device__ __forceinline__ void item_f32(const uint4 w, const float s, const unsigned char* act, int G, int g, float* acc)
+{
+    const float4* xsm = reinterpret_cast<const float4*>(act);
+    const int sw = g & 7;
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int b = 0; b < B; b++) {
+        const float4* xr = xsm + (b * G + g) * 8;
+        float2 d = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int wi = 0; wi < 4; wi++) d = word_f32(ww[wi], xr[(2 * wi) ^ sw], xr[(2 * wi + 1) ^ sw], d);
+        acc[b] = fmaf(s, d.x + d.y, acc[b]);
+    }
+}
+
+// ---- the kernel -----------------------------------------------------------------
+// Consumer mapping: warp w takes rows w, w+8, ... of the staged row block; lane l
+// takes groups l, l+32, ... of the row (consecutive 16-byte items: conflict-free
+// shared-memory reads); the 32 partial sums of a row meet in a shuffle tree.
+template <int B, int KIND>
+__global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
+{
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    float* red = reinterpret_cast<float*>(smem + 64);
+    __shared__ int abort_flag;
+    unsigned char* act = smem + SMEM_HDR;
+    float* xbuf = reinterpret_cast<float*>(act + a.act_bytes);
+    unsigned char* stages = act + a.act_bytes + a.xbuf_bytes;
+    constexpr bool gateup = KIND == KIND_GATEUP;
+    constexpr int NM = gateup ? 2 : 1;
+    const int stage_bytes = NM * a.slot_bytes;
+    const int G = a.K >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+
+    // ---- prologue (independent of earlier kernels): barriers + first weight stages
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < a.nst; s++) mbar_init(&bars[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int j = 0; j < a.nst; j++) {
+            const int rb = blockIdx.x + j * gridDim.x;
+            if (rb >= a.nrb) break;
+            issue_block(a, rb, stages + j * stage_bytes, &bars[j], gateup);
+        }
+    }
+    __syncthreads();
+
+    // ---- wait for the producer of the activation, then prepare it
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    if (KIND == KIND_F32) stage_f32<B>(a, act, red);
+    else stage_q8<B>(a, act, xbuf, a.xbuf_bytes >> 2, red);
+    __syncthreads();
+
+    // f32 activation of a single row kept in registers (groups lane, lane+32),
+    // un-swizzled on the way in so every register index is static
+    constexpr bool XREG = KIND == KIND_F32 && B == 1;
+    float4 xr0[8], xr1[8];
+    if (XREG && G <= 64) {
+        const float4* xsm = reinterpret_cast<const float4*>(act);
+        if (lane < G) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) xr0[j] = xsm[lane * 8 + (j ^ (lane & 7))];
+        }
+        if (lane + 32 < G) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) xr1[j] = xsm[(lane + 32) * 8 + (j ^ (lane & 7))];
+        }
+    }
+
+    for (int j = 0;; j++) {
+        const int rb = blockIdx.x + j * gridDim.x;
+        if (rb >= a.nrb) break;
+        const int st = j % a.nst;
+        const Block bl = block_of(a, rb, gateup);
+        if (!mbar_wait(&bars[st], (uint32_t)((j / a.nst) & 1))) {
+            abort_flag = 1;
+            if (a.err) atomicExch(a.err, ERR_WAIT_TIMEOUT);
+        }
+        const unsigned char* stg = stages + st * stage_bytes;
+        const bool sbulk = scales_bulk(bl.nrows, G);
+        if (!abort_flag) {
+            for (int r = wid; r < bl.nrows; r += THREADS / 32) {
+                float acc[NM][B];
+#pragma unroll
+                for (int s = 0; s < NM; s++)
+#pragma unroll
+                    for (int b = 0; b < B; b++) acc[s][b] = 0.0f;
+#pragma unroll
+                for (int s = 0; s < NM; s++) {
+                    const unsigned char* slot = stg + s * a.slot_bytes;
+                    const uint4* wrow = reinterpret_cast<const uint4*>(slot) + (size_t)r * G;
+                    const uint16_t* srow = sbulk ? reinterpret_cast<const uint16_t*>(slot + (size_t)a.RB * (a.K >> 1)) + (size_t)r * G
+                                                 : a.m[gateup ? s : bl.mi].scales + (size_t)(bl.row0 + r) * G;
+                    if (XREG && G <= 64) {
+                        if (lane < G) {
+                            const uint4 w = wrow[lane];
+                            float2 d = make_float2(0.0f, 0.0f);
+                            d = word_f32(w.x, xr0[0], xr0[1], d);
+                            d = word_f32(w.y, xr0[2], xr0[3], d);
+                            d = word_f32(w.z, xr0[4], xr0[5], d);
+                            d = word_f32(w.w, xr0[6], xr0[7], d);
+                            acc[s][0] = fmaf(tb_h2f(srow[lane]), d.x + d.y, acc[s][0]);
+                        }
+                        if (lane + 32 < G) {
+                            const uint4 w = wrow[lane + 32];
+                            float2 d = make_float2(0.0f, 0.0f);
+                            d = word_f32(w.x, xr1[0], xr1[1], d);
+                            d = word_f32(w.y, xr1[2], xr1[3], d);
+                            d = word_f32(w.z, xr1[4], xr1[5], d);
+                            d = word_f32(w.w, xr1[6], xr1[7], d);
+                            acc[s][0] = fmaf(tb_h2f(srow[lane + 32]), d.x + d.y, acc[s][0]);
+                        }
+                    } else {
+                        for (int g = lane; g < G; g += 32) {
+                            const uint4 w = wrow[g];
+                            const float sc = tb_h2f(srow[g]);
+                            if (KIND == KIND_F32) item_f32<B>(w, sc, act, G, g, acc[s]);
+                            else item_q8<B>(w, sc, act, G, g, acc[s]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int s = 0; s < NM; s++)
+#pragma unroll
+                    for (int b = 0; b < B; b++) acc[s][b] = warp_sum(acc[s][b]);
+                if (lane == 0) {
+                    const int row = bl.row0 + r;
+                    if (gateup) {
+                        const int N = a.m[0].N;
+#pragma unroll
+                        for (int b = 0; b < B; b++) {
+                            const float g = acc[0][b], u = acc[NM - 1][b];
+                            a.m[0].y[(size_t)b * N + row] = __fdiv_rn(g, 1.0f + expf(-g)) * u;
+                        }
+                    } else {
+                        const Mat& M = a.m[bl.mi];
+#pragma unroll
+                        for (int b = 0; b < B; b++) {
+                            float* yp = M.y + (size_t)b * M.N + row;
+                            *yp = (a.acc ? *yp : 0.0f) + acc[0][b];
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();   // stage st fully consumed
+        if (abort_flag) break;
+        if (tid == 0) {
+            const int nrb2 = blockIdx.x + (j + a.nst) * gridDim.x;
+            if (nrb2 < a.nrb) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_block(a, nrb2, stages + st * stage_bytes, &bars[st], gateup);
+            }
+        }
+    }
+    if (abort_flag && tid == 0) {
+        // let copies still in flight land before the CTA's shared memory is released
+        for (int s = 0; s < a.nst; s++) { mbar_wait(&bars[s], 0); mbar_wait(&bars[s], 1); }
+    }
+}
+
+// ---- host side ------------------------------------------------------------------
+struct Plan {
+    int RB, nst, slot_bytes, act_bytes, xbuf_bytes, smem, grid, nrb;
+};
+
+int act_bytes_for(int kind, int B, int G) { return kind == KIND_F32 ? B * G * 128 : B * G * 40; }
+
+int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count, Plan& p)
+{
+    const int G = K / 32;
+    const int nm = kind == KIND_GATEUP ? 2 : 1;
+    const int mats = kind == KIND_GATEUP ? 1 : count;
+    long long rows = 0;
+    for (int i = 0; i < mats; i++) rows += Ns[i];
+    p.act_bytes = (act_bytes_for(kind, B, G) + 127) & ~127;
+    // f32 staging buffer for the Q8 prologue (whole rows, up to 48 KB)
+    p.xbuf_bytes = kind == KIND_F32 ? 0 : std::min(B * K * 4, std::max(48 * 1024, K * 4));
+    p.xbuf_bytes = (p.xbuf_bytes + 127) & ~127;
+    const int target = 2 * ctx->num_sms;
+    const int budget = 112 * 1024;   // leave room for the next kernel's CTA under PDL
+    int RB = 8;
+    while (RB < 64 && rows / (2 * RB) >= target) RB *= 2;
+    for (;; RB /= 2) {
+        const int wb = RB * (K / 2), sb = RB * G * 2;
+        p.slot_bytes = (wb + sb + 127) & ~127;
+        const int per_stage = nm * p.slot_bytes;
+        int nrb = 0;
+        for (int i = 0; i < mats; i++) nrb += tb_cdiv(Ns[i], RB);
+        const int blocks_per_cta = tb_cdiv(nrb, target);
+        int nst = std::min(MAX_NST, std::max(1, blocks_per_cta));
+        const int fixed = SMEM_HDR + p.act_bytes + p.xbuf_bytes;
+        while (nst > 1 && fixed + nst * per_stage > budget) nst--;
+        p.smem = fixed + nst * per_stage;
+        if (p.smem <= 200 * 1024 || RB == 8) {
+            p.RB = RB;
+            p.nst = nst;
+            p.nrb = nrb;
+            break;
+        }
+    }
+    if (p.smem > 220 * 1024)
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "K=%d batch=%d needs %d bytes of shared memory", K, B, p.smem);
+    int occ = p.smem <= 100 * 1024 ? 2 : 1;
+    p.grid = std::min(p.nrb, ctx->num_sms * occ);
+    return TB_OK;
+}
+
+template <int B, int KIND>
+int launch_B(tb_ctx* ctx, Args& a, const Plan& p)
+{
+    auto kern = k_gemv<B, KIND>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    e = tb_launch(ctx, kern, dim3(p.grid), dim3(THREADS), (size_t)p.smem, a);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+template <int KIND>
+int launch_kind(tb_ctx* ctx, Args& a, const Plan& p, int B)
+{
+    switch (B) {
+    case 1: return launch_B<1, KIND>(ctx, a, p);
+    case 2: return launch_B<2, KIND>(ctx, a, p);
+    case 3: return launch_B<3, KIND>(ctx, a, p);
+    case 4: return launch_B<4, KIND>(ctx, a, p);
+    case 5: return launch_B<5, KIND>(ctx, a, p);
+    case 6: return launch_B<6, KIND>(ctx, a, p);
+    case 7: return launch_B<7, KIND>(ctx, a, p);
+    case 8: return launch_B<8, KIND>(ctx, a, p);
+    }
+    return tb_fail(ctx, TB_ERR_INVALID, "batch must be 1..8 (got %d)", B);
+}
+
+int check_mat(tb_ctx* ctx, const uint32_t* pack, const uint16_t* scales, const float* y, int64_t N, int64_t K)
+{
+    TB_REQUIRE(ctx, pack && scales && y, "null weight or output pointer");
+    TB_REQUIRE(ctx, N > 0 && N < (1LL << 30), "N out of range (%lld)", (long long)N);
+    TB_REQUIRE(ctx, TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 16), "pack and scales must be 16-byte aligned");
+    return TB_OK;
+}
+
+struct ActIn {
+    int src;
+    const float* x;
+    const int8_t* xq;
+    const float* xs;
+    const uint16_t* normw;
+    float eps;
+};
+
+int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* const* packs,
+        const uint16_t* const* scales, const int64_t* Ns, const ActIn& in, int64_t K, int batch, int acc)
+{
+    TB_REQUIRE(ctx, K > 0 && K % 32 == 0 && K <= 16384, "K must be a multiple of 32 in [32, 16384] (got %lld)", (long long)K);
+    TB_REQUIRE(ctx, batch >= 1 && batch <= 8, "batch must be 1..8 (got %d)", batch);
+    TB_REQUIRE(ctx, count >= 1 && count <= 4, "count must be 1..4");
+    if (in.src == ACT_PREQ) {
+        TB_REQUIRE(ctx, in.xq && in.xs && TB_ALIGNED(in.xq, 16), "xq (16-byte aligned) and xs required");
+    } else {
+        TB_REQUIRE(ctx, in.x && TB_ALIGNED(in.x, 16), "x must be non-null and 16-byte aligned");
+        TB_REQUIRE(ctx, in.src != ACT_RMSNORM || in.normw, "norm weight required");
+    }
+    Args a{};
+    a.count = count;
+    a.K = (int)K;
+    a.acc = acc ? 1 : 0;
+    a.act_src = in.src;
+    a.x = in.x;
+    a.xq = in.xq;
+    a.xs = in.xs;
+    a.normw = in.normw;
+    a.eps = in.eps;
+    a.err = ctx->dev_error;
+    for (int i = 0; i < count; i++) {
+        int rc = check_mat(ctx, packs[i], scales[i], ys[i], Ns[i], K);
+        if (rc) return rc;
+    }
+    if (kind == KIND_GATEUP) TB_REQUIRE(ctx, Ns[0] == Ns[1], "gate and up must have the same rows");
+    // f32 rows take 4 bytes per element of shared memory: split big batches
+    // into launches of rows that fit (each launch covers its own rows of y).
+    const int bmax = kind == KIND_F32 ? std::max(1, (int)((96 * 1024) / (K * 4))) : 8;
+    if (batch > bmax) {
+        for (int b0 = 0; b0 < batch; b0 += bmax) {
+            const int nb = std::min(bmax, batch - b0);
+            float* ys2[4];
+            for (int i = 0; i < count; i++) ys2[i] = ys[i] + (size_t)b0 * Ns[i];
+            ActIn in2 = in;
+            if (in2.x) in2.x += (size_t)b0 * K;
+            int rc = run(ctx, kind, count, ys2, packs, scales, Ns, in2, K, nb, acc);
+            if (rc) return rc;
+        }
+        return TB_OK;
+    }
+    Plan p{};
+    int rc = make_plan(ctx, kind, batch, (int)K, Ns, count, p);
+    if (rc) return rc;
+    int rb = 0;
+    for (int i = 0; i < 4; i++) {
+        if (i < count) {
+            a.m[i] = Mat{packs[i], scales[i], ys[i], (int)Ns[i], rb};
+            if (kind != KIND_GATEUP) rb += tb_cdiv(Ns[i], p.RB);
+        } else {
+            a.m[i] = Mat{nullptr, nullptr, nullptr, 0, 1 << 30};
+        }
+    }
+    if (kind == KIND_GATEUP) a.m[1].rb_begin = 0;
+    a.nrb = p.nrb;
+    a.RB = p.RB;
+    a.nst = p.nst;
+    a.slot_bytes = p.slot_bytes;
+    a.act_bytes = p.act_bytes;
+    a.xbuf_bytes = p.xbuf_bytes;
+    switch (kind) {
+    case KIND_Q8: return launch_kind<KIND_Q8>(ctx, a, p, batch);
+    case KIND_GATEUP: return launch_kind<KIND_GATEUP>(ctx, a, p, batch);
+    default: return launch_kind<KIND_F32>(ctx, a, p, batch);
+    }
+}
+
+ActIn act_f32(const float* x, const uint16_t* normw, float eps)
+{
+    return ActIn{normw ? ACT_RMSNORM : ACT_F32, x, nullptr, nullptr, normw, eps};
+}
+ActIn act_preq(const int8_t* xq, const float* xs) { return ActIn{ACT_PREQ, nullptr, xq, xs, nullptr, 0.0f}; }
+
+}  // namespace
+
+// shared with tb_linear.cu
+int tb_gemv_q8_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                    const uint16_t* const* scales, const int64_t* Ns, const int8_t* xq, const float* xs,
+                    int64_t K, int batch, int acc)
+{
+    return run(ctx, KIND_Q8, count, ys, packs, scales, Ns, act_preq(xq, xs), K, batch, acc);
+}
+int tb_gemv_dp4a_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                      const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
+                      float eps, int64_t K, int batch, int acc)
+{
+    return run(ctx, KIND_Q8, count, ys, packs, scales, Ns, act_f32(x, normw, eps), K, batch, acc);
+}
+int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
+                     int64_t N, int64_t K, int batch, int acc)
+{
+    return run(ctx, KIND_F32, 1, &y, &pack, &scales, &N, act_f32(x, nullptr, 0.0f), K, batch, acc);
+}
+
+extern "C" {
+
+TB_API int tb_gemv_int4_q8(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                           const uint16_t* scales, int64_t N, int64_t K, int batch, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return run(ctx, KIND_Q8, 1, &y, &pack, &scales, &N, act_preq(xq, xs), K, batch, acc);
+}
+
+TB_API int tb_gemv_int4_q8_multi(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                                 const uint16_t* const* scales, const int64_t* Ns, const int8_t* xq,
+                                 const float* xs, int64_t K, int batch, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, ys && packs && scales && Ns, "null array");
+    return run(ctx, KIND_Q8, count, ys, packs, scales, Ns, act_preq(xq, xs), K, batch, acc);
+}
+
+TB_API int tb_gemv_int4_f32(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
+                            int64_t N, int64_t K, int batch, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return run(ctx, KIND_F32, 1, &y, &pack, &scales, &N, act_f32(x, nullptr, 0.0f), K, batch, acc);
+}
+
+TB_API int tb_gemv_int4_f32_norm(tb_ctx* ctx, float* y, const float* x, const uint16_t* norm_w16, float eps,
+                                 const uint32_t* pack, const uint16_t* scales, int64_t N, int64_t K, int batch,
+                                 int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return run(ctx, KIND_F32, 1, &y, &pack, &scales, &N, act_f32(x, norm_w16, eps), K, batch, acc);
+}
+
+TB_API int tb_gateup_silu_int4_q8(tb_ctx* ctx, float* swi, const int8_t* xq, const float* xs, const uint32_t* gpack,
+                                  const uint16_t* gscales, const uint32_t* upack, const uint16_t* uscales, int64_t I,
+                                  int64_t H, int batch)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    float* ys[2] = {swi, swi};
+    const uint32_t* packs[2] = {gpack, upack};
+    const uint16_t* scs[2] = {gscales, uscales};
+    int64_t Ns[2] = {I, I};
+    return run(ctx, KIND_GATEUP, 2, ys, packs, scs, Ns, act_preq(xq, xs), H, batch, 0);
+}
+
+TB_API int tb_gemv_int4_dp4a(tb_ctx* ctx, float* y, const float* x, const uint16_t* norm_w16, float eps,
+                             const uint32_t* pack, const uint16_t* scales, int64_t N, int64_t K, int batch, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return run(ctx, KIND_Q8, 1, &y, &pack, &scales, &N, act_f32(x, norm_w16, eps), K, batch, acc);
+}
+
+TB_API int tb_gemv_int4_dp4a_multi(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                                   const uint16_t* const* scales, const int64_t* Ns, const float* x,
+                                   const uint16_t* norm_w16, float eps, int64_t K, int batch, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, ys && packs && scales && Ns, "null array");
+    return run(ctx, KIND_Q8, count, ys, packs, scales, Ns, act_f32(x, norm_w16, eps), K, batch, acc);
+}
+
+TB_API int tb_gateup_silu_int4_dp4a(tb_ctx* ctx, float* swi, const float* x, const uint16_t* norm_w16, float eps,
+                                    const uint32_t* gpack, const uint16_t* gscales, const uint32_t* upack,
+                                    const uint16_t* uscales, int64_t I, int64_t H, int batch)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    float* ys[2] = {swi, swi};
+    const uint32_t* packs[2] = {gpack, upack};
+    const uint16_t* scs[2] = {gscales, uscales};
+    int64_t Ns[2] = {I, I};
+    return run(ctx, KIND_GATEUP, 2, ys, packs, scs, Ns, act_f32(x, norm_w16, eps), H, batch, 0);
+}
+
+}  // extern "C"

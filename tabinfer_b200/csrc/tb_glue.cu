@@ -1,5 +1,5 @@
 // tb_glue.cu -- decode-step glue: argmax, RMSNorm, embedding gather.
-#include "tb_common.cuh"
+#include "tb_act.cuh"
 
 namespace {
 
@@ -70,27 +70,17 @@ __global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p2(const unsigned long 
     if (threadIdx.x == 0) out[row] = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
 }
 
-// RMSNorm, qwen3.js:60-88: one CTA per row.
+// RMSNorm, qwen3.js:60-88: one 256-thread CTA per row (the reduction the
+// fused lm_head prologue uses too, tb_act.cuh).
 __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const uint16_t* __restrict__ w16,
                                                  float* __restrict__ y, int H, float eps)
 {
     __shared__ float red[32];
     tb_pdl_wait();
     tb_pdl_trigger();
-    const int row = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int row = blockIdx.x;
     const float* xr = x + (long long)row * H;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) { float v = xr[i]; ss = fmaf(v, v, ss); }
-    ss = warp_sum(ss);
-    if (lane == 0) red[wid] = ss;
-    __syncthreads();
-    if (wid == 0) {
-        float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) red[0] = t;
-    }
-    __syncthreads();
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], (float)H), eps)));
+    const float inv = rms_inv(block256_sumsq(xr, H, red), H, eps);
     for (int i = threadIdx.x; i < H; i += blockDim.x)
         y[(long long)row * H + i] = __fmul_rn(__fmul_rn(xr[i], inv), tb_h2f(w16[i]));
 }

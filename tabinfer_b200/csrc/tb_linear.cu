@@ -4,12 +4,11 @@
 // (native/crates/n2-core/src/model.rs:316-339).
 #include "tb_common.cuh"
 
-int tb_gemv_q8_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
-                    const uint16_t* const* scales, const int64_t* Ns, const int8_t* xq, const float* xs,
-                    int64_t K, int batch, int acc);
+int tb_gemv_dp4a_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                      const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
+                      float eps, int64_t K, int batch, int acc);
 int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
                      int64_t N, int64_t K, int batch, int acc);
-int tb_quant_q8_impl(tb_ctx* ctx, const float* x, int8_t* xq, float* xs, int32_t* xsum16, int64_t T, int64_t K);
 int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,
                       const int32_t* xsum, int64_t N, int64_t K, int batch, const float* act_scale);
 int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K);
@@ -28,14 +27,8 @@ TB_API int tb_linear_int4(tb_ctx* ctx, float* y, const float* x, const uint32_t*
     if (T > 8)
         return tb_fail(ctx, TB_ERR_UNSUPPORTED, "linear_int4: T=%lld > 8 is the prefill GEMM (tb_gemm_int4_g32)",
                        (long long)T);
-    size_t xq_b = up256((size_t)T * K), xs_b = up256((size_t)T * (K / 32) * 4);
-    unsigned char* scr = static_cast<unsigned char*>(tb_ctx_scratch(ctx, xq_b + xs_b));
-    if (!scr) return TB_ERR_NOMEM;
-    int8_t* xq = reinterpret_cast<int8_t*>(scr);
-    float* xs = reinterpret_cast<float*>(scr + xq_b);
-    int rc = tb_quant_q8_impl(ctx, x, xq, xs, nullptr, T, K);
-    if (rc) return rc;
-    return tb_gemv_q8_impl(ctx, 1, &y, &pack, &scales, &N, xq, xs, K, (int)T, acc);
+    // quantQ8 / QUANTQ8T runs inside the GEMV prologue (bit-identical int8 rows)
+    return tb_gemv_dp4a_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
 }
 
 TB_API int tb_linear_tern(tb_ctx* ctx, float* y, const float* x, const uint8_t* codes, const float* scales, int64_t T,

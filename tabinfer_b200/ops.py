@@ -14,6 +14,7 @@ import torch
 from ._lib import LIB, P
 
 TB_ACT_F32, TB_ACT_Q8 = 0, 1
+CUDA_STREAM_LEGACY = 0x1   # cudaStreamLegacy
 
 
 class TabInferError(RuntimeError):
@@ -38,8 +39,16 @@ class Context:
             raise TabInferError("%s: status %d: %s" % (what, rc, msg.decode() if msg else ""))
 
     def bind_stream(self):
+        """Order the library's work on torch's current stream.  torch reports its
+        default (legacy NULL) stream as handle 0, which the C ABI reads as "the
+        context's own stream", so it is passed as cudaStreamLegacy (0x1)."""
         s = torch.cuda.current_stream(self.device).cuda_stream
-        LIB.tb_ctx_set_stream(self.h, P(s))
+        LIB.tb_ctx_set_stream(self.h, P(s if s else CUDA_STREAM_LEGACY))
+
+    def own_stream(self):
+        """Handle of the context's own (non-blocking) stream; binds it."""
+        LIB.tb_ctx_set_stream(self.h, None)
+        return LIB.tb_ctx_get_stream(self.h)
 
     def set_pdl(self, on):
         LIB.tb_ctx_set_pdl(self.h, 1 if on else 0)
@@ -170,6 +179,64 @@ def gemv_dp4_multi(xq, xs, mats, ys=None, acc=False):
                                       ctypes.cast(arr_n, P), _p(xq2), _p(xs), K, B, 1 if acc else 0),
             "gemv_int4_q8_multi")
     return ys
+
+
+def gemv_dp4a(x, pack, scales, norm_w=None, eps=1e-6, y=None, acc=False):
+    """gemvDP4A (qwen3.js:428-431): quantQ8 + gemvDP4 in one launch; with norm_w it is
+    rmsnormQ + gemvDP4_only (forward, qwen3.js:3981-3984)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((B, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_gemv_int4_dp4a(c.h, _p(y), _p(x2), _p(norm_w), float(eps), _p(pack), _p(scales), N, K, B,
+                                  1 if acc else 0), "gemv_int4_dp4a")
+    return y
+
+
+def gemv_dp4a_multi(x, mats, norm_w=None, eps=1e-6, ys=None, acc=False):
+    """rmsnormQ + q/k/v projGemv (qwen3.js:3981-3984) in one launch.  mats: [(pack, scales)]."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    n = len(mats)
+    if ys is None:
+        ys = [torch.zeros((B, p.shape[0]), dtype=torch.float32, device=x.device) for p, _ in mats]
+    arr_y = (P * n)(*[y.data_ptr() for y in ys])
+    arr_p = (P * n)(*[p.data_ptr() for p, _ in mats])
+    arr_s = (P * n)(*[s.data_ptr() for _, s in mats])
+    arr_n = (ctypes.c_int64 * n)(*[p.shape[0] for p, _ in mats])
+    c = _ctx(x)
+    c.check(LIB.tb_gemv_int4_dp4a_multi(c.h, n, ctypes.cast(arr_y, P), ctypes.cast(arr_p, P), ctypes.cast(arr_s, P),
+                                        ctypes.cast(arr_n, P), _p(x2), _p(norm_w), float(eps), K, B,
+                                        1 if acc else 0), "gemv_int4_dp4a_multi")
+    return ys
+
+
+def gate_up_silu_dp4a(x, gpack, gscales, upack, uscales, norm_w=None, eps=1e-6, swi=None):
+    """rmsnormQ + gateUpSiluDP4_only (qwen3.js:4023-4024) in one launch."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, Hd = x2.shape
+    I = gpack.shape[0]
+    if swi is None:
+        swi = torch.empty((B, I), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_gateup_silu_int4_dp4a(c.h, _p(swi), _p(x2), _p(norm_w), float(eps), _p(gpack), _p(gscales),
+                                         _p(upack), _p(uscales), I, Hd, B), "gateup_silu_int4_dp4a")
+    return swi
+
+
+def gemv_q_norm(x, norm_w, eps, pack, scales, y=None, acc=False):
+    """rmsnorm + gemvQ (the final norm + lm_head of forward, qwen3.js:4037-4049) in one launch."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((B, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_gemv_int4_f32_norm(c.h, _p(y), _p(x2), _p(norm_w), float(eps), _p(pack), _p(scales), N, K, B,
+                                      1 if acc else 0), "gemv_int4_f32_norm")
+    return y
 
 
 def gemv_q(x, pack, scales, y=None, acc=False):

@@ -24,6 +24,22 @@ def cuda():
     return torch.device("cuda", 0)
 
 
+@pytest.fixture(autouse=True)
+def _no_device_wait_timeouts(request):
+    """After every GPU test: the device error word that bounded in-kernel waits
+    set must still be clear (a timed-out wait would otherwise only show up as
+    missing output)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    import tabinfer_b200 as tb
+    code = tb.default_context(0).device_error()
+    assert code == 0, "a bounded device-side wait timed out (code 0x%x)" % code
+
+
 @pytest.fixture(scope="session")
 def golden():
     import numpy as np

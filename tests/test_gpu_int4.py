@@ -168,6 +168,64 @@ def test_gateup_silu(cuda, I, H, B):
     assert row_rel_err(host(swi), ref) < TOL
 
 
+@pytest.mark.parametrize("B", [1, 4, 8])
+@pytest.mark.parametrize("K", [1024, 2048, 3072, 6144])
+def test_fused_rmsnorm_quant_gemv(cuda, K, B):
+    """rmsnormQ + projGemv fused: the in-kernel int8 rows equal tb_rmsnorm_q8's, and the
+    outputs match the oracle on those rows (one launch vs two)."""
+    N = 1000
+    pack, sc = _mat(K + B, N, K)
+    rng = np.random.default_rng(K * B)
+    x = rng.normal(0, 2, (B, K)).astype(np.float32)
+    w16 = np.float16(rng.uniform(0.5, 1.5, K)).view(np.uint16)
+    xd, wd = torch.from_numpy(x).cuda(), u16_dev(w16)
+    xq, xs, _ = tb.rmsnorm_q8(xd, wd, 1e-6)
+    y_fused = tb.gemv_dp4a(xd, u32_dev(pack), u16_dev(sc), norm_w=wd, eps=1e-6)
+    y_sep = tb.gemv_dp4(xq, xs, u32_dev(pack), u16_dev(sc))
+    np.testing.assert_array_equal(host(y_fused), host(y_sep))
+    ref = oracle.gemv_int4_q8act(host(xq), host(xs), pack, sc)
+    assert row_rel_err(host(y_fused), ref) < TOL
+    # plain quantQ8 prologue (gemvDP4A)
+    y2 = tb.gemv_dp4a(xd, u32_dev(pack), u16_dev(sc))
+    oq, os_, _ = oracle.quant_q8(x)
+    assert row_rel_err(host(y2), oracle.gemv_int4_q8act(oq, os_, pack, sc)) < TOL
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_fused_multi_and_gateup(cuda, B):
+    H = 2048
+    mats = [_mat(10 + i, n, H) for i, n in enumerate([2048, 1024, 1024])]
+    gp, gs = _mat(20, 6144, H)
+    up, us = _mat(21, 6144, H)
+    rng = np.random.default_rng(B)
+    x = rng.normal(0, 1, (B, H)).astype(np.float32)
+    w16 = np.float16(rng.uniform(0.5, 1.5, H)).view(np.uint16)
+    xd, wd = torch.from_numpy(x).cuda(), u16_dev(w16)
+    xq, xs, _ = tb.rmsnorm_q8(xd, wd, 1e-6)
+    ys = tb.gemv_dp4a_multi(xd, [(u32_dev(p), u16_dev(s)) for p, s in mats], norm_w=wd)
+    for (p, s), y in zip(mats, ys):
+        assert row_rel_err(host(y), oracle.gemv_int4_q8act(host(xq), host(xs), p, s)) < TOL
+    swi = tb.gate_up_silu_dp4a(xd, u32_dev(gp), u16_dev(gs), u32_dev(up), u16_dev(us), norm_w=wd)
+    ref = oracle.gateup_q8act(host(xq), host(xs), gp, gs, up, us)
+    assert row_rel_err(host(swi), ref) < TOL
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_fused_norm_lm_head(cuda, B):
+    """final rmsnorm + gemvQ lm_head in one launch == tb_rmsnorm then gemvQ."""
+    N, K = 20000, 2048
+    pack, sc = _mat(33, N, K)
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 3, (B, K)).astype(np.float32)
+    w16 = np.float16(rng.uniform(0.5, 1.5, K)).view(np.uint16)
+    xd, wd = torch.from_numpy(x).cuda(), u16_dev(w16)
+    normed = tb.rmsnorm(xd, wd, 1e-6)
+    y_sep = tb.gemv_q(normed, u32_dev(pack), u16_dev(sc))
+    y_fused = tb.gemv_q_norm(xd, wd, 1e-6, u32_dev(pack), u16_dev(sc))
+    np.testing.assert_array_equal(host(y_fused), host(y_sep))
+    assert row_rel_err(host(y_fused), oracle.gemv_int4_f32act(host(normed), pack, sc)) < TOL
+
+
 @pytest.mark.parametrize("T,N", [(1, 1024), (1, 20000), (4, 3072), (8, 1024)])
 def test_linear_router(cuda, T, N):
     """linearQ routing (qwen3.js:1597-1608): T=1 N<16384 int8; T=1 N>=16384 f32; T>1 per-token int8."""
@@ -208,6 +266,21 @@ def test_lm_head_full_size_sampled_rows_and_linearity(cuda):
     wp, ws = oracle.quant_int4_g32(host(w[rt].view(torch.int16), np.uint16))
     np.testing.assert_array_equal(wp, p_s)
     np.testing.assert_array_equal(ws, s_s)
+
+
+def test_stream_ordering_with_torch(cuda):
+    """The library's kernels run on torch's current stream: a torch upload, the
+    GEMV and a torch readback issued back to back (no explicit sync) always see
+    each other's results, on the default stream and on a side stream."""
+    pack, sc = _mat(77, 20000, 2048)
+    x = np.random.default_rng(1).normal(0, 1, (8, 2048)).astype(np.float32)
+    ref = oracle.gemv_int4_f32act(x, pack, sc)
+    for stream in (None, torch.cuda.Stream()):
+        ctx_mgr = torch.cuda.stream(stream) if stream is not None else torch.cuda.stream(torch.cuda.current_stream())
+        with ctx_mgr:
+            for _ in range(6):
+                y = tb.gemv_q(torch.from_numpy(x).cuda(), u32_dev(pack), u16_dev(sc))
+                assert row_rel_err(host(y), ref) < TOL
 
 
 def test_bad_shapes_raise(cuda):
