@@ -216,6 +216,20 @@ TB_API int tb_attn_decode_q8(tb_ctx *ctx, float *out, const float *qr,
                              const int8_t *Kq, const float *Ks, const int8_t *Vq, const float *Vs,
                              int64_t S, int64_t nHq, int64_t nKv, int64_t hd, int nsplit);
 
+/* Allocation-free form of tb_attn_decode_q8, for callers that cannot let the
+ * library call cudaMalloc (a process that gives its whole device budget to its
+ * own pool at start-up, or a loop that must not let an allocation synchronize
+ * the device mid-step).  No counterpart in the reference.  The split partials
+ * live in a fixed 1 MiB device array inside the library instead of context
+ * scratch: requests with nHq*nsplit*(hd+2) > 262144 floats are rejected with
+ * TB_ERR_INVALID.  The first call on a device looks up the array's address
+ * (make it before any stream capture); calls share the array, so calls that
+ * overlap on the GPU race and must be ordered by the caller. */
+TB_API int tb_attn_decode_q8_noalloc(tb_ctx *ctx, float *out, const float *qr,
+                                     const int8_t *Kq, const float *Ks, const int8_t *Vq,
+                                     const float *Vs, int64_t S, int64_t nHq, int64_t nKv,
+                                     int64_t hd, int nsplit);
+
 /* ---- decode-step glue ------------------------------------------------------ */
 
 /* Argmax over `rows` rows of n logits -> out_idx[row*stride + offset]

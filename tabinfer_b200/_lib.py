@@ -51,6 +51,7 @@ SIGNATURES = {
     "tb_attn_prep_q8": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, F32, F32],
     "tb_kv_quant_write": [P, P, P, P, P, P, P, I64, I64, I64, I64],
     "tb_attn_decode_q8": [P, P, P, P, P, P, P, I64, I64, I64, I64, I32],
+    "tb_attn_decode_q8_noalloc": [P, P, P, P, P, P, P, I64, I64, I64, I64, I32],
     "tb_argmax": [P, P, I64, I64, P, I64],
     "tb_rmsnorm": [P, P, P, P, I64, I64, F32],
     "tb_embed_gather": [P, P, I64, P, P, I64, I64],

@@ -373,3 +373,75 @@ TB_API int tb_attn_decode_q8(tb_ctx* ctx, float* out, const float* qr, const int
 }
 
 }  // extern "C"
+
+// ---- allocation-free split-KV decode ----------------------------------------------
+// No counterpart in the reference.  tb_attn_decode_q8 keeps its split partials in
+// context scratch, which it allocates with cudaMalloc the first time a size is
+// needed.  Some callers cannot allow that: a serving process that hands its whole
+// device memory budget to its own pool at start-up and forbids later driver
+// allocations, or a host loop that must not let cudaMalloc/cudaFree synchronize
+// the device in the middle of a decode step.  This variant allocates nothing: its
+// partials live in the file-scope array below, sized at NOALLOC_SCRATCH_FLOATS
+// floats (1 MiB), which every GPU that loads this library holds until exit.
+//  * Limit: nHq * nsplit * (hd + 2) <= NOALLOC_SCRATCH_FLOATS (Qwen3-1.7B, 16 q
+//    heads x hd 128, fits up to 126 splits); larger requests are rejected with
+//    TB_ERR_INVALID before anything is enqueued.
+//  * The device address of the array is looked up once per device, on the first
+//    call made on that device (cudaGetSymbolAddress with the device current); make
+//    that first call before any stream capture.
+//  * Every call shares the one array and it keeps the last call's contents.
+//    Nothing needs clearing (each split writes its partial before the combine
+//    reads it), but calls that overlap on the GPU (other streams, other contexts
+//    on the same device) race on it: order them.
+constexpr size_t NOALLOC_SCRATCH_FLOATS = size_t(1) << 18;
+static __device__ __align__(256) float g_attn_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
+
+#include <mutex>
+
+namespace {
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+// Device address of the array on ctx's device (host code may not use the
+// symbol itself as an address).
+int noalloc_scratch(tb_ctx* ctx, float** out)
+{
+    TB_REQUIRE(ctx, ctx->device >= 0 && ctx->device < NOALLOC_MAX_DEVICES, "device index out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[ctx->device]) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaError_t e = cudaSetDevice(ctx->device);
+        void* p = nullptr;
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        cudaSetDevice(prev);
+        if (e != cudaSuccess || !p)
+            return tb_fail(ctx, TB_ERR_CUDA, "cudaGetSymbolAddress(attention scratch): %s", cudaGetErrorString(e));
+        g_noalloc_ptr[ctx->device] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_ptr[ctx->device];
+    return TB_OK;
+}
+}  // namespace
+
+extern "C" TB_API int tb_attn_decode_q8_noalloc(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq,
+                                                const float* Ks, const int8_t* Vq, const float* Vs, int64_t S,
+                                                int64_t nHq, int64_t nKv, int64_t hd, int nsplit)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    int rc = tb_attn_check(ctx, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit);
+    if (rc) return rc;
+    TB_REQUIRE(ctx, out != nullptr, "null output");
+    if (nsplit == 0) nsplit = tb_attn_auto_nsplit(ctx, S, nKv);
+    const size_t need = (size_t)nHq * nsplit * (hd + 2);
+    if (need > NOALLOC_SCRATCH_FLOATS)
+        return tb_fail(ctx, TB_ERR_INVALID,
+                       "attn_decode_q8_noalloc: nHq*nsplit*(hd+2) = %zu floats exceeds the fixed scratch of %zu floats "
+                       "(use fewer splits or tb_attn_decode_q8)", need, NOALLOC_SCRATCH_FLOATS);
+    float* scr = nullptr;
+    rc = noalloc_scratch(ctx, &scr);
+    if (rc) return rc;
+    return tb_attn_decode_impl(ctx, out, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit, scr,
+                               scr + (size_t)nHq * nsplit * hd);
+}
