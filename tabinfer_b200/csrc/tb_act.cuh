@@ -4,60 +4,52 @@
 #pragma once
 #include "tb_common.cuh"
 
-// Sum of squares of xr[0..H) by a 256-thread block, in a fixed order
-// (thread-strided fmaf, warp butterfly, then warp 0 over the 8 warp sums).
-// Every thread returns the same value.  `red` is >= 32 floats of shared memory.
-__device__ __forceinline__ float block256_sumsq(const float* __restrict__ xr, int H, float* red)
+// Canonical RMSNorm reduction order, shared by every RMSNorm here (fused into a
+// GEMV prologue or standalone) so they agree bit for bit.  In a 256-thread
+// block, thread t accumulates, with fmaf, the float4s f = t, t+256, ... of the
+// row (components x, y, z, w in turn); each warp reduces its 32 partials with
+// an xor butterfly; every thread then adds the 8 warp sums in warp order.
+__device__ __forceinline__ float sumsq_f4(float4 v, float ss)
 {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < H; i += 256) { float v = xr[i]; ss = fmaf(v, v, ss); }
-    ss = warp_sum(ss);
-    __syncthreads();
-    if (lane == 0) red[wid] = ss;
-    __syncthreads();
-    if (wid == 0) {
-        float t = lane < 8 ? red[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) red[8] = t;
-    }
-    __syncthreads();
-    return red[8];
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    return fmaf(v.w, v.w, ss);
 }
 
-// block256_sumsq for NB rows at once (same per-row order and result), reading
-// element i of row b through `at(b, i)`.  out[b] valid in every thread.
-template <int NB, typename At>
-__device__ __forceinline__ void block256_sumsq_rows(At at, int H, float* red, float* out)
+// Block-reduce per-thread partial sums of NB rows (NB <= 8) in the canonical
+// order; the total of row b is returned in out[b] by every thread.  One
+// __syncthreads; `red` holds >= 64 floats and may be reused after the next
+// __syncthreads.
+template <int NB>
+__device__ __forceinline__ void block256_reduce_rows(const float* part, float* red, float* out)
 {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    float ss[NB];
 #pragma unroll
-    for (int b = 0; b < NB; b++) ss[b] = 0.0f;
-    for (int i = threadIdx.x; i < H; i += 256) {
-#pragma unroll
-        for (int b = 0; b < NB; b++) { const float v = at(b, i); ss[b] = fmaf(v, v, ss[b]); }
-    }
-#pragma unroll
-    for (int b = 0; b < NB; b++) ss[b] = warp_sum(ss[b]);
-    __syncthreads();
-    if (lane == 0) {
-#pragma unroll
-        for (int b = 0; b < NB; b++) red[b * 8 + wid] = ss[b];
-    }
-    __syncthreads();
-    if (wid == 0) {
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
-            float t = lane < 8 ? red[b * 8 + lane] : 0.0f;
-            t = warp_sum(t);
-            if (lane == 0) red[64 + b] = t;
-        }
+    for (int b = 0; b < NB; b++) {
+        const float s = warp_sum(part[b]);
+        if (lane == 0) red[b * 8 + wid] = s;
     }
     __syncthreads();
 #pragma unroll
-    for (int b = 0; b < NB; b++) out[b] = red[64 + b];
+    for (int b = 0; b < NB; b++) {
+        float t = red[b * 8];
+#pragma unroll
+        for (int w = 1; w < 8; w++) t = __fadd_rn(t, red[b * 8 + w]);
+        out[b] = t;
+    }
+}
+
+// Sum of squares of one row in the canonical order (H % 4 == 0, 16-byte aligned).
+__device__ __forceinline__ float block256_sumsq(const float* __restrict__ xr, int H, float* red)
+{
+    float ss = 0.0f;
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    for (int f = threadIdx.x; f < (H >> 2); f += 256) ss = sumsq_f4(x4[f], ss);
+    float out;
+    block256_reduce_rows<1>(&ss, red, &out);
     __syncthreads();
+    return out;
 }
 
 __device__ __forceinline__ float rms_inv(float sumsq, int H, float eps)
@@ -65,17 +57,22 @@ __device__ __forceinline__ float rms_inv(float sumsq, int H, float eps)
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), eps)));
 }
 
-// Per-32 int8 quantization of one group held one element per lane (WGSL f32
-// semantics: scale = maxabs/127, q = clamp(round_half_even(x * (1/scale)))).
+// WGSL f32 semantics of the per-32 quantization: scale = maxabs/127,
+// q = clamp(round_half_even(x * (1/scale)), -127, 127).
+__device__ __forceinline__ float q8_scale(float maxabs) { return __fdiv_rn(maxabs, 127.0f); }
+__device__ __forceinline__ float q8_inv(float scale) { return scale > 0.0f ? __frcp_rn(scale) : 0.0f; }
+__device__ __forceinline__ int q8_quant(float v, float inv)
+{
+    return max(-127, min(127, __float2int_rn(__fmul_rn(v, inv))));
+}
+
+// Per-32 quantization of one group held one element per lane.
 struct Q8Group {
     int q;        // this lane's int8 value
     float scale;  // group scale (maxabs/127)
 };
 __device__ __forceinline__ Q8Group q8_group(float v)
 {
-    const float m = warp_max(fabsf(v));
-    const float scale = __fdiv_rn(m, 127.0f);
-    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    int q = __float2int_rn(__fmul_rn(v, inv));
-    return Q8Group{max(-127, min(127, q)), scale};
+    const float scale = q8_scale(warp_max(fabsf(v)));
+    return Q8Group{q8_quant(v, q8_inv(scale)), scale};
 }

@@ -57,6 +57,7 @@ struct Args {
     int slot_bytes;        // bytes of one matrix's row block in a stage (weights, then scales)
     int act_bytes;         // staged activation (Q8 or f32 layout)
     int xbuf_bytes;        // f32 staging of raw rows for the Q8 prologue
+    int nw_bytes;          // f16 RMSNorm weight, prefetched before the wait
     int* err;
 };
 
@@ -150,18 +151,53 @@ __device__ void issue_block(const Args& a, int rb, unsigned char* stage, uint64_
 // flight per thread) before any of it is used: the prologue costs one memory
 // round trip, not one per 32-group.
 
-// Sum of squares in block256_sumsq's order, reading element i of a row that is
-// stored in the swizzled f32 layout below.
+// Index of element i of row b in the swizzled f32 layout (per (b, g) 8 float4,
+// float4 index XOR-swizzled by (g & 7)).
 __device__ __forceinline__ int swz_index(int G, int b, int i)
 {
     const int f = i >> 2, g = f >> 3, j = f & 7;
     return ((b * G + g) * 8 + (j ^ (g & 7))) * 4 + (i & 3);
 }
 
+// Copy nb rows of K4 float4 from global into the swizzled shared layout and
+// accumulate each row's sum of squares in the canonical order (thread t:
+// float4 t, t+256, ... of the row).  Loads are issued in batches of 8 per
+// thread before any store, so a batch costs one memory round trip.
+template <int B>
+__device__ __forceinline__ void load_rows_swz(const float4* __restrict__ src, int nb, int K4, float4* dst, float* ss)
+{
+    constexpr int LPT = 8;
+    const int tid = threadIdx.x;
+    const int kpt = (K4 + THREADS - 1) / THREADS;   // float4 per thread per row
+    const int n_items = nb * kpt;
+#pragma unroll
+    for (int b = 0; b < B; b++) ss[b] = 0.0f;
+    for (int u0 = 0; u0 < n_items; u0 += LPT) {
+        float4 v[LPT];
+#pragma unroll
+        for (int u = 0; u < LPT; u++) {
+            const int it = u0 + u, bb = it / kpt, f = (it - bb * kpt) * THREADS + tid;
+            if (it < n_items && f < K4) v[u] = __ldg(src + (size_t)bb * K4 + f);
+        }
+#pragma unroll
+        for (int u = 0; u < LPT; u++) {
+            const int it = u0 + u, bb = it / kpt, f = (it - bb * kpt) * THREADS + tid;
+            if (it < n_items && f < K4) {
+                const int g = f >> 3, j = f & 7;
+                dst[bb * K4 + g * 8 + (j ^ (g & 7))] = v[u];
+#pragma unroll
+                for (int b = 0; b < B; b++)
+                    if (b == bb) ss[b] = sumsq_f4(v[u], ss[b]);
+            }
+        }
+    }
+}
+
 // Q8 layout per (b, g): lo = (e0,o0,e1,o1), hi = (e2,o2,e3,o3) (e_w / o_w = even /
 // odd k of weight word w, one int8 per byte), s8 = 8*sum(x), sf = scale.
 template <int B>
-__device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbuf_floats, float* red)
+__device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbuf_floats, float* red,
+                         const uint16_t* nws)
 {
     const int G = a.K >> 5;
     uint4* xlo = reinterpret_cast<uint4*>(act);
@@ -191,111 +227,111 @@ __device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbu
         }
         return;
     }
-    // f32 rows -> swizzled shared copy (one burst of loads) -> one thread per (row, group)
+    // f32 rows -> swizzled shared copy (one burst of loads, the RMSNorm sums of
+    // squares accumulated on the way in, canonical order of tb_act.cuh); then
+    // 2 threads per (row, 32-group), one pass: thread h of the pair owns k =
+    // 16h..16h+15, i.e. exactly the permuted dp4a half `lo` (h = 0) or `hi`.
     const int K4 = a.K >> 2;
     const int rows_per_chunk = max(1, xbuf_floats / a.K);
     float4* xb4 = reinterpret_cast<float4*>(xbuf);
+    const int h2 = tid & 1;
     for (int b0 = 0; b0 < B; b0 += rows_per_chunk) {
         const int nb = min(rows_per_chunk, B - b0);
         const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)b0 * a.K);
-#pragma unroll 8
-        for (int i = tid; i < nb * K4; i += THREADS) {
-            const int bb = i / K4, f = i - bb * K4, g = f >> 3, j = f & 7;
-            xb4[bb * K4 + g * 8 + (j ^ (g & 7))] = src[i];
-        }
-        __syncthreads();
-        float inv[B];
-#pragma unroll
-        for (int b = 0; b < B; b++) inv[b] = 1.0f;
+        float ss[B], inv[B];
+        load_rows_swz<B>(src, nb, K4, xb4, ss);
         if (a.act_src == ACT_RMSNORM) {
-            float ss[B];
-            block256_sumsq_rows<B>([&](int bb, int i) {
-                return bb < nb ? xbuf[bb * a.K + swz_index(G, 0, i)] : 0.0f;
-            }, a.K, red, ss);
+            block256_reduce_rows<B>(ss, red, inv);   // includes the __syncthreads for xb4
 #pragma unroll
-            for (int b = 0; b < B; b++) inv[b] = rms_inv(ss[b], a.K, a.eps);
+            for (int b = 0; b < B; b++) inv[b] = rms_inv(inv[b], a.K, a.eps);
+        } else {
+            __syncthreads();
+#pragma unroll
+            for (int b = 0; b < B; b++) inv[b] = 1.0f;
         }
-        for (int item = tid; item < nb * G; item += THREADS) {
-            const int bb = item / G, g = item - bb * G;
-            const float4* xg = xb4 + bb * K4 + g * 8;
-            float v[32];
+        // both threads of a pair run the same number of passes (shuffles stay converged)
+        for (int base = 0; base < nb * G * 2; base += THREADS) {
+            const int item = (base + tid) >> 1;
+            const bool live = item < nb * G;
+            const int bb = live ? item / G : 0, g = live ? item - bb * G : 0;
+            float v[16];
+            {
+                const float4* xg = xb4 + bb * K4 + g * 8;
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float4 t = xg[j ^ (g & 7)];
-                v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+                for (int q = 0; q < 4; q++) {
+                    const float4 t = xg[(4 * h2 + q) ^ (g & 7)];
+                    v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+                }
             }
             if (a.act_src == ACT_RMSNORM) {
                 float ib = inv[0];
 #pragma unroll
                 for (int b = 1; b < B; b++) if (bb == b) ib = inv[b];
-                const uint4* wq = reinterpret_cast<const uint4*>(a.normw + g * 32);
+                const uint4* wq = reinterpret_cast<const uint4*>(nws + g * 32 + 16 * h2);
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const uint4 wv = __ldg(wq + j);
+                for (int q = 0; q < 2; q++) {
+                    const uint4 wv = wq[q];
                     const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
                     for (int h = 0; h < 4; h++) {
-                        const int k = 8 * j + 2 * h;
+                        const int k = 8 * q + 2 * h;
                         v[k] = __fmul_rn(__fmul_rn(v[k], ib), tb_h2f((uint16_t)(ww[h] & 0xffffu)));
                         v[k + 1] = __fmul_rn(__fmul_rn(v[k + 1], ib), tb_h2f((uint16_t)(ww[h] >> 16)));
                     }
                 }
             }
-            float m = 0.0f;
+            float m[4];
 #pragma unroll
-            for (int k = 0; k < 32; k++) m = fmaxf(m, fabsf(v[k]));
-            const float scale = __fdiv_rn(m, 127.0f);
-            const float is = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-            uint32_t words[8];
+            for (int i = 0; i < 4; i++) m[i] = fmaxf(fmaxf(fabsf(v[i]), fabsf(v[i + 4])), fmaxf(fabsf(v[i + 8]), fabsf(v[i + 12])));
+            float mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            const float scale = q8_scale(mx), is = q8_inv(scale);
+            uint32_t wd[4];
             int sum = 0;
 #pragma unroll
-            for (int wd = 0; wd < 4; wd++) {
+            for (int w = 0; w < 2; w++) {
                 uint32_t e = 0, o = 0;
 #pragma unroll
                 for (int h = 0; h < 4; h++) {
-                    int qe = max(-127, min(127, __float2int_rn(__fmul_rn(v[8 * wd + 2 * h], is))));
-                    int qo = max(-127, min(127, __float2int_rn(__fmul_rn(v[8 * wd + 2 * h + 1], is))));
+                    const int qe = q8_quant(v[8 * w + 2 * h], is), qo = q8_quant(v[8 * w + 2 * h + 1], is);
                     sum += qe + qo;
                     e |= ((uint32_t)qe & 0xffu) << (8 * h);
                     o |= ((uint32_t)qo & 0xffu) << (8 * h);
                 }
-                words[2 * wd] = e;
-                words[2 * wd + 1] = o;
+                wd[2 * w] = e;
+                wd[2 * w + 1] = o;
             }
-            const int i = (b0 + bb) * G + g;
-            xlo[i] = make_uint4(words[0], words[1], words[2], words[3]);
-            xhi[i] = make_uint4(words[4], words[5], words[6], words[7]);
-            xs8[i] = 8 * sum;
-            xsf[i] = scale;
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            if (live) {
+                const int i = (b0 + bb) * G + g;
+                (h2 ? xhi : xlo)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                if (h2 == 0) { xs8[i] = 8 * sum; xsf[i] = scale; }
+            }
         }
-        __syncthreads();   // xbuf is reused by the next chunk
+        __syncthreads();   // xbuf and red are reused by the next chunk
     }
 }
 
 // F32 layout: per (b, g) 8 float4, float4 index XOR-swizzled by (g & 7).
 template <int B>
-__device__ void stage_f32(const Args& a, unsigned char* act, float* red)
+__device__ void stage_f32(const Args& a, unsigned char* act, float* red, const uint16_t* nws)
 {
     const int G = a.K >> 5, K4 = a.K >> 2;
     float4* xsm = reinterpret_cast<float4*>(act);
-    const float4* src = reinterpret_cast<const float4*>(a.x);
-#pragma unroll 8
-    for (int i = threadIdx.x; i < B * K4; i += THREADS) {
-        const int b = i / K4, f = i - b * K4, g = f >> 3, j = f & 7;
-        xsm[(b * G + g) * 8 + (j ^ (g & 7))] = src[i];
-    }
-    __syncthreads();
-    if (a.act_src != ACT_RMSNORM) return;
-    float* xf = reinterpret_cast<float*>(act);
-    float ss[B];
-    block256_sumsq_rows<B>([&](int b, int i) { return xf[swz_index(G, b, i)]; }, a.K, red, ss);
-    for (int i = threadIdx.x; i < B * a.K; i += THREADS) {
-        const int b = i / a.K, k = i - b * a.K;
-        float inv = rms_inv(ss[0], a.K, a.eps);
+    float ss[B], inv[B];
+    load_rows_swz<B>(reinterpret_cast<const float4*>(a.x), B, K4, xsm, ss);
+    if (a.act_src != ACT_RMSNORM) { __syncthreads(); return; }
+    block256_reduce_rows<B>(ss, red, inv);
 #pragma unroll
-        for (int bb = 1; bb < B; bb++) if (b == bb) inv = rms_inv(ss[bb], a.K, a.eps);
-        float* p = xf + swz_index(G, b, k);
-        *p = __fmul_rn(__fmul_rn(*p, inv), tb_h2f(a.normw[k]));
+    for (int b = 0; b < B; b++) inv[b] = rms_inv(inv[b], a.K, a.eps);
+    float* xf = reinterpret_cast<float*>(act);
+    for (int i = threadIdx.x; i < a.K; i += THREADS) {
+        const float w = tb_h2f(nws[i]);
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            float* p = xf + swz_index(G, b, i);
+            *p = __fmul_rn(__fmul_rn(*p, inv[b]), w);
+        }
     }
     __syncthreads();
 }
@@ -379,14 +415,20 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
     __shared__ int abort_flag;
     unsigned char* act = smem + SMEM_HDR;
     float* xbuf = reinterpret_cast<float*>(act + a.act_bytes);
-    unsigned char* stages = act + a.act_bytes + a.xbuf_bytes;
+    uint16_t* nws = reinterpret_cast<uint16_t*>(act + a.act_bytes + a.xbuf_bytes);
+    unsigned char* stages = act + a.act_bytes + a.xbuf_bytes + a.nw_bytes;
     constexpr bool gateup = KIND == KIND_GATEUP;
     constexpr int NM = gateup ? 2 : 1;
     const int stage_bytes = NM * a.slot_bytes;
     const int G = a.K >> 5;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
 
-    // ---- prologue (independent of earlier kernels): barriers + first weight stages
+    // ---- prologue (independent of earlier kernels): norm weights, barriers and
+    // the first weight stages
+    if (a.act_src == ACT_RMSNORM) {
+        for (int i = tid; i < (a.K >> 3); i += THREADS)
+            reinterpret_cast<uint4*>(nws)[i] = __ldg(reinterpret_cast<const uint4*>(a.normw) + i);
+    }
     if (tid == 0) {
         abort_flag = 0;
         for (int s = 0; s < a.nst; s++) mbar_init(&bars[s], 1);
@@ -403,15 +445,16 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
     // ---- wait for the producer of the activation, then prepare it
     tb_pdl_wait();
     tb_pdl_trigger();
-    if (KIND == KIND_F32) stage_f32<B>(a, act, red);
-    else stage_q8<B>(a, act, xbuf, a.xbuf_bytes >> 2, red);
+    if (KIND == KIND_F32) stage_f32<B>(a, act, red, nws);
+    else stage_q8<B>(a, act, xbuf, a.xbuf_bytes >> 2, red, nws);
     __syncthreads();
 
     // f32 activation of a single row kept in registers (groups lane, lane+32),
     // un-swizzled on the way in so every register index is static
     constexpr bool XREG = KIND == KIND_F32 && B == 1;
+    const bool xreg = XREG && G <= 64;
     float4 xr0[8], xr1[8];
-    if (XREG && G <= 64) {
+    if (XREG && xreg) {
         const float4* xsm = reinterpret_cast<const float4*>(act);
         if (lane < G) {
 #pragma unroll
@@ -447,7 +490,7 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
                     const uint4* wrow = reinterpret_cast<const uint4*>(slot) + (size_t)r * G;
                     const uint16_t* srow = sbulk ? reinterpret_cast<const uint16_t*>(slot + (size_t)a.RB * (a.K >> 1)) + (size_t)r * G
                                                  : a.m[gateup ? s : bl.mi].scales + (size_t)(bl.row0 + r) * G;
-                    if (XREG && G <= 64) {
+                    if (XREG && xreg) {
                         if (lane < G) {
                             const uint4 w = wrow[lane];
                             float2 d = make_float2(0.0f, 0.0f);
@@ -517,12 +560,12 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
 
 // ---- host side ------------------------------------------------------------------
 struct Plan {
-    int RB, nst, slot_bytes, act_bytes, xbuf_bytes, smem, grid, nrb;
+    int RB, nst, slot_bytes, act_bytes, xbuf_bytes, nw_bytes, smem, grid, nrb;
 };
 
 int act_bytes_for(int kind, int B, int G) { return kind == KIND_F32 ? B * G * 128 : B * G * 40; }
 
-int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count, Plan& p)
+int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count, bool norm, Plan& p)
 {
     const int G = K / 32;
     const int nm = kind == KIND_GATEUP ? 2 : 1;
@@ -533,6 +576,7 @@ int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count,
     // f32 staging buffer for the Q8 prologue (whole rows, up to 48 KB)
     p.xbuf_bytes = kind == KIND_F32 ? 0 : std::min(B * K * 4, std::max(48 * 1024, K * 4));
     p.xbuf_bytes = (p.xbuf_bytes + 127) & ~127;
+    p.nw_bytes = norm ? ((K * 2 + 127) & ~127) : 0;
     const int target = 2 * ctx->num_sms;
     const int budget = 112 * 1024;   // leave room for the next kernel's CTA under PDL
     int RB = 8;
@@ -545,7 +589,7 @@ int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count,
         for (int i = 0; i < mats; i++) nrb += tb_cdiv(Ns[i], RB);
         const int blocks_per_cta = tb_cdiv(nrb, target);
         int nst = std::min(MAX_NST, std::max(1, blocks_per_cta));
-        const int fixed = SMEM_HDR + p.act_bytes + p.xbuf_bytes;
+        const int fixed = SMEM_HDR + p.act_bytes + p.xbuf_bytes + p.nw_bytes;
         while (nst > 1 && fixed + nst * per_stage > budget) nst--;
         p.smem = fixed + nst * per_stage;
         if (p.smem <= 200 * 1024 || RB == 8) {
@@ -616,7 +660,8 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
         TB_REQUIRE(ctx, in.xq && in.xs && TB_ALIGNED(in.xq, 16), "xq (16-byte aligned) and xs required");
     } else {
         TB_REQUIRE(ctx, in.x && TB_ALIGNED(in.x, 16), "x must be non-null and 16-byte aligned");
-        TB_REQUIRE(ctx, in.src != ACT_RMSNORM || in.normw, "norm weight required");
+        TB_REQUIRE(ctx, in.src != ACT_RMSNORM || (in.normw && TB_ALIGNED(in.normw, 16)),
+                   "norm weight required (16-byte aligned)");
     }
     Args a{};
     a.count = count;
@@ -650,7 +695,7 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
         return TB_OK;
     }
     Plan p{};
-    int rc = make_plan(ctx, kind, batch, (int)K, Ns, count, p);
+    int rc = make_plan(ctx, kind, batch, (int)K, Ns, count, in.src == ACT_RMSNORM, p);
     if (rc) return rc;
     int rb = 0;
     for (int i = 0; i < 4; i++) {
@@ -668,6 +713,7 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
     a.slot_bytes = p.slot_bytes;
     a.act_bytes = p.act_bytes;
     a.xbuf_bytes = p.xbuf_bytes;
+    a.nw_bytes = p.nw_bytes;
     switch (kind) {
     case KIND_Q8: return launch_kind<KIND_Q8>(ctx, a, p, batch);
     case KIND_GATEUP: return launch_kind<KIND_GATEUP>(ctx, a, p, batch);

@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p2(const unsigned long 
 __global__ void __launch_bounds__(256) k_rmsnorm(const float* __restrict__ x, const uint16_t* __restrict__ w16,
                                                  float* __restrict__ y, int H, float eps)
 {
-    __shared__ float red[32];
+    __shared__ float red[80];
     tb_pdl_wait();
     tb_pdl_trigger();
     const int row = blockIdx.x;
@@ -134,7 +134,8 @@ TB_API int tb_rmsnorm(tb_ctx* ctx, const float* x, const uint16_t* w16, float* y
 {
     if (!ctx) return TB_ERR_INVALID;
     TB_REQUIRE(ctx, x && w16 && y, "null pointer");
-    TB_REQUIRE(ctx, T > 0 && T <= 65535 && H > 0, "bad shape");
+    TB_REQUIRE(ctx, T > 0 && T <= 65535 && H > 0 && H % 4 == 0, "bad shape (H %% 4 must be 0)");
+    TB_REQUIRE(ctx, TB_ALIGNED(x, 16), "x must be 16-byte aligned");
     cudaError_t e = tb_launch(ctx, k_rmsnorm, dim3((unsigned)T), dim3(256), 0, x, w16, y, (int)H, eps);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "rmsnorm launch: %s", cudaGetErrorString(e));
     return TB_OK;

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm_q8(const float* __restrict__ x,
                                                     float eps, int H, int8_t* __restrict__ xq,
                                                     float* __restrict__ xs, int32_t* __restrict__ xsum16)
 {
-    __shared__ float red[32];
+    __shared__ float red[80];
     tb_pdl_wait();
     tb_pdl_trigger();
     const int row = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -170,6 +170,7 @@ TB_API int tb_rmsnorm_q8(tb_ctx* ctx, const float* x, const uint16_t* w16, float
     if (!ctx) return TB_ERR_INVALID;
     TB_REQUIRE(ctx, x && w16 && xq && xs, "null pointer");
     TB_REQUIRE(ctx, T > 0 && T <= 65535 && H > 0 && H % 32 == 0, "bad shape T=%lld H=%lld", (long long)T, (long long)H);
+    TB_REQUIRE(ctx, TB_ALIGNED(x, 16), "x must be 16-byte aligned");
     cudaError_t e = tb_launch(ctx, k_rmsnorm_q8, dim3((unsigned)T), dim3(256), 0, x, w16, eps, (int)H, xq, xs, xsum16);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "rmsnorm_q8 launch: %s", cudaGetErrorString(e));
     return TB_OK;
