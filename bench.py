@@ -297,6 +297,55 @@ def dominant_kernel_roofline(chain, ctx, peak, reps=3):
     return dom, res
 
 
+def profile_case():
+    """One cold-L2 launch of each kernel kind, for `ncu --set full` on a small
+    case (a few hundred MB on the device): the five GEMV kinds of the 0.6B chain
+    at batch 1, the config-1 ternary qkv GEMV (4096 x 2048) and int8-KV decode
+    attention at S = 4096 (1.7B heads).  Every launch is preceded by a 256 MB
+    write that evicts L2."""
+    import numpy as np
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def q(N, K):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        return tb.quantize_int4_bf16(w.view(torch.int16))
+
+    qm, km, vm, om = q(2048, H), q(1024, H), q(1024, H), q(H, 2048)
+    gm, um, dm, lm = q(INTER, H), q(INTER, H), q(H, INTER), q(VOCAB, H)
+    ln = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half().view(torch.int16)
+    tw = (torch.randint(0, 3, (4096, 2048), device=dev, generator=g).float() - 1.0) * 0.03
+    codes, tsc = tb.pack_ternary(tw)
+    S, nHq, nKv, hd = 4096, 16, 8, 128
+    Kq = torch.randint(-127, 128, (S, nKv * hd), device=dev, generator=g, dtype=torch.int8)
+    Vq = torch.randint(-127, 128, (S, nKv * hd), device=dev, generator=g, dtype=torch.int8)
+    Ks = torch.rand(S, nKv * hd // 32, device=dev, generator=g) + 0.5
+    Vs = torch.rand(S, nKv * hd // 32, device=dev, generator=g) + 0.5
+    qr = torch.randn(nHq * hd, device=dev, generator=g)
+    x1, x2, x3 = (torch.randn(1, k, device=dev, generator=g) for k in (H, 2048, INTER))
+    xt = torch.randn(1, 2048, device=dev, generator=g)
+    act, xsum, _ = tb.quantize_act(xt)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    launches = [
+        lambda: tb.gemv_dp4a_multi(x1, [qm, km, vm], norm_w=ln),
+        lambda: tb.gemv_dp4a(x2, *om),
+        lambda: tb.gate_up_silu_dp4a(x1, *gm, *um, norm_w=ln),
+        lambda: tb.gemv_dp4a(x3, *dm),
+        lambda: tb.gemv_q_norm(x1, ln, 1e-6, *lm),
+        lambda: tb.gemv_tern(codes, tsc, act, xsum),
+        lambda: tb.attention_decode_q8(qr, (Kq, Ks, Vq, Vs), S, nHq, nKv, hd),
+    ]
+    torch.cuda.synchronize()
+    for it in range(2):
+        for fn in launches:
+            flush.fill_(it)
+            fn()
+    torch.cuda.synchronize()
+    print("profile case done", flush=True)
+
+
 def cpu_baseline_sample(threads, budget_s=12.0):
     """The transcribed CPU path (oracle/tb_cpu_ref.c, linearQ math) on a bounded
     sample: 2 decoder layers' 7 matrices + 1/16 of the lm_head rows, repeated
@@ -373,7 +422,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="one cold-L2 launch per kernel kind (for ncu), then exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case()
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
