@@ -20,19 +20,13 @@ namespace {
 constexpr int ATT_WARPS = 4;
 constexpr int ATT_THREADS = ATT_WARPS * 32;
 constexpr int ATT_MAXG = 8;       // q heads per kv head handled by one CTA
+constexpr int ATT_MAXSPLIT = 1024; // splits per decode call
 constexpr float NEG_BIG = -3.0e38f;
 
 __device__ __forceinline__ int8_t snorm8(float v)
 {
     float c = fminf(1.0f, fmaxf(-1.0f, v));
     return (int8_t)floorf(__fadd_rn(0.5f, __fmul_rn(127.0f, c)));
-}
-
-// signed byte i of w as an exact float
-__device__ __forceinline__ float sbyte_f(uint32_t w, int i)
-{
-    uint32_t u = __byte_perm(w ^ 0x80808080u, 0x4B000000u, 0x7540 + i);   // 2^23 + (c+128)
-    return __uint_as_float(u) - 8388736.0f;
 }
 
 // ---- fused prep: q rope, k rope + quant-write, v quant-write ---------------
@@ -112,158 +106,345 @@ struct AttnArgs {
     const float* Vs;
     float* PO;             // [nHq][nsplit][hd]
     float* PML;            // [nHq][nsplit][2]
+    float* out;            // [nHq*hd]
+    unsigned* counters;    // [nKv] split arrivals, zero between calls
     int S, nHq, nKv, nsplit, per;
 };
 
-// hd fixed at compile time (128 for Qwen3); GRP = q heads per kv head.
+// ---- cp.async (16-byte and 8-byte global -> shared copies, per thread) -----
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)),
+                 "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* sdst, const void* gsrc)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)),
+                 "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Shared-memory layout of k_attn_decode<HD, GRP> (dynamic, bytes).  Each warp
+// owns NST stages; a stage holds one tile of 32 keys: K rows, V rows (HD bytes
+// each, 16-byte chunk i of key j stored at chunk i ^ (j % KV16) so the per-key
+// 16-byte copies and reads are bank-conflict free), then the 32 keys' K and V
+// group scales.
+template <int HD, int GRP>
+struct DecLayout {
+    static constexpr int KV16 = HD / 16, NG = HD / 32, NST = 2;
+    static constexpr int ST_K = 0, ST_V = 32 * HD, ST_KS = 64 * HD, ST_VS = 64 * HD + 32 * NG * 4;
+    static constexpr int STAGE = 64 * HD + 64 * NG * 4;
+    static constexpr int OFF_QS = 0;                                  // float [GRP][HD]
+    static constexpr int OFF_PS = OFF_QS + GRP * HD * 4;              // float [W][32 keys][NG][GRP]
+    static constexpr int OFF_WM = OFF_PS + ATT_WARPS * 32 * NG * GRP * 4;   // float [W][GRP]
+    static constexpr int OFF_WL = OFF_WM + ATT_WARPS * GRP * 4;       // float [W][GRP]
+    static constexpr int OFF_ST = (OFF_WL + ATT_WARPS * GRP * 4 + 127) / 128 * 128;
+    static constexpr int BYTES = OFF_ST + ATT_WARPS * NST * STAGE;
+    // after the key loop the stages are reused for the warps' outputs, float [W][GRP][HD]
+    static_assert(ATT_WARPS * GRP * HD * 4 <= ATT_WARPS * NST * STAGE, "merge buffer must fit in the stages");
+    static_assert(STAGE % 16 == 0 && ST_KS % 16 == 0 && ST_VS % 16 == 0, "stage alignment");
+    // the combining CTA keeps its split weights [GRP][nsplit] there too
+    static_assert(GRP * ATT_MAXSPLIT * 4 + (GRP * HD / 4 > ATT_THREADS ? GRP * HD / 4 : ATT_THREADS) * 16 <=
+                      ATT_WARPS * NST * STAGE,
+                  "split weights and column partials must fit in the stages");
+};
+
+// hd fixed at compile time (64 or 128); GRP = q heads per kv head.
+// CTA = 4 warps over one (kv head, split).  Warp w takes the 32-key tiles
+// w, w+4, w+8, ... of the split and runs a two-stage cp.async pipeline over
+// them: while tile j is scored, tile j+1's K rows, V rows and scales are in
+// flight.  Lane = key for the scores (K row from shared memory against q held
+// in shared memory, packed f32x2 FMAs); the lane's key then writes
+// p * vscale / 127 per V group, and P.V runs lane = 4 dims (2 for hd 64)
+// over the tile's keys.  Softmax is online per warp; the 4 warps merge at the
+// end into the split's partial (PO, PML).
 template <int HD, int GRP>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
 {
-    constexpr int NG = HD / 32;          // scale groups per head row
-    constexpr int DPL = HD / 32;         // dims per lane in P.V
-    __shared__ __align__(16) float qs[GRP][HD];
-    __shared__ float wm[ATT_WARPS][GRP], wl[ATT_WARPS][GRP];
-    __shared__ __align__(16) float wo[ATT_WARPS][GRP][HD];
+    using L = DecLayout<HD, GRP>;
+    constexpr int KV16 = L::KV16, NG = L::NG, NST = L::NST;
+    constexpr int DPL = HD / 32;                // dims per lane in P.V
+    extern __shared__ __align__(128) uint8_t smem[];
+    float* qs = reinterpret_cast<float*>(smem + L::OFF_QS);
+    float* ps_all = reinterpret_cast<float*>(smem + L::OFF_PS);
+    float* wm = reinterpret_cast<float*>(smem + L::OFF_WM);
+    float* wl = reinterpret_cast<float*>(smem + L::OFF_WL);
+
+    const int hk = blockIdx.x, split = blockIdx.y;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const long long row_elems = (long long)a.nKv * HD, row_groups = row_elems / 32;
+    const int c0 = split * a.per, c1 = min(a.S, c0 + a.per);
+    const int span = c1 - c0;
+    const int ntile = span > wid * 32 ? (span - wid * 32 + ATT_WARPS * 32 - 1) / (ATT_WARPS * 32) : 0;
+    uint8_t* stages = smem + L::OFF_ST + wid * NST * L::STAGE;
+    float* ps = ps_all + wid * 32 * NG * GRP;
+
+    // tile j of this warp -> stage s; always commits a group (possibly empty).
+    // Rows are copied coalesced: in copy r, lanes 8q..8q+7 (4q..4q+3 for hd 64)
+    // move the KV16 16-byte chunks of key r*RPI + q.  Scales: lane = key.
+    auto issue = [&](int j, int s) {
+        constexpr int RPI = 32 / KV16;                  // rows per copy instruction
+        const int tb0 = c0 + (wid + ATT_WARPS * j) * 32;
+        uint8_t* st = stages + s * L::STAGE;
+        const int ch = lane % KV16;
+#pragma unroll
+        for (int r = 0; r < KV16; r++) {
+            const int kr = r * RPI + lane / KV16;
+            if (tb0 + kr < c1) {
+                const long long src = (long long)(tb0 + kr) * row_elems + hk * HD + ch * 16;
+                const int dst = (kr * KV16 + (ch ^ (kr & (KV16 - 1)))) * 16;
+                cp_async16(st + L::ST_K + dst, a.Kq + src);
+                cp_async16(st + L::ST_V + dst, a.Vq + src);
+            }
+        }
+        const int t = tb0 + lane;
+        if (t < c1) {
+            float* ksd = reinterpret_cast<float*>(st + L::ST_KS) + lane * NG;
+            float* vsd = reinterpret_cast<float*>(st + L::ST_VS) + lane * NG;
+            const float* ksr = a.Ks + (long long)t * row_groups + hk * NG;
+            const float* vsr = a.Vs + (long long)t * row_groups + hk * NG;
+            if (NG * 4 == 16) {
+                cp_async16(ksd, ksr);
+                cp_async16(vsd, vsr);
+            } else {
+#pragma unroll
+                for (int g = 0; g < NG; g += 2) { cp_async8(ksd + g, ksr + g); cp_async8(vsd + g, vsr + g); }
+            }
+        }
+        cp_async_commit();
+    };
 
     tb_pdl_wait();
     tb_pdl_trigger();
-    const int hk = blockIdx.x, split = blockIdx.y;
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int row_elems = a.nKv * HD, row_groups = row_elems / 32;
+    issue(0, 0);
     const float qscale = rsqrtf((float)HD) * (1.0f / 127.0f);
-    for (int i = threadIdx.x; i < GRP * HD; i += ATT_THREADS) {
-        int h = i / HD, d = i - h * HD;
-        qs[h][d] = a.qr[(long long)(hk * GRP + h) * HD + d];
-    }
+    for (int i = threadIdx.x; i < GRP * HD; i += ATT_THREADS) qs[i] = a.qr[(long long)hk * GRP * HD + i];
     __syncthreads();
 
-    const int c0 = split * a.per, c1 = min(a.S, c0 + a.per);
-    float m[GRP], l[GRP], o[GRP][DPL];
+    float m[GRP], l[GRP];
+    float2 o[GRP][DPL / 2];
 #pragma unroll
     for (int h = 0; h < GRP; h++) {
         m[h] = NEG_BIG; l[h] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < DPL; i++) o[h][i] = 0.0f;
+        for (int i = 0; i < DPL / 2; i++) o[h][i] = make_float2(0.0f, 0.0f);
     }
+    const int gsel = (lane * DPL) / 32;               // V group of this lane's dims
+    const int vc = (lane * DPL) >> 4, vcw = ((lane * DPL) & 15) / DPL;   // 16-byte chunk, word in chunk
 
-    for (int t0 = c0 + wid * 32; t0 < c1; t0 += ATT_WARPS * 32) {
-        const int t = t0 + lane;
-        const bool valid = t < c1;
-        // ---- scores: lane per key
+    for (int j = 0; j < ntile; j++) {
+        issue(j + 1, (j + 1) % NST);
+        cp_async_wait<NST - 1>();
+        __syncwarp();
+        const uint8_t* st = stages + (j % NST) * L::STAGE;
+        const int t0 = c0 + (wid + ATT_WARPS * j) * 32;
+        const bool valid = t0 + lane < c1;
+        const int nk = min(32, c1 - t0);
+
+        // ---- scores: lane = key
         float s[GRP];
 #pragma unroll
         for (int h = 0; h < GRP; h++) s[h] = 0.0f;
         if (valid) {
-            const uint4* kr = reinterpret_cast<const uint4*>(a.Kq + (long long)t * row_elems + hk * HD);
-            const float* ksr = a.Ks + (long long)t * row_groups + hk * NG;
-            uint4 kv[HD / 16];
-#pragma unroll
-            for (int i = 0; i < HD / 16; i++) kv[i] = __ldg(kr + i);
-            float kscale[NG];
-#pragma unroll
-            for (int g = 0; g < NG; g++) kscale[g] = __ldg(ksr + g);
+            const uint4* kd = reinterpret_cast<const uint4*>(st + L::ST_K) + lane * KV16;
+            const float* ksd = reinterpret_cast<const float*>(st + L::ST_KS) + lane * NG;
 #pragma unroll
             for (int g = 0; g < NG; g++) {
-                float p[GRP];
+                float2 acc[GRP];
 #pragma unroll
-                for (int h = 0; h < GRP; h++) p[h] = 0.0f;
+                for (int h = 0; h < GRP; h++) acc[h] = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int i = 0; i < 2; i++) {
-                    const uint4 w4 = kv[g * 2 + i];
+                for (int i2 = 0; i2 < 2; i2++) {
+                    const int i = g * 2 + i2;
+                    const uint4 w4 = kd[i ^ (lane & (KV16 - 1))];
                     const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                    for (int wq = 0; wq < 4; wq++)
+                    for (int wq = 0; wq < 4; wq++) {
+                        const float2 k01 = sbytes_f2(ww[wq], 0), k23 = sbytes_f2(ww[wq], 1);
+                        const int d = i * 16 + wq * 4;
 #pragma unroll
-                        for (int bb = 0; bb < 4; bb++) {
-                            const float kf = sbyte_f(ww[wq], bb);
-                            const int d = g * 32 + i * 16 + wq * 4 + bb;
-#pragma unroll
-                            for (int h = 0; h < GRP; h++) p[h] = fmaf(qs[h][d], kf, p[h]);
+                        for (int h = 0; h < GRP; h++) {
+                            const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + d);
+                            acc[h] = ffma2(make_float2(q4.x, q4.y), k01, acc[h]);
+                            acc[h] = ffma2(make_float2(q4.z, q4.w), k23, acc[h]);
                         }
+                    }
                 }
+                const float ksc = ksd[g];
 #pragma unroll
-                for (int h = 0; h < GRP; h++) s[h] = fmaf(p[h], kscale[g], s[h]);
+                for (int h = 0; h < GRP; h++) s[h] = fmaf(acc[h].x + acc[h].y, ksc, s[h]);
             }
         }
-        // ---- online softmax update, per q head
+        // ---- online softmax (per lane partial l; m warp-uniform)
         float pr[GRP];
 #pragma unroll
         for (int h = 0; h < GRP; h++) {
             const float sc = valid ? s[h] * qscale : NEG_BIG;
-            const float mt = warp_max(sc);
-            const float mn = fmaxf(m[h], mt);
+            const float mn = fmaxf(m[h], warp_max(sc));
             const float corr = __expf(m[h] - mn);
             pr[h] = valid ? __expf(sc - mn) : 0.0f;
-            l[h] = l[h] * corr + warp_sum(pr[h]);
+            l[h] = fmaf(l[h], corr, pr[h]);
             m[h] = mn;
 #pragma unroll
-            for (int i = 0; i < DPL; i++) o[h][i] *= corr;
+            for (int i = 0; i < DPL / 2; i++) o[h][i] = make_float2(o[h][i].x * corr, o[h][i].y * corr);
         }
-        // ---- P.V: lane owns dims [lane*DPL, lane*DPL+DPL)
-        const int nk = min(32, c1 - t0);
-        for (int kk = 0; kk < nk; kk++) {
-            const long long tr = (long long)(t0 + kk);
-            const int8_t* vrow = a.Vq + tr * row_elems + hk * HD;
-            const uint32_t vw = DPL == 4 ? __ldg(reinterpret_cast<const uint32_t*>(vrow) + lane)
-                                         : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(vrow) + lane);
-            const float vs = __ldg(a.Vs + tr * row_groups + hk * NG + (lane * DPL) / 32) * (1.0f / 127.0f);
+        // ---- this key's weights per V group: p * vscale / 127
+        {
+            const float* vsd = reinterpret_cast<const float*>(st + L::ST_VS) + lane * NG;
 #pragma unroll
-            for (int h = 0; h < GRP; h++) {
-                const float pw = __shfl_sync(0xffffffffu, pr[h], kk) * vs;
+            for (int g = 0; g < NG; g++) {
+                const float vsc = valid ? vsd[g] * (1.0f / 127.0f) : 0.0f;
 #pragma unroll
-                for (int i = 0; i < DPL; i++) o[h][i] = fmaf(pw, sbyte_f(vw, i), o[h][i]);
+                for (int h = 0; h < GRP; h++) ps[(lane * NG + g) * GRP + h] = pr[h] * vsc;
             }
         }
+        __syncwarp();
+        // ---- P.V: lane = DPL dims
+        const uint4* vt = reinterpret_cast<const uint4*>(st + L::ST_V);
+#pragma unroll 4
+        for (int kk = 0; kk < nk; kk++) {
+            const uint4* vrow = vt + kk * KV16 + (vc ^ (kk & (KV16 - 1)));
+            const uint32_t vw = DPL == 4 ? reinterpret_cast<const uint32_t*>(vrow)[vcw]
+                                         : (uint32_t)reinterpret_cast<const uint16_t*>(vrow)[vcw];
+            const float* pp = ps + (kk * NG + gsel) * GRP;
+            float pw[GRP];
+#pragma unroll
+            for (int h = 0; h < GRP; h++) pw[h] = pp[h];
+            const float2 v01 = sbytes_f2(vw, 0);
+#pragma unroll
+            for (int h = 0; h < GRP; h++) o[h][0] = ffma2(v01, make_float2(pw[h], pw[h]), o[h][0]);
+            if (DPL == 4) {
+                const float2 v23 = sbytes_f2(vw, 1);
+#pragma unroll
+                for (int h = 0; h < GRP; h++) o[h][DPL / 2 - 1] = ffma2(v23, make_float2(pw[h], pw[h]), o[h][DPL / 2 - 1]);
+            }
+        }
+        __syncwarp();   // stage j % NST and ps are rewritten next iteration
     }
+    cp_async_wait<0>();
+    __syncthreads();    // every warp is done with its stages: reuse them for the merge
+
     // ---- merge warps
+    float* wo = reinterpret_cast<float*>(smem + L::OFF_ST);     // [W][GRP][HD]
 #pragma unroll
     for (int h = 0; h < GRP; h++) {
-        if (lane == 0) { wm[wid][h] = m[h]; wl[wid][h] = l[h]; }
+        const float lt = warp_sum(l[h]);
+        if (lane == 0) { wm[wid * GRP + h] = m[h]; wl[wid * GRP + h] = lt; }
 #pragma unroll
-        for (int i = 0; i < DPL; i++) wo[wid][h][lane * DPL + i] = o[h][i];
+        for (int i = 0; i < DPL / 2; i++)
+            *reinterpret_cast<float2*>(wo + (wid * GRP + h) * HD + lane * DPL + 2 * i) = o[h][i];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < GRP * HD; i += ATT_THREADS) {
         const int h = i / HD, d = i - h * HD;
         float M = NEG_BIG;
 #pragma unroll
-        for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, wm[w][h]);
-        float L = 0.0f, O = 0.0f;
+        for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, wm[w * GRP + h]);
+        float Ls = 0.0f, O = 0.0f;
 #pragma unroll
         for (int w = 0; w < ATT_WARPS; w++) {
-            const float e = __expf(wm[w][h] - M);
-            L = fmaf(wl[w][h], e, L);
-            O = fmaf(wo[w][h][d], e, O);
+            const float e = __expf(wm[w * GRP + h] - M);
+            Ls = fmaf(wl[w * GRP + h], e, Ls);
+            O = fmaf(wo[(w * GRP + h) * HD + d], e, O);
         }
-        const long long pidx = (long long)(hk * GRP + h) * a.nsplit + split;
-        a.PO[pidx * HD + d] = O;
-        if (d == 0) { a.PML[pidx * 2] = M; a.PML[pidx * 2 + 1] = L; }
+        if (a.nsplit == 1) {
+            a.out[(long long)(hk * GRP + h) * HD + d] = Ls > 0.0f ? O / Ls : 0.0f;
+        } else {
+            const long long pidx = (long long)(hk * GRP + h) * a.nsplit + split;
+            a.PO[pidx * HD + d] = O;
+            if (d == 0) { a.PML[pidx * 2] = M; a.PML[pidx * 2 + 1] = Ls; }
+        }
     }
-}
+    if (a.nsplit == 1) return;
 
-// combine: one CTA per q head, one thread per dim
-__global__ void __launch_bounds__(256) k_attn_combine(const float* __restrict__ PO, const float* __restrict__ PML,
-                                                      float* __restrict__ out, int nsplit, int hd)
-{
-    tb_pdl_wait();
-    tb_pdl_trigger();
-    const int hq = blockIdx.x, d = threadIdx.x;
-    const float* pml = PML + (long long)hq * nsplit * 2;
-    float M = NEG_BIG;
-    for (int i = 0; i < nsplit; i++) M = fmaxf(M, pml[2 * i]);
-    float L = 0.0f, O = 0.0f;
-    for (int i = 0; i < nsplit; i++) {
-        const float e = __expf(pml[2 * i] - M);
-        L = fmaf(pml[2 * i + 1], e, L);
-        O = fmaf(PO[((long long)hq * nsplit + i) * hd + d], e, O);
+    // ---- the last split of this kv head to finish combines all of them
+    //      (ATTN_DEC_COMBINE, qwen3.js:2048-2069): out = sum_i e_i O_i / sum_i e_i l_i,
+    //      e_i = exp(m_i - max m).  Partials are read through L2 (ld.cg).
+    __threadfence();
+    __syncthreads();
+    int* last = reinterpret_cast<int*>(wm);          // wm/wl are free again after the loop above
+    if (threadIdx.x == 0) *last = atomicAdd(a.counters + hk, 1u) == (unsigned)(a.nsplit - 1);
+    __syncthreads();
+    if (!*last) return;
+    __threadfence();
+    float* wts = reinterpret_cast<float*>(smem + L::OFF_ST);    // [GRP][nsplit]
+    float* lsum = wl;                                            // [GRP]
+    for (int h = wid; h < GRP; h += ATT_WARPS) {
+        const float* pml = a.PML + (long long)(hk * GRP + h) * a.nsplit * 2;
+        float M = NEG_BIG;
+        for (int i = lane; i < a.nsplit; i += 32) M = fmaxf(M, __ldcg(pml + 2 * i));
+        M = warp_max(M);
+        float Ls = 0.0f;
+        for (int i = lane; i < a.nsplit; i += 32) {
+            const float e = __expf(__ldcg(pml + 2 * i) - M);
+            wts[h * a.nsplit + i] = e;
+            Ls = fmaf(__ldcg(pml + 2 * i + 1), e, Ls);
+        }
+        Ls = warp_sum(Ls);
+        if (lane == 0) lsum[h] = Ls;
     }
-    out[(long long)hq * hd + d] = L > 0.0f ? O / L : 0.0f;
+    __syncthreads();
+    // float4 columns (head h, dims 4c..4c+3); when there are fewer columns than
+    // threads, P threads share a column, each summing every P-th split with 8
+    // loads in flight, and the P partials are added in part order.
+    constexpr int NCOL = GRP * HD / 4;
+    constexpr int P = NCOL >= ATT_THREADS ? 1 : ATT_THREADS / NCOL;
+    float4* part = reinterpret_cast<float4*>(wts + GRP * ATT_MAXSPLIT);     // [P][NCOL]
+    for (int i = threadIdx.x; i < NCOL * P; i += ATT_THREADS) {
+        const int col = i % NCOL, pp = i / NCOL;
+        const int h = col / (HD / 4), c4 = col - h * (HD / 4);
+        const float4* po = reinterpret_cast<const float4*>(a.PO + (long long)(hk * GRP + h) * a.nsplit * HD) + c4;
+        const float* w = wts + h * a.nsplit;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        int k = pp;
+        for (; k + 7 * P < a.nsplit; k += 8 * P) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = __ldcg(po + (long long)(k + u * P) * (HD / 4));
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float e = w[k + u * P];
+                acc.x = fmaf(v[u].x, e, acc.x); acc.y = fmaf(v[u].y, e, acc.y);
+                acc.z = fmaf(v[u].z, e, acc.z); acc.w = fmaf(v[u].w, e, acc.w);
+            }
+        }
+        for (; k < a.nsplit; k += P) {
+            const float4 v = __ldcg(po + (long long)k * (HD / 4));
+            const float e = w[k];
+            acc.x = fmaf(v.x, e, acc.x); acc.y = fmaf(v.y, e, acc.y);
+            acc.z = fmaf(v.z, e, acc.z); acc.w = fmaf(v.w, e, acc.w);
+        }
+        part[pp * NCOL + col] = acc;
+    }
+    __syncthreads();
+    for (int col = threadIdx.x; col < NCOL; col += ATT_THREADS) {
+        const int h = col / (HD / 4), c4 = col - h * (HD / 4);
+        float4 O = part[col];
+        for (int pp = 1; pp < P; pp++) {
+            const float4 v = part[pp * NCOL + col];
+            O.x += v.x; O.y += v.y; O.z += v.z; O.w += v.w;
+        }
+        const float Ls = lsum[h];
+        const float4 res = Ls > 0.0f ? make_float4(O.x / Ls, O.y / Ls, O.z / Ls, O.w / Ls)
+                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        reinterpret_cast<float4*>(a.out + (long long)(hk * GRP + h) * HD)[c4] = res;
+    }
+    if (threadIdx.x == 0) a.counters[hk] = 0u;     // ready for the next call
 }
 
 template <int HD, int GRP>
 int launch_decode(tb_ctx* ctx, const AttnArgs& a)
 {
-    cudaError_t e = tb_launch(ctx, k_attn_decode<HD, GRP>, dim3(a.nKv, a.nsplit), dim3(ATT_THREADS), 0, a);
+    constexpr int bytes = DecLayout<HD, GRP>::BYTES;
+    static bool attr_set[64] = {};   // per device and instantiation; setting it twice is harmless
+    if (ctx->device >= 64 || !attr_set[ctx->device]) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_decode<HD, GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode smem attribute: %s", cudaGetErrorString(e));
+        if (ctx->device < 64) attr_set[ctx->device] = true;
+    }
+    cudaError_t e = tb_launch(ctx, k_attn_decode<HD, GRP>, dim3(a.nKv, a.nsplit), dim3(ATT_THREADS), bytes, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -271,47 +452,41 @@ int launch_decode(tb_ctx* ctx, const AttnArgs& a)
 }  // namespace
 
 // Split count used when the caller passes nsplit = 0: at least 128 keys per
-// CTA, and enough CTAs (nKv * nsplit) for ~4 per SM at long context.
+// CTA, and enough CTAs (nKv * nsplit) for ~2 per SM (the decode kernel's
+// shared-memory occupancy) at long context.
 int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv)
 {
     long long by_keys = (S + 127) / 128;
-    long long by_fill = (4LL * ctx->num_sms + nKv - 1) / nKv;
+    long long by_fill = (2LL * ctx->num_sms + nKv - 1) / nKv;
     long long n = std::min(by_keys, by_fill);
     return (int)std::max(1LL, std::min(n, 1024LL));
 }
 
 int tb_attn_decode_impl(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
                         const int8_t* Vq, const float* Vs, int64_t S, int64_t nHq, int64_t nKv, int64_t hd,
-                        int nsplit, float* PO, float* PML)
+                        int nsplit, float* PO, float* PML, unsigned* counters)
 {
-    AttnArgs a{qr, Kq, Ks, Vq, Vs, PO, PML, (int)S, (int)nHq, (int)nKv, nsplit, 0};
+    AttnArgs a{qr, Kq, Ks, Vq, Vs, PO, PML, out, counters, (int)S, (int)nHq, (int)nKv, nsplit, 0};
     a.per = (int)((S + nsplit - 1) / nsplit);
     const int grp = (int)(nHq / nKv);
-    int rc = TB_OK;
     if (hd == 128) {
         switch (grp) {
-        case 1: rc = launch_decode<128, 1>(ctx, a); break;
-        case 2: rc = launch_decode<128, 2>(ctx, a); break;
-        case 4: rc = launch_decode<128, 4>(ctx, a); break;
-        case 8: rc = launch_decode<128, 8>(ctx, a); break;
+        case 1: return launch_decode<128, 1>(ctx, a);
+        case 2: return launch_decode<128, 2>(ctx, a);
+        case 4: return launch_decode<128, 4>(ctx, a);
+        case 8: return launch_decode<128, 8>(ctx, a);
         default: return tb_fail(ctx, TB_ERR_UNSUPPORTED, "nHq/nKv = %d not built (1, 2, 4, 8)", grp);
         }
     } else if (hd == 64) {
         switch (grp) {
-        case 1: rc = launch_decode<64, 1>(ctx, a); break;
-        case 2: rc = launch_decode<64, 2>(ctx, a); break;
-        case 4: rc = launch_decode<64, 4>(ctx, a); break;
-        case 8: rc = launch_decode<64, 8>(ctx, a); break;
+        case 1: return launch_decode<64, 1>(ctx, a);
+        case 2: return launch_decode<64, 2>(ctx, a);
+        case 4: return launch_decode<64, 4>(ctx, a);
+        case 8: return launch_decode<64, 8>(ctx, a);
         default: return tb_fail(ctx, TB_ERR_UNSUPPORTED, "nHq/nKv = %d not built (1, 2, 4, 8)", grp);
         }
-    } else {
-        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "head_dim %lld not built (64, 128)", (long long)hd);
     }
-    if (rc) return rc;
-    cudaError_t e = tb_launch(ctx, k_attn_combine, dim3((unsigned)nHq), dim3((unsigned)hd), 0,
-                              (const float*)PO, (const float*)PML, out, nsplit, (int)hd);
-    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_combine launch: %s", cudaGetErrorString(e));
-    return TB_OK;
+    return tb_fail(ctx, TB_ERR_UNSUPPORTED, "head_dim %lld not built (64, 128)", (long long)hd);
 }
 
 int tb_attn_check(tb_ctx* ctx, const float* qr, const int8_t* Kq, const float* Ks, const int8_t* Vq, const float* Vs,
@@ -319,11 +494,12 @@ int tb_attn_check(tb_ctx* ctx, const float* qr, const int8_t* Kq, const float* K
 {
     TB_REQUIRE(ctx, qr && Kq && Ks && Vq && Vs, "null pointer");
     TB_REQUIRE(ctx, S >= 0 && S < (1LL << 31), "bad S");
-    TB_REQUIRE(ctx, nKv > 0 && nHq > 0 && nHq % nKv == 0 && nHq / nKv <= ATT_MAXG, "bad head counts nHq=%lld nKv=%lld",
-               (long long)nHq, (long long)nKv);
+    TB_REQUIRE(ctx, nKv > 0 && nKv <= TB_ATTN_MAX_KV && nHq > 0 && nHq % nKv == 0 && nHq / nKv <= ATT_MAXG,
+               "bad head counts nHq=%lld nKv=%lld", (long long)nHq, (long long)nKv);
     TB_REQUIRE(ctx, hd == 64 || hd == 128, "head_dim must be 64 or 128 (got %lld)", (long long)hd);
-    TB_REQUIRE(ctx, TB_ALIGNED(Kq, 16) && TB_ALIGNED(Vq, 16) && TB_ALIGNED(Ks, 16), "KV cache must be 16-byte aligned");
-    TB_REQUIRE(ctx, nsplit >= 0 && nsplit <= 1024, "nsplit must be 0..1024");
+    TB_REQUIRE(ctx, TB_ALIGNED(Kq, 16) && TB_ALIGNED(Vq, 16) && TB_ALIGNED(Ks, 16) && TB_ALIGNED(Vs, 16),
+               "KV cache must be 16-byte aligned");
+    TB_REQUIRE(ctx, nsplit >= 0 && nsplit <= ATT_MAXSPLIT, "nsplit must be 0..%d", ATT_MAXSPLIT);
     return TB_OK;
 }
 
@@ -364,12 +540,13 @@ TB_API int tb_attn_decode_q8(tb_ctx* ctx, float* out, const float* qr, const int
     if (!ctx) return TB_ERR_INVALID;
     int rc = tb_attn_check(ctx, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit);
     if (rc) return rc;
-    TB_REQUIRE(ctx, out != nullptr, "null output");
+    TB_REQUIRE(ctx, out != nullptr && TB_ALIGNED(out, 16), "output must be non-null and 16-byte aligned");
     if (nsplit == 0) nsplit = tb_attn_auto_nsplit(ctx, S, nKv);
     size_t po = (size_t)nHq * nsplit * hd * sizeof(float), pml = (size_t)nHq * nsplit * 2 * sizeof(float);
     float* scr = static_cast<float*>(tb_ctx_scratch(ctx, po + pml));
     if (!scr) return TB_ERR_NOMEM;
-    return tb_attn_decode_impl(ctx, out, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit, scr, scr + po / sizeof(float));
+    return tb_attn_decode_impl(ctx, out, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit, scr, scr + po / sizeof(float),
+                               ctx->attn_counters);
 }
 
 }  // extern "C"
@@ -391,10 +568,12 @@ TB_API int tb_attn_decode_q8(tb_ctx* ctx, float* out, const float* qr, const int
 //    that first call before any stream capture.
 //  * Every call shares the one array and it keeps the last call's contents.
 //    Nothing needs clearing (each split writes its partial before the combine
-//    reads it), but calls that overlap on the GPU (other streams, other contexts
-//    on the same device) race on it: order them.
+//    reads it; the split-arrival counters beside it start at zero and each call
+//    leaves them at zero), but calls that overlap on the GPU (other streams,
+//    other contexts on the same device) race on them: order them.
 constexpr size_t NOALLOC_SCRATCH_FLOATS = size_t(1) << 18;
 static __device__ __align__(256) float g_attn_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
+static __device__ unsigned g_attn_noalloc_counters[TB_ATTN_MAX_KV];
 
 #include <mutex>
 
@@ -402,10 +581,11 @@ namespace {
 constexpr int NOALLOC_MAX_DEVICES = 64;
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+unsigned* g_noalloc_cnt[NOALLOC_MAX_DEVICES] = {};
 
-// Device address of the array on ctx's device (host code may not use the
-// symbol itself as an address).
-int noalloc_scratch(tb_ctx* ctx, float** out)
+// Device addresses of the arrays on ctx's device (host code may not use the
+// symbols themselves as addresses).
+int noalloc_scratch(tb_ctx* ctx, float** out, unsigned** counters)
 {
     TB_REQUIRE(ctx, ctx->device >= 0 && ctx->device < NOALLOC_MAX_DEVICES, "device index out of range");
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
@@ -414,13 +594,17 @@ int noalloc_scratch(tb_ctx* ctx, float** out)
         cudaGetDevice(&prev);
         cudaError_t e = cudaSetDevice(ctx->device);
         void* p = nullptr;
+        void* c = nullptr;
         if (e == cudaSuccess) e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&c, g_attn_noalloc_counters);
         cudaSetDevice(prev);
-        if (e != cudaSuccess || !p)
+        if (e != cudaSuccess || !p || !c)
             return tb_fail(ctx, TB_ERR_CUDA, "cudaGetSymbolAddress(attention scratch): %s", cudaGetErrorString(e));
+        g_noalloc_cnt[ctx->device] = static_cast<unsigned*>(c);
         g_noalloc_ptr[ctx->device] = static_cast<float*>(p);
     }
     *out = g_noalloc_ptr[ctx->device];
+    *counters = g_noalloc_cnt[ctx->device];
     return TB_OK;
 }
 }  // namespace
@@ -432,7 +616,7 @@ extern "C" TB_API int tb_attn_decode_q8_noalloc(tb_ctx* ctx, float* out, const f
     if (!ctx) return TB_ERR_INVALID;
     int rc = tb_attn_check(ctx, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit);
     if (rc) return rc;
-    TB_REQUIRE(ctx, out != nullptr, "null output");
+    TB_REQUIRE(ctx, out != nullptr && TB_ALIGNED(out, 16), "output must be non-null and 16-byte aligned");
     if (nsplit == 0) nsplit = tb_attn_auto_nsplit(ctx, S, nKv);
     const size_t need = (size_t)nHq * nsplit * (hd + 2);
     if (need > NOALLOC_SCRATCH_FLOATS)
@@ -440,8 +624,9 @@ extern "C" TB_API int tb_attn_decode_q8_noalloc(tb_ctx* ctx, float* out, const f
                        "attn_decode_q8_noalloc: nHq*nsplit*(hd+2) = %zu floats exceeds the fixed scratch of %zu floats "
                        "(use fewer splits or tb_attn_decode_q8)", need, NOALLOC_SCRATCH_FLOATS);
     float* scr = nullptr;
-    rc = noalloc_scratch(ctx, &scr);
+    unsigned* cnt = nullptr;
+    rc = noalloc_scratch(ctx, &scr, &cnt);
     if (rc) return rc;
     return tb_attn_decode_impl(ctx, out, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit, scr,
-                               scr + (size_t)nHq * nsplit * hd);
+                               scr + (size_t)nHq * nsplit * hd, cnt);
 }

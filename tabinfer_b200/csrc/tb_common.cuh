@@ -16,6 +16,9 @@ struct tb_ctx {
     cudaStream_t own_stream = nullptr;  // created by tb_ctx_create, destroyed with the context
     std::string last_error;
     int* dev_error = nullptr;           // device word written by bounded waits that gave up
+    // split-arrival counters of the decode attention, one per kv head; zero
+    // between calls (the last split of a head resets its counter)
+    unsigned* attn_counters = nullptr;
     // scratch for the combined calls (quantized activations); grown on demand, never shrunk
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
@@ -92,5 +95,36 @@ __device__ __forceinline__ float warp_max(float v)
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+
+// packed f32x2 arithmetic (sm_100): two IEEE round-to-nearest lanes per instruction
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
+{
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n mov.b64 rc, {%6,%7};\n"
+        " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0,%1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b)
+{
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
+        " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0,%1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// signed bytes 0,1 (lo) or 2,3 (hi) of w as exact floats: PRMT builds 2^23 + (c+128),
+// one packed add removes the bias.
+__device__ __forceinline__ float2 sbytes_f2(uint32_t w, int hi)
+{
+    const uint32_t x = w ^ 0x80808080u;
+    const int b = hi ? 2 : 0;
+    return fadd2(make_float2(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7540 + b)),
+                             __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7541 + b))),
+                 make_float2(-8388736.0f, -8388736.0f));
+}
+
+constexpr int TB_ATTN_MAX_KV = 1024;   // kv heads per decode call (counter slots)
 
 static inline int tb_cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }

@@ -74,8 +74,12 @@ TB_API int tb_ctx_create(int device, tb_ctx** out)
     }
     if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&c->dev_error, sizeof(int)) != cudaSuccess ||
-        cudaMemset(c->dev_error, 0, sizeof(int)) != cudaSuccess) {
+        cudaMemset(c->dev_error, 0, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&c->attn_counters, TB_ATTN_MAX_KV * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(c->attn_counters, 0, TB_ATTN_MAX_KV * sizeof(unsigned)) != cudaSuccess) {
         cudaGetLastError();
+        if (c->dev_error) cudaFree(c->dev_error);
+        if (c->attn_counters) cudaFree(c->attn_counters);
         if (c->own_stream) cudaStreamDestroy(c->own_stream);
         delete c;
         cudaSetDevice(prev);
@@ -93,6 +97,7 @@ TB_API int tb_ctx_destroy(tb_ctx* ctx)
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->dev_error) cudaFree(ctx->dev_error);
+    if (ctx->attn_counters) cudaFree(ctx->attn_counters);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return TB_OK;
