@@ -346,6 +346,29 @@ def profile_case():
     print("profile case done", flush=True)
 
 
+def profile_attn(S):
+    """Three cold-L2 launches of int8-KV decode attention at context S (Qwen3-1.7B
+    heads: 16 q / 8 kv, hd 128; auto split count), for an ncu capture of one."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    nHq, nKv, hd = 16, 8, 128
+    Kq = torch.randint(-127, 128, (S, nKv * hd), device=dev, generator=g, dtype=torch.int8)
+    Vq = torch.randint(-127, 128, (S, nKv * hd), device=dev, generator=g, dtype=torch.int8)
+    Ks = torch.rand(S, nKv * hd // 32, device=dev, generator=g) + 0.5
+    Vs = torch.rand(S, nKv * hd // 32, device=dev, generator=g) + 0.5
+    qr = torch.randn(nHq * hd, device=dev, generator=g)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for it in range(3):
+        flush.fill_(it)
+        tb.attention_decode_q8(qr, (Kq, Ks, Vq, Vs), S, nHq, nKv, hd)
+    torch.cuda.synchronize()
+    err = tb.default_context(0).device_error()
+    assert err == 0, err
+    print("profile attn done", flush=True)
+
+
 def cpu_baseline_sample(threads, budget_s=12.0):
     """The transcribed CPU path (oracle/tb_cpu_ref.c, linearQ math) on a bounded
     sample: 2 decoder layers' 7 matrices + 1/16 of the lm_head rows, repeated
@@ -424,9 +447,14 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--profile-case", action="store_true",
                     help="one cold-L2 launch per kernel kind (for ncu), then exit")
+    ap.add_argument("--profile-attn", type=int, default=0, metavar="S",
+                    help="three cold-L2 decode-attention launches at context S (for ncu), then exit")
     args = ap.parse_args()
     if args.profile_case:
         profile_case()
+        return
+    if args.profile_attn:
+        profile_attn(args.profile_attn)
         return
 
     rank = int(os.environ.get("RANK", "0"))
