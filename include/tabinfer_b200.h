@@ -230,6 +230,26 @@ TB_API int tb_attn_decode_q8_noalloc(tb_ctx *ctx, float *out, const float *qr,
                                      const float *Vs, int64_t S, int64_t nHq, int64_t nKv,
                                      int64_t hd, int nsplit);
 
+/* Batched, graph-replayable forms (the decode step records them once and
+ * replays them every token).  `batch` sequences; sequence b's cache holds
+ * cache_rows rows and starts cache_rows rows after sequence b-1's; q/k/v/qr/out
+ * rows are [batch][heads*hd].  Positions live on the device: dpos[b] is the row
+ * written by the prep and the context is S_b = dpos[b] + 1 rows.  A position
+ * outside [0, cache_rows) sets the context's device error word
+ * (tb_ctx_device_error) and leaves that sequence's cache and output row
+ * unwritten / zero.  S_max (<= cache_rows) fixes the split count (nsplit = 0:
+ * automatic).  Same math as tb_attn_prep_q8 / tb_attn_decode_q8. */
+TB_API int tb_attn_prep_q8_batch(tb_ctx *ctx, const float *q, const float *k, const float *v,
+                                 const uint16_t *qw16, const uint16_t *kw16, float *qr,
+                                 int8_t *Kq, float *Ks, int8_t *Vq, float *Vs,
+                                 int64_t nHq, int64_t nKv, int64_t hd, int64_t batch,
+                                 int64_t cache_rows, const int32_t *dpos, float theta, float eps);
+TB_API int tb_attn_decode_q8_batch(tb_ctx *ctx, float *out, const float *qr,
+                                   const int8_t *Kq, const float *Ks, const int8_t *Vq,
+                                   const float *Vs, int64_t batch, int64_t cache_rows,
+                                   const int32_t *dpos, int64_t S_max, int64_t nHq, int64_t nKv,
+                                   int64_t hd, int nsplit);
+
 /* ---- decode-step glue ------------------------------------------------------ */
 
 /* Argmax over `rows` rows of n logits -> out_idx[row*stride + offset]
@@ -245,6 +265,79 @@ TB_API int tb_rmsnorm(tb_ctx *ctx, const float *x, const uint16_t *w16, float *y
 /* y[t,:] = f32(embed_f16[ids[idoff+t], :]).  embedGather, qwen3.js:1663-1675. */
 TB_API int tb_embed_gather(tb_ctx *ctx, const uint32_t *ids, int64_t idoff,
                            const uint16_t *embed_f16, float *y, int64_t T, int64_t H);
+
+/* bf16 -> f16 bits, rounded half-up as the loader's bf16ToF16bits
+ * (models/qwen3.js:3357-3390): the f16 copies of the embedding table and the
+ * norm weights. */
+TB_API int tb_convert_bf16_f16(tb_ctx *ctx, const uint16_t *in_bf16, uint16_t *out_f16, int64_t n);
+
+/* ---- Qwen3 decode step (models/qwen3.js forward, :3938-4069) ---------------
+ * A model object owns its weights (quantized on arrival), its int8 KV cache,
+ * its activations and the recorded step.  One step decodes one token for each
+ * of `batch` sequences: ids[b] (device, u32) is read by the embedding gather
+ * and overwritten with the argmax token; pos[b] (device, i32) is the cache row
+ * written this step and is advanced by one, so consecutive steps need no host
+ * work (the reference's GPU token history, :4055-4060).  The first
+ * tb_qwen3_decode_step records the step as a CUDA graph; later calls replay it
+ * on the context's stream.
+ *
+ * Tensor parallelism (tp_size > 1, one context and process per GPU): each
+ * rank keeps q/k/v and gate/up row blocks, o and down column blocks, its
+ * n_kv_heads/tp_size kv heads (with their q heads) and vocab/tp_size lm_head
+ * rows; partial o and down products are summed by an NCCL allreduce of the
+ * batch x hidden residual, and the argmax by an allgather of per-rank keys.
+ * Every rank passes the FULL bf16 tensors to tb_qwen3_set_weight and keeps its
+ * own slice (tb_qwen3_shard tells which). */
+typedef struct tb_qwen3_config {
+  int32_t hidden, layers, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+  float rope_theta, rms_eps;
+  int32_t max_seq;   /* KV cache rows per sequence */
+  int32_t batch;     /* sequences per step, 1..16 */
+  int32_t tp_size;   /* ranks sharing the model (1 = single GPU) */
+  int32_t tp_rank;
+} tb_qwen3_config;
+
+typedef struct tb_qwen3 tb_qwen3;
+
+/* weight kinds (checkpoint names as in the reference's _weights map) */
+enum {
+  TB_QW_EMBED = 0,       /* model.embed_tokens.weight   [vocab][hidden] -> f16 */
+  TB_QW_LM_HEAD = 1,     /* lm_head.weight              [vocab][hidden] -> int4 */
+  TB_QW_FINAL_NORM = 2,  /* model.norm.weight           [hidden]        -> f16 */
+  TB_QW_Q = 3,           /* layers.l.self_attn.q_proj   [n_heads*hd][hidden] */
+  TB_QW_K = 4,           /* k_proj [n_kv*hd][hidden] */
+  TB_QW_V = 5,           /* v_proj [n_kv*hd][hidden] */
+  TB_QW_O = 6,           /* o_proj [hidden][n_heads*hd] */
+  TB_QW_GATE = 7,        /* mlp.gate_proj [inter][hidden] */
+  TB_QW_UP = 8,          /* mlp.up_proj   [inter][hidden] */
+  TB_QW_DOWN = 9,        /* mlp.down_proj [hidden][inter] */
+  TB_QW_LN_ATTN = 10,    /* input_layernorm [hidden] */
+  TB_QW_LN_MLP = 11,     /* post_attention_layernorm [hidden] */
+  TB_QW_Q_NORM = 12,     /* self_attn.q_norm [hd] */
+  TB_QW_K_NORM = 13      /* self_attn.k_norm [hd] */
+};
+
+/* Host-only: the block of a full [rows][cols] tensor of `kind` that rank
+ * cfg->tp_rank keeps (norm vectors count as one row). */
+TB_API int tb_qwen3_shard(const tb_qwen3_config *cfg, int kind, int64_t *row0, int64_t *nrows,
+                          int64_t *col0, int64_t *ncols);
+TB_API int tb_qwen3_create(tb_ctx *ctx, const tb_qwen3_config *cfg, tb_qwen3 **out);
+TB_API int tb_qwen3_destroy(tb_qwen3 *m);
+/* Full bf16 tensor [rows][cols] on the device (16-byte aligned); quantized /
+ * converted into the model's shard, ordered on the context's stream. */
+TB_API int tb_qwen3_set_weight(tb_qwen3 *m, int kind, int layer, const uint16_t *bf16,
+                               int64_t rows, int64_t cols);
+/* This rank's cache of a layer: int8 [batch][max_seq][n_kv/tp*hd] and f32
+ * scales [batch][max_seq][n_kv/tp*hd/32] (fill prefixes with tb_kv_quant_write). */
+TB_API int tb_qwen3_kv(tb_qwen3 *m, int layer, int8_t **Kq, float **Ks, int8_t **Vq, float **Vs);
+/* Device buffers: ids u32 [batch], pos i32 [batch], logits f32 [batch][vocab/tp]. */
+TB_API int tb_qwen3_io(tb_qwen3 *m, uint32_t **ids, int32_t **pos, float **logits);
+/* 128-byte NCCL unique id (rank 0 makes it, every rank passes it to tp_init). */
+TB_API int tb_nccl_unique_id(void *out128);
+TB_API int tb_qwen3_tp_init(tb_qwen3 *m, const void *unique_id128);
+TB_API int tb_qwen3_decode_step(tb_qwen3 *m);
+/* Kernels of this library in one recorded step, and NCCL collectives. */
+TB_API int tb_qwen3_launches_per_step(tb_qwen3 *m, int *kernels, int *collectives);
 
 #ifdef __cplusplus
 }

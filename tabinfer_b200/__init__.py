@@ -15,3 +15,4 @@ from .ops import (  # noqa: F401
     gate_up_silu_dp4, pack_ternary, quantize_act, gemv_tern, linear_tern,
     attn_prep_q8, kv_quant_write, attention_decode_q8, argmax, rmsnorm, embed_gather,
 )
+from .qwen3 import Qwen3, QWEN3_1_7B, QWEN3_0_6B  # noqa: F401,E402

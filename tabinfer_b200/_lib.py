@@ -55,7 +55,34 @@ SIGNATURES = {
     "tb_argmax": [P, P, I64, I64, P, I64],
     "tb_rmsnorm": [P, P, P, P, I64, I64, F32],
     "tb_embed_gather": [P, P, I64, P, P, I64, I64],
+    "tb_attn_prep_q8_batch": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, P, F32, F32],
+    "tb_attn_decode_q8_batch": [P, P, P, P, P, P, P, I64, I64, P, I64, I64, I64, I64, I32],
+    "tb_convert_bf16_f16": [P, P, P, I64],
+    "tb_qwen3_shard": [P, I32, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)],
+    "tb_qwen3_create": [P, P, ctypes.POINTER(P)],
+    "tb_qwen3_destroy": [P],
+    "tb_qwen3_set_weight": [P, I32, I32, P, I64, I64],
+    "tb_qwen3_kv": [P, I32, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],
+    "tb_qwen3_io": [P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],
+    "tb_nccl_unique_id": [P],
+    "tb_qwen3_tp_init": [P, P],
+    "tb_qwen3_decode_step": [P],
+    "tb_qwen3_launches_per_step": [P, ctypes.POINTER(I32), ctypes.POINTER(I32)],
 }
+
+
+class Qwen3Config(ctypes.Structure):
+    """tb_qwen3_config (include/tabinfer_b200.h)."""
+    _fields_ = [("hidden", ctypes.c_int32), ("layers", ctypes.c_int32), ("n_heads", ctypes.c_int32),
+                ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float),
+                ("max_seq", ctypes.c_int32), ("batch", ctypes.c_int32), ("tp_size", ctypes.c_int32),
+                ("tp_rank", ctypes.c_int32)]
+
+
+# weight kinds (TB_QW_*)
+QW_EMBED, QW_LM_HEAD, QW_FINAL_NORM, QW_Q, QW_K, QW_V, QW_O, QW_GATE, QW_UP, QW_DOWN, \
+    QW_LN_ATTN, QW_LN_MLP, QW_Q_NORM, QW_K_NORM = range(14)
 RESTYPES = {
     "tb_last_error": ctypes.c_char_p,
     "tb_ctx_get_stream": P,

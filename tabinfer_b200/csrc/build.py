@@ -59,7 +59,7 @@ def build(verbose=False, jobs=8):
             if log:
                 print("==", s, "\n" + log)
     if not os.path.exists(OUT) or max(os.path.getmtime(o) for o in objs) > os.path.getmtime(OUT):
-        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", OUT + ".tmp"] + objs
+        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", OUT + ".tmp"] + objs + ["-ldl"]
         subprocess.check_call(cmd)
         os.replace(OUT + ".tmp", OUT)
     return OUT

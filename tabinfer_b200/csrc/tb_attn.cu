@@ -13,7 +13,7 @@
 // keeps its own online-softmax state; the CTA merges warps and writes one
 // (m, l, o) partial per q head; a combine kernel merges the splits
 // (ATTN_DEC_COMBINE, qwen3.js:2048-2069).
-#include "tb_common.cuh"
+#include "tb_internal.h"
 
 namespace {
 
@@ -29,21 +29,40 @@ __device__ __forceinline__ int8_t snorm8(float v)
     return (int8_t)floorf(__fadd_rn(0.5f, __fmul_rn(127.0f, c)));
 }
 
+// Error word codes written by the attention kernels when a device-resident
+// position is outside the cache (the host cannot check it).
+constexpr int ERR_ATTN_POS = 0x6a01;
+
 // ---- fused prep: q rope, k rope + quant-write, v quant-write ---------------
-// grid = nHq + 2*nKv CTAs, block = hd threads (hd % 32 == 0, hd <= 256).
+// grid = (nHq + 2*nKv, B) CTAs, block = hd threads (hd % 32 == 0, hd <= 256).
+// Sequence b reads q/k/v row b, writes qr row b and cache row pos_b of its own
+// cache (cache_rows rows per sequence); pos_b = dpos[b] when dpos is given
+// (graph-replayable decode), else `pos`.
 __global__ void __launch_bounds__(256) k_attn_prep(const float* __restrict__ q, const float* __restrict__ k,
                                                    const float* __restrict__ v, const uint16_t* __restrict__ qw,
                                                    const uint16_t* __restrict__ kw, float* __restrict__ qr,
                                                    int8_t* __restrict__ Kq, float* __restrict__ Ks,
                                                    int8_t* __restrict__ Vq, float* __restrict__ Vs,
-                                                   int nHq, int nKv, int hd, long long pos, float theta, float eps)
+                                                   int nHq, int nKv, int hd, long long pos, float theta, float eps,
+                                                   const int* __restrict__ dpos, long long cache_rows, int* err)
 {
     __shared__ float rk[256];
     __shared__ float red[8];
     tb_pdl_wait();
     tb_pdl_trigger();
     const int j = threadIdx.x, lane = j & 31, wid = j >> 5, nw = hd >> 5;
-    const int role = blockIdx.x;
+    const int role = blockIdx.x, b = blockIdx.y;
+    if (dpos) {
+        pos = dpos[b];
+        if (pos < 0 || pos >= cache_rows) {
+            if (j == 0) atomicExch(err, ERR_ATTN_POS);
+            return;
+        }
+    }
+    const long long cache_off = (long long)b * cache_rows * nKv * hd;
+    Kq += cache_off; Vq += cache_off; Ks += cache_off / 32; Vs += cache_off / 32;
+    q += (long long)b * nHq * hd; qr += (long long)b * nHq * hd;
+    k += (long long)b * nKv * hd; v += (long long)b * nKv * hd;
     const bool isQ = role < nHq, isK = !isQ && role < nHq + nKv;
     const int head = isQ ? role : (isK ? role - nHq : role - nHq - nKv);
     const float* src = isQ ? q : (isK ? k : v);
@@ -107,8 +126,12 @@ struct AttnArgs {
     float* PO;             // [nHq][nsplit][hd]
     float* PML;            // [nHq][nsplit][2]
     float* out;            // [nHq*hd]
-    unsigned* counters;    // [nKv] split arrivals, zero between calls
-    int S, nHq, nKv, nsplit, per;
+    unsigned* counters;    // [B][nKv] split arrivals, zero between calls
+    const int* dpos;       // [B] device positions (context S_b = dpos[b] + 1), or null: S for all
+    int* err;              // device error word
+    long long cache_rows;  // rows of each sequence's cache
+    int S, nHq, nKv, nsplit;
+    int grid_z;            // sequences
 };
 
 // ---- cp.async (16-byte and 8-byte global -> shared copies, per thread) -----
@@ -172,10 +195,31 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
     float* wm = reinterpret_cast<float*>(smem + L::OFF_WM);
     float* wl = reinterpret_cast<float*>(smem + L::OFF_WL);
 
-    const int hk = blockIdx.x, split = blockIdx.y;
+    const int hk = blockIdx.x, split = blockIdx.y, zb = blockIdx.z;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const long long row_elems = (long long)a.nKv * HD, row_groups = row_elems / 32;
-    const int c0 = split * a.per, c1 = min(a.S, c0 + a.per);
+    // this CTA's sequence: its cache, q row, partials, output and counters
+    const int8_t* Kq = a.Kq + zb * a.cache_rows * row_elems;
+    const int8_t* Vq = a.Vq + zb * a.cache_rows * row_elems;
+    const float* Ks = a.Ks + zb * a.cache_rows * row_groups;
+    const float* Vs = a.Vs + zb * a.cache_rows * row_groups;
+    const float* qrow = a.qr + (long long)zb * a.nHq * HD;
+    float* PO = a.PO + (long long)zb * a.nHq * a.nsplit * HD;
+    float* PML = a.PML + (long long)zb * a.nHq * a.nsplit * 2;
+    float* outp = a.out + (long long)zb * a.nHq * HD;
+    unsigned* counter = a.counters + (long long)zb * a.nKv + hk;
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    int S = a.S;
+    if (a.dpos) {
+        S = a.dpos[zb] + 1;
+        if (S < 1 || S > a.cache_rows) {
+            if (threadIdx.x == 0) atomicExch(a.err, ERR_ATTN_POS);
+            S = 0;   // every split empty: the output row is written as zeros
+        }
+    }
+    const int per = (S + a.nsplit - 1) / a.nsplit;
+    const int c0 = split * per, c1 = min(S, c0 + per);
     const int span = c1 - c0;
     const int ntile = span > wid * 32 ? (span - wid * 32 + ATT_WARPS * 32 - 1) / (ATT_WARPS * 32) : 0;
     uint8_t* stages = smem + L::OFF_ST + wid * NST * L::STAGE;
@@ -195,16 +239,16 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
             if (tb0 + kr < c1) {
                 const long long src = (long long)(tb0 + kr) * row_elems + hk * HD + ch * 16;
                 const int dst = (kr * KV16 + (ch ^ (kr & (KV16 - 1)))) * 16;
-                cp_async16(st + L::ST_K + dst, a.Kq + src);
-                cp_async16(st + L::ST_V + dst, a.Vq + src);
+                cp_async16(st + L::ST_K + dst, Kq + src);
+                cp_async16(st + L::ST_V + dst, Vq + src);
             }
         }
         const int t = tb0 + lane;
         if (t < c1) {
             float* ksd = reinterpret_cast<float*>(st + L::ST_KS) + lane * NG;
             float* vsd = reinterpret_cast<float*>(st + L::ST_VS) + lane * NG;
-            const float* ksr = a.Ks + (long long)t * row_groups + hk * NG;
-            const float* vsr = a.Vs + (long long)t * row_groups + hk * NG;
+            const float* ksr = Ks + (long long)t * row_groups + hk * NG;
+            const float* vsr = Vs + (long long)t * row_groups + hk * NG;
             if (NG * 4 == 16) {
                 cp_async16(ksd, ksr);
                 cp_async16(vsd, vsr);
@@ -216,11 +260,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
         cp_async_commit();
     };
 
-    tb_pdl_wait();
-    tb_pdl_trigger();
     issue(0, 0);
     const float qscale = rsqrtf((float)HD) * (1.0f / 127.0f);
-    for (int i = threadIdx.x; i < GRP * HD; i += ATT_THREADS) qs[i] = a.qr[(long long)hk * GRP * HD + i];
+    for (int i = threadIdx.x; i < GRP * HD; i += ATT_THREADS) qs[i] = qrow[(long long)hk * GRP * HD + i];
     __syncthreads();
 
     float m[GRP], l[GRP];
@@ -350,11 +392,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
             O = fmaf(wo[(w * GRP + h) * HD + d], e, O);
         }
         if (a.nsplit == 1) {
-            a.out[(long long)(hk * GRP + h) * HD + d] = Ls > 0.0f ? O / Ls : 0.0f;
+            outp[(long long)(hk * GRP + h) * HD + d] = Ls > 0.0f ? O / Ls : 0.0f;
         } else {
             const long long pidx = (long long)(hk * GRP + h) * a.nsplit + split;
-            a.PO[pidx * HD + d] = O;
-            if (d == 0) { a.PML[pidx * 2] = M; a.PML[pidx * 2 + 1] = Ls; }
+            PO[pidx * HD + d] = O;
+            if (d == 0) { PML[pidx * 2] = M; PML[pidx * 2 + 1] = Ls; }
         }
     }
     if (a.nsplit == 1) return;
@@ -365,14 +407,14 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
     __threadfence();
     __syncthreads();
     int* last = reinterpret_cast<int*>(wm);          // wm/wl are free again after the loop above
-    if (threadIdx.x == 0) *last = atomicAdd(a.counters + hk, 1u) == (unsigned)(a.nsplit - 1);
+    if (threadIdx.x == 0) *last = atomicAdd(counter, 1u) == (unsigned)(a.nsplit - 1);
     __syncthreads();
     if (!*last) return;
     __threadfence();
     float* wts = reinterpret_cast<float*>(smem + L::OFF_ST);    // [GRP][nsplit]
     float* lsum = wl;                                            // [GRP]
     for (int h = wid; h < GRP; h += ATT_WARPS) {
-        const float* pml = a.PML + (long long)(hk * GRP + h) * a.nsplit * 2;
+        const float* pml = PML + (long long)(hk * GRP + h) * a.nsplit * 2;
         float M = NEG_BIG;
         for (int i = lane; i < a.nsplit; i += 32) M = fmaxf(M, __ldcg(pml + 2 * i));
         M = warp_max(M);
@@ -395,7 +437,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
     for (int i = threadIdx.x; i < NCOL * P; i += ATT_THREADS) {
         const int col = i % NCOL, pp = i / NCOL;
         const int h = col / (HD / 4), c4 = col - h * (HD / 4);
-        const float4* po = reinterpret_cast<const float4*>(a.PO + (long long)(hk * GRP + h) * a.nsplit * HD) + c4;
+        const float4* po = reinterpret_cast<const float4*>(PO + (long long)(hk * GRP + h) * a.nsplit * HD) + c4;
         const float* w = wts + h * a.nsplit;
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         int k = pp;
@@ -429,9 +471,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
         const float Ls = lsum[h];
         const float4 res = Ls > 0.0f ? make_float4(O.x / Ls, O.y / Ls, O.z / Ls, O.w / Ls)
                                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        reinterpret_cast<float4*>(a.out + (long long)(hk * GRP + h) * HD)[c4] = res;
+        reinterpret_cast<float4*>(outp + (long long)(hk * GRP + h) * HD)[c4] = res;
     }
-    if (threadIdx.x == 0) a.counters[hk] = 0u;     // ready for the next call
+    if (threadIdx.x == 0) *counter = 0u;     // ready for the next call
 }
 
 template <int HD, int GRP>
@@ -444,7 +486,7 @@ int launch_decode(tb_ctx* ctx, const AttnArgs& a)
         if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode smem attribute: %s", cudaGetErrorString(e));
         if (ctx->device < 64) attr_set[ctx->device] = true;
     }
-    cudaError_t e = tb_launch(ctx, k_attn_decode<HD, GRP>, dim3(a.nKv, a.nsplit), dim3(ATT_THREADS), bytes, a);
+    cudaError_t e = tb_launch(ctx, k_attn_decode<HD, GRP>, dim3(a.nKv, a.nsplit, a.grid_z), dim3(ATT_THREADS), bytes, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -462,12 +504,16 @@ int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv)
     return (int)std::max(1LL, std::min(n, 1024LL));
 }
 
+// batch sequences (grid.z); sequence b's cache starts cache_rows rows after
+// sequence b-1's; with dpos, S_b = dpos[b] + 1 is read on the device.
 int tb_attn_decode_impl(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
                         const int8_t* Vq, const float* Vs, int64_t S, int64_t nHq, int64_t nKv, int64_t hd,
-                        int nsplit, float* PO, float* PML, unsigned* counters)
+                        int nsplit, float* PO, float* PML, unsigned* counters, int64_t batch,
+                        int64_t cache_rows, const int32_t* dpos)
 {
-    AttnArgs a{qr, Kq, Ks, Vq, Vs, PO, PML, out, counters, (int)S, (int)nHq, (int)nKv, nsplit, 0};
-    a.per = (int)((S + nsplit - 1) / nsplit);
+    AttnArgs a{qr, Kq, Ks, Vq, Vs, PO, PML, out, counters, (const int*)dpos, ctx->dev_error,
+               (long long)(cache_rows > 0 ? cache_rows : S), (int)S, (int)nHq, (int)nKv, nsplit};
+    a.grid_z = (int)batch;
     const int grp = (int)(nHq / nKv);
     if (hd == 128) {
         switch (grp) {
@@ -514,7 +560,24 @@ TB_API int tb_attn_prep_q8(tb_ctx* ctx, const float* q, const float* k, const fl
     TB_REQUIRE(ctx, hd % 32 == 0 && hd >= 32 && hd <= 256, "head_dim must be a multiple of 32 in [32, 256]");
     TB_REQUIRE(ctx, nHq > 0 && nKv > 0 && pos >= 0, "bad head counts or position");
     cudaError_t e = tb_launch(ctx, k_attn_prep, dim3((unsigned)(nHq + 2 * nKv)), dim3((unsigned)hd), 0, q, k, v, qw16,
-                              kw16, qr, Kq, Ks, Vq, Vs, (int)nHq, (int)nKv, (int)hd, (long long)pos, theta, eps);
+                              kw16, qr, Kq, Ks, Vq, Vs, (int)nHq, (int)nKv, (int)hd, (long long)pos, theta, eps,
+                              (const int*)nullptr, (long long)(pos + 1), ctx->dev_error);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_prep launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_attn_prep_q8_batch(tb_ctx* ctx, const float* q, const float* k, const float* v, const uint16_t* qw16,
+                                 const uint16_t* kw16, float* qr, int8_t* Kq, float* Ks, int8_t* Vq, float* Vs,
+                                 int64_t nHq, int64_t nKv, int64_t hd, int64_t batch, int64_t cache_rows,
+                                 const int32_t* dpos, float theta, float eps)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, q && k && v && qw16 && kw16 && qr && Kq && Ks && Vq && Vs && dpos, "null pointer");
+    TB_REQUIRE(ctx, hd % 32 == 0 && hd >= 32 && hd <= 256, "head_dim must be a multiple of 32 in [32, 256]");
+    TB_REQUIRE(ctx, nHq > 0 && nKv > 0 && batch > 0 && batch <= 65535 && cache_rows > 0, "bad head counts, batch or cache rows");
+    cudaError_t e = tb_launch(ctx, k_attn_prep, dim3((unsigned)(nHq + 2 * nKv), (unsigned)batch), dim3((unsigned)hd), 0,
+                              q, k, v, qw16, kw16, qr, Kq, Ks, Vq, Vs, (int)nHq, (int)nKv, (int)hd, 0LL, theta, eps,
+                              (const int*)dpos, (long long)cache_rows, ctx->dev_error);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_prep launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -547,6 +610,26 @@ TB_API int tb_attn_decode_q8(tb_ctx* ctx, float* out, const float* qr, const int
     if (!scr) return TB_ERR_NOMEM;
     return tb_attn_decode_impl(ctx, out, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit, scr, scr + po / sizeof(float),
                                ctx->attn_counters);
+}
+
+TB_API int tb_attn_decode_q8_batch(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
+                                   const int8_t* Vq, const float* Vs, int64_t batch, int64_t cache_rows,
+                                   const int32_t* dpos, int64_t S_max, int64_t nHq, int64_t nKv, int64_t hd, int nsplit)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    int rc = tb_attn_check(ctx, qr, Kq, Ks, Vq, Vs, S_max, nHq, nKv, hd, nsplit);
+    if (rc) return rc;
+    TB_REQUIRE(ctx, out != nullptr && TB_ALIGNED(out, 16), "output must be non-null and 16-byte aligned");
+    TB_REQUIRE(ctx, dpos != nullptr, "null positions");
+    TB_REQUIRE(ctx, batch > 0 && batch <= 65535 && batch * nKv <= TB_ATTN_MAX_KV, "batch * nKv must be <= %d",
+               TB_ATTN_MAX_KV);
+    TB_REQUIRE(ctx, cache_rows >= S_max && S_max >= 1, "S_max must be in [1, cache_rows]");
+    if (nsplit == 0) nsplit = tb_attn_auto_nsplit(ctx, S_max, nKv * batch);
+    size_t po = (size_t)batch * nHq * nsplit * hd * sizeof(float), pml = (size_t)batch * nHq * nsplit * 2 * sizeof(float);
+    float* scr = static_cast<float*>(tb_ctx_scratch(ctx, po + pml));
+    if (!scr) return TB_ERR_NOMEM;
+    return tb_attn_decode_impl(ctx, out, qr, Kq, Ks, Vq, Vs, S_max, nHq, nKv, hd, nsplit, scr,
+                               scr + po / sizeof(float), ctx->attn_counters, batch, cache_rows, dpos);
 }
 
 }  // extern "C"

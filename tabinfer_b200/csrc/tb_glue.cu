@@ -1,5 +1,6 @@
 // tb_glue.cu -- decode-step glue: argmax, RMSNorm, embedding gather.
 #include "tb_act.cuh"
+#include "tb_internal.h"
 
 namespace {
 
@@ -55,8 +56,12 @@ __global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p1(const float* __restr
     if (threadIdx.x == 0) part[(long long)row * gridDim.x + blockIdx.x] = best;
 }
 
+// stage 2: one block per row.  Writes the row's index (out, + idx_base: the
+// first global row of this vocab shard) and/or its ordered key (out_key, for a
+// cross-shard merge), and advances the row's position (pos_inc) when given.
 __global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p2(const unsigned long long* __restrict__ part, int nparts,
-                                                            uint32_t* __restrict__ out)
+                                                            uint32_t* __restrict__ out, unsigned long long* out_key,
+                                                            unsigned idx_base, int* pos_inc)
 {
     tb_pdl_wait();
     tb_pdl_trigger();
@@ -67,7 +72,30 @@ __global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p2(const unsigned long 
         best = k > best ? k : best;
     }
     best = block_max_key(best);
-    if (threadIdx.x == 0) out[row] = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+    if (threadIdx.x == 0) {
+        const uint32_t idx = 0xffffffffu - (uint32_t)(best & 0xffffffffu) + idx_base;
+        if (out) out[row] = idx;
+        if (out_key) out_key[row] = (best & 0xffffffff00000000ull) | (0xffffffffu - idx);
+        if (pos_inc) pos_inc[row] += 1;
+    }
+}
+
+// merge of per-shard keys [nshard][rows]: the largest key wins (value, then the
+// lower global index), as a single argmax over the whole vocabulary would.
+__global__ void k_argmax_merge(const unsigned long long* __restrict__ keys, int nshard, int rows,
+                               uint32_t* __restrict__ out, int* pos_inc)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    unsigned long long best = 0ull;
+    for (int s = 0; s < nshard; s++) {
+        const unsigned long long k = keys[(long long)s * rows + row];
+        best = k > best ? k : best;
+    }
+    out[row] = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+    if (pos_inc) pos_inc[row] += 1;
 }
 
 // RMSNorm, qwen3.js:60-88: one 256-thread CTA per row (the reduction the
@@ -101,13 +129,22 @@ __global__ void __launch_bounds__(256) k_embed(const uint32_t* __restrict__ ids,
 }  // namespace
 
 int tb_argmax_impl(tb_ctx* ctx, const float* x, int64_t n, int64_t rows, uint32_t* out, unsigned long long* part,
-                   int nparts)
+                   int nparts, unsigned long long* out_key, uint32_t idx_base, int32_t* pos_inc)
 {
     cudaError_t e = tb_launch(ctx, k_argmax_p1, dim3(nparts, (unsigned)rows), dim3(AMAX_THREADS), 0, x, (long long)n, part);
     if (e == cudaSuccess)
         e = tb_launch(ctx, k_argmax_p2, dim3((unsigned)rows), dim3(AMAX_THREADS), 0,
-                      (const unsigned long long*)part, nparts, out);
+                      (const unsigned long long*)part, nparts, out, out_key, (unsigned)idx_base, (int*)pos_inc);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "argmax launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+int tb_argmax_merge_impl(tb_ctx* ctx, const unsigned long long* keys, int nshard, int rows, uint32_t* out,
+                         int32_t* pos_inc)
+{
+    cudaError_t e = tb_launch(ctx, k_argmax_merge, dim3((unsigned)((rows + 127) / 128)), dim3(128), 0, keys, nshard,
+                              rows, out, (int*)pos_inc);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "argmax merge launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
 
@@ -127,7 +164,7 @@ TB_API int tb_argmax(tb_ctx* ctx, const float* x, int64_t n, int64_t rows, uint3
     int nparts = tb_argmax_parts(ctx, n);
     auto* part = static_cast<unsigned long long*>(tb_ctx_scratch(ctx, (size_t)rows * nparts * 8));
     if (!part) return TB_ERR_NOMEM;
-    return tb_argmax_impl(ctx, x, n, rows, out_idx + out_offset, part, nparts);
+    return tb_argmax_impl(ctx, x, n, rows, out_idx + out_offset, part, nparts, nullptr, 0, nullptr);
 }
 
 TB_API int tb_rmsnorm(tb_ctx* ctx, const float* x, const uint16_t* w16, float* y, int64_t T, int64_t H, float eps)

@@ -7,6 +7,7 @@
 // loader or its quant cache are read unchanged): pack u32 [N][K/8], weight k of
 // row n in word k/8 at bits 4*(k%8) as q+8; scales f16 [N][K/32].
 #include "tb_act.cuh"
+#include "tb_internal.h"
 
 namespace {
 
@@ -41,13 +42,18 @@ __device__ __forceinline__ double js_round(double v)
 }
 
 // One thread per (row, 32-group).  The JS runs in doubles, so does this.
+// Row n of the source starts ld elements after row n-1 (ld = K for a whole
+// matrix; a column slice of a wider matrix for a row-split shard: the groups
+// of a slice that starts at a multiple of 32 are the full matrix's groups).
 __global__ void __launch_bounds__(256) k_quant_int4_g32(const uint16_t* __restrict__ w, uint32_t* __restrict__ pack,
-                                                        uint16_t* __restrict__ scales, long long ngroups)
+                                                        uint16_t* __restrict__ scales, long long ngroups,
+                                                        long long gpr, long long ld)
 {
     tb_pdl_wait();
     for (long long gi = blockIdx.x * (long long)blockDim.x + threadIdx.x; gi < ngroups;
          gi += (long long)gridDim.x * blockDim.x) {
-        const uint4* src = reinterpret_cast<const uint4*>(w + gi * 32);
+        const long long row = gi / gpr;
+        const uint4* src = reinterpret_cast<const uint4*>(w + row * ld + (gi - row * gpr) * 32);
         uint32_t u[16];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -77,6 +83,16 @@ __global__ void __launch_bounds__(256) k_quant_int4_g32(const uint16_t* __restri
         reinterpret_cast<uint4*>(pack)[gi] = make_uint4(words[0], words[1], words[2], words[3]);
         scales[gi] = (uint16_t)sb;
     }
+}
+
+// bf16ToF16bits, models/qwen3.js:3386-3390: the loader's f16 copy of the
+// embedding table and norm weights (bf16 -> f32 exactly -> f16 rounded half-up).
+__global__ void __launch_bounds__(256) k_bf16_to_f16_js(const uint16_t* __restrict__ in, uint16_t* __restrict__ out,
+                                                        long long n)
+{
+    tb_pdl_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = (uint16_t)js_f32_to_f16(__uint_as_float((uint32_t)in[i] << 16));
 }
 
 // ---------------------------------------------------------------------------
@@ -132,6 +148,20 @@ __global__ void __launch_bounds__(256) k_rmsnorm_q8(const float* __restrict__ x,
 
 }  // namespace
 
+// N x K slice of a row-major bf16 matrix with row stride ld (elements; w and
+// ld*2 bytes 16-byte aligned) -> int4 G32 pack [N][K/8] + f16 scales [N][K/32].
+int tb_quant_int4_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint32_t* pack, uint16_t* scales,
+                               int64_t N, int64_t K)
+{
+    TB_REQUIRE(ctx, TB_ALIGNED(w, 16) && ld % 8 == 0 && ld >= K, "quant_int4: source must be 16-byte aligned rows");
+    long long ng = N * (K / 32);
+    int grid = (int)std::min<long long>((ng + 255) / 256, (long long)ctx->num_sms * 16);
+    cudaError_t e = tb_launch(ctx, k_quant_int4_g32, dim3(grid), dim3(256), 0, w, pack, scales, ng,
+                              (long long)(K / 32), (long long)ld);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_int4 launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
 int tb_quant_q8_impl(tb_ctx* ctx, const float* x, int8_t* xq, float* xs, int32_t* xsum16, int64_t T, int64_t K)
 {
     TB_REQUIRE(ctx, x && xq && xs, "null pointer");
@@ -151,10 +181,17 @@ TB_API int tb_quant_int4_g32(tb_ctx* ctx, const uint16_t* w, uint32_t* pack, uin
     TB_REQUIRE(ctx, w && pack && scales, "null pointer");
     TB_REQUIRE(ctx, N > 0 && K > 0 && K % 32 == 0, "bad shape N=%lld K=%lld (K%%32 must be 0)", (long long)N, (long long)K);
     TB_REQUIRE(ctx, TB_ALIGNED(w, 16) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 2), "misaligned pointer");
-    long long ng = N * (K / 32);
-    int grid = (int)std::min<long long>((ng + 255) / 256, (long long)ctx->num_sms * 16);
-    cudaError_t e = tb_launch(ctx, k_quant_int4_g32, dim3(grid), dim3(256), 0, w, pack, scales, ng);
-    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_int4 launch: %s", cudaGetErrorString(e));
+    return tb_quant_int4_strided_impl(ctx, w, K, pack, scales, N, K);
+}
+
+TB_API int tb_convert_bf16_f16(tb_ctx* ctx, const uint16_t* in, uint16_t* out, int64_t n)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, in && out && n >= 0, "null pointer or negative size");
+    if (n == 0) return TB_OK;
+    int grid = (int)std::min<long long>((n + 255) / 256, (long long)ctx->num_sms * 16);
+    cudaError_t e = tb_launch(ctx, k_bf16_to_f16_js, dim3(grid), dim3(256), 0, in, out, (long long)n);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "bf16_to_f16 launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
 

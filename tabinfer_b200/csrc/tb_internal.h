@@ -1,0 +1,38 @@
+// tb_internal.h -- library-internal entry points shared between translation
+// units (not part of the C ABI): the unchecked launch paths behind the public
+// calls, for callers that own their buffers (the model runner records them into
+// one CUDA graph, so nothing may allocate).
+#pragma once
+#include "tb_common.cuh"
+
+int tb_gemv_dp4a_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                      const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
+                      float eps, int64_t K, int batch, int acc);
+int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
+                     int64_t N, int64_t K, int batch, int acc);
+int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,
+                      const int32_t* xsum, int64_t N, int64_t K, int batch, const float* act_scale);
+int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K);
+
+// split-KV decode attention over `batch` sequences; sequence b's cache starts
+// cache_rows rows after sequence b-1's; with dpos, S_b = dpos[b] + 1 is read on
+// the device.  PO/PML: batch*nHq*nsplit*(hd, 2) floats; counters: batch*nKv
+// words that are zero between calls.
+int tb_attn_decode_impl(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
+                        const int8_t* Vq, const float* Vs, int64_t S, int64_t nHq, int64_t nKv, int64_t hd,
+                        int nsplit, float* PO, float* PML, unsigned* counters, int64_t batch = 1,
+                        int64_t cache_rows = 0, const int32_t* dpos = nullptr);
+int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv);
+
+// two-stage argmax of `rows` rows of n; part holds rows*nparts keys.  out gets
+// the index + idx_base, out_key the ordered key (for tb_argmax_merge_impl),
+// pos_inc[row] += 1 when given.
+int tb_argmax_impl(tb_ctx* ctx, const float* x, int64_t n, int64_t rows, uint32_t* out, unsigned long long* part,
+                   int nparts, unsigned long long* out_key, uint32_t idx_base, int32_t* pos_inc);
+int tb_argmax_parts(tb_ctx* ctx, int64_t n);
+int tb_argmax_merge_impl(tb_ctx* ctx, const unsigned long long* keys, int nshard, int rows, uint32_t* out,
+                         int32_t* pos_inc);
+
+// int4 G32 quantization of an N x K slice with source row stride ld (elements)
+int tb_quant_int4_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint32_t* pack, uint16_t* scales,
+                               int64_t N, int64_t K);

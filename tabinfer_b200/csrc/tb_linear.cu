@@ -2,16 +2,7 @@
 // activation into context scratch and run the matching GEMV:
 // linearQ (models/qwen3.js:1588-1608) and Model::linear
 // (native/crates/n2-core/src/model.rs:316-339).
-#include "tb_common.cuh"
-
-int tb_gemv_dp4a_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
-                      const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
-                      float eps, int64_t K, int batch, int acc);
-int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
-                     int64_t N, int64_t K, int batch, int acc);
-int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,
-                      const int32_t* xsum, int64_t N, int64_t K, int batch, const float* act_scale);
-int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K);
+#include "tb_internal.h"
 
 static inline size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
 

@@ -1,0 +1,547 @@
+// tb_qwen3.cu -- the Qwen3 decode step (models/qwen3.js forward, 3938-4069, the
+// T = 1 / int8-KV branch) as one CUDA graph per step, tensor-parallel across
+// the GPUs of one box.
+//
+// Per step and sequence (batch B, positions pos_b held on the device):
+//   x = f32(embed_f16[ids_b])                                   embedGather :3959
+//   per layer:
+//     q,k,v = W_{q,k,v} . int8(rmsnorm(x) * ln1)                rmsnormQ + projGemv :3981-3984
+//     qr, K/V cache row pos_b = attnPrepQ8(q, k, v)             :4003
+//     attn = attentionQ8(qr, cache, S_b = pos_b + 1)            :4004
+//     x += W_o . int8(attn)                                     linearQ acc :4015
+//     swi = silu(W_g . a) * (W_u . a), a = int8(rmsnorm(x)*ln2) rmsnormQ + gateUpSiluDP4_only :4023-4024
+//     x += W_down . int8(swi)                                   linearQ acc :4033
+//   logits = W_lm . (rmsnorm(x) * final_norm)                   :4037-4049 (gemvQ at B = 1)
+//   ids_b = argmax(logits_b); pos_b += 1                        argmaxKernel :4058
+//
+// Tensor parallelism over P ranks (one context per GPU, one process per GPU):
+// q/k/v and gate/up keep their row blocks (rank r: q heads [r*nHq/P, ...),
+// kv heads [r*nKv/P, ...), the matching gate/up rows), o and down keep their
+// column blocks (the matching attn / swi slice), and after each of them the
+// partial products are summed with an NCCL allreduce of the B x hidden f32
+// residual.  The lm_head keeps vocab rows [r*V/P, ...); each rank's argmax key
+// (value, global index) is all-gathered and every rank takes the same winner.
+// KV heads are never exchanged: each rank caches only its own heads.
+#include "tb_internal.h"
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <mutex>
+#include <vector>
+
+namespace {
+
+constexpr int GEMV_MAX_B = 8;      // rows per fused-GEMV launch
+
+// NCCL entry points, resolved from the process's libnccl.so.2 (the one the
+// framework that created the ranks already loaded, when there is one).
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    bool ok = false;
+    std::string why;
+};
+
+NcclApi& nccl()
+{
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) { api.why = std::string("cannot load libnccl.so.2: ") + dlerror(); return; }
+        api.GetUniqueId = (decltype(api.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+        api.CommInitRank = (decltype(api.CommInitRank))dlsym(h, "ncclCommInitRank");
+        api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
+        api.AllReduce = (decltype(api.AllReduce))dlsym(h, "ncclAllReduce");
+        api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
+        api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce && api.AllGather &&
+                 api.GetErrorString;
+        if (!api.ok) api.why = "libnccl.so.2 lacks an expected symbol";
+    });
+    return api;
+}
+
+struct Mat {
+    uint32_t* pack = nullptr;
+    uint16_t* scales = nullptr;
+    int64_t N = 0, K = 0;
+    bool set = false;
+};
+
+struct Layer {
+    Mat q, k, v, o, gate, up, down;
+    uint16_t *ln1 = nullptr, *ln2 = nullptr, *qn = nullptr, *kn = nullptr;
+    int8_t *Kq = nullptr, *Vq = nullptr;
+    float *Ks = nullptr, *Vs = nullptr;
+};
+
+}  // namespace
+
+struct tb_qwen3 {
+    tb_ctx* ctx = nullptr;
+    tb_qwen3_config c{};
+    int P = 1, r = 0;
+    int64_t nHq = 0, nKv = 0, I = 0, V = 0;      // this rank's heads, intermediate rows, vocab rows
+    std::vector<Layer> L;
+    uint16_t* embed = nullptr;                   // f16 [vocab][H] (whole table on every rank)
+    uint16_t* fnorm = nullptr;
+    Mat lm;
+    // activations
+    float* x[2] = {nullptr, nullptr};            // residual (ping-pong under TP)
+    float *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *attn = nullptr, *swi = nullptr;
+    float *logits = nullptr, *PO = nullptr, *PML = nullptr;
+    uint32_t* ids = nullptr;
+    int32_t* pos = nullptr;
+    unsigned long long *amax_part = nullptr, *amax_key = nullptr, *amax_all = nullptr;
+    unsigned* counters = nullptr;
+    int nsplit = 1, amax_nparts = 1;
+    // graph
+    cudaStream_t cap_stream = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    // tensor parallel
+    ncclComm_t comm = nullptr;
+    std::vector<void*> allocs;
+};
+
+namespace {
+
+template <typename T>
+int alloc(tb_qwen3* m, T** p, size_t count)
+{
+    void* q = nullptr;
+    size_t bytes = (count * sizeof(T) + 255) & ~size_t(255);
+    if (cudaMalloc(&q, bytes ? bytes : 256) != cudaSuccess) {
+        cudaGetLastError();
+        return tb_fail(m->ctx, TB_ERR_NOMEM, "qwen3: cudaMalloc of %zu bytes failed", bytes);
+    }
+    m->allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return TB_OK;
+}
+
+int alloc_mat(tb_qwen3* m, Mat& w, int64_t N, int64_t K)
+{
+    w.N = N; w.K = K;
+    int rc = alloc(m, &w.pack, (size_t)N * K / 8);
+    if (!rc) rc = alloc(m, &w.scales, (size_t)N * K / 32);
+    return rc;
+}
+
+// the slice of a full [rows][cols] tensor that rank r keeps (rows x cols block)
+struct Slice { int64_t row0, nrows, col0, ncols; };
+
+int shard_of(const tb_qwen3_config& c, int kind, Slice& s, int64_t* full_rows, int64_t* full_cols)
+{
+    const int64_t P = c.tp_size, r = c.tp_rank, H = c.hidden, hd = c.head_dim;
+    const int64_t qN = (int64_t)c.n_heads * hd, kvN = (int64_t)c.n_kv_heads * hd, I = c.intermediate, V = c.vocab;
+    int64_t R = 0, C = 0;
+    switch (kind) {
+    case TB_QW_EMBED: R = V; C = H; s = {0, V, 0, H}; break;
+    case TB_QW_LM_HEAD: R = V; C = H; s = {r * (V / P), V / P, 0, H}; break;
+    case TB_QW_FINAL_NORM: case TB_QW_LN_ATTN: case TB_QW_LN_MLP: R = 1; C = H; s = {0, 1, 0, H}; break;
+    case TB_QW_Q_NORM: case TB_QW_K_NORM: R = 1; C = hd; s = {0, 1, 0, hd}; break;
+    case TB_QW_Q: R = qN; C = H; s = {r * (qN / P), qN / P, 0, H}; break;
+    case TB_QW_K: case TB_QW_V: R = kvN; C = H; s = {r * (kvN / P), kvN / P, 0, H}; break;
+    case TB_QW_O: R = H; C = qN; s = {0, H, r * (qN / P), qN / P}; break;
+    case TB_QW_GATE: case TB_QW_UP: R = I; C = H; s = {r * (I / P), I / P, 0, H}; break;
+    case TB_QW_DOWN: R = H; C = I; s = {0, H, r * (I / P), I / P}; break;
+    default: return TB_ERR_INVALID;
+    }
+    if (full_rows) *full_rows = R;
+    if (full_cols) *full_cols = C;
+    return TB_OK;
+}
+
+int check_config(const tb_qwen3_config& c, char* why, size_t n)
+{
+    const int P = c.tp_size;
+    auto bad = [&](const char* s) { snprintf(why, n, "%s", s); return TB_ERR_INVALID; };
+    if (c.hidden <= 0 || c.layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 ||
+        c.intermediate <= 0 || c.vocab <= 0 || c.max_seq <= 0)
+        return bad("all sizes must be positive");
+    if (P < 1 || c.tp_rank < 0 || c.tp_rank >= P) return bad("bad tp_size / tp_rank");
+    if (c.batch < 1 || c.batch > 16) return bad("batch must be 1..16");
+    if (c.head_dim != 64 && c.head_dim != 128) return bad("head_dim must be 64 or 128");
+    if (c.n_heads % c.n_kv_heads) return bad("n_heads must be a multiple of n_kv_heads");
+    const int grp = c.n_heads / c.n_kv_heads;
+    if (grp != 1 && grp != 2 && grp != 4 && grp != 8) return bad("n_heads / n_kv_heads must be 1, 2, 4 or 8");
+    if (c.n_kv_heads % P) return bad("n_kv_heads must be a multiple of tp_size (kv heads are sharded whole)");
+    if (c.hidden % 32 || c.hidden % 4) return bad("hidden must be a multiple of 32");
+    if (c.intermediate % (32 * P)) return bad("intermediate must be a multiple of 32 * tp_size");
+    if (c.vocab % P) return bad("vocab must be a multiple of tp_size");
+    if ((int64_t)c.batch * (c.n_kv_heads / P) > TB_ATTN_MAX_KV) return bad("batch * kv heads per rank too large");
+    if (c.vocab >= (1LL << 31)) return bad("vocab too large");
+    return TB_OK;
+}
+
+// ---- the step, issued on ctx->stream ------------------------------------------
+#define TRY(x) do { int rc_ = (x); if (rc_) return rc_; } while (0)
+
+int nccl_check(tb_qwen3* m, ncclResult_t r, const char* what)
+{
+    if (r == ncclSuccess) return TB_OK;
+    return tb_fail(m->ctx, TB_ERR_CUDA, "%s: %s", what, nccl().GetErrorString(r));
+}
+
+// y (+)= W . x over B rows, in launches of at most GEMV_MAX_B rows (fused int8
+// quantization of x, optional fused RMSNorm with norm_w)
+int gemv_rows(tb_qwen3* m, float* y, const float* x, const Mat& w, const uint16_t* norm_w, int acc)
+{
+    const int B = m->c.batch;
+    for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
+        const int nb = std::min(GEMV_MAX_B, B - b0);
+        TRY(tb_gemv_int4_dp4a(m->ctx, y + (int64_t)b0 * w.N, x + (int64_t)b0 * w.K, norm_w, m->c.rms_eps, w.pack,
+                              w.scales, w.N, w.K, nb, acc));
+    }
+    return TB_OK;
+}
+
+// x_next = x + sum over ranks of (W_r . a_r); returns the buffer holding x_next
+int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w)
+{
+    if (m->P == 1) return gemv_rows(m, m->x[cur], a, w, nullptr, 1);
+    const int nxt = cur ^ 1;
+    const size_t bytes = (size_t)m->c.batch * m->c.hidden * sizeof(float);
+    if (m->r == 0) {
+        // rank 0 carries the residual into the sum
+        cudaError_t e = cudaMemcpyAsync(m->x[nxt], m->x[cur], bytes, cudaMemcpyDeviceToDevice, m->ctx->stream);
+        if (e != cudaSuccess) return tb_fail(m->ctx, TB_ERR_CUDA, "residual copy: %s", cudaGetErrorString(e));
+        TRY(gemv_rows(m, m->x[nxt], a, w, nullptr, 1));
+    } else {
+        TRY(gemv_rows(m, m->x[nxt], a, w, nullptr, 0));
+    }
+    TRY(nccl_check(m, nccl().AllReduce(m->x[nxt], m->x[nxt], (size_t)m->c.batch * m->c.hidden, ncclFloat32, ncclSum,
+                                       m->comm, m->ctx->stream), "allreduce"));
+    cur = nxt;
+    return TB_OK;
+}
+
+int issue_step(tb_qwen3* m)
+{
+    tb_ctx* ctx = m->ctx;
+    const tb_qwen3_config& c = m->c;
+    const int B = c.batch, H = c.hidden, hd = c.head_dim;
+    int cur = 0;
+    TRY(tb_embed_gather(ctx, m->ids, 0, m->embed, m->x[cur], B, H));
+    for (int l = 0; l < c.layers; l++) {
+        Layer& Ly = m->L[l];
+        // fused rmsnormQ + q/k/v (one launch per <= 8 rows)
+        for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
+            const int nb = std::min(GEMV_MAX_B, B - b0);
+            float* ys[3] = {m->q + (int64_t)b0 * Ly.q.N, m->k + (int64_t)b0 * Ly.k.N, m->v + (int64_t)b0 * Ly.v.N};
+            const uint32_t* packs[3] = {Ly.q.pack, Ly.k.pack, Ly.v.pack};
+            const uint16_t* scs[3] = {Ly.q.scales, Ly.k.scales, Ly.v.scales};
+            const int64_t Ns[3] = {Ly.q.N, Ly.k.N, Ly.v.N};
+            TRY(tb_gemv_int4_dp4a_multi(ctx, 3, ys, packs, scs, Ns, m->x[cur] + (int64_t)b0 * H, Ly.ln1, c.rms_eps, H,
+                                        nb, 0));
+        }
+        TRY(tb_attn_prep_q8_batch(ctx, m->q, m->k, m->v, Ly.qn, Ly.kn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, m->nHq,
+                                  m->nKv, hd, B, c.max_seq, m->pos, c.rope_theta, c.rms_eps));
+        TRY(tb_attn_decode_impl(ctx, m->attn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, c.max_seq, m->nHq, m->nKv, hd,
+                                m->nsplit, m->PO, m->PML, m->counters, B, c.max_seq, m->pos));
+        TRY(proj_residual(m, cur, m->attn, Ly.o));
+        for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
+            const int nb = std::min(GEMV_MAX_B, B - b0);
+            TRY(tb_gateup_silu_int4_dp4a(ctx, m->swi + (int64_t)b0 * m->I, m->x[cur] + (int64_t)b0 * H, Ly.ln2,
+                                         c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack, Ly.up.scales, m->I, H,
+                                         nb));
+        }
+        TRY(proj_residual(m, cur, m->swi, Ly.down));
+    }
+    // final norm + lm_head: gemvQ (f32 activation) at one row, as linearQ routes
+    // T = 1 with N >= 16384; the int8 DP4A GEMV for several rows
+    if (B == 1 && m->V >= 16384) {
+        TRY(tb_gemv_int4_f32_norm(ctx, m->logits, m->x[cur], m->fnorm, c.rms_eps, m->lm.pack, m->lm.scales, m->V, H, 1,
+                                  0));
+    } else {
+        TRY(gemv_rows(m, m->logits, m->x[cur], m->lm, m->fnorm, 0));
+    }
+    if (m->P == 1) {
+        TRY(tb_argmax_impl(ctx, m->logits, m->V, B, m->ids, m->amax_part, m->amax_nparts, nullptr, 0, m->pos));
+    } else {
+        TRY(tb_argmax_impl(ctx, m->logits, m->V, B, nullptr, m->amax_part, m->amax_nparts, m->amax_key,
+                           (uint32_t)(m->r * m->V), nullptr));
+        TRY(nccl_check(m, nccl().AllGather(m->amax_key, m->amax_all, (size_t)B, ncclUint64, m->comm, ctx->stream),
+                       "allgather"));
+        TRY(tb_argmax_merge_impl(ctx, m->amax_all, m->P, B, m->ids, m->pos));
+    }
+    return TB_OK;
+}
+
+void release_graph(tb_qwen3* m)
+{
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    m->exec = nullptr;
+    m->graph = nullptr;
+}
+
+}  // namespace
+
+extern "C" {
+
+TB_API int tb_qwen3_shard(const tb_qwen3_config* c, int kind, int64_t* row0, int64_t* nrows, int64_t* col0,
+                          int64_t* ncols)
+{
+    if (!c || !row0 || !nrows || !col0 || !ncols) return TB_ERR_INVALID;
+    char why[128];
+    if (check_config(*c, why, sizeof why)) return TB_ERR_INVALID;
+    Slice s{};
+    if (shard_of(*c, kind, s, nullptr, nullptr)) return TB_ERR_INVALID;
+    *row0 = s.row0; *nrows = s.nrows; *col0 = s.col0; *ncols = s.ncols;
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** out)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, cfg && out, "null pointer");
+    *out = nullptr;
+    char why[160];
+    if (check_config(*cfg, why, sizeof why)) return tb_fail(ctx, TB_ERR_INVALID, "qwen3 config: %s", why);
+    tb_qwen3* m = new (std::nothrow) tb_qwen3();
+    if (!m) return TB_ERR_NOMEM;
+    m->ctx = ctx;
+    m->c = *cfg;
+    const tb_qwen3_config& c = m->c;
+    m->P = c.tp_size; m->r = c.tp_rank;
+    m->nHq = c.n_heads / m->P; m->nKv = c.n_kv_heads / m->P;
+    m->I = c.intermediate / m->P; m->V = c.vocab / m->P;
+    const int64_t B = c.batch, H = c.hidden, hd = c.head_dim;
+    const int64_t kvrow = m->nKv * hd;
+    m->L.resize(c.layers);
+    int rc = TB_OK;
+    auto fail = [&](int code) { tb_qwen3_destroy(m); return code; };
+    for (int l = 0; l < c.layers && !rc; l++) {
+        Layer& Ly = m->L[l];
+        rc = alloc_mat(m, Ly.q, m->nHq * hd, H);
+        if (!rc) rc = alloc_mat(m, Ly.k, kvrow, H);
+        if (!rc) rc = alloc_mat(m, Ly.v, kvrow, H);
+        if (!rc) rc = alloc_mat(m, Ly.o, H, m->nHq * hd);
+        if (!rc) rc = alloc_mat(m, Ly.gate, m->I, H);
+        if (!rc) rc = alloc_mat(m, Ly.up, m->I, H);
+        if (!rc) rc = alloc_mat(m, Ly.down, H, m->I);
+        if (!rc) rc = alloc(m, &Ly.ln1, H);
+        if (!rc) rc = alloc(m, &Ly.ln2, H);
+        if (!rc) rc = alloc(m, &Ly.qn, hd);
+        if (!rc) rc = alloc(m, &Ly.kn, hd);
+        const size_t cache = (size_t)B * c.max_seq * kvrow;
+        if (!rc) rc = alloc(m, &Ly.Kq, cache);
+        if (!rc) rc = alloc(m, &Ly.Vq, cache);
+        if (!rc) rc = alloc(m, &Ly.Ks, cache / 32);
+        if (!rc) rc = alloc(m, &Ly.Vs, cache / 32);
+    }
+    if (!rc) rc = alloc(m, &m->embed, (size_t)c.vocab * H);
+    if (!rc) rc = alloc(m, &m->fnorm, H);
+    if (!rc) rc = alloc_mat(m, m->lm, m->V, H);
+    if (!rc) rc = alloc(m, &m->x[0], B * H);
+    if (!rc) rc = alloc(m, &m->x[1], B * H);
+    if (!rc) rc = alloc(m, &m->q, B * m->nHq * hd);
+    if (!rc) rc = alloc(m, &m->k, B * kvrow);
+    if (!rc) rc = alloc(m, &m->v, B * kvrow);
+    if (!rc) rc = alloc(m, &m->qr, B * m->nHq * hd);
+    if (!rc) rc = alloc(m, &m->attn, B * m->nHq * hd);
+    if (!rc) rc = alloc(m, &m->swi, B * m->I);
+    if (!rc) rc = alloc(m, &m->logits, B * m->V);
+    m->nsplit = tb_attn_auto_nsplit(ctx, c.max_seq, m->nKv * B);
+    if (!rc) rc = alloc(m, &m->PO, (size_t)B * m->nHq * m->nsplit * hd);
+    if (!rc) rc = alloc(m, &m->PML, (size_t)B * m->nHq * m->nsplit * 2);
+    if (!rc) rc = alloc(m, &m->counters, (size_t)B * m->nKv);
+    if (!rc) rc = alloc(m, &m->ids, B);
+    if (!rc) rc = alloc(m, &m->pos, B);
+    m->amax_nparts = tb_argmax_parts(ctx, m->V);
+    if (!rc) rc = alloc(m, &m->amax_part, (size_t)B * m->amax_nparts);
+    if (!rc) rc = alloc(m, &m->amax_key, B);
+    if (!rc) rc = alloc(m, &m->amax_all, (size_t)B * m->P);
+    if (rc) return fail(rc);
+    // counters start at zero; ids/pos start at token 0, position 0
+    for (void* p : {(void*)m->counters, (void*)m->ids, (void*)m->pos}) {
+        size_t bytes = p == (void*)m->counters ? (size_t)B * m->nKv * 4 : (size_t)B * 4;
+        if (cudaMemset(p, 0, bytes) != cudaSuccess) { cudaGetLastError(); return fail(TB_ERR_CUDA); }
+    }
+    if (cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(TB_ERR_CUDA);
+    }
+    *out = m;
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_destroy(tb_qwen3* m)
+{
+    if (!m) return TB_OK;
+    cudaStreamSynchronize(m->ctx->stream);
+    release_graph(m);
+    if (m->comm) nccl().CommDestroy(m->comm);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
+    delete m;
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_set_weight(tb_qwen3* m, int kind, int layer, const uint16_t* bf16, int64_t rows, int64_t cols)
+{
+    if (!m) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    TB_REQUIRE(ctx, bf16 != nullptr, "null weight");
+    Slice s{};
+    int64_t R = 0, C = 0;
+    TB_REQUIRE(ctx, shard_of(m->c, kind, s, &R, &C) == TB_OK, "unknown weight kind %d", kind);
+    TB_REQUIRE(ctx, rows == R && cols == C, "weight kind %d: expected %lld x %lld, got %lld x %lld", kind,
+               (long long)R, (long long)C, (long long)rows, (long long)cols);
+    const bool per_layer = kind >= TB_QW_Q;
+    TB_REQUIRE(ctx, !per_layer || (layer >= 0 && layer < m->c.layers), "layer %d out of range", layer);
+    release_graph(m);   // weights are baked into the recorded step only by address, but be conservative
+    const uint16_t* src = bf16 + s.row0 * C + s.col0;
+    auto quant = [&](Mat& w) {
+        int rc = tb_quant_int4_strided_impl(ctx, src, C, w.pack, w.scales, s.nrows, s.ncols);
+        if (!rc) w.set = true;
+        return rc;
+    };
+    auto f16 = [&](uint16_t* dst) { return tb_convert_bf16_f16(ctx, src, dst, s.nrows * s.ncols); };
+    Layer* Ly = per_layer ? &m->L[layer] : nullptr;
+    switch (kind) {
+    case TB_QW_EMBED: return f16(m->embed);
+    case TB_QW_LM_HEAD: return quant(m->lm);
+    case TB_QW_FINAL_NORM: return f16(m->fnorm);
+    case TB_QW_Q: return quant(Ly->q);
+    case TB_QW_K: return quant(Ly->k);
+    case TB_QW_V: return quant(Ly->v);
+    case TB_QW_O: return quant(Ly->o);
+    case TB_QW_GATE: return quant(Ly->gate);
+    case TB_QW_UP: return quant(Ly->up);
+    case TB_QW_DOWN: return quant(Ly->down);
+    case TB_QW_LN_ATTN: return f16(Ly->ln1);
+    case TB_QW_LN_MLP: return f16(Ly->ln2);
+    case TB_QW_Q_NORM: return f16(Ly->qn);
+    case TB_QW_K_NORM: return f16(Ly->kn);
+    }
+    return tb_fail(ctx, TB_ERR_INVALID, "unknown weight kind %d", kind);
+}
+
+TB_API int tb_qwen3_kv(tb_qwen3* m, int layer, int8_t** Kq, float** Ks, int8_t** Vq, float** Vs)
+{
+    if (!m) return TB_ERR_INVALID;
+    TB_REQUIRE(m->ctx, layer >= 0 && layer < m->c.layers && Kq && Ks && Vq && Vs, "bad layer or null pointer");
+    Layer& Ly = m->L[layer];
+    *Kq = Ly.Kq; *Ks = Ly.Ks; *Vq = Ly.Vq; *Vs = Ly.Vs;
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_io(tb_qwen3* m, uint32_t** ids, int32_t** pos, float** logits)
+{
+    if (!m) return TB_ERR_INVALID;
+    if (ids) *ids = m->ids;
+    if (pos) *pos = m->pos;
+    if (logits) *logits = m->logits;
+    return TB_OK;
+}
+
+TB_API int tb_nccl_unique_id(void* out128)
+{
+    if (!out128) return TB_ERR_INVALID;
+    NcclApi& api = nccl();
+    if (!api.ok) return TB_ERR_UNSUPPORTED;
+    ncclUniqueId id;
+    if (api.GetUniqueId(&id) != ncclSuccess) return TB_ERR_CUDA;
+    memcpy(out128, &id, sizeof id);
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_tp_init(tb_qwen3* m, const void* unique_id128)
+{
+    if (!m) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    TB_REQUIRE(ctx, unique_id128 != nullptr, "null unique id");
+    if (m->P == 1) return TB_OK;
+    NcclApi& api = nccl();
+    if (!api.ok) return tb_fail(ctx, TB_ERR_UNSUPPORTED, "NCCL unavailable: %s", api.why.c_str());
+    TB_REQUIRE(ctx, m->comm == nullptr, "tensor parallelism already initialised");
+    ncclUniqueId id;
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+    memcpy(&id, unique_id128, sizeof id);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    ncclResult_t r = api.CommInitRank(&m->comm, m->P, id, m->r);
+    cudaSetDevice(prev);
+    if (r != ncclSuccess) {
+        m->comm = nullptr;
+        return tb_fail(ctx, TB_ERR_CUDA, "ncclCommInitRank: %s", api.GetErrorString(r));
+    }
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_decode_step(tb_qwen3* m)
+{
+    if (!m) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    TB_REQUIRE(ctx, m->P == 1 || m->comm != nullptr, "tensor parallel model needs tb_qwen3_tp_init first");
+    for (const Layer& Ly : m->L)
+        TB_REQUIRE(ctx, Ly.q.set && Ly.k.set && Ly.v.set && Ly.o.set && Ly.gate.set && Ly.up.set && Ly.down.set,
+                   "a projection weight was never set");
+    TB_REQUIRE(ctx, m->lm.set, "lm_head weight was never set");
+    if (!m->exec) {
+        // record the step once on a private stream, after everything queued so far
+        cudaStream_t user = ctx->stream;
+        cudaEvent_t ev;
+        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        cudaEventRecord(ev, user);
+        cudaStreamWaitEvent(m->cap_stream, ev, 0);
+        cudaEventDestroy(ev);
+        ctx->stream = m->cap_stream;
+        cudaError_t e = cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal);
+        int rc = e == cudaSuccess ? issue_step(m) : tb_fail(ctx, TB_ERR_CUDA, "begin capture: %s",
+                                                             cudaGetErrorString(e));
+        cudaGraph_t g = nullptr;
+        cudaError_t e2 = cudaStreamEndCapture(m->cap_stream, &g);
+        ctx->stream = user;
+        if (!rc && e2 != cudaSuccess) rc = tb_fail(ctx, TB_ERR_CUDA, "end capture: %s", cudaGetErrorString(e2));
+        if (!rc) {
+            e = cudaGraphInstantiate(&m->exec, g, 0);
+            if (e != cudaSuccess) rc = tb_fail(ctx, TB_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
+        }
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            m->exec = nullptr;
+            cudaGetLastError();
+            return rc;
+        }
+        m->graph = g;
+    }
+    cudaError_t e = cudaGraphLaunch(m->exec, ctx->stream);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_launches_per_step(tb_qwen3* m, int* kernels, int* collectives)
+{
+    if (!m || !kernels) return TB_ERR_INVALID;
+    if (!m->graph) return tb_fail(m->ctx, TB_ERR_INVALID, "step not recorded yet");
+    // kernel nodes of the recorded step; NCCL's own kernels (one per collective)
+    // are among them, and are reported apart
+    size_t n = 0;
+    if (cudaGraphGetNodes(m->graph, nullptr, &n) != cudaSuccess) return TB_ERR_CUDA;
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (cudaGraphGetNodes(m->graph, nodes.data(), &n) != cudaSuccess) return TB_ERR_CUDA;
+    int k = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+    }
+    const int coll = m->P > 1 ? 2 * m->c.layers + 1 : 0;
+    *kernels = k - coll;
+    if (collectives) *collectives = coll;
+    return TB_OK;
+}
+
+}  // extern "C"
