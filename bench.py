@@ -1,26 +1,31 @@
-"""bench.py -- int4 decode-GEMV throughput on B200.
+"""bench.py -- Qwen3-1.7B int4 decode on B200, with the
+int4 GEMV roofline of its kernels.
 
-One step = the int4 GEMV chain of one Qwen3-0.6B decode token at batch B, in
-the order models/qwen3.js:forward (3938-4069) issues it, attention left out:
-per layer (x28) fused RMSNorm->int8, q/k/v GEMVs in one launch, int8 of the
-q row (standing in for the attention output, same shape) -> o GEMV (+residual),
-fused RMSNorm->int8, gate+up+SiLU, int8 of swi -> down GEMV (+residual); then
-RMSNorm and the tied lm_head (151936 x 1024; f32-activation gemvQ at B=1 as
-linearQ routes it, the int8 DP4A math at B>1) and a GPU argmax.
-Weights: bf16 N(0, 0.02) quantized on the GPU with the reference's int4 G=32
-scheme; activations N(0,1) rows.  The packed weights (335 MB) exceed the
-126 MB L2, so every step streams them from HBM.
+One step = one decode token for each of `batch` sequences through the recorded
+Qwen3 decode step of libtabinfer_b200 (tb_qwen3_decode_step: the forward of
+models/qwen3.js:3938-4069 at T = 1 with the int8 KV cache): embedding gather,
+28 x (fused RMSNorm+int8+q/k/v GEMV, attention prep (q/k norm, RoPE, int8 K/V
+write), split-KV GQA decode attention over the context, o GEMV + residual,
+fused RMSNorm+int8+gate/up+SiLU, down GEMV + residual), final norm + tied
+lm_head (151936 x 2048) and GPU argmax that feeds the next step.  With N GPUs
+the step is tensor-parallel (q/k/v, gate/up, lm_head rows and kv heads split,
+o/down columns split, NCCL allreduce after o and down): strong scaling, the
+same tokens per step on 1..8 GPUs.
 
-value = algorithmic bytes per step (packed weights + f16 scales + activations in
-and outputs out of every GEMV) / device time per step, summed over ranks
-(weak scaling: every rank runs its own replica; there is no data-path
-collective).  e2e = the same bytes per step measured through the C ABI with
-host buffers: tb_copy_h2d of the input rows from pinned memory, tb_batch_submit
-of the recorded step, tb_copy_d2h of the token ids, all inside the timed region.
+Weights: bf16 N(0, 0.02) (norms 1 + N(0, 0.1)) generated on the GPU from a
+fixed seed and quantized on arrival with the reference's int4 G=32 scheme;
+the KV cache holds `context - 1` rows of N(0, 1) keys/values quantized with the
+reference's int8 per-32 scheme; each step appends one row.  The weights
+(0.97 GB) and the cache exceed the 126 MB L2, so every step streams from HBM.
 
---impl reference times the reference's CPU path for the same chain (the scalar
-transcription of the JS linearQ math in oracle/tb_cpu_ref.c, all host
-threads) on a bounded sample of the layers.
+value = tokens per second (batch x steps / device time, max over ranks).
+e2e = the same through the public API with host buffers: per step the pinned
+host ids and positions are copied in (tb_copy_h2d), the step runs, and the new
+token ids are read back (tb_copy_d2h), all inside the timed region.
+
+--impl reference times the reference's CPU path for the same step (the C
+transcription of the JS int4 linearQ math in oracle/tb_cpu_ref.c over all host
+threads) on a bounded sample of the matrices.
 """
 import argparse
 import ctypes
@@ -35,12 +40,17 @@ import time
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-H, NHQ, NKV, HD, INTER, VOCAB, LAYERS = 1024, 16, 8, 128, 3072, 151936, 28
-MATS = [("q", NHQ * HD, H), ("k", NKV * HD, H), ("v", NKV * HD, H), ("o", H, NHQ * HD),
-        ("gate", INTER, H), ("up", INTER, H), ("down", H, INTER)]
+# Qwen3-1.7B
+Q17 = dict(hidden=2048, layers=28, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=6144, vocab=151936,
+           rope_theta=1e6, rms_eps=1e-6)
+# Qwen3-0.6B GEMV chain, reported beside the decode step
+H6, NHQ6, NKV6, HD6, INTER6, VOCAB6, LAYERS6 = 1024, 16, 8, 128, 3072, 151936, 28
+MATS6 = [("q", NHQ6 * HD6, H6), ("k", NKV6 * HD6, H6), ("v", NKV6 * HD6, H6), ("o", H6, NHQ6 * HD6),
+         ("gate", INTER6, H6), ("up", INTER6, H6), ("down", H6, INTER6)]
 
 
 def wbytes(N, K):
+    """int4 G32 weight bytes: packed nibbles + f16 scales."""
     return N * K // 2 + N * (K // 32) * 2
 
 
@@ -49,13 +59,31 @@ def gemv_bytes(N, K, B, act_bytes):
     return wbytes(N, K) + B * K * act_bytes + B * N * 4
 
 
-def step_bytes(B):
+def step_matrices(cfg, P):
+    """(name, N, K, launches-per-step) of one rank's int4 matrices."""
+    H, hd, I, V = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"]
+    q, kv = cfg["n_heads"] * hd // P, cfg["n_kv_heads"] * hd // P
+    L = cfg["layers"]
+    return [("q", q, H, L), ("k", kv, H, L), ("v", kv, H, L), ("o", H, cfg["n_heads"] * hd // P, L),
+            ("gate", I // P, H, L), ("up", I // P, H, L), ("down", H, I // P, L), ("lm_head", V // P, H, 1)]
+
+
+def kv_bytes(cfg, P, S):
+    """int8 K and V + f32 per-32 scales read by one attention launch (one layer,
+    one sequence, S context rows)."""
+    row = cfg["n_kv_heads"] // P * cfg["head_dim"]
+    return 2 * S * row * (1 + 4 / 32)
+
+
+def step_bytes(cfg, P, B, S):
+    """Algorithmic HBM bytes of one rank's step: every weight once, the KV
+    context of every sequence, activations in/out of the GEMVs."""
     tot = 0
-    q8 = 1 + 4 / 32   # int8 activation + one f32 scale per 32
-    for _, N, K in MATS:
-        tot += gemv_bytes(N, K, B, q8)
-    tot *= LAYERS
-    tot += gemv_bytes(VOCAB, H, B, 4 if B == 1 else q8)
+    q8 = 1 + 4 / 32
+    for name, N, K, n in step_matrices(cfg, P):
+        act = 4 if (name == "lm_head" and B == 1) else q8
+        tot += n * gemv_bytes(N, K, B, act)
+    tot += cfg["layers"] * B * kv_bytes(cfg, P, S)
     return int(tot)
 
 
@@ -64,6 +92,8 @@ def step_bytes(B):
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
+    """nvidia-smi samples (100 ms) of SM clock, power and throttle reasons while
+    the timed region runs."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -107,13 +137,14 @@ class ClockSampler:
                 return None
         sm = [num(r[1]) for r in rows if num(r[1]) is not None]
         pw = [num(r[3]) for r in rows]
-        # samples "under load": power above the midpoint of the observed range
-        lo, hi = min(p for p in pw if p is not None), max(p for p in pw if p is not None)
+        good = [p for p in pw if p is not None]
+        lo, hi = (min(good), max(good)) if good else (0.0, 0.0)
         load = [num(r[1]) for r, p in zip(rows, pw) if p is not None and p >= (lo + hi) / 2 and num(r[1])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(load or sm), "sm_max_mhz": max(num(r[2]) or 0 for r in rows),
-                "reasons": reasons, "samples": len(rows), "power_w_max": hi}
+        return {"sm_mhz": statistics.median(load or sm) if (load or sm) else None,
+                "sm_max_mhz": max(num(r[2]) or 0 for r in rows), "reasons": reasons, "samples": len(rows),
+                "power_w_max": hi}
 
 
 def load_peaks():
@@ -125,7 +156,170 @@ def load_peaks():
 
 
 # ---------------------------------------------------------------------------
-# GPU workload
+# the decode model
+# ---------------------------------------------------------------------------
+
+def build_model(cfg, dev, batch, context, extra_rows, P, rank, seed=1234):
+    """A Qwen3 rank with random weights (same full tensors on every rank; each
+    keeps its shard) and a cache prefilled to context - 1 rows."""
+    import torch
+    import tabinfer_b200 as tb
+    full = dict(cfg, max_seq=context + extra_rows, batch=batch, tp_size=P, tp_rank=rank)
+    m = tb.Qwen3(full, device=dev.index)
+    H, hd, I, V = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"]
+    nq, nkv = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    g = torch.Generator(device=dev)
+
+    def load(name, shape, std, k):
+        g.manual_seed(seed * 1000 + k)
+        if std is None:
+            w = (1.0 + 0.1 * torch.randn(shape, device=dev, generator=g)).to(torch.bfloat16)
+        else:
+            w = (torch.randn(shape, device=dev, generator=g) * std).to(torch.bfloat16)
+        m.load(name, w.view(torch.int16))
+
+    load("model.embed_tokens.weight", (V, H), 0.02, 0)
+    load("lm_head.weight", (V, H), 0.02, 0)          # tied: the same bf16 table
+    load("model.norm.weight", (H,), None, 1)
+    k = 2
+    for l in range(cfg["layers"]):
+        p = "model.layers.%d." % l
+        for name, shape, std in (("self_attn.q_proj.weight", (nq, H), 0.02), ("self_attn.k_proj.weight", (nkv, H), 0.02),
+                                 ("self_attn.v_proj.weight", (nkv, H), 0.02), ("self_attn.o_proj.weight", (H, nq), 0.02),
+                                 ("mlp.gate_proj.weight", (I, H), 0.02), ("mlp.up_proj.weight", (I, H), 0.02),
+                                 ("mlp.down_proj.weight", (H, I), 0.02), ("input_layernorm.weight", (H,), None),
+                                 ("post_attention_layernorm.weight", (H,), None),
+                                 ("self_attn.q_norm.weight", (hd,), None), ("self_attn.k_norm.weight", (hd,), None)):
+            load(p + name, shape, std, k)
+            k += 1
+    # cache: rows [0, context-1) of N(0,1) keys/values, int8 per-32 (kvQuantWrite);
+    # one random block serves every layer and sequence
+    rows = context - 1
+    if rows > 0:
+        g.manual_seed(seed + 7 + rank)
+        kr = torch.randn(rows, m.n_kv_local * hd, device=dev, generator=g)
+        vr = torch.randn(rows, m.n_kv_local * hd, device=dev, generator=g)
+        for l in range(cfg["layers"]):
+            for b in range(batch):
+                m.kv_fill(l, b, kr, vr, 0)
+        del kr, vr
+    torch.cuda.synchronize(dev)
+    return m
+
+
+def time_steps(m, K, stream):
+    """Device time (ms) of K replays of the recorded step (CUDA events on the
+    stream the step is launched on)."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        m.step()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def time_e2e(m, K, stream, ids0, pos0):
+    """K steps through the public API with host buffers: pinned ids/positions in,
+    the step, the new ids out (tb_copy_h2d / tb_qwen3_decode_step / tb_copy_d2h)."""
+    import torch
+    from tabinfer_b200._lib import LIB
+    B = m.cfg["batch"]
+    hin = torch.tensor(list(ids0) + list(pos0), dtype=torch.int32).pin_memory()
+    hout = torch.zeros(B, dtype=torch.int32).pin_memory()
+    ids_dev, pos_dev, _ = m._io
+    c = m.ctx
+    P = ctypes.c_void_p
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        c.check(LIB.tb_copy_h2d(c.h, P(ids_dev), P(hin.data_ptr()), 4 * B), "h2d ids")
+        c.check(LIB.tb_copy_h2d(c.h, P(pos_dev), P(hin.data_ptr() + 4 * B), 4 * B), "h2d pos")
+        m.step()
+        c.check(LIB.tb_copy_d2h(c.h, P(hout.data_ptr()), P(ids_dev), 4 * B), "d2h ids")
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1), 8 * B, 4 * B
+
+
+def kernel_kinds(cfg, dev, P, context, peak):
+    """Per-launch device time of each kernel kind of one rank's step at batch 1,
+    cold L2 (a 256 MB write between launches), CUDA events on the launching
+    stream.  Returns {kind: {...}} with algorithmic bytes and GB/s."""
+    import torch
+    import tabinfer_b200 as tb
+    g = torch.Generator(device=dev).manual_seed(99)
+    H, hd, I, V, L = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"], cfg["layers"]
+    nHq, nKv = cfg["n_heads"] // P, cfg["n_kv_heads"] // P
+
+    def mat(N, K):
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        return tb.quantize_int4_bf16(w.view(torch.int16))
+
+    # a few copies of each matrix so back-to-back launches do not hit L2
+    NC = 4
+    qm = [mat(nHq * hd, H) for _ in range(NC)]
+    km = [mat(nKv * hd, H) for _ in range(NC)]
+    vm = [mat(nKv * hd, H) for _ in range(NC)]
+    om = [mat(H, nHq * hd) for _ in range(NC)]
+    gm = [mat(I // P, H) for _ in range(NC)]
+    um = [mat(I // P, H) for _ in range(NC)]
+    dm = [mat(H, I // P) for _ in range(NC)]
+    lm = mat(V // P, H)
+    ln = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half().view(torch.int16)
+    x = torch.randn(1, H, device=dev, generator=g)
+    xa = torch.randn(1, nHq * hd, device=dev, generator=g)
+    xs = torch.randn(1, I // P, device=dev, generator=g)
+    S = context
+    row = nKv * hd
+    Kq = torch.randint(-127, 128, (S, row), device=dev, generator=g, dtype=torch.int8)
+    Vq = torch.randint(-127, 128, (S, row), device=dev, generator=g, dtype=torch.int8)
+    Ks = torch.rand(S, row // 32, device=dev, generator=g) + 0.5
+    Vs = torch.rand(S, row // 32, device=dev, generator=g) + 0.5
+    qr = torch.randn(nHq * hd, device=dev, generator=g)
+    outs = {n: torch.zeros(1, N, device=dev) for n, N in (("q", nHq * hd), ("k", nKv * hd), ("v", nKv * hd),
+                                                             ("o", H), ("swi", I // P), ("lm", V // P))}
+    att = torch.zeros(nHq * hd, device=dev)
+    kinds = {
+        "gemv rmsnorm+qkv": (lambda i: tb.gemv_dp4a_multi(x, [qm[i], km[i], vm[i]], norm_w=ln,
+                                                          ys=[outs["q"], outs["k"], outs["v"]]),
+                             sum(wbytes(N, H) + N * 4 for N in (nHq * hd, nKv * hd, nKv * hd)) + H * 4, L),
+        "gemv o": (lambda i: tb.gemv_dp4a(xa, *om[i], y=outs["o"], acc=True), gemv_bytes(H, nHq * hd, 1, 4), L),
+        "gemv rmsnorm+gate+up+silu": (lambda i: tb.gate_up_silu_dp4a(x, *gm[i], *um[i], norm_w=ln, swi=outs["swi"]),
+                                      2 * wbytes(I // P, H) + H * 4 + (I // P) * 4, L),
+        "gemv down": (lambda i: tb.gemv_dp4a(xs, *dm[i], y=outs["o"], acc=True), gemv_bytes(H, I // P, 1, 4), L),
+        "gemv rmsnorm+lm_head (f32)": (lambda i: tb.gemv_q_norm(x, ln, 1e-6, *lm, y=outs["lm"]),
+                                       gemv_bytes(V // P, H, 1, 4), 1),
+        "attn decode S=%d" % S: (lambda i: tb.attention_decode_q8(qr, (Kq, Ks, Vq, Vs), S, nHq, nKv, hd, out=att),
+                                 kv_bytes(cfg, P, S) + 2 * nHq * hd * 4, L),
+    }
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for name, (fn, nbytes, per_step) in kinds.items():
+        fn(0)
+        ts = []
+        for r in range(12):
+            flush.fill_(r & 0xff)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn(r % NC)
+            e1.record(stream)
+            e1.synchronize()
+            if r >= 2:
+                ts.append(e0.elapsed_time(e1))
+        us = statistics.median(ts) * 1e3
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"us_per_launch": round(us, 3), "bytes_per_launch": int(nbytes), "launches_per_step": per_step,
+                     "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4), "us_per_step": round(us * per_step, 2)}
+    del flush
+    torch.cuda.synchronize(dev)
+    return res
+
+
+# ---------------------------------------------------------------------------
+# Qwen3-0.6B GEMV chain (configs[1]): int4 GEMV HBM GB/s without attention
 # ---------------------------------------------------------------------------
 
 class Chain:
@@ -137,194 +331,105 @@ class Chain:
         self.dev = dev
         g = torch.Generator(device=dev).manual_seed(seed)
         self.layers = []
-        for _ in range(LAYERS):
+        for _ in range(LAYERS6):
             L = {}
-            for name, N, K in MATS:
+            for name, N, K in MATS6:
                 w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
                 L[name] = tb.quantize_int4_bf16(w.view(torch.int16))
-            L["ln1"] = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).half().view(torch.int16)
-            L["ln2"] = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).half().view(torch.int16)
+            L["ln1"] = (1.0 + 0.1 * torch.randn(H6, device=dev, generator=g)).half().view(torch.int16)
+            L["ln2"] = (1.0 + 0.1 * torch.randn(H6, device=dev, generator=g)).half().view(torch.int16)
             self.layers.append(L)
-        w = (torch.randn(VOCAB, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w = (torch.randn(VOCAB6, H6, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         self.lm_head = tb.quantize_int4_bf16(w.view(torch.int16))
-        self.norm = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).half().view(torch.int16)
+        self.norm = (1.0 + 0.1 * torch.randn(H6, device=dev, generator=g)).half().view(torch.int16)
         del w
         torch.cuda.synchronize(dev)
 
 
-class ChainRun:
-    """Activation buffers for batch B and the recorded step."""
-
-    def __init__(self, chain, B, ctx):
-        import torch
-        dev = chain.dev
-        self.chain, self.B, self.ctx = chain, B, ctx
-        z = lambda *s, dt=torch.float32: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
-        self.x = z(B, H)
-        self.q, self.k, self.v = z(B, NHQ * HD), z(B, NKV * HD), z(B, NKV * HD)
-        self.swi = z(B, INTER)
-        self.logits = z(B, VOCAB)
-        self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.batch = None
-        self.launches = 0
-
-    def step(self):
-        """Issue one step's calls (eager, or under recording): 4 fused launches per layer."""
-        import tabinfer_b200 as tb
-        c = self.chain
-        n = 0
-        for L in c.layers:
-            tb.gemv_dp4a_multi(self.x, [L["q"], L["k"], L["v"]], norm_w=L["ln1"], eps=1e-6, ys=[self.q, self.k, self.v])
-            tb.gemv_dp4a(self.q, *L["o"], y=self.x, acc=True)
-            tb.gate_up_silu_dp4a(self.x, *L["gate"], *L["up"], norm_w=L["ln2"], eps=1e-6, swi=self.swi)
-            tb.gemv_dp4a(self.swi, *L["down"], y=self.x, acc=True)
-            n += 4
-        if self.B == 1:
-            tb.gemv_q_norm(self.x, c.norm, 1e-6, *c.lm_head, y=self.logits)
-        else:
-            tb.gemv_dp4a(self.x, *c.lm_head, norm_w=c.norm, eps=1e-6, y=self.logits)
-        tb.argmax(self.logits, out=self.tok)
-        self.launches = n + 3
-
-    def record(self):
-        import torch
-        from tabinfer_b200._lib import LIB, P
-        stream = torch.cuda.ExternalStream(self.ctx.own_stream(), device=self.chain.dev)
-        self.stream = stream
-        with torch.cuda.stream(stream):
-            self.step()                      # eager warm-up (sizes any scratch)
-            stream.synchronize()
-            self.ctx.check(LIB.tb_batch_begin(self.ctx.h), "batch_begin")
-            self.step()
-            h = P()
-            self.ctx.check(LIB.tb_batch_end(self.ctx.h, ctypes.byref(h)), "batch_end")
-        self.batch = h
-
-    def submit(self):
-        from tabinfer_b200._lib import LIB
-        self.ctx.check(LIB.tb_batch_submit(self.ctx.h, self.batch), "batch_submit")
-
-    def close(self):
-        from tabinfer_b200._lib import LIB
-        if self.batch is not None:
-            LIB.tb_batch_destroy(self.batch)
-            self.batch = None
+def chain_bytes(B):
+    q8 = 1 + 4 / 32
+    tot = sum(gemv_bytes(N, K, B, q8) for _, N, K in MATS6) * LAYERS6
+    return int(tot + gemv_bytes(VOCAB6, H6, B, 4 if B == 1 else q8))
 
 
-def time_replays(run, K):
-    import torch
-    s = run.stream
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(K):
-        run.submit()
-    e1.record(s)
-    e1.synchronize()
-    return e0.elapsed_time(e1) / K
-
-
-def time_e2e(run, K):
-    """Same step through the C ABI with host buffers: pinned H2D of the input
-    rows, one recorded-batch submit, D2H of the token ids."""
-    import torch
-    from tabinfer_b200._lib import LIB, P
-    s = run.stream
-    hx = torch.randn(run.B, H).pin_memory()
-    htok = torch.zeros(run.B, dtype=torch.int32).pin_memory()
-    h2d = hx.numel() * 4
-    d2h = htok.numel() * 4
-    c = run.ctx
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(K):
-        c.check(LIB.tb_copy_h2d(c.h, P(run.x.data_ptr()), P(hx.data_ptr()), h2d), "h2d")
-        run.submit()
-        c.check(LIB.tb_copy_d2h(c.h, P(htok.data_ptr()), P(run.tok.data_ptr()), d2h), "d2h")
-    e1.record(s)
-    e1.synchronize()
-    return e0.elapsed_time(e1) / K, h2d, d2h
-
-
-def dominant_kernel_roofline(chain, ctx, peak, reps=3):
-    """Per-launch device time of each GEMV kind, cold L2 (a 256 MB buffer is
-    written between launches), with CUDA events on the launching stream.
-    Returns the kind with the largest share of the step and all kinds."""
+def chain_gbs(dev, ctx, B, steps):
+    """GB/s of the 0.6B GEMV chain (4 fused GEMV launches per layer + lm_head +
+    argmax, attention left out), recorded with tb_batch and replayed."""
     import torch
     import tabinfer_b200 as tb
-    from tabinfer_b200._lib import LIB
-    dev = chain.dev
-    s = torch.cuda.ExternalStream(ctx.own_stream(), device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    B = 1
-    x1 = torch.randn(B, H, device=dev)
-    x2 = torch.randn(B, NHQ * HD, device=dev)
-    x3 = torch.randn(B, INTER, device=dev)
-    ln = chain.layers[0]["ln1"]
-    with torch.cuda.stream(s):
-        outs = {n: torch.zeros(B, N, device=dev) for n, N, _ in MATS}
-        logits = torch.zeros(B, VOCAB, device=dev)
-        swi = torch.zeros(B, INTER, device=dev)
-        kinds = {
-            "gemv_dp4a rmsnorm+qkv (4096x1024)": (lambda L: tb.gemv_dp4a_multi(x1, [L["q"], L["k"], L["v"]], norm_w=ln,
-                                                                                ys=[outs["q"], outs["k"], outs["v"]]),
-                                                  gemv_bytes(4096, H, B, 1.125), LAYERS),
-            "gemv_dp4a o (1024x2048)": (lambda L: tb.gemv_dp4a(x2, *L["o"], y=outs["o"]),
-                                        gemv_bytes(H, 2048, B, 1.125), LAYERS),
-            "gemv_dp4a rmsnorm+gate+up+silu (2x3072x1024)": (
-                lambda L: tb.gate_up_silu_dp4a(x1, *L["gate"], *L["up"], norm_w=ln, swi=swi),
-                2 * wbytes(INTER, H) + B * H * 1.125 + B * INTER * 4, LAYERS),
-            "gemv_dp4a down (1024x3072)": (lambda L: tb.gemv_dp4a(x3, *L["down"], y=outs["down"]),
-                                           gemv_bytes(H, INTER, B, 1.125), LAYERS),
-            "gemv_f32 rmsnorm+lm_head (151936x1024)": (lambda L: tb.gemv_q_norm(x1, chain.norm, 1e-6, *chain.lm_head, y=logits),
-                                                       gemv_bytes(VOCAB, H, B, 4), 1),
-        }
-        res = {}
-        for name, (fn, nbytes, per_step) in kinds.items():
-            ts = []
-            for r in range(reps):
-                for li, L in enumerate(chain.layers if per_step > 1 else chain.layers[:1]):
-                    flush.fill_(r & 0xff)
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record(s)
-                    fn(L)
-                    e1.record(s)
-                    e1.synchronize()
-                    ts.append(e0.elapsed_time(e1))
-            us = statistics.median(ts) * 1e3
-            res[name] = {"us_per_launch": us, "bytes_per_launch": int(nbytes), "launches_per_step": per_step,
-                         "gbs": nbytes / (us * 1e-6) / 1e9, "us_per_step": us * per_step}
-    dom = max(res, key=lambda k: res[k]["us_per_step"])
-    return dom, res
+    from tabinfer_b200._lib import LIB, P
+    c = Chain(dev, 1000)
+    z = lambda *s: torch.zeros(*s, dtype=torch.float32, device=dev)  # noqa: E731
+    x, q, k, v, swi, logits = z(B, H6), z(B, NHQ6 * HD6), z(B, NKV6 * HD6), z(B, NKV6 * HD6), z(B, INTER6), z(B, VOCAB6)
+    tok = torch.zeros(B, dtype=torch.int32, device=dev)
 
+    def step():
+        for L in c.layers:
+            tb.gemv_dp4a_multi(x, [L["q"], L["k"], L["v"]], norm_w=L["ln1"], eps=1e-6, ys=[q, k, v])
+            tb.gemv_dp4a(q, *L["o"], y=x, acc=True)
+            tb.gate_up_silu_dp4a(x, *L["gate"], *L["up"], norm_w=L["ln2"], eps=1e-6, swi=swi)
+            tb.gemv_dp4a(swi, *L["down"], y=x, acc=True)
+        if B == 1:
+            tb.gemv_q_norm(x, c.norm, 1e-6, *c.lm_head, y=logits)
+        else:
+            tb.gemv_dp4a(x, *c.lm_head, norm_w=c.norm, eps=1e-6, y=logits)
+        tb.argmax(logits, out=tok)
+
+    stream = torch.cuda.ExternalStream(ctx.own_stream(), device=dev)
+    with torch.cuda.stream(stream):
+        step()
+        stream.synchronize()
+        ctx.check(LIB.tb_batch_begin(ctx.h), "batch_begin")
+        step()
+        h = P()
+        ctx.check(LIB.tb_batch_end(ctx.h, ctypes.byref(h)), "batch_end")
+        for _ in range(5):
+            ctx.check(LIB.tb_batch_submit(ctx.h, h), "submit")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            ctx.check(LIB.tb_batch_submit(ctx.h, h), "submit")
+        e1.record(stream)
+        e1.synchronize()
+    LIB.tb_batch_destroy(h)
+    ms = e0.elapsed_time(e1) / steps
+    del c
+    torch.cuda.synchronize(dev)
+    return {"gbs": round(chain_bytes(B) / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4), "batch": B,
+            "bytes_per_step": chain_bytes(B), "launches_per_step": 4 * LAYERS6 + 3}
+
+
+# ---------------------------------------------------------------------------
+# profiling cases (for ncu on a small case)
+# ---------------------------------------------------------------------------
 
 def profile_case():
-    """One cold-L2 launch of each kernel kind, for `ncu --set full` on a small
-    case (a few hundred MB on the device): the five GEMV kinds of the 0.6B chain
-    at batch 1, the config-1 ternary qkv GEMV (4096 x 2048) and int8-KV decode
-    attention at S = 4096 (1.7B heads).  Every launch is preceded by a 256 MB
-    write that evicts L2."""
-    import numpy as np
+    """One cold-L2 launch of each kernel kind of the 1.7B step at batch 1 (TP 1):
+    the four per-layer GEMV kinds, the f32 lm_head, the config-1 ternary qkv
+    GEMV (4096 x 2048) and decode attention at S=4096.  Every launch is preceded
+    by a 256 MB write that evicts L2; two passes."""
     import torch
     import tabinfer_b200 as tb
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
+    H, hd, I, V = Q17["hidden"], Q17["head_dim"], Q17["intermediate"], Q17["vocab"]
 
     def q(N, K):
         w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         return tb.quantize_int4_bf16(w.view(torch.int16))
 
     qm, km, vm, om = q(2048, H), q(1024, H), q(1024, H), q(H, 2048)
-    gm, um, dm, lm = q(INTER, H), q(INTER, H), q(H, INTER), q(VOCAB, H)
+    gm, um, dm, lm = q(I, H), q(I, H), q(H, I), q(V, H)
     ln = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half().view(torch.int16)
     tw = (torch.randint(0, 3, (4096, 2048), device=dev, generator=g).float() - 1.0) * 0.03
     codes, tsc = tb.pack_ternary(tw)
-    S, nHq, nKv, hd = 4096, 16, 8, 128
+    S, nHq, nKv = 4096, 16, 8
     Kq = torch.randint(-127, 128, (S, nKv * hd), device=dev, generator=g, dtype=torch.int8)
     Vq = torch.randint(-127, 128, (S, nKv * hd), device=dev, generator=g, dtype=torch.int8)
     Ks = torch.rand(S, nKv * hd // 32, device=dev, generator=g) + 0.5
     Vs = torch.rand(S, nKv * hd // 32, device=dev, generator=g) + 0.5
     qr = torch.randn(nHq * hd, device=dev, generator=g)
-    x1, x2, x3 = (torch.randn(1, k, device=dev, generator=g) for k in (H, 2048, INTER))
+    x1, x2, x3 = (torch.randn(1, k, device=dev, generator=g) for k in (H, 2048, I))
     xt = torch.randn(1, 2048, device=dev, generator=g)
     act, xsum, _ = tb.quantize_act(xt)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -343,6 +448,7 @@ def profile_case():
             flush.fill_(it)
             fn()
     torch.cuda.synchronize()
+    assert tb.default_context(0).device_error() == 0
     print("profile case done", flush=True)
 
 
@@ -369,82 +475,100 @@ def profile_attn(S):
     print("profile attn done", flush=True)
 
 
-def cpu_baseline_sample(threads, budget_s=12.0):
-    """The transcribed CPU path (oracle/tb_cpu_ref.c, linearQ math) on a bounded
-    sample: 2 decoder layers' 7 matrices + 1/16 of the lm_head rows, repeated
-    until `budget_s` of CPU work.  Returns GB/s of the same algorithmic bytes."""
+# ---------------------------------------------------------------------------
+# CPU path (the reference's int4 linearQ math, C transcription)
+# ---------------------------------------------------------------------------
+
+def cpu_step_seconds(threads, budget_s, cfg=Q17):
+    """Seconds per decode token of the transcribed CPU GEMV path
+    (oracle/tb_cpu_ref.c: linearQ's DP4A math for N < 16384, gemvQ's f32 math
+    for the lm_head), measured on a bounded sample -- 2 of the 28 layers' seven
+    matrices and 1/16 of the lm_head rows, repeated for `budget_s` -- and scaled
+    to the whole step.  Attention is not included (the reference has no CPU
+    int8-KV attention on this path), so the CPU rate is an upper bound."""
     import numpy as np
     import oracle
     lib = oracle.cpuref()
     rng = np.random.default_rng(7)
+    H, I, V = cfg["hidden"], cfg["intermediate"], cfg["vocab"]
+    nq, nkv = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
+    shapes = [(nq, H), (nkv, H), (nkv, H), (H, nq), (I, H), (I, H), (H, I)]
     mats = []
     for _ in range(2):
-        for _, N, K in MATS:
+        for N, K in shapes:
             mats.append((N, K, rng.integers(0, 2 ** 32, (N, K // 8), dtype=np.uint32),
-                         np.float16(rng.uniform(0.001, 0.004, (N, K // 32))).view(np.uint16)))
-    Nl = VOCAB // 16
+                         np.float16(rng.uniform(0.001, 0.004, (N, K // 32))).view(np.uint16), False))
+    Nl = V // 16
     mats.append((Nl, H, rng.integers(0, 2 ** 32, (Nl, H // 8), dtype=np.uint32),
-                 np.float16(rng.uniform(0.001, 0.004, (Nl, H // 32))).view(np.uint16)))
+                 np.float16(rng.uniform(0.001, 0.004, (Nl, H // 32))).view(np.uint16), True))
     P = ctypes.c_void_p
-    xs = {K: rng.normal(0, 1, K).astype(np.float32) for K in (H, 2048, INTER)}
-    xq = np.zeros(INTER, np.int8)
-    xsc = np.zeros(INTER // 32, np.float32)
-    ys = [np.zeros(N, np.float32) for N, *_ in mats]
-    nbytes = 0
-    t0 = time.perf_counter()
+    Kmax = max(m[1] for m in mats)
+    xs = {m[1]: rng.normal(0, 1, m[1]).astype(np.float32) for m in mats}
+    xq = np.zeros(Kmax, np.int8)
+    xsc = np.zeros(Kmax // 32, np.float32)
+    ys = [np.zeros(m[0], np.float32) for m in mats]
+    t_layers = t_lm = 0.0
     reps = 0
+    t0 = time.perf_counter()
     while True:
-        for (N, K, pk, sc), y in zip(mats, ys):
-            if N == Nl:   # lm_head rows keep linearQ's f32 (gemvQ) route, as at N >= 16384
+        for (N, K, pk, sc, is_lm), y in zip(mats, ys):
+            ta = time.perf_counter()
+            if is_lm:
                 lib.tbr_gemv_int4_f32(P(y.ctypes.data), P(xs[K].ctypes.data), P(pk.ctypes.data), P(sc.ctypes.data),
                                       ctypes.c_int64(N), ctypes.c_int64(K), ctypes.c_int(0), ctypes.c_int(threads))
+                t_lm += time.perf_counter() - ta
             else:
                 lib.tbr_linear_int4(P(y.ctypes.data), P(xs[K].ctypes.data), P(pk.ctypes.data), P(sc.ctypes.data),
                                     ctypes.c_int64(N), ctypes.c_int64(K), ctypes.c_int(0), P(xq.ctypes.data),
                                     P(xsc.ctypes.data), ctypes.c_int(threads))
-            nbytes += gemv_bytes(N, K, 1, 1.125 if N != Nl else 4)
+                t_layers += time.perf_counter() - ta
         reps += 1
         if time.perf_counter() - t0 > budget_s:
             break
-    dt = time.perf_counter() - t0
-    return nbytes / dt / 1e9, reps, dt
+    per_step = (t_layers / reps) * (cfg["layers"] / 2) + (t_lm / reps) * 16
+    return per_step, reps, time.perf_counter() - t0
 
-
-# ---------------------------------------------------------------------------
 
 def run_reference(args, rank, world):
+    """The reference's CPU path for the same decode step on all host threads."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     vals = []
-    budget = max(1.0, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
+    budget = max(0.25, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
     for i in range(args.warmup + args.steps):
-        gbs, reps, dt = cpu_baseline_sample(threads, budget_s=budget)
+        sec, reps, dt = cpu_step_seconds(threads, budget)
         if i >= args.warmup:
-            vals.append(gbs)
+            vals.append(args.batch / sec)
     v = statistics.median(vals)
-    sample = ("2 of 28 Qwen3-0.6B decoder layers (q,k,v,o,gate,up,down) + 1/16 of the lm_head rows per "
-              "repetition, repeated for %.1f s per step" % budget)
-    line = {"metric": "int4 decode GEMV HBM GB/s (Qwen3-0.6B chain, batch 1)", "impl": "reference",
-            "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-            "data": "synthetic", "config": {"workload": "qwen3-0.6b int4 decode GEMV chain", "batch": 1},
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+    sample = ("2 of 28 Qwen3-1.7B decoder layers (q,k,v,o,gate,up,down) + 1/16 of the lm_head rows per repetition, "
+              "%.1f s per step, scaled to the full step; attention excluded" % budget)
+    line = {"metric": "Qwen3-1.7B int4 decode tok/s (context %d, batch %d)" % (args.context, args.batch),
+            "impl": "reference", "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1e3 * args.batch / v, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "qwen3-1.7b int4 decode step", "batch": args.batch, "context": args.context},
+            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": sample},
-            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference CPU path = C transcription of the JS linearQ int4 math (no node/cargo in this "
-                    "image); row-partitioned over all host threads as cpu/kernel/cpuengine-mt.js does"}
+                    "image), row-partitioned over all host threads as cpu/kernel/cpuengine-mt.js does"}
     print(json.dumps(line), flush=True)
 
+
+# ---------------------------------------------------------------------------
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--tp-exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="tensor-parallel sums: this library's peer-memory kernels, or NCCL")
     ap.add_argument("--profile-case", action="store_true",
                     help="one cold-L2 launch per kernel kind (for ncu), then exit")
     ap.add_argument("--profile-attn", type=int, default=0, metavar="S",
@@ -474,95 +598,135 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
     import tabinfer_b200 as tb
+    from tabinfer_b200.qwen3 import nccl_unique_id
     ctx = tb.default_context(local)
-    ctx.own_stream()
-    chain = Chain(dev, seed=1000 + rank)
-    run = ChainRun(chain, args.batch, ctx)
-    run.record()
-    for _ in range(args.warmup):
-        run.submit()
-    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def tp_setup(m):
+        if world == 1:
+            return
+        if args.tp_exchange == "nccl":
+            uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+            dist.broadcast(uid, 0)
+            m.tp_init(bytes(uid.cpu().numpy().tobytes()))
+            return
+        mine = torch.frombuffer(bytearray(m.tp_handle()), dtype=torch.uint8).to(dev)
+        allh = [torch.zeros(64, dtype=torch.uint8, device=dev) for _ in range(world)]
+        dist.all_gather(allh, mine)
+        m.tp_connect([bytes(h.cpu().numpy().tobytes()) for h in allh])
+
+    B, S = args.batch, args.context
+    K2 = max(50, args.steps // 4)
+    extra = args.warmup + args.steps + K2 + 16
+    m = build_model(Q17, dev, B, S, extra, world, rank)
+    tp_setup(m)
+    ids0 = [(1000 + 7919 * b) % Q17["vocab"] for b in range(B)]
+    pos0 = [S - 1] * B
+    m.set_tokens(ids0, pos0)
+    for _ in range(args.warmup):
+        m.step()
+    torch.cuda.synchronize(dev)
+    m.set_tokens(ids0, pos0)
     barrier()
     torch.cuda.synchronize(dev)
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    ms = time_replays(run, args.steps)
+    ms = time_steps(m, args.steps, stream) / args.steps
     clocks_info = clocks.stop()
     torch.cuda.synchronize(dev)
     barrier()
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(ms)
+    kernels, colls = m.launches_per_step()
+    # e2e through the public API with host buffers
+    m.set_tokens(ids0, pos0)
+    barrier()
+    e2e_total, h2d, d2h = time_e2e(m, K2, stream, ids0, pos0)
+    e2e_ms = max_over_ranks(e2e_total / K2)
+    err = ctx.device_error()
+    assert err == 0, "device error word 0x%x" % err
+    m.close()
+    del m
+    torch.cuda.synchronize(dev)
 
-    B = args.batch
-    nbytes = step_bytes(B)
-    value = nbytes * world / (ms_max * 1e-3) / 1e9
-
-    # e2e through the C ABI with host buffers
-    e2e_ms, h2d, d2h = time_e2e(run, max(50, args.steps // 4))
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e = {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
-
+    value = B * 1e3 / ms_max
     peak, peak_src = load_peaks()
-    extras = {}
+    nbytes = step_bytes(Q17, world, B, S)
+    extras = {"step_hbm_gbs_per_rank": round(nbytes / (ms_max * 1e-3) / 1e9, 1),
+              "step_hbm_frac_per_rank": round(nbytes / (ms_max * 1e-3) / 1e9 / peak, 4)}
     roof = None
+    cpu = None
     if rank == 0 and not args.no_extras:
-        dom, kinds = dominant_kernel_roofline(chain, ctx, peak)
+        kinds = kernel_kinds(Q17, dev, world, S, peak)
+        dom = max(kinds, key=lambda k: kinds[k]["us_per_step"])
         d = kinds[dom]
         traffic = None
         tp = os.path.join(REPO, "profiles", "traffic.json")
-        if os.path.exists(tp):
+        if os.path.exists(tp) and world == 1:
             traffic = json.load(open(tp)).get(dom)
-        roof = {"bound": "hbm", "kernel": dom, "achieved": round(d["gbs"], 1), "peak": peak, "unit": "GB/s",
-                "frac": round(d["gbs"] / peak, 4), "traffic": traffic, "peak_source": peak_src + " hbm_gbs (burst copy)",
-                "algorithmic_bytes_per_launch": d["bytes_per_launch"], "us_per_launch": round(d["us_per_launch"], 3)}
-        extras["kernels"] = {k: {kk: round(vv, 3) if isinstance(vv, float) else vv for kk, vv in v.items()}
-                             for k, v in kinds.items()}
-        for Bx in (4, 8):
-            if Bx == B:
+        roof = {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": d["frac_of_peak"], "traffic": traffic,
+                "peak_source": peak_src + " hbm_gbs (burst copy)",
+                "algorithmic_bytes_per_launch": d["bytes_per_launch"], "us_per_launch": d["us_per_launch"],
+                "timing": "cold L2 (256 MB write before each launch), CUDA events on the launching stream"}
+        extras["kernels"] = kinds
+    if world == 1 and rank == 0 and not args.no_extras:
+        extras["gemv_chain_0.6b"] = chain_gbs(dev, ctx, 1, max(100, args.steps))
+        extras["gemv_chain_0.6b"]["frac_of_peak"] = round(extras["gemv_chain_0.6b"]["gbs"] / peak, 4)
+        for (Bx, Sx) in ((16, 4096), (1, 32768)):
+            if (Bx, Sx) == (B, S):
                 continue
-            r2 = ChainRun(chain, Bx, ctx)
-            r2.record()
+            mx = build_model(Q17, dev, Bx, Sx, 64 + 16, 1, 0)
+            mx.set_tokens([(3 + 101 * b) % Q17["vocab"] for b in range(Bx)], [Sx - 1] * Bx)
             for _ in range(5):
-                r2.submit()
-            ms2 = time_replays(r2, max(50, args.steps // 4))
-            extras["batch%d" % Bx] = {"gbs": round(step_bytes(Bx) / (ms2 * 1e-3) / 1e9, 1), "ms_per_step": round(ms2, 4),
-                                      "tok_per_s_gemv_only": round(Bx * 1e3 / ms2, 1)}
-            r2.close()
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_extras:
-        gbs, reps, dt = cpu_baseline_sample(1, budget_s=12.0)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
-               "sample": "2 of 28 decoder layers (7 matrices each) + 1/16 of the lm_head rows, %d repetitions in %.1f s, "
-                         "C transcription of the JS linearQ int4 math, 1 thread" % (reps, dt)}
+                mx.step()
+            torch.cuda.synchronize(dev)
+            msx = time_steps(mx, 50, stream) / 50
+            extras["batch%d_context%d" % (Bx, Sx)] = {
+                "tok_per_s": round(Bx * 1e3 / msx, 1), "ms_per_step": round(msx, 4),
+                "step_hbm_gbs": round(step_bytes(Q17, 1, Bx, Sx) / (msx * 1e-3) / 1e9, 1)}
+            mx.close()
+            del mx
+            torch.cuda.synchronize(dev)
+        sec, reps, dt = cpu_step_seconds(1, 12.0)
+        cpu = {"value": round(B / sec, 4), "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": "2 of 28 decoder layers (7 matrices each) + 1/16 of the lm_head rows, %d repetitions in "
+                         "%.1f s, scaled to the full step; C transcription of the JS linearQ int4 math, 1 thread; "
+                         "attention excluded" % (reps, dt)}
 
     if rank == 0:
-        line = {"metric": "int4 decode GEMV HBM GB/s (Qwen3-0.6B chain, batch %d)" % B, "value": round(value, 2),
-                "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "u8", "data": "synthetic",
-                "config": {"workload": "qwen3-0.6b int4 decode GEMV chain (28 layers + tied lm_head)", "batch": B,
-                           "hidden": H, "intermediate": INTER, "vocab": VOCAB, "layers": LAYERS,
-                           "bytes_per_step": nbytes, "l2": "weights 335 MB > 126 MB L2 (no flush needed)",
-                           "parallelism": "replicas" if world > 1 else "single"},
-                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": run.launches * args.steps,
+        line = {"metric": "Qwen3-1.7B int4 decode tok/s (context %d, batch %d)" % (S, B), "value": round(value, 2),
+                "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+                "config": {"workload": "qwen3-1.7b int4 decode step (28 layers, int8 KV, tied lm_head)",
+                           "batch": B, "context": S, "hidden": Q17["hidden"], "layers": Q17["layers"],
+                           "heads": "%d q / %d kv x %d" % (Q17["n_heads"], Q17["n_kv_heads"], Q17["head_dim"]),
+                           "intermediate": Q17["intermediate"], "vocab": Q17["vocab"],
+                           "bytes_per_step_per_rank": nbytes,
+                           "l2": "weights 0.97 GB + KV cache > 126 MB L2 (no flush needed)",
+                           "parallelism": "tp%d" % world if world > 1 else "single"},
+                "roofline": roof, "cpu_baseline": cpu,
+                "e2e": {"value": round(B * 1e3 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+                "gpu_launches": kernels * args.steps, "nccl_collectives_per_step": colls,
+                "tp_exchange": args.tp_exchange if world > 1 else None,
                 "clocks": clocks_info}
         line.update(extras)
         print(json.dumps(line), flush=True)
-    run.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -335,6 +335,14 @@ TB_API int tb_qwen3_io(tb_qwen3 *m, uint32_t **ids, int32_t **pos, float **logit
 /* 128-byte NCCL unique id (rank 0 makes it, every rank passes it to tp_init). */
 TB_API int tb_nccl_unique_id(void *out128);
 TB_API int tb_qwen3_tp_init(tb_qwen3 *m, const void *unique_id128);
+/* Exchange over NVLink peer memory instead of NCCL: every rank gets its
+ * 64-byte CUDA IPC handle, the handles of all ranks are shared (rank order,
+ * P x 64 bytes) and passed to tb_qwen3_tp_connect.  The step then sums the
+ * o/down partials and merges the argmax with this library's own exchange
+ * kernels (peer loads + system-scope flags, bounded waits that set the
+ * device error word); the result is identical on every rank. */
+TB_API int tb_qwen3_tp_handle(tb_qwen3 *m, void *out64);
+TB_API int tb_qwen3_tp_connect(tb_qwen3 *m, const void *handles);
 TB_API int tb_qwen3_decode_step(tb_qwen3 *m);
 /* Kernels of this library in one recorded step, and NCCL collectives. */
 TB_API int tb_qwen3_launches_per_step(tb_qwen3 *m, int *kernels, int *collectives);

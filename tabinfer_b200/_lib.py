@@ -66,6 +66,8 @@ SIGNATURES = {
     "tb_qwen3_io": [P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],
     "tb_nccl_unique_id": [P],
     "tb_qwen3_tp_init": [P, P],
+    "tb_qwen3_tp_handle": [P, P],
+    "tb_qwen3_tp_connect": [P, P],
     "tb_qwen3_decode_step": [P],
     "tb_qwen3_launches_per_step": [P, ctypes.POINTER(I32), ctypes.POINTER(I32)],
 }

@@ -36,3 +36,11 @@ int tb_argmax_merge_impl(tb_ctx* ctx, const unsigned long long* keys, int nshard
 // int4 G32 quantization of an N x K slice with source row stride ld (elements)
 int tb_quant_int4_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint32_t* pack, uint16_t* scales,
                                int64_t N, int64_t K);
+
+// tensor-parallel exchanges over IPC-mapped peer arenas (tb_tp.cu)
+size_t tb_tp_arena_bytes(int P, int64_t n);
+void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long** keys, unsigned** flag,
+                        unsigned** flag2, unsigned** step);
+int tb_tp_allreduce_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, float* x, int xi, int nx);
+int tb_tp_argmax_merge_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, int rows, uint32_t* ids,
+                            int32_t* pos);

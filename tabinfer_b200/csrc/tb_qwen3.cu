@@ -107,8 +107,12 @@ struct tb_qwen3 {
     cudaStream_t cap_stream = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
-    // tensor parallel
+    // tensor parallel: NCCL, or the exchange kernels over IPC-mapped peer arenas
     ncclComm_t comm = nullptr;
+    char* arena = nullptr;                       // this rank's exchange arena (tb_tp.cu)
+    char* peer_arena[8] = {};                    // every rank's arena, mapped here (own at [r])
+    bool p2p = false;
+    int ncoll = 0;                               // NCCL calls in the recorded step
     std::vector<void*> allocs;
 };
 
@@ -205,10 +209,18 @@ int gemv_rows(tb_qwen3* m, float* y, const float* x, const Mat& w, const uint16_
     return TB_OK;
 }
 
-// x_next = x + sum over ranks of (W_r . a_r); returns the buffer holding x_next
-int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w)
+// x_next = x + sum over ranks of (W_r . a_r); `cur` names the buffer holding
+// x_next afterwards.  xi: index of this exchange within the step.
+int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w, int xi)
 {
     if (m->P == 1) return gemv_rows(m, m->x[cur], a, w, nullptr, 1);
+    if (m->p2p) {
+        const int64_t n = (int64_t)m->c.batch * m->c.hidden;
+        float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
+        tb_tp_arena_layout(m->arena, n, &part, &keys, &flag, &flag2, &step);
+        TRY(gemv_rows(m, part + (size_t)((xi + 1) & 1) * n, a, w, nullptr, 0));
+        return tb_tp_allreduce_impl(m->ctx, m->peer_arena, m->P, m->r, n, m->x[cur], xi, 2 * m->c.layers);
+    }
     const int nxt = cur ^ 1;
     const size_t bytes = (size_t)m->c.batch * m->c.hidden * sizeof(float);
     if (m->r == 0) {
@@ -221,6 +233,7 @@ int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w)
     }
     TRY(nccl_check(m, nccl().AllReduce(m->x[nxt], m->x[nxt], (size_t)m->c.batch * m->c.hidden, ncclFloat32, ncclSum,
                                        m->comm, m->ctx->stream), "allreduce"));
+    m->ncoll++;
     cur = nxt;
     return TB_OK;
 }
@@ -231,6 +244,7 @@ int issue_step(tb_qwen3* m)
     const tb_qwen3_config& c = m->c;
     const int B = c.batch, H = c.hidden, hd = c.head_dim;
     int cur = 0;
+    m->ncoll = 0;
     TRY(tb_embed_gather(ctx, m->ids, 0, m->embed, m->x[cur], B, H));
     for (int l = 0; l < c.layers; l++) {
         Layer& Ly = m->L[l];
@@ -248,14 +262,14 @@ int issue_step(tb_qwen3* m)
                                   m->nKv, hd, B, c.max_seq, m->pos, c.rope_theta, c.rms_eps));
         TRY(tb_attn_decode_impl(ctx, m->attn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, c.max_seq, m->nHq, m->nKv, hd,
                                 m->nsplit, m->PO, m->PML, m->counters, B, c.max_seq, m->pos));
-        TRY(proj_residual(m, cur, m->attn, Ly.o));
+        TRY(proj_residual(m, cur, m->attn, Ly.o, 2 * l));
         for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
             const int nb = std::min(GEMV_MAX_B, B - b0);
             TRY(tb_gateup_silu_int4_dp4a(ctx, m->swi + (int64_t)b0 * m->I, m->x[cur] + (int64_t)b0 * H, Ly.ln2,
                                          c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack, Ly.up.scales, m->I, H,
                                          nb));
         }
-        TRY(proj_residual(m, cur, m->swi, Ly.down));
+        TRY(proj_residual(m, cur, m->swi, Ly.down, 2 * l + 1));
     }
     // final norm + lm_head: gemvQ (f32 activation) at one row, as linearQ routes
     // T = 1 with N >= 16384; the int8 DP4A GEMV for several rows
@@ -267,11 +281,19 @@ int issue_step(tb_qwen3* m)
     }
     if (m->P == 1) {
         TRY(tb_argmax_impl(ctx, m->logits, m->V, B, m->ids, m->amax_part, m->amax_nparts, nullptr, 0, m->pos));
+    } else if (m->p2p) {
+        const int64_t n = (int64_t)B * H;
+        float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
+        tb_tp_arena_layout(m->arena, n, &part, &keys, &flag, &flag2, &step);
+        TRY(tb_argmax_impl(ctx, m->logits, m->V, B, nullptr, m->amax_part, m->amax_nparts, keys,
+                           (uint32_t)(m->r * m->V), nullptr));
+        TRY(tb_tp_argmax_merge_impl(ctx, m->peer_arena, m->P, m->r, n, B, m->ids, m->pos));
     } else {
         TRY(tb_argmax_impl(ctx, m->logits, m->V, B, nullptr, m->amax_part, m->amax_nparts, m->amax_key,
                            (uint32_t)(m->r * m->V), nullptr));
         TRY(nccl_check(m, nccl().AllGather(m->amax_key, m->amax_all, (size_t)B, ncclUint64, m->comm, ctx->stream),
                        "allgather"));
+        m->ncoll++;
         TRY(tb_argmax_merge_impl(ctx, m->amax_all, m->P, B, m->ids, m->pos));
     }
     return TB_OK;
@@ -362,6 +384,10 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
     if (!rc) rc = alloc(m, &m->amax_part, (size_t)B * m->amax_nparts);
     if (!rc) rc = alloc(m, &m->amax_key, B);
     if (!rc) rc = alloc(m, &m->amax_all, (size_t)B * m->P);
+    if (!rc && m->P > 1) {
+        rc = alloc(m, &m->arena, tb_tp_arena_bytes(m->P, B * H));
+        if (!rc && cudaMemset(m->arena, 0, tb_tp_arena_bytes(m->P, B * H)) != cudaSuccess) rc = TB_ERR_CUDA;
+    }
     if (rc) return fail(rc);
     // counters start at zero; ids/pos start at token 0, position 0
     for (void* p : {(void*)m->counters, (void*)m->ids, (void*)m->pos}) {
@@ -382,6 +408,8 @@ TB_API int tb_qwen3_destroy(tb_qwen3* m)
     cudaStreamSynchronize(m->ctx->stream);
     release_graph(m);
     if (m->comm) nccl().CommDestroy(m->comm);
+    for (int s = 0; s < m->P && s < 8; s++)
+        if (s != m->r && m->peer_arena[s]) cudaIpcCloseMemHandle(m->peer_arena[s]);
     for (void* p : m->allocs) cudaFree(p);
     if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
     delete m;
@@ -481,11 +509,54 @@ TB_API int tb_qwen3_tp_init(tb_qwen3* m, const void* unique_id128)
     return TB_OK;
 }
 
+TB_API int tb_qwen3_tp_handle(tb_qwen3* m, void* out64)
+{
+    if (!m || !out64) return TB_ERR_INVALID;
+    TB_REQUIRE(m->ctx, m->P > 1 && m->arena, "tp_handle: model is not tensor-parallel");
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle is 64 bytes");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, m->arena);
+    if (e != cudaSuccess) return tb_fail(m->ctx, TB_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    memcpy(out64, &h, sizeof h);
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_tp_connect(tb_qwen3* m, const void* handles)
+{
+    if (!m || !handles) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    TB_REQUIRE(ctx, m->P > 1 && m->P <= 8 && m->arena, "tp_connect: model is not tensor-parallel (2..8 ranks)");
+    TB_REQUIRE(ctx, !m->p2p, "tp_connect: already connected");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    int rc = TB_OK;
+    for (int s = 0; s < m->P && !rc; s++) {
+        if (s == m->r) { m->peer_arena[s] = m->arena; continue; }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char*>(handles) + 64 * s, sizeof h);
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) rc = tb_fail(ctx, TB_ERR_CUDA, "cudaIpcOpenMemHandle(rank %d): %s", s, cudaGetErrorString(e));
+        else m->peer_arena[s] = static_cast<char*>(p);
+    }
+    cudaSetDevice(prev);
+    if (rc) {
+        for (int s = 0; s < m->P; s++)
+            if (s != m->r && m->peer_arena[s]) { cudaIpcCloseMemHandle(m->peer_arena[s]); m->peer_arena[s] = nullptr; }
+        return rc;
+    }
+    release_graph(m);
+    m->p2p = true;
+    return TB_OK;
+}
+
 TB_API int tb_qwen3_decode_step(tb_qwen3* m)
 {
     if (!m) return TB_ERR_INVALID;
     tb_ctx* ctx = m->ctx;
-    TB_REQUIRE(ctx, m->P == 1 || m->comm != nullptr, "tensor parallel model needs tb_qwen3_tp_init first");
+    TB_REQUIRE(ctx, m->P == 1 || m->p2p || m->comm != nullptr,
+               "tensor parallel model needs tb_qwen3_tp_connect (or tb_qwen3_tp_init) first");
     for (const Layer& Ly : m->L)
         TB_REQUIRE(ctx, Ly.q.set && Ly.k.set && Ly.v.set && Ly.o.set && Ly.gate.set && Ly.up.set && Ly.down.set,
                    "a projection weight was never set");
@@ -538,7 +609,7 @@ TB_API int tb_qwen3_launches_per_step(tb_qwen3* m, int* kernels, int* collective
         cudaGraphNodeType t;
         if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
     }
-    const int coll = m->P > 1 ? 2 * m->c.layers + 1 : 0;
+    const int coll = m->ncoll;      // each NCCL call records one kernel node
     *kernels = k - coll;
     if (collectives) *collectives = coll;
     return TB_OK;

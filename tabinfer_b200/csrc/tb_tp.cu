@@ -1,0 +1,182 @@
+// tb_tp.cu -- tensor-parallel exchanges of the decode step over NVLink peer
+// memory: one kernel per exchange, no library collective.
+//
+// Every rank owns a small "exchange arena" in its own HBM, mapped into every
+// other rank with CUDA IPC:
+//   part[2][n]   f32 partial products of the row-split o / down GEMVs, double
+//                buffered by exchange parity
+//   keys[16]     u64 argmax keys of this rank's vocab shard (value, index)
+//   flag[P]      u32 epochs written by the peers ("my part for epoch e is ready")
+//   flag2[P]     the same for the argmax keys
+//   step         u32 steps completed (local)
+// An exchange: after the producing kernel finished (griddepcontrol.wait), rank
+// r stores epoch e into flag[r] of every rank with a system-scope release,
+// waits until its own flag[s] >= e for every s (acquire, bounded), then reads
+// the P partials straight from the peers' arenas and adds them in rank order,
+// so every rank computes the identical sum.  Epochs e = step * nx + i + 1 grow
+// monotonically, so the flags never need clearing and the recorded step can be
+// replayed.  Reuse is safe with two part buffers: rank r overwrites
+// part[parity(e)] at exchange e+2 only after every peer signalled e+1, which a
+// peer does only after it finished reading exchange e.
+#include "tb_internal.h"
+
+namespace {
+
+constexpr int TP_MAX = 8;
+constexpr long long TP_WAIT_LIMIT = 1LL << 22;    // x 64+ ns sleeps: a fraction of a second to seconds
+constexpr int ERR_TP_WAIT = 0x7a01;
+
+struct TpArgs {
+    const float* part[TP_MAX];      // this exchange's part buffer on every rank
+    unsigned* peer_flag[TP_MAX];    // &flag[r] on every rank (where this rank signals)
+    const unsigned* my_flag;        // flag[0..P) of this rank
+    const unsigned* step;           // steps completed
+    float* x;                       // residual, updated in place: x += sum_s part_s
+    int n, P, xi, nx;
+    int* err;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_volatile_f4(const float* p)
+{
+    float4 v;
+    asm volatile("ld.volatile.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p) : "memory");
+    return v;
+}
+
+// signal flag slot of every rank, then wait for every rank's signal (bounded)
+__device__ __forceinline__ void tp_signal_wait(unsigned* const* peer_flag, const unsigned* my_flag, int P, unsigned e,
+                                               bool signal, int* err)
+{
+    if (signal && threadIdx.x < P) st_release_sys(peer_flag[threadIdx.x], e);
+    if (threadIdx.x < P) {
+        long long it = 0;
+        while ((int)(ld_acquire_sys(my_flag + threadIdx.x) - e) < 0) {
+            if (++it > TP_WAIT_LIMIT) {
+                atomicExch(err, ERR_TP_WAIT);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+}
+
+// x[i] += part_0[i] + part_1[i] + ... (rank order), float4 per thread
+__global__ void __launch_bounds__(256) k_tp_allreduce(const TpArgs a)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const unsigned e = *a.step * (unsigned)a.nx + (unsigned)a.xi + 1u;
+    tp_signal_wait(a.peer_flag, a.my_flag, a.P, e, blockIdx.x == 0, a.err);
+    const int n4 = a.n >> 2;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        float4 v = reinterpret_cast<const float4*>(a.x)[i];
+        for (int s = 0; s < a.P; s++) {
+            const float4 p = ld_volatile_f4(a.part[s] + 4 * i);
+            v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+        }
+        reinterpret_cast<float4*>(a.x)[i] = v;
+    }
+}
+
+struct TpKeyArgs {
+    const unsigned long long* keys[TP_MAX];   // every rank's argmax keys
+    unsigned* peer_flag2[TP_MAX];
+    const unsigned* my_flag2;
+    unsigned* step;                           // incremented here: the last kernel of a step
+    uint32_t* ids;
+    int32_t* pos;
+    int rows, P;
+    int* err;
+};
+
+// the argmax over all vocab shards: the largest key (value, then lower global
+// index) of the P ranks; ids/pos updated, step counter advanced
+__global__ void __launch_bounds__(32) k_tp_argmax_merge(const TpKeyArgs a)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const unsigned e = *a.step + 1u;
+    tp_signal_wait(a.peer_flag2, a.my_flag2, a.P, e, true, a.err);
+    for (int row = threadIdx.x; row < a.rows; row += blockDim.x) {
+        unsigned long long best = 0ull;
+        for (int s = 0; s < a.P; s++) {
+            const unsigned long long k = *reinterpret_cast<const volatile unsigned long long*>(a.keys[s] + row);
+            best = k > best ? k : best;
+        }
+        a.ids[row] = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+        a.pos[row] += 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *a.step = e;
+}
+
+}  // namespace
+
+// ---- arena layout -----------------------------------------------------------
+size_t tb_tp_arena_bytes(int P, int64_t n)
+{
+    (void)P;
+    const size_t part = ((size_t)2 * n * 4 + 255) & ~size_t(255);
+    return part + 16 * 8 + 2 * TP_MAX * 4 + 256;
+}
+
+void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long** keys, unsigned** flag,
+                        unsigned** flag2, unsigned** step)
+{
+    const size_t part_b = ((size_t)2 * n * 4 + 255) & ~size_t(255);
+    *part = reinterpret_cast<float*>(base);
+    *keys = reinterpret_cast<unsigned long long*>(base + part_b);
+    *flag = reinterpret_cast<unsigned*>(base + part_b + 16 * 8);
+    *flag2 = *flag + TP_MAX;
+    *step = *flag2 + TP_MAX;
+}
+
+// x += sum over ranks of part (exchange xi of nx per step, parity buffer
+// (xi + 1) & 1 of every rank's arena)
+int tb_tp_allreduce_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, float* x, int xi, int nx)
+{
+    TB_REQUIRE(ctx, P >= 2 && P <= TP_MAX && n % 4 == 0 && TB_ALIGNED(x, 16), "tp allreduce: bad arguments");
+    TpArgs a{};
+    for (int s = 0; s < P; s++) {
+        float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
+        tb_tp_arena_layout(arenas[s], n, &part, &keys, &flag, &flag2, &step);
+        a.part[s] = part + (size_t)((xi + 1) & 1) * n;
+        a.peer_flag[s] = flag + r;
+        if (s == r) { a.my_flag = flag; a.step = step; }
+    }
+    a.x = x; a.n = (int)n; a.P = P; a.xi = xi; a.nx = nx; a.err = ctx->dev_error;
+    const int grid = (int)std::min<int64_t>(std::max<int64_t>(1, (n / 4 + 255) / 256), 32);
+    cudaError_t e = tb_launch(ctx, k_tp_allreduce, dim3(grid), dim3(256), 0, a);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "tp allreduce launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+int tb_tp_argmax_merge_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, int rows, uint32_t* ids,
+                            int32_t* pos)
+{
+    TB_REQUIRE(ctx, P >= 2 && P <= TP_MAX && rows >= 1 && rows <= 16, "tp argmax: bad arguments");
+    TpKeyArgs a{};
+    for (int s = 0; s < P; s++) {
+        float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
+        tb_tp_arena_layout(arenas[s], n, &part, &keys, &flag, &flag2, &step);
+        a.keys[s] = keys;
+        a.peer_flag2[s] = flag2 + r;
+        if (s == r) { a.my_flag2 = flag2; a.step = step; }
+    }
+    a.ids = ids; a.pos = pos; a.rows = rows; a.P = P; a.err = ctx->dev_error;
+    cudaError_t e = tb_launch(ctx, k_tp_argmax_merge, dim3(1), dim3(32), 0, a);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "tp argmax launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}

@@ -140,7 +140,20 @@ class Qwen3:
         return True
 
     def tp_init(self, unique_id):
+        """NCCL exchange: every rank passes the same 128-byte unique id."""
         self.ctx.check(LIB.tb_qwen3_tp_init(self.h, ctypes.c_char_p(bytes(unique_id))), "tp_init")
+
+    def tp_handle(self):
+        """This rank's 64-byte IPC handle of its exchange arena."""
+        buf = ctypes.create_string_buffer(64)
+        self.ctx.check(LIB.tb_qwen3_tp_handle(self.h, buf), "tp_handle")
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """Peer-memory exchange: handles = every rank's tp_handle(), rank order."""
+        blob = b"".join(bytes(h) for h in handles)
+        assert len(blob) == 64 * self.cfg["tp_size"]
+        self.ctx.check(LIB.tb_qwen3_tp_connect(self.h, ctypes.c_char_p(blob)), "tp_connect")
 
     # ---- cache and I/O ----------------------------------------------------------
     def kv_pointers(self, layer):
