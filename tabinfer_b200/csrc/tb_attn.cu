@@ -33,6 +33,57 @@ __device__ __forceinline__ int8_t snorm8(float v)
 // position is outside the cache (the host cannot check it).
 constexpr int ERR_ATTN_POS = 0x6a01;
 
+// ---- attnPrepQ8 math (qwen3.js:2228-2296) -----------------------------------
+// RoPE angle of dimension j (split-half pairs j, j + hd/2) at position pos, in
+// double: pos * theta^(-2 fi / hd).
+__device__ __forceinline__ void rope_cs(int j, int hd, long long pos, float theta, float* c, float* s)
+{
+    const int half = hd >> 1;
+    const int fi = j < half ? j : j - half;
+    const double ang = (double)pos * pow((double)theta, -2.0 * (double)fi / (double)hd);
+    double sd, cd;
+    sincos(ang, &sd, &cd);
+    *c = (float)cd;
+    *s = (float)sd;
+}
+
+// Per-head RMSNorm (w16) + RoPE of x (thread j holds element j of the head,
+// threads j >= hd hold nothing); every thread of the block calls it.  rk: hd
+// floats of shared memory, red: 8.
+__device__ __forceinline__ float norm_rope(float x, const uint16_t* w16, int hd, float eps, float c, float s, float* rk,
+                                           float* red)
+{
+    const int j = threadIdx.x, lane = j & 31, wid = j >> 5, nw = hd >> 5;
+    const float ss = warp_sum(j < hd ? x * x : 0.0f);
+    if (lane == 0 && wid < nw) red[wid] = ss;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < nw; i++) t += red[i];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), eps)));
+    if (j < hd) rk[j] = __fmul_rn(__fmul_rn(x, inv), tb_h2f(w16[j]));
+    __syncthreads();
+    float y = 0.0f;
+    if (j < hd) {
+        const int half = hd >> 1;
+        const float partner = j < half ? rk[j + half] : rk[j - half];
+        const float rot = j < half ? -partner : partner;
+        y = fmaf(rk[j], c, rot * s);
+    }
+    __syncthreads();   // rk and red may be reused
+    return y;
+}
+
+// snorm int8 of one 32-group per warp (pack4x8snorm of x / max(1e-12, maxabs))
+// into row dq / scales ds (element j of the head at dq[j], group scale at ds[j/32])
+__device__ __forceinline__ void quant_row(float x, int hd, int8_t* dq, float* ds)
+{
+    const int j = threadIdx.x, lane = j & 31;
+    if ((j >> 5) >= (hd >> 5)) return;
+    const float m = fmaxf(1e-12f, warp_max(fabsf(x)));
+    dq[j] = snorm8(__fdiv_rn(x, m));
+    if (lane == 0) ds[j >> 5] = m;
+}
+
 // ---- fused prep: q rope, k rope + quant-write, v quant-write ---------------
 // grid = (nHq + 2*nKv, B) CTAs, block = hd threads (hd % 32 == 0, hd <= 256).
 // Sequence b reads q/k/v row b, writes qr row b and cache row pos_b of its own
@@ -68,32 +119,15 @@ __global__ void __launch_bounds__(256) k_attn_prep(const float* __restrict__ q, 
     const float* src = isQ ? q : (isK ? k : v);
     float x = src[(long long)head * hd + j];
     if (isQ || isK) {
-        float ss = warp_sum(x * x);
-        if (lane == 0) red[wid] = ss;
-        __syncthreads();
-        float t = 0.0f;
-        for (int i = 0; i < nw; i++) t += red[i];
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), eps)));
-        rk[j] = __fmul_rn(__fmul_rn(x, inv), tb_h2f((isQ ? qw : kw)[j]));
-        __syncthreads();
-        const int half = hd >> 1;
-        const int fi = j < half ? j : j - half;
-        // angle in double: pos * theta^(-2 fi / hd)
-        double ang = (double)pos * pow((double)theta, -2.0 * (double)fi / (double)hd);
-        double sd, cd;
-        sincos(ang, &sd, &cd);
-        const float partner = j < half ? rk[j + half] : rk[j - half];
-        const float rot = j < half ? -partner : partner;
-        x = fmaf(rk[j], (float)cd, rot * (float)sd);
+        float c, sn;
+        rope_cs(j, hd, pos, theta, &c, &sn);
+        x = norm_rope(x, isQ ? qw : kw, hd, eps, c, sn, rk, red);
         if (isQ) { qr[(long long)head * hd + j] = x; return; }
     }
     // quantize one 32-group per warp straight into the cache row `pos`
-    const float m = fmaxf(1e-12f, warp_max(fabsf(x)));
     const long long row = pos * nKv * hd + (long long)head * hd;
-    int8_t* dq = isK ? Kq : Vq;
-    float* ds = isK ? Ks : Vs;
-    dq[row + j] = snorm8(__fdiv_rn(x, m));
-    if (lane == 0) ds[row / 32 + wid] = m;
+    quant_row(x, hd, (isK ? Kq : Vq) + row, (isK ? Ks : Vs) + row / 32);
+    (void)lane; (void)wid; (void)nw;
 }
 
 // ---- prefill quant-write of T rows (KVQW) -----------------------------------
@@ -133,6 +167,11 @@ struct AttnArgs {
     int S, nHq, nKv, nsplit;
     int grid_z;            // sequences
 };
+
+// k_attn_decode mode EARLY (the decode step): the position and every cache row
+// below S-1 were written by earlier steps, so each warp's first tile is fetched
+// before griddepcontrol.wait unless it holds row S-1, which the preceding prep
+// kernel writes.
 
 // ---- cp.async (16-byte and 8-byte global -> shared copies, per thread) -----
 __device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc)
@@ -183,7 +222,7 @@ struct DecLayout {
 // p * vscale / 127 per V group, and P.V runs lane = 4 dims (2 for hd 64)
 // over the tile's keys.  Softmax is online per warp; the 4 warps merge at the
 // end into the split's partial (PO, PML).
-template <int HD, int GRP>
+template <int HD, int GRP, bool EARLY>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
 {
     using L = DecLayout<HD, GRP>;
@@ -208,8 +247,10 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
     float* PML = a.PML + (long long)zb * a.nHq * a.nsplit * 2;
     float* outp = a.out + (long long)zb * a.nHq * HD;
     unsigned* counter = a.counters + (long long)zb * a.nKv + hk;
-    tb_pdl_wait();
-    tb_pdl_trigger();
+    if (!EARLY) {
+        tb_pdl_wait();
+        tb_pdl_trigger();
+    }
     int S = a.S;
     if (a.dpos) {
         S = a.dpos[zb] + 1;
@@ -260,8 +301,17 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
         cp_async_commit();
     };
 
-    issue(0, 0);
     const float qscale = rsqrtf((float)HD) * (1.0f / 127.0f);
+    if constexpr (EARLY) {
+        const int last = S - 1, t00 = c0 + wid * 32;
+        const bool first_new = ntile > 0 && t00 <= last && last < t00 + 32;
+        if (!first_new) issue(0, 0);
+        tb_pdl_wait();
+        tb_pdl_trigger();
+        if (first_new) issue(0, 0);
+    } else {
+        issue(0, 0);
+    }
     for (int i = threadIdx.x; i < GRP * HD; i += ATT_THREADS) qs[i] = qrow[(long long)hk * GRP * HD + i];
     __syncthreads();
 
@@ -476,19 +526,43 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
     if (threadIdx.x == 0) *counter = 0u;     // ready for the next call
 }
 
-template <int HD, int GRP>
+template <int HD, int GRP, bool EARLY>
 int launch_decode(tb_ctx* ctx, const AttnArgs& a)
 {
     constexpr int bytes = DecLayout<HD, GRP>::BYTES;
+    auto kern = k_attn_decode<HD, GRP, EARLY>;
     static bool attr_set[64] = {};   // per device and instantiation; setting it twice is harmless
     if (ctx->device >= 64 || !attr_set[ctx->device]) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_decode<HD, GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode smem attribute: %s", cudaGetErrorString(e));
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode attribute: %s", cudaGetErrorString(e));
         if (ctx->device < 64) attr_set[ctx->device] = true;
     }
-    cudaError_t e = tb_launch(ctx, k_attn_decode<HD, GRP>, dim3(a.nKv, a.nsplit, a.grid_z), dim3(ATT_THREADS), bytes, a);
+    cudaError_t e = tb_launch(ctx, kern, dim3(a.nKv, a.nsplit, a.grid_z), dim3(ATT_THREADS), bytes, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
     return TB_OK;
+}
+
+template <bool EARLY>
+int decode_dispatch(tb_ctx* ctx, const AttnArgs& a, int64_t hd, int grp)
+{
+    if (hd == 128) {
+        switch (grp) {
+        case 1: return launch_decode<128, 1, EARLY>(ctx, a);
+        case 2: return launch_decode<128, 2, EARLY>(ctx, a);
+        case 4: return launch_decode<128, 4, EARLY>(ctx, a);
+        case 8: return launch_decode<128, 8, EARLY>(ctx, a);
+        default: return tb_fail(ctx, TB_ERR_UNSUPPORTED, "nHq/nKv = %d not built (1, 2, 4, 8)", grp);
+        }
+    } else if (hd == 64) {
+        switch (grp) {
+        case 1: return launch_decode<64, 1, EARLY>(ctx, a);
+        case 2: return launch_decode<64, 2, EARLY>(ctx, a);
+        case 4: return launch_decode<64, 4, EARLY>(ctx, a);
+        case 8: return launch_decode<64, 8, EARLY>(ctx, a);
+        default: return tb_fail(ctx, TB_ERR_UNSUPPORTED, "nHq/nKv = %d not built (1, 2, 4, 8)", grp);
+        }
+    }
+    return tb_fail(ctx, TB_ERR_UNSUPPORTED, "head_dim %lld not built (64, 128)", (long long)hd);
 }
 
 }  // namespace
@@ -509,30 +583,13 @@ int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv)
 int tb_attn_decode_impl(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
                         const int8_t* Vq, const float* Vs, int64_t S, int64_t nHq, int64_t nKv, int64_t hd,
                         int nsplit, float* PO, float* PML, unsigned* counters, int64_t batch,
-                        int64_t cache_rows, const int32_t* dpos)
+                        int64_t cache_rows, const int32_t* dpos, bool early)
 {
     AttnArgs a{qr, Kq, Ks, Vq, Vs, PO, PML, out, counters, (const int*)dpos, ctx->dev_error,
                (long long)(cache_rows > 0 ? cache_rows : S), (int)S, (int)nHq, (int)nKv, nsplit};
     a.grid_z = (int)batch;
-    const int grp = (int)(nHq / nKv);
-    if (hd == 128) {
-        switch (grp) {
-        case 1: return launch_decode<128, 1>(ctx, a);
-        case 2: return launch_decode<128, 2>(ctx, a);
-        case 4: return launch_decode<128, 4>(ctx, a);
-        case 8: return launch_decode<128, 8>(ctx, a);
-        default: return tb_fail(ctx, TB_ERR_UNSUPPORTED, "nHq/nKv = %d not built (1, 2, 4, 8)", grp);
-        }
-    } else if (hd == 64) {
-        switch (grp) {
-        case 1: return launch_decode<64, 1>(ctx, a);
-        case 2: return launch_decode<64, 2>(ctx, a);
-        case 4: return launch_decode<64, 4>(ctx, a);
-        case 8: return launch_decode<64, 8>(ctx, a);
-        default: return tb_fail(ctx, TB_ERR_UNSUPPORTED, "nHq/nKv = %d not built (1, 2, 4, 8)", grp);
-        }
-    }
-    return tb_fail(ctx, TB_ERR_UNSUPPORTED, "head_dim %lld not built (64, 128)", (long long)hd);
+    return early ? decode_dispatch<true>(ctx, a, hd, (int)(nHq / nKv))
+                 : decode_dispatch<false>(ctx, a, hd, (int)(nHq / nKv));
 }
 
 int tb_attn_check(tb_ctx* ctx, const float* qr, const int8_t* Kq, const float* Ks, const int8_t* Vq, const float* Vs,

@@ -17,13 +17,15 @@ int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, f
 // split-KV decode attention over `batch` sequences; sequence b's cache starts
 // cache_rows rows after sequence b-1's; with dpos, S_b = dpos[b] + 1 is read on
 // the device.  PO/PML: batch*nHq*nsplit*(hd, 2) floats; counters: batch*nKv
-// words that are zero between calls.
+// words that are zero between calls.  early: dpos and every cache row below
+// S_b - 1 are complete before the preceding kernel in the stream runs (only
+// that kernel may write row S_b - 1), so the first tiles are fetched before
+// griddepcontrol.wait.
 int tb_attn_decode_impl(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
                         const int8_t* Vq, const float* Vs, int64_t S, int64_t nHq, int64_t nKv, int64_t hd,
                         int nsplit, float* PO, float* PML, unsigned* counters, int64_t batch = 1,
-                        int64_t cache_rows = 0, const int32_t* dpos = nullptr);
+                        int64_t cache_rows = 0, const int32_t* dpos = nullptr, bool early = false);
 int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv);
-
 // two-stage argmax of `rows` rows of n; part holds rows*nparts keys.  out gets
 // the index + idx_base, out_key the ordered key (for tb_argmax_merge_impl),
 // pos_inc[row] += 1 when given.

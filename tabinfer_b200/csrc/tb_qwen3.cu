@@ -98,10 +98,10 @@ struct tb_qwen3 {
     float* x[2] = {nullptr, nullptr};            // residual (ping-pong under TP)
     float *q = nullptr, *k = nullptr, *v = nullptr, *qr = nullptr, *attn = nullptr, *swi = nullptr;
     float *logits = nullptr, *PO = nullptr, *PML = nullptr;
+    unsigned* counters = nullptr;
     uint32_t* ids = nullptr;
     int32_t* pos = nullptr;
     unsigned long long *amax_part = nullptr, *amax_key = nullptr, *amax_all = nullptr;
-    unsigned* counters = nullptr;
     int nsplit = 1, amax_nparts = 1;
     // graph
     cudaStream_t cap_stream = nullptr;
@@ -261,7 +261,7 @@ int issue_step(tb_qwen3* m)
         TRY(tb_attn_prep_q8_batch(ctx, m->q, m->k, m->v, Ly.qn, Ly.kn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, m->nHq,
                                   m->nKv, hd, B, c.max_seq, m->pos, c.rope_theta, c.rms_eps));
         TRY(tb_attn_decode_impl(ctx, m->attn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, c.max_seq, m->nHq, m->nKv, hd,
-                                m->nsplit, m->PO, m->PML, m->counters, B, c.max_seq, m->pos));
+                                m->nsplit, m->PO, m->PML, m->counters, B, c.max_seq, m->pos, true));
         TRY(proj_residual(m, cur, m->attn, Ly.o, 2 * l));
         for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
             const int nb = std::min(GEMV_MAX_B, B - b0);
@@ -370,11 +370,11 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
     if (!rc) rc = alloc(m, &m->q, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->k, B * kvrow);
     if (!rc) rc = alloc(m, &m->v, B * kvrow);
-    if (!rc) rc = alloc(m, &m->qr, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->attn, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->swi, B * m->I);
     if (!rc) rc = alloc(m, &m->logits, B * m->V);
     m->nsplit = tb_attn_auto_nsplit(ctx, c.max_seq, m->nKv * B);
+    if (!rc) rc = alloc(m, &m->qr, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->PO, (size_t)B * m->nHq * m->nsplit * hd);
     if (!rc) rc = alloc(m, &m->PML, (size_t)B * m->nHq * m->nsplit * 2);
     if (!rc) rc = alloc(m, &m->counters, (size_t)B * m->nKv);

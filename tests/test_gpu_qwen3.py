@@ -60,10 +60,16 @@ def _check_step(m, om, cfg, ids, pos, route_f32):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("batch,hd,heads", [(2, 128, (4, 2)), (9, 64, (8, 2)), (1, 128, (8, 8))])
-def test_decode_step_matches_oracle(cuda, batch, hd, heads):
-    cfg = dict(SMALL, batch=batch, head_dim=hd, n_heads=heads[0], n_kv_heads=heads[1])
-    prefill = [(5 + 7 * b) % 40 for b in range(batch)]
+@pytest.mark.parametrize("batch,hd,heads,max_seq,layers", [(2, 128, (4, 2), 64, 2), (9, 64, (8, 2), 64, 2),
+                                                           (1, 128, (8, 8), 64, 2), (2, 128, (4, 2), 1024, 1),
+                                                           (3, 128, (16, 8), 4096, 1), (1, 64, (8, 1), 2000, 1)])
+def test_decode_step_matches_oracle(cuda, batch, hd, heads, max_seq, layers):
+    """max_seq sets the attention's split count (the automatic rule at S_max =
+    max_seq), so the larger cases combine many splits."""
+    cfg = dict(SMALL, batch=batch, head_dim=hd, n_heads=heads[0], n_kv_heads=heads[1], max_seq=max_seq,
+               layers=layers)
+    prefill = [(5 + 7 * b) % 40 if max_seq <= 64 else (max_seq * (b + 1)) // (batch + 2) + 3 * b
+               for b in range(batch)]
     W, m = _build(cfg, 11 + batch, prefill)
     om = OracleModel(cfg, W)
     ids = [(17 + 131 * b) % cfg["vocab"] for b in range(batch)]
