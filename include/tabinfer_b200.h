@@ -115,8 +115,8 @@ TB_API int tb_gemv_int4_f32(tb_ctx *ctx, float *y, const float *x, const uint32_
 /* The linearQ router for one int4 matrix, models/qwen3.js:1588-1608:
  * T==1 and N<16384 -> quantQ8 + gemvDP4; T==1 and N>=16384 -> gemvQ;
  * 1<T<=8 -> per-token int8 (QUANTQ8T) x int4 math of gemmDP4A (:1397-1407);
- * T>8 -> TB_ERR_UNSUPPORTED until the prefill GEMM entry point is used.
- * Uses context-owned scratch for the quantized activation. */
+ * T>8 -> the f16 prefill GEMM (gemmQ, tb_gemm_int4_g32) when T % 128 == 0,
+ * N % 256 == 0 and K % 64 == 0, else TB_ERR_UNSUPPORTED. */
 TB_API int tb_linear_int4(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
                           const uint16_t *scales, int64_t T, int64_t N, int64_t K, int acc);
 
@@ -265,6 +265,15 @@ TB_API int tb_rmsnorm(tb_ctx *ctx, const float *x, const uint16_t *w16, float *y
 /* y[t,:] = f32(embed_f16[ids[idoff+t], :]).  embedGather, qwen3.js:1663-1675. */
 TB_API int tb_embed_gather(tb_ctx *ctx, const uint32_t *ids, int64_t idoff,
                            const uint16_t *embed_f16, float *y, int64_t T, int64_t H);
+
+/* ---- prefill GEMM (tcgen05 / TMEM) -------------------------------------------
+ * Y[M,N] (+)= f16(X[M,K]) . f16(deq(W[N,K]))^T with f32 accumulation: the
+ * reference's f16 prefill GEMM gemmQ (models/qwen3.js:964-1026, gemmqWgsl), the
+ * weights in the int4 G=32 layout of tb_quant_int4_g32.  X is f32 (x_bf16 = 0,
+ * as linearQ's buffers) or bf16 (x_bf16 = 1).  M % 128 == 0, N % 256 == 0,
+ * K % 64 == 0; x, pack, y 16-byte aligned, scales 4-byte aligned. */
+TB_API int tb_gemm_int4_g32(tb_ctx *ctx, float *y, const void *x, int x_bf16, const uint32_t *pack,
+                            const uint16_t *scales, int64_t M, int64_t N, int64_t K, int acc);
 
 /* bf16 -> f16 bits, rounded half-up as the loader's bf16ToF16bits
  * (models/qwen3.js:3357-3390): the f16 copies of the embedding table and the

@@ -152,6 +152,20 @@ def gemv_int4_f32act(x, pack, scales):
     return y
 
 
+def gemm_int4_f16(x, pack, scales):
+    """f16 prefill GEMM (gemmQ): x [M,K] f32 or bf16 bits (uint16) -> y [M,N] f64."""
+    x = np.ascontiguousarray(x)
+    bf16 = x.dtype == np.uint16
+    if not bf16:
+        x = np.ascontiguousarray(x, np.float32)
+    M, K = x.shape
+    N = pack.shape[0]
+    y = np.zeros((M, N), np.float64)
+    lib().tbo_gemm_int4_f16(_ptr(x), ctypes.c_int(1 if bf16 else 0), _ptr(np.ascontiguousarray(pack)),
+                            _ptr(np.ascontiguousarray(scales)), _I(M), _I(N), _I(K), _ptr(y))
+    return y
+
+
 def quant_q8(x):
     x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
     T, K = x.shape

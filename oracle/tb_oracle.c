@@ -159,6 +159,47 @@ TBO_API void tbo_gemv_int4_f32act(const float *x, const uint32_t *pack,
 }
 
 /* ------------------------------------------------------------------------ */
+/* f16 prefill GEMM -- gemmqWgsl / gemmQ, qwen3.js:964-1026: the activation   */
+/* tile is stored as f16 (vec4<f16>(X), round to nearest even), each weight as */
+/* f16((nib - 8) * f32(scale)) (the product is exact in f32, one rounding),    */
+/* and the f16 products are summed in f32 on the GPU; here in f64.             */
+/* ------------------------------------------------------------------------ */
+
+/* x [M,K] f32 (or bf16 bits when x_bf16), pack/scales of W [N,K] -> y [M,N]. */
+TBO_API void tbo_gemm_int4_f16(const void *x, int x_bf16, const uint32_t *pack, const uint16_t *scales,
+                               int64_t M, int64_t N, int64_t K, double *y)
+{
+    const int64_t wpr = K / 8, gpr = K / 32;
+    double *wrow = (double *)malloc(sizeof(double) * (size_t)K);
+    double *xf = (double *)malloc(sizeof(double) * (size_t)(M * K));
+    for (int64_t i = 0; i < M * K; i++) {
+        float v;
+        if (x_bf16) {
+            uint32_t b = (uint32_t)((const uint16_t *)x)[i] << 16;
+            memcpy(&v, &b, 4);
+        } else {
+            v = ((const float *)x)[i];
+        }
+        xf[i] = (double)(_Float16)v;          /* round to nearest even */
+    }
+    for (int64_t n = 0; n < N; n++) {
+        for (int64_t k = 0; k < K; k++) {
+            const float s = (float)tbo_f16_to_f64(scales[n * gpr + k / 32]);
+            const int nib = (int)((pack[n * wpr + (k >> 3)] >> (4 * (k & 7))) & 0xFu);
+            wrow[k] = (double)(_Float16)((float)(nib - 8) * s);
+        }
+        for (int64_t m = 0; m < M; m++) {
+            double a = 0.0;
+            const double *xr = xf + m * K;
+            for (int64_t k = 0; k < K; k++) a += xr[k] * wrow[k];
+            y[m * N + n] = a;
+        }
+    }
+    free(wrow);
+    free(xf);
+}
+
+/* ------------------------------------------------------------------------ */
 /* int8 per-32 activation quantizer -- QUANTQ8 qwen3.js:332-358 (one row),    */
 /* QUANTQ8T qwen3.js:1210-1231 (T rows).  WGSL f32 semantics.                */
 /* ------------------------------------------------------------------------ */

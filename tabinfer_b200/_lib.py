@@ -58,6 +58,7 @@ SIGNATURES = {
     "tb_attn_prep_q8_batch": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, P, F32, F32],
     "tb_attn_decode_q8_batch": [P, P, P, P, P, P, P, I64, I64, P, I64, I64, I64, I64, I32],
     "tb_convert_bf16_f16": [P, P, P, I64],
+    "tb_gemm_int4_g32": [P, P, P, I32, P, P, I64, I64, I64, I32],
     "tb_qwen3_shard": [P, I32, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)],
     "tb_qwen3_create": [P, P, ctypes.POINTER(P)],
     "tb_qwen3_destroy": [P],

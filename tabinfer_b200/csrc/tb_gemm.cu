@@ -1,0 +1,298 @@
+// tb_gemm.cu -- prefill GEMM Y[M,N] (+)= f16(X[M,K]) . f16(deq(W[N,K]))^T on the
+// 5th-generation tensor cores (tcgen05.mma kind::f16, f32 accumulator in TMEM).
+//
+// The math is the reference's f16 prefill GEMM (gemmqWgsl / gemmQ,
+// models/qwen3.js:964-1026): every activation is rounded to f16, every weight is
+// dequantized as f16((nib - 8) * f16 scale) (one rounding of the exact product),
+// and the products are summed in f32.
+//
+// CTA tile 128 (M) x 256 (N), K in steps of 64.  Warps 0-7 are producers: per
+// stage they read a 128 x 64 block of X (f32 or bf16) and the 256 x 64 block of
+// packed int4 weights with its f16 scales, convert both to f16 and write them
+// into shared memory in the 128-byte-swizzled K-major layout the tensor core
+// reads (8-row x 128-byte atoms).  Warp 8 allocates 256 TMEM columns and one of
+// its threads issues four 128x256x16 MMAs per stage; tcgen05.commit frees the
+// stage when they complete.  After the last stage warps 0-7 read the
+// accumulator (tcgen05.ld, warp w owns TMEM lanes 32*(w%4)..+31 and column half
+// w/4) and store f32 rows.  Waits are bounded: on a timeout the CTA records
+// ERR_GEMM_WAIT, stops issuing, and still frees its TMEM.
+#include "tb_internal.h"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, NST = 4;
+constexpr int PROD_WARPS = 8, THREADS = (PROD_WARPS + 1) * 32;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = 1024 + NST * STAGE + 256;
+constexpr int TMEM_COLS = 256;
+constexpr long long GEMM_WAIT_LIMIT = 1LL << 22;   // polls; with the back-off below, well under a second
+constexpr int ERR_GEMM_WAIT = 0x6b01;
+
+struct GemmArgs {
+    const void* x;          // [M][K] f32 or bf16
+    const uint32_t* pack;   // [N][K/8]
+    const uint16_t* scales; // [N][K/32] f16
+    float* y;               // [M][N]
+    int M, N, K, acc;
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b)
+{
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(b)) : "memory");
+}
+// true once the phase with this parity has completed; false after the limit
+// (non-blocking polls, with a short sleep once the wait is not immediate)
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity)
+{
+    const uint32_t a = smem_u32(b);
+    for (long long it = 0; it < GEMM_WAIT_LIMIT; it++) {
+        uint32_t done;
+        asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+        if (it >= 64) __nanosleep(32);
+    }
+    return false;
+}
+
+// K-major operand, 128-byte swizzle: 8-row atoms of 128-byte rows, atoms 1024
+// bytes apart (stride byte offset), leading byte offset unused (16 B).
+__device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N = BN, M = BM
+constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+// byte offset of 16-byte chunk c (0..7) of row r in a swizzled K-major tile
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi)
+{
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// 8 weights of one packed word -> 8 f16 f16((nib - 8) * s) in k order (16 bytes)
+__device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2)
+{
+    const uint32_t magic = 0x64006400u;   // f16 1024 + nib in both halves
+    uint32_t p0 = (w & 0x000F000Fu) | magic;           // k0, k4
+    uint32_t p1 = ((w >> 4) & 0x000F000Fu) | magic;    // k1, k5
+    uint32_t p2 = ((w >> 8) & 0x000F000Fu) | magic;    // k2, k6
+    uint32_t p3 = ((w >> 12) & 0x000F000Fu) | magic;   // k3, k7
+    const uint32_t bias = 0x64086408u;                 // 1032 = 1024 + 8
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p0) : "r"(bias));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p1) : "r"(bias));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p2) : "r"(bias));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p3) : "r"(bias));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p0) : "r"(s2));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p1) : "r"(s2));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p2) : "r"(s2));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p3) : "r"(s2));
+    return make_uint4(__byte_perm(p0, p1, 0x5410), __byte_perm(p2, p3, 0x5410), __byte_perm(p0, p1, 0x7632),
+                      __byte_perm(p2, p3, 0x7632));
+}
+
+template <bool XBF16>
+__global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* base = smem_raw + (((raw + 1023) & ~1023u) - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + NST * STAGE);
+    uint64_t* empty = full + NST;
+    uint64_t* done = empty + NST;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < NST; s++) { mbar_init(&full[s], PROD_WARPS); mbar_init(&empty[s], 1); }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == PROD_WARPS) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    tb_pdl_wait();
+    tb_pdl_trigger();
+
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, nk = a.K / BK;
+    if (warp < PROD_WARPS) {
+        // ---- producers: X rows (2 threads a row, 32 k each), W rows (1 thread a row)
+        const int xr = tid >> 1, xh = tid & 1;
+        const int wr = tid;
+        for (int i = 0; i < nk; i++) {
+            const int s = i % NST;
+            if (!mbar_wait(&empty[s], ((i / NST) & 1) ^ 1)) {
+                *abort_flag = 1;
+                atomicExch(a.err, ERR_GEMM_WAIT);
+            }
+            if (*abort_flag) break;
+            uint8_t* A = base + s * STAGE;
+            uint8_t* Bt = A + A_BYTES;
+            const int k0 = i * BK;
+            // X: 32 values of row m0 + xr starting at k0 + 32 xh -> chunks 4 xh .. 4 xh + 3
+            if (XBF16) {
+                const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) +
+                                                                  (size_t)(m0 + xr) * a.K + k0 + 32 * xh);
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const uint4 v = __ldg(src + c);
+                    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        o[j] = f32x2_to_f16x2(__uint_as_float(in[j] << 16), __uint_as_float(in[j] & 0xFFFF0000u));
+                    *reinterpret_cast<uint4*>(A + sw128(xr, 4 * xh + c)) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            } else {
+                const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) +
+                                                                    (size_t)(m0 + xr) * a.K + k0 + 32 * xh);
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const float4 u = __ldg(src + 2 * c), v = __ldg(src + 2 * c + 1);
+                    *reinterpret_cast<uint4*>(A + sw128(xr, 4 * xh + c)) =
+                        make_uint4(f32x2_to_f16x2(u.x, u.y), f32x2_to_f16x2(u.z, u.w), f32x2_to_f16x2(v.x, v.y),
+                                   f32x2_to_f16x2(v.z, v.w));
+                }
+            }
+            // W: row n0 + wr, words k0/8 .. k0/8 + 7, scales of groups k0/32, k0/32 + 1
+            {
+                const uint4* wp = reinterpret_cast<const uint4*>(a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8);
+                const uint4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+                const uint32_t sc = __ldg(reinterpret_cast<const uint32_t*>(a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32));
+                const uint32_t s0 = (sc & 0xFFFFu) * 0x10001u, s1 = (sc >> 16) * 0x10001u;
+                const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int c = 0; c < 8; c++)
+                    *reinterpret_cast<uint4*>(Bt + sw128(wr, c)) = dequant_word(ws[c], c < 4 ? s0 : s1);
+            }
+            // generic-proxy writes -> visible to the tensor core (async proxy)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[s]);
+        }
+    } else if (lane == 0) {
+        // ---- MMA issuer
+        for (int i = 0; i < nk; i++) {
+            const int s = i % NST;
+            if (!mbar_wait(&full[s], (i / NST) & 1)) {
+                *abort_flag = 1;
+                atomicExch(a.err, ERR_GEMM_WAIT);
+            }
+            if (*abort_flag) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t A = smem_u32(base + s * STAGE), Bt = A + A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; kk++) {
+                const uint64_t da = kmajor_sw128_desc(A + kk * 32), db = kmajor_sw128_desc(Bt + kk * 32);
+                const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
+                asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                             " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}"
+                             ::"r"(tmem), "l"(da), "l"(db), "r"(IDESC), "r"(accum), "r"(0u) : "memory");
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         ::"r"(smem_u32(&empty[s])) : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     ::"r"(smem_u32(done)) : "memory");
+    }
+
+    if (warp < PROD_WARPS) {
+        // ---- epilogue: this warp's 32 TMEM lanes (rows) x 128 columns
+        const bool ok = mbar_wait(done, 0) && !*abort_flag;
+        if (!ok) atomicExch(a.err, ERR_GEMM_WAIT);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok) {
+            const int q = warp & 3, h = warp >> 2;
+            const int row = m0 + 32 * q + lane;
+            float* yrow = a.y + (size_t)row * a.N + n0 + 128 * h;
+#pragma unroll 1
+            for (int j = 0; j < 4; j++) {
+                uint32_t r[32];
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(128 * h + 32 * j);
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+                             "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                               "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+                               "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+                               "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+                               "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                             : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float4* yp = reinterpret_cast<float4*>(yrow + 32 * j);
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    float4 v = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                                           __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
+                    if (a.acc) {
+                        const float4 o = yp[c];
+                        v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+                    }
+                    yp[c] = v;
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == PROD_WARPS) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+template <bool XBF16>
+int launch_gemm(tb_ctx* ctx, const GemmArgs& a)
+{
+    static bool attr_set[64] = {};
+    if (ctx->device >= 64 || !attr_set[ctx->device]) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_int4<XBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm attribute: %s", cudaGetErrorString(e));
+        if (ctx->device < 64) attr_set[ctx->device] = true;
+    }
+    cudaError_t e = tb_launch(ctx, k_gemm_int4<XBF16>, dim3(a.N / BN, a.M / BM), dim3(THREADS), (size_t)SMEM_BYTES, a);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+}  // namespace
+
+int tb_gemm_int4_impl(tb_ctx* ctx, float* y, const void* x, int x_bf16, const uint32_t* pack, const uint16_t* scales,
+                      int64_t M, int64_t N, int64_t K, int acc)
+{
+    TB_REQUIRE(ctx, y && x && pack && scales, "null pointer");
+    TB_REQUIRE(ctx, M > 0 && M % BM == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
+               "gemm_int4: M %% %d, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BM, BN, BK,
+               (long long)M, (long long)N, (long long)K);
+    TB_REQUIRE(ctx, M / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_int4: shape too large");
+    TB_REQUIRE(ctx, TB_ALIGNED(x, 16) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) && TB_ALIGNED(y, 16),
+               "gemm_int4: x, pack, y 16-byte and scales 4-byte aligned");
+    GemmArgs a{x, pack, scales, y, (int)M, (int)N, (int)K, acc ? 1 : 0, ctx->dev_error};
+    return x_bf16 ? launch_gemm<true>(ctx, a) : launch_gemm<false>(ctx, a);
+}
+
+extern "C" TB_API int tb_gemm_int4_g32(tb_ctx* ctx, float* y, const void* x, int x_bf16, const uint32_t* pack,
+                                       const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return tb_gemm_int4_impl(ctx, y, x, x_bf16, pack, scales, M, N, K, acc);
+}

@@ -77,18 +77,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(saddr(dst)), "l"(src), "r"(bytes), "r"(saddr(bar)) : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity)
 {
     uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+    asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
                  : "=r"(ok) : "r"(saddr(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
-// Bounded wait: gives up after WAIT_LIMIT polls (each try_wait may suspend briefly).
+// Bounded wait: gives up after WAIT_LIMIT non-blocking polls, sleeping briefly
+// between polls once the wait is not immediate (well under a second in all).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
 {
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++)
-        if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if (i >= 64) __nanosleep(32);
+    }
     return false;
 }
 

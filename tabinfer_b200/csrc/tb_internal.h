@@ -46,3 +46,7 @@ void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long*
 int tb_tp_allreduce_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, float* x, int xi, int nx);
 int tb_tp_argmax_merge_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, int rows, uint32_t* ids,
                             int32_t* pos);
+
+// prefill GEMM Y (+)= f16(X) . f16(deq(W))^T on tcgen05 (M % 128, N % 256, K % 64)
+int tb_gemm_int4_impl(tb_ctx* ctx, float* y, const void* x, int x_bf16, const uint32_t* pack, const uint16_t* scales,
+                      int64_t M, int64_t N, int64_t K, int acc);

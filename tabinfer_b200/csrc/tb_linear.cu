@@ -15,9 +15,14 @@ TB_API int tb_linear_int4(tb_ctx* ctx, float* y, const float* x, const uint32_t*
     TB_REQUIRE(ctx, T >= 1, "T must be >= 1");
     TB_REQUIRE(ctx, K > 0 && K % 32 == 0, "K must be a positive multiple of 32");
     if (T == 1 && N >= 16384) return tb_gemv_f32_impl(ctx, y, x, pack, scales, N, K, 1, acc);
-    if (T > 8)
-        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "linear_int4: T=%lld > 8 is the prefill GEMM (tb_gemm_int4_g32)",
+    if (T > 8) {
+        // prefill: the f16 tensor-core GEMM (gemmQ) where its tile shapes fit
+        if (T % 128 == 0 && N % 256 == 0 && K % 64 == 0)
+            return tb_gemm_int4_impl(ctx, y, x, 0, pack, scales, T, N, K, acc);
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED,
+                       "linear_int4: T=%lld > 8 needs T %% 128 == 0, N %% 256 == 0, K %% 64 == 0 (prefill GEMM)",
                        (long long)T);
+    }
     // quantQ8 / QUANTQ8T runs inside the GEMV prologue (bit-identical int8 rows)
     return tb_gemv_dp4a_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
 }

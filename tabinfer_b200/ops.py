@@ -226,6 +226,19 @@ def gate_up_silu_dp4a(x, gpack, gscales, upack, uscales, norm_w=None, eps=1e-6, 
     return swi
 
 
+def gemm_q(x, pack, scales, y=None, acc=False):
+    """Prefill GEMM on the tensor cores: y[M,N] (+)= f16(x) . f16(deq(W))^T
+    (gemmQ, qwen3.js:964-1026).  x [M,K] f32 or bf16."""
+    x2 = x.reshape(-1, x.shape[-1])
+    M, K = x2.shape
+    N = pack.shape[0]
+    y = y if y is not None else torch.zeros((M, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_gemm_int4_g32(c.h, _p(y), _p(x2), 1 if x2.dtype == torch.bfloat16 else 0, _p(pack), _p(scales),
+                                 M, N, K, 1 if acc else 0), "gemm_int4_g32")
+    return y
+
+
 def gemv_q_norm(x, norm_w, eps, pack, scales, y=None, acc=False):
     """rmsnorm + gemvQ (the final norm + lm_head of forward, qwen3.js:4037-4049) in one launch."""
     x2 = x.reshape(-1, x.shape[-1])

@@ -1,0 +1,100 @@
+"""Prefill GEMM on tcgen05 (tb_gemm_int4_g32) against the CPU restatement of the
+reference's f16 prefill GEMM (gemmQ, models/qwen3.js:964-1026).
+
+Tolerance: every token row of Y within 1e-3 relative of the f64 sum of the same
+f16 operands, max_n |y - ref| / max_n |ref|.  (The GEMV tests' per-element form,
+|err| / max(|ref|, 1e-3 rms), is not used here: a K = 2048..6144 dot product
+summed in f32 -- on the tensor core as in the reference's own f32 gemmQ -- is off
+by ~1e-6 of the rms, which that form magnifies 1000x on near-zero outputs.)
+The rms-relative error is also held to 1e-4 (measured ~1e-5 at K = 2048: the
+tensor core's f32 accumulation keeps slightly fewer low bits than a sequential
+f32 sum)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import tabinfer_b200 as tb
+from helpers import bf16_normal, host, u16_dev, u32_dev
+
+TOL = 1e-3
+
+
+def row_rel_err(got, ref):
+    """max over token rows of max|got - ref| / max|ref|"""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.max(np.abs(got - ref), axis=1) / np.max(np.abs(ref), axis=1)))
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(rng, N, K):
+    w = bf16_normal(rng, (N, K), 0.02)
+    pack, sc = oracle.quant_int4_g32(w)
+    return pack, sc
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 512), (128, 1024, 2048), (384, 256, 6144),
+                                   (256, 768, 1024)])
+def test_gemm_f32_activations(cuda, M, N, K):
+    rng = np.random.default_rng(M + N + K)
+    pack, sc = _weights(rng, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    y = host(tb.gemm_q(torch.from_numpy(x).cuda(), u32_dev(pack), u16_dev(sc)))
+    ref = oracle.gemm_int4_f16(x, pack, sc)
+    err = row_rel_err(y, ref)
+    assert err < TOL, err
+    # exact f16 products summed in f32: the error is accumulation rounding only
+    rms_err = float(np.max(np.abs(y - ref)) / np.sqrt(np.mean(ref ** 2)))
+    assert rms_err < 1e-4, rms_err
+
+
+def test_gemm_bf16_activations_and_acc(cuda):
+    """config 4's bf16 activations; acc adds into y (linearQ's fused residual)."""
+    M, N, K = 256, 512, 2048
+    rng = np.random.default_rng(4)
+    pack, sc = _weights(rng, N, K)
+    xb = bf16_normal(rng, (M, K), 1.0)
+    y0 = rng.standard_normal((M, N)).astype(np.float32)
+    y = torch.from_numpy(y0.copy()).cuda()
+    xt = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+    tb.gemm_q(xt, u32_dev(pack), u16_dev(sc), y=y, acc=True)
+    ref = oracle.gemm_int4_f16(xb, pack, sc) + y0
+    assert row_rel_err(host(y), ref) < TOL
+
+
+def test_gemm_config4_shape_sampled_rows(cuda):
+    """Config 4 at full size (M = 2048 tokens x gate 6144 x 2048): a seeded
+    sample of token rows against the oracle, plus additivity over acc."""
+    M, N, K = 2048, 6144, 2048
+    g = torch.Generator(device="cuda").manual_seed(7)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    pack, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    y = tb.gemm_q(x, pack, sc)
+    rows = np.sort(np.random.default_rng(3).choice(M, 16, replace=False))
+    xs = host(x[torch.from_numpy(rows).cuda()].view(torch.int16)).view(np.uint16)
+    ref = oracle.gemm_int4_f16(xs, host(pack).view(np.uint32), host(sc).view(np.uint16))
+    assert row_rel_err(host(y)[rows], ref) < TOL
+    y2 = y.clone()
+    tb.gemm_q(x, pack, sc, y=y2, acc=True)
+    np.testing.assert_allclose(host(y2), 2 * host(y), rtol=1e-6, atol=1e-6)
+
+
+def test_linear_router_prefill_goes_to_gemm(cuda):
+    """linearQ with T > 8 (prefill) routes to the f16 GEMM."""
+    M, N, K = 256, 512, 1024
+    rng = np.random.default_rng(9)
+    pack, sc = _weights(rng, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    y = host(tb.linear_q(torch.from_numpy(x).cuda(), u32_dev(pack), u16_dev(sc)))
+    assert row_rel_err(y, oracle.gemm_int4_f16(x, pack, sc)) < TOL
+
+
+def test_gemm_rejects_untiled_shapes(cuda):
+    rng = np.random.default_rng(1)
+    pack, sc = _weights(rng, 256, 128)
+    x = torch.zeros(100, 128, device="cuda")
+    with pytest.raises(tb.TabInferError):
+        tb.gemm_q(x, u32_dev(pack), u16_dev(sc))
