@@ -475,6 +475,27 @@ def profile_attn(S):
     print("profile attn done", flush=True)
 
 
+def profile_gemm(M, N, K):
+    """Three cold-L2 launches of the tcgen05 prefill GEMM (bf16 activations) at
+    M x N x K (config 4: M in {512, 2048, 8192}), for an ncu capture of one."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    pack, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.empty(M, N, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for it in range(3):
+        flush.fill_(it)
+        tb.gemm_q(x, pack, sc, y=y)
+    torch.cuda.synchronize()
+    err = tb.default_context(0).device_error()
+    assert err == 0, err
+    print("profile gemm done", flush=True)
+
+
 # ---------------------------------------------------------------------------
 # CPU path (the reference's int4 linearQ math, C transcription)
 # ---------------------------------------------------------------------------
@@ -573,7 +594,12 @@ def main():
                     help="one cold-L2 launch per kernel kind (for ncu), then exit")
     ap.add_argument("--profile-attn", type=int, default=0, metavar="S",
                     help="three cold-L2 decode-attention launches at context S (for ncu), then exit")
+    ap.add_argument("--profile-gemm", type=int, nargs=3, default=None, metavar=("M", "N", "K"),
+                    help="three cold-L2 prefill-GEMM launches at M x N x K (for ncu), then exit")
     args = ap.parse_args()
+    if args.profile_gemm:
+        profile_gemm(*args.profile_gemm)
+        return
     if args.profile_case:
         profile_case()
         return

@@ -6,26 +6,37 @@
 // dequantized as f16((nib - 8) * f16 scale) (one rounding of the exact product),
 // and the products are summed in f32.
 //
-// CTA tile 128 (M) x 256 (N), K in steps of 64.  Warps 0-7 are producers: per
-// stage they read a 128 x 64 block of X (f32 or bf16) and the 256 x 64 block of
-// packed int4 weights with its f16 scales, convert both to f16 and write them
-// into shared memory in the 128-byte-swizzled K-major layout the tensor core
-// reads (8-row x 128-byte atoms).  Warp 8 allocates 256 TMEM columns and one of
-// its threads issues four 128x256x16 MMAs per stage; tcgen05.commit frees the
-// stage when they complete.  After the last stage warps 0-7 read the
-// accumulator (tcgen05.ld, warp w owns TMEM lanes 32*(w%4)..+31 and column half
-// w/4) and store f32 rows.  Waits are bounded: on a timeout the CTA records
+// CTA tile 128 (M) x 256 (N), K in steps of 64.  Warps 0-15 are producers: each
+// thread cp.asyncs its share of the raw 128 x 64 block of X (f32 or bf16) and of
+// the 256 x 64 block of packed int4 weights + f16 scales a few k-steps ahead,
+// then converts its share to f16 and writes it into shared memory in the
+// 128-byte-swizzled K-major layout the tensor core reads (8-row x 128-byte
+// atoms).  Warp 16 allocates 256 TMEM columns and one of its threads issues four
+// 128x256x16 MMAs per stage; tcgen05.commit frees the stage when they complete.
+// After the last stage warps 0-15 read the accumulator (tcgen05.ld, warp w owns
+// TMEM lanes 32*(w%4)..+31 and columns 64*(w/4)..+63) and store f32 rows.  Waits are bounded: on a timeout the CTA records
 // ERR_GEMM_WAIT, stops issuing, and still frees its TMEM.
 #include "tb_internal.h"
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, NST = 4;
-constexpr int PROD_WARPS = 8, THREADS = (PROD_WARPS + 1) * 32;
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int PROD_WARPS = 16, PROD = PROD_WARPS * 32, THREADS = PROD + 32;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = 1024 + NST * STAGE + 256;
+// raw staging ring, filled with cp.async NR-1 k-steps ahead of the conversion:
+// X as given (bf16 or f32), packed W, W scales; chunk-major (16-byte chunk c of
+// producer thread t at c * PROD + t) so copies and reads are bank-conflict free
+constexpr int RAW_W = PROD * 16, RAW_S = PROD * 4;
+template <bool XBF16> struct Cfg {
+    static constexpr int XC = XBF16 ? 2 : 4;                 // raw X chunks per producer thread
+    static constexpr int X = PROD * XC * 16;
+    static constexpr int RSTAGE = X + RAW_W + RAW_S;
+    static constexpr int NST = XBF16 ? 3 : 2;                // MMA operand stages
+    static constexpr int NR = 3;                             // raw stages
+    static constexpr int SMEM = 1024 + NST * STAGE + NR * RSTAGE + 256;
+};
 constexpr int TMEM_COLS = 256;
-constexpr long long GEMM_WAIT_LIMIT = 1LL << 22;   // polls; with the back-off below, well under a second
+constexpr int GEMM_WAIT_TRIES = 1000;      // x a 1 ms suspend bound per try: at most ~1 s
 constexpr int ERR_GEMM_WAIT = 0x6b01;
 
 struct GemmArgs {
@@ -47,17 +58,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b)
 {
     asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(b)) : "memory");
 }
-// true once the phase with this parity has completed; false after the limit
-// (non-blocking polls, with a short sleep once the wait is not immediate)
+// true once the phase with this parity has completed; false after the limit.
+// try_wait suspends the thread until the phase completes (woken at once) or the
+// 1 ms hint runs out, so the loop is bounded in time.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity)
 {
     const uint32_t a = smem_u32(b);
-    for (long long it = 0; it < GEMM_WAIT_LIMIT; it++) {
+    for (int it = 0; it < GEMM_WAIT_TRIES; it++) {
         uint32_t done;
-        asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                     " selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(done) : "r"(a), "r"(parity), "r"(1000000u) : "memory");
         if (done) return true;
-        if (it >= 64) __nanosleep(32);
     }
     return false;
 }
@@ -81,6 +93,18 @@ __device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi)
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
 }
+
+__device__ __forceinline__ void cp16(void* sdst, const void* gsrc)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp4(void* sdst, const void* gsrc)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // 8 weights of one packed word -> 8 f16 f16((nib - 8) * s) in k order (16 bytes)
 __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2)
@@ -106,10 +130,13 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2)
 template <bool XBF16>
 __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
 {
+    using R = Cfg<XBF16>;
+    constexpr int NST = R::NST;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* base = smem_raw + (((raw + 1023) & ~1023u) - raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + NST * STAGE);
+    uint8_t* rawbase = base + NST * STAGE;
+    uint64_t* full = reinterpret_cast<uint64_t*>(rawbase + R::NR * R::RSTAGE);
     uint64_t* empty = full + NST;
     uint64_t* done = empty + NST;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(done + 1);
@@ -136,10 +163,29 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
 
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, nk = a.K / BK;
     if (warp < PROD_WARPS) {
-        // ---- producers: X rows (2 threads a row, 32 k each), W rows (1 thread a row)
-        const int xr = tid >> 1, xh = tid & 1;
-        const int wr = tid;
+        // ---- producers: X rows (4 threads a row, 16 k each), W rows (2 threads a
+        // row, one 32-group each).  Each thread copies its own raw bytes
+        // (cp.async, NR-1 k-steps ahead) and converts only those, so no barrier
+        // is needed between copy and convert.
+        const int xr = tid >> 2, xq = tid & 3;
+        const int wr = tid >> 1, wh = tid & 1;
+        auto fetch = [&](int i) {
+            if (i < nk) {
+                uint8_t* rs = rawbase + (i % R::NR) * R::RSTAGE;
+                const int k0 = i * BK;
+                const uint8_t* xs = static_cast<const uint8_t*>(a.x) +
+                                    ((size_t)(m0 + xr) * a.K + k0 + 16 * xq) * (XBF16 ? 2 : 4);
+#pragma unroll
+                for (int c = 0; c < R::XC; c++) cp16(rs + (c * PROD + tid) * 16, xs + 16 * c);
+                cp16(rs + R::X + tid * 16, a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8 + 4 * wh);
+                cp4(rs + R::X + RAW_W + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32);
+            }
+            cp_commit();   // a group per k-step, empty past the end, keeps the count uniform
+        };
+        for (int i = 0; i < R::NR - 1; i++) fetch(i);
         for (int i = 0; i < nk; i++) {
+            fetch(i + R::NR - 1);
+            cp_wait<R::NR - 1>();        // this thread's raw bytes of k-step i have landed
             const int s = i % NST;
             if (!mbar_wait(&empty[s], ((i / NST) & 1) ^ 1)) {
                 *abort_flag = 1;
@@ -148,48 +194,44 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
             if (*abort_flag) break;
             uint8_t* A = base + s * STAGE;
             uint8_t* Bt = A + A_BYTES;
-            const int k0 = i * BK;
-            // X: 32 values of row m0 + xr starting at k0 + 32 xh -> chunks 4 xh .. 4 xh + 3
+            const uint8_t* rs = rawbase + (i % R::NR) * R::RSTAGE;
+            // X: 16 values of row xr -> f16 chunks 2 xq, 2 xq + 1
             if (XBF16) {
-                const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) +
-                                                                  (size_t)(m0 + xr) * a.K + k0 + 32 * xh);
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const uint4 v = __ldg(src + c);
+                for (int c = 0; c < 2; c++) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(rs + (c * PROD + tid) * 16);
                     const uint32_t in[4] = {v.x, v.y, v.z, v.w};
                     uint32_t o[4];
 #pragma unroll
                     for (int j = 0; j < 4; j++)
                         o[j] = f32x2_to_f16x2(__uint_as_float(in[j] << 16), __uint_as_float(in[j] & 0xFFFF0000u));
-                    *reinterpret_cast<uint4*>(A + sw128(xr, 4 * xh + c)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq + c)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
             } else {
-                const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) +
-                                                                    (size_t)(m0 + xr) * a.K + k0 + 32 * xh);
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const float4 u = __ldg(src + 2 * c), v = __ldg(src + 2 * c + 1);
-                    *reinterpret_cast<uint4*>(A + sw128(xr, 4 * xh + c)) =
+                for (int c = 0; c < 2; c++) {
+                    const float4 u = *reinterpret_cast<const float4*>(rs + ((2 * c) * PROD + tid) * 16);
+                    const float4 v = *reinterpret_cast<const float4*>(rs + ((2 * c + 1) * PROD + tid) * 16);
+                    *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq + c)) =
                         make_uint4(f32x2_to_f16x2(u.x, u.y), f32x2_to_f16x2(u.z, u.w), f32x2_to_f16x2(v.x, v.y),
                                    f32x2_to_f16x2(v.z, v.w));
                 }
             }
-            // W: row n0 + wr, words k0/8 .. k0/8 + 7, scales of groups k0/32, k0/32 + 1
+            // W: 32 weights (4 words) of row wr, group wh of the k-step
             {
-                const uint4* wp = reinterpret_cast<const uint4*>(a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8);
-                const uint4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
-                const uint32_t sc = __ldg(reinterpret_cast<const uint32_t*>(a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32));
-                const uint32_t s0 = (sc & 0xFFFFu) * 0x10001u, s1 = (sc >> 16) * 0x10001u;
-                const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const uint4 w4 = *reinterpret_cast<const uint4*>(rs + R::X + tid * 16);
+                const uint32_t sc = *reinterpret_cast<const uint32_t*>(rs + R::X + RAW_W + tid * 4);
+                const uint32_t s2 = (wh ? (sc >> 16) : (sc & 0xFFFFu)) * 0x10001u;
+                const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                for (int c = 0; c < 8; c++)
-                    *reinterpret_cast<uint4*>(Bt + sw128(wr, c)) = dequant_word(ws[c], c < 4 ? s0 : s1);
+                for (int c = 0; c < 4; c++) *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_word(ws[c], s2);
             }
             // generic-proxy writes -> visible to the tensor core (async proxy)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&full[s]);
         }
+        cp_wait<0>();   // no copy in flight when the CTA leaves
     } else if (lane == 0) {
         // ---- MMA issuer
         for (int i = 0; i < nk; i++) {
@@ -222,13 +264,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
         if (!ok) atomicExch(a.err, ERR_GEMM_WAIT);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok) {
-            const int q = warp & 3, h = warp >> 2;
+            const int q = warp & 3, h = warp >> 2;      // TMEM lanes 32q.., columns 64h..
             const int row = m0 + 32 * q + lane;
-            float* yrow = a.y + (size_t)row * a.N + n0 + 128 * h;
+            float* yrow = a.y + (size_t)row * a.N + n0 + 64 * h;
 #pragma unroll 1
-            for (int j = 0; j < 4; j++) {
+            for (int j = 0; j < 2; j++) {
                 uint32_t r[32];
-                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(128 * h + 32 * j);
+                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(64 * h + 32 * j);
                 asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
                              "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
                              : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
@@ -265,11 +307,14 @@ int launch_gemm(tb_ctx* ctx, const GemmArgs& a)
 {
     static bool attr_set[64] = {};
     if (ctx->device >= 64 || !attr_set[ctx->device]) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_int4<XBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_int4<XBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg<XBF16>::SMEM);
         if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm attribute: %s", cudaGetErrorString(e));
         if (ctx->device < 64) attr_set[ctx->device] = true;
     }
-    cudaError_t e = tb_launch(ctx, k_gemm_int4<XBF16>, dim3(a.N / BN, a.M / BM), dim3(THREADS), (size_t)SMEM_BYTES, a);
+    static_assert(Cfg<XBF16>::SMEM <= 227 * 1024, "shared memory");
+    cudaError_t e = tb_launch(ctx, k_gemm_int4<XBF16>, dim3(a.N / BN, a.M / BM), dim3(THREADS),
+                              (size_t)Cfg<XBF16>::SMEM, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }

@@ -30,7 +30,7 @@ namespace {
 constexpr int THREADS = 256;
 constexpr int MAX_NST = 4;
 constexpr int SMEM_HDR = 512;   // mbarriers (64 B) + reduction scratch (>= 72 floats)
-constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr uint32_t WAIT_TRIES = 1000;
 constexpr int ERR_WAIT_TIMEOUT = 0x6d01;
 
 enum Kind { KIND_Q8 = 0, KIND_GATEUP = 1, KIND_F32 = 2 };
@@ -77,20 +77,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(saddr(dst)), "l"(src), "r"(bytes), "r"(saddr(bar)) : "memory");
 }
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(ok) : "r"(saddr(bar)), "r"(parity) : "memory");
-    return ok != 0;
-}
-// Bounded wait: gives up after WAIT_LIMIT non-blocking polls, sleeping briefly
-// between polls once the wait is not immediate (well under a second in all).
+// Bounded wait: try_wait suspends until the phase completes (woken at once) or
+// its 1 ms hint runs out; WAIT_TRIES tries bound the whole wait to ~1 s.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
 {
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
-        if (mbar_test_wait(bar, parity)) return true;
-        if (i >= 64) __nanosleep(32);
+    for (uint32_t i = 0; i < WAIT_TRIES; i++) {
+        uint32_t ok;
+        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                     " selp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(ok) : "r"(saddr(bar)), "r"(parity), "r"(1000000u) : "memory");
+        if (ok) return true;
     }
     return false;
 }

@@ -23,7 +23,7 @@
 namespace {
 
 constexpr int TP_MAX = 8;
-constexpr long long TP_WAIT_LIMIT = 1LL << 22;    // x 64+ ns sleeps: a fraction of a second to seconds
+constexpr long long TP_WAIT_LIMIT = 1LL << 22;    // polls (sleeping 64+ ns after the first 4096): ~1 s
 constexpr int ERR_TP_WAIT = 0x7a01;
 
 struct TpArgs {
@@ -66,7 +66,7 @@ __device__ __forceinline__ void tp_signal_wait(unsigned* const* peer_flag, const
                 atomicExch(err, ERR_TP_WAIT);
                 break;
             }
-            __nanosleep(64);
+            if (it > 4096) __nanosleep(64);   // a healthy peer answers within the first polls
         }
     }
     __syncthreads();
