@@ -275,6 +275,29 @@ TB_API int tb_embed_gather(tb_ctx *ctx, const uint32_t *ids, int64_t idoff,
 TB_API int tb_gemm_int4_g32(tb_ctx *ctx, float *y, const void *x, int x_bf16, const uint32_t *pack,
                             const uint16_t *scales, int64_t M, int64_t N, int64_t K, int acc);
 
+/* ---- int3 mixture of experts (LFM2.5, models/lfm25.js) ---------------------
+ * int3 layout as the reference: per (row, 32-group) three u32 bitplanes of the
+ * stored value q3 + 4 (bit i of plane p = bit p of weight i) and an f16 scale;
+ * expert e's rows are e*N .. e*N+N-1. */
+/* _requant43 (lfm25.js:833-855): int4 G32 pack/scales -> p3 u32 [rows][K/32][3],
+ * s3 f16 [rows][K/32]; bit-exact with the reference (JS doubles, the engine's
+ * f32ToF16). */
+TB_API int tb_requant_int4_int3(tb_ctx *ctx, uint32_t *p3, uint16_t *s3, const uint32_t *pack4,
+                                const uint16_t *s4, int64_t rows, int64_t K);
+/* ROUTER_WGSL (lfm25.js:111-141): idx u32 [T][K], wt f32 [T][K] from logits
+ * f32 [T][nE] and expert_bias f32 [nE] (nE <= 64). */
+TB_API int tb_moe_router(tb_ctx *ctx, uint32_t *idx, float *wt, const float *logits, const float *bias,
+                         int64_t T, int64_t nE, int64_t K);
+/* The MoE FFN of T tokens (idxGemv3 w1, w3, SiLU, idxGemv3 w2, MOECOMBINE):
+ * x_out[t] += sum_k wt[t,k] * W2_e(silu(W1_e x_in[t]) * W3_e x_in[t]), e = idx[t,k].
+ * w1/w3 planes [nE*I][H/32][3] + scales, w2 [nE*H][I/32][3] + scales.  The
+ * (token, expert) pairs are grouped by expert so each expert's weights are
+ * decoded once per chunk of its pairs.  Context-owned scratch. */
+TB_API int tb_moe_ffn_int3(tb_ctx *ctx, float *x_out, const float *x_in, const uint32_t *idx, const float *wt,
+                           const uint32_t *w1p, const uint16_t *w1s, const uint32_t *w3p, const uint16_t *w3s,
+                           const uint32_t *w2p, const uint16_t *w2s, int64_t T, int64_t K, int64_t nE,
+                           int64_t H, int64_t I);
+
 /* bf16 -> f16 bits, rounded half-up as the loader's bf16ToF16bits
  * (models/qwen3.js:3357-3390): the f16 copies of the embedding table and the
  * norm weights. */

@@ -304,3 +304,44 @@ def dec_nsplit(S):
 def argmax(x):
     x = np.ascontiguousarray(x, np.float32)
     return int(lib().tbo_argmax(_ptr(x), _I(x.size)))
+
+
+# --------------------------------------------------------------------------
+# int3 MoE (lfm25.js)
+# --------------------------------------------------------------------------
+
+def requant43(pack4, s4):
+    """_requant43: int4 pack [rows][K/8] + f16 scales -> int3 planes [rows][K/32][3], f16 scales."""
+    pack4 = np.ascontiguousarray(pack4, np.uint32)
+    rows, K = pack4.shape[0], pack4.shape[1] * 8
+    p3 = np.zeros((rows, K // 32, 3), np.uint32)
+    s3 = np.zeros((rows, K // 32), np.uint16)
+    lib().tbo_requant43(_ptr(pack4), _ptr(np.ascontiguousarray(s4, np.uint16)), _I(rows), _I(K), _ptr(p3), _ptr(s3))
+    return p3, s3
+
+
+def engine_f32_to_f16(v):
+    lib().tbo_engine_f32_to_f16.restype = ctypes.c_uint16
+    return lib().tbo_engine_f32_to_f16(ctypes.c_float(v))
+
+
+def moe_router(logits, bias, K):
+    logits = np.ascontiguousarray(logits, np.float32)
+    T, nE = logits.shape
+    idx = np.zeros((T, K), np.uint32)
+    wt = np.zeros((T, K), np.float32)
+    lib().tbo_moe_router(_ptr(logits), _ptr(np.ascontiguousarray(bias, np.float32)), _I(T), _I(nE), _I(K),
+                         _ptr(idx), _ptr(wt))
+    return idx, wt
+
+
+def moe_ffn_int3(a, idx, wt, w1, w3, w2, H, I):
+    """sum_k wt * W2_e(silu(W1_e a) * W3_e a) per token (f64); w* = (planes, scales)."""
+    a = np.ascontiguousarray(a, np.float32)
+    T = a.shape[0]
+    K = idx.shape[1]
+    out = np.zeros((T, H), np.float64)
+    lib().tbo_moe_ffn_int3(_ptr(a), _ptr(np.ascontiguousarray(idx, np.uint32)), _ptr(np.ascontiguousarray(wt, np.float32)),
+                           _ptr(w1[0]), _ptr(w1[1]), _ptr(w3[0]), _ptr(w3[1]), _ptr(w2[0]), _ptr(w2[1]),
+                           _I(T), _I(K), _I(H), _I(I), _ptr(out))
+    return out

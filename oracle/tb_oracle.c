@@ -533,3 +533,140 @@ TBO_API int64_t tbo_argmax(const float *x, int64_t n)
     for (int64_t i = 0; i < n; i++) if (x[i] > bv) { bv = x[i]; bi = i; }
     return bi;
 }
+
+
+/* ------------------------------------------------------------------------ */
+/* int3 MoE of LFM2.5 (models/lfm25.js)                                       */
+/* ------------------------------------------------------------------------ */
+
+/* engine/webgpu-engine.js:217-236 f32ToF16: half-up on mantissa bit 12, the
+ * rounded mantissa ORed into the exponent field (a carry survives only when the
+ * exponent's low bit is clear). */
+TBO_API uint16_t tbo_engine_f32_to_f16(float v)
+{
+    uint32_t x;
+    memcpy(&x, &v, 4);
+    uint32_t sign = (x >> 16) & 0x8000u, mant = x & 0x007fffffu;
+    int ex = (int)((x >> 23) & 0xffu);
+    if (ex == 255) return (uint16_t)(sign | (mant ? 0x7e00u : 0x7c00u));
+    int e = ex - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        mant = (mant | 0x00800000u) >> (1 - e);
+        return (uint16_t)(sign | ((mant + 0x00001000u) >> 13));
+    }
+    return (uint16_t)(sign | ((uint32_t)e << 10) | ((mant + 0x00001000u) >> 13));
+}
+
+/* _requant43, lfm25.js:833-855: int4 group (nibble q+8) -> int3 bitplanes of
+ * stored value q3+4 with q3 = clamp(Math.round(q4 * (4/m)), -4, 3), m = max|q4|;
+ * scale = f32(f16(s4) * m / 4) through the engine's f32ToF16; m = 0 -> scale 0
+ * and planes {0, 0, ~0}.  JS doubles. */
+TBO_API void tbo_requant43(const uint32_t *pack4, const uint16_t *s4, int64_t rows, int64_t K, uint32_t *p3,
+                           uint16_t *s3)
+{
+    const int64_t ng = rows * (K / 32);
+    for (int64_t gi = 0; gi < ng; gi++) {
+        int q4[32], m = 0;
+        for (int i = 0; i < 32; i++) {
+            q4[i] = (int)((pack4[gi * 4 + (i >> 3)] >> (4 * (i & 7))) & 15u) - 8;
+            int a = q4[i] < 0 ? -q4[i] : q4[i];
+            if (a > m) m = a;
+        }
+        if (m == 0) {
+            p3[gi * 3] = 0; p3[gi * 3 + 1] = 0; p3[gi * 3 + 2] = 0xFFFFFFFFu;
+            s3[gi] = tbo_engine_f32_to_f16(0.0f);
+            continue;
+        }
+        const double ratio = 4.0 / (double)m;
+        const float s3f = (float)(tbo_f16_to_f64(s4[gi]) * (double)m / 4.0);
+        uint32_t b0 = 0, b1 = 0, b2 = 0;
+        for (int i = 0; i < 32; i++) {
+            double v = (double)q4[i] * ratio;
+            double f = floor(v);
+            int q = (int)((v - f) >= 0.5 ? f + 1.0 : f);   /* Math.round: ties toward +inf */
+            if (q > 3) q = 3; else if (q < -4) q = -4;
+            uint32_t st = (uint32_t)(q + 4);
+            b0 |= (st & 1u) << i;
+            b1 |= ((st >> 1) & 1u) << i;
+            b2 |= ((st >> 2) & 1u) << i;
+        }
+        p3[gi * 3] = b0; p3[gi * 3 + 1] = b1; p3[gi * 3 + 2] = b2;
+        s3[gi] = tbo_engine_f32_to_f16(s3f);
+    }
+}
+
+/* ROUTER_WGSL, lfm25.js:111-141: sigmoid scores, K first-maximum passes over
+ * score + bias (strict >: lower expert on ties), weights score / (sum + 1e-6).
+ * f32 arithmetic as the shader (exp in double, rounded to f32). */
+TBO_API void tbo_moe_router(const float *logits, const float *bias, int64_t T, int64_t nE, int64_t K, uint32_t *idx,
+                            float *wt)
+{
+    for (int64_t t = 0; t < T; t++) {
+        float sc[256], sel[256];
+        for (int64_t e = 0; e < nE; e++) {
+            float ex = (float)exp(-(double)logits[t * nE + e]);
+            sc[e] = 1.0f / (1.0f + ex);
+            sel[e] = sc[e] + bias[e];
+        }
+        float sum = 0.0f;
+        for (int64_t k = 0; k < K; k++) {
+            int64_t best = 0;
+            float bv = -1.0e30f;
+            for (int64_t j = 0; j < nE; j++)
+                if (sel[j] > bv) { bv = sel[j]; best = j; }
+            sel[best] = -2.0e30f;
+            idx[t * K + k] = (uint32_t)best;
+            wt[t * K + k] = sc[best];
+            sum += sc[best];
+        }
+        for (int64_t k = 0; k < K; k++) wt[t * K + k] = wt[t * K + k] / (sum + 1e-6f);
+    }
+}
+
+/* idxGemv3 (lfm25.js:1924-1973) for one pair: y[n] = sum_g s[row,g] * sum_i (q_i - 4) x[32g+i],
+ * row = e*N + n; f64. */
+static void moe_gemv3_row(const uint32_t *p3, const uint16_t *s3, int64_t e, int64_t N, int64_t Kc, const double *x,
+                          double *y)
+{
+    const int64_t G = Kc / 32;
+    for (int64_t n = 0; n < N; n++) {
+        const int64_t row = e * N + n;
+        double acc = 0.0;
+        for (int64_t g = 0; g < G; g++) {
+            const uint32_t *w = p3 + (row * G + g) * 3;
+            double sum = 0.0;
+            for (int i = 0; i < 32; i++) {
+                int st = (int)(((w[0] >> i) & 1u) | (((w[1] >> i) & 1u) << 1) | (((w[2] >> i) & 1u) << 2));
+                sum += (double)(st - 4) * x[g * 32 + i];
+            }
+            acc += tbo_f16_to_f64(s3[row * G + g]) * sum;
+        }
+        y[n] = acc;
+    }
+}
+
+/* MoE FFN (w1/w3 gate+up with SiLU, w2 down, MOECOMBINE lfm25.js:1982-2000):
+ * x_out[t] = x_in_res[t] + sum_k wt[t,k] * W2_e(silu(W1_e a_t) * W3_e a_t). */
+TBO_API void tbo_moe_ffn_int3(const float *a, const uint32_t *idx, const float *wt, const uint32_t *w1p,
+                              const uint16_t *w1s, const uint32_t *w3p, const uint16_t *w3s, const uint32_t *w2p,
+                              const uint16_t *w2s, int64_t T, int64_t K, int64_t H, int64_t I, double *out)
+{
+    double *xa = (double *)malloc(sizeof(double) * (size_t)H);
+    double *g = (double *)malloc(sizeof(double) * (size_t)I);
+    double *u = (double *)malloc(sizeof(double) * (size_t)I);
+    double *o = (double *)malloc(sizeof(double) * (size_t)H);
+    for (int64_t t = 0; t < T; t++) {
+        for (int64_t h = 0; h < H; h++) { xa[h] = a[t * H + h]; out[t * H + h] = 0.0; }
+        for (int64_t k = 0; k < K; k++) {
+            const int64_t e = idx[t * K + k];
+            moe_gemv3_row(w1p, w1s, e, I, H, xa, g);
+            moe_gemv3_row(w3p, w3s, e, I, H, xa, u);
+            for (int64_t i = 0; i < I; i++) g[i] = g[i] / (1.0 + exp(-g[i])) * u[i];
+            moe_gemv3_row(w2p, w2s, e, H, I, g, o);
+            for (int64_t h = 0; h < H; h++) out[t * H + h] += (double)wt[t * K + k] * o[h];
+        }
+    }
+    free(xa); free(g); free(u); free(o);
+}

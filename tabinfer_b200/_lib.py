@@ -59,6 +59,9 @@ SIGNATURES = {
     "tb_attn_decode_q8_batch": [P, P, P, P, P, P, P, I64, I64, P, I64, I64, I64, I64, I32],
     "tb_convert_bf16_f16": [P, P, P, I64],
     "tb_gemm_int4_g32": [P, P, P, I32, P, P, I64, I64, I64, I32],
+    "tb_requant_int4_int3": [P, P, P, P, P, I64, I64],
+    "tb_moe_router": [P, P, P, P, P, I64, I64, I64],
+    "tb_moe_ffn_int3": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64],
     "tb_qwen3_shard": [P, I32, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)],
     "tb_qwen3_create": [P, P, ctypes.POINTER(P)],
     "tb_qwen3_destroy": [P],

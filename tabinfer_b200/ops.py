@@ -239,6 +239,35 @@ def gemm_q(x, pack, scales, y=None, acc=False):
     return y
 
 
+def requant_int3(pack4, scales4):
+    """_requant43 (lfm25.js:833-855): int4 G32 -> int3 bitplanes [rows][K/32][3] + f16 scales."""
+    rows, K = pack4.shape[0], pack4.shape[1] * 8
+    p3 = torch.empty((rows, K // 32, 3), dtype=torch.int32, device=pack4.device)
+    s3 = torch.empty((rows, K // 32), dtype=torch.int16, device=pack4.device)
+    c = _ctx(pack4)
+    c.check(LIB.tb_requant_int4_int3(c.h, _p(p3), _p(s3), _p(pack4), _p(scales4), rows, K), "requant_int4_int3")
+    return p3, s3
+
+
+def moe_router(logits, bias, K):
+    """ROUTER_WGSL (lfm25.js:111-141) -> (idx [T,K] int32, wt [T,K] f32)."""
+    T, nE = logits.shape
+    idx = torch.empty((T, K), dtype=torch.int32, device=logits.device)
+    wt = torch.empty((T, K), dtype=torch.float32, device=logits.device)
+    c = _ctx(logits)
+    c.check(LIB.tb_moe_router(c.h, _p(idx), _p(wt), _p(logits), _p(bias), T, nE, K), "moe_router")
+    return idx, wt
+
+
+def moe_ffn_int3(x_out, x_in, idx, wt, w1, w3, w2, n_experts, hidden, inter):
+    """x_out += sum_k wt * W2_e(silu(W1_e x_in) * W3_e x_in); w* = (planes, scales)."""
+    T, K = idx.shape
+    c = _ctx(x_in)
+    c.check(LIB.tb_moe_ffn_int3(c.h, _p(x_out), _p(x_in), _p(idx), _p(wt), _p(w1[0]), _p(w1[1]), _p(w3[0]),
+                                _p(w3[1]), _p(w2[0]), _p(w2[1]), T, K, n_experts, hidden, inter), "moe_ffn_int3")
+    return x_out
+
+
 def gemv_q_norm(x, norm_w, eps, pack, scales, y=None, acc=False):
     """rmsnorm + gemvQ (the final norm + lm_head of forward, qwen3.js:4037-4049) in one launch."""
     x2 = x.reshape(-1, x.shape[-1])
