@@ -400,6 +400,99 @@ def chain_gbs(dev, ctx, B, steps):
 
 
 # ---------------------------------------------------------------------------
+# prefill GEMM and int3 MoE beside the decode step
+# ---------------------------------------------------------------------------
+
+def _cold_time(fn, flush, stream, reps=5):
+    """median CUDA-event time (ms) of fn() after an L2-evicting write"""
+    import torch
+    fn()
+    ts = []
+    for r in range(reps + 1):
+        flush.fill_(r & 0xff)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        e1.synchronize()
+        if r:
+            ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def prefill_extra(dev, peak_tf, stream):
+    """The seven Qwen3-1.7B layer matrices as prefill GEMMs (tcgen05, f16 math of
+    gemmQ) on M = 512 / 2048 / 8192 bf16 activation rows: TFLOP/s of 2*M*N*K."""
+    import torch
+    import tabinfer_b200 as tb
+    g = torch.Generator(device=dev).manual_seed(5)
+    H, I = Q17["hidden"], Q17["intermediate"]
+    shapes = [(2048, H), (1024, H), (1024, H), (H, 2048), (I, H), (I, H), (H, I)]
+    mats = []
+    for N, K in shapes:
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        mats.append(tb.quantize_int4_bf16(w.view(torch.int16)))
+        del w
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    for M in (512, 2048, 8192):
+        ms = 0.0
+        flop = 0
+        for (N, K), (pk, sc) in zip(shapes, mats):
+            x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty(M, N, device=dev)
+            ms += _cold_time(lambda: tb.gemm_q(x, pk, sc, y=y), flush, stream)
+            flop += 2 * M * N * K
+        tf = flop / (ms * 1e-3) / 1e12
+        out["M%d" % M] = {"us_7_matrices": round(ms * 1e3, 1), "tflops": round(tf, 1),
+                          "frac_of_bf16_peak": round(tf / peak_tf, 4)}
+    del flush
+    torch.cuda.synchronize(dev)
+    return out
+
+
+def moe_extra(dev, peak_gbs, stream):
+    """One LFM2.5-8B-A1B-shaped int3 MoE FFN (hidden 2048, 32 experts, I 1792,
+    top-4, group-32 int3 as the reference's _requant43) over 1 / 8 / 64 tokens:
+    router + grouped expert GEMVs + combine.  Algorithmic bytes = the int3 planes
+    and scales of every expert routed to + activations."""
+    import torch
+    import tabinfer_b200 as tb
+    H, I, NE, K = 2048, 1792, 32, 4
+    g = torch.Generator(device=dev).manual_seed(11)
+    ws = []
+    for rows, cols in ((NE * I, H), (NE * I, H), (NE * H, I)):
+        w = (torch.randn(rows, cols, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        pk, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+        del w
+        ws.append(tb.requant_int3(pk, sc))
+        del pk, sc
+    per_expert = (2 * I * H + H * I) * 14 // 32
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    for T in (1, 8, 64):
+        logits = torch.randn(T, NE, device=dev, generator=g)
+        bias = torch.zeros(NE, device=dev)
+        a = torch.randn(T, H, device=dev, generator=g)
+        x = torch.zeros(T, H, device=dev)
+
+        def step():
+            idx, wt = tb.moe_router(logits, bias, K)
+            tb.moe_ffn_int3(x, a, idx, wt, ws[0], ws[1], ws[2], NE, H, I)
+        step()
+        idx, _ = tb.moe_router(logits, bias, K)
+        used = len(set(idx.flatten().tolist()))
+        ms = _cold_time(step, flush, stream)
+        nbytes = used * per_expert + T * H * 4 * 2 + T * K * (I + H) * 4 * 2
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out["T%d" % T] = {"us": round(ms * 1e3, 1), "experts_used": used, "bytes": int(nbytes),
+                          "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak_gbs, 4)}
+    del flush
+    torch.cuda.synchronize(dev)
+    return out
+
+
+# ---------------------------------------------------------------------------
 # profiling cases (for ncu on a small case)
 # ---------------------------------------------------------------------------
 
@@ -727,6 +820,12 @@ def main():
             mx.close()
             del mx
             torch.cuda.synchronize(dev)
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if os.path.exists(
+            os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
+        extras["prefill_gemm_1.7b"] = prefill_extra(dev, peaks.get("bf16_tflops", 1590.0), stream)
+        extras["prefill_gemm_1.7b"]["peak"] = "bf16_tflops %s (cuBLAS burst)" % (
+            "measured" if peaks else "fallback 1590")
+        extras["moe_int3_lfm2.5"] = moe_extra(dev, peak, stream)
         sec, reps, dt = cpu_step_seconds(1, 12.0)
         cpu = {"value": round(B / sec, 4), "unit": "tok/s", "cores": 1, "kind": "port",
                "sample": "2 of 28 decoder layers (7 matrices each) + 1/16 of the lm_head rows, %d repetitions in "
