@@ -19,7 +19,12 @@ namespace {
 
 constexpr int MB = 8;          // pairs per chunk
 constexpr int MOE_THREADS = 256;
-constexpr int MOE_RB = 32;     // rows per CTA
+// rows per warp (and per CTA): gate/up decodes two matrices, so one row a warp
+template <int KIND> constexpr int moe_rpw() { return KIND == 0 ? 1 : 2; }
+template <int KIND> constexpr int moe_rb() { return moe_rpw<KIND>() * MOE_THREADS / 32; }
+constexpr int MOE_GPL = 2;     // 32-groups per lane and row (K <= 2048)
+constexpr int MOE_BPC = 4;     // row blocks per CTA (weights of the next one in flight)
+constexpr int XS_PAD = 36;     // floats per staged 32-group (4 of padding: conflict-free 16-byte reads)
 
 // ---- _requant43 -------------------------------------------------------------
 // The engine's f32ToF16 (engine/webgpu-engine.js:217-236): mantissa rounded
@@ -190,66 +195,114 @@ template <int KIND>
 __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
 {
     constexpr int NM = KIND == MOE_GATEUP ? 2 : 1;
-    extern __shared__ float xs[];            // [MB][32][G + 1]: xs[b][i][g] = x_b[32 g + i]
+    constexpr int RPW = moe_rpw<KIND>();
+    extern __shared__ __align__(16) float xs[];   // [MB][G][XS_PAD]: xs[b][g][i] = x_b[32 g + i]
     tb_pdl_wait();
     tb_pdl_trigger();
-    const int e = blockIdx.y, r0 = blockIdx.x * MOE_RB;
+    const int e = blockIdx.y;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int G = a.G, GP = G + 1;
+    const int G = a.G;
     const int p0 = a.offsets[e], np = a.offsets[e + 1] - p0;
+    if (np == 0) return;
+    // planes and scales of one row block of this warp, requested before use
+    struct W {
+        uint32_t w[RPW][MOE_GPL][NM][3];
+        float s[RPW][MOE_GPL][NM];
+    };
+    auto fetch = [&](int blk, W& d) {
+        const int rw0 = (blockIdx.x * MOE_BPC + blk) * moe_rb<KIND>() + wid * RPW;
+#pragma unroll
+        for (int j = 0; j < RPW; j++)
+#pragma unroll
+            for (int t = 0; t < MOE_GPL; t++)
+#pragma unroll
+                for (int m = 0; m < NM; m++) {
+                    const int r = rw0 + j, g = lane + 32 * t;
+                    const bool ok = r < a.N && g < G;
+                    const long long row = (long long)e * a.N + (ok ? r : 0);
+                    const uint32_t* w = a.p3[m] + (row * G + (ok ? g : 0)) * 3;
+                    d.w[j][t][m][0] = ok ? __ldg(w) : 0u;
+                    d.w[j][t][m][1] = ok ? __ldg(w + 1) : 0u;
+                    d.w[j][t][m][2] = ok ? __ldg(w + 2) : 0u;
+                    d.s[j][t][m] = ok ? tb_h2f(__ldg(a.s3[m] + row * G + (ok ? g : 0))) : 0.0f;
+                }
+    };
     for (int c0 = 0; c0 < np; c0 += MB) {
         const int nb = min(MB, np - c0);
+        W cur, nxt;
+        fetch(0, cur);                       // in flight while the activations are staged
         __syncthreads();                     // the previous chunk's reads are done
         for (int b = 0; b < nb; b++) {
             const int p = a.order[p0 + c0 + b];
             const float* src = a.x + (long long)(p / a.xdiv) * a.x_stride;
             for (int k = threadIdx.x; k < a.Kc; k += MOE_THREADS)
-                xs[(b * 32 + (k & 31)) * GP + (k >> 5)] = src[k];
+                xs[(b * G + (k >> 5)) * XS_PAD + (k & 31)] = src[k];
         }
         __syncthreads();
-        for (int r = r0 + wid; r < min(r0 + MOE_RB, a.N); r += MOE_THREADS / 32) {
-            const long long row = (long long)e * a.N + r;
-            float acc[NM][MB];
+        for (int blk = 0; blk < MOE_BPC; blk++) {
+            if (blk + 1 < MOE_BPC) fetch(blk + 1, nxt);
+            const int rw0 = (blockIdx.x * MOE_BPC + blk) * moe_rb<KIND>() + wid * RPW;
+            float acc[NM][RPW][MB];
 #pragma unroll
             for (int m = 0; m < NM; m++)
 #pragma unroll
-                for (int b = 0; b < MB; b++) acc[m][b] = 0.0f;
-            for (int g = lane; g < G; g += 32) {
+                for (int j = 0; j < RPW; j++)
 #pragma unroll
-                for (int m = 0; m < NM; m++) {
-                    const uint32_t* w = a.p3[m] + (row * G + g) * 3;
-                    float q[32];
-                    decode32(__ldg(w), __ldg(w + 1), __ldg(w + 2), q);
-                    const float s = tb_h2f(__ldg(a.s3[m] + row * G + g));
+                    for (int b = 0; b < MB; b++) acc[m][j][b] = 0.0f;
 #pragma unroll
-                    for (int b = 0; b < MB; b++) {
-                        if (b < nb) {
-                            const float* xb = xs + (b * 32) * GP + g;
-                            float sum = 0.0f;
+            for (int t = 0; t < MOE_GPL; t++) {
+                const int g = lane + 32 * t;
+                if (g < G) {
 #pragma unroll
-                            for (int i = 0; i < 32; i++) sum = fmaf(q[i], xb[i * GP], sum);
-                            acc[m][b] = fmaf(s, sum, acc[m][b]);
+                    for (int j = 0; j < RPW; j++)
+#pragma unroll
+                        for (int m = 0; m < NM; m++) {
+                            float q[32];
+                            decode32(cur.w[j][t][m][0], cur.w[j][t][m][1], cur.w[j][t][m][2], q);
+#pragma unroll
+                            for (int b = 0; b < MB; b++) {
+                                if (b < nb) {
+                                    const float4* xb = reinterpret_cast<const float4*>(xs + (b * G + g) * XS_PAD);
+                                    float sum = 0.0f;
+#pragma unroll
+                                    for (int i4 = 0; i4 < 8; i4++) {
+                                        const float4 xv = xb[i4];
+                                        sum = fmaf(q[4 * i4], xv.x, sum);
+                                        sum = fmaf(q[4 * i4 + 1], xv.y, sum);
+                                        sum = fmaf(q[4 * i4 + 2], xv.z, sum);
+                                        sum = fmaf(q[4 * i4 + 3], xv.w, sum);
+                                    }
+                                    acc[m][j][b] = fmaf(cur.s[j][t][m], sum, acc[m][j][b]);
+                                }
+                            }
                         }
-                    }
                 }
             }
 #pragma unroll
             for (int m = 0; m < NM; m++)
 #pragma unroll
-                for (int b = 0; b < MB; b++) acc[m][b] = warp_sum(acc[m][b]);
+                for (int j = 0; j < RPW; j++)
+#pragma unroll
+                    for (int b = 0; b < MB; b++) acc[m][j][b] = warp_sum(acc[m][j][b]);
             if (lane == 0) {
-                for (int b = 0; b < nb; b++) {
-                    const int p = a.order[p0 + c0 + b];
-                    float v;
-                    if (KIND == MOE_GATEUP) {
-                        const float g = acc[0][b], u = acc[NM - 1][b];
-                        v = __fdiv_rn(g, 1.0f + expf(-g)) * u;      // silu(gate) * up
-                    } else {
-                        v = acc[0][b];
+#pragma unroll
+                for (int j = 0; j < RPW; j++) {
+                    const int r = rw0 + j;
+                    if (r >= a.N) continue;
+                    for (int b = 0; b < nb; b++) {
+                        const int p = a.order[p0 + c0 + b];
+                        float v;
+                        if (KIND == MOE_GATEUP) {
+                            const float gg = acc[0][j][b], u = acc[NM - 1][j][b];
+                            v = __fdiv_rn(gg, 1.0f + expf(-gg)) * u;      // silu(gate) * up
+                        } else {
+                            v = acc[0][j][b];
+                        }
+                        a.y[(long long)p * a.N + r] = v;
                     }
-                    a.y[(long long)p * a.N + r] = v;
                 }
             }
+            cur = nxt;
         }
     }
 }
@@ -268,16 +321,18 @@ __global__ void __launch_bounds__(256) k_moe_combine(float* __restrict__ x, cons
     }
 }
 
-size_t moe_smem(int Kc) { return (size_t)MB * 32 * (Kc / 32 + 1) * sizeof(float); }
+size_t moe_smem(int Kc) { return (size_t)MB * (Kc / 32) * XS_PAD * sizeof(float); }
 
 template <int KIND>
 int launch_moe(tb_ctx* ctx, const MoeArgs& a, int nE)
 {
     const size_t smem = moe_smem(a.Kc);
+    TB_REQUIRE(ctx, a.G <= 32 * MOE_GPL, "moe: K = %d above %d", a.Kc, 32 * 32 * MOE_GPL);
     TB_REQUIRE(ctx, smem <= 200 * 1024, "moe: K = %d too large for the staged activations", a.Kc);
     cudaError_t e = cudaFuncSetAttribute(k_moe_gemv3<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
-        e = tb_launch(ctx, k_moe_gemv3<KIND>, dim3((unsigned)tb_cdiv(a.N, MOE_RB), (unsigned)nE), dim3(MOE_THREADS),
+        e = tb_launch(ctx, k_moe_gemv3<KIND>, dim3((unsigned)tb_cdiv(a.N, moe_rb<KIND>() * MOE_BPC), (unsigned)nE),
+                      dim3(MOE_THREADS),
                       smem, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe gemv launch: %s", cudaGetErrorString(e));
     return TB_OK;
@@ -322,8 +377,9 @@ TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const u
 {
     if (!ctx) return TB_ERR_INVALID;
     TB_REQUIRE(ctx, x_out && x_in && idx && wt && w1p && w1s && w3p && w3s && w2p && w2s, "null pointer");
-    TB_REQUIRE(ctx, T > 0 && K > 0 && nE > 0 && nE <= 256 && H % 32 == 0 && I % 32 == 0 && H > 0 && I > 0,
-               "bad MoE shape (H, I multiples of 32, nE <= 256)");
+    TB_REQUIRE(ctx, T > 0 && K > 0 && nE > 0 && nE <= 256 && H % 32 == 0 && I % 32 == 0 && H > 0 && I > 0 &&
+                        H <= 2048 && I <= 2048,
+               "bad MoE shape (H, I multiples of 32 up to 2048, nE <= 256)");
     const int64_t P = T * K;
     TB_REQUIRE(ctx, P <= (1 << 20), "too many (token, expert) pairs");
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
