@@ -568,6 +568,24 @@ def profile_attn(S):
     print("profile attn done", flush=True)
 
 
+def profile_decode(context):
+    """Three recorded Qwen3-1.7B decode steps (batch 1) at the given context on
+    one GPU, for an ncu launch list of one step (172 kernels)."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    m = build_model(Q17, dev, 1, context, 16, 1, 0)
+    m.set_tokens([1000], [context - 1])
+    for _ in range(3):
+        m.step()
+    torch.cuda.synchronize()
+    kernels, _ = m.launches_per_step()
+    err = tb.default_context(0).device_error()
+    assert err == 0, err
+    m.close()
+    print("profile decode done: %d kernels per step" % kernels, flush=True)
+
+
 def profile_gemm(M, N, K):
     """Three cold-L2 launches of the tcgen05 prefill GEMM (bf16 activations) at
     M x N x K (config 4: M in {512, 2048, 8192}), for an ncu capture of one."""
@@ -689,7 +707,12 @@ def main():
                     help="three cold-L2 decode-attention launches at context S (for ncu), then exit")
     ap.add_argument("--profile-gemm", type=int, nargs=3, default=None, metavar=("M", "N", "K"),
                     help="three cold-L2 prefill-GEMM launches at M x N x K (for ncu), then exit")
+    ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
+                    help="three recorded decode steps at context S (for an ncu launch list), then exit")
     args = ap.parse_args()
+    if args.profile_decode:
+        profile_decode(args.profile_decode)
+        return
     if args.profile_gemm:
         profile_gemm(*args.profile_gemm)
         return
