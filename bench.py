@@ -492,6 +492,81 @@ def moe_extra(dev, peak_gbs, stream):
     return out
 
 
+def _tern_weights(dev, g, N, K):
+    """A ternary bf16 matrix (per 32-group {-m, 0, +m}) packed on the device in the
+    WebGPU layout (quantizeTernaryBf16)."""
+    import torch
+    import tabinfer_b200 as tb
+    mag = (torch.rand(N, K // 32, device=dev, generator=g) * 0.05 + 0.005).view(torch.int32) >> 16
+    t = torch.randint(-1, 2, (N, K), device=dev, generator=g, dtype=torch.int32)
+    bits = torch.where(t == 0, torch.zeros_like(t), mag.repeat_interleave(32, dim=1) | ((t < 0).int() << 15))
+    w = torch.where(bits >= 32768, bits - 65536, bits).to(torch.int16)
+    del t, bits, mag
+    r = tb.quantize_tern_bf16(w)
+    assert r is not None
+    return r
+
+
+def tern_extra(dev, peak_gbs, peak_tf, stream):
+    """Ternary weights in the WebGPU layout at Bonsai-1.7B shapes (Qwen3-1.7B
+    architecture): the batch-1 decode GEMVs (quantQ8 fused, cold L2) with their
+    algorithmic bytes (codes K/4 + f16 scales K/16 bytes a row, f32 activation in,
+    f32 out), and the prefill GEMM on 2048 rows (2*M*N*K flops)."""
+    import torch
+    import tabinfer_b200 as tb
+    g = torch.Generator(device=dev).manual_seed(21)
+    H, I, V = Q17["hidden"], Q17["intermediate"], Q17["vocab"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    mats = {n: _tern_weights(dev, g, N, K) for n, (N, K) in
+            {"q": (2048, H), "k": (1024, H), "v": (1024, H), "o": (H, 2048), "gate": (I, H), "up": (I, H),
+             "down": (H, I), "lm_head": (V, H)}.items()}
+
+    def tb_bytes(N, K, nact=1):
+        return N * K // 4 + N * K // 16 + nact * K * 4 + N * 4
+
+    x = torch.randn(1, H, device=dev, generator=g)
+    xi = torch.randn(1, I, device=dev, generator=g)
+    ys = {n: torch.empty(1, p.shape[0], device=dev) for n, (p, _) in mats.items()}
+    swi = torch.empty(1, I, device=dev)
+    cases = {
+        "qkv": (lambda: tb.gemv_tern_wgsl_dp4a_multi(x, [mats["q"], mats["k"], mats["v"]],
+                                                     ys=[ys["q"], ys["k"], ys["v"]]),
+                tb_bytes(2048, H) + 2 * tb_bytes(1024, H)),
+        "o": (lambda: tb.linear_tern_wgsl(x, *mats["o"], y=ys["o"]), tb_bytes(H, 2048)),
+        "gateup": (lambda: tb.gate_up_silu_tern_dp4a(x, *mats["gate"], *mats["up"], swi=swi), 2 * tb_bytes(I, H)),
+        "down": (lambda: tb.linear_tern_wgsl(xi, *mats["down"], y=ys["down"]), tb_bytes(H, I)),
+        "lm_head": (lambda: tb.linear_tern_wgsl(x, *mats["lm_head"], y=ys["lm_head"]), tb_bytes(V, H)),
+    }
+    tot_ms = tot_b = 0.0
+    for name, (fn, nbytes) in cases.items():
+        ms = _cold_time(fn, flush, stream, reps=9)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "bytes": int(nbytes), "gbs": round(gbs, 1),
+                     "frac_of_peak": round(gbs / peak_gbs, 4)}
+        if name != "lm_head":
+            tot_ms += ms
+            tot_b += nbytes
+    out["layer_gemvs"] = {"us": round(tot_ms * 1e3, 2), "gbs": round(tot_b / (tot_ms * 1e-3) / 1e9, 1),
+                          "frac_of_peak": round(tot_b / (tot_ms * 1e-3) / 1e9 / peak_gbs, 4)}
+    M = 2048
+    ms = flop = 0.0
+    for n in ("q", "k", "v", "o", "gate", "up", "down"):
+        pk, sc = mats[n]
+        N, K = pk.shape[0], pk.shape[1] * 16
+        xq = torch.randint(-127, 128, (M, K), device=dev, generator=g, dtype=torch.int32).to(torch.int8)
+        xs = torch.rand(M, K // 32, device=dev, generator=g) * 0.01
+        y = torch.empty(M, N, device=dev)
+        ms += _cold_time(lambda: tb.gemm_tern(xq, xs, pk, sc, y=y), flush, stream)
+        flop += 2 * M * N * K
+    tf = flop / (ms * 1e-3) / 1e12
+    out["prefill_M2048"] = {"us_7_matrices": round(ms * 1e3, 1), "tflops": round(tf, 1),
+                            "frac_of_bf16_peak": round(tf / peak_tf, 4)}
+    del flush, mats
+    torch.cuda.synchronize(dev)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # profiling cases (for ncu on a small case)
 # ---------------------------------------------------------------------------
@@ -849,6 +924,7 @@ def main():
         extras["prefill_gemm_1.7b"]["peak"] = "bf16_tflops %s (cuBLAS burst)" % (
             "measured" if peaks else "fallback 1590")
         extras["moe_int3_lfm2.5"] = moe_extra(dev, peak, stream)
+        extras["ternary_wgsl_bonsai_1.7b"] = tern_extra(dev, peak, peaks.get("bf16_tflops", 1590.0), stream)
         sec, reps, dt = cpu_step_seconds(1, 12.0)
         cpu = {"value": round(B / sec, 4), "unit": "tok/s", "cores": 1, "kind": "port",
                "sample": "2 of 28 decoder layers (7 matrices each) + 1/16 of the lm_head rows, %d repetitions in "

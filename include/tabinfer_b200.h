@@ -187,6 +187,64 @@ TB_API int tb_gemv_tern_q2g64(tb_ctx *ctx, float *out, const uint8_t *codes, con
 TB_API int tb_linear_tern(tb_ctx *ctx, float *y, const float *x, const uint8_t *codes,
                           const float *scales, int64_t T, int64_t N, int64_t K);
 
+/* ---- ternary, WebGPU layout (models/qwen3.js) ------------------------------
+ * The layout of the reference's browser engine for Bonsai/BitNet-style weights:
+ * pack u32 [N][K/16], 16 codes w+1 in {0,1,2} per word, weight k = 16w+4s+b at
+ * bits 8b+2s of word w; f16 scales [N][K/32] (the int4 scale layout).  The
+ * GEMVs take the per-32 int8 activation of tb_quant_q8 (QUANTQ8) and compute,
+ * per 32-group, f32(scale) * xs * sum((c-1) * xq) with an exact int32 sum. */
+
+/* Lossless ternary detection + pack, quantizeTernaryBf16 (qwen3.js:3435-3469):
+ * bf16 [N,K] -> pack + scales as above.  *nonternary (a DEVICE int) is set to
+ * nonzero when the matrix is not ternary (some nonzero magnitude more than 2
+ * bf16 ulps below its 32-group's maximum, or K % 64 != 0) -- the reference's
+ * null return, after which the caller quantizes to int4 instead. */
+TB_API int tb_quant_tern_wgsl_bf16(tb_ctx *ctx, const uint16_t *w_bf16, uint32_t *pack,
+                                   uint16_t *scales, int64_t N, int64_t K, int *nonternary);
+
+/* gemvTern_only (qwen3.js:548-556; shader gemvTern2Wgsl :449-503) against a
+ * pre-quantized QUANTQ8 activation of `batch` rows (1..8); y [batch][N]
+ * (+= y when acc).  K % 64 == 0; pack, scales, xq 16-byte aligned. */
+TB_API int tb_gemv_tern_wgsl_q8(tb_ctx *ctx, float *y, const int8_t *xq, const float *xs,
+                                const uint32_t *pack, const uint16_t *scales, int64_t N, int64_t K,
+                                int batch, int acc);
+
+/* quantQ8 (or the fused RMSNorm of RMSNORMQ when norm_w16 != NULL) followed by
+ * gemvTern_only for 1..4 matrices sharing the activation (projGemv at the
+ * q/k/v call sites, qwen3.js:558-561, 3982-3984), in one launch. */
+TB_API int tb_gemv_tern_wgsl_dp4a_multi(tb_ctx *ctx, int count, float *const *ys,
+                                        const uint32_t *const *packs, const uint16_t *const *scales,
+                                        const int64_t *Ns, const float *x, const uint16_t *norm_w16,
+                                        float eps, int64_t K, int batch, int acc);
+
+/* Fused ternary gate+up+SiLU, gateupTern2Wgsl (qwen3.js:747-810) as routed by
+ * gateUpSiluDP4_only / gateUpSiluQ (:730, :861-870): swi [batch][I] =
+ * silu(g) * u.  _q8 takes the QUANTQ8 activation, _dp4a the f32 row (and the
+ * optional RMSNorm weight). */
+TB_API int tb_gateup_silu_tern_wgsl_q8(tb_ctx *ctx, float *swi, const int8_t *xq, const float *xs,
+                                       const uint32_t *gpack, const uint16_t *gscales,
+                                       const uint32_t *upack, const uint16_t *uscales,
+                                       int64_t I, int64_t H, int batch);
+TB_API int tb_gateup_silu_tern_wgsl_dp4a(tb_ctx *ctx, float *swi, const float *x,
+                                         const uint16_t *norm_w16, float eps,
+                                         const uint32_t *gpack, const uint16_t *gscales,
+                                         const uint32_t *upack, const uint16_t *uscales,
+                                         int64_t I, int64_t H, int batch);
+
+/* Prefill GEMM of ternary weights (gemmTern, qwen3.js:1410-1420) on tcgen05:
+ * y[M,N] (+)= f16(xs * xq) . f16((c-1) * s)^T with f32 accumulation, from the
+ * QUANTQ8T rows xq int8 [M,K] / xs f32 [M,K/32].  M % 128 == 0, N % 256 == 0,
+ * K % 64 == 0; xq, pack, y 16-byte aligned, xs and scales 4-byte aligned. */
+TB_API int tb_gemm_tern_wgsl(tb_ctx *ctx, float *y, const int8_t *xq, const float *xs,
+                             const uint32_t *pack, const uint16_t *scales, int64_t M, int64_t N,
+                             int64_t K, int acc);
+
+/* linearQ for a ternary weight record (qwen3.js:1594-1598): T <= 8 rows run the
+ * ternary GEMV (quantQ8 fused), T > 8 quantize (QUANTQ8T) into context scratch
+ * and run tb_gemm_tern_wgsl (T % 128 == 0, N % 256 == 0). */
+TB_API int tb_linear_tern_wgsl(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
+                               const uint16_t *scales, int64_t T, int64_t N, int64_t K, int acc);
+
 /* ---- int8 KV cache + split-KV GQA decode attention ----------------------- */
 
 /* Fused decode attention prep at position `pos` (T=1):

@@ -123,6 +123,11 @@ def f16_to_f64(h):
     return lib().tbo_f16_to_f64(int(h))
 
 
+def f16_bits_to_f64(h):
+    """f16 bit patterns (any shape) -> exact float64 values."""
+    return np.ascontiguousarray(h, np.uint16).view(np.float16).astype(np.float64)
+
+
 def quant_int4_g32(w_bf16):
     w = np.ascontiguousarray(w_bf16, np.uint16)
     N, K = w.shape
@@ -214,6 +219,43 @@ def gateup_q8act(xq, xs, gpack, gscales, upack, uscales):
 # --------------------------------------------------------------------------
 # ternary path
 # --------------------------------------------------------------------------
+
+def quant_tern_wgsl(w_bf16):
+    """quantizeTernaryBf16 (qwen3.js:3435-3469): (pack u32 [N,K/16], scales f16 bits
+    [N,K/32]) or None when not ternary."""
+    w = np.ascontiguousarray(w_bf16, np.uint16)
+    N, K = w.shape
+    pack = np.zeros((N, max(K // 16, 1)), np.uint32)
+    scales = np.zeros((N, max(K // 32, 1)), np.uint16)
+    ok = lib().tbo_quant_tern_wgsl(_ptr(w), _I(N), _I(K), _ptr(pack), _ptr(scales))
+    return (pack, scales) if ok else None
+
+
+def gemv_tern_wgsl_q8act(xq, xs, pack, scales):
+    """gemvTern2Wgsl (qwen3.js:449-503) in double over exact per-group int32 dots."""
+    xq = np.ascontiguousarray(np.atleast_2d(xq), np.int8)
+    xs = np.ascontiguousarray(np.atleast_2d(xs), np.float32)
+    B, K = xq.shape
+    N = pack.shape[0]
+    y = np.zeros((B, N), np.float64)
+    lib().tbo_gemv_tern_wgsl_q8act(_ptr(xq), _ptr(xs), _ptr(np.ascontiguousarray(pack, np.uint32)),
+                                   _ptr(np.ascontiguousarray(scales, np.uint16)), _I(N), _I(K), _I(B), _ptr(y))
+    return y
+
+
+def gateup_tern_wgsl_q8act(xq, xs, gpack, gscales, upack, uscales):
+    """gateupTern2Wgsl (qwen3.js:747-810): silu(g) * u in double."""
+    xq = np.ascontiguousarray(np.atleast_2d(xq), np.int8)
+    xs = np.ascontiguousarray(np.atleast_2d(xs), np.float32)
+    B, H = xq.shape
+    I = gpack.shape[0]
+    y = np.zeros((B, I), np.float64)
+    lib().tbo_gateup_tern_wgsl_q8act(_ptr(xq), _ptr(xs), _ptr(np.ascontiguousarray(gpack, np.uint32)),
+                                     _ptr(np.ascontiguousarray(gscales, np.uint16)),
+                                     _ptr(np.ascontiguousarray(upack, np.uint32)),
+                                     _ptr(np.ascontiguousarray(uscales, np.uint16)), _I(I), _I(H), _I(B), _ptr(y))
+    return y
+
 
 def pack_ternary(w):
     w = np.ascontiguousarray(w, np.float32)

@@ -316,6 +316,82 @@ TBO_API void tbo_gateup_q8act(const int8_t *xq, const float *xs,
 }
 
 /* ------------------------------------------------------------------------ */
+/* Ternary, WebGPU layout -- models/qwen3.js                                 */
+/* ------------------------------------------------------------------------ */
+
+/* quantizeTernaryBf16, qwen3.js:3435-3469.  Returns 1 and fills pack u32
+ * [N,K/16] + f16 scales [N,K/32] when every 32-group holds only {-s, 0, +s}
+ * (nonzero magnitude bits at most TOL = 2 below the group's maximum mx);
+ * returns 0 (the reference's null) otherwise or when K % 64 != 0.
+ * Code w+1: 1 for a zero magnitude, 0 negative, 2 positive; weight k at bits
+ * 8*(k&3) + 2*((k>>2)&3) of word k>>4; scale = bf16ToF16bits(mx)
+ * (qwen3.js:3386-3390: bf16 -> f32 exactly, then f32ToF16). */
+TBO_API int tbo_quant_tern_wgsl(const uint16_t *w, int64_t N, int64_t K,
+                                uint32_t *pack, uint16_t *scales)
+{
+    const int TOL = 2;
+    if (K % 64 != 0) return 0;
+    const int64_t wpr = K / 16, gpr = K / 32;
+    memset(pack, 0, (size_t)(N * wpr) * sizeof(uint32_t));
+    for (int64_t n = 0; n < N; n++)
+        for (int64_t g = 0; g < gpr; g++) {
+            const uint16_t *src = w + n * K + g * 32;
+            int mx = 0;
+            for (int j = 0; j < 32; j++) { int m = src[j] & 0x7FFF; if (m > mx) mx = m; }
+            scales[n * gpr + g] = tbo_f32_to_f16_js(bits_f32((uint32_t)mx << 16));
+            for (int j = 0; j < 32; j++) {
+                int64_t k = g * 32 + j;
+                int m = src[j] & 0x7FFF;
+                if (m != 0 && mx - m > TOL) return 0;
+                uint32_t c = m == 0 ? 1u : ((src[j] & 0x8000) ? 0u : 2u);
+                pack[n * wpr + (k >> 4)] |= c << (((k & 3) << 3) + ((k >> 2) & 3) * 2);
+            }
+        }
+    return 1;
+}
+
+/* gemvTern2Wgsl / gemvTernWgsl, qwen3.js:449-546 (and the ternary tiles of the
+ * prefill GEMM, gemmdp4Wgsl(tern) :1357-1359, whose QUANTQ8T rows equal
+ * QUANTQ8's): per (row, 32-group) the exact int32 sum((c-1) * xq), scaled by
+ * f32(s16) * xs (an f32 product, as the shader's f32(sc) * xsc).  Groups summed
+ * in double. */
+TBO_API void tbo_gemv_tern_wgsl_q8act(const int8_t *xq, const float *xs,
+                                      const uint32_t *pack, const uint16_t *scales,
+                                      int64_t N, int64_t K, int64_t batch, double *y)
+{
+    const int64_t wpr = K / 16, gpr = K / 32;
+    for (int64_t n = 0; n < N; n++)
+        for (int64_t b = 0; b < batch; b++) {
+            double a = 0.0;
+            for (int64_t g = 0; g < gpr; g++) {
+                int32_t dot = 0;
+                for (int j = 0; j < 32; j++) {
+                    int64_t k = g * 32 + j;
+                    int c = (int)((pack[n * wpr + (k >> 4)] >> (((k & 3) << 3) + ((k >> 2) & 3) * 2)) & 3u);
+                    dot += (c - 1) * (int32_t)xq[b * K + k];
+                }
+                float s = (float)tbo_f16_to_f64(scales[n * gpr + g]) * xs[b * gpr + g];
+                a += (double)s * (double)dot;
+            }
+            y[b * N + n] = a;
+        }
+}
+
+/* gateupTern2Wgsl, qwen3.js:747-810: swi = silu(g) * u of the two ternary GEMVs. */
+TBO_API void tbo_gateup_tern_wgsl_q8act(const int8_t *xq, const float *xs,
+                                        const uint32_t *gpack, const uint16_t *gscales,
+                                        const uint32_t *upack, const uint16_t *uscales,
+                                        int64_t I, int64_t H, int64_t batch, double *swi)
+{
+    double *g = (double *)malloc(sizeof(double) * (size_t)(I * batch));
+    double *u = (double *)malloc(sizeof(double) * (size_t)(I * batch));
+    tbo_gemv_tern_wgsl_q8act(xq, xs, gpack, gscales, I, H, batch, g);
+    tbo_gemv_tern_wgsl_q8act(xq, xs, upack, uscales, I, H, batch, u);
+    for (int64_t i = 0; i < I * batch; i++) swi[i] = g[i] / (1.0 + exp(-g[i])) * u[i];
+    free(g); free(u);
+}
+
+/* ------------------------------------------------------------------------ */
 /* Ternary Q2_0_g64 -- native/crates/n2-kernels/src/tern.rs                  */
 /* ------------------------------------------------------------------------ */
 

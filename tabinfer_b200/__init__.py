@@ -4,7 +4,8 @@ The product is libtabinfer_b200.so (hand-written sm_100a CUDA behind the C ABI
 in include/tabinfer_b200.h).  This package is the host-side mirror of the
 reference's operator interface for that path (models/qwen3.js linearQ /
 gemvQ / gemvDP4A / rmsnormQ / gateUpSiluDP4 / attnPrepQ8 / attentionQ8 /
-argmaxKernel, and native/crates/n2-kernels tern::{pack_ternary,
+argmaxKernel, the ternary WebGPU layout quantizeTernaryBf16 / gemvTern /
+gateupTern, and native/crates/n2-kernels tern::{pack_ternary,
 quantize_act, gemv_tern}), taking torch CUDA tensors as device buffers.
 Errors raise TabInferError, as the reference throws.
 """
@@ -14,6 +15,8 @@ from .ops import (  # noqa: F401
     gemv_dp4a, gemv_dp4a_multi, gate_up_silu_dp4a, gemv_q_norm, gemm_q,
     requant_int3, moe_router, moe_ffn_int3,
     gate_up_silu_dp4, pack_ternary, quantize_act, gemv_tern, linear_tern,
+    quantize_tern_bf16, gemv_tern_wgsl, gemv_tern_wgsl_dp4a_multi, gate_up_silu_tern, gate_up_silu_tern_dp4a,
+    gemm_tern, linear_tern_wgsl,
     attn_prep_q8, kv_quant_write, attention_decode_q8, argmax, rmsnorm, embed_gather,
 )
 from .qwen3 import Qwen3, QWEN3_1_7B, QWEN3_0_6B  # noqa: F401,E402

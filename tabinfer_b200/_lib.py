@@ -45,6 +45,13 @@ SIGNATURES = {
     "tb_gateup_silu_int4_dp4a": [P, P, P, P, F32, P, P, P, P, I64, I64, I32],
     "tb_gemv_int4_f32_norm": [P, P, P, P, F32, P, P, I64, I64, I32, I32],
     "tb_pack_tern_q2g64": [P, P, P, P, I64, I64],
+    "tb_quant_tern_wgsl_bf16": [P, P, P, P, I64, I64, P],
+    "tb_gemv_tern_wgsl_q8": [P, P, P, P, P, P, I64, I64, I32, I32],
+    "tb_gemv_tern_wgsl_dp4a_multi": [P, I32, P, P, P, P, P, P, F32, I64, I32, I32],
+    "tb_gateup_silu_tern_wgsl_q8": [P, P, P, P, P, P, P, P, I64, I64, I32],
+    "tb_gateup_silu_tern_wgsl_dp4a": [P, P, P, P, F32, P, P, P, P, I64, I64, I32],
+    "tb_gemm_tern_wgsl": [P, P, P, P, P, P, I64, I64, I64, I32],
+    "tb_linear_tern_wgsl": [P, P, P, P, P, I64, I64, I64, I32],
     "tb_quant_act_q8": [P, P, P, P, P, I64, I64],
     "tb_gemv_tern_q2g64": [P, P, P, P, P, P, I64, I64, I32],
     "tb_linear_tern": [P, P, P, P, P, I64, I64, I64],

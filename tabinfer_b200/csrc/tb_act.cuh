@@ -76,3 +76,21 @@ __device__ __forceinline__ Q8Group q8_group(float v)
     const float scale = q8_scale(warp_max(fabsf(v)));
     return Q8Group{q8_quant(v, q8_inv(scale)), scale};
 }
+
+// models/qwen3.js:3357-3374: f16 bits of an f32, mantissa rounded half-up.
+__device__ __forceinline__ uint32_t js_f32_to_f16(float val)
+{
+    uint32_t x = __float_as_uint(val);
+    uint32_t sign = (x >> 16) & 0x8000u, ex = (x >> 23) & 0xffu, mant = x & 0x7fffffu;
+    if (ex == 0xffu) return sign | (mant ? 0x7e00u : 0x7c00u);
+    int e = (int)ex - 127 + 15;
+    if (e >= 31) return sign | 0x7c00u;
+    if (e <= 0) {
+        if (e < -10) return sign;
+        uint32_t m = mant | 0x800000u;
+        int shift = 14 - e;
+        uint32_t half = (m >> shift) + ((m >> (shift - 1)) & 1u);
+        return sign | half;
+    }
+    return sign | ((((uint32_t)e << 10) | (mant >> 13)) + ((mant >> 12) & 1u));
+}

@@ -13,6 +13,12 @@
 // 128-byte-swizzled K-major layout the tensor core reads (8-row x 128-byte
 // atoms).  Warp 16 allocates 256 TMEM columns and one of its threads issues four
 // 128x256x16 MMAs per stage; tcgen05.commit frees the stage when they complete.
+// Ternary weights in the WebGPU layout (gemmTern, qwen3.js:1410-1420) use the
+// same pipeline with the operands of that GEMM: X arrives as QUANTQ8T int8 rows
+// with per-32 f32 scales and becomes f16(xs * q); a weight becomes the exact
+// f16 (c - 1) * s.  (The reference sums the int8 products of a group exactly
+// and scales once per group; here f16(xs * q) rounds each activation to 11
+// bits, ~1e-4 of a row's scale.)
 // After the last stage warps 0-15 read the accumulator (tcgen05.ld, warp w owns
 // TMEM lanes 32*(w%4)..+31 and columns 64*(w/4)..+63) and store f32 rows.  Waits are bounded: on a timeout the CTA records
 // ERR_GEMM_WAIT, stops issuing, and still frees its TMEM.
@@ -27,11 +33,15 @@ constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_
 // X as given (bf16 or f32), packed W, W scales; chunk-major (16-byte chunk c of
 // producer thread t at c * PROD + t) so copies and reads are bank-conflict free
 constexpr int RAW_W = PROD * 16, RAW_S = PROD * 4;
-template <bool XBF16> struct Cfg {
-    static constexpr int XC = XBF16 ? 2 : 4;                 // raw X chunks per producer thread
-    static constexpr int X = PROD * XC * 16;
-    static constexpr int RSTAGE = X + RAW_W + RAW_S;
-    static constexpr int NST = XBF16 ? 3 : 2;                // MMA operand stages
+enum XMode { X_F32 = 0, X_BF16 = 1, X_Q8_TERN = 2 };
+template <int MODE> struct Cfg {
+    static constexpr bool TERN = MODE == X_Q8_TERN;
+    static constexpr int XC = MODE == X_F32 ? 4 : (MODE == X_BF16 ? 2 : 1);   // raw X chunks per producer thread
+    static constexpr int XS = TERN ? PROD * 4 : 0;           // int8 rows: one f32 group scale per thread
+    static constexpr int X = PROD * XC * 16 + XS;
+    static constexpr int WB = TERN ? PROD * 8 : RAW_W;       // raw weight bytes (ternary: 2 words per thread)
+    static constexpr int RSTAGE = X + WB + RAW_S;
+    static constexpr int NST = MODE == X_F32 ? 2 : 3;        // MMA operand stages
     static constexpr int NR = 3;                             // raw stages
     static constexpr int SMEM = 1024 + NST * STAGE + NR * RSTAGE + 256;
 };
@@ -40,8 +50,9 @@ constexpr int GEMM_WAIT_TRIES = 1000;      // x a 1 ms suspend bound per try: at
 constexpr int ERR_GEMM_WAIT = 0x6b01;
 
 struct GemmArgs {
-    const void* x;          // [M][K] f32 or bf16
-    const uint32_t* pack;   // [N][K/8]
+    const void* x;          // [M][K] f32, bf16 or int8 (ternary mode)
+    const float* xs;        // [M][K/32] group scales of int8 rows (ternary mode)
+    const uint32_t* pack;   // [N][K/8] int4, or [N][K/16] ternary codes
     const uint16_t* scales; // [N][K/32] f16
     float* y;               // [M][N]
     int M, N, K, acc;
@@ -98,6 +109,10 @@ __device__ __forceinline__ void cp16(void* sdst, const void* gsrc)
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
 }
+__device__ __forceinline__ void cp8(void* sdst, const void* gsrc)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
 __device__ __forceinline__ void cp4(void* sdst, const void* gsrc)
 {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
@@ -127,10 +142,48 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2)
                       __byte_perm(p2, p3, 0x7632));
 }
 
-template <bool XBF16>
+// 8 ternary codes k = 8h..8h+7 of one word (k = 4s+b at bits 8b+2s, s = 2h, 2h+1)
+// -> 8 f16 (c - 1) * s in k order (16 bytes); exact: c - 1 is -1, 0 or 1.
+__device__ __forceinline__ uint4 dequant_tern8(uint32_t w, int h, uint32_t s2)
+{
+    const uint32_t magic = 0x64006400u;   // f16 1024 + c in both halves
+    const uint32_t lo = w >> (4 * h), hi = w >> (4 * h + 2);
+    uint32_t p0 = (lo & 0x00030003u) | magic;          // s = 2h:   b0, b2
+    uint32_t p1 = ((lo >> 8) & 0x00030003u) | magic;   //           b1, b3
+    uint32_t p2 = (hi & 0x00030003u) | magic;          // s = 2h+1: b0, b2
+    uint32_t p3 = ((hi >> 8) & 0x00030003u) | magic;   //           b1, b3
+    const uint32_t bias = 0x64016401u;                 // 1025 = 1024 + 1
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p0) : "r"(bias));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p1) : "r"(bias));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p2) : "r"(bias));
+    asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(p3) : "r"(bias));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p0) : "r"(s2));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p1) : "r"(s2));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p2) : "r"(s2));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p3) : "r"(s2));
+    return make_uint4(__byte_perm(p0, p1, 0x5410), __byte_perm(p0, p1, 0x7632), __byte_perm(p2, p3, 0x5410),
+                      __byte_perm(p2, p3, 0x7632));
+}
+
+// 4 int8 (one word) -> 4 floats exactly (2^23 + (q ^ 0x80) - (2^23 + 128)), times xs
+__device__ __forceinline__ void q8x4_scaled(uint32_t w, float xs, float2& a, float2& b)
+{
+    const uint32_t u = w ^ 0x80808080u;
+    const float2 M2 = make_float2(-8388736.0f, -8388736.0f);   // -(2^23 + 128)
+    const float2 S2 = make_float2(xs, xs);
+    a = fadd2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
+                          __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541))), M2);
+    b = fadd2(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
+                          __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543))), M2);
+    a = make_float2(__fmul_rn(a.x, S2.x), __fmul_rn(a.y, S2.y));
+    b = make_float2(__fmul_rn(b.x, S2.x), __fmul_rn(b.y, S2.y));
+}
+
+template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
 {
-    using R = Cfg<XBF16>;
+    using R = Cfg<MODE>;
+    constexpr bool XBF16 = MODE == X_BF16, TERN = R::TERN;
     constexpr int NST = R::NST;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -174,11 +227,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
                 uint8_t* rs = rawbase + (i % R::NR) * R::RSTAGE;
                 const int k0 = i * BK;
                 const uint8_t* xs = static_cast<const uint8_t*>(a.x) +
-                                    ((size_t)(m0 + xr) * a.K + k0 + 16 * xq) * (XBF16 ? 2 : 4);
+                                    ((size_t)(m0 + xr) * a.K + k0 + 16 * xq) * (MODE == X_F32 ? 4 : (XBF16 ? 2 : 1));
 #pragma unroll
                 for (int c = 0; c < R::XC; c++) cp16(rs + (c * PROD + tid) * 16, xs + 16 * c);
-                cp16(rs + R::X + tid * 16, a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8 + 4 * wh);
-                cp4(rs + R::X + RAW_W + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32);
+                if (TERN) {
+                    cp4(rs + PROD * 16 + tid * 4, a.xs + (size_t)(m0 + xr) * (a.K / 32) + k0 / 32 + (xq >> 1));
+                    cp8(rs + R::X + tid * 8, a.pack + (size_t)(n0 + wr) * (a.K / 16) + k0 / 16 + 2 * wh);
+                } else {
+                    cp16(rs + R::X + tid * 16, a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8 + 4 * wh);
+                }
+                cp4(rs + R::X + R::WB + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32);
             }
             cp_commit();   // a group per k-step, empty past the end, keeps the count uniform
         };
@@ -196,7 +254,21 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
             uint8_t* Bt = A + A_BYTES;
             const uint8_t* rs = rawbase + (i % R::NR) * R::RSTAGE;
             // X: 16 values of row xr -> f16 chunks 2 xq, 2 xq + 1
-            if (XBF16) {
+            if (TERN) {
+                const uint4 v = *reinterpret_cast<const uint4*>(rs + tid * 16);
+                const float xsc = *reinterpret_cast<const float*>(rs + PROD * 16 + tid * 4);
+                const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+                uint32_t o[8];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float2 p, q;
+                    q8x4_scaled(in[j], xsc, p, q);
+                    o[2 * j] = f32x2_to_f16x2(p.x, p.y);
+                    o[2 * j + 1] = f32x2_to_f16x2(q.x, q.y);
+                }
+                *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+            } else if (XBF16) {
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     const uint4 v = *reinterpret_cast<const uint4*>(rs + (c * PROD + tid) * 16);
@@ -217,14 +289,21 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
                                    f32x2_to_f16x2(v.z, v.w));
                 }
             }
-            // W: 32 weights (4 words) of row wr, group wh of the k-step
+            // W: 32 weights of row wr, group wh of the k-step
             {
-                const uint4 w4 = *reinterpret_cast<const uint4*>(rs + R::X + tid * 16);
-                const uint32_t sc = *reinterpret_cast<const uint32_t*>(rs + R::X + RAW_W + tid * 4);
+                const uint32_t sc = *reinterpret_cast<const uint32_t*>(rs + R::X + R::WB + tid * 4);
                 const uint32_t s2 = (wh ? (sc >> 16) : (sc & 0xFFFFu)) * 0x10001u;
-                const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+                if (TERN) {
+                    const uint2 w2 = *reinterpret_cast<const uint2*>(rs + R::X + tid * 8);
 #pragma unroll
-                for (int c = 0; c < 4; c++) *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_word(ws[c], s2);
+                    for (int c = 0; c < 4; c++)
+                        *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_tern8(c < 2 ? w2.x : w2.y, c & 1, s2);
+                } else {
+                    const uint4 w4 = *reinterpret_cast<const uint4*>(rs + R::X + tid * 16);
+                    const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++) *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_word(ws[c], s2);
+                }
             }
             // generic-proxy writes -> visible to the tensor core (async proxy)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -302,19 +381,19 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
     }
 }
 
-template <bool XBF16>
+template <int MODE>
 int launch_gemm(tb_ctx* ctx, const GemmArgs& a)
 {
     static bool attr_set[64] = {};
     if (ctx->device >= 64 || !attr_set[ctx->device]) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_int4<XBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg<XBF16>::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_int4<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg<MODE>::SMEM);
         if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm attribute: %s", cudaGetErrorString(e));
         if (ctx->device < 64) attr_set[ctx->device] = true;
     }
-    static_assert(Cfg<XBF16>::SMEM <= 227 * 1024, "shared memory");
-    cudaError_t e = tb_launch(ctx, k_gemm_int4<XBF16>, dim3(a.N / BN, a.M / BM), dim3(THREADS),
-                              (size_t)Cfg<XBF16>::SMEM, a);
+    static_assert(Cfg<MODE>::SMEM <= 227 * 1024, "shared memory");
+    cudaError_t e = tb_launch(ctx, k_gemm_int4<MODE>, dim3(a.N / BN, a.M / BM), dim3(THREADS),
+                              (size_t)Cfg<MODE>::SMEM, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -331,8 +410,30 @@ int tb_gemm_int4_impl(tb_ctx* ctx, float* y, const void* x, int x_bf16, const ui
     TB_REQUIRE(ctx, M / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_int4: shape too large");
     TB_REQUIRE(ctx, TB_ALIGNED(x, 16) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) && TB_ALIGNED(y, 16),
                "gemm_int4: x, pack, y 16-byte and scales 4-byte aligned");
-    GemmArgs a{x, pack, scales, y, (int)M, (int)N, (int)K, acc ? 1 : 0, ctx->dev_error};
-    return x_bf16 ? launch_gemm<true>(ctx, a) : launch_gemm<false>(ctx, a);
+    GemmArgs a{x, nullptr, pack, scales, y, (int)M, (int)N, (int)K, acc ? 1 : 0, ctx->dev_error};
+    return x_bf16 ? launch_gemm<X_BF16>(ctx, a) : launch_gemm<X_F32>(ctx, a);
+}
+
+int tb_gemm_tern_wgsl_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                           const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc)
+{
+    TB_REQUIRE(ctx, y && xq && xs && pack && scales, "null pointer");
+    TB_REQUIRE(ctx, M > 0 && M % BM == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
+               "gemm_tern: M %% %d, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BM, BN, BK,
+               (long long)M, (long long)N, (long long)K);
+    TB_REQUIRE(ctx, M / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_tern: shape too large");
+    TB_REQUIRE(ctx, TB_ALIGNED(xq, 16) && TB_ALIGNED(xs, 4) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) &&
+                        TB_ALIGNED(y, 16),
+               "gemm_tern: xq, pack, y 16-byte and xs, scales 4-byte aligned");
+    GemmArgs a{xq, xs, pack, scales, y, (int)M, (int)N, (int)K, acc ? 1 : 0, ctx->dev_error};
+    return launch_gemm<X_Q8_TERN>(ctx, a);
+}
+
+extern "C" TB_API int tb_gemm_tern_wgsl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                                        const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return tb_gemm_tern_wgsl_impl(ctx, y, xq, xs, pack, scales, M, N, K, acc);
 }
 
 extern "C" TB_API int tb_gemm_int4_g32(tb_ctx* ctx, float* y, const void* x, int x_bf16, const uint32_t* pack,

@@ -23,6 +23,13 @@
 //  * A warp owns a row of the staged block, its lanes the row's 16-byte groups
 //    (conflict-free shared-memory reads), reduced with a shuffle tree; lane 0
 //    writes (optionally += y, the fused residual; or silu(g)*u for gate/up).
+//  * Ternary weights in the WebGPU layout (models/qwen3.js:3427-3469: 16 2-bit
+//    codes w+1 per u32, weight k = 16w+4s+b at bits 8b+2s, f16 scales [N][K/32])
+//    stream through the same row blocks at 8 bytes per 32-group.  Their int8
+//    activation is staged in natural k order, so (word >> 2s) & 0x03030303 meets
+//    x[16w+4s .. 16w+4s+3] in dp4a byte lanes, and (c-1)*x = c*x - x turns the
+//    sign decode into one subtraction of the group's sum of x (gemvTern2Wgsl,
+//    qwen3.js:449-503; gateupTern2Wgsl, qwen3.js:747-810).
 #include "tb_act.cuh"
 
 namespace {
@@ -33,7 +40,9 @@ constexpr int SMEM_HDR = 512;   // mbarriers (64 B) + reduction scratch (>= 72 f
 constexpr uint32_t WAIT_TRIES = 1000;
 constexpr int ERR_WAIT_TIMEOUT = 0x6d01;
 
-enum Kind { KIND_Q8 = 0, KIND_GATEUP = 1, KIND_F32 = 2 };
+enum Kind { KIND_Q8 = 0, KIND_GATEUP = 1, KIND_F32 = 2, KIND_TERN = 3, KIND_GATEUP_TERN = 4 };
+__host__ __device__ constexpr bool kind_tern(int k) { return k == KIND_TERN || k == KIND_GATEUP_TERN; }
+__host__ __device__ constexpr bool kind_gateup(int k) { return k == KIND_GATEUP || k == KIND_GATEUP_TERN; }
 enum ActSrc { ACT_PREQ = 0, ACT_F32 = 1, ACT_RMSNORM = 2 };
 
 struct Mat {
@@ -47,6 +56,7 @@ struct Mat {
 struct Args {
     Mat m[4];
     int count, nrb, RB, K, acc;
+    int wrow_bytes;        // packed weight bytes per row: K/2 (int4) or K/4 (ternary)
     int act_src;
     const float* x;        // f32 [B][K] (ACT_F32 / ACT_RMSNORM)
     const int8_t* xq;      // int8 [B][K]   (ACT_PREQ)
@@ -115,7 +125,7 @@ __device__ void issue_block(const Args& a, int rb, unsigned char* stage, uint64_
 {
     const int G = a.K >> 5;
     const Block bl = block_of(a, rb, gateup);
-    const uint32_t wb = (uint32_t)bl.nrows * (a.K >> 1);
+    const uint32_t wb = (uint32_t)bl.nrows * a.wrow_bytes;
     const uint32_t sb = (uint32_t)bl.nrows * G * 2;
     const bool sbulk = scales_bulk(bl.nrows, G);
     const int nm = gateup ? 2 : 1;
@@ -123,8 +133,8 @@ __device__ void issue_block(const Args& a, int rb, unsigned char* stage, uint64_
     for (int s = 0; s < nm; s++) {
         const Mat& M = a.m[gateup ? s : bl.mi];
         unsigned char* dst = stage + s * a.slot_bytes;
-        bulk_g2s(dst, M.pack + (size_t)bl.row0 * (a.K >> 3), wb, bar);
-        if (sbulk) bulk_g2s(dst + (size_t)a.RB * (a.K >> 1), M.scales + (size_t)bl.row0 * G, sb, bar);
+        bulk_g2s(dst, reinterpret_cast<const unsigned char*>(M.pack) + (size_t)bl.row0 * a.wrow_bytes, wb, bar);
+        if (sbulk) bulk_g2s(dst + (size_t)a.RB * a.wrow_bytes, M.scales + (size_t)bl.row0 * G, sb, bar);
     }
 }
 
@@ -177,7 +187,9 @@ __device__ __forceinline__ void load_rows_swz(const float4* __restrict__ src, in
 
 // Q8 layout per (b, g): lo = (e0,o0,e1,o1), hi = (e2,o2,e3,o3) (e_w / o_w = even /
 // odd k of weight word w, one int8 per byte), s8 = 8*sum(x), sf = scale.
-template <int B>
+// NAT (ternary weights): lo / hi = x[0..15] / x[16..31] in natural order and
+// s8 = sum(x).
+template <int B, bool NAT>
 __device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbuf_floats, float* red,
                          const uint16_t* nws)
 {
@@ -202,9 +214,15 @@ __device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbu
                 s = __dp4a((int)w[2 * j], 0x01010101, s);
                 s = __dp4a((int)w[2 * j + 1], 0x01010101, s);
             }
-            xlo[i] = make_uint4(e[0], o[0], e[1], o[1]);
-            xhi[i] = make_uint4(e[2], o[2], e[3], o[3]);
-            xs8[i] = 8 * s;
+            if (NAT) {
+                xlo[i] = p;
+                xhi[i] = q;
+                xs8[i] = s;
+            } else {
+                xlo[i] = make_uint4(e[0], o[0], e[1], o[1]);
+                xhi[i] = make_uint4(e[2], o[2], e[3], o[3]);
+                xs8[i] = 8 * s;
+            }
             xsf[i] = a.xs[(size_t)b * G + g];
         }
         return;
@@ -270,24 +288,38 @@ __device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbu
             const float scale = q8_scale(mx), is = q8_inv(scale);
             uint32_t wd[4];
             int sum = 0;
+            if (NAT) {
 #pragma unroll
-            for (int w = 0; w < 2; w++) {
-                uint32_t e = 0, o = 0;
+                for (int w = 0; w < 4; w++) {
+                    uint32_t n = 0;
 #pragma unroll
-                for (int h = 0; h < 4; h++) {
-                    const int qe = q8_quant(v[8 * w + 2 * h], is), qo = q8_quant(v[8 * w + 2 * h + 1], is);
-                    sum += qe + qo;
-                    e |= ((uint32_t)qe & 0xffu) << (8 * h);
-                    o |= ((uint32_t)qo & 0xffu) << (8 * h);
+                    for (int h = 0; h < 4; h++) {
+                        const int qv = q8_quant(v[4 * w + h], is);
+                        sum += qv;
+                        n |= ((uint32_t)qv & 0xffu) << (8 * h);
+                    }
+                    wd[w] = n;
                 }
-                wd[2 * w] = e;
-                wd[2 * w + 1] = o;
+            } else {
+#pragma unroll
+                for (int w = 0; w < 2; w++) {
+                    uint32_t e = 0, o = 0;
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const int qe = q8_quant(v[8 * w + 2 * h], is), qo = q8_quant(v[8 * w + 2 * h + 1], is);
+                        sum += qe + qo;
+                        e |= ((uint32_t)qe & 0xffu) << (8 * h);
+                        o |= ((uint32_t)qo & 0xffu) << (8 * h);
+                    }
+                    wd[2 * w] = e;
+                    wd[2 * w + 1] = o;
+                }
             }
             sum += __shfl_xor_sync(0xffffffffu, sum, 1);
             if (live) {
                 const int i = (b0 + bb) * G + g;
                 (h2 ? xhi : xlo)[i] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-                if (h2 == 0) { xs8[i] = 8 * sum; xsf[i] = scale; }
+                if (h2 == 0) { xs8[i] = NAT ? sum : 8 * sum; xsf[i] = scale; }
             }
         }
         __syncthreads();   // xbuf and red are reused by the next chunk
@@ -347,6 +379,35 @@ __device__ __forceinline__ void item_q8(const uint4 w, const float s, const unsi
     }
 }
 
+// One ternary 32-group (two code words) against the natural-order int8 row:
+// sum (c-1)*x = sum_s dp4a((word >> 2s) & 0x03030303, x word s) - sum(x).
+template <int B>
+__device__ __forceinline__ void item_tern(const uint2 w, const float s, const unsigned char* act, int G, int g, float* acc)
+{
+    const uint4* xlo = reinterpret_cast<const uint4*>(act);
+    const uint4* xhi = xlo + B * G;
+    const int* xsum = reinterpret_cast<const int*>(xhi + B * G);
+    const float* xsf = reinterpret_cast<const float*>(xsum + B * G);
+    constexpr uint32_t M = 0x03030303u;
+    const uint32_t a0 = w.x & M, a1 = (w.x >> 2) & M, a2 = (w.x >> 4) & M, a3 = (w.x >> 6) & M;
+    const uint32_t c0 = w.y & M, c1 = (w.y >> 2) & M, c2 = (w.y >> 4) & M, c3 = (w.y >> 6) & M;
+#pragma unroll
+    for (int b = 0; b < B; b++) {
+        const int i = b * G + g;
+        const uint4 xl = xlo[i], xh = xhi[i];
+        int d = -xsum[i];
+        d = __dp4a((int)a0, (int)xl.x, d);
+        d = __dp4a((int)a1, (int)xl.y, d);
+        d = __dp4a((int)a2, (int)xl.z, d);
+        d = __dp4a((int)a3, (int)xl.w, d);
+        d = __dp4a((int)c0, (int)xh.x, d);
+        d = __dp4a((int)c1, (int)xh.y, d);
+        d = __dp4a((int)c2, (int)xh.z, d);
+        d = __dp4a((int)c3, (int)xh.w, d);
+        acc[b] = fmaf(s * xsf[i], (float)d, acc[b]);
+    }
+}
+
 // One weight word (8 nibbles, k = 8wi..8wi+7) against x[k..k+7] = (xa, xb).
 __device__ __forceinline__ float2 word_f32(uint32_t word, float4 xa, float4 xb, float2 d)
 {
@@ -399,7 +460,8 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
     float* xbuf = reinterpret_cast<float*>(act + a.act_bytes);
     uint16_t* nws = reinterpret_cast<uint16_t*>(act + a.act_bytes + a.xbuf_bytes);
     unsigned char* stages = act + a.act_bytes + a.xbuf_bytes + a.nw_bytes;
-    constexpr bool gateup = KIND == KIND_GATEUP;
+    constexpr bool gateup = kind_gateup(KIND);
+    constexpr bool TERN = kind_tern(KIND);
     constexpr int NM = gateup ? 2 : 1;
     const int stage_bytes = NM * a.slot_bytes;
     const int G = a.K >> 5;
@@ -428,7 +490,7 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
     tb_pdl_wait();
     tb_pdl_trigger();
     if (KIND == KIND_F32) stage_f32<B>(a, act, red, nws);
-    else stage_q8<B>(a, act, xbuf, a.xbuf_bytes >> 2, red, nws);
+    else stage_q8<B, TERN>(a, act, xbuf, a.xbuf_bytes >> 2, red, nws);
     __syncthreads();
 
     // f32 activation of a single row kept in registers (groups lane, lane+32),
@@ -470,9 +532,12 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
                 for (int s = 0; s < NM; s++) {
                     const unsigned char* slot = stg + s * a.slot_bytes;
                     const uint4* wrow = reinterpret_cast<const uint4*>(slot) + (size_t)r * G;
-                    const uint16_t* srow = sbulk ? reinterpret_cast<const uint16_t*>(slot + (size_t)a.RB * (a.K >> 1)) + (size_t)r * G
+                    const uint16_t* srow = sbulk ? reinterpret_cast<const uint16_t*>(slot + (size_t)a.RB * a.wrow_bytes) + (size_t)r * G
                                                  : a.m[gateup ? s : bl.mi].scales + (size_t)(bl.row0 + r) * G;
-                    if (XREG && xreg) {
+                    if (TERN) {
+                        const uint2* trow = reinterpret_cast<const uint2*>(slot) + (size_t)r * G;
+                        for (int g = lane; g < G; g += 32) item_tern<B>(trow[g], tb_h2f(srow[g]), act, G, g, acc[s]);
+                    } else if (XREG && xreg) {
                         if (lane < G) {
                             const uint4 w = wrow[lane];
                             float2 d = make_float2(0.0f, 0.0f);
@@ -550,8 +615,9 @@ int act_bytes_for(int kind, int B, int G) { return kind == KIND_F32 ? B * G * 12
 int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count, bool norm, Plan& p)
 {
     const int G = K / 32;
-    const int nm = kind == KIND_GATEUP ? 2 : 1;
-    const int mats = kind == KIND_GATEUP ? 1 : count;
+    const int nm = kind_gateup(kind) ? 2 : 1;
+    const int mats = kind_gateup(kind) ? 1 : count;
+    const int wrow = kind_tern(kind) ? K / 4 : K / 2;
     long long rows = 0;
     for (int i = 0; i < mats; i++) rows += Ns[i];
     p.act_bytes = (act_bytes_for(kind, B, G) + 127) & ~127;
@@ -564,7 +630,7 @@ int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count,
     int RB = 8;
     while (RB < 64 && rows / (2 * RB) >= target) RB *= 2;
     for (;; RB /= 2) {
-        const int wb = RB * (K / 2), sb = RB * G * 2;
+        const int wb = RB * wrow, sb = RB * G * 2;
         p.slot_bytes = (wb + sb + 127) & ~127;
         const int per_stage = nm * p.slot_bytes;
         int nrb = 0;
@@ -660,7 +726,8 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
         int rc = check_mat(ctx, packs[i], scales[i], ys[i], Ns[i], K);
         if (rc) return rc;
     }
-    if (kind == KIND_GATEUP) TB_REQUIRE(ctx, Ns[0] == Ns[1], "gate and up must have the same rows");
+    if (kind_gateup(kind)) TB_REQUIRE(ctx, Ns[0] == Ns[1], "gate and up must have the same rows");
+    if (kind_tern(kind)) TB_REQUIRE(ctx, K % 64 == 0, "ternary weights need K %% 64 == 0 (got %lld)", (long long)K);
     // f32 rows take 4 bytes per element of shared memory: split big batches
     // into launches of rows that fit (each launch covers its own rows of y).
     const int bmax = kind == KIND_F32 ? std::max(1, (int)((96 * 1024) / (K * 4))) : 8;
@@ -683,12 +750,13 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
     for (int i = 0; i < 4; i++) {
         if (i < count) {
             a.m[i] = Mat{packs[i], scales[i], ys[i], (int)Ns[i], rb};
-            if (kind != KIND_GATEUP) rb += tb_cdiv(Ns[i], p.RB);
+            if (!kind_gateup(kind)) rb += tb_cdiv(Ns[i], p.RB);
         } else {
             a.m[i] = Mat{nullptr, nullptr, nullptr, 0, 1 << 30};
         }
     }
-    if (kind == KIND_GATEUP) a.m[1].rb_begin = 0;
+    if (kind_gateup(kind)) a.m[1].rb_begin = 0;
+    a.wrow_bytes = kind_tern(kind) ? (int)(K / 4) : (int)(K / 2);
     a.nrb = p.nrb;
     a.RB = p.RB;
     a.nst = p.nst;
@@ -699,6 +767,8 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
     switch (kind) {
     case KIND_Q8: return launch_kind<KIND_Q8>(ctx, a, p, batch);
     case KIND_GATEUP: return launch_kind<KIND_GATEUP>(ctx, a, p, batch);
+    case KIND_TERN: return launch_kind<KIND_TERN>(ctx, a, p, batch);
+    case KIND_GATEUP_TERN: return launch_kind<KIND_GATEUP_TERN>(ctx, a, p, batch);
     default: return launch_kind<KIND_F32>(ctx, a, p, batch);
     }
 }
@@ -728,6 +798,12 @@ int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack
                      int64_t N, int64_t K, int batch, int acc)
 {
     return run(ctx, KIND_F32, 1, &y, &pack, &scales, &N, act_f32(x, nullptr, 0.0f), K, batch, acc);
+}
+int tb_gemv_tern_wgsl_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                           const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
+                           float eps, int64_t K, int batch, int acc)
+{
+    return run(ctx, KIND_TERN, count, ys, packs, scales, Ns, act_f32(x, normw, eps), K, batch, acc);
 }
 
 extern "C" {
@@ -801,6 +877,56 @@ TB_API int tb_gateup_silu_int4_dp4a(tb_ctx* ctx, float* swi, const float* x, con
     const uint16_t* scs[2] = {gscales, uscales};
     int64_t Ns[2] = {I, I};
     return run(ctx, KIND_GATEUP, 2, ys, packs, scs, Ns, act_f32(x, norm_w16, eps), H, batch, 0);
+}
+
+// ---- ternary weights, WebGPU layout ----------------------------------------------
+// gemvTern_only (models/qwen3.js:548-556) against a pre-quantized QUANTQ8 row;
+// the per-group sum of x is recomputed from xq in the prologue (the same exact
+// integer as the reference's xsum buffer, so no xsum argument).
+TB_API int tb_gemv_tern_wgsl_q8(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                                const uint16_t* scales, int64_t N, int64_t K, int batch, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return run(ctx, KIND_TERN, 1, &y, &pack, &scales, &N, act_preq(xq, xs), K, batch, acc);
+}
+
+// quantQ8 + gemvTern_only for up to four matrices sharing one activation
+// (projGemv at the q/k/v call sites, qwen3.js:558-561, 3982-3984), with the
+// optional fused RMSNorm of RMSNORMQ.
+TB_API int tb_gemv_tern_wgsl_dp4a_multi(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                                        const uint16_t* const* scales, const int64_t* Ns, const float* x,
+                                        const uint16_t* norm_w16, float eps, int64_t K, int batch, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, ys && packs && scales && Ns, "null array");
+    return run(ctx, KIND_TERN, count, ys, packs, scales, Ns, act_f32(x, norm_w16, eps), K, batch, acc);
+}
+
+// gate+up+SiLU of ternary weights (gateupTern2Wgsl, qwen3.js:747-810, routed by
+// gateUpSiluDP4_only, qwen3.js:861-870).
+TB_API int tb_gateup_silu_tern_wgsl_q8(tb_ctx* ctx, float* swi, const int8_t* xq, const float* xs,
+                                       const uint32_t* gpack, const uint16_t* gscales, const uint32_t* upack,
+                                       const uint16_t* uscales, int64_t I, int64_t H, int batch)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    float* ys[2] = {swi, swi};
+    const uint32_t* packs[2] = {gpack, upack};
+    const uint16_t* scs[2] = {gscales, uscales};
+    int64_t Ns[2] = {I, I};
+    return run(ctx, KIND_GATEUP_TERN, 2, ys, packs, scs, Ns, act_preq(xq, xs), H, batch, 0);
+}
+
+TB_API int tb_gateup_silu_tern_wgsl_dp4a(tb_ctx* ctx, float* swi, const float* x, const uint16_t* norm_w16,
+                                         float eps, const uint32_t* gpack, const uint16_t* gscales,
+                                         const uint32_t* upack, const uint16_t* uscales, int64_t I, int64_t H,
+                                         int batch)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    float* ys[2] = {swi, swi};
+    const uint32_t* packs[2] = {gpack, upack};
+    const uint16_t* scs[2] = {gscales, uscales};
+    int64_t Ns[2] = {I, I};
+    return run(ctx, KIND_GATEUP_TERN, 2, ys, packs, scs, Ns, act_f32(x, norm_w16, eps), H, batch, 0);
 }
 
 }  // extern "C"

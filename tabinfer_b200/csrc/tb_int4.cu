@@ -15,24 +15,6 @@ namespace {
 // quant-on-arrival (bit-exact with quantizeInt4Bf16, models/qwen3.js:3405-3426)
 // ---------------------------------------------------------------------------
 
-// models/qwen3.js:3357-3374: f16 bits of an f32, mantissa rounded half-up.
-__device__ __forceinline__ uint32_t js_f32_to_f16(float val)
-{
-    uint32_t x = __float_as_uint(val);
-    uint32_t sign = (x >> 16) & 0x8000u, ex = (x >> 23) & 0xffu, mant = x & 0x7fffffu;
-    if (ex == 0xffu) return sign | (mant ? 0x7e00u : 0x7c00u);
-    int e = (int)ex - 127 + 15;
-    if (e >= 31) return sign | 0x7c00u;
-    if (e <= 0) {
-        if (e < -10) return sign;
-        uint32_t m = mant | 0x800000u;
-        int shift = 14 - e;
-        uint32_t half = (m >> shift) + ((m >> (shift - 1)) & 1u);
-        return sign | half;
-    }
-    return sign | ((((uint32_t)e << 10) | (mant >> 13)) + ((mant >> 12) & 1u));
-}
-
 // JavaScript Math.round on a double (ties toward +inf; NaN/Inf unchanged).
 __device__ __forceinline__ double js_round(double v)
 {
@@ -83,6 +65,43 @@ __global__ void __launch_bounds__(256) k_quant_int4_g32(const uint16_t* __restri
         reinterpret_cast<uint4*>(pack)[gi] = make_uint4(words[0], words[1], words[2], words[3]);
         scales[gi] = (uint16_t)sb;
     }
+}
+
+// Ternary detection + pack of the WebGPU layout (quantizeTernaryBf16,
+// models/qwen3.js:3435-3469).  A warp takes 64 consecutive weights of a row
+// (two 32-groups), lane l the bf16 pair 2l, 2l+1.  Per group: mx = max of the
+// magnitude bits (bits & 0x7fff); the matrix is not ternary when any nonzero
+// magnitude sits more than TOL = 2 ulps below its group's mx (then *fail is
+// set and the pack is not used); code = 1 for a zero magnitude, else 0 / 2 by
+// sign; weight k lands at bits 8*(k%4) + 2*((k/4)%4) of word k/16 (OR-reduced
+// over the 8 lanes of a word); scale = bf16ToF16bits(mx).
+__global__ void __launch_bounds__(256) k_quant_tern_wgsl(const uint32_t* __restrict__ w, uint32_t* __restrict__ pack,
+                                                         uint16_t* __restrict__ scales, long long nchunks,
+                                                         int* __restrict__ fail)
+{
+    tb_pdl_wait();
+    constexpr uint32_t TOL = 2;
+    const int lane = threadIdx.x & 31;
+    const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+    bool bad = false;
+    for (long long c = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); c < nchunks; c += nwarps) {
+        const uint32_t u = __ldg(w + c * 32 + lane);   // chunk c = row-major weights 64c .. 64c+63
+        const uint32_t lo = u & 0xffffu, hi = u >> 16;
+        const uint32_t m0 = lo & 0x7fffu, m1 = hi & 0x7fffu;
+        uint32_t mx = max(m0, m1);
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        bad |= (m0 != 0u && mx - m0 > TOL) || (m1 != 0u && mx - m1 > TOL);
+        const uint32_t c0 = m0 == 0u ? 1u : ((lo & 0x8000u) ? 0u : 2u);
+        const uint32_t c1 = m1 == 0u ? 1u : ((hi & 0x8000u) ? 0u : 2u);
+        const int k0 = (2 * lane) & 15, k1 = k0 + 1;   // positions inside the 16-weight word
+        uint32_t word = (c0 << (((k0 & 3) << 3) + ((k0 >> 2) & 3) * 2)) | (c1 << (((k1 & 3) << 3) + ((k1 >> 2) & 3) * 2));
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+        if ((lane & 7) == 0) pack[c * 4 + (lane >> 3)] = word;
+        if ((lane & 15) == 0) scales[c * 2 + (lane >> 4)] = (uint16_t)js_f32_to_f16(__uint_as_float(mx << 16));
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(fail, 1);
 }
 
 // bf16ToF16bits, models/qwen3.js:3386-3390: the loader's f16 copy of the
@@ -182,6 +201,26 @@ TB_API int tb_quant_int4_g32(tb_ctx* ctx, const uint16_t* w, uint32_t* pack, uin
     TB_REQUIRE(ctx, N > 0 && K > 0 && K % 32 == 0, "bad shape N=%lld K=%lld (K%%32 must be 0)", (long long)N, (long long)K);
     TB_REQUIRE(ctx, TB_ALIGNED(w, 16) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 2), "misaligned pointer");
     return tb_quant_int4_strided_impl(ctx, w, K, pack, scales, N, K);
+}
+
+TB_API int tb_quant_tern_wgsl_bf16(tb_ctx* ctx, const uint16_t* w, uint32_t* pack, uint16_t* scales, int64_t N,
+                                  int64_t K, int* nonternary)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, w && pack && scales && nonternary, "null pointer");
+    TB_REQUIRE(ctx, N > 0 && K > 0, "bad shape N=%lld K=%lld", (long long)N, (long long)K);
+    TB_REQUIRE(ctx, TB_ALIGNED(w, 4) && TB_ALIGNED(pack, 4) && TB_ALIGNED(scales, 2) && TB_ALIGNED(nonternary, 4),
+               "misaligned pointer");
+    // K % 64 != 0: not representable in this layout, the caller keeps int4 (qwen3.js:3436)
+    cudaError_t e = cudaMemsetAsync(nonternary, K % 64 ? 1 : 0, sizeof(int), ctx->stream);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "memset: %s", cudaGetErrorString(e));
+    if (K % 64) return TB_OK;
+    const long long nchunks = N * (K / 64);
+    int grid = (int)std::min<long long>((nchunks + 7) / 8, (long long)ctx->num_sms * 16);
+    e = tb_launch(ctx, k_quant_tern_wgsl, dim3(grid), dim3(256), 0, reinterpret_cast<const uint32_t*>(w), pack,
+                  scales, nchunks, nonternary);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_tern_wgsl launch: %s", cudaGetErrorString(e));
+    return TB_OK;
 }
 
 TB_API int tb_convert_bf16_f16(tb_ctx* ctx, const uint16_t* in, uint16_t* out, int64_t n)

@@ -50,3 +50,12 @@ int tb_tp_argmax_merge_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int6
 // prefill GEMM Y (+)= f16(X) . f16(deq(W))^T on tcgen05 (M % 128, N % 256, K % 64)
 int tb_gemm_int4_impl(tb_ctx* ctx, float* y, const void* x, int x_bf16, const uint32_t* pack, const uint16_t* scales,
                       int64_t M, int64_t N, int64_t K, int acc);
+// the same GEMM for ternary weights (WebGPU layout) against QUANTQ8T int8 rows
+int tb_gemm_tern_wgsl_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                           const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc);
+// quantQ8 (+ optional RMSNorm) and the ternary (WebGPU layout) GEMV, batch 1..8
+int tb_gemv_tern_wgsl_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                           const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
+                           float eps, int64_t K, int batch, int acc);
+// per-32 int8 quantization of T rows (QUANTQ8 / QUANTQ8T)
+int tb_quant_q8_impl(tb_ctx* ctx, const float* x, int8_t* xq, float* xs, int32_t* xsum16, int64_t T, int64_t K);

@@ -1,6 +1,6 @@
 // tb_linear.cu -- the router-level entry points that quantize an f32
 // activation into context scratch and run the matching GEMV:
-// linearQ (models/qwen3.js:1588-1608) and Model::linear
+// linearQ (models/qwen3.js:1588-1608, both weight kinds) and Model::linear
 // (native/crates/n2-core/src/model.rs:316-339).
 #include "tb_internal.h"
 
@@ -25,6 +25,31 @@ TB_API int tb_linear_int4(tb_ctx* ctx, float* y, const float* x, const uint32_t*
     }
     // quantQ8 / QUANTQ8T runs inside the GEMV prologue (bit-identical int8 rows)
     return tb_gemv_dp4a_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
+}
+
+// linearQ's ternary branch (qwen3.js:1594-1598).  T <= 8 runs the ternary GEMV
+// with quantQ8 in its prologue: per 32-group the same exact int32 sum and f32
+// scaling as the reference's gemvTern (T = 1) and gemmTern tiles (T > 1).
+// T > 8 quantizes the rows (QUANTQ8T) into context scratch and runs the
+// tcgen05 GEMM on them (gemmTern).
+TB_API int tb_linear_tern_wgsl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
+                               int64_t T, int64_t N, int64_t K, int acc)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, T >= 1, "T must be >= 1");
+    TB_REQUIRE(ctx, K > 0 && K % 64 == 0, "K must be a positive multiple of 64");
+    if (T <= 8) return tb_gemv_tern_wgsl_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
+    if (T % 128 != 0 || N % 256 != 0)
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED,
+                       "linear_tern_wgsl: T=%lld > 8 needs T %% 128 == 0 and N %% 256 == 0 (prefill GEMM)", (long long)T);
+    const size_t xq_b = up256((size_t)T * K), xs_b = up256((size_t)T * (K / 32) * 4);
+    unsigned char* scr = static_cast<unsigned char*>(tb_ctx_scratch(ctx, xq_b + xs_b));
+    if (!scr) return TB_ERR_NOMEM;
+    int8_t* xq = reinterpret_cast<int8_t*>(scr);
+    float* xs = reinterpret_cast<float*>(scr + xq_b);
+    int rc = tb_quant_q8_impl(ctx, x, xq, xs, nullptr, T, K);
+    if (rc) return rc;
+    return tb_gemm_tern_wgsl_impl(ctx, y, xq, xs, pack, scales, T, N, K, acc);
 }
 
 TB_API int tb_linear_tern(tb_ctx* ctx, float* y, const float* x, const uint8_t* codes, const float* scales, int64_t T,

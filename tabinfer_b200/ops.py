@@ -320,6 +320,110 @@ def gate_up_silu_dp4(xq, xs, gpack, gscales, upack, uscales, swi=None):
 
 
 # --------------------------------------------------------------------------
+# ternary, WebGPU layout (models/qwen3.js): pack u32 [N,K/16], f16 scales [N,K/32]
+# --------------------------------------------------------------------------
+
+def quantize_tern_bf16(w):
+    """quantizeTernaryBf16 (qwen3.js:3435-3469): bf16 [N,K] -> (pack int32 [N,K/16],
+    scales f16 [N,K/32]), or None when the matrix is not ternary (the reference's
+    null, after which its loader quantizes to int4).  Synchronises to read the flag."""
+    N, K = w.shape
+    pack = torch.empty((N, max(K // 16, 1)), dtype=torch.int32, device=w.device)
+    scales = torch.empty((N, max(K // 32, 1)), dtype=torch.float16, device=w.device)
+    flag = torch.empty(1, dtype=torch.int32, device=w.device)
+    c = _ctx(w)
+    c.check(LIB.tb_quant_tern_wgsl_bf16(c.h, _p(w), _p(pack), _p(scales), N, K, _p(flag)), "quant_tern_wgsl_bf16")
+    if int(flag.item()) != 0:
+        return None
+    return pack, scales
+
+
+def gemv_tern_wgsl(xq, xs, pack, scales, y=None, acc=False):
+    """gemvTern_only (qwen3.js:548-556) against a QUANTQ8 activation; batch = xq rows."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    B, K = xq2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((B, N), dtype=torch.float32, device=xq.device)
+    c = _ctx(xq)
+    c.check(LIB.tb_gemv_tern_wgsl_q8(c.h, _p(y), _p(xq2), _p(xs), _p(pack), _p(scales), N, K, B, 1 if acc else 0),
+            "gemv_tern_wgsl_q8")
+    return y
+
+
+def gemv_tern_wgsl_dp4a_multi(x, mats, norm_w=None, eps=1e-6, ys=None, acc=False):
+    """quantQ8 (or rmsnormQ) + projGemv of ternary q/k/v (qwen3.js:558-561, 3981-3984),
+    one launch.  mats: [(pack, scales)]."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    n = len(mats)
+    if ys is None:
+        ys = [torch.zeros((B, p.shape[0]), dtype=torch.float32, device=x.device) for p, _ in mats]
+    arr_y = (P * n)(*[y.data_ptr() for y in ys])
+    arr_p = (P * n)(*[p.data_ptr() for p, _ in mats])
+    arr_s = (P * n)(*[s.data_ptr() for _, s in mats])
+    arr_n = (ctypes.c_int64 * n)(*[p.shape[0] for p, _ in mats])
+    c = _ctx(x)
+    c.check(LIB.tb_gemv_tern_wgsl_dp4a_multi(c.h, n, ctypes.cast(arr_y, P), ctypes.cast(arr_p, P),
+                                             ctypes.cast(arr_s, P), ctypes.cast(arr_n, P), _p(x2), _p(norm_w),
+                                             float(eps), K, B, 1 if acc else 0), "gemv_tern_wgsl_dp4a_multi")
+    return ys
+
+
+def gate_up_silu_tern(xq, xs, gpack, gscales, upack, uscales, swi=None):
+    """gateUpSiluDP4_only's ternary branch (qwen3.js:861-870, gateupTern2Wgsl :747-810)."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    B, H = xq2.shape
+    I = gpack.shape[0]
+    if swi is None:
+        swi = torch.empty((B, I), dtype=torch.float32, device=xq.device)
+    c = _ctx(xq)
+    c.check(LIB.tb_gateup_silu_tern_wgsl_q8(c.h, _p(swi), _p(xq2), _p(xs), _p(gpack), _p(gscales), _p(upack),
+                                            _p(uscales), I, H, B), "gateup_silu_tern_wgsl_q8")
+    return swi
+
+
+def gate_up_silu_tern_dp4a(x, gpack, gscales, upack, uscales, norm_w=None, eps=1e-6, swi=None):
+    """gateUpSiluQ's ternary branch (qwen3.js:730): quantQ8 (or rmsnormQ) + gateupTern2, one launch."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, H = x2.shape
+    I = gpack.shape[0]
+    if swi is None:
+        swi = torch.empty((B, I), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_gateup_silu_tern_wgsl_dp4a(c.h, _p(swi), _p(x2), _p(norm_w), float(eps), _p(gpack),
+                                              _p(gscales), _p(upack), _p(uscales), I, H, B),
+            "gateup_silu_tern_wgsl_dp4a")
+    return swi
+
+
+def gemm_tern(xq, xs, pack, scales, y=None, acc=False):
+    """gemmTern (qwen3.js:1410-1420) on the tensor cores from QUANTQ8T rows:
+    y[M,N] (+)= f16(xs*xq) . f16((c-1)*s)^T."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    M, K = xq2.shape
+    N = pack.shape[0]
+    y = y if y is not None else torch.zeros((M, N), dtype=torch.float32, device=xq.device)
+    c = _ctx(xq)
+    c.check(LIB.tb_gemm_tern_wgsl(c.h, _p(y), _p(xq2), _p(xs), _p(pack), _p(scales), M, N, K, 1 if acc else 0),
+            "gemm_tern_wgsl")
+    return y
+
+
+def linear_tern_wgsl(x, pack, scales, y=None, acc=False):
+    """linearQ for a ternary weight record (qwen3.js:1594-1598), T = x rows."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, K = x2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((T, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_linear_tern_wgsl(c.h, _p(y), _p(x2), _p(pack), _p(scales), T, N, K, 1 if acc else 0),
+            "linear_tern_wgsl")
+    return y
+
+
+# --------------------------------------------------------------------------
 # ternary Q2_0_g64 (native/crates/n2-kernels/src/tern.rs)
 # --------------------------------------------------------------------------
 

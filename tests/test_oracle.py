@@ -307,3 +307,99 @@ def test_dec_nsplit_rule():
 def test_argmax_lowest_index_on_ties():
     x = np.array([1.0, 5.0, 3.0, 5.0], np.float32)
     assert oracle.argmax(x) == 1
+
+
+# ---- ternary, WebGPU layout (quantizeTernaryBf16, models/qwen3.js:3435-3469) ----
+# The reference holds no fixtures for this path and no JavaScript runtime is
+# available to run it, so the restatement is pinned by properties its comments
+# state (lossless, the dot4 lane layout, the 2-ulp tolerance) and by decoding to
+# the same matrix as the Q2_0_g64 packer, which is pinned on tern.rs's fixtures.
+
+from helpers import tern_bf16, tern_wgsl_codes  # noqa: E402
+
+
+def _bf16_val(bits):
+    return oracle.bf16_to_f32(bits).astype(np.float64)
+
+
+def test_tern_wgsl_pack_is_lossless():
+    rng = np.random.default_rng(1)
+    w = tern_bf16(rng, 16, 256)
+    pack, sc = oracle.quant_tern_wgsl(w)
+    dq = (tern_wgsl_codes(pack, 256) - 1) * np.repeat(oracle.f16_bits_to_f64(sc), 32, axis=1)
+    np.testing.assert_array_equal(dq, _bf16_val(w))
+
+
+def test_tern_wgsl_dot4_lane_layout():
+    """(word >> 2s) & 0x03030303 holds the codes of k = 16w+4s .. 16w+4s+3 in byte lanes."""
+    rng = np.random.default_rng(2)
+    w = tern_bf16(rng, 2, 128)
+    pack, _ = oracle.quant_tern_wgsl(w)
+    codes = tern_wgsl_codes(pack, 128)
+    for wi in range(8):
+        for s in range(4):
+            v = (int(pack[0, wi]) >> (2 * s)) & 0x03030303
+            lanes = [(v >> (8 * b)) & 0xFF for b in range(4)]
+            assert lanes == list(codes[0, 16 * wi + 4 * s: 16 * wi + 4 * s + 4])
+
+
+def test_tern_wgsl_matches_q2g64_decode():
+    """The same ternary matrix packed in both layouts decodes to the same weights."""
+    rng = np.random.default_rng(3)
+    N, K = 8, 512
+    s = (rng.uniform(0.01, 0.05, (N, K // 64)).astype(np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)
+    t = rng.integers(-1, 2, (N, K)).astype(np.float32)
+    w = t * np.repeat(s, 64, axis=1)
+    codes, sc64 = oracle.pack_ternary(w)
+    pack, sc = oracle.quant_tern_wgsl(oracle.f32_to_bf16_trunc(w))
+    # Q2_0_g64: code j of a 64-group in byte j % 16 at bit 2 * (j // 16)
+    j = np.arange(K) % 64
+    byte = (np.arange(K) // 64) * 16 + (j % 16)
+    c64 = (codes[:, byte] >> (2 * (j // 16))) & 3
+    dq64 = (c64.astype(np.float64) - 1) * np.repeat(sc64.astype(np.float64), 64, axis=1)
+    dqw = (tern_wgsl_codes(pack, K) - 1) * np.repeat(oracle.f16_bits_to_f64(sc), 32, axis=1)
+    np.testing.assert_array_equal(dqw, dq64)
+
+
+def test_tern_wgsl_tolerance_zero_groups_and_rejections():
+    rng = np.random.default_rng(4)
+    w = tern_bf16(rng, 6, 128, wobble=0.3, negzero=0.5)
+    pack, sc = oracle.quant_tern_wgsl(w)
+    mag = w & 0x7FFF
+    sign = (w >> 15) & 1
+    exp_codes = np.where(mag == 0, 1, np.where(sign == 1, 0, 2))
+    np.testing.assert_array_equal(tern_wgsl_codes(pack, 128), exp_codes)   # wobble snaps to +-1, -0 is 0
+    z = w.copy()
+    z[0, 32:64] = 0
+    pz, sz = oracle.quant_tern_wgsl(z)
+    assert sz[0, 1] == 0 and np.all(pz[0, 2:4] == 0x55555555)
+    bad = w.copy()
+    g = bad[5, 96:128]
+    i = int(np.flatnonzero(g & 0x7FFF)[0])
+    bad[5, 96 + i] = (int(np.max(g & 0x7FFF)) - 3) | (int(g[i]) & 0x8000)   # 3 ulps below: not ternary
+    assert oracle.quant_tern_wgsl(bad) is None
+    assert oracle.quant_tern_wgsl(w[:, :96]) is None                        # K % 64 != 0
+    assert oracle.quant_tern_wgsl(oracle.f32_to_bf16_trunc(rng.normal(0, 0.02, (4, 64)).astype(np.float32))) is None
+
+
+def test_tern_wgsl_scale_is_bf16_to_f16_half_up():
+    """scale = bf16ToF16bits(group max) (qwen3.js:3386-3390)."""
+    rng = np.random.default_rng(5)
+    w = tern_bf16(rng, 4, 64)
+    _, sc = oracle.quant_tern_wgsl(w)
+    mx = np.max(w.reshape(4, 2, 32) & 0x7FFF, axis=2)
+    vals = oracle.bf16_to_f32(mx.astype(np.uint16)).ravel()
+    exp = np.array([oracle.f32_to_f16_js(float(v)) for v in vals], np.uint16).reshape(mx.shape)
+    np.testing.assert_array_equal(sc, exp)
+
+
+def test_tern_wgsl_gemv_oracle_is_dequant_dot():
+    rng = np.random.default_rng(6)
+    w = tern_bf16(rng, 40, 256)
+    pack, sc = oracle.quant_tern_wgsl(w)
+    xq, xs, _ = oracle.quant_q8(rng.normal(0, 1, (3, 256)).astype(np.float32))
+    y = oracle.gemv_tern_wgsl_q8act(xq, xs, pack, sc)
+    xd = xq.astype(np.float64) * np.repeat(xs.astype(np.float64), 32, axis=1)
+    ref = xd @ _bf16_val(w).T
+    # the only rounding is the f32 product f32(s) * xs of each group (~6e-8)
+    np.testing.assert_allclose(y, ref, rtol=0, atol=1e-6 * np.max(np.abs(ref)))
