@@ -682,6 +682,39 @@ def profile_gemm(M, N, K):
     print("profile gemm done", flush=True)
 
 
+def profile_lm_head(kind):
+    """Three cold-L2 batch-1 lm_head GEMVs (151936 x 2048, RMSNorm fused) of one
+    weight kind -- int4_f32 (gemvQ), int4_dp4a (rmsnormQ + gemvDP4) or tern
+    (ternary WebGPU layout) -- for an ncu capture of one."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    N, K = Q17["vocab"], Q17["hidden"]
+    if kind == "tern":
+        pack, sc = _tern_weights(dev, g, N, K)
+    else:
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        pack, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+        del w
+    nw = (1 + 0.1 * torch.randn(K, device=dev, generator=g)).half().view(torch.int16)
+    x = torch.randn(1, K, device=dev, generator=g)
+    y = torch.empty(1, N, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for it in range(3):
+        flush.fill_(it)
+        if kind == "int4_f32":
+            tb.gemv_q_norm(x, nw, 1e-6, pack, sc, y=y)
+        elif kind == "int4_dp4a":
+            tb.gemv_dp4a(x, pack, sc, norm_w=nw, y=y)
+        else:
+            tb.gemv_tern_wgsl_dp4a_multi(x, [(pack, sc)], norm_w=nw, ys=[y])
+    torch.cuda.synchronize()
+    err = tb.default_context(0).device_error()
+    assert err == 0, err
+    print("profile lm_head %s done" % kind, flush=True)
+
+
 # ---------------------------------------------------------------------------
 # CPU path (the reference's int4 linearQ math, C transcription)
 # ---------------------------------------------------------------------------
@@ -782,11 +815,16 @@ def main():
                     help="three cold-L2 decode-attention launches at context S (for ncu), then exit")
     ap.add_argument("--profile-gemm", type=int, nargs=3, default=None, metavar=("M", "N", "K"),
                     help="three cold-L2 prefill-GEMM launches at M x N x K (for ncu), then exit")
+    ap.add_argument("--profile-lm-head", default=None, choices=("int4_f32", "int4_dp4a", "tern"),
+                    help="three cold-L2 batch-1 lm_head GEMVs of one weight kind (for ncu), then exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
     args = ap.parse_args()
     if args.profile_decode:
         profile_decode(args.profile_decode)
+        return
+    if args.profile_lm_head:
+        profile_lm_head(args.profile_lm_head)
         return
     if args.profile_gemm:
         profile_gemm(*args.profile_gemm)

@@ -379,6 +379,74 @@ __device__ __forceinline__ void item_q8(const uint4 w, const float s, const unsi
     }
 }
 
+// The int8 activation of one 32-group for all B rows, loaded once and shared by
+// the several weight rows a warp carries.
+template <int B>
+struct XQ {
+    uint4 lo[B], hi[B];
+    int s8[B];
+    float sf[B];
+};
+template <int B>
+__device__ __forceinline__ void load_xq(XQ<B>& x, const unsigned char* act, int G, int g)
+{
+    const uint4* xlo = reinterpret_cast<const uint4*>(act);
+    const uint4* xhi = xlo + B * G;
+    const int* xs8 = reinterpret_cast<const int*>(xhi + B * G);
+    const float* xsf = reinterpret_cast<const float*>(xs8 + B * G);
+#pragma unroll
+    for (int b = 0; b < B; b++) {
+        const int i = b * G + g;
+        x.lo[b] = xlo[i];
+        x.hi[b] = xhi[i];
+        x.s8[b] = xs8[i];
+        x.sf[b] = xsf[i];
+    }
+}
+// int4 word quadruple (32 nibbles) against the permuted int8 layout
+template <int B>
+__device__ __forceinline__ void item_q8x(const uint4 w, const float s, const XQ<B>& x, float* acc)
+{
+    const uint32_t l0 = w.x & 0x0f0f0f0fu, h0 = (w.x >> 4) & 0x0f0f0f0fu;
+    const uint32_t l1 = w.y & 0x0f0f0f0fu, h1 = (w.y >> 4) & 0x0f0f0f0fu;
+    const uint32_t l2 = w.z & 0x0f0f0f0fu, h2 = (w.z >> 4) & 0x0f0f0f0fu;
+    const uint32_t l3 = w.w & 0x0f0f0f0fu, h3 = (w.w >> 4) & 0x0f0f0f0fu;
+#pragma unroll
+    for (int b = 0; b < B; b++) {
+        int d = -x.s8[b];
+        d = __dp4a((int)l0, (int)x.lo[b].x, d);
+        d = __dp4a((int)h0, (int)x.lo[b].y, d);
+        d = __dp4a((int)l1, (int)x.lo[b].z, d);
+        d = __dp4a((int)h1, (int)x.lo[b].w, d);
+        d = __dp4a((int)l2, (int)x.hi[b].x, d);
+        d = __dp4a((int)h2, (int)x.hi[b].y, d);
+        d = __dp4a((int)l3, (int)x.hi[b].z, d);
+        d = __dp4a((int)h3, (int)x.hi[b].w, d);
+        acc[b] = fmaf(s * x.sf[b], (float)d, acc[b]);
+    }
+}
+// ternary group (two code words) against the natural-order int8 layout
+template <int B>
+__device__ __forceinline__ void item_ternx(const uint2 w, const float s, const XQ<B>& x, float* acc)
+{
+    constexpr uint32_t M = 0x03030303u;
+    const uint32_t a0 = w.x & M, a1 = (w.x >> 2) & M, a2 = (w.x >> 4) & M, a3 = (w.x >> 6) & M;
+    const uint32_t c0 = w.y & M, c1 = (w.y >> 2) & M, c2 = (w.y >> 4) & M, c3 = (w.y >> 6) & M;
+#pragma unroll
+    for (int b = 0; b < B; b++) {
+        int d = -x.s8[b];
+        d = __dp4a((int)a0, (int)x.lo[b].x, d);
+        d = __dp4a((int)a1, (int)x.lo[b].y, d);
+        d = __dp4a((int)a2, (int)x.lo[b].z, d);
+        d = __dp4a((int)a3, (int)x.lo[b].w, d);
+        d = __dp4a((int)c0, (int)x.hi[b].x, d);
+        d = __dp4a((int)c1, (int)x.hi[b].y, d);
+        d = __dp4a((int)c2, (int)x.hi[b].z, d);
+        d = __dp4a((int)c3, (int)x.hi[b].w, d);
+        acc[b] = fmaf(s * x.sf[b], (float)d, acc[b]);
+    }
+}
+
 // One ternary 32-group (two code words) against the natural-order int8 row:
 // sum (c-1)*x = sum_s dp4a((word >> 2s) & 0x03030303, x word s) - sum(x).
 template <int B>
@@ -450,7 +518,7 @@ __device__ __forceinline__ void item_f32(const uint4 w, const float s, const uns
 // takes groups l, l+32, ... of the row (consecutive 16-byte items: conflict-free
 // shared-memory reads); the 32 partial sums of a row meet in a shuffle tree.
 template <int B, int KIND>
-__global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
+__global__ void __launch_bounds__(THREADS, 2) k_gemv(const Args a)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
@@ -520,70 +588,130 @@ __global__ void __launch_bounds__(THREADS) k_gemv(const Args a)
             if (a.err) atomicExch(a.err, ERR_WAIT_TIMEOUT);
         }
         const unsigned char* stg = stages + st * stage_bytes;
-        const bool sbulk = scales_bulk(bl.nrows, G);
+        if (!scales_bulk(bl.nrows, G) && !abort_flag) {
+            // a tail block whose scales are not a whole number of 16-byte chunks:
+            // copy them into the slot with plain loads, so every scale read below
+            // is a shared-memory read
+            for (int s = 0; s < NM; s++) {
+                uint16_t* dst = reinterpret_cast<uint16_t*>(stages + st * stage_bytes + s * a.slot_bytes +
+                                                            (size_t)a.RB * a.wrow_bytes);
+                const uint16_t* src = a.m[gateup ? s : bl.mi].scales + (size_t)bl.row0 * G;
+                for (int i = tid; i < bl.nrows * G; i += THREADS) dst[i] = src[i];
+            }
+            // these generic-proxy writes precede a later bulk copy into the same slot
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+        }
         if (!abort_flag) {
-            for (int r = wid; r < bl.nrows; r += THREADS / 32) {
-                float acc[NM][B];
+            // a warp carries RPW rows at once (rows r0, r0 + 8, ...): independent dp4a /
+            // FMA chains and shuffle trees that overlap, and one activation load per
+            // group for all of them, instead of one row's latency chain
+            constexpr int RPW = B == 1 ? 4 : (B == 2 ? 2 : 1);
+            constexpr int NW = THREADS / 32;
+            for (int r0 = wid; r0 < bl.nrows; r0 += NW * RPW) {
+                float acc[RPW][NM][B];
 #pragma unroll
-                for (int s = 0; s < NM; s++)
+                for (int q = 0; q < RPW; q++)
 #pragma unroll
-                    for (int b = 0; b < B; b++) acc[s][b] = 0.0f;
+                    for (int s = 0; s < NM; s++)
+#pragma unroll
+                        for (int b = 0; b < B; b++) acc[q][s][b] = 0.0f;
 #pragma unroll
                 for (int s = 0; s < NM; s++) {
                     const unsigned char* slot = stg + s * a.slot_bytes;
-                    const uint4* wrow = reinterpret_cast<const uint4*>(slot) + (size_t)r * G;
-                    const uint16_t* srow = sbulk ? reinterpret_cast<const uint16_t*>(slot + (size_t)a.RB * a.wrow_bytes) + (size_t)r * G
-                                                 : a.m[gateup ? s : bl.mi].scales + (size_t)(bl.row0 + r) * G;
+                    const uint16_t* sbase = reinterpret_cast<const uint16_t*>(slot + (size_t)a.RB * a.wrow_bytes);
                     if (TERN) {
-                        const uint2* trow = reinterpret_cast<const uint2*>(slot) + (size_t)r * G;
-                        for (int g = lane; g < G; g += 32) item_tern<B>(trow[g], tb_h2f(srow[g]), act, G, g, acc[s]);
-                    } else if (XREG && xreg) {
-                        if (lane < G) {
-                            const uint4 w = wrow[lane];
-                            float2 d = make_float2(0.0f, 0.0f);
-                            d = word_f32(w.x, xr0[0], xr0[1], d);
-                            d = word_f32(w.y, xr0[2], xr0[3], d);
-                            d = word_f32(w.z, xr0[4], xr0[5], d);
-                            d = word_f32(w.w, xr0[6], xr0[7], d);
-                            acc[s][0] = fmaf(tb_h2f(srow[lane]), d.x + d.y, acc[s][0]);
+                        const uint2* tw = reinterpret_cast<const uint2*>(slot);
+                        for (int g = lane; g < G; g += 32) {
+                            if constexpr (RPW > 1) {
+                                XQ<B> xg;
+                                load_xq<B>(xg, act, G, g);
+#pragma unroll
+                                for (int q = 0; q < RPW; q++) {
+                                    const int r = r0 + q * NW;
+                                    if (r < bl.nrows) item_ternx<B>(tw[r * G + g], tb_h2f(sbase[r * G + g]), xg, acc[q][s]);
+                                }
+                            } else {
+                                item_tern<B>(tw[r0 * G + g], tb_h2f(sbase[r0 * G + g]), act, G, g, acc[0][s]);
+                            }
                         }
-                        if (lane + 32 < G) {
-                            const uint4 w = wrow[lane + 32];
-                            float2 d = make_float2(0.0f, 0.0f);
-                            d = word_f32(w.x, xr1[0], xr1[1], d);
-                            d = word_f32(w.y, xr1[2], xr1[3], d);
-                            d = word_f32(w.z, xr1[4], xr1[5], d);
-                            d = word_f32(w.w, xr1[6], xr1[7], d);
-                            acc[s][0] = fmaf(tb_h2f(srow[lane + 32]), d.x + d.y, acc[s][0]);
+                    } else if (XREG && xreg) {
+#pragma unroll
+                        for (int q = 0; q < RPW; q++) {
+                            const int r = r0 + q * NW;
+                            if (r >= bl.nrows) continue;
+                            const uint4* wrow = reinterpret_cast<const uint4*>(slot) + (size_t)r * G;
+                            const uint16_t* srow = sbase + (size_t)r * G;
+                            if (lane < G) {
+                                const uint4 w = wrow[lane];
+                                float2 d = make_float2(0.0f, 0.0f);
+                                d = word_f32(w.x, xr0[0], xr0[1], d);
+                                d = word_f32(w.y, xr0[2], xr0[3], d);
+                                d = word_f32(w.z, xr0[4], xr0[5], d);
+                                d = word_f32(w.w, xr0[6], xr0[7], d);
+                                acc[q][s][0] = fmaf(tb_h2f(srow[lane]), d.x + d.y, acc[q][s][0]);
+                            }
+                            if (lane + 32 < G) {
+                                const uint4 w = wrow[lane + 32];
+                                float2 d = make_float2(0.0f, 0.0f);
+                                d = word_f32(w.x, xr1[0], xr1[1], d);
+                                d = word_f32(w.y, xr1[2], xr1[3], d);
+                                d = word_f32(w.z, xr1[4], xr1[5], d);
+                                d = word_f32(w.w, xr1[6], xr1[7], d);
+                                acc[q][s][0] = fmaf(tb_h2f(srow[lane + 32]), d.x + d.y, acc[q][s][0]);
+                            }
                         }
                     } else {
+                        const uint4* wq = reinterpret_cast<const uint4*>(slot);
                         for (int g = lane; g < G; g += 32) {
-                            const uint4 w = wrow[g];
-                            const float sc = tb_h2f(srow[g]);
-                            if (KIND == KIND_F32) item_f32<B>(w, sc, act, G, g, acc[s]);
-                            else item_q8<B>(w, sc, act, G, g, acc[s]);
+                            if constexpr (RPW > 1 && KIND != KIND_F32) {
+                                XQ<B> xg;
+                                load_xq<B>(xg, act, G, g);
+#pragma unroll
+                                for (int q = 0; q < RPW; q++) {
+                                    const int r = r0 + q * NW;
+                                    if (r < bl.nrows) item_q8x<B>(wq[r * G + g], tb_h2f(sbase[r * G + g]), xg, acc[q][s]);
+                                }
+                            } else {
+#pragma unroll
+                                for (int q = 0; q < RPW; q++) {
+                                    const int r = r0 + q * NW;
+                                    if (r >= bl.nrows) continue;
+                                    const uint4 w = wq[r * G + g];
+                                    const float sc = tb_h2f(sbase[r * G + g]);
+                                    if (KIND == KIND_F32) item_f32<B>(w, sc, act, G, g, acc[q][s]);
+                                    else item_q8<B>(w, sc, act, G, g, acc[q][s]);
+                                }
+                            }
                         }
                     }
                 }
 #pragma unroll
-                for (int s = 0; s < NM; s++)
+                for (int q = 0; q < RPW; q++)
 #pragma unroll
-                    for (int b = 0; b < B; b++) acc[s][b] = warp_sum(acc[s][b]);
+                    for (int s = 0; s < NM; s++)
+#pragma unroll
+                        for (int b = 0; b < B; b++) acc[q][s][b] = warp_sum(acc[q][s][b]);
                 if (lane == 0) {
-                    const int row = bl.row0 + r;
-                    if (gateup) {
-                        const int N = a.m[0].N;
 #pragma unroll
-                        for (int b = 0; b < B; b++) {
-                            const float g = acc[0][b], u = acc[NM - 1][b];
-                            a.m[0].y[(size_t)b * N + row] = __fdiv_rn(g, 1.0f + expf(-g)) * u;
-                        }
-                    } else {
-                        const Mat& M = a.m[bl.mi];
+                    for (int q = 0; q < RPW; q++) {
+                        const int r = r0 + q * NW;
+                        if (r >= bl.nrows) continue;
+                        const int row = bl.row0 + r;
+                        if (gateup) {
+                            const int N = a.m[0].N;
 #pragma unroll
-                        for (int b = 0; b < B; b++) {
-                            float* yp = M.y + (size_t)b * M.N + row;
-                            *yp = (a.acc ? *yp : 0.0f) + acc[0][b];
+                            for (int b = 0; b < B; b++) {
+                                const float g = acc[q][0][b], u = acc[q][NM - 1][b];
+                                a.m[0].y[(size_t)b * N + row] = __fdiv_rn(g, 1.0f + expf(-g)) * u;
+                            }
+                        } else {
+                            const Mat& M = a.m[bl.mi];
+#pragma unroll
+                            for (int b = 0; b < B; b++) {
+                                float* yp = M.y + (size_t)b * M.N + row;
+                                *yp = (a.acc ? *yp : 0.0f) + acc[q][0][b];
+                            }
                         }
                     }
                 }
