@@ -245,6 +245,46 @@ TB_API int tb_gemm_tern_wgsl(tb_ctx *ctx, float *y, const int8_t *xq, const floa
 TB_API int tb_linear_tern_wgsl(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
                                const uint16_t *scales, int64_t T, int64_t N, int64_t K, int acc);
 
+/* ---- `.cpu.bin` ternary model container (native/docs/FORMAT.md) ----------
+ * The native Bonsai engine's on-disk format: u32 le header length, a JSON header
+ * {"G": 64, "tensors": {...}}, then a blob of 16-byte-aligned entries: `tern`
+ * (Q2_0_g64 codes u8 [N][K/4] + f32 scales [N][K/64], ready for
+ * tb_gemv_tern_q2g64), `embed_f16` (f16 bits) and `f32` (norm weights). */
+typedef struct tb_bin tb_bin;
+enum { TB_BIN_TERN = 0, TB_BIN_EMBED_F16 = 1, TB_BIN_F32 = 2 };
+typedef struct {
+    const char *name;       /* valid while the container is open */
+    int kind;               /* TB_BIN_* */
+    int64_t N, K;           /* tern: rows, columns */
+    int ndim;
+    int64_t shape[4];
+    const void *data;       /* device: codes (tern) or the tensor's bytes */
+    int64_t bytes;
+    const void *scales;     /* device: f32 scales (tern), else NULL */
+    int64_t scales_bytes;
+    int64_t blob_offset;    /* data's offset in the blob */
+} tb_bin_tensor;
+
+/* Validate a container's header exactly as the reference reader does
+ * (Container::open / assemble / validate, native/crates/n2-core/src/binfmt.rs:
+ * 104-257) without touching a GPU: G == 64 (absent means 64), known kinds,
+ * K % G == 0, codesLen == N*K/4, scalesLen == N*(K/G)*4, every range inside the
+ * blob.  TB_OK, or TB_ERR_INVALID with the reason in err (the reference's wording). */
+TB_API int tb_bin_check(const char *path, char *err, size_t err_len);
+
+/* Container::open onto the device: validates as tb_bin_check, then streams the
+ * whole blob into one device allocation (pinned double-buffered copies on the
+ * context's stream); returns when the blob is resident.  Tensors are pointers
+ * into it, in the reference's layout. */
+TB_API int tb_bin_open(tb_ctx *ctx, const char *path, tb_bin **out);
+TB_API int tb_bin_close(tb_bin *bin);
+TB_API int64_t tb_bin_blob_bytes(const tb_bin *bin);
+/* tensors in name order (the reference's BTreeMap order) */
+TB_API int tb_bin_count(const tb_bin *bin);
+TB_API int tb_bin_info(const tb_bin *bin, int index, tb_bin_tensor *info);
+/* by name (Container::get / ternary / f32s, binfmt.rs:267-321) */
+TB_API int tb_bin_find(const tb_bin *bin, const char *name, tb_bin_tensor *info);
+
 /* ---- int8 KV cache + split-KV GQA decode attention ----------------------- */
 
 /* Fused decode attention prep at position `pos` (T=1):
@@ -385,6 +425,9 @@ typedef struct tb_qwen3_config {
   int32_t batch;     /* sequences per step, 1..16 */
   int32_t tp_size;   /* ranks sharing the model (1 = single GPU) */
   int32_t tp_rank;
+  int32_t ternary;   /* 1: tb_qwen3_set_weight tries the lossless ternary (WebGPU layout)
+                        record before int4, as the reference loader does
+                        (qwen3.js:3508-3523); 0: int4 only (its __noTernary) */
 } tb_qwen3_config;
 
 typedef struct tb_qwen3 tb_qwen3;
@@ -417,6 +460,19 @@ TB_API int tb_qwen3_destroy(tb_qwen3 *m);
  * converted into the model's shard, ordered on the context's stream. */
 TB_API int tb_qwen3_set_weight(tb_qwen3 *m, int kind, int layer, const uint16_t *bf16,
                                int64_t rows, int64_t cols);
+/* Formats of an already-quantized tensor (the quant cache's segment kinds,
+ * qwen3.js:3671-3717): int4 G32 pack + f16 scales, ternary WebGPU-layout pack +
+ * f16 scales, or the f16 buffer of a non-projection tensor. */
+enum { TB_QW_FMT_INT4 = 0, TB_QW_FMT_TERN = 1, TB_QW_FMT_F16 = 2 };
+/* Set a weight from its FULL [rows][cols] tensor already in `fmt` (host or
+ * device memory): `data` = pack (or the f16 buffer), `scales` = f16 scales
+ * (NULL for TB_QW_FMT_F16).  The rank's shard is copied out (32-aligned column
+ * slices for int4, 64-aligned for ternary).  What loadQuantCache does with
+ * each cached segment; synchronous for pageable host memory. */
+TB_API int tb_qwen3_set_weight_q(tb_qwen3 *m, int kind, int layer, int fmt, const void *data,
+                                 const void *scales, int64_t rows, int64_t cols);
+/* The format tb_qwen3_set_weight chose for a weight (TB_QW_FMT_*), or -1 if unset. */
+TB_API int tb_qwen3_weight_format(const tb_qwen3 *m, int kind, int layer);
 /* This rank's cache of a layer: int8 [batch][max_seq][n_kv/tp*hd] and f32
  * scales [batch][max_seq][n_kv/tp*hd/32] (fill prefixes with tb_kv_quant_write). */
 TB_API int tb_qwen3_kv(tb_qwen3 *m, int layer, int8_t **Kq, float **Ks, int8_t **Vq, float **Vs);

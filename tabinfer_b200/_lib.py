@@ -32,6 +32,13 @@ SIGNATURES = {
     "tb_batch_destroy": [P],
     "tb_copy_h2d": [P, P, P, ctypes.c_size_t],
     "tb_copy_d2h": [P, P, P, ctypes.c_size_t],
+    "tb_bin_check": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t],
+    "tb_bin_open": [P, ctypes.c_char_p, ctypes.POINTER(P)],
+    "tb_bin_close": [P],
+    "tb_bin_blob_bytes": [P],
+    "tb_bin_count": [P],
+    "tb_bin_info": [P, I32, P],
+    "tb_bin_find": [P, ctypes.c_char_p, P],
     "tb_quant_int4_g32": [P, P, P, P, I64, I64],
     "tb_quant_q8": [P, P, P, P, P, I64, I64],
     "tb_rmsnorm_q8": [P, P, P, F32, P, P, P, I64, I64],
@@ -73,6 +80,8 @@ SIGNATURES = {
     "tb_qwen3_create": [P, P, ctypes.POINTER(P)],
     "tb_qwen3_destroy": [P],
     "tb_qwen3_set_weight": [P, I32, I32, P, I64, I64],
+    "tb_qwen3_set_weight_q": [P, I32, I32, I32, P, P, I64, I64],
+    "tb_qwen3_weight_format": [P, I32, I32],
     "tb_qwen3_kv": [P, I32, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],
     "tb_qwen3_io": [P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],
     "tb_nccl_unique_id": [P],
@@ -90,16 +99,29 @@ class Qwen3Config(ctypes.Structure):
                 ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("intermediate", ctypes.c_int32),
                 ("vocab", ctypes.c_int32), ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float),
                 ("max_seq", ctypes.c_int32), ("batch", ctypes.c_int32), ("tp_size", ctypes.c_int32),
-                ("tp_rank", ctypes.c_int32)]
+                ("tp_rank", ctypes.c_int32), ("ternary", ctypes.c_int32)]
 
 
 # weight kinds (TB_QW_*)
 QW_EMBED, QW_LM_HEAD, QW_FINAL_NORM, QW_Q, QW_K, QW_V, QW_O, QW_GATE, QW_UP, QW_DOWN, \
     QW_LN_ATTN, QW_LN_MLP, QW_Q_NORM, QW_K_NORM = range(14)
+# formats of pre-quantized weights (TB_QW_FMT_*)
+QW_FMT_INT4, QW_FMT_TERN, QW_FMT_F16 = 0, 1, 2
 RESTYPES = {
+    "tb_bin_blob_bytes": I64,
     "tb_last_error": ctypes.c_char_p,
     "tb_ctx_get_stream": P,
 }
+
+
+class BinTensor(ctypes.Structure):
+    """tb_bin_tensor (include/tabinfer_b200.h)"""
+    _fields_ = [("name", ctypes.c_char_p), ("kind", ctypes.c_int), ("N", I64), ("K", I64), ("ndim", ctypes.c_int),
+                ("shape", I64 * 4), ("data", P), ("bytes", I64), ("scales", P), ("scales_bytes", I64),
+                ("blob_offset", I64)]
+
+
+BIN_TERN, BIN_EMBED_F16, BIN_F32 = 0, 1, 2
 
 
 def load(path=LIB_PATH):

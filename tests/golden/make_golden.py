@@ -23,6 +23,12 @@ What pins what:
   cross-checks the C oracle against different code written from the same
   reference lines, on the self-test fixtures (qwen3.js:3077-3157) and edge
   cases (all-zero groups, scale underflow, negative zero, large values).
+* tiny.cpu.bin + tiny_bin_weights.npz -- a `.cpu.bin` container written by the
+  REFERENCE'S OWN writer, native/tools/pack_bin.py:31-75 (main), run on a
+  synthetic two-shard safetensors checkpoint of Bonsai tensor names (f16
+  embedding and norms, bf16 ternary projections and lm_head, seeded); the npz
+  holds the checkpoint's raw 16-bit tensors.  It pins the device loader
+  (tb_bin_open) against the format's own writer.
 """
 import os
 import sys
@@ -144,6 +150,64 @@ def ternary_cases(pack_ternary_ref):
     return out
 
 
+def _write_safetensors(path, tensors):
+    """tensors: name -> (dtype str, shape, uint16 array)"""
+    import json
+    import struct
+    hdr, off, blobs = {}, 0, []
+    for name, (dt, shape, u16) in tensors.items():
+        b = np.ascontiguousarray(u16, np.uint16).tobytes()
+        hdr[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + len(b)]}
+        off += len(b)
+        blobs.append(b)
+    h = json.dumps(hdr).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+
+
+def tiny_checkpoint(seed=0xB1F):
+    """Bonsai-named tensors: ternary bf16 projections (per-64 bf16 scales),
+    f16 embedding and norms."""
+    rng = np.random.default_rng(seed)
+    H, V, I = 128, 96, 192
+
+    def tern_bf16(N, K):
+        s = (rng.uniform(0.01, 0.05, (N, K // 64)).astype(np.float32).view(np.uint32) & 0xFFFF0000).view(np.float32)
+        w = rng.integers(-1, 2, (N, K)).astype(np.float32) * np.repeat(s, 64, axis=1)
+        return (w.view(np.uint32) >> 16).astype(np.uint16)
+
+    def f16(shape, lo, hi):
+        return rng.uniform(lo, hi, shape).astype(np.float16).view(np.uint16)
+
+    shard1 = {"model.embed_tokens.weight": ("F16", (V, H), f16((V, H), -1, 1)),
+              "model.norm.weight": ("F16", (H,), f16((H,), 0.5, 1.5)),
+              "model.layers.0.input_layernorm.weight": ("F16", (H,), f16((H,), 0.5, 1.5)),
+              "model.layers.0.self_attn.q_proj.weight": ("BF16", (H, H), tern_bf16(H, H))}
+    shard2 = {"model.layers.0.mlp.down_proj.weight": ("BF16", (H, I), tern_bf16(H, I)),
+              "lm_head.weight": ("BF16", (V, H), tern_bf16(V, H))}
+    return shard1, shard2
+
+
+def bin_container(pack_bin):
+    import json
+    import tempfile
+    shard1, shard2 = tiny_checkpoint()
+    with tempfile.TemporaryDirectory() as d:
+        _write_safetensors(os.path.join(d, "model-00001-of-00002.safetensors"), shard1)
+        _write_safetensors(os.path.join(d, "model-00002-of-00002.safetensors"), shard2)
+        wm = {n: "model-00001-of-00002.safetensors" for n in shard1}
+        wm.update({n: "model-00002-of-00002.safetensors" for n in shard2})
+        json.dump({"weight_map": wm}, open(os.path.join(d, "model.safetensors.index.json"), "w"))
+        pack_bin.ROOT = d
+        pack_bin.OUT = os.path.join(HERE, "tiny.cpu.bin")
+        pack_bin.main()
+    np.savez_compressed(os.path.join(HERE, "tiny_bin_weights.npz"),
+                        **{n.replace(".", "__"): u16 for n, (_, _, u16) in {**shard1, **shard2}.items()})
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TABINFER_REF", "")
     tools = os.path.join(ref, "native", "tools")
@@ -151,6 +215,8 @@ def main():
         sys.exit("usage: make_golden.py <TabInfer checkout>  (native/tools/pack_bin.py not found)")
     sys.path.insert(0, tools)
     import pack_bin  # the reference's own packer (module import only sets path constants)
+
+    bin_container(pack_bin)
 
     tern = ternary_cases(pack_bin.pack_ternary)
     np.savez_compressed(os.path.join(HERE, "ternary_packs.npz"), **tern)
