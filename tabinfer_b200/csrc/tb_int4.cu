@@ -74,10 +74,12 @@ __global__ void __launch_bounds__(256) k_quant_int4_g32(const uint16_t* __restri
 // magnitude sits more than TOL = 2 ulps below its group's mx (then *fail is
 // set and the pack is not used); code = 1 for a zero magnitude, else 0 / 2 by
 // sign; weight k lands at bits 8*(k%4) + 2*((k/4)%4) of word k/16 (OR-reduced
-// over the 8 lanes of a word); scale = bf16ToF16bits(mx).
-__global__ void __launch_bounds__(256) k_quant_tern_wgsl(const uint32_t* __restrict__ w, uint32_t* __restrict__ pack,
-                                                         uint16_t* __restrict__ scales, long long nchunks,
-                                                         int* __restrict__ fail)
+// over the 8 lanes of a word); scale = bf16ToF16bits(mx).  Source rows are ldw
+// u32 (bf16 pairs) apart and cpr chunks long (a column slice of a wider matrix
+// when ldw > 32 * cpr); pack == nullptr checks without writing.
+__global__ void __launch_bounds__(256) k_quant_tern_wgsl(const uint32_t* __restrict__ w, long long ldw, long long cpr,
+                                                         uint32_t* __restrict__ pack, uint16_t* __restrict__ scales,
+                                                         long long nchunks, int* __restrict__ fail)
 {
     tb_pdl_wait();
     constexpr uint32_t TOL = 2;
@@ -85,7 +87,8 @@ __global__ void __launch_bounds__(256) k_quant_tern_wgsl(const uint32_t* __restr
     const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
     bool bad = false;
     for (long long c = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); c < nchunks; c += nwarps) {
-        const uint32_t u = __ldg(w + c * 32 + lane);   // chunk c = row-major weights 64c .. 64c+63
+        const long long row = c / cpr;
+        const uint32_t u = __ldg(w + row * ldw + (c - row * cpr) * 32 + lane);   // weights 64c .. 64c+63 of the slice
         const uint32_t lo = u & 0xffffu, hi = u >> 16;
         const uint32_t m0 = lo & 0x7fffu, m1 = hi & 0x7fffu;
         uint32_t mx = max(m0, m1);
@@ -98,8 +101,8 @@ __global__ void __launch_bounds__(256) k_quant_tern_wgsl(const uint32_t* __restr
         uint32_t word = (c0 << (((k0 & 3) << 3) + ((k0 >> 2) & 3) * 2)) | (c1 << (((k1 & 3) << 3) + ((k1 >> 2) & 3) * 2));
 #pragma unroll
         for (int o = 1; o < 8; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
-        if ((lane & 7) == 0) pack[c * 4 + (lane >> 3)] = word;
-        if ((lane & 15) == 0) scales[c * 2 + (lane >> 4)] = (uint16_t)js_f32_to_f16(__uint_as_float(mx << 16));
+        if (pack && (lane & 7) == 0) pack[c * 4 + (lane >> 3)] = word;
+        if (pack && (lane & 15) == 0) scales[c * 2 + (lane >> 4)] = (uint16_t)js_f32_to_f16(__uint_as_float(mx << 16));
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(fail, 1);
 }
@@ -192,6 +195,20 @@ int tb_quant_q8_impl(tb_ctx* ctx, const float* x, int8_t* xq, float* xs, int32_t
     return TB_OK;
 }
 
+// flag (device int) |= 1 when the N x K slice (rows ld elements apart) is not
+// ternary; it must be zero beforehand.  pack == nullptr: check only.
+int tb_quant_tern_wgsl_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint32_t* pack, uint16_t* scales,
+                                    int64_t N, int64_t K, int* flag)
+{
+    TB_REQUIRE(ctx, w && flag && K % 64 == 0 && ld % 2 == 0 && ld >= K && N > 0, "quant_tern_wgsl: bad slice");
+    const long long nchunks = N * (K / 64);
+    int grid = (int)std::min<long long>((nchunks + 7) / 8, (long long)ctx->num_sms * 16);
+    cudaError_t e = tb_launch(ctx, k_quant_tern_wgsl, dim3(grid), dim3(256), 0, reinterpret_cast<const uint32_t*>(w),
+                              (long long)(ld / 2), (long long)(K / 64), pack, scales, nchunks, flag);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_tern_wgsl launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
 extern "C" {
 
 TB_API int tb_quant_int4_g32(tb_ctx* ctx, const uint16_t* w, uint32_t* pack, uint16_t* scales, int64_t N, int64_t K)
@@ -215,12 +232,7 @@ TB_API int tb_quant_tern_wgsl_bf16(tb_ctx* ctx, const uint16_t* w, uint32_t* pac
     cudaError_t e = cudaMemsetAsync(nonternary, K % 64 ? 1 : 0, sizeof(int), ctx->stream);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "memset: %s", cudaGetErrorString(e));
     if (K % 64) return TB_OK;
-    const long long nchunks = N * (K / 64);
-    int grid = (int)std::min<long long>((nchunks + 7) / 8, (long long)ctx->num_sms * 16);
-    e = tb_launch(ctx, k_quant_tern_wgsl, dim3(grid), dim3(256), 0, reinterpret_cast<const uint32_t*>(w), pack,
-                  scales, nchunks, nonternary);
-    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_tern_wgsl launch: %s", cudaGetErrorString(e));
-    return TB_OK;
+    return tb_quant_tern_wgsl_strided_impl(ctx, w, K, pack, scales, N, K, nonternary);
 }
 
 TB_API int tb_convert_bf16_f16(tb_ctx* ctx, const uint16_t* in, uint16_t* out, int64_t n)

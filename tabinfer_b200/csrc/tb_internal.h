@@ -59,3 +59,7 @@ int tb_gemv_tern_wgsl_impl(tb_ctx* ctx, int count, float* const* ys, const uint3
                            float eps, int64_t K, int batch, int acc);
 // per-32 int8 quantization of T rows (QUANTQ8 / QUANTQ8T)
 int tb_quant_q8_impl(tb_ctx* ctx, const float* x, int8_t* xq, float* xs, int32_t* xsum16, int64_t T, int64_t K);
+// ternary (WebGPU layout) detect + pack of an N x K slice, rows ld elements apart;
+// flag |= 1 when not ternary (zero it first); pack == nullptr checks only
+int tb_quant_tern_wgsl_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint32_t* pack, uint16_t* scales,
+                                    int64_t N, int64_t K, int* flag);

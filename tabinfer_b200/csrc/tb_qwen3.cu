@@ -69,11 +69,15 @@ NcclApi& nccl()
     return api;
 }
 
+// a quantized weight record: int4 G32 (pack [N][K/8]) or ternary in the WebGPU
+// layout (pack [N][K/16]), f16 scales [N][K/32] either way (the reference's
+// wrec {pack, scales, int4 | tern}); storage is sized for int4
 struct Mat {
     uint32_t* pack = nullptr;
     uint16_t* scales = nullptr;
     int64_t N = 0, K = 0;
     bool set = false;
+    bool tern = false;
 };
 
 struct Layer {
@@ -184,6 +188,7 @@ int check_config(const tb_qwen3_config& c, char* why, size_t n)
     if (c.vocab % P) return bad("vocab must be a multiple of tp_size");
     if ((int64_t)c.batch * (c.n_kv_heads / P) > TB_ATTN_MAX_KV) return bad("batch * kv heads per rank too large");
     if (c.vocab >= (1LL << 31)) return bad("vocab too large");
+    if (c.ternary != 0 && c.ternary != 1) return bad("ternary must be 0 or 1");
     return TB_OK;
 }
 
@@ -203,8 +208,13 @@ int gemv_rows(tb_qwen3* m, float* y, const float* x, const Mat& w, const uint16_
     const int B = m->c.batch;
     for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
         const int nb = std::min(GEMV_MAX_B, B - b0);
-        TRY(tb_gemv_int4_dp4a(m->ctx, y + (int64_t)b0 * w.N, x + (int64_t)b0 * w.K, norm_w, m->c.rms_eps, w.pack,
-                              w.scales, w.N, w.K, nb, acc));
+        float* yb = y + (int64_t)b0 * w.N;
+        const float* xb = x + (int64_t)b0 * w.K;
+        if (w.tern)
+            TRY(tb_gemv_tern_wgsl_impl(m->ctx, 1, &yb, &w.pack, &w.scales, &w.N, xb, norm_w, m->c.rms_eps, w.K, nb,
+                                       acc));
+        else
+            TRY(tb_gemv_int4_dp4a(m->ctx, yb, xb, norm_w, m->c.rms_eps, w.pack, w.scales, w.N, w.K, nb, acc));
     }
     return TB_OK;
 }
@@ -255,8 +265,20 @@ int issue_step(tb_qwen3* m)
             const uint32_t* packs[3] = {Ly.q.pack, Ly.k.pack, Ly.v.pack};
             const uint16_t* scs[3] = {Ly.q.scales, Ly.k.scales, Ly.v.scales};
             const int64_t Ns[3] = {Ly.q.N, Ly.k.N, Ly.v.N};
-            TRY(tb_gemv_int4_dp4a_multi(ctx, 3, ys, packs, scs, Ns, m->x[cur] + (int64_t)b0 * H, Ly.ln1, c.rms_eps, H,
-                                        nb, 0));
+            const float* xb = m->x[cur] + (int64_t)b0 * H;
+            if (Ly.q.tern == Ly.k.tern && Ly.k.tern == Ly.v.tern) {
+                if (Ly.q.tern) TRY(tb_gemv_tern_wgsl_impl(ctx, 3, ys, packs, scs, Ns, xb, Ly.ln1, c.rms_eps, H, nb, 0));
+                else TRY(tb_gemv_int4_dp4a_multi(ctx, 3, ys, packs, scs, Ns, xb, Ly.ln1, c.rms_eps, H, nb, 0));
+            } else {   // mixed weight kinds: one launch per matrix
+                const Mat* ms[3] = {&Ly.q, &Ly.k, &Ly.v};
+                for (int i = 0; i < 3; i++) {
+                    if (ms[i]->tern)
+                        TRY(tb_gemv_tern_wgsl_impl(ctx, 1, &ys[i], &packs[i], &scs[i], &Ns[i], xb, Ly.ln1, c.rms_eps,
+                                                   H, nb, 0));
+                    else
+                        TRY(tb_gemv_int4_dp4a(ctx, ys[i], xb, Ly.ln1, c.rms_eps, packs[i], scs[i], Ns[i], H, nb, 0));
+                }
+            }
         }
         TRY(tb_attn_prep_q8_batch(ctx, m->q, m->k, m->v, Ly.qn, Ly.kn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, m->nHq,
                                   m->nKv, hd, B, c.max_seq, m->pos, c.rope_theta, c.rms_eps));
@@ -265,15 +287,21 @@ int issue_step(tb_qwen3* m)
         TRY(proj_residual(m, cur, m->attn, Ly.o, 2 * l));
         for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
             const int nb = std::min(GEMV_MAX_B, B - b0);
-            TRY(tb_gateup_silu_int4_dp4a(ctx, m->swi + (int64_t)b0 * m->I, m->x[cur] + (int64_t)b0 * H, Ly.ln2,
-                                         c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack, Ly.up.scales, m->I, H,
-                                         nb));
+            if (Ly.gate.tern)   // gateUpSiluQ's ternary branch (qwen3.js:730)
+                TRY(tb_gateup_silu_tern_wgsl_dp4a(ctx, m->swi + (int64_t)b0 * m->I, m->x[cur] + (int64_t)b0 * H,
+                                                  Ly.ln2, c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack,
+                                                  Ly.up.scales, m->I, H, nb));
+            else
+                TRY(tb_gateup_silu_int4_dp4a(ctx, m->swi + (int64_t)b0 * m->I, m->x[cur] + (int64_t)b0 * H, Ly.ln2,
+                                             c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack, Ly.up.scales, m->I,
+                                             H, nb));
         }
         TRY(proj_residual(m, cur, m->swi, Ly.down, 2 * l + 1));
     }
     // final norm + lm_head: gemvQ (f32 activation) at one row, as linearQ routes
-    // T = 1 with N >= 16384; the int8 DP4A GEMV for several rows
-    if (B == 1 && m->V >= 16384) {
+    // T = 1 with N >= 16384; the int8 DP4A GEMV for several rows; a ternary
+    // lm_head takes gemvTern at every N (qwen3.js:1594-1598)
+    if (B == 1 && m->V >= 16384 && !m->lm.tern) {
         TRY(tb_gemv_int4_f32_norm(ctx, m->logits, m->x[cur], m->fnorm, c.rms_eps, m->lm.pack, m->lm.scales, m->V, H, 1,
                                   0));
     } else {
@@ -431,8 +459,28 @@ TB_API int tb_qwen3_set_weight(tb_qwen3* m, int kind, int layer, const uint16_t*
     release_graph(m);   // weights are baked into the recorded step only by address, but be conservative
     const uint16_t* src = bf16 + s.row0 * C + s.col0;
     auto quant = [&](Mat& w) {
+        // _uploadTensor (qwen3.js:3508-3523): the lossless ternary record when the
+        // WHOLE tensor is ternary, else int4.  This rank's slice must start and end
+        // on 64-column boundaries for the ternary layout; otherwise int4.
+        if (m->c.ternary && C % 64 == 0 && s.col0 % 64 == 0 && s.ncols % 64 == 0) {
+            int* flag = static_cast<int*>(tb_ctx_scratch(ctx, 256));
+            if (!flag) return (int)TB_ERR_NOMEM;
+            int h = 1;
+            cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), ctx->stream);
+            if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "memset: %s", cudaGetErrorString(e));
+            TRY(tb_quant_tern_wgsl_strided_impl(ctx, bf16, C, nullptr, nullptr, R, C, flag));
+            e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+            if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "ternary check: %s", cudaGetErrorString(e));
+            if (h == 0) {
+                TRY(tb_quant_tern_wgsl_strided_impl(ctx, src, C, w.pack, w.scales, s.nrows, s.ncols, flag));
+                w.tern = true;
+                w.set = true;
+                return (int)TB_OK;
+            }
+        }
         int rc = tb_quant_int4_strided_impl(ctx, src, C, w.pack, w.scales, s.nrows, s.ncols);
-        if (!rc) w.set = true;
+        if (!rc) { w.set = true; w.tern = false; }
         return rc;
     };
     auto f16 = [&](uint16_t* dst) { return tb_convert_bf16_f16(ctx, src, dst, s.nrows * s.ncols); };
@@ -454,6 +502,87 @@ TB_API int tb_qwen3_set_weight(tb_qwen3* m, int kind, int layer, const uint16_t*
     case TB_QW_K_NORM: return f16(Ly->kn);
     }
     return tb_fail(ctx, TB_ERR_INVALID, "unknown weight kind %d", kind);
+}
+
+// the Mat or f16 buffer behind a weight kind
+static int weight_slot(tb_qwen3* m, int kind, int layer, Mat** mat, uint16_t** buf)
+{
+    *mat = nullptr;
+    *buf = nullptr;
+    const bool per_layer = kind >= TB_QW_Q;
+    if (per_layer && (layer < 0 || layer >= m->c.layers)) return TB_ERR_INVALID;
+    Layer* Ly = per_layer ? &m->L[layer] : nullptr;
+    switch (kind) {
+    case TB_QW_EMBED: *buf = m->embed; break;
+    case TB_QW_LM_HEAD: *mat = &m->lm; break;
+    case TB_QW_FINAL_NORM: *buf = m->fnorm; break;
+    case TB_QW_Q: *mat = &Ly->q; break;
+    case TB_QW_K: *mat = &Ly->k; break;
+    case TB_QW_V: *mat = &Ly->v; break;
+    case TB_QW_O: *mat = &Ly->o; break;
+    case TB_QW_GATE: *mat = &Ly->gate; break;
+    case TB_QW_UP: *mat = &Ly->up; break;
+    case TB_QW_DOWN: *mat = &Ly->down; break;
+    case TB_QW_LN_ATTN: *buf = Ly->ln1; break;
+    case TB_QW_LN_MLP: *buf = Ly->ln2; break;
+    case TB_QW_Q_NORM: *buf = Ly->qn; break;
+    case TB_QW_K_NORM: *buf = Ly->kn; break;
+    default: return TB_ERR_INVALID;
+    }
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_set_weight_q(tb_qwen3* m, int kind, int layer, int fmt, const void* data, const void* scales,
+                                 int64_t rows, int64_t cols)
+{
+    if (!m) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    TB_REQUIRE(ctx, data != nullptr, "null weight");
+    Slice s{};
+    int64_t R = 0, C = 0;
+    TB_REQUIRE(ctx, shard_of(m->c, kind, s, &R, &C) == TB_OK, "unknown weight kind %d", kind);
+    TB_REQUIRE(ctx, rows == R && cols == C, "weight kind %d: expected %lld x %lld, got %lld x %lld", kind,
+               (long long)R, (long long)C, (long long)rows, (long long)cols);
+    Mat* w = nullptr;
+    uint16_t* buf = nullptr;
+    TB_REQUIRE(ctx, weight_slot(m, kind, layer, &w, &buf) == TB_OK, "layer %d out of range", layer);
+    release_graph(m);
+    auto copy2d = [&](void* dst, const void* src, size_t spitch, size_t width, size_t height) {
+        cudaError_t e = cudaMemcpy2DAsync(dst, width, src, spitch, width, height, cudaMemcpyDefault, ctx->stream);
+        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "set_weight_q copy: %s", cudaGetErrorString(e));
+        return (int)TB_OK;
+    };
+    if (buf) {
+        TB_REQUIRE(ctx, fmt == TB_QW_FMT_F16, "weight kind %d is an f16 tensor (fmt %d given)", kind, fmt);
+        const char* src = static_cast<const char*>(data) + (size_t)(s.row0 * C + s.col0) * 2;
+        return copy2d(buf, src, (size_t)C * 2, (size_t)s.ncols * 2, (size_t)s.nrows);
+    }
+    TB_REQUIRE(ctx, fmt == TB_QW_FMT_INT4 || fmt == TB_QW_FMT_TERN, "weight kind %d is quantized (fmt %d given)", kind,
+               fmt);
+    TB_REQUIRE(ctx, scales != nullptr, "null scales");
+    const bool tern = fmt == TB_QW_FMT_TERN;
+    const int64_t align = tern ? 64 : 32;
+    TB_REQUIRE(ctx, C % align == 0 && s.col0 % align == 0 && s.ncols % align == 0,
+               "weight kind %d: this shard's columns are not %lld-aligned for the %s layout", kind, (long long)align,
+               tern ? "ternary" : "int4");
+    const int64_t per = tern ? 4 : 2;   // weights per byte
+    const char* ps = static_cast<const char*>(data) + (size_t)(s.row0 * (C / per) + s.col0 / per);
+    TRY(copy2d(w->pack, ps, (size_t)(C / per), (size_t)(s.ncols / per), (size_t)s.nrows));
+    const char* ss = static_cast<const char*>(scales) + (size_t)(s.row0 * (C / 32) + s.col0 / 32) * 2;
+    TRY(copy2d(w->scales, ss, (size_t)(C / 32) * 2, (size_t)(s.ncols / 32) * 2, (size_t)s.nrows));
+    w->tern = tern;
+    w->set = true;
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_weight_format(const tb_qwen3* m, int kind, int layer)
+{
+    if (!m) return -1;
+    Mat* w = nullptr;
+    uint16_t* buf = nullptr;
+    if (weight_slot(const_cast<tb_qwen3*>(m), kind, layer, &w, &buf) != TB_OK) return -1;
+    if (buf) return TB_QW_FMT_F16;
+    return w->set ? (w->tern ? TB_QW_FMT_TERN : TB_QW_FMT_INT4) : -1;
 }
 
 TB_API int tb_qwen3_kv(tb_qwen3* m, int layer, int8_t** Kq, float** Ks, int8_t** Vq, float** Vs)

@@ -125,6 +125,14 @@ def quantize_int4_bf16(w, pack=None, scales=None):
     return pack, scales
 
 
+def convert_bf16_f16(w, out=None):
+    """bf16ToF16bits (qwen3.js:3386-3390): the loader's f16 copy of a non-projection tensor."""
+    out = out if out is not None else torch.empty(w.shape, dtype=torch.int16, device=w.device)
+    c = _ctx(w)
+    c.check(LIB.tb_convert_bf16_f16(c.h, _p(w.contiguous()), _p(out), w.numel()), "convert_bf16_f16")
+    return out
+
+
 def quant_q8(x, xq=None, xs=None, xsum16=None):
     """quantQ8 / QUANTQ8T (qwen3.js:332-358, 1210-1231): f32 [T,K] -> int8, per-32 scales, per-16 sums."""
     x2 = x.reshape(-1, x.shape[-1])

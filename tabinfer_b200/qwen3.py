@@ -76,7 +76,7 @@ def _hp(t):
 def make_config(cfg):
     c = _lib.Qwen3Config()
     for f, _ in _lib.Qwen3Config._fields_:
-        default = {"tp_size": 1, "tp_rank": 0, "batch": 1}.get(f)
+        default = {"tp_size": 1, "tp_rank": 0, "batch": 1, "ternary": 1}.get(f)
         v = cfg.get(f, default)
         if v is None:
             raise KeyError("qwen3 config needs '%s'" % f)
@@ -138,6 +138,42 @@ class Qwen3:
         rows, cols = (1, w.numel()) if w.dim() == 1 else tuple(w.shape)
         self.ctx.check(LIB.tb_qwen3_set_weight(self.h, kind, layer, _p(w), rows, cols), "set_weight " + name)
         return True
+
+    def load_quantized(self, name, fmt, data, scales=None, shape=None):
+        """Set one tensor from its already-quantized FULL form (what the quant
+        cache holds, qwen3.js:3671-3717): fmt QW_FMT_INT4 / QW_FMT_TERN with pack
+        and f16 scales, or QW_FMT_F16 with the f16 buffer.  data / scales are
+        numpy arrays (host) or CUDA tensors; shape = (rows, cols) of the tensor."""
+        kl = weight_kind(name)
+        if kl is None:
+            return False
+        kind, layer = kl
+        rows, cols = shape
+
+        keep = []
+
+        def ptr(a):
+            if a is None:
+                return None
+            if isinstance(a, torch.Tensor):
+                a = a.contiguous()
+                keep.append(a)
+                return _p(a) if a.is_cuda else ctypes.c_void_p(a.data_ptr())
+            import numpy as np
+            a = np.ascontiguousarray(a)
+            keep.append(a)
+            return ctypes.c_void_p(a.ctypes.data)
+        self.ctx.check(LIB.tb_qwen3_set_weight_q(self.h, kind, layer, fmt, ptr(data), ptr(scales), rows, cols),
+                       "set_weight_q " + name)
+        self.ctx.synchronize()   # the host buffers may be reused by the caller
+        return True
+
+    def weight_format(self, name):
+        """QW_FMT_* the loader chose for a tensor (-1 when unset or unknown)."""
+        kl = weight_kind(name)
+        if kl is None:
+            return -1
+        return LIB.tb_qwen3_weight_format(self.h, kl[0], kl[1])
 
     def tp_init(self, unique_id):
         """NCCL exchange: every rank passes the same 128-byte unique id."""
