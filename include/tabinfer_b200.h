@@ -245,6 +245,17 @@ TB_API int tb_gemm_tern_wgsl(tb_ctx *ctx, float *y, const int8_t *xq, const floa
 TB_API int tb_linear_tern_wgsl(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
                                const uint16_t *scales, int64_t T, int64_t N, int64_t K, int acc);
 
+/* int8-KV prefill attention: attentionQ8 with T > 1 (qwen3.js:2534-2577; the
+ * flash kernels ATTN_WGSL / attnF16Wgsl with dequantizing tile loads).  Query i
+ * of T (q f32 [T][nHq*hd], after q_norm + RoPE) sits at position S - T + i and
+ * attends causally to keys 0 .. S - T + i of the int8 cache (layout of
+ * tb_attn_prep_q8: Kq/Vq int8 [S][nKv*hd], Ks/Vs f32 [S][nKv*hd/32]); out f32
+ * [T][nHq*hd].  1 <= T <= S, hd 64 or 128, nHq/nKv in {1,2,4,8}.  Tensor-core
+ * math with f16 operands and f32 sums (within ~1e-3 of the exact result). */
+TB_API int tb_attn_prefill_q8(tb_ctx *ctx, float *out, const float *q, const int8_t *Kq,
+                              const float *Ks, const int8_t *Vq, const float *Vs, int64_t T,
+                              int64_t S, int64_t nHq, int64_t nKv, int64_t hd);
+
 /* ---- `.cpu.bin` ternary model container (native/docs/FORMAT.md) ----------
  * The native Bonsai engine's on-disk format: u32 le header length, a JSON header
  * {"G": 64, "tensors": {...}}, then a blob of 16-byte-aligned entries: `tern`

@@ -339,6 +339,16 @@ def attn_decode_q8(q, Kq, Ks, Vq, Vs, S, nHq, nKv, hd):
     return out
 
 
+def attn_prefill_q8(q, Kq, Ks, Vq, Vs, T, S, nHq, nKv, hd):
+    """attentionQ8 at T > 1 (qwen3.js:2534-2577), causal over the int8 cache, in double."""
+    out = np.zeros((T, nHq * hd), np.float64)
+    lib().tbo_attn_prefill_q8(_ptr(np.ascontiguousarray(q, np.float32)), _ptr(np.ascontiguousarray(Kq, np.int8)),
+                              _ptr(np.ascontiguousarray(Ks, np.float32)), _ptr(np.ascontiguousarray(Vq, np.int8)),
+                              _ptr(np.ascontiguousarray(Vs, np.float32)), _I(T), _I(S), _I(nHq), _I(nKv), _I(hd),
+                              _ptr(out))
+    return out
+
+
 def dec_nsplit(S):
     return lib().tbo_dec_nsplit(int(S))
 

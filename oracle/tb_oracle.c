@@ -589,6 +589,19 @@ TBO_API void tbo_attn_decode_q8(const float *q, const int8_t *Kq, const float *K
     free(sc);
 }
 
+/* int8-KV prefill attention, attentionQ8 with T > 1 (qwen3.js:2534-2577: the
+ * flash kernels ATTN_WGSL / attnF16Wgsl with int8 tile loads): query i of T sits
+ * at position S - T + i and sees keys 0 .. S - T + i (the causal mask
+ * gk <= gqpos); per query this is the decode attention above over S - T + i + 1
+ * keys.  q [T][nHq*hd], out [T][nHq*hd] in double. */
+TBO_API void tbo_attn_prefill_q8(const float *q, const int8_t *Kq, const float *Ks,
+                                 const int8_t *Vq, const float *Vs, int64_t T, int64_t S,
+                                 int64_t nHq, int64_t nKv, int64_t hd, double *out)
+{
+    for (int64_t i = 0; i < T; i++)
+        tbo_attn_decode_q8(q + i * nHq * hd, Kq, Ks, Vq, Vs, S - T + i + 1, nHq, nKv, hd, out + i * nHq * hd);
+}
+
 /* Split count rule, _decNsplit qwen3.js:2354 (DEC_TK = 128, max 16 splits). */
 TBO_API int tbo_dec_nsplit(int64_t S)
 {

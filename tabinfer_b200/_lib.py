@@ -32,6 +32,7 @@ SIGNATURES = {
     "tb_batch_destroy": [P],
     "tb_copy_h2d": [P, P, P, ctypes.c_size_t],
     "tb_copy_d2h": [P, P, P, ctypes.c_size_t],
+    "tb_attn_prefill_q8": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64],
     "tb_bin_check": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t],
     "tb_bin_open": [P, ctypes.c_char_p, ctypes.POINTER(P)],
     "tb_bin_close": [P],

@@ -405,6 +405,19 @@ def gate_up_silu_tern_dp4a(x, gpack, gscales, upack, uscales, norm_w=None, eps=1
     return swi
 
 
+def attention_prefill_q8(q, kv, S, nHq, nKv, hd, out=None):
+    """attentionQ8 at T > 1 (qwen3.js:2534-2577): q [T, nHq*hd] after norm+RoPE at
+    positions S-T .. S-1, causal over the int8 cache kv = (Kq, Ks, Vq, Vs)."""
+    q2 = q.reshape(-1, nHq * hd)
+    T = q2.shape[0]
+    Kq, Ks, Vq, Vs = kv
+    out = out if out is not None else torch.empty((T, nHq * hd), dtype=torch.float32, device=q.device)
+    c = _ctx(q)
+    c.check(LIB.tb_attn_prefill_q8(c.h, _p(out), _p(q2), _p(Kq), _p(Ks), _p(Vq), _p(Vs), T, S, nHq, nKv, hd),
+            "attn_prefill_q8")
+    return out
+
+
 def gemm_tern(xq, xs, pack, scales, y=None, acc=False):
     """gemmTern (qwen3.js:1410-1420) on the tensor cores from QUANTQ8T rows:
     y[M,N] (+)= f16(xs*xq) . f16((c-1)*s)^T."""
