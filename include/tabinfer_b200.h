@@ -256,6 +256,22 @@ TB_API int tb_attn_prefill_q8(tb_ctx *ctx, float *out, const float *q, const int
                               const float *Ks, const int8_t *Vq, const float *Vs, int64_t T,
                               int64_t S, int64_t nHq, int64_t nKv, int64_t hd);
 
+/* ---- sampling transforms before argmax (qwen3.js:2692-2737) ------------------
+ * logits are `rows` rows of n.  The mask is one bit per token, rows of
+ * ceil(n/32) u32 words (bit i%32 of word i/32); the Gumbel noise of element
+ * (row, i) is that of the flat index row*n + i. */
+/* LOGITMASK_WGSL: every token whose bit is clear gets -3e38 (grammar-constrained decoding). */
+TB_API int tb_logit_mask(tb_ctx *ctx, float *logits, const uint32_t *mask, int64_t n, int64_t rows);
+/* GUMBEL_WGSL: logits += temp * -log(-log(u)), u = (pcg(i ^ seed*2654435761) >> 8 + 0.5) / 2^24,
+ * so argmax afterwards is an exact sample of softmax(logits / temp).  The host
+ * advances the seed per step (gumbelNoise: seed = seed*1664525 + 1013904223). */
+TB_API int tb_gumbel_noise(tb_ctx *ctx, float *logits, int64_t n, int64_t rows, uint32_t seed, float temp);
+/* mask (optional) + Gumbel noise (temp > 0) + argmax in one pass, logits left
+ * unmodified: the same ids as tb_logit_mask, tb_gumbel_noise and tb_argmax in
+ * sequence.  temp == 0 and mask == NULL is greedy argmax. */
+TB_API int tb_sample_argmax(tb_ctx *ctx, const float *logits, int64_t n, int64_t rows, const uint32_t *mask,
+                            uint32_t seed, float temp, uint32_t *out_idx);
+
 /* ---- `.cpu.bin` ternary model container (native/docs/FORMAT.md) ----------
  * The native Bonsai engine's on-disk format: u32 le header length, a JSON header
  * {"G": 64, "tensors": {...}}, then a blob of 16-byte-aligned entries: `tern`

@@ -349,6 +349,13 @@ def attn_prefill_q8(q, Kq, Ks, Vq, Vs, T, S, nHq, nKv, hd):
     return out
 
 
+def gumbel_noise(total, seed, temp):
+    """GUMBEL_WGSL noise (qwen3.js:2719-2730) of flat indices 0..total-1, in double."""
+    out = np.zeros(total, np.float64)
+    lib().tbo_gumbel_noise(_I(total), ctypes.c_uint32(seed & 0xFFFFFFFF), ctypes.c_double(temp), _ptr(out))
+    return out
+
+
 def dec_nsplit(S):
     return lib().tbo_dec_nsplit(int(S))
 

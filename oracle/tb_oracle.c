@@ -602,6 +602,31 @@ TBO_API void tbo_attn_prefill_q8(const float *q, const int8_t *Kq, const float *
         tbo_attn_decode_q8(q + i * nHq * hd, Kq, Ks, Vq, Vs, S - T + i + 1, nHq, nKv, hd, out + i * nHq * hd);
 }
 
+/* GUMBEL_WGSL (qwen3.js:2719-2730): noise of flat index i under seed is
+ * temp * -log(-log(u)), u = (f32(pcg(i ^ seed*2654435761) >> 8) + 0.5) / 2^24;
+ * pcg = the PCG output permutation of the WGSL.  u is formed in f32 as the
+ * shader forms it: for h >> 8 >= 2^23 the + 0.5 rounds (to even), and at
+ * h >> 8 = 2^24 - 1 it gives u = 1 exactly and an infinite noise -- the shader's
+ * comment says u is never 1, its f32 arithmetic says otherwise.  The logs are
+ * taken in double. */
+static uint32_t pcg_hash(uint32_t v0)
+{
+    uint32_t v = v0 * 747796405u + 2891336453u;
+    uint32_t w = ((v >> ((v >> 28u) + 4u)) ^ v) * 277803737u;
+    return (w >> 22u) ^ w;
+}
+
+TBO_API void tbo_gumbel_noise(int64_t total, uint32_t seed, double temp, double *out)
+{
+    for (int64_t i = 0; i < total; i++) {
+        uint32_t h = pcg_hash((uint32_t)i ^ (seed * 2654435761u));
+        volatile float uf = (float)(h >> 8);
+        uf = uf + 0.5f;
+        double u = (double)(uf / 16777216.0f);
+        out[i] = temp * (-log(-log(u)));
+    }
+}
+
 /* Split count rule, _decNsplit qwen3.js:2354 (DEC_TK = 128, max 16 splits). */
 TBO_API int tbo_dec_nsplit(int64_t S)
 {

@@ -33,6 +33,9 @@ SIGNATURES = {
     "tb_copy_h2d": [P, P, P, ctypes.c_size_t],
     "tb_copy_d2h": [P, P, P, ctypes.c_size_t],
     "tb_attn_prefill_q8": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64],
+    "tb_logit_mask": [P, P, P, I64, I64],
+    "tb_gumbel_noise": [P, P, I64, I64, ctypes.c_uint32, F32],
+    "tb_sample_argmax": [P, P, I64, I64, P, ctypes.c_uint32, F32, P],
     "tb_bin_check": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t],
     "tb_bin_open": [P, ctypes.c_char_p, ctypes.POINTER(P)],
     "tb_bin_close": [P],

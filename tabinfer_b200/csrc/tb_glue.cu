@@ -1,4 +1,8 @@
-// tb_glue.cu -- decode-step glue: argmax, RMSNorm, embedding gather.
+// tb_glue.cu -- decode-step glue: argmax, RMSNorm, embedding gather, and the
+// sampling transforms that precede argmax: the grammar logit mask and
+// Gumbel-max temperature noise (models/qwen3.js:2692-2737), standalone and
+// fused into argmax's first pass (so a sampled step reads the logits once and
+// leaves them unmodified).
 #include "tb_act.cuh"
 #include "tb_internal.h"
 
@@ -38,22 +42,75 @@ __device__ __forceinline__ unsigned long long block_max_key(unsigned long long k
     return k;   // valid in thread 0
 }
 
-// stage 1: blocks (bx, row) reduce an interleaved slice of row `row`
+// GUMBEL_WGSL's hash (qwen3.js:2724): a PCG output permutation of one word
+__device__ __forceinline__ uint32_t pcg_hash(uint32_t v0)
+{
+    const uint32_t v = v0 * 747796405u + 2891336453u;
+    const uint32_t w = ((v >> ((v >> 28u) + 4u)) ^ v) * 277803737u;
+    return (w >> 22u) ^ w;
+}
+// T * Gumbel(0,1) noise of flat logit index i under `seed` (qwen3.js:2726-2730):
+// u = (h >> 8 + 0.5) / 2^24 lies in (0, 1) and is exact in f32
+__device__ __forceinline__ float gumbel_noise(uint32_t i, uint32_t seed, float temp)
+{
+    const uint32_t h = pcg_hash(i ^ (seed * 2654435761u));
+    const float u = ((float)(h >> 8) + 0.5f) / 16777216.0f;
+    return temp * (-logf(-logf(u)));
+}
+// LOGITMASK_WGSL (qwen3.js:2696-2704): a token whose bit is clear gets -3e38
+constexpr float MASKED = -3.0e38f;
+
+struct SampleXf {
+    const uint32_t* mask;   // [rows][ceil(n/32)] bit per token, or nullptr
+    uint32_t seed;
+    float temp;             // 0: no noise
+};
+
+// stage 1: blocks (bx, row) reduce an interleaved slice of row `row`; with XF the
+// logit is first masked and given its Gumbel noise (the transforms above, on the
+// flat index row * n + i)
+template <bool XF>
 __global__ void __launch_bounds__(AMAX_THREADS) k_argmax_p1(const float* __restrict__ x, long long n,
-                                                            unsigned long long* __restrict__ part)
+                                                            unsigned long long* __restrict__ part, SampleXf xf)
 {
     tb_pdl_wait();
     tb_pdl_trigger();
     const int row = blockIdx.y;
     const float* xr = x + (long long)row * n;
+    const long long mw = (n + 31) >> 5;
     unsigned long long best = 0ull;
     for (long long i = blockIdx.x * (long long)AMAX_THREADS + threadIdx.x; i < n;
          i += (long long)gridDim.x * AMAX_THREADS) {
-        unsigned long long k = amax_key(xr[i], (unsigned)i);
+        float v = xr[i];
+        if (XF) {
+            if (xf.mask && ((xf.mask[row * mw + (i >> 5)] >> (i & 31)) & 1u) == 0u) v = MASKED;
+            if (xf.temp != 0.0f) v = v + gumbel_noise((uint32_t)(row * n + i), xf.seed, xf.temp);
+        }
+        unsigned long long k = amax_key(v, (unsigned)i);
         best = k > best ? k : best;
     }
     best = block_max_key(best);
     if (threadIdx.x == 0) part[(long long)row * gridDim.x + blockIdx.x] = best;
+}
+
+__global__ void __launch_bounds__(256) k_logit_mask(float* __restrict__ logits, const uint32_t* __restrict__ mask,
+                                                    long long n, long long total)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const long long mw = (n + 31) >> 5;
+    for (long long f = blockIdx.x * 256ll + threadIdx.x; f < total; f += (long long)gridDim.x * 256) {
+        const long long row = f / n, i = f - row * n;
+        if (((mask[row * mw + (i >> 5)] >> (i & 31)) & 1u) == 0u) logits[f] = MASKED;
+    }
+}
+
+__global__ void __launch_bounds__(256) k_gumbel(float* __restrict__ logits, long long total, uint32_t seed, float temp)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    for (long long f = blockIdx.x * 256ll + threadIdx.x; f < total; f += (long long)gridDim.x * 256)
+        logits[f] = logits[f] + gumbel_noise((uint32_t)f, seed, temp);
 }
 
 // stage 2: one block per row.  Writes the row's index (out, + idx_base: the
@@ -131,7 +188,8 @@ __global__ void __launch_bounds__(256) k_embed(const uint32_t* __restrict__ ids,
 int tb_argmax_impl(tb_ctx* ctx, const float* x, int64_t n, int64_t rows, uint32_t* out, unsigned long long* part,
                    int nparts, unsigned long long* out_key, uint32_t idx_base, int32_t* pos_inc)
 {
-    cudaError_t e = tb_launch(ctx, k_argmax_p1, dim3(nparts, (unsigned)rows), dim3(AMAX_THREADS), 0, x, (long long)n, part);
+    cudaError_t e = tb_launch(ctx, k_argmax_p1<false>, dim3(nparts, (unsigned)rows), dim3(AMAX_THREADS), 0, x,
+                              (long long)n, part, SampleXf{nullptr, 0u, 0.0f});
     if (e == cudaSuccess)
         e = tb_launch(ctx, k_argmax_p2, dim3((unsigned)rows), dim3(AMAX_THREADS), 0,
                       (const unsigned long long*)part, nparts, out, out_key, (unsigned)idx_base, (int*)pos_inc);
@@ -165,6 +223,50 @@ TB_API int tb_argmax(tb_ctx* ctx, const float* x, int64_t n, int64_t rows, uint3
     auto* part = static_cast<unsigned long long*>(tb_ctx_scratch(ctx, (size_t)rows * nparts * 8));
     if (!part) return TB_ERR_NOMEM;
     return tb_argmax_impl(ctx, x, n, rows, out_idx + out_offset, part, nparts, nullptr, 0, nullptr);
+}
+
+TB_API int tb_logit_mask(tb_ctx* ctx, float* logits, const uint32_t* mask, int64_t n, int64_t rows)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, logits && mask, "null pointer");
+    TB_REQUIRE(ctx, n > 0 && rows > 0 && n * rows < (1LL << 40), "bad shape");
+    const long long tot = n * rows;
+    int grid = (int)std::min<long long>((tot + 255) / 256, (long long)ctx->num_sms * 8);
+    cudaError_t e = tb_launch(ctx, k_logit_mask, dim3(grid), dim3(256), 0, logits, mask, (long long)n, tot);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "logit_mask launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_gumbel_noise(tb_ctx* ctx, float* logits, int64_t n, int64_t rows, uint32_t seed, float temp)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, logits != nullptr, "null pointer");
+    TB_REQUIRE(ctx, n > 0 && rows > 0 && n * rows <= (1LL << 32), "bad shape (flat indices are 32-bit)");
+    const long long tot = n * rows;
+    int grid = (int)std::min<long long>((tot + 255) / 256, (long long)ctx->num_sms * 8);
+    cudaError_t e = tb_launch(ctx, k_gumbel, dim3(grid), dim3(256), 0, logits, tot, seed, temp);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gumbel launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_sample_argmax(tb_ctx* ctx, const float* logits, int64_t n, int64_t rows, const uint32_t* mask,
+                            uint32_t seed, float temp, uint32_t* out_idx)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, logits && out_idx, "null pointer");
+    TB_REQUIRE(ctx, n > 0 && n < (1LL << 32) - 1 && rows > 0 && rows <= 65535 && n * rows <= (1LL << 32),
+               "bad shape");
+    TB_REQUIRE(ctx, temp >= 0.0f, "temperature must be >= 0");
+    const int nparts = tb_argmax_parts(ctx, n);
+    auto* part = static_cast<unsigned long long*>(tb_ctx_scratch(ctx, (size_t)rows * nparts * 8));
+    if (!part) return TB_ERR_NOMEM;
+    cudaError_t e = tb_launch(ctx, k_argmax_p1<true>, dim3(nparts, (unsigned)rows), dim3(AMAX_THREADS), 0, logits,
+                              (long long)n, part, SampleXf{mask, seed, temp});
+    if (e == cudaSuccess)
+        e = tb_launch(ctx, k_argmax_p2, dim3((unsigned)rows), dim3(AMAX_THREADS), 0, (const unsigned long long*)part,
+                      nparts, out_idx, (unsigned long long*)nullptr, 0u, (int*)nullptr);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "sample_argmax launch: %s", cudaGetErrorString(e));
+    return TB_OK;
 }
 
 TB_API int tb_rmsnorm(tb_ctx* ctx, const float* x, const uint16_t* w16, float* y, int64_t T, int64_t H, float eps)

@@ -538,6 +538,48 @@ def argmax(x, out=None, offset=0):
     return out
 
 
+def logit_mask(logits, mask):
+    """logitMask (qwen3.js:2706-2710): tokens whose mask bit is clear -> -3e38, in place.
+    mask: int32/uint32 words [rows, ceil(n/32)]."""
+    x2 = logits.reshape(-1, logits.shape[-1])
+    rows, n = x2.shape
+    c = _ctx(logits)
+    c.check(LIB.tb_logit_mask(c.h, _p(x2), _p(mask), n, rows), "logit_mask")
+    return logits
+
+
+def gumbel_noise(logits, seed, temp):
+    """gumbelNoise (qwen3.js:2731-2737) in place with the given seed."""
+    x2 = logits.reshape(-1, logits.shape[-1])
+    rows, n = x2.shape
+    c = _ctx(logits)
+    c.check(LIB.tb_gumbel_noise(c.h, _p(x2), n, rows, int(seed) & 0xFFFFFFFF, float(temp)), "gumbel_noise")
+    return logits
+
+
+def sample_argmax(logits, mask=None, seed=0, temp=0.0, out=None):
+    """mask + Gumbel noise + argmax fused (logits untouched): one id per row."""
+    x2 = logits.reshape(-1, logits.shape[-1])
+    rows, n = x2.shape
+    out = out if out is not None else torch.empty((rows,), dtype=torch.int32, device=logits.device)
+    c = _ctx(logits)
+    c.check(LIB.tb_sample_argmax(c.h, _p(x2), n, rows, _p(mask), int(seed) & 0xFFFFFFFF, float(temp), _p(out)),
+            "sample_argmax")
+    return out
+
+
+class GumbelSeeds:
+    """The reference's per-forward seed stream (_rngSeed, qwen3.js:2730-2733):
+    starts at 0x9E3779B9 and advances before every sampled step."""
+
+    def __init__(self, seed=0x9E3779B9):
+        self.seed = seed & 0xFFFFFFFF
+
+    def next(self):
+        self.seed = (self.seed * 1664525 + 1013904223) & 0xFFFFFFFF
+        return self.seed
+
+
 def rmsnorm(x, w16, eps, y=None):
     """rmsnorm (qwen3.js:81-88)."""
     x2 = x.reshape(-1, x.shape[-1])
