@@ -49,14 +49,15 @@ MATS6 = [("q", NHQ6 * HD6, H6), ("k", NKV6 * HD6, H6), ("v", NKV6 * HD6, H6), ("
          ("gate", INTER6, H6), ("up", INTER6, H6), ("down", H6, INTER6)]
 
 
-def wbytes(N, K):
-    """int4 G32 weight bytes: packed nibbles + f16 scales."""
-    return N * K // 2 + N * (K // 32) * 2
+def wbytes(N, K, tern=False):
+    """int4 G32 weight bytes (packed nibbles + f16 scales), or ternary WebGPU-layout
+    bytes (2-bit codes + f16 scales)."""
+    return N * K // (4 if tern else 2) + N * (K // 32) * 2
 
 
-def gemv_bytes(N, K, B, act_bytes):
+def gemv_bytes(N, K, B, act_bytes, tern=False):
     """packed weights + scales read once, B activation rows in, B output rows out."""
-    return wbytes(N, K) + B * K * act_bytes + B * N * 4
+    return wbytes(N, K, tern) + B * K * act_bytes + B * N * 4
 
 
 def step_matrices(cfg, P):
@@ -75,14 +76,14 @@ def kv_bytes(cfg, P, S):
     return 2 * S * row * (1 + 4 / 32)
 
 
-def step_bytes(cfg, P, B, S):
+def step_bytes(cfg, P, B, S, tern=False):
     """Algorithmic HBM bytes of one rank's step: every weight once, the KV
     context of every sequence, activations in/out of the GEMVs."""
     tot = 0
     q8 = 1 + 4 / 32
     for name, N, K, n in step_matrices(cfg, P):
-        act = 4 if (name == "lm_head" and B == 1) else q8
-        tot += n * gemv_bytes(N, K, B, act)
+        act = 4 if (name == "lm_head" and B == 1 and not tern) else q8
+        tot += n * gemv_bytes(N, K, B, act, tern)
     tot += cfg["layers"] * B * kv_bytes(cfg, P, S)
     return int(tot)
 
@@ -159,9 +160,11 @@ def load_peaks():
 # the decode model
 # ---------------------------------------------------------------------------
 
-def build_model(cfg, dev, batch, context, extra_rows, P, rank, seed=1234):
+def build_model(cfg, dev, batch, context, extra_rows, P, rank, seed=1234, ternary=False):
     """A Qwen3 rank with random weights (same full tensors on every rank; each
-    keeps its shard) and a cache prefilled to context - 1 rows."""
+    keeps its shard) and a cache prefilled to context - 1 rows.  ternary: the
+    projections and lm_head are Bonsai-style ternary bf16 ({-m, 0, +m} per
+    32-group, m U(0.005, 0.055)), which the loader stores as ternary records."""
     import torch
     import tabinfer_b200 as tb
     full = dict(cfg, max_seq=context + extra_rows, batch=batch, tp_size=P, tp_rank=rank)
@@ -174,12 +177,19 @@ def build_model(cfg, dev, batch, context, extra_rows, P, rank, seed=1234):
         g.manual_seed(seed * 1000 + k)
         if std is None:
             w = (1.0 + 0.1 * torch.randn(shape, device=dev, generator=g)).to(torch.bfloat16)
+        elif ternary and ("_proj." in name or name == "lm_head.weight"):
+            N, K = shape
+            mag = (torch.rand(N, K // 32, device=dev, generator=g) * 0.05 + 0.005).view(torch.int32) >> 16
+            t = torch.randint(-1, 2, (N, K), device=dev, generator=g, dtype=torch.int32)
+            bits = torch.where(t == 0, torch.zeros_like(t), mag.repeat_interleave(32, dim=1) | ((t < 0).int() << 15))
+            w = torch.where(bits >= 32768, bits - 65536, bits).to(torch.int16)
+            del t, bits, mag
         else:
             w = (torch.randn(shape, device=dev, generator=g) * std).to(torch.bfloat16)
         m.load(name, w.view(torch.int16))
 
     load("model.embed_tokens.weight", (V, H), 0.02, 0)
-    load("lm_head.weight", (V, H), 0.02, 0)          # tied: the same bf16 table
+    load("lm_head.weight", (V, H), 0.02, 0)          # tied: the same bf16 table (int4); ternary: its own
     load("model.norm.weight", (H,), None, 1)
     k = 2
     for l in range(cfg["layers"]):
@@ -682,6 +692,52 @@ def profile_gemm(M, N, K):
     print("profile gemm done", flush=True)
 
 
+def bonsai_extra(dev, peak_gbs, stream, context=4096):
+    """Bonsai-1.7B (the Qwen3-1.7B architecture with ternary projections and
+    lm_head, loaded as ternary WebGPU-layout records) through the recorded
+    decode step: tok/s at batch 1, context 4096."""
+    import torch
+    m = build_model(Q17, dev, 1, context, 16, 1, 0, seed=77, ternary=True)
+    m.set_tokens([1000], [context - 1])
+    for _ in range(5):
+        m.step()
+    torch.cuda.synchronize(dev)
+    ms = time_steps(m, 50, stream) / 50
+    nb = step_bytes(Q17, 1, 1, context, tern=True)
+    kinds = sorted({m.weight_format(n) for n in ("lm_head.weight", "model.layers.0.mlp.down_proj.weight")})
+    m.close()
+    torch.cuda.synchronize(dev)
+    return {"tok_per_s": round(1e3 / ms, 1), "ms_per_step": round(ms, 4), "bytes_per_step": int(nb),
+            "step_hbm_gbs": round(nb / (ms * 1e-3) / 1e9, 1), "frac_of_peak": round(nb / (ms * 1e-3) / 1e9 / peak_gbs, 4),
+            "weight_formats": kinds, "reference_webgpu_tok_per_s": "21.7 (Iris Xe)"}
+
+
+def prefill_attn_extra(dev, peak_tf, stream):
+    """int8-KV prefill attention of one Qwen3-1.7B layer (16 q / 8 kv heads of
+    128) over T = S = 512 / 2048 / 8192: TFLOP/s of the causal 4 * pairs * hd * heads."""
+    import torch
+    import tabinfer_b200 as tb
+    g = torch.Generator(device=dev).manual_seed(9)
+    nHq, nKv, hd = Q17["n_heads"], Q17["n_kv_heads"], Q17["head_dim"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    for T in (512, 2048, 8192):
+        S = T
+        Kq = torch.randint(-127, 128, (S, nKv * hd), device=dev, dtype=torch.int32, generator=g).to(torch.int8)
+        Vq = torch.randint(-127, 128, (S, nKv * hd), device=dev, dtype=torch.int32, generator=g).to(torch.int8)
+        Ks = torch.rand(S, nKv * hd // 32, device=dev, generator=g) * 0.02
+        Vs = torch.rand(S, nKv * hd // 32, device=dev, generator=g) * 0.02
+        q = torch.randn(T, nHq * hd, device=dev, generator=g)
+        o = torch.empty(T, nHq * hd, device=dev)
+        ms = _cold_time(lambda: tb.attention_prefill_q8(q, (Kq, Ks, Vq, Vs), S, nHq, nKv, hd, out=o), flush, stream)
+        fl = 4 * (T * (T + 1) / 2) * hd * nHq
+        tf = fl / (ms * 1e-3) / 1e12
+        out["T%d" % T] = {"us": round(ms * 1e3, 1), "tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / peak_tf, 4)}
+    del flush
+    torch.cuda.synchronize(dev)
+    return out
+
+
 def profile_lm_head(kind):
     """Three cold-L2 batch-1 lm_head GEMVs (151936 x 2048, RMSNorm fused) of one
     weight kind -- int4_f32 (gemvQ), int4_dp4a (rmsnormQ + gemvDP4) or tern
@@ -963,6 +1019,8 @@ def main():
             "measured" if peaks else "fallback 1590")
         extras["moe_int3_lfm2.5"] = moe_extra(dev, peak, stream)
         extras["ternary_wgsl_bonsai_1.7b"] = tern_extra(dev, peak, peaks.get("bf16_tflops", 1590.0), stream)
+        extras["ternary_wgsl_bonsai_1.7b"]["decode_step_context4096"] = bonsai_extra(dev, peak, stream)
+        extras["prefill_attention_1.7b"] = prefill_attn_extra(dev, peaks.get("bf16_tflops", 1590.0), stream)
         sec, reps, dt = cpu_step_seconds(1, 12.0)
         cpu = {"value": round(B / sec, 4), "unit": "tok/s", "cores": 1, "kind": "port",
                "sample": "2 of 28 decoder layers (7 matrices each) + 1/16 of the lm_head rows, %d repetitions in "
