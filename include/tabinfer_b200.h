@@ -115,8 +115,10 @@ TB_API int tb_gemv_int4_f32(tb_ctx *ctx, float *y, const float *x, const uint32_
 /* The linearQ router for one int4 matrix, models/qwen3.js:1588-1608:
  * T==1 and N<16384 -> quantQ8 + gemvDP4; T==1 and N>=16384 -> gemvQ;
  * 1<T<=8 -> per-token int8 (QUANTQ8T) x int4 math of gemmDP4A (:1397-1407);
- * T>8 -> the f16 prefill GEMM (gemmQ, tb_gemm_int4_g32) when T % 128 == 0,
- * N % 256 == 0 and K % 64 == 0, else TB_ERR_UNSUPPORTED. */
+ * T>8 -> QUANTQ8T into context scratch + gemmDP4A with exact group sums
+ * (tb_gemm_dp4, the reference's default; its __noDp4Gemm f16 route is
+ * tb_gemm_int4_g32) when T, N and K are multiples of 128, else
+ * TB_ERR_UNSUPPORTED. */
 TB_API int tb_linear_int4(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
                           const uint16_t *scales, int64_t T, int64_t N, int64_t K, int acc);
 
@@ -400,6 +402,26 @@ TB_API int tb_embed_gather(tb_ctx *ctx, const uint32_t *ids, int64_t idoff,
 TB_API int tb_gemm_int4_g32(tb_ctx *ctx, float *y, const void *x, int x_bf16, const uint32_t *pack,
                             const uint16_t *scales, int64_t M, int64_t N, int64_t K, int acc);
 
+/* The reference's integer prefill GEMMs, gemmDP4A (int4) and gemmTern (ternary
+ * WebGPU layout), qwen3.js:1321-1420, with their exact arithmetic: per 32-group
+ * the int8 activation (QUANTQ8T xq int8 [M][K], xs f32 [M][K/32]) times the int8
+ * weight (nib - 8 or code - 1) summed exactly in int32 on the tensor cores, then
+ * y (epilogue)= sum_g f32(s) * xs * sum in f32.  tern selects the weight layout.
+ * epilogue: 0 y =, 1 y +=, 2 y = silu(y) * (fused swiglu).  M, N, K % 128 == 0;
+ * xq, xs, pack 16-byte, scales and y 8-byte aligned. */
+TB_API int tb_gemm_dp4(tb_ctx *ctx, float *y, const int8_t *xq, const float *xs, const uint32_t *pack,
+                       const uint16_t *scales, int64_t M, int64_t N, int64_t K, int epilogue, int tern);
+
+/* gemmDP4A's data flow on tcgen05 with f16 operands (a faster, rounded form of
+ * tb_gemm_dp4 -- linearQ routes to the exact one, qwen3.js:1605-1607): X as QUANTQ8T rows xq int8 [M][K] + xs f32 [M][K/32]
+ * (tb_quant_q8), W int4 G32; y = f16(xs*q) . f16((nib-8)*s)^T summed in f32
+ * (the reference sums each group's int8 products exactly; the f16 rounding of
+ * xs*q is the only difference, ~2^-11).  epilogue: 0 y =, 1 y +=, 2 y =
+ * silu(y) * (the forward's swiglu fused: y holds the gate projection).
+ * M % 128, N % 256, K % 64 == 0. */
+TB_API int tb_gemm_int4_q8(tb_ctx *ctx, float *y, const int8_t *xq, const float *xs, const uint32_t *pack,
+                           const uint16_t *scales, int64_t M, int64_t N, int64_t K, int epilogue);
+
 /* ---- int3 mixture of experts (LFM2.5, models/lfm25.js) ---------------------
  * int3 layout as the reference: per (row, 32-group) three u32 bitplanes of the
  * stored value q3 + 4 (bit i of plane p = bit p of weight i) and an f16 scale;
@@ -498,6 +520,16 @@ enum { TB_QW_FMT_INT4 = 0, TB_QW_FMT_TERN = 1, TB_QW_FMT_F16 = 2 };
  * each cached segment; synchronous for pageable host memory. */
 TB_API int tb_qwen3_set_weight_q(tb_qwen3 *m, int kind, int layer, int fmt, const void *data,
                                  const void *scales, int64_t rows, int64_t cols);
+/* forward(ids, posBase) at T > 1 -- prefill -- for sequence `seq` (qwen3.js:
+ * 3938-4069): T token ids (host) at positions pos0 .. pos0+T-1 run through every
+ * layer as GEMMs (QUANTQ8T + tb_gemm_dp4: gemmDP4A / gemmTern with exact group
+ * sums, residual and SwiGLU fused into their epilogues), the rows' K/V are written to the
+ * sequence's cache and the int8-KV prefill attention runs over it; the last
+ * row's lm_head + argmax sets ids[seq] and pos[seq] = pos0 + T, so the next
+ * tb_qwen3_decode_step continues the sequence.  Returns when done.  tp_size 1;
+ * hidden, heads*head_dim, kv_heads*head_dim and intermediate multiples of 128.
+ * Buffers grow on the first call for a larger T (allocation). */
+TB_API int tb_qwen3_prefill(tb_qwen3 *m, int seq, const uint32_t *ids, int64_t T, int64_t pos0);
 /* The format tb_qwen3_set_weight chose for a weight (TB_QW_FMT_*), or -1 if unset. */
 TB_API int tb_qwen3_weight_format(const tb_qwen3 *m, int kind, int layer);
 /* This rank's cache of a layer: int8 [batch][max_seq][n_kv/tp*hd] and f32

@@ -339,6 +339,16 @@ def attn_decode_q8(q, Kq, Ks, Vq, Vs, S, nHq, nKv, hd):
     return out
 
 
+def attn_decode_q8_f16ops(q, Kq, Ks, Vq, Vs, S, nHq, nKv, hd):
+    """decode attention at the reference's f16 prefill-kernel operand precision (q, K, V, p in f16)."""
+    out = np.zeros(nHq * hd, np.float64)
+    lib().tbo_attn_decode_q8_f16ops(_ptr(np.ascontiguousarray(q, np.float32)), _ptr(np.ascontiguousarray(Kq, np.int8)),
+                                    _ptr(np.ascontiguousarray(Ks, np.float32)), _ptr(np.ascontiguousarray(Vq, np.int8)),
+                                    _ptr(np.ascontiguousarray(Vs, np.float32)), _I(S), _I(nHq), _I(nKv), _I(hd),
+                                    _ptr(out))
+    return out
+
+
 def attn_prefill_q8(q, Kq, Ks, Vq, Vs, T, S, nHq, nKv, hd):
     """attentionQ8 at T > 1 (qwen3.js:2534-2577), causal over the int8 cache, in double."""
     out = np.zeros((T, nHq * hd), np.float64)

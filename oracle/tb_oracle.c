@@ -589,6 +589,44 @@ TBO_API void tbo_attn_decode_q8(const float *q, const int8_t *Kq, const float *K
     free(sc);
 }
 
+/* The same decode attention at the operand precision of the reference's f16
+ * prefill kernel (attnF16Wgsl via _q8PrefillWgsl, qwen3.js:2396-2532, 2540-2560:
+ * q, the dequantized K and V (max(c/127,-1) * scale, formed in f32) and the
+ * softmax weights p are f16 values), summed exactly here; l = sum of the
+ * unrounded p as in its f32 lsh. */
+TBO_API void tbo_attn_decode_q8_f16ops(const float *q, const int8_t *Kq, const float *Ks,
+                                       const int8_t *Vq, const float *Vs, int64_t S,
+                                       int64_t nHq, int64_t nKv, int64_t hd, double *out)
+{
+    const int64_t grp = nHq / nKv, row = nKv * hd, rowg = row / 32;
+    double *sc = (double *)malloc(sizeof(double) * (size_t)(S > 0 ? S : 1));
+    const double scale = 1.0 / sqrt((double)hd);
+    for (int64_t hq = 0; hq < nHq; hq++) {
+        int64_t hk = hq / grp;
+        double mx = -INFINITY;
+        for (int64_t t = 0; t < S; t++) {
+            double s = 0.0;
+            for (int64_t d = 0; d < hd; d++) {
+                float kf = fmaxf((float)Kq[t * row + hk * hd + d] / 127.0f, -1.0f) * Ks[t * rowg + hk * (hd / 32) + d / 32];
+                s += (double)(_Float16)q[hq * hd + d] * (double)(_Float16)kf;
+            }
+            sc[t] = s * scale;
+            if (sc[t] > mx) mx = sc[t];
+        }
+        double l = 0.0;
+        for (int64_t t = 0; t < S; t++) { sc[t] = exp(sc[t] - mx); l += sc[t]; }
+        for (int64_t d = 0; d < hd; d++) {
+            double o = 0.0;
+            for (int64_t t = 0; t < S; t++) {
+                float vf = fmaxf((float)Vq[t * row + hk * hd + d] / 127.0f, -1.0f) * Vs[t * rowg + hk * (hd / 32) + d / 32];
+                o += (double)(_Float16)(float)sc[t] * (double)(_Float16)vf;
+            }
+            out[hq * hd + d] = S > 0 ? o / l : 0.0;
+        }
+    }
+    free(sc);
+}
+
 /* int8-KV prefill attention, attentionQ8 with T > 1 (qwen3.js:2534-2577: the
  * flash kernels ATTN_WGSL / attnF16Wgsl with int8 tile loads): query i of T sits
  * at position S - T + i and sees keys 0 .. S - T + i (the causal mask

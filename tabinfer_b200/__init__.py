@@ -16,7 +16,7 @@ from .ops import (  # noqa: F401
     requant_int3, moe_router, moe_ffn_int3,
     gate_up_silu_dp4, pack_ternary, quantize_act, gemv_tern, linear_tern,
     quantize_tern_bf16, gemv_tern_wgsl, gemv_tern_wgsl_dp4a_multi, gate_up_silu_tern, gate_up_silu_tern_dp4a,
-    gemm_tern, linear_tern_wgsl,
+    gemm_tern, gemm_dp4, gemm_dp4_f16, linear_tern_wgsl,
     attn_prep_q8, kv_quant_write, attention_decode_q8, attention_prefill_q8, argmax,
     logit_mask, gumbel_noise, sample_argmax, GumbelSeeds, rmsnorm, embed_gather,
 )

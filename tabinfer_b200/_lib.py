@@ -62,6 +62,8 @@ SIGNATURES = {
     "tb_gateup_silu_tern_wgsl_q8": [P, P, P, P, P, P, P, P, I64, I64, I32],
     "tb_gateup_silu_tern_wgsl_dp4a": [P, P, P, P, F32, P, P, P, P, I64, I64, I32],
     "tb_gemm_tern_wgsl": [P, P, P, P, P, P, I64, I64, I64, I32],
+    "tb_gemm_int4_q8": [P, P, P, P, P, P, I64, I64, I64, I32],
+    "tb_gemm_dp4": [P, P, P, P, P, P, I64, I64, I64, I32, I32],
     "tb_linear_tern_wgsl": [P, P, P, P, P, I64, I64, I64, I32],
     "tb_quant_act_q8": [P, P, P, P, P, I64, I64],
     "tb_gemv_tern_q2g64": [P, P, P, P, P, P, I64, I64, I32],
@@ -85,6 +87,7 @@ SIGNATURES = {
     "tb_qwen3_destroy": [P],
     "tb_qwen3_set_weight": [P, I32, I32, P, I64, I64],
     "tb_qwen3_set_weight_q": [P, I32, I32, I32, P, P, I64, I64],
+    "tb_qwen3_prefill": [P, I32, P, I64, I64],
     "tb_qwen3_weight_format": [P, I32, I32],
     "tb_qwen3_kv": [P, I32, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],
     "tb_qwen3_io": [P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],

@@ -87,15 +87,17 @@ __device__ __forceinline__ void quant_row(float x, int hd, int8_t* dq, float* ds
 // ---- fused prep: q rope, k rope + quant-write, v quant-write ---------------
 // grid = (nHq + 2*nKv, B) CTAs, block = hd threads (hd % 32 == 0, hd <= 256).
 // Sequence b reads q/k/v row b, writes qr row b and cache row pos_b of its own
-// cache (cache_rows rows per sequence); pos_b = dpos[b] when dpos is given
-// (graph-replayable decode), else `pos`.
+// cache (cache_rows rows per sequence, caches seq_stride rows apart: seq_stride =
+// cache_rows for a batch of sequences, 0 for the T tokens of one sequence's
+// prefill); pos_b = dpos[b] when dpos is given (graph-replayable decode), else `pos`.
 __global__ void __launch_bounds__(256) k_attn_prep(const float* __restrict__ q, const float* __restrict__ k,
                                                    const float* __restrict__ v, const uint16_t* __restrict__ qw,
                                                    const uint16_t* __restrict__ kw, float* __restrict__ qr,
                                                    int8_t* __restrict__ Kq, float* __restrict__ Ks,
                                                    int8_t* __restrict__ Vq, float* __restrict__ Vs,
                                                    int nHq, int nKv, int hd, long long pos, float theta, float eps,
-                                                   const int* __restrict__ dpos, long long cache_rows, int* err)
+                                                   const int* __restrict__ dpos, long long cache_rows,
+                                                   long long seq_stride, int* err)
 {
     __shared__ float rk[256];
     __shared__ float red[8];
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(256) k_attn_prep(const float* __restrict__ q, 
             return;
         }
     }
-    const long long cache_off = (long long)b * cache_rows * nKv * hd;
+    const long long cache_off = (long long)b * seq_stride * nKv * hd;
     Kq += cache_off; Vq += cache_off; Ks += cache_off / 32; Vs += cache_off / 32;
     q += (long long)b * nHq * hd; qr += (long long)b * nHq * hd;
     k += (long long)b * nKv * hd; v += (long long)b * nKv * hd;
@@ -606,6 +608,21 @@ int tb_attn_check(tb_ctx* ctx, const float* qr, const int8_t* Kq, const float* K
     return TB_OK;
 }
 
+// the prep of T tokens of ONE sequence (prefill): row t reads q/k/v row t,
+// writes qr row t and cache row dpos[t] < cache_rows of the same cache
+int tb_attn_prep_rows_impl(tb_ctx* ctx, const float* q, const float* k, const float* v, const uint16_t* qw16,
+                           const uint16_t* kw16, float* qr, int8_t* Kq, float* Ks, int8_t* Vq, float* Vs, int64_t nHq,
+                           int64_t nKv, int64_t hd, int64_t T, int64_t cache_rows, const int32_t* dpos, float theta,
+                           float eps)
+{
+    TB_REQUIRE(ctx, hd % 32 == 0 && hd >= 32 && hd <= 256 && T > 0 && T <= 65535, "attn prep rows: bad shape");
+    cudaError_t e = tb_launch(ctx, k_attn_prep, dim3((unsigned)(nHq + 2 * nKv), (unsigned)T), dim3((unsigned)hd), 0,
+                              q, k, v, qw16, kw16, qr, Kq, Ks, Vq, Vs, (int)nHq, (int)nKv, (int)hd, 0LL, theta, eps,
+                              (const int*)dpos, (long long)cache_rows, 0LL, ctx->dev_error);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_prep launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
 extern "C" {
 
 TB_API int tb_attn_prep_q8(tb_ctx* ctx, const float* q, const float* k, const float* v, const uint16_t* qw16,
@@ -618,7 +635,7 @@ TB_API int tb_attn_prep_q8(tb_ctx* ctx, const float* q, const float* k, const fl
     TB_REQUIRE(ctx, nHq > 0 && nKv > 0 && pos >= 0, "bad head counts or position");
     cudaError_t e = tb_launch(ctx, k_attn_prep, dim3((unsigned)(nHq + 2 * nKv)), dim3((unsigned)hd), 0, q, k, v, qw16,
                               kw16, qr, Kq, Ks, Vq, Vs, (int)nHq, (int)nKv, (int)hd, (long long)pos, theta, eps,
-                              (const int*)nullptr, (long long)(pos + 1), ctx->dev_error);
+                              (const int*)nullptr, (long long)(pos + 1), 0LL, ctx->dev_error);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_prep launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -634,10 +651,12 @@ TB_API int tb_attn_prep_q8_batch(tb_ctx* ctx, const float* q, const float* k, co
     TB_REQUIRE(ctx, nHq > 0 && nKv > 0 && batch > 0 && batch <= 65535 && cache_rows > 0, "bad head counts, batch or cache rows");
     cudaError_t e = tb_launch(ctx, k_attn_prep, dim3((unsigned)(nHq + 2 * nKv), (unsigned)batch), dim3((unsigned)hd), 0,
                               q, k, v, qw16, kw16, qr, Kq, Ks, Vq, Vs, (int)nHq, (int)nKv, (int)hd, 0LL, theta, eps,
-                              (const int*)dpos, (long long)cache_rows, ctx->dev_error);
+                              (const int*)dpos, (long long)cache_rows, (long long)cache_rows, ctx->dev_error);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_prep launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
+
+
 
 TB_API int tb_kv_quant_write(tb_ctx* ctx, const float* kr, const float* v, int8_t* Kq, float* Ks, int8_t* Vq,
                              float* Vs, int64_t T, int64_t nKv, int64_t hd, int64_t posBase)

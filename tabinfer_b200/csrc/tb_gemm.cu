@@ -33,11 +33,14 @@ constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_
 // X as given (bf16 or f32), packed W, W scales; chunk-major (16-byte chunk c of
 // producer thread t at c * PROD + t) so copies and reads are bank-conflict free
 constexpr int RAW_W = PROD * 16, RAW_S = PROD * 4;
-enum XMode { X_F32 = 0, X_BF16 = 1, X_Q8_TERN = 2 };
+// X operand: f32 / bf16 rows (gemmQ), or QUANTQ8T int8 rows + f32 group scales
+// (gemmDP4A and gemmTern); W: int4, or ternary for X_Q8_TERN
+enum XMode { X_F32 = 0, X_BF16 = 1, X_Q8_TERN = 2, X_Q8_INT4 = 3 };
 template <int MODE> struct Cfg {
     static constexpr bool TERN = MODE == X_Q8_TERN;
+    static constexpr bool XQ8 = MODE == X_Q8_TERN || MODE == X_Q8_INT4;
     static constexpr int XC = MODE == X_F32 ? 4 : (MODE == X_BF16 ? 2 : 1);   // raw X chunks per producer thread
-    static constexpr int XS = TERN ? PROD * 4 : 0;           // int8 rows: one f32 group scale per thread
+    static constexpr int XS = XQ8 ? PROD * 4 : 0;            // int8 rows: one f32 group scale per thread
     static constexpr int X = PROD * XC * 16 + XS;
     static constexpr int WB = TERN ? PROD * 8 : RAW_W;       // raw weight bytes (ternary: 2 words per thread)
     static constexpr int RSTAGE = X + WB + RAW_S;
@@ -183,7 +186,7 @@ template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
 {
     using R = Cfg<MODE>;
-    constexpr bool XBF16 = MODE == X_BF16, TERN = R::TERN;
+    constexpr bool XBF16 = MODE == X_BF16, TERN = R::TERN, XQ8 = R::XQ8;
     constexpr int NST = R::NST;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -230,8 +233,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
                                     ((size_t)(m0 + xr) * a.K + k0 + 16 * xq) * (MODE == X_F32 ? 4 : (XBF16 ? 2 : 1));
 #pragma unroll
                 for (int c = 0; c < R::XC; c++) cp16(rs + (c * PROD + tid) * 16, xs + 16 * c);
+                if (XQ8) cp4(rs + PROD * 16 + tid * 4, a.xs + (size_t)(m0 + xr) * (a.K / 32) + k0 / 32 + (xq >> 1));
                 if (TERN) {
-                    cp4(rs + PROD * 16 + tid * 4, a.xs + (size_t)(m0 + xr) * (a.K / 32) + k0 / 32 + (xq >> 1));
                     cp8(rs + R::X + tid * 8, a.pack + (size_t)(n0 + wr) * (a.K / 16) + k0 / 16 + 2 * wh);
                 } else {
                     cp16(rs + R::X + tid * 16, a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8 + 4 * wh);
@@ -254,7 +257,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
             uint8_t* Bt = A + A_BYTES;
             const uint8_t* rs = rawbase + (i % R::NR) * R::RSTAGE;
             // X: 16 values of row xr -> f16 chunks 2 xq, 2 xq + 1
-            if (TERN) {
+            if (XQ8) {
                 const uint4 v = *reinterpret_cast<const uint4*>(rs + tid * 16);
                 const float xsc = *reinterpret_cast<const float*>(rs + PROD * 16 + tid * 4);
                 const uint32_t in[4] = {v.x, v.y, v.z, v.w};
@@ -364,9 +367,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
                 for (int c = 0; c < 8; c++) {
                     float4 v = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
                                            __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
-                    if (a.acc) {
+                    if (a.acc == 1) {          // fused residual: y += X W^T
                         const float4 o = yp[c];
                         v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+                    } else if (a.acc == 2) {   // fused SwiGLU: y holds gate, y = silu(gate) * (X W_up^T)
+                        const float4 gt = yp[c];
+                        v.x = __fdiv_rn(gt.x, 1.0f + expf(-gt.x)) * v.x;
+                        v.y = __fdiv_rn(gt.y, 1.0f + expf(-gt.y)) * v.y;
+                        v.z = __fdiv_rn(gt.z, 1.0f + expf(-gt.z)) * v.z;
+                        v.w = __fdiv_rn(gt.w, 1.0f + expf(-gt.w)) * v.w;
                     }
                     yp[c] = v;
                 }
@@ -414,6 +423,25 @@ int tb_gemm_int4_impl(tb_ctx* ctx, float* y, const void* x, int x_bf16, const ui
     return x_bf16 ? launch_gemm<X_BF16>(ctx, a) : launch_gemm<X_F32>(ctx, a);
 }
 
+// gemmDP4A (qwen3.js:1232-1400, linearQ's default prefill route) on the tensor
+// cores: QUANTQ8T rows become f16(xs * q), int4 weights f16((nib - 8) * s).
+// epilogue: 0 store, 1 y += (fused residual), 2 y = silu(y) * (fused SwiGLU).
+int tb_gemm_q8_int4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                         const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue)
+{
+    TB_REQUIRE(ctx, y && xq && xs && pack && scales, "null pointer");
+    TB_REQUIRE(ctx, M > 0 && M % BM == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
+               "gemm_q8: M %% %d, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BM, BN, BK,
+               (long long)M, (long long)N, (long long)K);
+    TB_REQUIRE(ctx, M / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_q8: shape too large");
+    TB_REQUIRE(ctx, epilogue >= 0 && epilogue <= 2, "gemm_q8: bad epilogue %d", epilogue);
+    TB_REQUIRE(ctx, TB_ALIGNED(xq, 16) && TB_ALIGNED(xs, 4) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) &&
+                        TB_ALIGNED(y, 16),
+               "gemm_q8: xq, pack, y 16-byte and xs, scales 4-byte aligned");
+    GemmArgs a{xq, xs, pack, scales, y, (int)M, (int)N, (int)K, epilogue, ctx->dev_error};
+    return launch_gemm<X_Q8_INT4>(ctx, a);
+}
+
 int tb_gemm_tern_wgsl_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
                            const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc)
 {
@@ -425,8 +453,16 @@ int tb_gemm_tern_wgsl_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float*
     TB_REQUIRE(ctx, TB_ALIGNED(xq, 16) && TB_ALIGNED(xs, 4) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) &&
                         TB_ALIGNED(y, 16),
                "gemm_tern: xq, pack, y 16-byte and xs, scales 4-byte aligned");
-    GemmArgs a{xq, xs, pack, scales, y, (int)M, (int)N, (int)K, acc ? 1 : 0, ctx->dev_error};
+    TB_REQUIRE(ctx, acc >= 0 && acc <= 2, "gemm_tern: bad epilogue %d", acc);
+    GemmArgs a{xq, xs, pack, scales, y, (int)M, (int)N, (int)K, acc, ctx->dev_error};
     return launch_gemm<X_Q8_TERN>(ctx, a);
+}
+
+extern "C" TB_API int tb_gemm_int4_q8(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                                      const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return tb_gemm_q8_int4_impl(ctx, y, xq, xs, pack, scales, M, N, K, epilogue);
 }
 
 extern "C" TB_API int tb_gemm_tern_wgsl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,

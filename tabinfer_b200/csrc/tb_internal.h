@@ -63,3 +63,15 @@ int tb_quant_q8_impl(tb_ctx* ctx, const float* x, int8_t* xq, float* xs, int32_t
 // flag |= 1 when not ternary (zero it first); pack == nullptr checks only
 int tb_quant_tern_wgsl_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint32_t* pack, uint16_t* scales,
                                     int64_t N, int64_t K, int* flag);
+// gemmDP4A on the tensor cores (QUANTQ8T rows x int4); epilogue 0 store, 1 add, 2 SwiGLU
+int tb_gemm_q8_int4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                         const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue);
+// attention prep of T tokens of one sequence (prefill): cache row dpos[t] of one cache
+int tb_attn_prep_rows_impl(tb_ctx* ctx, const float* q, const float* k, const float* v, const uint16_t* qw16,
+                           const uint16_t* kw16, float* qr, int8_t* Kq, float* Ks, int8_t* Vq, float* Vs, int64_t nHq,
+                           int64_t nKv, int64_t hd, int64_t T, int64_t cache_rows, const int32_t* dpos, float theta,
+                           float eps);
+// the reference's integer prefill GEMM (gemmDP4A / gemmTern) with exact per-32-group
+// int8 sums (tb_gemm_dp4.cu); M % 128, N % 128, K % 128; epilogue 0 store, 1 add, 2 SwiGLU
+int tb_gemm_dp4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                     const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue, bool tern);

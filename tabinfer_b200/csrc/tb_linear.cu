@@ -16,12 +16,19 @@ TB_API int tb_linear_int4(tb_ctx* ctx, float* y, const float* x, const uint32_t*
     TB_REQUIRE(ctx, K > 0 && K % 32 == 0, "K must be a positive multiple of 32");
     if (T == 1 && N >= 16384) return tb_gemv_f32_impl(ctx, y, x, pack, scales, N, K, 1, acc);
     if (T > 8) {
-        // prefill: the f16 tensor-core GEMM (gemmQ) where its tile shapes fit
-        if (T % 128 == 0 && N % 256 == 0 && K % 64 == 0)
-            return tb_gemm_int4_impl(ctx, y, x, 0, pack, scales, T, N, K, acc);
-        return tb_fail(ctx, TB_ERR_UNSUPPORTED,
-                       "linear_int4: T=%lld > 8 needs T %% 128 == 0, N %% 256 == 0, K %% 64 == 0 (prefill GEMM)",
-                       (long long)T);
+        // prefill: linearQ's default gemmDP4A (qwen3.js:1605-1607) -- QUANTQ8T rows
+        // into context scratch, then the tensor-core GEMM on them
+        if (T % 128 != 0 || N % 128 != 0 || K % 128 != 0)
+            return tb_fail(ctx, TB_ERR_UNSUPPORTED,
+                           "linear_int4: T=%lld > 8 needs T, N and K multiples of 128 (prefill GEMM)", (long long)T);
+        const size_t xq_b = up256((size_t)T * K), xs_b = up256((size_t)T * (K / 32) * 4);
+        unsigned char* scr = static_cast<unsigned char*>(tb_ctx_scratch(ctx, xq_b + xs_b));
+        if (!scr) return TB_ERR_NOMEM;
+        int8_t* xq = reinterpret_cast<int8_t*>(scr);
+        float* xs = reinterpret_cast<float*>(scr + xq_b);
+        int rc = tb_quant_q8_impl(ctx, x, xq, xs, nullptr, T, K);
+        if (rc) return rc;
+        return tb_gemm_dp4_impl(ctx, y, xq, xs, pack, scales, T, N, K, acc ? 1 : 0, false);
     }
     // quantQ8 / QUANTQ8T runs inside the GEMV prologue (bit-identical int8 rows)
     return tb_gemv_dp4a_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
@@ -30,8 +37,8 @@ TB_API int tb_linear_int4(tb_ctx* ctx, float* y, const float* x, const uint32_t*
 // linearQ's ternary branch (qwen3.js:1594-1598).  T <= 8 runs the ternary GEMV
 // with quantQ8 in its prologue: per 32-group the same exact int32 sum and f32
 // scaling as the reference's gemvTern (T = 1) and gemmTern tiles (T > 1).
-// T > 8 quantizes the rows (QUANTQ8T) into context scratch and runs the
-// tcgen05 GEMM on them (gemmTern).
+// T > 8 quantizes the rows (QUANTQ8T) into context scratch and runs gemmTern
+// with its exact group sums (tb_gemm_dp4).
 TB_API int tb_linear_tern_wgsl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
                                int64_t T, int64_t N, int64_t K, int acc)
 {
@@ -39,9 +46,9 @@ TB_API int tb_linear_tern_wgsl(tb_ctx* ctx, float* y, const float* x, const uint
     TB_REQUIRE(ctx, T >= 1, "T must be >= 1");
     TB_REQUIRE(ctx, K > 0 && K % 64 == 0, "K must be a positive multiple of 64");
     if (T <= 8) return tb_gemv_tern_wgsl_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
-    if (T % 128 != 0 || N % 256 != 0)
+    if (T % 128 != 0 || N % 128 != 0 || K % 128 != 0)
         return tb_fail(ctx, TB_ERR_UNSUPPORTED,
-                       "linear_tern_wgsl: T=%lld > 8 needs T %% 128 == 0 and N %% 256 == 0 (prefill GEMM)", (long long)T);
+                       "linear_tern_wgsl: T=%lld > 8 needs T, N and K multiples of 128 (prefill GEMM)", (long long)T);
     const size_t xq_b = up256((size_t)T * K), xs_b = up256((size_t)T * (K / 32) * 4);
     unsigned char* scr = static_cast<unsigned char*>(tb_ctx_scratch(ctx, xq_b + xs_b));
     if (!scr) return TB_ERR_NOMEM;
@@ -49,7 +56,7 @@ TB_API int tb_linear_tern_wgsl(tb_ctx* ctx, float* y, const float* x, const uint
     float* xs = reinterpret_cast<float*>(scr + xq_b);
     int rc = tb_quant_q8_impl(ctx, x, xq, xs, nullptr, T, K);
     if (rc) return rc;
-    return tb_gemm_tern_wgsl_impl(ctx, y, xq, xs, pack, scales, T, N, K, acc);
+    return tb_gemm_dp4_impl(ctx, y, xq, xs, pack, scales, T, N, K, acc ? 1 : 0, true);
 }
 
 TB_API int tb_linear_tern(tb_ctx* ctx, float* y, const float* x, const uint8_t* codes, const float* scales, int64_t T,

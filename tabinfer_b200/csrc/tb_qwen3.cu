@@ -118,6 +118,13 @@ struct tb_qwen3 {
     bool p2p = false;
     int ncoll = 0;                               // NCCL calls in the recorded step
     std::vector<void*> allocs;
+    // prefill (forward at T > 1): buffers of `pf_cap` rows, grown on demand
+    int64_t pf_cap = 0;
+    float *pf_x = nullptr, *pf_norm = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_qr = nullptr,
+          *pf_attn = nullptr, *pf_gate = nullptr, *pf_xs = nullptr;
+    int8_t* pf_xq = nullptr;
+    uint32_t* pf_ids = nullptr;
+    int32_t* pf_pos = nullptr;
 };
 
 namespace {
@@ -327,6 +334,116 @@ int issue_step(tb_qwen3* m)
     return TB_OK;
 }
 
+void free_prefill(tb_qwen3* m)
+{
+    for (void* p : {(void*)m->pf_x, (void*)m->pf_norm, (void*)m->pf_q, (void*)m->pf_k, (void*)m->pf_v,
+                    (void*)m->pf_qr, (void*)m->pf_attn, (void*)m->pf_gate, (void*)m->pf_xs, (void*)m->pf_xq,
+                    (void*)m->pf_ids, (void*)m->pf_pos})
+        if (p) cudaFree(p);
+    m->pf_x = m->pf_norm = m->pf_q = m->pf_k = m->pf_v = m->pf_qr = m->pf_attn = m->pf_gate = m->pf_xs = nullptr;
+    m->pf_xq = nullptr;
+    m->pf_ids = nullptr;
+    m->pf_pos = nullptr;
+    m->pf_cap = 0;
+}
+
+int prefill_buffers(tb_qwen3* m, int64_t Tp)
+{
+    if (m->pf_cap >= Tp) return TB_OK;
+    cudaStreamSynchronize(m->ctx->stream);   // earlier prefills may still use the old buffers
+    free_prefill(m);
+    const tb_qwen3_config& c = m->c;
+    const int64_t H = c.hidden, qN = (int64_t)c.n_heads * c.head_dim, kvN = (int64_t)c.n_kv_heads * c.head_dim;
+    const int64_t kmax = std::max(H, std::max(qN, (int64_t)c.intermediate));
+    bool ok = true;
+    auto get = [&](auto** p, size_t bytes) {
+        if (ok && cudaMalloc((void**)p, (bytes + 255) & ~size_t(255)) != cudaSuccess) { cudaGetLastError(); ok = false; }
+    };
+    get(&m->pf_x, Tp * H * 4); get(&m->pf_norm, Tp * H * 4);
+    get(&m->pf_q, Tp * qN * 4); get(&m->pf_k, Tp * kvN * 4); get(&m->pf_v, Tp * kvN * 4);
+    get(&m->pf_qr, Tp * qN * 4); get(&m->pf_attn, Tp * qN * 4); get(&m->pf_gate, Tp * c.intermediate * 4);
+    get(&m->pf_xq, Tp * kmax); get(&m->pf_xs, Tp * (kmax / 32) * 4);
+    get(&m->pf_ids, Tp * 4); get(&m->pf_pos, Tp * 4);
+    if (!ok) {
+        free_prefill(m);
+        return tb_fail(m->ctx, TB_ERR_NOMEM, "qwen3 prefill: cudaMalloc for %lld rows failed", (long long)Tp);
+    }
+    m->pf_cap = Tp;
+    return TB_OK;
+}
+
+// y (=, +=, = silu(y) *) W . x for the prefill rows, x already quantized (QUANTQ8T)
+int pf_gemm(tb_qwen3* m, float* y, const Mat& w, int64_t Tp, int epi)
+{
+    return tb_gemm_dp4_impl(m->ctx, y, m->pf_xq, m->pf_xs, w.pack, w.scales, Tp, w.N, w.K, epi, w.tern);
+}
+
+int pf_quant(tb_qwen3* m, const float* x, int64_t Tp, int64_t K)
+{
+    return tb_quant_q8_impl(m->ctx, x, m->pf_xq, m->pf_xs, nullptr, Tp, K);
+}
+
+// forward(ids, posBase) at T > 1 for sequence `seq` (models/qwen3.js:3938-4069,
+// the prefill branch): rmsnorm -> q/k/v (linearQ: QUANTQ8T + gemmDP4A, or
+// gemmTern, with exact group sums) -> rope + quantized KV write -> int8-KV prefill attention -> o
+// (+= residual) -> rmsnorm -> gate, up (swiglu fused) -> down (+= residual);
+// final rmsnorm + lm_head of the last row; argmax into ids[seq]; pos[seq] =
+// pos0 + T.  Rows are padded to the GEMM's 128 (zero rows stay zero).
+int prefill(tb_qwen3* m, int seq, const uint32_t* ids_host, int64_t T, int64_t pos0)
+{
+    tb_ctx* ctx = m->ctx;
+    const tb_qwen3_config& c = m->c;
+    const int64_t H = c.hidden, hd = c.head_dim, qN = m->nHq * hd, kvN = m->nKv * hd, I = m->I, V = m->V;
+    const int64_t Tp = (T + 127) / 128 * 128;
+    TRY(prefill_buffers(m, Tp));
+    std::vector<int32_t> posv((size_t)T);
+    for (int64_t t = 0; t < T; t++) posv[t] = (int32_t)(pos0 + t);
+    cudaError_t e = cudaMemcpyAsync(m->pf_ids, ids_host, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pf_pos, posv.data(), (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess && Tp > T) e = cudaMemsetAsync(m->pf_x + T * H, 0, (size_t)(Tp - T) * H * 4, ctx->stream);
+    if (e == cudaSuccess && Tp > T) e = cudaMemsetAsync(m->pf_attn + T * qN, 0, (size_t)(Tp - T) * qN * 4, ctx->stream);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "prefill setup: %s", cudaGetErrorString(e));
+    TRY(tb_embed_gather(ctx, m->pf_ids, 0, m->embed, m->pf_x, T, H));
+    const int64_t crow = (int64_t)seq * c.max_seq * kvN;   // this sequence's cache
+    for (int l = 0; l < c.layers; l++) {
+        Layer& Ly = m->L[l];
+        TRY(tb_rmsnorm(ctx, m->pf_x, Ly.ln1, m->pf_norm, Tp, H, c.rms_eps));
+        TRY(pf_quant(m, m->pf_norm, Tp, H));
+        TRY(pf_gemm(m, m->pf_q, Ly.q, Tp, 0));
+        TRY(pf_gemm(m, m->pf_k, Ly.k, Tp, 0));
+        TRY(pf_gemm(m, m->pf_v, Ly.v, Tp, 0));
+        TRY(tb_attn_prep_rows_impl(ctx, m->pf_q, m->pf_k, m->pf_v, Ly.qn, Ly.kn, m->pf_qr, Ly.Kq + crow,
+                                   Ly.Ks + crow / 32, Ly.Vq + crow, Ly.Vs + crow / 32, m->nHq, m->nKv, hd, T,
+                                   c.max_seq, m->pf_pos, c.rope_theta, c.rms_eps));
+        TRY(tb_attn_prefill_q8(ctx, m->pf_attn, m->pf_qr, Ly.Kq + crow, Ly.Ks + crow / 32, Ly.Vq + crow,
+                               Ly.Vs + crow / 32, T, pos0 + T, m->nHq, m->nKv, hd));
+        TRY(pf_quant(m, m->pf_attn, Tp, qN));
+        TRY(pf_gemm(m, m->pf_x, Ly.o, Tp, 1));
+        TRY(tb_rmsnorm(ctx, m->pf_x, Ly.ln2, m->pf_norm, Tp, H, c.rms_eps));
+        TRY(pf_quant(m, m->pf_norm, Tp, H));
+        TRY(pf_gemm(m, m->pf_gate, Ly.gate, Tp, 0));
+        TRY(pf_gemm(m, m->pf_gate, Ly.up, Tp, 2));
+        TRY(pf_quant(m, m->pf_gate, Tp, I));
+        TRY(pf_gemm(m, m->pf_x, Ly.down, Tp, 1));
+    }
+    // the last row: final norm + lm_head (linearQ at T = 1) + argmax into the history
+    const float* xl = m->pf_x + (T - 1) * H;
+    float* lg = m->logits + (int64_t)seq * V;
+    if (m->lm.tern) {
+        TRY(tb_gemv_tern_wgsl_impl(ctx, 1, &lg, &m->lm.pack, &m->lm.scales, &m->V, xl, m->fnorm, c.rms_eps, H, 1, 0));
+    } else if (V >= 16384) {
+        TRY(tb_gemv_int4_f32_norm(ctx, lg, xl, m->fnorm, c.rms_eps, m->lm.pack, m->lm.scales, V, H, 1, 0));
+    } else {
+        TRY(tb_gemv_int4_dp4a(ctx, lg, xl, m->fnorm, c.rms_eps, m->lm.pack, m->lm.scales, V, H, 1, 0));
+    }
+    TRY(tb_argmax_impl(ctx, lg, V, 1, m->ids + seq, m->amax_part, m->amax_nparts, nullptr, 0, nullptr));
+    const int32_t next = (int32_t)(pos0 + T);
+    e = cudaMemcpyAsync(m->pos + seq, &next, 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);   // host arrays above are released on return
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "prefill: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
 void release_graph(tb_qwen3* m)
 {
     if (m->exec) cudaGraphExecDestroy(m->exec);
@@ -439,6 +556,7 @@ TB_API int tb_qwen3_destroy(tb_qwen3* m)
     for (int s = 0; s < m->P && s < 8; s++)
         if (s != m->r && m->peer_arena[s]) cudaIpcCloseMemHandle(m->peer_arena[s]);
     for (void* p : m->allocs) cudaFree(p);
+    free_prefill(m);
     if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
     delete m;
     return TB_OK;
@@ -583,6 +701,26 @@ TB_API int tb_qwen3_weight_format(const tb_qwen3* m, int kind, int layer)
     if (weight_slot(const_cast<tb_qwen3*>(m), kind, layer, &w, &buf) != TB_OK) return -1;
     if (buf) return TB_QW_FMT_F16;
     return w->set ? (w->tern ? TB_QW_FMT_TERN : TB_QW_FMT_INT4) : -1;
+}
+
+TB_API int tb_qwen3_prefill(tb_qwen3* m, int seq, const uint32_t* ids, int64_t T, int64_t pos0)
+{
+    if (!m) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    const tb_qwen3_config& c = m->c;
+    TB_REQUIRE(ctx, ids != nullptr, "null ids");
+    TB_REQUIRE(ctx, seq >= 0 && seq < c.batch, "sequence %d out of range", seq);
+    TB_REQUIRE(ctx, T >= 1 && pos0 >= 0 && pos0 + T <= c.max_seq && T <= 65535,
+               "prefill of %lld tokens at %lld does not fit the %d-row cache", (long long)T, (long long)pos0, c.max_seq);
+    if (m->P != 1)
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "qwen3 prefill: tensor-parallel prefill is not built (tp_size %d)", m->P);
+    const int64_t hd = c.head_dim, qN = m->nHq * hd, kvN = m->nKv * hd, H = c.hidden;
+    const int64_t Ns[4] = {qN, kvN, H, m->I};
+    for (int64_t n : Ns)
+        if (n % 128)
+            return tb_fail(ctx, TB_ERR_UNSUPPORTED, "qwen3 prefill: GEMM needs every projection's size %% 128 == 0 (%lld)",
+                           (long long)n);
+    return prefill(m, seq, ids, T, pos0);
 }
 
 TB_API int tb_qwen3_kv(tb_qwen3* m, int layer, int8_t** Kq, float** Ks, int8_t** Vq, float** Vs)

@@ -418,6 +418,31 @@ def attention_prefill_q8(q, kv, S, nHq, nKv, hd, out=None):
     return out
 
 
+def gemm_dp4(xq, xs, pack, scales, y=None, epilogue=0, tern=False):
+    """gemmDP4A / gemmTern (qwen3.js:1321-1420) with exact per-group int8 sums, from
+    QUANTQ8T rows.  epilogue 0: y =, 1: y +=, 2: y = silu(y) * (X W^T)."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    M, K = xq2.shape
+    N = pack.shape[0]
+    y = y if y is not None else torch.zeros((M, N), dtype=torch.float32, device=xq.device)
+    c = _ctx(xq)
+    c.check(LIB.tb_gemm_dp4(c.h, _p(y), _p(xq2), _p(xs), _p(pack), _p(scales), M, N, K, int(epilogue),
+                            1 if tern else 0), "gemm_dp4")
+    return y
+
+
+def gemm_dp4_f16(xq, xs, pack, scales, y=None, epilogue=0):
+    """gemmDP4A's data flow on tcgen05 with f16 operands f16(xs*q) and f16((nib-8)*s)."""
+    xq2 = xq.reshape(-1, xq.shape[-1])
+    M, K = xq2.shape
+    N = pack.shape[0]
+    y = y if y is not None else torch.zeros((M, N), dtype=torch.float32, device=xq.device)
+    c = _ctx(xq)
+    c.check(LIB.tb_gemm_int4_q8(c.h, _p(y), _p(xq2), _p(xs), _p(pack), _p(scales), M, N, K, int(epilogue)),
+            "gemm_int4_q8")
+    return y
+
+
 def gemm_tern(xq, xs, pack, scales, y=None, acc=False):
     """gemmTern (qwen3.js:1410-1420) on the tensor cores from QUANTQ8T rows:
     y[M,N] (+)= f16(xs*xq) . f16((c-1)*s)^T."""

@@ -168,6 +168,17 @@ class Qwen3:
         self.ctx.synchronize()   # the host buffers may be reused by the caller
         return True
 
+    def prefill(self, seq, ids, pos0=0):
+        """forward(ids, posBase) at T > 1 for sequence `seq` (qwen3.js:3938-4069):
+        runs the T tokens, fills their cache rows, and returns the next token id
+        (also left in the decode step's ids / pos for `seq`)."""
+        import numpy as np
+        a = np.ascontiguousarray(ids, np.uint32)
+        self.ctx.check(LIB.tb_qwen3_prefill(self.h, int(seq), ctypes.c_void_p(a.ctypes.data), a.size, int(pos0)),
+                       "prefill")
+        toks, _ = self.tokens()
+        return toks[seq]
+
     def weight_format(self, name):
         """QW_FMT_* the loader chose for a tensor (-1 when unset or unknown)."""
         kl = weight_kind(name)

@@ -79,12 +79,13 @@ class OracleModel:
     def embed_row(self, tok):
         return f16_to_f32(f16_of_bf16(self.W["model.embed_tokens.weight"][tok]))
 
-    def step(self, tok, pos, cache, route_f32=False):
+    def step(self, tok, pos, cache, route_f32=False, attn_f16ops=False):
         """One decode step of one sequence.  cache: per layer (Kq, Ks, Vq, Vs)
         numpy arrays [max_seq][...] holding rows < pos; row `pos` is written
         into them (as attnPrepQ8 does).  route_f32: the lm_head runs as gemvQ on
         the f32 row (linearQ's route for one row with vocab >= 16384), else as
-        the int8 DP4A GEMV.  Returns f64 logits."""
+        the int8 DP4A GEMV.  attn_f16ops: the attention at the operand precision
+        of the reference's f16 prefill kernel (a prefill token).  Returns f64 logits."""
         c = self.cfg
         H, hd, nHq, nKv, eps, theta = (c[k] for k in ("hidden", "head_dim", "n_heads", "n_kv_heads", "rms_eps",
                                                       "rope_theta"))
@@ -102,8 +103,9 @@ class OracleModel:
             vq_row, vs_row = oracle.kv_quant_q8(v.ravel())
             Kq[pos], Ks[pos], Vq[pos], Vs[pos] = kq_row, ks_row, vq_row, vs_row
             S = pos + 1
-            attn = oracle.attn_decode_q8(qr.astype(np.float32).ravel(), Kq[:S], Ks[:S], Vq[:S], Vs[:S], S, nHq,
-                                         nKv, hd).astype(np.float32)
+            att = oracle.attn_decode_q8_f16ops if attn_f16ops else oracle.attn_decode_q8
+            attn = att(qr.astype(np.float32).ravel(), Kq[:S], Ks[:S], Vq[:S], Vs[:S], S, nHq, nKv,
+                       hd).astype(np.float32)
             aq, as_, _ = oracle.quant_q8(attn)
             x = x + self._gemv(p + "self_attn.o_proj.weight", aq, as_)[0]
             x = x.astype(np.float32).astype(np.float64)

@@ -82,14 +82,85 @@ def test_gemm_config4_shape_sampled_rows(cuda):
     np.testing.assert_allclose(host(y2), 2 * host(y), rtol=1e-6, atol=1e-6)
 
 
+def _dp4_budget_err(got, ref, xq, xs, pack, sc):
+    """max over outputs of |err| / (2^-10 sum_k |w x|): the f16 rounding of xs*q
+    (2^-11) is the one difference from gemmDP4A's exact group sums."""
+    K = xq.shape[1]
+    w = np.abs(oracle.dequant_int4_g32(pack, sc).astype(np.float64))
+    absx = np.abs(xq.astype(np.float64)) * np.repeat(xs.astype(np.float64), 32, axis=1)
+    return float(np.max(np.abs(np.asarray(got, np.float64) - ref) / (2.0 ** -10 * (absx @ w.T) + 1e-30)))
+
+
+def _rms_err(got, ref):
+    return float(np.max(np.abs(np.asarray(got, np.float64) - ref)) / np.sqrt(np.mean(ref ** 2)))
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 512, 2048), (384, 768, 6144), (128, 2048, 1024)])
+def test_gemm_dp4_exact_group_sums(cuda, M, N, K):
+    """gemmDP4A with exact per-group int8 sums against the oracle's: only the f32
+    accumulation of the per-group terms differs (~1e-6 of the rms)."""
+    rng = np.random.default_rng(M * 3 + K)
+    pack, sc = _weights(rng, N, K)
+    xq, xs, _ = oracle.quant_q8(rng.standard_normal((M, K)).astype(np.float32))
+    y = host(tb.gemm_dp4(torch.from_numpy(xq).cuda(), torch.from_numpy(xs).cuda(), u32_dev(pack), u16_dev(sc)))
+    ref = oracle.gemv_int4_q8act(xq, xs, pack, sc)
+    assert _rms_err(y, ref) < 1e-5
+    assert row_rel_err(y, ref) < 1e-5
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (256, 768, 2048)])
+def test_gemm_dp4_exact_ternary(cuda, M, N, K):
+    """gemmTern (qwen3.js:1410-1420) with exact group sums."""
+    from helpers import tern_bf16
+    rng = np.random.default_rng(M + N + K)
+    pack, sc = oracle.quant_tern_wgsl(tern_bf16(rng, N, K))
+    xq, xs, _ = oracle.quant_q8(rng.standard_normal((M, K)).astype(np.float32))
+    y = host(tb.gemm_dp4(torch.from_numpy(xq).cuda(), torch.from_numpy(xs).cuda(), u32_dev(pack), u16_dev(sc),
+                         tern=True))
+    ref = oracle.gemv_tern_wgsl_q8act(xq, xs, pack, sc)
+    assert _rms_err(y, ref) < 1e-5
+
+
+def test_gemm_dp4_f16_within_rounding_budget(cuda):
+    """The tcgen05 f16-operand form: every output within 2^-10 * sum |w x|."""
+    M, N, K = 256, 512, 2048
+    rng = np.random.default_rng(31)
+    pack, sc = _weights(rng, N, K)
+    xq, xs, _ = oracle.quant_q8(rng.standard_normal((M, K)).astype(np.float32))
+    y = host(tb.gemm_dp4_f16(torch.from_numpy(xq).cuda(), torch.from_numpy(xs).cuda(), u32_dev(pack), u16_dev(sc)))
+    ref = oracle.gemv_int4_q8act(xq, xs, pack, sc)
+    assert row_rel_err(y, ref) < TOL
+    assert _dp4_budget_err(y, ref, xq, xs, pack, sc) < 1.0
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_gemm_dp4_epilogues(cuda, f16):
+    """epilogue 1 adds into y; epilogue 2 is the forward's swiglu, silu(gate) * up."""
+    M, N, K = 128, 512, 1024
+    rng = np.random.default_rng(12)
+    pack, sc = _weights(rng, N, K)
+    xq, xs, _ = oracle.quant_q8(rng.standard_normal((M, K)).astype(np.float32))
+    args = (torch.from_numpy(xq).cuda(), torch.from_numpy(xs).cuda(), u32_dev(pack), u16_dev(sc))
+    fn = tb.gemm_dp4_f16 if f16 else tb.gemm_dp4
+    base = host(fn(*args))
+    y0 = rng.standard_normal((M, N)).astype(np.float32)
+    y1 = host(fn(*args, y=torch.from_numpy(y0.copy()).cuda(), epilogue=1))
+    np.testing.assert_allclose(y1, y0 + base, rtol=1e-6, atol=1e-6)
+    y2 = host(fn(*args, y=torch.from_numpy(y0.copy()).cuda(), epilogue=2))
+    g = y0.astype(np.float64)
+    np.testing.assert_allclose(y2, g / (1 + np.exp(-g)) * base, rtol=1e-5, atol=1e-6)
+
+
 def test_linear_router_prefill_goes_to_gemm(cuda):
-    """linearQ with T > 8 (prefill) routes to the f16 GEMM."""
+    """linearQ with T > 8 (prefill) routes to gemmDP4A: QUANTQ8T rows then the exact GEMM."""
     M, N, K = 256, 512, 1024
     rng = np.random.default_rng(9)
     pack, sc = _weights(rng, N, K)
     x = rng.standard_normal((M, K)).astype(np.float32)
     y = host(tb.linear_q(torch.from_numpy(x).cuda(), u32_dev(pack), u16_dev(sc)))
-    assert row_rel_err(y, oracle.gemm_int4_f16(x, pack, sc)) < TOL
+    xq, xs, _ = oracle.quant_q8(x)
+    ref = oracle.gemv_int4_q8act(xq, xs, pack, sc)
+    assert _rms_err(y, ref) < 1e-5
 
 
 def test_gemm_rejects_untiled_shapes(cuda):
