@@ -32,6 +32,7 @@ import ctypes
 import json
 import os
 import statistics
+import numpy as np
 import subprocess
 import sys
 import tempfile
@@ -712,6 +713,28 @@ def bonsai_extra(dev, peak_gbs, stream, context=4096):
             "weight_formats": kinds, "reference_webgpu_tok_per_s": "21.7 (Iris Xe)"}
 
 
+def prefill_forward_extra(dev, stream, T=2048):
+    """forward(ids, 0) at T tokens (tb_qwen3_prefill) of Qwen3-1.7B, int4 weights:
+    prompt tokens per second, one sequence (exact-sum GEMMs, int8-KV prefill
+    attention, T-row KV writes, last-row lm_head)."""
+    import torch
+    m = build_model(Q17, dev, 1, T + 16, 16, 1, 0, seed=91)
+    ids = list(np.random.default_rng(3).integers(0, Q17["vocab"], T))
+    m.prefill(0, ids, 0)                       # buffers, warm-up
+    ts = []
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m.prefill(0, ids, 0)
+        e1.record(stream)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    m.close()
+    torch.cuda.synchronize(dev)
+    ms = statistics.median(ts)
+    return {"tokens": T, "ms": round(ms, 3), "tok_per_s": round(T / (ms * 1e-3), 1)}
+
+
 def prefill_attn_extra(dev, peak_tf, stream):
     """int8-KV prefill attention of one Qwen3-1.7B layer (16 q / 8 kv heads of
     128) over T = S = 512 / 2048 / 8192: TFLOP/s of the causal 4 * pairs * hd * heads."""
@@ -1021,6 +1044,7 @@ def main():
         extras["ternary_wgsl_bonsai_1.7b"] = tern_extra(dev, peak, peaks.get("bf16_tflops", 1590.0), stream)
         extras["ternary_wgsl_bonsai_1.7b"]["decode_step_context4096"] = bonsai_extra(dev, peak, stream)
         extras["prefill_attention_1.7b"] = prefill_attn_extra(dev, peaks.get("bf16_tflops", 1590.0), stream)
+        extras["prefill_forward_1.7b"] = prefill_forward_extra(dev, stream)
         sec, reps, dt = cpu_step_seconds(1, 12.0)
         cpu = {"value": round(B / sec, 4), "unit": "tok/s", "cores": 1, "kind": "port",
                "sample": "2 of 28 decoder layers (7 matrices each) + 1/16 of the lm_head rows, %d repetitions in "
