@@ -761,6 +761,49 @@ def prefill_attn_extra(dev, peak_tf, stream):
     return out
 
 
+def profile_prefill_attn(T):
+    """Three launches of the int8-KV prefill attention of one Qwen3-1.7B layer at
+    T = S tokens (cold L2 before each), for an ncu capture of one."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    nHq, nKv, hd = Q17["n_heads"], Q17["n_kv_heads"], Q17["head_dim"]
+    Kq = torch.randint(-127, 128, (T, nKv * hd), device=dev, dtype=torch.int32, generator=g).to(torch.int8)
+    Vq = torch.randint(-127, 128, (T, nKv * hd), device=dev, dtype=torch.int32, generator=g).to(torch.int8)
+    Ks = torch.rand(T, nKv * hd // 32, device=dev, generator=g) * 0.02
+    Vs = torch.rand(T, nKv * hd // 32, device=dev, generator=g) * 0.02
+    q = torch.randn(T, nHq * hd, device=dev, generator=g)
+    o = torch.empty(T, nHq * hd, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for it in range(3):
+        flush.fill_(it)
+        tb.attention_prefill_q8(q, (Kq, Ks, Vq, Vs), T, nHq, nKv, hd, out=o)
+    torch.cuda.synchronize()
+    assert tb.default_context(0).device_error() == 0
+    print("profile prefill attention done", flush=True)
+
+
+def profile_gemm_dp4(M, N, K):
+    """Three launches of the exact-sum prefill GEMM (gemmDP4A) at M x N x K."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    pack, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+    xq = torch.randint(-127, 128, (M, K), device=dev, dtype=torch.int32, generator=g).to(torch.int8)
+    xs = torch.rand(M, K // 32, device=dev, generator=g) * 0.01
+    y = torch.empty(M, N, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for it in range(3):
+        flush.fill_(it)
+        tb.gemm_dp4(xq, xs, pack, sc, y=y)
+    torch.cuda.synchronize()
+    assert tb.default_context(0).device_error() == 0
+    print("profile gemm_dp4 done", flush=True)
+
+
 def profile_lm_head(kind):
     """Three cold-L2 batch-1 lm_head GEMVs (151936 x 2048, RMSNorm fused) of one
     weight kind -- int4_f32 (gemvQ), int4_dp4a (rmsnormQ + gemvDP4) or tern
@@ -894,6 +937,10 @@ def main():
                     help="three cold-L2 decode-attention launches at context S (for ncu), then exit")
     ap.add_argument("--profile-gemm", type=int, nargs=3, default=None, metavar=("M", "N", "K"),
                     help="three cold-L2 prefill-GEMM launches at M x N x K (for ncu), then exit")
+    ap.add_argument("--profile-prefill-attn", type=int, default=0, metavar="T",
+                    help="three cold-L2 prefill-attention launches at T = S tokens (for ncu), then exit")
+    ap.add_argument("--profile-gemm-dp4", type=int, nargs=3, default=None, metavar=("M", "N", "K"),
+                    help="three cold-L2 exact-sum prefill GEMM launches (for ncu), then exit")
     ap.add_argument("--profile-lm-head", default=None, choices=("int4_f32", "int4_dp4a", "tern"),
                     help="three cold-L2 batch-1 lm_head GEMVs of one weight kind (for ncu), then exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
@@ -904,6 +951,12 @@ def main():
         return
     if args.profile_lm_head:
         profile_lm_head(args.profile_lm_head)
+        return
+    if args.profile_prefill_attn:
+        profile_prefill_attn(args.profile_prefill_attn)
+        return
+    if args.profile_gemm_dp4:
+        profile_gemm_dp4(*args.profile_gemm_dp4)
         return
     if args.profile_gemm:
         profile_gemm(*args.profile_gemm)
