@@ -526,8 +526,12 @@ TB_API int tb_qwen3_set_weight_q(tb_qwen3 *m, int kind, int layer, int fmt, cons
  * sums, residual and SwiGLU fused into their epilogues), the rows' K/V are written to the
  * sequence's cache and the int8-KV prefill attention runs over it; the last
  * row's lm_head + argmax sets ids[seq] and pos[seq] = pos0 + T, so the next
- * tb_qwen3_decode_step continues the sequence.  Returns when done.  tp_size 1;
- * hidden, heads*head_dim, kv_heads*head_dim and intermediate multiples of 128.
+ * tb_qwen3_decode_step continues the sequence.  Returns when done.  Under
+ * tensor parallelism (NCCL exchange, tb_qwen3_tp_init) every rank calls it with
+ * the same ids: column-split q/k/v/gate/up, row-split o/down with an allreduce
+ * of the T rows after each, local heads against the local cache shard, the
+ * vocab-split lm_head's argmax merged across ranks.  The rank's sizes
+ * (hidden, heads*head_dim, kv_heads*head_dim, intermediate) multiples of 128.
  * Buffers grow on the first call for a larger T (allocation). */
 TB_API int tb_qwen3_prefill(tb_qwen3 *m, int seq, const uint32_t *ids, int64_t T, int64_t pos0);
 /* The format tb_qwen3_set_weight chose for a weight (TB_QW_FMT_*), or -1 if unset. */

@@ -383,6 +383,17 @@ int pf_quant(tb_qwen3* m, const float* x, int64_t Tp, int64_t K)
     return tb_quant_q8_impl(m->ctx, x, m->pf_xq, m->pf_xs, nullptr, Tp, K);
 }
 
+// x += W . a for the prefill rows: one rank adds into x; under tensor
+// parallelism (row-split W) rank 0 carries the residual, the others write their
+// partial sums over x, and an allreduce over all ranks completes x
+int pf_residual(tb_qwen3* m, const Mat& w, int64_t Tp)
+{
+    if (m->P == 1) return pf_gemm(m, m->pf_x, w, Tp, 1);
+    TRY(pf_gemm(m, m->pf_x, w, Tp, m->r == 0 ? 1 : 0));
+    return nccl_check(m, nccl().AllReduce(m->pf_x, m->pf_x, (size_t)(Tp * m->c.hidden), ncclFloat32, ncclSum, m->comm,
+                                          m->ctx->stream), "prefill allreduce");
+}
+
 // forward(ids, posBase) at T > 1 for sequence `seq` (models/qwen3.js:3938-4069,
 // the prefill branch): rmsnorm -> q/k/v (linearQ: QUANTQ8T + gemmDP4A, or
 // gemmTern, with exact group sums) -> rope + quantized KV write -> int8-KV prefill attention -> o
@@ -418,13 +429,13 @@ int prefill(tb_qwen3* m, int seq, const uint32_t* ids_host, int64_t T, int64_t p
         TRY(tb_attn_prefill_q8(ctx, m->pf_attn, m->pf_qr, Ly.Kq + crow, Ly.Ks + crow / 32, Ly.Vq + crow,
                                Ly.Vs + crow / 32, T, pos0 + T, m->nHq, m->nKv, hd));
         TRY(pf_quant(m, m->pf_attn, Tp, qN));
-        TRY(pf_gemm(m, m->pf_x, Ly.o, Tp, 1));
+        TRY(pf_residual(m, Ly.o, Tp));
         TRY(tb_rmsnorm(ctx, m->pf_x, Ly.ln2, m->pf_norm, Tp, H, c.rms_eps));
         TRY(pf_quant(m, m->pf_norm, Tp, H));
         TRY(pf_gemm(m, m->pf_gate, Ly.gate, Tp, 0));
         TRY(pf_gemm(m, m->pf_gate, Ly.up, Tp, 2));
         TRY(pf_quant(m, m->pf_gate, Tp, I));
-        TRY(pf_gemm(m, m->pf_x, Ly.down, Tp, 1));
+        TRY(pf_residual(m, Ly.down, Tp));
     }
     // the last row: final norm + lm_head (linearQ at T = 1) + argmax into the history
     const float* xl = m->pf_x + (T - 1) * H;
@@ -436,7 +447,15 @@ int prefill(tb_qwen3* m, int seq, const uint32_t* ids_host, int64_t T, int64_t p
     } else {
         TRY(tb_gemv_int4_dp4a(ctx, lg, xl, m->fnorm, c.rms_eps, m->lm.pack, m->lm.scales, V, H, 1, 0));
     }
-    TRY(tb_argmax_impl(ctx, lg, V, 1, m->ids + seq, m->amax_part, m->amax_nparts, nullptr, 0, nullptr));
+    if (m->P == 1) {
+        TRY(tb_argmax_impl(ctx, lg, V, 1, m->ids + seq, m->amax_part, m->amax_nparts, nullptr, 0, nullptr));
+    } else {   // vocab shards: ordered keys of every rank, gathered and merged
+        TRY(tb_argmax_impl(ctx, lg, V, 1, nullptr, m->amax_part, m->amax_nparts, m->amax_key + seq,
+                           (uint32_t)(m->r * V), nullptr));
+        TRY(nccl_check(m, nccl().AllGather(m->amax_key + seq, m->amax_all, 1, ncclUint64, m->comm, ctx->stream),
+                       "prefill allgather"));
+        TRY(tb_argmax_merge_impl(ctx, m->amax_all, m->P, 1, m->ids + seq, nullptr));
+    }
     const int32_t next = (int32_t)(pos0 + T);
     e = cudaMemcpyAsync(m->pos + seq, &next, 4, cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);   // host arrays above are released on return
@@ -712,8 +731,10 @@ TB_API int tb_qwen3_prefill(tb_qwen3* m, int seq, const uint32_t* ids, int64_t T
     TB_REQUIRE(ctx, seq >= 0 && seq < c.batch, "sequence %d out of range", seq);
     TB_REQUIRE(ctx, T >= 1 && pos0 >= 0 && pos0 + T <= c.max_seq && T <= 65535,
                "prefill of %lld tokens at %lld does not fit the %d-row cache", (long long)T, (long long)pos0, c.max_seq);
-    if (m->P != 1)
-        return tb_fail(ctx, TB_ERR_UNSUPPORTED, "qwen3 prefill: tensor-parallel prefill is not built (tp_size %d)", m->P);
+    if (m->P != 1 && !m->comm)
+        return tb_fail(ctx, TB_ERR_UNSUPPORTED,
+                       "qwen3 prefill: tensor-parallel prefill uses the NCCL exchange (tb_qwen3_tp_init), tp_size %d",
+                       m->P);
     const int64_t hd = c.head_dim, qN = m->nHq * hd, kvN = m->nKv * hd, H = c.hidden;
     const int64_t Ns[4] = {qN, kvN, H, m->I};
     for (int64_t n : Ns)
