@@ -445,6 +445,38 @@ TB_API int tb_moe_ffn_int3(tb_ctx *ctx, float *x_out, const float *x_in, const u
                            const uint32_t *w2p, const uint16_t *w2s, int64_t T, int64_t K, int64_t nE,
                            int64_t H, int64_t I);
 
+/* Expert parallelism (no reference counterpart: the reference keeps every
+ * expert on one device, lfm25.js:824-830): the MoE FFN of tb_moe_ffn_int3 over
+ * P ranks (one process and GPU each), experts [r*nE/P, (r+1)*nE/P) on rank r.
+ * Each rank routes its own tokens; a forward sends every token row once to each
+ * rank that owns one of its experts (stores into that rank's IPC-mapped arena
+ * over NVLink), the owner runs the grouped int3 GEMVs on what it received and
+ * writes each (token, expert) output straight back into the origin's arena, and
+ * the origin combines in top-k order: the result is bit-identical to
+ * tb_moe_ffn_int3 on one device with all experts.  Every rank calls
+ * tb_moe_ep_forward the same number of times (T may differ per rank); waits
+ * for peers are bounded (about a second) and record a device error.
+ * Lifecycle: create (every rank) -> handle -> exchange the P handles (any
+ * host channel) -> connect (P > 1) -> set_experts -> forward ... -> destroy. */
+typedef struct tb_moe_ep tb_moe_ep;
+/* nE % P == 0, nE/P <= 256, K <= 8, H and I multiples of 32 up to 2048, up to
+ * Tmax <= 1024 tokens per rank and call.  Allocates the arena and buffers. */
+TB_API int tb_moe_ep_create(tb_ctx *ctx, int P, int rank, int64_t nE, int64_t K, int64_t H, int64_t I,
+                            int64_t Tmax, tb_moe_ep **out);
+TB_API void tb_moe_ep_destroy(tb_moe_ep *m);
+/* 64-byte CUDA IPC handle of this rank's arena */
+TB_API int tb_moe_ep_handle(tb_moe_ep *m, void *out64);
+/* handles: P x 64 bytes, rank order */
+TB_API int tb_moe_ep_connect(tb_moe_ep *m, const void *handles);
+/* this rank's experts, layout as tb_moe_ffn_int3 with nE/P experts (referenced,
+ * not copied: keep them alive) */
+TB_API int tb_moe_ep_set_experts(tb_moe_ep *m, const uint32_t *w1p, const uint16_t *w1s, const uint32_t *w3p,
+                                 const uint16_t *w3s, const uint32_t *w2p, const uint16_t *w2s);
+/* x_out [T][H] += MoE FFN of x_in [T][H] routed by idx/wt [T][K] (global
+ * expert ids, as tb_moe_router); x rows 16-byte aligned. */
+TB_API int tb_moe_ep_forward(tb_moe_ep *m, float *x_out, const float *x_in, const uint32_t *idx, const float *wt,
+                             int64_t T);
+
 /* bf16 -> f16 bits, rounded half-up as the loader's bf16ToF16bits
  * (models/qwen3.js:3357-3390): the f16 copies of the embedding table and the
  * norm weights. */

@@ -21,3 +21,4 @@ from .ops import (  # noqa: F401
     logit_mask, gumbel_noise, sample_argmax, GumbelSeeds, rmsnorm, embed_gather,
 )
 from .qwen3 import Qwen3, QWEN3_1_7B, QWEN3_0_6B  # noqa: F401,E402
+from .moe_ep import MoeEP  # noqa: F401,E402

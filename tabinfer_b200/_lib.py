@@ -82,6 +82,12 @@ SIGNATURES = {
     "tb_requant_int4_int3": [P, P, P, P, P, I64, I64],
     "tb_moe_router": [P, P, P, P, P, I64, I64, I64],
     "tb_moe_ffn_int3": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64],
+    "tb_moe_ep_create": [P, ctypes.c_int, ctypes.c_int, I64, I64, I64, I64, I64, P],
+    "tb_moe_ep_destroy": [P],
+    "tb_moe_ep_handle": [P, P],
+    "tb_moe_ep_connect": [P, P],
+    "tb_moe_ep_set_experts": [P, P, P, P, P, P, P],
+    "tb_moe_ep_forward": [P, P, P, P, P, I64],
     "tb_qwen3_shard": [P, I32, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)],
     "tb_qwen3_create": [P, P, ctypes.POINTER(P)],
     "tb_qwen3_destroy": [P],
@@ -118,6 +124,7 @@ RESTYPES = {
     "tb_bin_blob_bytes": I64,
     "tb_last_error": ctypes.c_char_p,
     "tb_ctx_get_stream": P,
+    "tb_moe_ep_destroy": None,
 }
 
 

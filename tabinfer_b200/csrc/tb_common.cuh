@@ -125,6 +125,25 @@ __device__ __forceinline__ float2 sbytes_f2(uint32_t w, int hi)
                  make_float2(-8388736.0f, -8388736.0f));
 }
 
+// system-scope flag handshakes between GPUs (peer memory over NVLink)
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_volatile_f4(const float* p)
+{
+    float4 v;
+    asm volatile("ld.volatile.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p) : "memory");
+    return v;
+}
+
 constexpr int TB_ATTN_MAX_KV = 1024;   // kv heads per decode call (counter slots)
 
 static inline int tb_cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }

@@ -163,6 +163,8 @@ __global__ void __launch_bounds__(256) k_moe_group(const uint32_t* __restrict__ 
 // ---- grouped int3 expert GEMV ---------------------------------------------------
 enum { MOE_GATEUP = 0, MOE_DOWN = 1 };
 
+constexpr int EP_MAX = 8;       // expert-parallel ranks
+
 struct MoeArgs {
     const float* x;              // activation rows
     long long x_stride;          // floats between activation rows
@@ -170,9 +172,14 @@ struct MoeArgs {
     const uint32_t* p3[2];       // [E*N][G][3]
     const uint16_t* s3[2];       // [E*N][G]
     float* y;                    // [P][N]: swi (gate/up) or expert outputs (down)
-    const int* order;
+    const int* order;            // position -> pair; null: the identity
     const int* offsets;
     int N, Kc, G;
+    const int* xrow = nullptr;   // when set, pair p reads activation row xrow[p]
+    // when set (expert parallel), pair p's output row goes to another rank's
+    // memory: c = ydst[p], row (c & 0xffffff) of ypeer[c >> 24]
+    const uint32_t* ydst = nullptr;
+    float* ypeer[EP_MAX] = {};
 };
 
 // 32 weights (q3 + 4 in three bitplanes) of one group as floats q - 4
@@ -233,8 +240,8 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
         fetch(0, cur);                       // in flight while the activations are staged
         __syncthreads();                     // the previous chunk's reads are done
         for (int b = 0; b < nb; b++) {
-            const int p = a.order[p0 + c0 + b];
-            const float* src = a.x + (long long)(p / a.xdiv) * a.x_stride;
+            const int p = a.order ? a.order[p0 + c0 + b] : p0 + c0 + b;
+            const float* src = a.x + (long long)(a.xrow ? a.xrow[p] : p / a.xdiv) * a.x_stride;
             for (int k = threadIdx.x; k < a.Kc; k += MOE_THREADS)
                 xs[(b * G + (k >> 5)) * XS_PAD + (k & 31)] = src[k];
         }
@@ -290,7 +297,7 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
                     const int r = rw0 + j;
                     if (r >= a.N) continue;
                     for (int b = 0; b < nb; b++) {
-                        const int p = a.order[p0 + c0 + b];
+                        const int p = a.order ? a.order[p0 + c0 + b] : p0 + c0 + b;
                         float v;
                         if (KIND == MOE_GATEUP) {
                             const float gg = acc[0][j][b], u = acc[NM - 1][j][b];
@@ -298,7 +305,12 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
                         } else {
                             v = acc[0][j][b];
                         }
-                        a.y[(long long)p * a.N + r] = v;
+                        if (a.ydst) {
+                            const uint32_t c = a.ydst[p];
+                            a.ypeer[c >> 24][(long long)(c & 0xffffffu) * a.N + r] = v;
+                        } else {
+                            a.y[(long long)p * a.N + r] = v;
+                        }
                     }
                 }
             }
@@ -403,6 +415,474 @@ TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const u
     const int grid = (int)std::min<long long>((total + 255) / 256, (long long)ctx->num_sms * 8);
     e = tb_launch(ctx, k_moe_combine, dim3(grid), dim3(256), 0, x_out, (const float*)o, wt, (int)H, (int)K, total);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe combine launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+}  // extern "C"
+
+// ============================================================================
+// Expert parallelism: the MoE FFN over P ranks (one process and GPU each), nE/P
+// experts per rank.  The reference keeps every expert on its one device
+// (lfm25.js:824-830); the exchange below is this library's own.
+//
+// Each rank owns an exchange arena in its HBM, mapped into every other rank
+// with CUDA IPC:
+//   rows[P][Tmax][H]  f32   token rows sent here, region s written by rank s
+//   meta[P][Tmax][K]  u32   per row and top-k slot: (local expert << 24) | origin
+//                           pair t*K + k, or ~0 when that slot's expert is elsewhere
+//   cnt[8], dflag[8], rflag[8]   u32 rows sent by / dispatch epoch of / return
+//                           epoch of each rank; then cfg[6] (P, nE, K, H, I,
+//                           Tmax), compared across ranks at connect
+//   ret[Tmax*K][H]    f32   the expert outputs of this rank's own pairs, each
+//                           written straight into its slot by the owner
+// A forward (epoch e): dispatch stores every local token row once per rank
+// that owns one of its experts (plain stores over NVLink), the last CTA per
+// destination releases cnt + dflag there; the owner's plan kernel acquires all
+// P dispatch flags and groups the received pairs by local expert; the grouped
+// int3 GEMVs run (the down GEMV's epilogue writes each pair's output row into
+// its origin's ret slot); a signal kernel releases rflag on every rank; the
+// combine waits for all P owners and adds sum_k wt * o_k in k order -- the
+// single-device arithmetic, so the result is bit-identical to tb_moe_ffn_int3.
+// Buffers are reused without double buffering: rank s dispatches epoch e+1
+// only after its combine of e saw every owner's return flag, which an owner
+// releases after it finished reading epoch e's rows; an owner writes epoch
+// e+1's outputs into s's ret only after s's dispatch of e+1, issued after s's
+// combine of e.  Every wait is bounded (~1 s) and records an error on timeout.
+namespace {
+
+constexpr int EP_TMAX = 1024;
+constexpr long long EP_WAIT_LIMIT = 1LL << 22;
+constexpr int ERR_EP_WAIT = 0x6c10;
+constexpr int ERR_EP_EXPERT = 0x6c11;
+constexpr int EP_CFG_OFF = 3 * EP_MAX * 4;    // bytes into the flags block
+constexpr int EP_CFG_WORDS = 6;
+
+size_t ep_up(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct EpLayout {
+    size_t rows, meta, flags, ret, total;
+};
+EpLayout ep_layout(int P, int64_t Tmax, int64_t K, int64_t H)
+{
+    EpLayout L{};
+    L.rows = 0;
+    L.meta = L.rows + ep_up((size_t)P * Tmax * H * 4);
+    L.flags = L.meta + ep_up((size_t)P * Tmax * K * 4);
+    L.ret = L.flags + ep_up(3 * EP_MAX * 4);
+    L.total = L.ret + ep_up((size_t)Tmax * K * H * 4);
+    return L;
+}
+
+__device__ __forceinline__ void ep_wait(const unsigned* flag, unsigned e, int* err)
+{
+    long long it = 0;
+    while ((int)(ld_acquire_sys(flag) - e) < 0) {
+        if (++it > EP_WAIT_LIMIT) {
+            atomicExch(err, ERR_EP_WAIT);
+            break;
+        }
+        if (it > 4096) __nanosleep(64);
+    }
+}
+
+__device__ __forceinline__ unsigned ld_volatile_u32(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct EpDispatchArgs {
+    const float* x;                 // [T][H] this rank's token rows
+    const uint32_t* idx;            // [T][K] routed experts (global ids)
+    float* rows[EP_MAX];            // destination d: its rows region of this rank
+    uint32_t* meta[EP_MAX];         // destination d: its meta region of this rank
+    unsigned* cnt[EP_MAX];          // destination d: &cnt[this rank]
+    unsigned* flag[EP_MAX];         // destination d: &dflag[this rank]
+    unsigned* ctr;                  // [EP_MAX] CTA arrival counters (local, zero between calls)
+    int T, K, H, El, nE;
+    unsigned e;
+    int* err;
+};
+
+// grid (P, NB): CTA (d, b) lists the tokens routed to rank d (one slot per
+// token, in token order), copies the rows of slots b*8+w, b*8+w + 8*NB, ...
+// (warp w) with their meta, and the last CTA of d publishes the count
+__global__ void __launch_bounds__(256) k_ep_dispatch(const EpDispatchArgs a)
+{
+    __shared__ int slot_tok[EP_TMAX];
+    __shared__ int wtot[8];
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int d = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int t0 = threadIdx.x * 4;
+    unsigned m = 0;
+    int c = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int t = t0 + i;
+        if (t >= a.T) break;
+        bool in = false;
+        for (int k = 0; k < a.K; k++) {
+            const uint32_t ex = a.idx[(long long)t * a.K + k];
+            if (ex >= (uint32_t)a.nE) {
+                if (d == 0 && blockIdx.y == 0) atomicExch(a.err, ERR_EP_EXPERT);
+            } else if ((int)(ex / (uint32_t)a.El) == d) {
+                in = true;
+            }
+        }
+        if (in) { m |= 1u << i; c++; }
+    }
+    // block exclusive scan of c
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) wtot[w] = incl;
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        before += i < w ? wtot[i] : 0;
+        total += wtot[i];
+    }
+    int j = before + incl - c;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        if (m & (1u << i)) slot_tok[j++] = t0 + i;
+    __syncthreads();
+    float* rows = a.rows[d];
+    uint32_t* meta = a.meta[d];
+    const int H4 = a.H >> 2;
+    for (int s = blockIdx.y * 8 + w; s < total; s += gridDim.y * 8) {
+        const int t = slot_tok[s];
+        const float4* src = reinterpret_cast<const float4*>(a.x + (long long)t * a.H);
+        float4* dst = reinterpret_cast<float4*>(rows + (long long)s * a.H);
+        for (int i = lane; i < H4; i += 32) dst[i] = src[i];
+        if (lane < a.K) {
+            const uint32_t ex = a.idx[(long long)t * a.K + lane];
+            const bool here = ex < (uint32_t)a.nE && (int)(ex / (uint32_t)a.El) == d;
+            meta[(long long)s * a.K + lane] =
+                here ? ((ex % (uint32_t)a.El) << 24) | (uint32_t)(t * a.K + lane) : 0xffffffffu;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned old = atomicAdd(a.ctr + d, 1u);
+        if (old == gridDim.y - 1) {          // every CTA of d has fenced its stores
+            a.ctr[d] = 0u;
+            __threadfence_system();
+            *reinterpret_cast<volatile unsigned*>(a.cnt[d]) = (unsigned)total;
+            st_release_sys(a.flag[d], a.e);
+        }
+    }
+}
+
+struct EpPlanArgs {
+    const uint32_t* meta;           // this rank's meta [P][Tmax][K]
+    const unsigned* cnt;            // this rank's cnt[P]
+    const unsigned* dflag;          // this rank's dflag[P]
+    int* xrow;                      // [pairs] received row s*Tmax + j
+    uint32_t* ydst;                 // [pairs] (origin rank << 24) | origin pair
+    int* offsets;                   // [El + 1]
+    int P, Tmax, K, El;
+    unsigned e;
+    int* err;
+};
+
+// one CTA: wait for every rank's dispatch, then place the received pairs
+// grouped by local expert (positions within an expert in arrival order of the
+// atomics: a pair's result does not depend on its position)
+__global__ void __launch_bounds__(512) k_ep_plan(const EpPlanArgs a)
+{
+    __shared__ int ecnt[256], ecur[256];
+    __shared__ unsigned scnt[EP_MAX];
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    if (threadIdx.x < a.P) {
+        ep_wait(a.dflag + threadIdx.x, a.e, a.err);
+        const unsigned n = ld_volatile_u32(a.cnt + threadIdx.x);
+        scnt[threadIdx.x] = n <= (unsigned)a.Tmax ? n : 0u;
+    }
+    for (int i = threadIdx.x; i < a.El; i += blockDim.x) ecnt[i] = 0;
+    __syncthreads();
+    for (int s = 0; s < a.P; s++) {
+        const int n = (int)scnt[s] * a.K;
+        const uint32_t* ms = a.meta + (long long)s * a.Tmax * a.K;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t code = ld_volatile_u32(ms + i);
+            if (code != 0xffffffffu && (int)(code >> 24) < a.El) atomicAdd(&ecnt[code >> 24], 1);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int i = 0; i < a.El; i++) {
+            a.offsets[i] = run;
+            ecur[i] = run;
+            run += ecnt[i];
+        }
+        a.offsets[a.El] = run;
+    }
+    __syncthreads();
+    for (int s = 0; s < a.P; s++) {
+        const int n = (int)scnt[s] * a.K;
+        const uint32_t* ms = a.meta + (long long)s * a.Tmax * a.K;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t code = ld_volatile_u32(ms + i);
+            if (code == 0xffffffffu || (int)(code >> 24) >= a.El) continue;
+            const int pos = atomicAdd(&ecur[code >> 24], 1);
+            a.xrow[pos] = s * a.Tmax + i / a.K;
+            a.ydst[pos] = ((uint32_t)s << 24) | (code & 0xffffffu);
+        }
+    }
+}
+
+// after the down GEMV (griddepcontrol.wait: its stores are complete), release
+// this rank's return flag on every rank
+struct EpSignalArgs {
+    unsigned* flag[EP_MAX];         // rank s: &rflag[this rank]
+    int P;
+    unsigned e;
+};
+__global__ void __launch_bounds__(32) k_ep_signal(const EpSignalArgs a)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    __threadfence_system();
+    if ((int)threadIdx.x < a.P) st_release_sys(a.flag[threadIdx.x], a.e);
+}
+
+// x[t, :] += sum_k wt[t, k] * ret[t*K + k, :] (k in order, as k_moe_combine),
+// after every owner's return flag
+__global__ void __launch_bounds__(256) k_ep_combine(float* __restrict__ x, const float* ret, const float* __restrict__ wt,
+                                                    const unsigned* rflag, int P, unsigned e, int H, int K, int total4,
+                                                    int* err)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    if ((int)threadIdx.x < P) ep_wait(rflag + threadIdx.x, e, err);
+    __syncthreads();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += gridDim.x * blockDim.x) {
+        const int t = (4 * i) / H, h = 4 * i - t * H;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < K; k++) {
+            const float wk = wt[t * K + k];
+            const float4 o = ld_volatile_f4(ret + (long long)(t * K + k) * H + h);
+            s.x = fmaf(wk, o.x, s.x);
+            s.y = fmaf(wk, o.y, s.y);
+            s.z = fmaf(wk, o.z, s.z);
+            s.w = fmaf(wk, o.w, s.w);
+        }
+        float4 v = reinterpret_cast<float4*>(x)[i];
+        v.x += s.x; v.y += s.y; v.z += s.z; v.w += s.w;
+        reinterpret_cast<float4*>(x)[i] = v;
+    }
+}
+
+}  // namespace
+
+struct tb_moe_ep {
+    tb_ctx* ctx = nullptr;
+    int P = 1, r = 0;
+    int64_t nE = 0, El = 0, K = 0, H = 0, I = 0, Tmax = 0;
+    EpLayout L{};
+    char* arena = nullptr;
+    char* peer[EP_MAX] = {};
+    bool connected = false;
+    float* swi = nullptr;
+    int* xrow = nullptr;
+    uint32_t* ydst = nullptr;
+    int* offsets = nullptr;
+    unsigned* ctr = nullptr;
+    const uint32_t* wp[3] = {};
+    const uint16_t* ws[3] = {};
+    unsigned epoch = 0;
+};
+
+namespace {
+
+void ep_free(tb_moe_ep* m)
+{
+    for (int s = 0; s < m->P; s++)
+        if (s != m->r && m->peer[s]) cudaIpcCloseMemHandle(m->peer[s]);
+    for (void* p : {(void*)m->arena, (void*)m->swi, (void*)m->xrow, (void*)m->ydst, (void*)m->offsets, (void*)m->ctr})
+        if (p) cudaFree(p);
+}
+
+}  // namespace
+
+extern "C" {
+
+TB_API int tb_moe_ep_create(tb_ctx* ctx, int P, int rank, int64_t nE, int64_t K, int64_t H, int64_t I, int64_t Tmax,
+                            tb_moe_ep** out)
+{
+    if (!ctx || !out) return TB_ERR_INVALID;
+    *out = nullptr;
+    TB_REQUIRE(ctx, P >= 1 && P <= EP_MAX && rank >= 0 && rank < P, "moe ep: %d ranks (1..%d), rank %d", P, EP_MAX,
+               rank);
+    TB_REQUIRE(ctx, nE > 0 && nE % P == 0 && nE / P <= 256, "moe ep: %lld experts over %d ranks", (long long)nE, P);
+    TB_REQUIRE(ctx, K >= 1 && K <= 8 && K <= nE, "moe ep: top-k %lld (1..8)", (long long)K);
+    TB_REQUIRE(ctx, H > 0 && I > 0 && H % 32 == 0 && I % 32 == 0 && H <= 2048 && I <= 2048,
+               "moe ep: H, I multiples of 32 up to 2048");
+    TB_REQUIRE(ctx, Tmax >= 1 && Tmax <= EP_TMAX, "moe ep: up to %d tokens per rank and call", EP_TMAX);
+    tb_moe_ep* m = new tb_moe_ep;
+    m->ctx = ctx; m->P = P; m->r = rank; m->nE = nE; m->El = nE / P; m->K = K; m->H = H; m->I = I; m->Tmax = Tmax;
+    m->L = ep_layout(P, Tmax, K, H);
+    const int64_t pairs = (int64_t)P * Tmax * K;     // at most K codes per received row
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    cudaError_t e = cudaMalloc(&m->arena, m->L.total);
+    if (e == cudaSuccess) e = cudaMemset(m->arena, 0, m->L.total);
+    if (e == cudaSuccess) e = cudaMalloc(&m->swi, (size_t)pairs * I * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->xrow, (size_t)pairs * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->ydst, (size_t)pairs * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->offsets, (size_t)(m->El + 1) * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->ctr, EP_MAX * 4);
+    if (e == cudaSuccess) e = cudaMemset(m->ctr, 0, EP_MAX * 4);
+    const uint32_t cfg[EP_CFG_WORDS] = {(uint32_t)P, (uint32_t)nE, (uint32_t)K, (uint32_t)H, (uint32_t)I, (uint32_t)Tmax};
+    if (e == cudaSuccess)
+        e = cudaMemcpy(m->arena + m->L.flags + EP_CFG_OFF, cfg, sizeof cfg, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        ep_free(m);
+        delete m;
+        return tb_fail(ctx, TB_ERR_NOMEM, "moe ep buffers: %s", cudaGetErrorString(e));
+    }
+    m->peer[rank] = m->arena;
+    m->connected = P == 1;
+    *out = m;
+    return TB_OK;
+}
+
+TB_API void tb_moe_ep_destroy(tb_moe_ep* m)
+{
+    if (!m) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    ep_free(m);
+    cudaSetDevice(prev);
+    delete m;
+}
+
+TB_API int tb_moe_ep_handle(tb_moe_ep* m, void* out64)
+{
+    if (!m || !out64) return TB_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, m->arena);
+    if (e != cudaSuccess) return tb_fail(m->ctx, TB_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    memcpy(out64, &h, sizeof h);
+    return TB_OK;
+}
+
+TB_API int tb_moe_ep_connect(tb_moe_ep* m, const void* handles)
+{
+    if (!m || !handles) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    TB_REQUIRE(ctx, m->P > 1 && !m->connected, "moe ep connect: single rank or already connected");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    int rc = TB_OK;
+    for (int s = 0; s < m->P && rc == TB_OK; s++) {
+        if (s == m->r) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char*>(handles) + 64 * s, sizeof h);
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            rc = tb_fail(ctx, TB_ERR_CUDA, "cudaIpcOpenMemHandle(rank %d): %s", s, cudaGetErrorString(e));
+            break;
+        }
+        m->peer[s] = static_cast<char*>(p);
+        // every rank must lay out its arena with the same sizes
+        uint32_t mine[EP_CFG_WORDS], theirs[EP_CFG_WORDS];
+        e = cudaMemcpy(mine, m->arena + m->L.flags + EP_CFG_OFF, sizeof mine, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(theirs, m->peer[s] + m->L.flags + EP_CFG_OFF, sizeof theirs, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = tb_fail(ctx, TB_ERR_CUDA, "moe ep connect: reading rank %d: %s", s, cudaGetErrorString(e));
+        else if (memcmp(mine, theirs, sizeof mine) != 0)
+            rc = tb_fail(ctx, TB_ERR_INVALID, "moe ep connect: rank %d was created with other sizes (P, nE, K, H, I, Tmax)", s);
+    }
+    cudaSetDevice(prev);
+    if (rc != TB_OK) {
+        for (int s = 0; s < m->P; s++)
+            if (s != m->r && m->peer[s]) { cudaIpcCloseMemHandle(m->peer[s]); m->peer[s] = nullptr; }
+        return rc;
+    }
+    m->connected = true;
+    return TB_OK;
+}
+
+TB_API int tb_moe_ep_set_experts(tb_moe_ep* m, const uint32_t* w1p, const uint16_t* w1s, const uint32_t* w3p,
+                                 const uint16_t* w3s, const uint32_t* w2p, const uint16_t* w2s)
+{
+    if (!m) return TB_ERR_INVALID;
+    TB_REQUIRE(m->ctx, w1p && w1s && w3p && w3s && w2p && w2s, "null pointer");
+    m->wp[0] = w1p; m->ws[0] = w1s; m->wp[1] = w3p; m->ws[1] = w3s; m->wp[2] = w2p; m->ws[2] = w2s;
+    return TB_OK;
+}
+
+TB_API int tb_moe_ep_forward(tb_moe_ep* m, float* x_out, const float* x_in, const uint32_t* idx, const float* wt,
+                             int64_t T)
+{
+    if (!m) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    TB_REQUIRE(ctx, x_out && x_in && idx && wt, "null pointer");
+    TB_REQUIRE(ctx, m->connected, "moe ep: connect the ranks first (tb_moe_ep_connect)");
+    TB_REQUIRE(ctx, m->wp[0], "moe ep: experts not set");
+    TB_REQUIRE(ctx, T >= 1 && T <= m->Tmax, "moe ep: %lld tokens (1..%lld)", (long long)T, (long long)m->Tmax);
+    TB_REQUIRE(ctx, TB_ALIGNED(x_out, 16) && TB_ALIGNED(x_in, 16), "moe ep: x rows must be 16-byte aligned");
+    const unsigned e = ++m->epoch;
+    const int P = m->P, r = m->r;
+    EpDispatchArgs da{};
+    for (int d = 0; d < P; d++) {
+        char* b = m->peer[d];
+        da.rows[d] = reinterpret_cast<float*>(b + m->L.rows) + (size_t)r * m->Tmax * m->H;
+        da.meta[d] = reinterpret_cast<uint32_t*>(b + m->L.meta) + (size_t)r * m->Tmax * m->K;
+        unsigned* fl = reinterpret_cast<unsigned*>(b + m->L.flags);
+        da.cnt[d] = fl + r;
+        da.flag[d] = fl + EP_MAX + r;
+    }
+    da.x = x_in; da.idx = idx; da.ctr = m->ctr; da.T = (int)T; da.K = (int)m->K; da.H = (int)m->H;
+    da.El = (int)m->El; da.nE = (int)m->nE; da.e = e; da.err = ctx->dev_error;
+    const int NB = std::min(16, tb_cdiv(T, 8));
+    cudaError_t ce = tb_launch(ctx, k_ep_dispatch, dim3((unsigned)P, (unsigned)NB), dim3(256), 0, da);
+    if (ce != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe ep dispatch launch: %s", cudaGetErrorString(ce));
+    unsigned* myfl = reinterpret_cast<unsigned*>(m->arena + m->L.flags);
+    EpPlanArgs pa{reinterpret_cast<const uint32_t*>(m->arena + m->L.meta), myfl, myfl + EP_MAX, m->xrow, m->ydst,
+                  m->offsets, P, (int)m->Tmax, (int)m->K, (int)m->El, e, ctx->dev_error};
+    ce = tb_launch(ctx, k_ep_plan, dim3(1), dim3(512), 0, pa);
+    if (ce != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe ep plan launch: %s", cudaGetErrorString(ce));
+    const int H = (int)m->H, I = (int)m->I;
+    MoeArgs g{reinterpret_cast<const float*>(m->arena + m->L.rows), H, 1, {m->wp[0], m->wp[1]}, {m->ws[0], m->ws[1]},
+              m->swi, nullptr, m->offsets, I, H, H / 32};
+    g.xrow = m->xrow;
+    int rc = launch_moe<MOE_GATEUP>(ctx, g, (int)m->El);
+    if (rc) return rc;
+    MoeArgs dn{m->swi, I, 1, {m->wp[2], m->wp[2]}, {m->ws[2], m->ws[2]}, nullptr, nullptr, m->offsets, H, I, I / 32};
+    dn.ydst = m->ydst;
+    for (int s = 0; s < P; s++) dn.ypeer[s] = reinterpret_cast<float*>(m->peer[s] + m->L.ret);
+    rc = launch_moe<MOE_DOWN>(ctx, dn, (int)m->El);
+    if (rc) return rc;
+    EpSignalArgs sa{};
+    for (int s = 0; s < P; s++) sa.flag[s] = reinterpret_cast<unsigned*>(m->peer[s] + m->L.flags) + 2 * EP_MAX + r;
+    sa.P = P;
+    sa.e = e;
+    ce = tb_launch(ctx, k_ep_signal, dim3(1), dim3(32), 0, sa);
+    if (ce != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe ep signal launch: %s", cudaGetErrorString(ce));
+    const int total4 = (int)(T * m->H / 4);
+    const int grid = std::max(1, std::min(tb_cdiv(total4, 256), ctx->num_sms));
+    ce = tb_launch(ctx, k_ep_combine, dim3((unsigned)grid), dim3(256), 0, x_out,
+                   (const float*)(m->arena + m->L.ret), wt, (const unsigned*)(myfl + 2 * EP_MAX), P, e, H, (int)m->K,
+                   total4, ctx->dev_error);
+    if (ce != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe ep combine launch: %s", cudaGetErrorString(ce));
     return TB_OK;
 }
 

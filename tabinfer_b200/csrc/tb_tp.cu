@@ -36,24 +36,6 @@ struct TpArgs {
     int* err;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v)
-{
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p)
-{
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ float4 ld_volatile_f4(const float* p)
-{
-    float4 v;
-    asm volatile("ld.volatile.global.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p) : "memory");
-    return v;
-}
-
 // signal flag slot of every rank, then wait for every rank's signal (bounded)
 __device__ __forceinline__ void tp_signal_wait(unsigned* const* peer_flag, const unsigned* my_flag, int P, unsigned e,
                                                bool signal, int* err)
