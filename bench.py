@@ -503,6 +503,76 @@ def moe_extra(dev, peak_gbs, stream):
     return out
 
 
+def moe_ep_extra(dev, world, rank, stream, peak_gbs, dist):
+    """Config 5 expert-parallel: the LFM2.5-8B-A1B-shaped int3 MoE FFN (hidden
+    2048, 32 experts, I 1792, top-4) with 32/world experts per GPU, every rank
+    routing its own 1 / 8 / 64 tokens (tb_moe_ep_forward: dispatch over NVLink
+    peer memory, grouped expert GEMVs, outputs written back into the origin,
+    combine).  Per forward: median of cold-L2 CUDA-event times on each rank,
+    max over ranks.  expert_gbs = int3 planes + scales of the experts this rank
+    ran / time (max-loaded rank)."""
+    import torch
+    import tabinfer_b200 as tb
+    H, I, NE, K = 2048, 1792, 32, 4
+    El = NE // world
+    ws = []
+    for j, (rows, cols) in enumerate(((I, H), (I, H), (H, I))):
+        g = torch.Generator(device=dev).manual_seed(40 + j)
+        w = (torch.randn(NE * rows, cols, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        pk, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+        del w
+        p3, s3 = tb.requant_int3(pk, sc)
+        del pk, sc
+        ws.append((p3[rank * El * rows:(rank + 1) * El * rows].clone(), s3[rank * El * rows:(rank + 1) * El * rows].clone()))
+        del p3, s3
+    per_expert = (2 * I * H + H * I) * 14 // 32
+    ep = tb.MoeEP(world, rank, NE, K, H, I, 64, device=dev.index)
+    if world > 1:
+        mine = torch.frombuffer(bytearray(ep.handle()), dtype=torch.uint8).to(dev)
+        allh = [torch.zeros(64, dtype=torch.uint8, device=dev) for _ in range(world)]
+        dist.all_gather(allh, mine)
+        ep.connect([bytes(h.cpu().numpy().tobytes()) for h in allh])
+    ep.set_experts(*ws)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {"experts_per_gpu": El, "gpus": world}
+    for T in (1, 8, 64):
+        g = torch.Generator(device=dev).manual_seed(1000 + 17 * rank + T)
+        logits = torch.randn(T, NE, device=dev, generator=g)
+        a = torch.randn(T, H, device=dev, generator=g)
+        x = torch.zeros(T, H, device=dev)
+        idx, wt = tb.moe_router(logits, torch.zeros(NE, device=dev), K)
+        ids = idx.flatten().tolist()
+        mine_used = len({e for e in ids if e // El == rank})
+        ts = []
+        for r in range(25):
+            flush.fill_(r & 0xff)
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ep.forward(x, a, idx, wt)
+            e1.record(stream)
+            e1.synchronize()
+            if r >= 5:
+                ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        ms_max, used_max = ms, mine_used
+        if world > 1:
+            t = torch.tensor([ms, float(mine_used)], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_max, used_max = float(t[0]), int(t[1])
+        gbs = used_max * per_expert / (ms_max * 1e-3) / 1e9
+        out["T%d_per_gpu" % T] = {"us": round(ms_max * 1e3, 1), "tokens_per_s": round(world * T / (ms_max * 1e-3), 1),
+                                  "experts_on_busiest_gpu": used_max, "expert_gbs": round(gbs, 1),
+                                  "frac_of_peak": round(gbs / peak_gbs, 4)}
+    err = ep.ctx.device_error()
+    assert err == 0, "moe ep device error 0x%x" % err
+    ep.close()
+    del flush, ws
+    torch.cuda.synchronize(dev)
+    return out
+
+
 def _tern_weights(dev, g, N, K):
     """A ternary bf16 matrix (per 32-group {-m, 0, +m}) packed on the device in the
     WebGPU layout (quantizeTernaryBf16)."""
@@ -1103,6 +1173,11 @@ def main():
                "sample": "2 of 28 decoder layers (7 matrices each) + 1/16 of the lm_head rows, %d repetitions in "
                          "%.1f s, scaled to the full step; C transcription of the JS linearQ int4 math, 1 thread; "
                          "attention excluded" % (reps, dt)}
+
+    if not args.no_extras:          # every rank: the expert-parallel exchange needs all of them
+        ep_out = moe_ep_extra(dev, world, rank, stream, peak, dist)
+        if rank == 0:
+            extras["moe_ep_lfm2.5"] = ep_out
 
     if rank == 0:
         line = {"metric": "Qwen3-1.7B int4 decode tok/s (context %d, batch %d)" % (S, B), "value": round(value, 2),

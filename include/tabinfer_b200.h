@@ -531,6 +531,19 @@ enum {
   TB_QW_K_NORM = 13      /* self_attn.k_norm [hd] */
 };
 
+/* How the decode step runs.  TB_QW_STEP_PERSISTENT: embed and every layer in
+ * ONE persistent kernel (one CTA per SM, grid barriers between the phases, each
+ * CTA requesting the weights of its next phases into shared memory while the
+ * current one runs), then lm_head and argmax; batch 1, one GPU, int4 layer
+ * weights.  TB_QW_STEP_KERNELS: one kernel per operation (~170 a step).
+ * TB_QW_STEP_AUTO (default): persistent where it applies.  Both compute the same
+ * bits.  No reference counterpart (the reference dispatches WebGPU passes). */
+#define TB_QW_STEP_AUTO 0
+#define TB_QW_STEP_KERNELS 1
+#define TB_QW_STEP_PERSISTENT 2
+TB_API int tb_qwen3_set_step_mode(tb_qwen3 *m, int mode);
+/* the kind the recorded step uses (TB_QW_STEP_KERNELS / _PERSISTENT), 0 before the first step */
+TB_API int tb_qwen3_step_kind(tb_qwen3 *m);
 /* Host-only: the block of a full [rows][cols] tensor of `kind` that rank
  * cfg->tp_rank keeps (norm vectors count as one row). */
 TB_API int tb_qwen3_shard(const tb_qwen3_config *cfg, int kind, int64_t *row0, int64_t *nrows,

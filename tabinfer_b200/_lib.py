@@ -99,6 +99,8 @@ SIGNATURES = {
     "tb_qwen3_io": [P, ctypes.POINTER(P), ctypes.POINTER(P), ctypes.POINTER(P)],
     "tb_nccl_unique_id": [P],
     "tb_qwen3_tp_init": [P, P],
+    "tb_qwen3_set_step_mode": [P, ctypes.c_int],
+    "tb_qwen3_step_kind": [P],
     "tb_qwen3_tp_handle": [P, P],
     "tb_qwen3_tp_connect": [P, P],
     "tb_qwen3_decode_step": [P],
@@ -120,6 +122,8 @@ QW_EMBED, QW_LM_HEAD, QW_FINAL_NORM, QW_Q, QW_K, QW_V, QW_O, QW_GATE, QW_UP, QW_
     QW_LN_ATTN, QW_LN_MLP, QW_Q_NORM, QW_K_NORM = range(14)
 # formats of pre-quantized weights (TB_QW_FMT_*)
 QW_FMT_INT4, QW_FMT_TERN, QW_FMT_F16 = 0, 1, 2
+# how the decode step runs (TB_QW_STEP_*)
+QW_STEP_AUTO, QW_STEP_KERNELS, QW_STEP_PERSISTENT = 0, 1, 2
 RESTYPES = {
     "tb_bin_blob_bytes": I64,
     "tb_last_error": ctypes.c_char_p,

@@ -1,0 +1,485 @@
+// tb_attn_dev.cuh -- device code of the int8-KV decode attention shared by the
+// standalone kernels (tb_attn.cu) and the persistent decode-step kernel
+// (tb_step.cu): the attnPrepQ8 math (qwen3.js:2228-2296), the KV quantization
+// (pack4x8snorm, qwen3.js:2180-2210), and one split of the split-KV decode with
+// the combine of ATTN_DEC_COMBINE (qwen3.js:2048-2069).  One copy of this code
+// means the two paths compute bit-identical attention.
+#pragma once
+#include "tb_common.cuh"
+
+namespace {
+
+constexpr int ATT_WARPS = 4;
+constexpr int ATT_THREADS = ATT_WARPS * 32;
+constexpr int ATT_MAXG = 8;       // q heads per kv head handled by one CTA
+constexpr int ATT_MAXSPLIT = 1024; // splits per decode call
+constexpr float NEG_BIG = -3.0e38f;
+
+__device__ __forceinline__ int8_t snorm8(float v)
+{
+    float c = fminf(1.0f, fmaxf(-1.0f, v));
+    return (int8_t)floorf(__fadd_rn(0.5f, __fmul_rn(127.0f, c)));
+}
+
+// Error word codes written by the attention kernels when a device-resident
+// position is outside the cache (the host cannot check it).
+constexpr int ERR_ATTN_POS = 0x6a01;
+
+// ---- attnPrepQ8 math (qwen3.js:2228-2296) -----------------------------------
+// RoPE angle of dimension j (split-half pairs j, j + hd/2) at position pos, in
+// double: pos * theta^(-2 fi / hd).
+__device__ __forceinline__ void rope_cs(int j, int hd, long long pos, float theta, float* c, float* s)
+{
+    const int half = hd >> 1;
+    const int fi = j < half ? j : j - half;
+    const double ang = (double)pos * pow((double)theta, -2.0 * (double)fi / (double)hd);
+    double sd, cd;
+    sincos(ang, &sd, &cd);
+    *c = (float)cd;
+    *s = (float)sd;
+}
+
+// Per-head RMSNorm (w16) + RoPE of x (thread j holds element j of the head,
+// threads j >= hd hold nothing); every thread of the block calls it.  rk: hd
+// floats of shared memory, red: 8.
+__device__ __forceinline__ float norm_rope(float x, const uint16_t* w16, int hd, float eps, float c, float s, float* rk,
+                                           float* red)
+{
+    const int j = threadIdx.x, lane = j & 31, wid = j >> 5, nw = hd >> 5;
+    const float ss = warp_sum(j < hd ? x * x : 0.0f);
+    if (lane == 0 && wid < nw) red[wid] = ss;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < nw; i++) t += red[i];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), eps)));
+    if (j < hd) rk[j] = __fmul_rn(__fmul_rn(x, inv), tb_h2f(w16[j]));
+    __syncthreads();
+    float y = 0.0f;
+    if (j < hd) {
+        const int half = hd >> 1;
+        const float partner = j < half ? rk[j + half] : rk[j - half];
+        const float rot = j < half ? -partner : partner;
+        y = fmaf(rk[j], c, rot * s);
+    }
+    __syncthreads();   // rk and red may be reused
+    return y;
+}
+
+// snorm int8 of one 32-group per warp (pack4x8snorm of x / max(1e-12, maxabs))
+// into row dq / scales ds (element j of the head at dq[j], group scale at ds[j/32])
+__device__ __forceinline__ void quant_row(float x, int hd, int8_t* dq, float* ds)
+{
+    const int j = threadIdx.x, lane = j & 31;
+    if ((j >> 5) >= (hd >> 5)) return;
+    const float m = fmaxf(1e-12f, warp_max(fabsf(x)));
+    dq[j] = snorm8(__fdiv_rn(x, m));
+    if (lane == 0) ds[j >> 5] = m;
+}
+
+// ---- split-KV decode --------------------------------------------------------
+struct AttnArgs {
+    const float* qr;       // [nHq*hd]
+    const int8_t* Kq;
+    const float* Ks;
+    const int8_t* Vq;
+    const float* Vs;
+    float* PO;             // [nHq][nsplit][hd]
+    float* PML;            // [nHq][nsplit][2]
+    float* out;            // [nHq*hd]
+    unsigned* counters;    // [B][nKv] split arrivals, zero between calls
+    const int* dpos;       // [B] device positions (context S_b = dpos[b] + 1), or null: S for all
+    int* err;              // device error word
+    long long cache_rows;  // rows of each sequence's cache
+    int S, nHq, nKv, nsplit;
+    int grid_z;            // sequences
+};
+
+// ---- cp.async (16-byte and 8-byte global -> shared copies, per thread) -----
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)),
+                 "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* sdst, const void* gsrc)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(sdst)),
+                 "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Shared-memory layout of one split unit (4 warps; dynamic, bytes).  Each warp
+// owns NST stages; a stage holds one tile of 32 keys: K rows, V rows (HD bytes
+// each, 16-byte chunk i of key j stored at chunk i ^ (j % KV16) so the per-key
+// 16-byte copies and reads are bank-conflict free), then the 32 keys' K and V
+// group scales.
+template <int HD, int GRP, int NST_>
+struct DecLayout {
+    static constexpr int KV16 = HD / 16, NG = HD / 32, NST = NST_;
+    // splits the combining unit can weigh (its [GRP][nsplit] weights live in the stages)
+    static constexpr int MAXSPLIT = NST == 1 ? 256 : ATT_MAXSPLIT;
+    static constexpr int ST_K = 0, ST_V = 32 * HD, ST_KS = 64 * HD, ST_VS = 64 * HD + 32 * NG * 4;
+    static constexpr int STAGE = 64 * HD + 64 * NG * 4;
+    static constexpr int OFF_QS = 0;                                  // float [GRP][HD]
+    static constexpr int OFF_PS = OFF_QS + GRP * HD * 4;              // float [W][32 keys][NG][GRP]
+    static constexpr int OFF_WM = OFF_PS + ATT_WARPS * 32 * NG * GRP * 4;   // float [W][GRP]
+    static constexpr int OFF_WL = OFF_WM + ATT_WARPS * GRP * 4;       // float [W][GRP]
+    static constexpr int OFF_ST = (OFF_WL + ATT_WARPS * GRP * 4 + 127) / 128 * 128;
+    static constexpr int BYTES = OFF_ST + ATT_WARPS * NST * STAGE;
+    // after the key loop the stages are reused for the warps' outputs, float [W][GRP][HD]
+    static_assert(ATT_WARPS * GRP * HD * 4 <= ATT_WARPS * NST * STAGE, "merge buffer must fit in the stages");
+    static_assert(STAGE % 16 == 0 && ST_KS % 16 == 0 && ST_VS % 16 == 0, "stage alignment");
+    // the combining unit keeps its split weights [GRP][nsplit] there too
+    static_assert(GRP * MAXSPLIT * 4 + (GRP * HD / 4 > ATT_THREADS ? GRP * HD / 4 : ATT_THREADS) * 16 <=
+                      ATT_WARPS * NST * STAGE,
+                  "split weights and column partials must fit in the stages");
+};
+
+// Barrier of the 4 warps running one unit: bar 0 is the whole CTA (a 128-thread
+// CTA), bar id > 0 a 128-thread group of a larger CTA.
+__device__ __forceinline__ void unit_sync(int bar)
+{
+    if (bar == 0) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(ATT_THREADS) : "memory");
+}
+
+// One (kv head, split) of the split-KV decode, run by 4 warps (tid 0..127).
+// Warp w takes the 32-key tiles w, w+4, w+8, ... of the split: with NST = 2 a
+// cp.async pipeline (tile j+1 in flight while tile j is scored), with NST = 1
+// one stage (tile j+1 requested after tile j is consumed).  Lane = key for the
+// scores (K row from shared memory against q held in shared memory, packed
+// f32x2 FMAs); the lane's key then writes p * vscale / 127 per V group, and
+// P.V runs lane = 4 dims (2 for hd 64) over the tile's keys.  Softmax is online
+// per warp; the 4 warps merge at the end into the split's partial (PO, PML);
+// the last split of the kv head to finish combines all of them.
+//
+// prefetch(early) requests each warp's first tile -- with early, not the tile
+// holding row S-1 (written by the step's own prep); run(early) requests that
+// one and does the rest.  The position (dpos) must not change in between.
+template <int HD, int GRP, int NST>
+struct DecUnit {
+    using L = DecLayout<HD, GRP, NST>;
+    static constexpr int KV16 = L::KV16, NG = L::NG;
+    static constexpr int DPL = HD / 32;                // dims per lane in P.V
+
+    const AttnArgs& a;
+    uint8_t* smem;
+    int hk, split, zb, tid, lane, wid, bar;
+    long long row_elems, row_groups;
+    const int8_t* Kq;
+    const int8_t* Vq;
+    const float* Ks;
+    const float* Vs;
+    int S, c0, c1, ntile;
+
+    __device__ DecUnit(const AttnArgs& a_, uint8_t* smem_, int hk_, int split_, int zb_, int tid_, int bar_)
+        : a(a_), smem(smem_), hk(hk_), split(split_), zb(zb_), tid(tid_), lane(tid_ & 31), wid(tid_ >> 5), bar(bar_)
+    {
+        row_elems = (long long)a.nKv * HD;
+        row_groups = row_elems / 32;
+        Kq = a.Kq + zb * a.cache_rows * row_elems;
+        Vq = a.Vq + zb * a.cache_rows * row_elems;
+        Ks = a.Ks + zb * a.cache_rows * row_groups;
+        Vs = a.Vs + zb * a.cache_rows * row_groups;
+        S = a.S;
+        if (a.dpos) {
+            S = a.dpos[zb] + 1;
+            if (S < 1 || S > a.cache_rows) {
+                if (tid == 0) atomicExch(a.err, ERR_ATTN_POS);
+                S = 0;   // every split empty: the output row is written as zeros
+            }
+        }
+        const int per = (S + a.nsplit - 1) / a.nsplit;
+        c0 = split * per;
+        c1 = min(S, c0 + per);
+        const int span = c1 - c0;
+        ntile = span > wid * 32 ? (span - wid * 32 + ATT_WARPS * 32 - 1) / (ATT_WARPS * 32) : 0;
+    }
+
+    __device__ uint8_t* stages() const { return smem + L::OFF_ST + wid * NST * L::STAGE; }
+
+    // tile j of this warp -> stage s; always commits a group (possibly empty).
+    // Rows are copied coalesced: in copy r, lanes 8q..8q+7 (4q..4q+3 for hd 64)
+    // move the KV16 16-byte chunks of key r*RPI + q.  Scales: lane = key.
+    __device__ void issue(int j, int s) const
+    {
+        constexpr int RPI = 32 / KV16;                  // rows per copy instruction
+        const int tb0 = c0 + (wid + ATT_WARPS * j) * 32;
+        uint8_t* st = stages() + s * L::STAGE;
+        const int ch = lane % KV16;
+#pragma unroll
+        for (int r = 0; r < KV16; r++) {
+            const int kr = r * RPI + lane / KV16;
+            if (tb0 + kr < c1) {
+                const long long src = (long long)(tb0 + kr) * row_elems + hk * HD + ch * 16;
+                const int dst = (kr * KV16 + (ch ^ (kr & (KV16 - 1)))) * 16;
+                cp_async16(st + L::ST_K + dst, Kq + src);
+                cp_async16(st + L::ST_V + dst, Vq + src);
+            }
+        }
+        const int t = tb0 + lane;
+        if (t < c1) {
+            float* ksd = reinterpret_cast<float*>(st + L::ST_KS) + lane * NG;
+            float* vsd = reinterpret_cast<float*>(st + L::ST_VS) + lane * NG;
+            const float* ksr = Ks + (long long)t * row_groups + hk * NG;
+            const float* vsr = Vs + (long long)t * row_groups + hk * NG;
+            if (NG * 4 == 16) {
+                cp_async16(ksd, ksr);
+                cp_async16(vsd, vsr);
+            } else {
+#pragma unroll
+                for (int g = 0; g < NG; g += 2) { cp_async8(ksd + g, ksr + g); cp_async8(vsd + g, vsr + g); }
+            }
+        }
+        cp_async_commit();
+    }
+
+    // does this warp's first tile hold row S-1?
+    __device__ bool first_new() const
+    {
+        const int last = S - 1, t00 = c0 + wid * 32;
+        return ntile > 0 && t00 <= last && last < t00 + 32;
+    }
+
+    __device__ void prefetch(bool early) const
+    {
+        if (!(early && first_new())) issue(0, 0);
+    }
+
+    __device__ void run(bool early) const
+    {
+        float* qs = reinterpret_cast<float*>(smem + L::OFF_QS);
+        float* ps_all = reinterpret_cast<float*>(smem + L::OFF_PS);
+        float* wm = reinterpret_cast<float*>(smem + L::OFF_WM);
+        float* wl = reinterpret_cast<float*>(smem + L::OFF_WL);
+        const float* qrow = a.qr + (long long)zb * a.nHq * HD;
+        float* PO = a.PO + (long long)zb * a.nHq * a.nsplit * HD;
+        float* PML = a.PML + (long long)zb * a.nHq * a.nsplit * 2;
+        float* outp = a.out + (long long)zb * a.nHq * HD;
+        unsigned* counter = a.counters + (long long)zb * a.nKv + hk;
+        uint8_t* stg = stages();
+        float* ps = ps_all + wid * 32 * NG * GRP;
+
+        const float qscale = rsqrtf((float)HD) * (1.0f / 127.0f);
+        if (early && first_new()) issue(0, 0);
+        for (int i = tid; i < GRP * HD; i += ATT_THREADS) qs[i] = __ldcg(qrow + (long long)hk * GRP * HD + i);
+        unit_sync(bar);
+
+        float m[GRP], l[GRP];
+        float2 o[GRP][DPL / 2];
+#pragma unroll
+        for (int h = 0; h < GRP; h++) {
+            m[h] = NEG_BIG; l[h] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < DPL / 2; i++) o[h][i] = make_float2(0.0f, 0.0f);
+        }
+        const int gsel = (lane * DPL) / 32;               // V group of this lane's dims
+        const int vc = (lane * DPL) >> 4, vcw = ((lane * DPL) & 15) / DPL;   // 16-byte chunk, word in chunk
+
+        for (int j = 0; j < ntile; j++) {
+            if constexpr (NST > 1) issue(j + 1, (j + 1) % NST);
+            cp_async_wait<NST - 1>();
+            __syncwarp();
+            const uint8_t* st = stg + (j % NST) * L::STAGE;
+            const int t0 = c0 + (wid + ATT_WARPS * j) * 32;
+            const bool valid = t0 + lane < c1;
+            const int nk = min(32, c1 - t0);
+
+            // ---- scores: lane = key
+            float s[GRP];
+#pragma unroll
+            for (int h = 0; h < GRP; h++) s[h] = 0.0f;
+            if (valid) {
+                const uint4* kd = reinterpret_cast<const uint4*>(st + L::ST_K) + lane * KV16;
+                const float* ksd = reinterpret_cast<const float*>(st + L::ST_KS) + lane * NG;
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    float2 acc[GRP];
+#pragma unroll
+                    for (int h = 0; h < GRP; h++) acc[h] = make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int i2 = 0; i2 < 2; i2++) {
+                        const int i = g * 2 + i2;
+                        const uint4 w4 = kd[i ^ (lane & (KV16 - 1))];
+                        const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int wq = 0; wq < 4; wq++) {
+                            const float2 k01 = sbytes_f2(ww[wq], 0), k23 = sbytes_f2(ww[wq], 1);
+                            const int d = i * 16 + wq * 4;
+#pragma unroll
+                            for (int h = 0; h < GRP; h++) {
+                                const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + d);
+                                acc[h] = ffma2(make_float2(q4.x, q4.y), k01, acc[h]);
+                                acc[h] = ffma2(make_float2(q4.z, q4.w), k23, acc[h]);
+                            }
+                        }
+                    }
+                    const float ksc = ksd[g];
+#pragma unroll
+                    for (int h = 0; h < GRP; h++) s[h] = fmaf(acc[h].x + acc[h].y, ksc, s[h]);
+                }
+            }
+            // ---- online softmax (per lane partial l; m warp-uniform)
+            float pr[GRP];
+#pragma unroll
+            for (int h = 0; h < GRP; h++) {
+                const float sc = valid ? s[h] * qscale : NEG_BIG;
+                const float mn = fmaxf(m[h], warp_max(sc));
+                const float corr = __expf(m[h] - mn);
+                pr[h] = valid ? __expf(sc - mn) : 0.0f;
+                l[h] = fmaf(l[h], corr, pr[h]);
+                m[h] = mn;
+#pragma unroll
+                for (int i = 0; i < DPL / 2; i++) o[h][i] = make_float2(o[h][i].x * corr, o[h][i].y * corr);
+            }
+            // ---- this key's weights per V group: p * vscale / 127
+            {
+                const float* vsd = reinterpret_cast<const float*>(st + L::ST_VS) + lane * NG;
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    const float vsc = valid ? vsd[g] * (1.0f / 127.0f) : 0.0f;
+#pragma unroll
+                    for (int h = 0; h < GRP; h++) ps[(lane * NG + g) * GRP + h] = pr[h] * vsc;
+                }
+            }
+            __syncwarp();
+            // ---- P.V: lane = DPL dims
+            const uint4* vt = reinterpret_cast<const uint4*>(st + L::ST_V);
+#pragma unroll 4
+            for (int kk = 0; kk < nk; kk++) {
+                const uint4* vrow = vt + kk * KV16 + (vc ^ (kk & (KV16 - 1)));
+                const uint32_t vw = DPL == 4 ? reinterpret_cast<const uint32_t*>(vrow)[vcw]
+                                             : (uint32_t)reinterpret_cast<const uint16_t*>(vrow)[vcw];
+                const float* pp = ps + (kk * NG + gsel) * GRP;
+                float pw[GRP];
+#pragma unroll
+                for (int h = 0; h < GRP; h++) pw[h] = pp[h];
+                const float2 v01 = sbytes_f2(vw, 0);
+#pragma unroll
+                for (int h = 0; h < GRP; h++) o[h][0] = ffma2(v01, make_float2(pw[h], pw[h]), o[h][0]);
+                if (DPL == 4) {
+                    const float2 v23 = sbytes_f2(vw, 1);
+#pragma unroll
+                    for (int h = 0; h < GRP; h++)
+                        o[h][DPL / 2 - 1] = ffma2(v23, make_float2(pw[h], pw[h]), o[h][DPL / 2 - 1]);
+                }
+            }
+            __syncwarp();   // stage j % NST and ps are rewritten next
+            if constexpr (NST == 1) {
+                if (j + 1 < ntile) issue(j + 1, 0);
+            }
+        }
+        cp_async_wait<0>();
+        unit_sync(bar);    // every warp is done with its stages: reuse them for the merge
+
+        // ---- merge warps
+        float* wo = reinterpret_cast<float*>(smem + L::OFF_ST);     // [W][GRP][HD]
+#pragma unroll
+        for (int h = 0; h < GRP; h++) {
+            const float lt = warp_sum(l[h]);
+            if (lane == 0) { wm[wid * GRP + h] = m[h]; wl[wid * GRP + h] = lt; }
+#pragma unroll
+            for (int i = 0; i < DPL / 2; i++)
+                *reinterpret_cast<float2*>(wo + (wid * GRP + h) * HD + lane * DPL + 2 * i) = o[h][i];
+        }
+        unit_sync(bar);
+        for (int i = tid; i < GRP * HD; i += ATT_THREADS) {
+            const int h = i / HD, d = i - h * HD;
+            float M = NEG_BIG;
+#pragma unroll
+            for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, wm[w * GRP + h]);
+            float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+            for (int w = 0; w < ATT_WARPS; w++) {
+                const float e = __expf(wm[w * GRP + h] - M);
+                Ls = fmaf(wl[w * GRP + h], e, Ls);
+                O = fmaf(wo[(w * GRP + h) * HD + d], e, O);
+            }
+            if (a.nsplit == 1) {
+                outp[(long long)(hk * GRP + h) * HD + d] = Ls > 0.0f ? O / Ls : 0.0f;
+            } else {
+                const long long pidx = (long long)(hk * GRP + h) * a.nsplit + split;
+                PO[pidx * HD + d] = O;
+                if (d == 0) { PML[pidx * 2] = M; PML[pidx * 2 + 1] = Ls; }
+            }
+        }
+        if (a.nsplit == 1) return;
+
+        // ---- the last split of this kv head to finish combines all of them
+        //      (ATTN_DEC_COMBINE, qwen3.js:2048-2069): out = sum_i e_i O_i / sum_i e_i l_i,
+        //      e_i = exp(m_i - max m).  Partials are read through L2 (ld.cg).
+        __threadfence();
+        unit_sync(bar);
+        int* last = reinterpret_cast<int*>(wm);          // wm/wl are free again after the loop above
+        if (tid == 0) *last = atomicAdd(counter, 1u) == (unsigned)(a.nsplit - 1);
+        unit_sync(bar);
+        if (!*last) return;
+        __threadfence();
+        float* wts = reinterpret_cast<float*>(smem + L::OFF_ST);    // [GRP][nsplit]
+        float* lsum = wl;                                            // [GRP]
+        for (int h = wid; h < GRP; h += ATT_WARPS) {
+            const float* pml = PML + (long long)(hk * GRP + h) * a.nsplit * 2;
+            float M = NEG_BIG;
+            for (int i = lane; i < a.nsplit; i += 32) M = fmaxf(M, __ldcg(pml + 2 * i));
+            M = warp_max(M);
+            float Ls = 0.0f;
+            for (int i = lane; i < a.nsplit; i += 32) {
+                const float e = __expf(__ldcg(pml + 2 * i) - M);
+                wts[h * a.nsplit + i] = e;
+                Ls = fmaf(__ldcg(pml + 2 * i + 1), e, Ls);
+            }
+            Ls = warp_sum(Ls);
+            if (lane == 0) lsum[h] = Ls;
+        }
+        unit_sync(bar);
+        // float4 columns (head h, dims 4c..4c+3); when there are fewer columns than
+        // threads, P threads share a column, each summing every P-th split with 8
+        // loads in flight, and the P partials are added in part order.
+        constexpr int NCOL = GRP * HD / 4;
+        constexpr int P = NCOL >= ATT_THREADS ? 1 : ATT_THREADS / NCOL;
+        float4* part = reinterpret_cast<float4*>(wts + GRP * L::MAXSPLIT);     // [P][NCOL]
+        for (int i = tid; i < NCOL * P; i += ATT_THREADS) {
+            const int col = i % NCOL, pp = i / NCOL;
+            const int h = col / (HD / 4), c4 = col - h * (HD / 4);
+            const float4* po = reinterpret_cast<const float4*>(PO + (long long)(hk * GRP + h) * a.nsplit * HD) + c4;
+            const float* w = wts + h * a.nsplit;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            int k = pp;
+            for (; k + 7 * P < a.nsplit; k += 8 * P) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) v[u] = __ldcg(po + (long long)(k + u * P) * (HD / 4));
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const float e = w[k + u * P];
+                    acc.x = fmaf(v[u].x, e, acc.x); acc.y = fmaf(v[u].y, e, acc.y);
+                    acc.z = fmaf(v[u].z, e, acc.z); acc.w = fmaf(v[u].w, e, acc.w);
+                }
+            }
+            for (; k < a.nsplit; k += P) {
+                const float4 v = __ldcg(po + (long long)k * (HD / 4));
+                const float e = w[k];
+                acc.x = fmaf(v.x, e, acc.x); acc.y = fmaf(v.y, e, acc.y);
+                acc.z = fmaf(v.z, e, acc.z); acc.w = fmaf(v.w, e, acc.w);
+            }
+            part[pp * NCOL + col] = acc;
+        }
+        unit_sync(bar);
+        for (int col = tid; col < NCOL; col += ATT_THREADS) {
+            const int h = col / (HD / 4), c4 = col - h * (HD / 4);
+            float4 O = part[col];
+            for (int pp = 1; pp < P; pp++) {
+                const float4 v = part[pp * NCOL + col];
+                O.x += v.x; O.y += v.y; O.z += v.z; O.w += v.w;
+            }
+            const float Ls = lsum[h];
+            const float4 res = Ls > 0.0f ? make_float4(O.x / Ls, O.y / Ls, O.z / Ls, O.w / Ls)
+                                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            reinterpret_cast<float4*>(outp + (long long)(hk * GRP + h) * HD)[c4] = res;
+        }
+        if (tid == 0) *counter = 0u;     // ready for the next call
+    }
+};
+
+}  // namespace

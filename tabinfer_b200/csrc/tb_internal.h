@@ -75,3 +75,25 @@ int tb_attn_prep_rows_impl(tb_ctx* ctx, const float* q, const float* k, const fl
 // int8 sums (tb_gemm_dp4.cu); M % 128, N % 128, K % 128; epilogue 0 store, 1 add, 2 SwiGLU
 int tb_gemm_dp4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
                      const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue, bool tern);
+
+// the decode step as one persistent kernel (tb_step.cu): batch 1, one GPU
+struct tb_step_plan;
+struct tb_step_io {
+    const void* layers;            // device array of the per-layer records (tb_step_layer_fill)
+    float eps, theta;
+    const uint32_t* ids;
+    const int32_t* pos;
+    const uint16_t* embed;
+    float *x, *q, *k, *v, *qr, *attn, *swi, *PO, *PML;
+    unsigned* counters;            // [nKv] attention split arrivals, zero between steps
+    unsigned* ctrl;                // [256] zero-initialised: block arrivals, grid barrier, abort word
+};
+int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I, int nsplit, int max_seq,
+                      tb_step_plan** out);
+void tb_step_plan_free(tb_step_plan* p);
+size_t tb_step_plan_smem(const tb_step_plan* p);
+int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io);
+size_t tb_step_layer_bytes();
+void tb_step_layer_fill(void* dst, const uint32_t* const* packs, const uint16_t* const* scales, const uint16_t* ln1,
+                        const uint16_t* ln2, const uint16_t* qn, const uint16_t* kn, int8_t* Kq, float* Ks, int8_t* Vq,
+                        float* Vs);

@@ -125,6 +125,13 @@ struct tb_qwen3 {
     int8_t* pf_xq = nullptr;
     uint32_t* pf_ids = nullptr;
     int32_t* pf_pos = nullptr;
+    // the decode step as one persistent kernel (tb_step.cu) when it applies
+    int step_mode = TB_QW_STEP_AUTO;             // requested
+    int step_kind = 0;                           // recorded: TB_QW_STEP_KERNELS or TB_QW_STEP_PERSISTENT
+    tb_step_plan* step = nullptr;
+    unsigned char* step_layers = nullptr;        // device per-layer records
+    unsigned* step_ctrl = nullptr;               // [256] block arrivals, grid barrier, abort word
+    bool step_direct = false;                    // persistent step launched per call (not capturable)
 };
 
 namespace {
@@ -255,6 +262,59 @@ int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w, int xi)
     return TB_OK;
 }
 
+int issue_head(tb_qwen3* m, int cur);
+
+// Can this model's step run as the persistent kernel?  (batch 1, one GPU, int4
+// q/k/v/o/gate/up/down in every layer, sizes tb_step_plan_make accepts)
+bool persistent_ok(tb_qwen3* m)
+{
+    if (m->P != 1 || m->c.batch != 1) return false;
+    for (const Layer& Ly : m->L)
+        if (Ly.q.tern || Ly.k.tern || Ly.v.tern || Ly.o.tern || Ly.gate.tern || Ly.up.tern || Ly.down.tern) return false;
+    if (!m->step) {
+        if (tb_step_plan_make(m->ctx, m->c.layers, m->c.hidden, (int)m->nHq, (int)m->nKv, m->c.head_dim, (int)m->I,
+                              m->nsplit, m->c.max_seq, &m->step) != TB_OK)
+            return false;
+    }
+    if (!m->step_layers) {
+        const size_t rec = tb_step_layer_bytes();
+        std::vector<unsigned char> host(rec * m->L.size());
+        for (size_t l = 0; l < m->L.size(); l++) {
+            const Layer& Ly = m->L[l];
+            const uint32_t* packs[7] = {Ly.q.pack, Ly.k.pack, Ly.v.pack, Ly.o.pack, Ly.gate.pack, Ly.up.pack,
+                                        Ly.down.pack};
+            const uint16_t* scs[7] = {Ly.q.scales, Ly.k.scales, Ly.v.scales, Ly.o.scales, Ly.gate.scales,
+                                      Ly.up.scales, Ly.down.scales};
+            tb_step_layer_fill(host.data() + rec * l, packs, scs, Ly.ln1, Ly.ln2, Ly.qn, Ly.kn, Ly.Kq, Ly.Ks, Ly.Vq,
+                               Ly.Vs);
+        }
+        if (alloc(m, &m->step_layers, host.size()) || alloc(m, &m->step_ctrl, 256)) return false;
+        if (cudaMemcpy(m->step_layers, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemset(m->step_ctrl, 0, 256 * 4) != cudaSuccess) {
+            cudaGetLastError();
+            m->step_layers = nullptr;
+            return false;
+        }
+    }
+    return true;
+}
+
+// the step as embed + 28 layers in one persistent kernel, then the shared head
+int issue_step_persistent(tb_qwen3* m)
+{
+    tb_step_io io{};
+    io.layers = m->step_layers;
+    io.eps = m->c.rms_eps;
+    io.theta = m->c.rope_theta;
+    io.ids = m->ids;
+    io.pos = m->pos;
+    io.embed = m->embed;
+    io.x = m->x[0]; io.q = m->q; io.k = m->k; io.v = m->v; io.qr = m->qr; io.attn = m->attn; io.swi = m->swi;
+    io.PO = m->PO; io.PML = m->PML; io.counters = m->counters; io.ctrl = m->step_ctrl;
+    TRY(tb_step_launch(m->ctx, m->step, &io));
+    return issue_head(m, 0);
+}
+
 int issue_step(tb_qwen3* m)
 {
     tb_ctx* ctx = m->ctx;
@@ -305,6 +365,15 @@ int issue_step(tb_qwen3* m)
         }
         TRY(proj_residual(m, cur, m->swi, Ly.down, 2 * l + 1));
     }
+    return issue_head(m, cur);
+}
+
+// final norm + lm_head + argmax of the step (x[cur] holds the last layer's output)
+int issue_head(tb_qwen3* m, int cur)
+{
+    tb_ctx* ctx = m->ctx;
+    const tb_qwen3_config& c = m->c;
+    const int B = c.batch, H = c.hidden;
     // final norm + lm_head: gemvQ (f32 activation) at one row, as linearQ routes
     // T = 1 with N >= 16384; the int8 DP4A GEMV for several rows; a ternary
     // lm_head takes gemvTern at every N (qwen3.js:1594-1598)
@@ -469,6 +538,7 @@ void release_graph(tb_qwen3* m)
     if (m->graph) cudaGraphDestroy(m->graph);
     m->exec = nullptr;
     m->graph = nullptr;
+    m->step_direct = false;
 }
 
 }  // namespace
@@ -576,6 +646,7 @@ TB_API int tb_qwen3_destroy(tb_qwen3* m)
         if (s != m->r && m->peer_arena[s]) cudaIpcCloseMemHandle(m->peer_arena[s]);
     for (void* p : m->allocs) cudaFree(p);
     free_prefill(m);
+    if (m->step) tb_step_plan_free(m->step);
     if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
     delete m;
     return TB_OK;
@@ -849,7 +920,12 @@ TB_API int tb_qwen3_decode_step(tb_qwen3* m)
         TB_REQUIRE(ctx, Ly.q.set && Ly.k.set && Ly.v.set && Ly.o.set && Ly.gate.set && Ly.up.set && Ly.down.set,
                    "a projection weight was never set");
     TB_REQUIRE(ctx, m->lm.set, "lm_head weight was never set");
-    if (!m->exec) {
+    if (!m->exec && !m->step_direct) {
+        const bool pers = m->step_mode != TB_QW_STEP_KERNELS && persistent_ok(m);
+        if (m->step_mode == TB_QW_STEP_PERSISTENT && !pers)
+            return tb_fail(ctx, TB_ERR_UNSUPPORTED,
+                           "persistent decode step needs batch 1, one GPU, int4 layer weights and sizes it supports");
+        m->step_kind = pers ? TB_QW_STEP_PERSISTENT : TB_QW_STEP_KERNELS;
         // record the step once on a private stream, after everything queued so far
         cudaStream_t user = ctx->stream;
         cudaEvent_t ev;
@@ -859,8 +935,8 @@ TB_API int tb_qwen3_decode_step(tb_qwen3* m)
         cudaEventDestroy(ev);
         ctx->stream = m->cap_stream;
         cudaError_t e = cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal);
-        int rc = e == cudaSuccess ? issue_step(m) : tb_fail(ctx, TB_ERR_CUDA, "begin capture: %s",
-                                                             cudaGetErrorString(e));
+        int rc = e == cudaSuccess ? (pers ? issue_step_persistent(m) : issue_step(m))
+                                  : tb_fail(ctx, TB_ERR_CUDA, "begin capture: %s", cudaGetErrorString(e));
         cudaGraph_t g = nullptr;
         cudaError_t e2 = cudaStreamEndCapture(m->cap_stream, &g);
         ctx->stream = user;
@@ -868,6 +944,28 @@ TB_API int tb_qwen3_decode_step(tb_qwen3* m)
         if (!rc) {
             e = cudaGraphInstantiate(&m->exec, g, 0);
             if (e != cudaSuccess) rc = tb_fail(ctx, TB_ERR_CUDA, "instantiate: %s", cudaGetErrorString(e));
+        }
+        if (rc && pers) {
+            // a driver that cannot capture the cooperative launch: launch the
+            // persistent step directly on every call (the graph of the head
+            // alone is kept for launch counting)
+            if (g) cudaGraphDestroy(g);
+            g = nullptr;
+            cudaGetLastError();
+            ctx->stream = m->cap_stream;
+            e = cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal);
+            rc = e == cudaSuccess ? issue_head(m, 0) : TB_ERR_CUDA;
+            e2 = cudaStreamEndCapture(m->cap_stream, &g);
+            ctx->stream = user;
+            if (rc || e2 != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                cudaGetLastError();
+                return tb_fail(ctx, TB_ERR_CUDA, "decode step: cannot record the step");
+            }
+            m->graph = g;
+            m->step_direct = true;
+            tb_fail(ctx, TB_OK, "");
+            return issue_step_persistent(m);
         }
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -877,9 +975,25 @@ TB_API int tb_qwen3_decode_step(tb_qwen3* m)
         }
         m->graph = g;
     }
+    if (m->step_direct) return issue_step_persistent(m);
     cudaError_t e = cudaGraphLaunch(m->exec, ctx->stream);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e));
     return TB_OK;
+}
+
+TB_API int tb_qwen3_set_step_mode(tb_qwen3* m, int mode)
+{
+    if (!m) return TB_ERR_INVALID;
+    TB_REQUIRE(m->ctx, mode == TB_QW_STEP_AUTO || mode == TB_QW_STEP_KERNELS || mode == TB_QW_STEP_PERSISTENT,
+               "step mode %d", mode);
+    m->step_mode = mode;
+    release_graph(m);
+    return TB_OK;
+}
+
+TB_API int tb_qwen3_step_kind(tb_qwen3* m)
+{
+    return m ? m->step_kind : 0;
 }
 
 TB_API int tb_qwen3_launches_per_step(tb_qwen3* m, int* kernels, int* collectives)

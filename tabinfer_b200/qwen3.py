@@ -190,6 +190,16 @@ class Qwen3:
         """NCCL exchange: every rank passes the same 128-byte unique id."""
         self.ctx.check(LIB.tb_qwen3_tp_init(self.h, ctypes.c_char_p(bytes(unique_id))), "tp_init")
 
+    def set_step_mode(self, mode):
+        """QW_STEP_AUTO (persistent where it applies), QW_STEP_KERNELS (one kernel
+        per operation) or QW_STEP_PERSISTENT (one persistent kernel for embed +
+        all layers; batch 1, one GPU, int4 layer weights)."""
+        self.ctx.check(LIB.tb_qwen3_set_step_mode(self.h, int(mode)), "set_step_mode")
+
+    def step_kind(self):
+        """QW_STEP_KERNELS or QW_STEP_PERSISTENT once the step was recorded, else 0."""
+        return int(LIB.tb_qwen3_step_kind(self.h))
+
     def tp_handle(self):
         """This rank's 64-byte IPC handle of its exchange arena."""
         buf = ctypes.create_string_buffer(64)

@@ -1,0 +1,75 @@
+"""The persistent decode step (tb_step.cu: embed and every layer in one kernel,
+grid barriers between the phases) against the multi-kernel step on identical
+models: logits bit-identical, the same ids, positions and cache rows, over
+several consecutive steps (graph replays), at the small test shapes and at
+Qwen3-1.7B width (context 4096, the bench's attention split), plus the oracle
+check of the persistent path at batch 1."""
+import numpy as np
+import pytest
+
+import tabinfer_b200 as tb
+from tabinfer_b200 import _lib
+from qwen3_oracle import OracleModel
+from test_gpu_qwen3 import SMALL, _build, _check_step
+
+pytestmark = pytest.mark.gpu
+
+WIDE = dict(hidden=2048, layers=2, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=6144, vocab=20000,
+            rope_theta=1e6, rms_eps=1e-6, max_seq=4200, batch=1)
+
+
+def _pair(cfg, seed, prefill):
+    out = []
+    for mode in (_lib.QW_STEP_KERNELS, _lib.QW_STEP_PERSISTENT):
+        W, m = _build(cfg, seed, prefill)
+        m.set_step_mode(mode)
+        out.append(m)
+    return out
+
+
+@pytest.mark.parametrize("cfg,prefill", [(dict(SMALL, batch=1), [23]), (dict(SMALL, batch=1, n_heads=8, n_kv_heads=8), [40]),
+                                         (dict(SMALL, batch=1, max_seq=1024, layers=3), [700]), (WIDE, [4095])])
+def test_persistent_step_equals_kernels(cuda, cfg, prefill):
+    mk, mp = _pair(cfg, 31, prefill)
+    ids = [777 % cfg["vocab"]]
+    for m in (mk, mp):
+        m.set_tokens(ids, prefill)
+    for step in range(3):
+        for m in (mk, mp):
+            m.step()
+        assert mk.step_kind() == _lib.QW_STEP_KERNELS and mp.step_kind() == _lib.QW_STEP_PERSISTENT
+        np.testing.assert_array_equal(mp.logits().numpy(), mk.logits().numpy(), err_msg="step %d" % step)
+        assert mp.tokens() == mk.tokens()
+    n = prefill[0] + 3                    # rows past these were never written (uninitialised)
+    for l in range(cfg["layers"]):
+        for a, b in zip(mp.kv_host(l), mk.kv_host(l)):
+            np.testing.assert_array_equal(a[:, :n], b[:, :n])
+    assert mp.ctx.device_error() == 0
+    k, c = mp.launches_per_step()
+    assert 0 < k <= 4 and c == 0          # the persistent kernel, lm_head, argmax
+    for m in (mk, mp):
+        m.close()
+
+
+def test_persistent_step_matches_oracle(cuda):
+    cfg = dict(SMALL, batch=1, layers=2)
+    W, m = _build(cfg, 41, [17])
+    m.set_step_mode(_lib.QW_STEP_PERSISTENT)
+    om = OracleModel(cfg, W)
+    m.set_tokens([5], [17])
+    ids, pos = _check_step(m, om, cfg, [5], [17], route_f32=False)
+    _check_step(m, om, cfg, ids, pos, route_f32=False)
+    assert m.step_kind() == _lib.QW_STEP_PERSISTENT
+    m.close()
+
+
+def test_persistent_mode_refused_where_it_does_not_apply(cuda):
+    cfg = dict(SMALL, batch=2)
+    W, m = _build(cfg, 43, [3, 4])
+    m.set_step_mode(_lib.QW_STEP_PERSISTENT)
+    with pytest.raises(tb.TabInferError):
+        m.step()
+    m.set_step_mode(_lib.QW_STEP_AUTO)
+    m.step()
+    assert m.step_kind() == _lib.QW_STEP_KERNELS
+    m.close()
