@@ -1013,6 +1013,8 @@ def main():
                     help="three cold-L2 exact-sum prefill GEMM launches (for ncu), then exit")
     ap.add_argument("--profile-lm-head", default=None, choices=("int4_f32", "int4_dp4a", "tern"),
                     help="three cold-L2 batch-1 lm_head GEMVs of one weight kind (for ncu), then exit")
+    ap.add_argument("--step-mode", default="auto", choices=("auto", "kernels", "persistent"),
+                    help="decode step as one persistent kernel (auto: where it applies) or one kernel per op")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
     args = ap.parse_args()
@@ -1090,6 +1092,9 @@ def main():
     extra = args.warmup + args.steps + K2 + 16
     m = build_model(Q17, dev, B, S, extra, world, rank)
     tp_setup(m)
+    from tabinfer_b200 import _lib as _tl
+    m.set_step_mode({"auto": _tl.QW_STEP_AUTO, "kernels": _tl.QW_STEP_KERNELS,
+                     "persistent": _tl.QW_STEP_PERSISTENT}[args.step_mode])
     ids0 = [(1000 + 7919 * b) % Q17["vocab"] for b in range(B)]
     pos0 = [S - 1] * B
     m.set_tokens(ids0, pos0)
@@ -1113,6 +1118,32 @@ def main():
     barrier()
     e2e_total, h2d, d2h = time_e2e(m, K2, stream, ids0, pos0)
     e2e_ms = max_over_ranks(e2e_total / K2)
+    step_kind = {_tl.QW_STEP_KERNELS: "kernels", _tl.QW_STEP_PERSISTENT: "persistent"}.get(m.step_kind(), "?")
+    pers_us = None
+    kernels_alt = None
+    if step_kind == "persistent":
+        # the persistent kernel alone (embed + all layers), for its roofline
+        for _ in range(3):
+            m.step_layers()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K2):
+            m.step_layers()
+        e1.record(stream)
+        e1.synchronize()
+        pers_us = e0.elapsed_time(e1) * 1e3 / K2
+        if not args.no_extras and world == 1:
+            # the same model as one kernel per operation (identical results), for comparison
+            m.set_step_mode(_tl.QW_STEP_KERNELS)
+            m.set_tokens(ids0, pos0)
+            for _ in range(args.warmup):
+                m.step()
+            m.set_tokens(ids0, pos0)
+            torch.cuda.synchronize(dev)
+            msk = time_steps(m, args.steps, stream) / args.steps
+            kernels_alt = {"tok_per_s": round(B * 1e3 / msk, 2), "ms_per_step": round(msk, 4),
+                           "launches_per_step": m.launches_per_step()[0]}
     err = ctx.device_error()
     assert err == 0, "device error word 0x%x" % err
     m.close()
@@ -1126,6 +1157,21 @@ def main():
               "step_hbm_frac_per_rank": round(nbytes / (ms_max * 1e-3) / 1e9 / peak, 4)}
     roof = None
     cpu = None
+    if pers_us is not None:
+        lm_bytes = gemv_bytes(Q17["vocab"] // world, Q17["hidden"], B, 4 if B == 1 else 1 + 4 / 32)
+        body = nbytes - int(lm_bytes)
+        gbs = body / (pers_us * 1e-6) / 1e9
+        tp = os.path.join(REPO, "profiles", "traffic.json")
+        traffic = json.load(open(tp)).get("k_decode_step") if os.path.exists(tp) else None
+        roof = {"bound": "hbm", "kernel": "k_decode_step (persistent: embed + %d layers)" % Q17["layers"],
+                "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                "traffic": traffic, "peak_source": peak_src + " hbm_gbs (burst copy)",
+                "algorithmic_bytes_per_launch": body, "us_per_launch": round(pers_us, 2),
+                "timing": "CUDA events on the launching stream over %d back-to-back launches (weights 0.97 GB "
+                          "> L2)" % K2}
+        extras["step_kind"] = step_kind
+        if kernels_alt:
+            extras["decode_step_one_kernel_per_op"] = kernels_alt
     if rank == 0 and not args.no_extras:
         kinds = kernel_kinds(Q17, dev, world, S, peak)
         dom = max(kinds, key=lambda k: kinds[k]["us_per_step"])
@@ -1134,11 +1180,12 @@ def main():
         tp = os.path.join(REPO, "profiles", "traffic.json")
         if os.path.exists(tp) and world == 1:
             traffic = json.load(open(tp)).get(dom)
-        roof = {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": d["frac_of_peak"], "traffic": traffic,
-                "peak_source": peak_src + " hbm_gbs (burst copy)",
-                "algorithmic_bytes_per_launch": d["bytes_per_launch"], "us_per_launch": d["us_per_launch"],
-                "timing": "cold L2 (256 MB write before each launch), CUDA events on the launching stream"}
+        if roof is None:
+            roof = {"bound": "hbm", "kernel": dom, "achieved": d["gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": d["frac_of_peak"], "traffic": traffic,
+                    "peak_source": peak_src + " hbm_gbs (burst copy)",
+                    "algorithmic_bytes_per_launch": d["bytes_per_launch"], "us_per_launch": d["us_per_launch"],
+                    "timing": "cold L2 (256 MB write before each launch), CUDA events on the launching stream"}
         extras["kernels"] = kinds
     if world == 1 and rank == 0 and not args.no_extras:
         extras["gemv_chain_0.6b"] = chain_gbs(dev, ctx, 1, max(100, args.steps))

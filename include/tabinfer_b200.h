@@ -544,6 +544,18 @@ enum {
 TB_API int tb_qwen3_set_step_mode(tb_qwen3 *m, int mode);
 /* the kind the recorded step uses (TB_QW_STEP_KERNELS / _PERSISTENT), 0 before the first step */
 TB_API int tb_qwen3_step_kind(tb_qwen3 *m);
+/* Launch the persistent kernel alone (embed + every layer; no lm_head, no
+ * argmax, ids and pos unchanged) on the context's stream, to time it apart.
+ * Needs a recorded persistent step. */
+TB_API int tb_qwen3_step_layers(tb_qwen3 *m);
+/* Profiling: %globaltimer stamps of the persistent kernel into trace (device,
+ * u64 [SM count][1 + 33 * layers]; null turns it off): per CTA the kernel start,
+ * then per layer and phase (q/k/v, attention, o, gate/up, down) the moments its
+ * weights were ready, its activation row arrived, its activation was staged, it
+ * finished, and its grid barrier opened; then per layer 8 stamps of the CTA's
+ * first attention unit (start, q prep, k/v prep, tiles done, partial written,
+ * arrival counted, end, whether it combined). */
+TB_API int tb_qwen3_step_trace(tb_qwen3 *m, void *trace);
 /* Host-only: the block of a full [rows][cols] tensor of `kind` that rank
  * cfg->tp_rank keeps (norm vectors count as one row). */
 TB_API int tb_qwen3_shard(const tb_qwen3_config *cfg, int kind, int64_t *row0, int64_t *nrows,

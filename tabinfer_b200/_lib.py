@@ -101,6 +101,8 @@ SIGNATURES = {
     "tb_qwen3_tp_init": [P, P],
     "tb_qwen3_set_step_mode": [P, ctypes.c_int],
     "tb_qwen3_step_kind": [P],
+    "tb_qwen3_step_layers": [P],
+    "tb_qwen3_step_trace": [P, P],
     "tb_qwen3_tp_handle": [P, P],
     "tb_qwen3_tp_connect": [P, P],
     "tb_qwen3_decode_step": [P],

@@ -39,21 +39,29 @@ __device__ __forceinline__ void rope_cs(int j, int hd, long long pos, float thet
     *s = (float)sd;
 }
 
-// Per-head RMSNorm (w16) + RoPE of x (thread j holds element j of the head,
-// threads j >= hd hold nothing); every thread of the block calls it.  rk: hd
-// floats of shared memory, red: 8.
-__device__ __forceinline__ float norm_rope(float x, const uint16_t* w16, int hd, float eps, float c, float s, float* rk,
-                                           float* red)
+// Barrier of the threads sharing a computation: bar 0 is the whole CTA, bar id >
+// 0 a 128-thread group (one split unit of 4 warps) of a larger CTA.
+__device__ __forceinline__ void unit_sync(int bar)
 {
-    const int j = threadIdx.x, lane = j & 31, wid = j >> 5, nw = hd >> 5;
+    if (bar == 0) __syncthreads();
+    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(ATT_THREADS) : "memory");
+}
+
+// Per-head RMSNorm (w16) + RoPE of x (thread j holds element j of the head,
+// threads j >= hd hold nothing); every thread of the block (bar 0) or of the
+// 128-thread group (bar > 0) calls it.  rk: hd floats of shared memory, red: 8.
+__device__ __forceinline__ float norm_rope(float x, const uint16_t* w16, int hd, float eps, float c, float s, float* rk,
+                                           float* red, int j = threadIdx.x, int bar = 0)
+{
+    const int lane = j & 31, wid = j >> 5, nw = hd >> 5;
     const float ss = warp_sum(j < hd ? x * x : 0.0f);
     if (lane == 0 && wid < nw) red[wid] = ss;
-    __syncthreads();
+    unit_sync(bar);
     float t = 0.0f;
     for (int i = 0; i < nw; i++) t += red[i];
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), eps)));
     if (j < hd) rk[j] = __fmul_rn(__fmul_rn(x, inv), tb_h2f(w16[j]));
-    __syncthreads();
+    unit_sync(bar);
     float y = 0.0f;
     if (j < hd) {
         const int half = hd >> 1;
@@ -61,15 +69,15 @@ __device__ __forceinline__ float norm_rope(float x, const uint16_t* w16, int hd,
         const float rot = j < half ? -partner : partner;
         y = fmaf(rk[j], c, rot * s);
     }
-    __syncthreads();   // rk and red may be reused
+    unit_sync(bar);    // rk and red may be reused
     return y;
 }
 
 // snorm int8 of one 32-group per warp (pack4x8snorm of x / max(1e-12, maxabs))
 // into row dq / scales ds (element j of the head at dq[j], group scale at ds[j/32])
-__device__ __forceinline__ void quant_row(float x, int hd, int8_t* dq, float* ds)
+__device__ __forceinline__ void quant_row(float x, int hd, int8_t* dq, float* ds, int j = threadIdx.x)
 {
-    const int j = threadIdx.x, lane = j & 31;
+    const int lane = j & 31;
     if ((j >> 5) >= (hd >> 5)) return;
     const float m = fmaxf(1e-12f, warp_max(fabsf(x)));
     dq[j] = snorm8(__fdiv_rn(x, m));
@@ -136,14 +144,6 @@ struct DecLayout {
                   "split weights and column partials must fit in the stages");
 };
 
-// Barrier of the 4 warps running one unit: bar 0 is the whole CTA (a 128-thread
-// CTA), bar id > 0 a 128-thread group of a larger CTA.
-__device__ __forceinline__ void unit_sync(int bar)
-{
-    if (bar == 0) __syncthreads();
-    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(ATT_THREADS) : "memory");
-}
-
 // One (kv head, split) of the split-KV decode, run by 4 warps (tid 0..127).
 // Warp w takes the 32-key tiles w, w+4, w+8, ... of the split: with NST = 2 a
 // cp.async pipeline (tile j+1 in flight while tile j is scored), with NST = 1
@@ -157,6 +157,17 @@ __device__ __forceinline__ void unit_sync(int bar)
 // prefetch(early) requests each warp's first tile -- with early, not the tile
 // holding row S-1 (written by the step's own prep); run(early) requests that
 // one and does the rest.  The position (dpos) must not change in between.
+// attnPrepQ8 folded into a unit (the persistent decode step): the unit computes
+// its GRP q heads' norm + RoPE into shared memory itself, and the unit whose
+// split holds row pos = S-1 also writes that row of the cache (k: norm + RoPE +
+// int8, v: int8), before any warp requests it.
+struct PrepIn {
+    const float *q, *k, *v;          // this step's projections
+    const uint16_t *qn, *kn;         // q / k norm weights
+    const float* cs;                 // cos [HD], sin [HD] at pos
+    float eps;
+};
+
 template <int HD, int GRP, int NST>
 struct DecUnit {
     using L = DecLayout<HD, GRP, NST>;
@@ -166,6 +177,20 @@ struct DecUnit {
     const AttnArgs& a;
     uint8_t* smem;
     int hk, split, zb, tid, lane, wid, bar;
+    // persistent step: the unit runs the prep, and row S-1 of a first tile is
+    // written into the stage by the prep instead of copied (inject)
+    const PrepIn* prep = nullptr;
+    bool inject = false;
+    unsigned long long* tr = nullptr;   // optional %globaltimer stamps of the unit's stages (8 slots)
+
+    __device__ void ts(int k) const
+    {
+        if (tr && tid == 0) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            tr[k] = t;
+        }
+    }
     long long row_elems, row_groups;
     const int8_t* Kq;
     const int8_t* Vq;
@@ -202,7 +227,7 @@ struct DecUnit {
     // tile j of this warp -> stage s; always commits a group (possibly empty).
     // Rows are copied coalesced: in copy r, lanes 8q..8q+7 (4q..4q+3 for hd 64)
     // move the KV16 16-byte chunks of key r*RPI + q.  Scales: lane = key.
-    __device__ void issue(int j, int s) const
+    __device__ void issue(int j, int s, int skip = -1) const
     {
         constexpr int RPI = 32 / KV16;                  // rows per copy instruction
         const int tb0 = c0 + (wid + ATT_WARPS * j) * 32;
@@ -211,7 +236,7 @@ struct DecUnit {
 #pragma unroll
         for (int r = 0; r < KV16; r++) {
             const int kr = r * RPI + lane / KV16;
-            if (tb0 + kr < c1) {
+            if (tb0 + kr < c1 && tb0 + kr != skip) {
                 const long long src = (long long)(tb0 + kr) * row_elems + hk * HD + ch * 16;
                 const int dst = (kr * KV16 + (ch ^ (kr & (KV16 - 1)))) * 16;
                 cp_async16(st + L::ST_K + dst, Kq + src);
@@ -219,7 +244,7 @@ struct DecUnit {
             }
         }
         const int t = tb0 + lane;
-        if (t < c1) {
+        if (t < c1 && t != skip) {
             float* ksd = reinterpret_cast<float*>(st + L::ST_KS) + lane * NG;
             float* vsd = reinterpret_cast<float*>(st + L::ST_VS) + lane * NG;
             const float* ksr = Ks + (long long)t * row_groups + hk * NG;
@@ -245,6 +270,7 @@ struct DecUnit {
     __device__ void prefetch(bool early) const
     {
         if (!(early && first_new())) issue(0, 0);
+        else if (inject) issue(0, 0, S - 1);     // every row but S-1, which the prep writes
     }
 
     __device__ void run(bool early) const
@@ -262,9 +288,61 @@ struct DecUnit {
         float* ps = ps_all + wid * 32 * NG * GRP;
 
         const float qscale = rsqrtf((float)HD) * (1.0f / 127.0f);
-        if (early && first_new()) issue(0, 0);
-        for (int i = tid; i < GRP * HD; i += ATT_THREADS) qs[i] = __ldcg(qrow + (long long)hk * GRP * HD + i);
-        unit_sync(bar);
+        ts(0);
+        if (prep) {
+            // the stages may still be receiving prefetched tiles: work in ps / wm
+            float* rk = ps_all;
+            float* red = wm;
+            const float c = tid < HD ? prep->cs[tid] : 0.0f, sn = tid < HD ? prep->cs[HD + tid] : 0.0f;
+            for (int h = 0; h < GRP; h++) {
+                const long long o = (long long)zb * a.nHq * HD + (long long)(hk * GRP + h) * HD;
+                const float x = tid < HD ? __ldcg(prep->q + o + tid) : 0.0f;
+                const float y = norm_rope(x, prep->qn, HD, prep->eps, c, sn, rk, red, tid, bar);
+                if (tid < HD) qs[h * HD + tid] = y;
+            }
+            ts(1);
+            const int last = S - 1;
+            // the warp whose FIRST tile holds row S-1 gets it straight into its stage
+            const int wl = S > 0 ? (last - c0) >> 5 : ATT_WARPS;
+            const bool into_stage = inject && early && S > 0 && c0 <= last && last < c1 && wl < ATT_WARPS;
+            if (S > 0 && c0 <= last && last < c1) {
+                const long long o = (long long)zb * a.nKv * HD + (long long)hk * HD;
+                const long long row = (long long)last * row_elems + (long long)hk * HD;
+                const float kx = tid < HD ? __ldcg(prep->k + o + tid) : 0.0f;
+                const float vx = tid < HD ? __ldcg(prep->v + o + tid) : 0.0f;
+                const float kr = norm_rope(kx, prep->kn, HD, prep->eps, c, sn, rk, red, tid, bar);
+                // quant_row's values, into the cache and (into_stage) the stage of warp wl
+                const float km = fmaxf(1e-12f, warp_max(fabsf(kr))), vm = fmaxf(1e-12f, warp_max(fabsf(vx)));
+                const int8_t kq = snorm8(__fdiv_rn(kr, km)), vq = snorm8(__fdiv_rn(vx, vm));
+                if (tid < HD) {
+                    const_cast<int8_t*>(Kq)[row + tid] = kq;
+                    const_cast<int8_t*>(Vq)[row + tid] = vq;
+                    if (lane == 0) {
+                        const_cast<float*>(Ks)[row / 32 + (tid >> 5)] = km;
+                        const_cast<float*>(Vs)[row / 32 + (tid >> 5)] = vm;
+                    }
+                    if (into_stage) {
+                        uint8_t* st = smem + L::OFF_ST + wl * NST * L::STAGE;
+                        const int kr_ = last - (c0 + wl * 32), ch = tid >> 4;
+                        const int off = (kr_ * KV16 + (ch ^ (kr_ & (KV16 - 1)))) * 16 + (tid & 15);
+                        st[L::ST_K + off] = (uint8_t)kq;
+                        st[L::ST_V + off] = (uint8_t)vq;
+                        if (lane == 0) {
+                            reinterpret_cast<float*>(st + L::ST_KS)[kr_ * NG + (tid >> 5)] = km;
+                            reinterpret_cast<float*>(st + L::ST_VS)[kr_ * NG + (tid >> 5)] = vm;
+                        }
+                    }
+                }
+                if (!into_stage) __threadfence();    // the row reaches L2 before a warp's cp.async reads it
+            }
+            unit_sync(bar);
+            ts(2);
+            if (early && first_new() && !inject) issue(0, 0);
+        } else {
+            if (early && first_new()) issue(0, 0);
+            for (int i = tid; i < GRP * HD; i += ATT_THREADS) qs[i] = __ldcg(qrow + (long long)hk * GRP * HD + i);
+            unit_sync(bar);
+        }
 
         float m[GRP], l[GRP];
         float2 o[GRP][DPL / 2];
@@ -372,6 +450,7 @@ struct DecUnit {
         }
         cp_async_wait<0>();
         unit_sync(bar);    // every warp is done with its stages: reuse them for the merge
+        ts(3);
 
         // ---- merge warps
         float* wo = reinterpret_cast<float*>(smem + L::OFF_ST);     // [W][GRP][HD]
@@ -405,6 +484,7 @@ struct DecUnit {
             }
         }
         if (a.nsplit == 1) return;
+        ts(4);
 
         // ---- the last split of this kv head to finish combines all of them
         //      (ATTN_DEC_COMBINE, qwen3.js:2048-2069): out = sum_i e_i O_i / sum_i e_i l_i,
@@ -414,6 +494,8 @@ struct DecUnit {
         int* last = reinterpret_cast<int*>(wm);          // wm/wl are free again after the loop above
         if (tid == 0) *last = atomicAdd(counter, 1u) == (unsigned)(a.nsplit - 1);
         unit_sync(bar);
+        ts(5);
+        if (tr && tid == 0) tr[7] = *last;
         if (!*last) return;
         __threadfence();
         float* wts = reinterpret_cast<float*>(smem + L::OFF_ST);    // [GRP][nsplit]
@@ -479,6 +561,7 @@ struct DecUnit {
             reinterpret_cast<float4*>(outp + (long long)(hk * GRP + h) * HD)[c4] = res;
         }
         if (tid == 0) *counter = 0u;     // ready for the next call
+        ts(6);
     }
 };
 

@@ -132,6 +132,7 @@ struct tb_qwen3 {
     unsigned char* step_layers = nullptr;        // device per-layer records
     unsigned* step_ctrl = nullptr;               // [256] block arrivals, grid barrier, abort word
     bool step_direct = false;                    // persistent step launched per call (not capturable)
+    void* step_trace = nullptr;                  // optional phase trace of the persistent kernel
 };
 
 namespace {
@@ -300,7 +301,7 @@ bool persistent_ok(tb_qwen3* m)
 }
 
 // the step as embed + 28 layers in one persistent kernel, then the shared head
-int issue_step_persistent(tb_qwen3* m)
+tb_step_io step_io(tb_qwen3* m)
 {
     tb_step_io io{};
     io.layers = m->step_layers;
@@ -311,6 +312,13 @@ int issue_step_persistent(tb_qwen3* m)
     io.embed = m->embed;
     io.x = m->x[0]; io.q = m->q; io.k = m->k; io.v = m->v; io.qr = m->qr; io.attn = m->attn; io.swi = m->swi;
     io.PO = m->PO; io.PML = m->PML; io.counters = m->counters; io.ctrl = m->step_ctrl;
+    io.trace = m->step_trace;
+    return io;
+}
+
+int issue_step_persistent(tb_qwen3* m)
+{
+    const tb_step_io io = step_io(m);
     TRY(tb_step_launch(m->ctx, m->step, &io));
     return issue_head(m, 0);
 }
@@ -608,6 +616,13 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
     if (!rc) rc = alloc(m, &m->swi, B * m->I);
     if (!rc) rc = alloc(m, &m->logits, B * m->V);
     m->nsplit = tb_attn_auto_nsplit(ctx, c.max_seq, m->nKv * B);
+    if (B == 1 && m->P == 1) {
+        // one sequence on one GPU: one (kv head, split) unit per SM, the split
+        // count the persistent step runs best with (both step kinds use it, so
+        // they compute the same bits)
+        const long long by_keys = (c.max_seq + 127) / 128;
+        m->nsplit = (int)std::max(1LL, std::min(by_keys, (long long)(ctx->num_sms / m->nKv)));
+    }
     if (!rc) rc = alloc(m, &m->qr, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->PO, (size_t)B * m->nHq * m->nsplit * hd);
     if (!rc) rc = alloc(m, &m->PML, (size_t)B * m->nHq * m->nsplit * 2);
@@ -994,6 +1009,31 @@ TB_API int tb_qwen3_set_step_mode(tb_qwen3* m, int mode)
 TB_API int tb_qwen3_step_kind(tb_qwen3* m)
 {
     return m ? m->step_kind : 0;
+}
+
+// Phase trace of the persistent kernel: trace (device, u64 [SMs][1 + 33 * layers])
+// receives %globaltimer stamps from every later launch (null: off).  Per CTA:
+// kernel start, then per layer and phase (qkv, attention, o, gate/up, down):
+// weights ready, activation row loaded, activation staged, phase done, barrier
+// passed; then per layer 8 stamps of the CTA's first attention unit.
+TB_API int tb_qwen3_step_trace(tb_qwen3* m, void* trace)
+{
+    if (!m) return TB_ERR_INVALID;
+    m->step_trace = trace;
+    release_graph(m);
+    return TB_OK;
+}
+
+// The persistent kernel alone (embed + every layer, no lm_head / argmax) on the
+// context's stream, for timing it apart from the step's head; ids and pos are
+// left as they are, so repeated calls recompute the same position.
+TB_API int tb_qwen3_step_layers(tb_qwen3* m)
+{
+    if (!m) return TB_ERR_INVALID;
+    TB_REQUIRE(m->ctx, m->step_kind == TB_QW_STEP_PERSISTENT && m->step && m->step_layers,
+               "step_layers: the recorded step is not the persistent kernel");
+    const tb_step_io io = step_io(m);
+    return tb_step_launch(m->ctx, m->step, &io);
 }
 
 TB_API int tb_qwen3_launches_per_step(tb_qwen3* m, int* kernels, int* collectives)

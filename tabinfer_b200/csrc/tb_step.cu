@@ -11,11 +11,12 @@
 // the arithmetic.
 //
 // Phases of layer l (barrier after each):
-//   A  RMSNorm + QUANTQ8 of x, q/k/v rows (head-aligned 32-row blocks); the
-//      last CTA of a head runs attnPrepQ8 for it (q: norm + RoPE into qr;
-//      k: norm + RoPE + int8 row into the cache; v: int8 row)
-//   B  split-KV attention: (kv head, split) units on 4-warp groups, two per CTA;
-//      the last split of a kv head combines (DecUnit, the standalone kernel's code)
+//   A  RMSNorm + QUANTQ8 of x, q/k/v rows (32-row blocks)
+//   B  split-KV attention: (kv head, split) units on 4-warp groups, two per CTA
+//      (DecUnit, the standalone kernel's code); each unit runs attnPrepQ8 for
+//      its own q heads (norm + RoPE) and the unit holding row pos writes that
+//      cache row (k: norm + RoPE + int8, v: int8); the last split of a kv head
+//      combines
 //   C  QUANTQ8 of the attention output, o rows, += residual
 //   D  RMSNorm + QUANTQ8 of x, gate/up rows, SwiGLU
 //   E  QUANTQ8 of swi, down rows, += residual
@@ -60,53 +61,65 @@ struct StepArgs {
     float *x, *q, *k, *v, *qr, *attn, *swi, *PO, *PML;
     unsigned* counters;      // [nKv] split arrivals (zero between steps)
     unsigned* head_ctr;      // [nHq + 2 nKv] phase-A block arrivals (zero between steps)
-    unsigned* bar_count;     // grid barrier: arrivals, generation
-    unsigned* bar_gen;
+    unsigned long long* bar_count;   // grid barrier: arrivals since the model was made (monotonic)
     unsigned* abort_word;    // == this launch's tag: a CTA gave up in this launch
     int* err;
+    // optional phase trace: per CTA 1 + 33 * L %globaltimer stamps (kernel start;
+    // per layer and phase: weights ready, activation row loaded, activation
+    // staged, phase done, barrier passed; then per layer 8 slots of the CTA's
+    // first attention unit: start, q prep, k/v prep, tiles done, partial
+    // written, arrival counted, end, last-split flag)
+    unsigned long long* trace;
     // shared-memory layout (bytes)
-    int off_P, off_Q, off_R, off_xbuf, off_act, off_misc;
-    int xbuf_floats;
+    int off_P, off_Q, off_R, off_act, off_misc;
     int rpC, rpD;            // rows per CTA of o / down (rpC) and gate / up (rpD)
 };
 
-// ---- grid barrier ---------------------------------------------------------------
-__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v)
+__device__ __forceinline__ void stamp(const StepArgs& a, int slot)
 {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    if (a.trace && threadIdx.x == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        a.trace[(size_t)blockIdx.x * (1 + 33 * a.L) + slot] = t;
+    }
 }
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p)
+#define STAMP(ph, k) stamp(a, 1 + 25 * l + 5 * (ph) + (k))
+
+// ---- grid barrier ---------------------------------------------------------------
+__device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v)
 {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
 struct Ctl {
-    unsigned gen;            // barrier generation seen by this CTA (thread 0)
-    unsigned tag;            // this launch: the generation every CTA saw at its start, + 1
+    unsigned long long base; // arrivals before this launch (a multiple of the grid)
+    unsigned nb;             // barriers of this launch so far
+    unsigned tag;            // this launch (base / grid + 1), marks its abort
     int abort;               // this CTA stops
     unsigned pend;           // bulk copies in flight: bit b = buffer b (P, Q, R)
     unsigned par;            // mbarrier parity per buffer
 };
 
-// Every CTA arrives; the last one resets the count and publishes the next
-// generation; the others poll it (acquire).  Returns false when the launch is
-// being abandoned.
+// Every CTA adds its arrival (release) to one monotonic counter and polls it
+// (acquire) until the whole grid has arrived: one fire-and-forget add and the
+// polls, no reset.  Returns false when the launch is being abandoned.
 __device__ bool grid_sync(const StepArgs& a, Ctl* ctl)
 {
-    __threadfence();          // every thread's stores of this phase, before the arrival
-    __syncthreads();
+    __syncthreads();          // the CTA's stores of this phase happen before thread 0's release
     if (threadIdx.x == 0 && !ctl->abort) {
         __threadfence();
-        const unsigned target = ctl->gen + 1u;
-        if (atomicAdd(a.bar_count, 1u) == gridDim.x - 1) {
-            atomicExch(a.bar_count, 0u);
-            __threadfence();
-            st_release_gpu(a.bar_gen, target);
-        } else {
+        ctl->nb++;
+        const unsigned long long target = ctl->base + (unsigned long long)ctl->nb * gridDim.x;
+        red_release_add(a.bar_count, 1ull);
+        {
             long long it = 0;
-            while (ld_acquire_gpu(a.bar_gen) != target) {
+            while (ld_acquire_u64(a.bar_count) < target) {
                 ++it;
                 if ((it & 255) == 0 && *reinterpret_cast<volatile unsigned*>(a.abort_word) == ctl->tag) {
                     ctl->abort = 1;
@@ -121,7 +134,6 @@ __device__ bool grid_sync(const StepArgs& a, Ctl* ctl)
                 if (it > 2048) __nanosleep(32);
             }
         }
-        ctl->gen = target;
     }
     __syncthreads();
     return !ctl->abort;
@@ -221,9 +233,11 @@ __device__ bool await_buf(const StepArgs& a, Ctl* ctl, int buf, uint64_t* bars)
 
 // ---- one phase's GEMV over the CTA's rows (the standalone consumer loop, B = 1) --
 // w_s: [n][G] 16-byte weight groups, then [n][G] f16 scales
+// own: this CTA's rows of the residual x kept in shared memory (their only
+// writer is this CTA), so y = own + W.a needs no read of y from memory
 template <int NM>
 __device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
-                          float* y, int row0, bool residual)
+                          float* y, int row0, float* own)
 {
     constexpr int RPW = 4, NW = THREADS / 32;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -261,26 +275,90 @@ __device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, con
                 if (NM == 2) {
                     const float g = acc[q][0], u = acc[q][NM - 1];
                     *yp = __fdiv_rn(g, 1.0f + expf(-g)) * u;
+                } else if (own) {
+                    const float v = own[r] + acc[q][0];
+                    own[r] = v;
+                    *yp = v;
                 } else {
-                    *yp = (residual ? __ldcg(yp) : 0.0f) + acc[q][0];
+                    *yp = 0.0f + acc[q][0];
                 }
             }
         }
     }
 }
 
-// QUANTQ8 (optionally RMSNorm first) of a whole f32 row written by other CTAs
-__device__ __forceinline__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, int K, bool norm,
-                                      const uint16_t* nws, float* red)
+// QUANTQ8 (optionally RMSNorm first) of a whole f32 row written by other CTAs,
+// into the permuted int8 layout of stage_q8<1, false> with the same bits: thread
+// t holds float4s f = t, t+256, ... in registers (the canonical sum-of-squares
+// order), 8 consecutive threads (one warp-aligned 32-group) find the group
+// maximum and sum with shuffles, and pairs of threads assemble the even / odd
+// byte words of a weight word.  Every thread is busy and there is one
+// round trip to memory.  K % 32 == 0, K <= 8192.
+__device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, int K, bool norm, const uint16_t* nws,
+                      float* red, int slot)
 {
-    Args a{};
-    a.K = K;
-    a.act_src = norm ? ACT_RMSNORM : ACT_F32;
-    a.x = x;
-    a.eps = sa.eps;
-    stage_q8<1, false, true>(a, smem + sa.off_act, reinterpret_cast<float*>(smem + sa.off_xbuf), sa.xbuf_floats, red,
-                             nws);
+    constexpr int MAXF = 8;
+    const int tid = threadIdx.x, G = K >> 5, K4 = K >> 2;
+    const int nf = (K4 + THREADS - 1) / THREADS;
+    float4 v[MAXF];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXF; i++) {
+        const int f = i * THREADS + tid;
+        v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < nf && f < K4) v[i] = __ldcg(reinterpret_cast<const float4*>(x) + f);
+    }
+#pragma unroll
+    for (int i = 0; i < MAXF; i++)
+        if (i < nf && i * THREADS + tid < K4) ss = sumsq_f4(v[i], ss);
+    if (sa.trace && tid == 0) {   // the row has arrived in thread 0's registers
+        asm volatile("" ::"f"(ss));
+        stamp(sa, slot);
+    }
+    float inv = 1.0f;
+    if (norm) {
+        float tot;
+        block256_reduce_rows<1>(&ss, red, &tot);
+        inv = rms_inv(tot, K, sa.eps);
+    }
+    uint4* xlo = reinterpret_cast<uint4*>(smem + sa.off_act);
+    uint4* xhi = xlo + G;
+    int* xs8 = reinterpret_cast<int*>(xhi + G);
+    float* xsf = reinterpret_cast<float*>(xs8 + G);
+#pragma unroll
+    for (int i = 0; i < MAXF; i++) {
+        if (i >= nf) break;
+        const int f = i * THREADS + tid;
+        const bool live = f < K4;              // whole 32-groups (8 consecutive f) are live or not
+        float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        if (norm && live) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) e[j] = __fmul_rn(__fmul_rn(e[j], inv), tb_h2f(nws[4 * f + j]));
+        }
+        float mx = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const float scale = q8_scale(mx), is = q8_inv(scale);
+        const int q0 = q8_quant(e[0], is), q1 = q8_quant(e[1], is), q2 = q8_quant(e[2], is), q3 = q8_quant(e[3], is);
+        // this thread's k = 4*j4 .. 4*j4+3 of the group: weight word j4/2, half j4&1
+        const uint32_t ev = ((uint32_t)q0 & 0xffu) | (((uint32_t)q2 & 0xffu) << 8);
+        const uint32_t od = ((uint32_t)q1 & 0xffu) | (((uint32_t)q3 & 0xffu) << 8);
+        const uint32_t ev_p = __shfl_xor_sync(0xffffffffu, ev, 1), od_p = __shfl_xor_sync(0xffffffffu, od, 1);
+        int sum = q0 + q1 + q2 + q3;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        const int j4 = f & 7, g = f >> 3;
+        if (live && !(j4 & 1)) {
+            const int w = j4 >> 1;
+            uint32_t* dst = reinterpret_cast<uint32_t*>((w < 2 ? xlo : xhi) + g) + 2 * (w & 1);
+            *reinterpret_cast<uint2*>(dst) = make_uint2(ev | (ev_p << 16), od | (od_p << 16));
+            if (j4 == 0) { xs8[g] = 8 * sum; xsf[g] = scale; }
+        }
+    }
     __syncthreads();
+    stamp(sa, slot + 1);
 }
 
 __device__ __forceinline__ AttnArgs attn_args(const StepArgs& a, const StepLayer& Ly)
@@ -292,57 +370,63 @@ __device__ __forceinline__ AttnArgs attn_args(const StepArgs& a, const StepLayer
     return t;
 }
 
-// attention units of this CTA: unit u = blockIdx.x + gridDim.x * (2 i + group)
-template <int GRP>
+// Units on CTAs: slot u = blockIdx.x + gridDim.x * (2 i + group).  The (kv head,
+// split) of slot u is rotated so the last splits (they hold row pos: prep of the
+// k/v row, usually the combine) land on the slots gridDim-nKv .. gridDim-1, whose
+// CTAs carry no second unit when there are fewer than 2 * gridDim units.
+__device__ __forceinline__ int unit_rot(const StepArgs& a, int u)
+{
+    const int N = a.nKv * a.nsplit, G = gridDim.x;
+    return N > G ? (u + N - G) % N : u;
+}
+
+// attention units of this CTA: unit u = blockIdx.x + gridDim.x * (NG i + group).
+// UNST = 2: at most one unit per CTA (group 0, two-stage tile pipeline); UNST = 1:
+// two groups, one stage each.
+template <int GRP, int UNST>
 __device__ void attn_prefetch(const StepArgs& a, int l, unsigned char* smem)
 {
-    using U = DecUnit<STEP_HD, GRP, 1>;
+    using U = DecUnit<STEP_HD, GRP, UNST>;
+    constexpr int NGR = UNST == 2 ? 1 : 2;
     const int grp = threadIdx.x >> 7, gtid = threadIdx.x & 127;
+    if (grp >= NGR) return;
     const int u = blockIdx.x + gridDim.x * grp;
     if (u >= a.nKv * a.nsplit) return;
     const AttnArgs t = attn_args(a, a.layers[l]);
-    U unit(t, smem + a.off_P + grp * U::L::BYTES, u % a.nKv, u / a.nKv, 0, gtid, 1 + grp);
+    const int r = unit_rot(a, u);
+    U unit(t, smem + a.off_P + grp * U::L::BYTES, r % a.nKv, r / a.nKv, 0, gtid, 1 + grp);
+    unit.inject = true;
     unit.prefetch(true);
 }
 
-template <int GRP>
-__device__ void attn_run(const StepArgs& a, int l, unsigned char* smem)
+template <int GRP, int UNST>
+__device__ void attn_run(const StepArgs& a, int l, unsigned char* smem, const float* cs)
 {
-    using U = DecUnit<STEP_HD, GRP, 1>;
+    using U = DecUnit<STEP_HD, GRP, UNST>;
+    constexpr int NGR = UNST == 2 ? 1 : 2;
     const int grp = threadIdx.x >> 7, gtid = threadIdx.x & 127;
-    const AttnArgs t = attn_args(a, a.layers[l]);
+    if (grp >= NGR) return;
+    const StepLayer& Ly = a.layers[l];
+    const AttnArgs t = attn_args(a, Ly);
+    const PrepIn pin{a.q, a.k, a.v, Ly.qn, Ly.kn, cs, a.eps};
     for (int i = 0;; i++) {
-        const int u = blockIdx.x + gridDim.x * (2 * i + grp);
+        const int u = blockIdx.x + gridDim.x * (NGR * i + grp);
         if (u >= a.nKv * a.nsplit) break;
-        U unit(t, smem + a.off_P + grp * U::L::BYTES, u % a.nKv, u / a.nKv, 0, gtid, 1 + grp);
-        if (i > 0) unit.prefetch(false);
-        unit.run(i == 0);
+        const int r = unit_rot(a, u);
+        U unit(t, smem + a.off_P + grp * U::L::BYTES, r % a.nKv, r / a.nKv, 0, gtid, 1 + grp);
+        unit.prep = &pin;
+        if (a.trace && i == 0 && grp == 0)
+            unit.tr = a.trace + (size_t)blockIdx.x * (1 + 33 * a.L) + 1 + 25 * a.L + 8 * l;
+        // the first unit's tiles were requested in an earlier phase (row pos is
+        // written into its stage by the prep); a later unit requests them now,
+        // the tile holding row pos only after the prep wrote that row
+        unit.inject = i == 0;
+        if (i > 0) unit.prefetch(true);
+        unit.run(true);
     }
 }
 
-// attnPrepQ8 of one head, by the whole CTA (thread j = element j), as k_attn_prep
-__device__ void prep_head(const StepArgs& a, const StepLayer& Ly, int head, int pos, const float* cs, float* rk,
-                          float* red)
-{
-    const int j = threadIdx.x, hd = STEP_HD;
-    const bool isQ = head < a.nHq, isK = !isQ && head < a.nHq + a.nKv;
-    const int hh = isQ ? head : (isK ? head - a.nHq : head - a.nHq - a.nKv);
-    const float* src = isQ ? a.q : (isK ? a.k : a.v);
-    float x = j < hd ? __ldcg(src + (long long)hh * hd + j) : 0.0f;
-    if (isQ || isK) {
-        const float c = j < hd ? cs[j] : 0.0f, s = j < hd ? cs[hd + j] : 0.0f;
-        x = norm_rope(x, isQ ? Ly.qn : Ly.kn, hd, a.eps, c, s, rk, red);
-        if (isQ) {
-            if (j < hd) a.qr[(long long)hh * hd + j] = x;
-            return;
-        }
-    }
-    if (pos < 0 || pos >= a.max_seq) return;   // reported by the attention units
-    const long long row = (long long)pos * a.nKv * hd + (long long)hh * hd;
-    quant_row(x, hd, (isK ? Ly.Kq : Ly.Vq) + row, (isK ? Ly.Ks : Ly.Vs) + row / 32);
-}
-
-template <int GRP>
+template <int GRP, int UNST>
 __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
 {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -353,14 +437,19 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
     float* cs = reinterpret_cast<float*>(misc + 512);                // cos [hd], sin [hd]
     float* rk = cs + 2 * STEP_HD;                                    // [hd]
     int* flag = reinterpret_cast<int*>(rk + STEP_HD);
+    float* xo = reinterpret_cast<float*>(misc + 2112);               // this CTA's rows of x [rpC <= 64]
     const int tid = threadIdx.x;
     const int pos = a.pos[0];
+    stamp(a, 0);
 
     if (tid == 0) {
-        // no barrier of this launch can complete before every CTA has read the
-        // generation, so all CTAs read the same value: it tags the launch
-        ctl->gen = ld_acquire_gpu(a.bar_gen);
-        ctl->tag = ctl->gen + 1u;
+        // every launch adds a whole number of grids of arrivals, and no barrier of
+        // this launch opens before every CTA arrived, so each CTA reads the count
+        // at most grid - 1 arrivals into this launch: rounding down gives the base
+        const unsigned long long c0 = ld_acquire_u64(a.bar_count);
+        ctl->base = c0 - c0 % gridDim.x;
+        ctl->nb = 0;
+        ctl->tag = (unsigned)(ctl->base / gridDim.x) + 1u;
         ctl->abort = 0;
         ctl->pend = 0;
         ctl->par = 0;
@@ -378,12 +467,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
         request(a, ctl, BUF_R, 0, 0, smem, bars);
         request(a, ctl, BUF_Q, 4, 0, smem, bars);
     }
-    attn_prefetch<GRP>(a, 0, smem);
+    attn_prefetch<GRP, UNST>(a, 0, smem);
     // embed: this CTA's rows of x (the o / down row slice)
     {
         const int r0 = rowsC0(a), n = rowsC(a);
         const uint32_t id = a.ids[0];
-        for (int i = tid; i < n; i += THREADS) a.x[r0 + i] = tb_h2f(a.embed[(long long)id * a.H + r0 + i]);
+        for (int i = tid; i < n; i += THREADS) {
+            const float e = tb_h2f(a.embed[(long long)id * a.H + r0 + i]);
+            xo[i] = e;
+            a.x[r0 + i] = e;
+        }
     }
     if (!grid_sync(a, ctl)) goto drain;
 
@@ -393,76 +486,77 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
         // ---- A: rmsnorm + quant of x, q/k/v rows, prep of completed heads
         {
             if (!await_buf(a, ctl, BUF_R, bars)) goto drain;
+            STAMP(0, 0);
             const BlockA b = block_a(a);
             const unsigned char* wR = smem + a.off_R;
             const uint16_t* nws = reinterpret_cast<const uint16_t*>(wR + (b.live ? mat_bytes(RBA, a.H) : 0));
             if (b.live) {
-                stage(a, smem, a.x, a.H, true, nws, red);
+                stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
                 float* y = b.mat == WQ ? a.q : (b.mat == WK ? a.k : a.v);
-                gemv_rows<1>(smem + a.off_act, wR, nullptr, RBA, a.H / 32, y, b.row0, false);
-                __threadfence();      // this block's rows, before its arrival at the head
-                __syncthreads();
-                if (tid == 0) {
-                    __threadfence();
-                    const unsigned bph = STEP_HD / RBA;
-                    *flag = atomicAdd(a.head_ctr + b.head, 1u) == bph - 1;
-                }
-                __syncthreads();
-                if (*flag) {
-                    __threadfence();
-                    prep_head(a, Ly, b.head, pos, cs, rk, red);
-                    __syncthreads();
-                    if (tid == 0) a.head_ctr[b.head] = 0u;
-                }
+                gemv_rows<1>(smem + a.off_act, wR, nullptr, RBA, a.H / 32, y, b.row0, nullptr);
             }
             __syncthreads();
             if (tid == 0) request(a, ctl, BUF_R, 2, l, smem, bars);
+            STAMP(0, 3);
             if (!grid_sync(a, ctl)) goto drain;
+            STAMP(0, 4);
         }
         // ---- B: attention (prep'd q, cache row pos written in A)
         {
-            attn_run<GRP>(a, l, smem);
+            STAMP(1, 0);
+            attn_run<GRP, UNST>(a, l, smem, cs);
             __syncthreads();
             if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
+            STAMP(1, 3);
             if (!grid_sync(a, ctl)) goto drain;
+            STAMP(1, 4);
         }
         // ---- C: quant of the attention output, o rows += x
         {
             if (!await_buf(a, ctl, BUF_R, bars)) goto drain;
+            STAMP(2, 0);
             const int n = rowsC(a);
             if (n > 0) {
-                stage(a, smem, a.attn, a.nHq * STEP_HD, false, nullptr, red);
-                gemv_rows<1>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x, rowsC0(a), true);
+                stage(a, smem, a.attn, a.nHq * STEP_HD, false, nullptr, red, 1 + 25 * l + 5 * 2 + 1);
+                gemv_rows<1>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
             if (tid == 0 && more) request(a, ctl, BUF_R, 0, l + 1, smem, bars);
+            STAMP(2, 3);
             if (!grid_sync(a, ctl)) goto drain;
+            STAMP(2, 4);
         }
         // ---- D: rmsnorm + quant of x, gate/up rows, swiglu
         {
             if (!await_buf(a, ctl, BUF_P, bars)) goto drain;
+            STAMP(3, 0);
             const int n = rowsD(a);
             const unsigned char* wP = smem + a.off_P;
             if (n > 0) {
                 const uint16_t* nws = reinterpret_cast<const uint16_t*>(wP + 2 * mat_bytes(n, a.H));
-                stage(a, smem, a.x, a.H, true, nws, red);
-                gemv_rows<2>(smem + a.off_act, wP, wP + mat_bytes(n, a.H), n, a.H / 32, a.swi, rowsD0(a), false);
+                stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 3 + 1);
+                gemv_rows<2>(smem + a.off_act, wP, wP + mat_bytes(n, a.H), n, a.H / 32, a.swi, rowsD0(a), nullptr);
             }
             __syncthreads();
-            if (more) attn_prefetch<GRP>(a, l + 1, smem);
+            if (more) attn_prefetch<GRP, UNST>(a, l + 1, smem);
+            STAMP(3, 3);
             if (!grid_sync(a, ctl)) goto drain;
+            STAMP(3, 4);
         }
         // ---- E: quant of swi, down rows += x
         {
             if (!await_buf(a, ctl, BUF_Q, bars)) goto drain;
+            STAMP(4, 0);
             const int n = rowsC(a);
             if (n > 0) {
-                stage(a, smem, a.swi, a.I, false, nullptr, red);
-                gemv_rows<1>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), true);
+                stage(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
+                gemv_rows<1>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
             if (tid == 0 && more) request(a, ctl, BUF_Q, 4, l + 1, smem, bars);
+            STAMP(4, 3);
             if (more && !grid_sync(a, ctl)) goto drain;
+            STAMP(4, 4);
         }
     }
 drain:
@@ -480,7 +574,7 @@ drain:
 // ---- host side ---------------------------------------------------------------------
 struct tb_step_plan {
     StepArgs a;
-    int smem = 0, grid = 0, grp = 0;
+    int smem = 0, grid = 0, grp = 0, unst = 1;
 };
 
 // Layout and feasibility of the persistent step for these sizes on this device;
@@ -495,36 +589,38 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     if (hd != STEP_HD || nKv <= 0 || nHq % nKv || (grp != 1 && grp != 2 && grp != 4 && grp != 8))
         return TB_ERR_UNSUPPORTED;
     // K % 256: every slice's scales (n * K/16 bytes) are whole 16-byte chunks for the bulk copies
-    if (H % 256 || I % 256 || (nHq * hd) % 256 || H > 8192 || I > 16384) return TB_ERR_UNSUPPORTED;
+    // K <= 8192: the activation staging holds a row in 8 float4 per thread
+    if (H % 256 || I % 256 || (nHq * hd) % 256 || H > 8192 || I > 8192 || nHq * hd > 8192) return TB_ERR_UNSUPPORTED;
     if ((nHq + 2 * nKv) * hd / RBA > G) return TB_ERR_UNSUPPORTED;   // one phase-A block per CTA
     if (nsplit < 1 || nsplit > 256) return TB_ERR_UNSUPPORTED;
     StepArgs a{};
     a.L = L; a.H = H; a.nHq = nHq; a.nKv = nKv; a.I = I; a.nsplit = nsplit; a.max_seq = max_seq;
     a.rpC = (H + G - 1) / G;
     a.rpD = (I + G - 1) / G;
+    if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
     auto mb = [](int n, int K) { return (size_t)n * (K / 2 + K / 16); };
+    // one unit per CTA (two-stage tiles) when the units fit the grid, else two
+    // one-stage units per CTA
+    const int unst = nKv * nsplit <= G ? 2 : 1;
     size_t unit_bytes = 0;
     switch (grp) {
-    case 1: unit_bytes = DecLayout<STEP_HD, 1, 1>::BYTES; break;
-    case 2: unit_bytes = DecLayout<STEP_HD, 2, 1>::BYTES; break;
-    case 4: unit_bytes = DecLayout<STEP_HD, 4, 1>::BYTES; break;
-    default: unit_bytes = DecLayout<STEP_HD, 8, 1>::BYTES; break;
+    case 1: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 1, 2>::BYTES : 2 * DecLayout<STEP_HD, 1, 1>::BYTES; break;
+    case 2: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 2, 2>::BYTES : 2 * DecLayout<STEP_HD, 2, 1>::BYTES; break;
+    case 4: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 4, 2>::BYTES : 2 * DecLayout<STEP_HD, 4, 1>::BYTES; break;
+    default: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 8, 2>::BYTES : 2 * DecLayout<STEP_HD, 8, 1>::BYTES; break;
     }
     auto up = [](size_t v) { return (v + 127) & ~size_t(127); };
-    const size_t bP = up(std::max(2 * unit_bytes, 2 * mb(a.rpD, H) + (size_t)H * 2));
+    const size_t bP = up(std::max(unit_bytes, 2 * mb(a.rpD, H) + (size_t)H * 2));
     const size_t bQ = up(mb(a.rpC, I));
     const size_t bR = up(std::max(mb(RBA, H) + (size_t)H * 2, mb(a.rpC, nHq * hd)));
     const int Kmax = std::max(std::max(H, I), nHq * hd);
-    const size_t xbuf = up((size_t)Kmax * 4);
     const size_t act = up((size_t)(Kmax / 32) * 40);
-    const size_t misc = 512 + 3 * STEP_HD * 4 + 128;
+    const size_t misc = 2112 + 64 * 4;     // barriers, control, reduction, rope, prep row, flag, own x rows
     a.off_P = 0;
     a.off_Q = (int)bP;
     a.off_R = (int)(bP + bQ);
-    a.off_xbuf = (int)(bP + bQ + bR);
-    a.off_act = (int)(bP + bQ + bR + xbuf);
-    a.off_misc = (int)(bP + bQ + bR + xbuf + act);
-    a.xbuf_floats = (int)(xbuf / 4);
+    a.off_act = (int)(bP + bQ + bR);
+    a.off_misc = (int)(bP + bQ + bR + act);
     const size_t total = (size_t)a.off_misc + misc;
     int maxsm = 0;
     cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device);
@@ -537,6 +633,7 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     p->smem = (int)total;
     p->grid = G;
     p->grp = grp;
+    p->unst = unst;
     *out = p;
     return TB_OK;
 }
@@ -554,14 +651,15 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.ids = io->ids; a.pos = io->pos; a.embed = io->embed;
     a.x = io->x; a.q = io->q; a.k = io->k; a.v = io->v; a.qr = io->qr; a.attn = io->attn; a.swi = io->swi;
     a.PO = io->PO; a.PML = io->PML; a.counters = io->counters; a.head_ctr = io->ctrl;
-    a.bar_count = io->ctrl + 64; a.bar_gen = io->ctrl + 96; a.abort_word = io->ctrl + 128;
+    a.bar_count = reinterpret_cast<unsigned long long*>(io->ctrl + 64); a.abort_word = io->ctrl + 128;
     a.err = ctx->dev_error;
+    a.trace = reinterpret_cast<unsigned long long*>(io->trace);
     void (*kern)(const StepArgs) = nullptr;
     switch (p->grp) {
-    case 1: kern = k_decode_step<1>; break;
-    case 2: kern = k_decode_step<2>; break;
-    case 4: kern = k_decode_step<4>; break;
-    default: kern = k_decode_step<8>; break;
+    case 1: kern = p->unst == 2 ? k_decode_step<1, 2> : k_decode_step<1, 1>; break;
+    case 2: kern = p->unst == 2 ? k_decode_step<2, 2> : k_decode_step<2, 1>; break;
+    case 4: kern = p->unst == 2 ? k_decode_step<4, 2> : k_decode_step<4, 1>; break;
+    default: kern = p->unst == 2 ? k_decode_step<8, 2> : k_decode_step<8, 1>; break;
     }
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "decode step attribute: %s", cudaGetErrorString(e));

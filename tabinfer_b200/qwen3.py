@@ -196,6 +196,16 @@ class Qwen3:
         all layers; batch 1, one GPU, int4 layer weights)."""
         self.ctx.check(LIB.tb_qwen3_set_step_mode(self.h, int(mode)), "set_step_mode")
 
+    def step_layers(self):
+        """The persistent kernel alone (embed + every layer) at the current
+        position, for timing; needs a recorded persistent step."""
+        self.ctx.check(LIB.tb_qwen3_step_layers(self.h), "step_layers")
+
+    def step_trace(self, buf):
+        """Phase trace of the persistent kernel into buf (int64 CUDA tensor of
+        SMs x (1 + 33 * layers)), or None to stop."""
+        self.ctx.check(LIB.tb_qwen3_step_trace(self.h, None if buf is None else _p(buf)), "step_trace")
+
     def step_kind(self):
         """QW_STEP_KERNELS or QW_STEP_PERSISTENT once the step was recorded, else 0."""
         return int(LIB.tb_qwen3_step_kind(self.h))
