@@ -742,6 +742,26 @@ def profile_decode(context):
     print("profile decode done: %d kernels per step" % kernels, flush=True)
 
 
+def profile_step(layers):
+    """The persistent decode step of a Qwen3-1.7B-width model with `layers` layers
+    (context 4096, batch 1): one recorded step, then three launches of the
+    persistent kernel alone, for an ncu capture of one of them."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    m = build_model(dict(Q17, layers=layers), dev, 1, 4096, 16, 1, 0)
+    m.set_tokens([1000], [4095])
+    m.step()
+    assert m.step_kind() == 2, "the persistent step does not apply"
+    for _ in range(3):
+        m.step_layers()
+    torch.cuda.synchronize()
+    err = tb.default_context(0).device_error()
+    assert err == 0, err
+    m.close()
+    print("profile step done", flush=True)
+
+
 def profile_gemm(M, N, K):
     """Three cold-L2 launches of the tcgen05 prefill GEMM (bf16 activations) at
     M x N x K (config 4: M in {512, 2048, 8192}), for an ncu capture of one."""
@@ -1015,11 +1035,16 @@ def main():
                     help="three cold-L2 batch-1 lm_head GEMVs of one weight kind (for ncu), then exit")
     ap.add_argument("--step-mode", default="auto", choices=("auto", "kernels", "persistent"),
                     help="decode step as one persistent kernel (auto: where it applies) or one kernel per op")
+    ap.add_argument("--profile-step", type=int, default=0, metavar="LAYERS",
+                    help="persistent decode step of a LAYERS-layer 1.7B-width model, launched alone (for ncu)")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
     args = ap.parse_args()
     if args.profile_decode:
         profile_decode(args.profile_decode)
+        return
+    if args.profile_step:
+        profile_step(args.profile_step)
         return
     if args.profile_lm_head:
         profile_lm_head(args.profile_lm_head)

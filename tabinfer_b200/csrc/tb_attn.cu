@@ -87,16 +87,16 @@ __global__ void __launch_bounds__(256) k_kv_quant_write(const float* __restrict_
 }
 
 // hd fixed at compile time (64 or 128); GRP = q heads per kv head.  One CTA
-// (4 warps) per (kv head, split); the split's work is DecUnit (tb_attn_dev.cuh).
-template <int HD, int GRP, bool EARLY>
-__global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
+// (W warps) per (kv head, split); the split's work is DecUnit (tb_attn_dev.cuh).
+template <int HD, int GRP, bool EARLY, int W>
+__global__ void __launch_bounds__(32 * W) k_attn_decode(const AttnArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     if constexpr (EARLY) {
         // the position and every cache row below S-1 come from earlier steps: a
         // warp's first tile is fetched before griddepcontrol.wait unless it holds
         // row S-1, which the preceding prep kernel writes
-        DecUnit<HD, GRP, 2> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
+        DecUnit<HD, GRP, 2, W> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
         u.prefetch(true);
         tb_pdl_wait();
         tb_pdl_trigger();
@@ -104,26 +104,34 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnArgs a)
     } else {
         tb_pdl_wait();
         tb_pdl_trigger();
-        DecUnit<HD, GRP, 2> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
+        DecUnit<HD, GRP, 2, W> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
         u.prefetch(false);
         u.run(false);
     }
 }
 
-template <int HD, int GRP, bool EARLY>
-int launch_decode(tb_ctx* ctx, const AttnArgs& a)
+template <int HD, int GRP, bool EARLY, int W>
+int launch_decode_w(tb_ctx* ctx, const AttnArgs& a)
 {
-    constexpr int bytes = DecLayout<HD, GRP, 2>::BYTES;
-    auto kern = k_attn_decode<HD, GRP, EARLY>;
+    constexpr int bytes = DecLayout<HD, GRP, 2, W>::BYTES;
+    auto kern = k_attn_decode<HD, GRP, EARLY, W>;
     static bool attr_set[64] = {};   // per device and instantiation; setting it twice is harmless
     if (ctx->device >= 64 || !attr_set[ctx->device]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
         if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode attribute: %s", cudaGetErrorString(e));
         if (ctx->device < 64) attr_set[ctx->device] = true;
     }
-    cudaError_t e = tb_launch(ctx, kern, dim3(a.nKv, a.nsplit, a.grid_z), dim3(ATT_THREADS), bytes, a);
+    cudaError_t e = tb_launch(ctx, kern, dim3(a.nKv, a.nsplit, a.grid_z), dim3(32 * W), bytes, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_decode launch: %s", cudaGetErrorString(e));
     return TB_OK;
+}
+
+// one sequence (the decode step at batch 1, ~one split per SM): 8-warp splits,
+// as the persistent decode step runs them; several sequences: 4-warp splits
+template <int HD, int GRP, bool EARLY>
+int launch_decode(tb_ctx* ctx, const AttnArgs& a)
+{
+    return a.grid_z == 1 ? launch_decode_w<HD, GRP, EARLY, 8>(ctx, a) : launch_decode_w<HD, GRP, EARLY, 4>(ctx, a);
 }
 
 template <bool EARLY>

@@ -40,28 +40,28 @@ __device__ __forceinline__ void rope_cs(int j, int hd, long long pos, float thet
 }
 
 // Barrier of the threads sharing a computation: bar 0 is the whole CTA, bar id >
-// 0 a 128-thread group (one split unit of 4 warps) of a larger CTA.
-__device__ __forceinline__ void unit_sync(int bar)
+// 0 a group of nthr threads (one split unit) of a larger CTA.
+__device__ __forceinline__ void unit_sync(int bar, int nthr = ATT_THREADS)
 {
     if (bar == 0) __syncthreads();
-    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(ATT_THREADS) : "memory");
+    else asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthr) : "memory");
 }
 
 // Per-head RMSNorm (w16) + RoPE of x (thread j holds element j of the head,
 // threads j >= hd hold nothing); every thread of the block (bar 0) or of the
 // 128-thread group (bar > 0) calls it.  rk: hd floats of shared memory, red: 8.
 __device__ __forceinline__ float norm_rope(float x, const uint16_t* w16, int hd, float eps, float c, float s, float* rk,
-                                           float* red, int j = threadIdx.x, int bar = 0)
+                                           float* red, int j = threadIdx.x, int bar = 0, int nthr = ATT_THREADS)
 {
     const int lane = j & 31, wid = j >> 5, nw = hd >> 5;
     const float ss = warp_sum(j < hd ? x * x : 0.0f);
     if (lane == 0 && wid < nw) red[wid] = ss;
-    unit_sync(bar);
+    unit_sync(bar, nthr);
     float t = 0.0f;
     for (int i = 0; i < nw; i++) t += red[i];
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), eps)));
     if (j < hd) rk[j] = __fmul_rn(__fmul_rn(x, inv), tb_h2f(w16[j]));
-    unit_sync(bar);
+    unit_sync(bar, nthr);
     float y = 0.0f;
     if (j < hd) {
         const int half = hd >> 1;
@@ -69,7 +69,31 @@ __device__ __forceinline__ float norm_rope(float x, const uint16_t* w16, int hd,
         const float rot = j < half ? -partner : partner;
         y = fmaf(rk[j], c, rot * s);
     }
-    unit_sync(bar);    // rk and red may be reused
+    unit_sync(bar, nthr);    // rk and red may be reused
+    return y;
+}
+
+// norm_rope of several heads at once, the same arithmetic per head: thread t
+// holds element t % hd of head slot t / hd (nthr threads, nthr % hd == 0, hd %
+// 32 == 0); each head's warp sums are added in warp order as above.  rk: nthr
+// floats, red: nthr / 32.
+__device__ __forceinline__ float norm_rope_heads(float x, const uint16_t* w16, int hd, float eps, float c, float s,
+                                                 float* rk, float* red, int t, int bar, int nthr)
+{
+    const int lane = t & 31, nw = hd >> 5, slot = t / hd, j = t - slot * hd;
+    const float ss = warp_sum(x * x);
+    if (lane == 0) red[t >> 5] = ss;
+    unit_sync(bar, nthr);
+    float tot = 0.0f;
+    for (int i = 0; i < nw; i++) tot += red[slot * nw + i];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)hd), eps)));
+    rk[t] = __fmul_rn(__fmul_rn(x, inv), tb_h2f(w16[j]));
+    unit_sync(bar, nthr);
+    const int half = hd >> 1;
+    const float partner = j < half ? rk[t + half] : rk[t - half];
+    const float rot = j < half ? -partner : partner;
+    const float y = fmaf(rk[t], c, rot * s);
+    unit_sync(bar, nthr);
     return y;
 }
 
@@ -122,25 +146,24 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // each, 16-byte chunk i of key j stored at chunk i ^ (j % KV16) so the per-key
 // 16-byte copies and reads are bank-conflict free), then the 32 keys' K and V
 // group scales.
-template <int HD, int GRP, int NST_>
+template <int HD, int GRP, int NST_, int W = ATT_WARPS>
 struct DecLayout {
-    static constexpr int KV16 = HD / 16, NG = HD / 32, NST = NST_;
+    static constexpr int KV16 = HD / 16, NG = HD / 32, NST = NST_, NT = 32 * W;
     // splits the combining unit can weigh (its [GRP][nsplit] weights live in the stages)
     static constexpr int MAXSPLIT = NST == 1 ? 256 : ATT_MAXSPLIT;
     static constexpr int ST_K = 0, ST_V = 32 * HD, ST_KS = 64 * HD, ST_VS = 64 * HD + 32 * NG * 4;
     static constexpr int STAGE = 64 * HD + 64 * NG * 4;
     static constexpr int OFF_QS = 0;                                  // float [GRP][HD]
     static constexpr int OFF_PS = OFF_QS + GRP * HD * 4;              // float [W][32 keys][NG][GRP]
-    static constexpr int OFF_WM = OFF_PS + ATT_WARPS * 32 * NG * GRP * 4;   // float [W][GRP]
-    static constexpr int OFF_WL = OFF_WM + ATT_WARPS * GRP * 4;       // float [W][GRP]
-    static constexpr int OFF_ST = (OFF_WL + ATT_WARPS * GRP * 4 + 127) / 128 * 128;
-    static constexpr int BYTES = OFF_ST + ATT_WARPS * NST * STAGE;
+    static constexpr int OFF_WM = OFF_PS + W * 32 * NG * GRP * 4;   // float [W][GRP]
+    static constexpr int OFF_WL = OFF_WM + W * GRP * 4;       // float [W][GRP]
+    static constexpr int OFF_ST = (OFF_WL + W * GRP * 4 + 127) / 128 * 128;
+    static constexpr int BYTES = OFF_ST + W * NST * STAGE;
     // after the key loop the stages are reused for the warps' outputs, float [W][GRP][HD]
-    static_assert(ATT_WARPS * GRP * HD * 4 <= ATT_WARPS * NST * STAGE, "merge buffer must fit in the stages");
+    static_assert(W * GRP * HD * 4 <= W * NST * STAGE, "merge buffer must fit in the stages");
     static_assert(STAGE % 16 == 0 && ST_KS % 16 == 0 && ST_VS % 16 == 0, "stage alignment");
     // the combining unit keeps its split weights [GRP][nsplit] there too
-    static_assert(GRP * MAXSPLIT * 4 + (GRP * HD / 4 > ATT_THREADS ? GRP * HD / 4 : ATT_THREADS) * 16 <=
-                      ATT_WARPS * NST * STAGE,
+    static_assert(GRP * MAXSPLIT * 4 + (GRP * HD / 4 > NT ? GRP * HD / 4 : NT) * 16 <= W * NST * STAGE,
                   "split weights and column partials must fit in the stages");
 };
 
@@ -168,10 +191,10 @@ struct PrepIn {
     float eps;
 };
 
-template <int HD, int GRP, int NST>
+template <int HD, int GRP, int NST, int W = ATT_WARPS>
 struct DecUnit {
-    using L = DecLayout<HD, GRP, NST>;
-    static constexpr int KV16 = L::KV16, NG = L::NG;
+    using L = DecLayout<HD, GRP, NST, W>;
+    static constexpr int KV16 = L::KV16, NG = L::NG, NT = 32 * W;
     static constexpr int DPL = HD / 32;                // dims per lane in P.V
 
     const AttnArgs& a;
@@ -219,7 +242,7 @@ struct DecUnit {
         c0 = split * per;
         c1 = min(S, c0 + per);
         const int span = c1 - c0;
-        ntile = span > wid * 32 ? (span - wid * 32 + ATT_WARPS * 32 - 1) / (ATT_WARPS * 32) : 0;
+        ntile = span > wid * 32 ? (span - wid * 32 + W * 32 - 1) / (W * 32) : 0;
     }
 
     __device__ uint8_t* stages() const { return smem + L::OFF_ST + wid * NST * L::STAGE; }
@@ -230,7 +253,7 @@ struct DecUnit {
     __device__ void issue(int j, int s, int skip = -1) const
     {
         constexpr int RPI = 32 / KV16;                  // rows per copy instruction
-        const int tb0 = c0 + (wid + ATT_WARPS * j) * 32;
+        const int tb0 = c0 + (wid + W * j) * 32;
         uint8_t* st = stages() + s * L::STAGE;
         const int ch = lane % KV16;
 #pragma unroll
@@ -293,55 +316,55 @@ struct DecUnit {
             // the stages may still be receiving prefetched tiles: work in ps / wm
             float* rk = ps_all;
             float* red = wm;
-            const float c = tid < HD ? prep->cs[tid] : 0.0f, sn = tid < HD ? prep->cs[HD + tid] : 0.0f;
-            for (int h = 0; h < GRP; h++) {
-                const long long o = (long long)zb * a.nHq * HD + (long long)(hk * GRP + h) * HD;
-                const float x = tid < HD ? __ldcg(prep->q + o + tid) : 0.0f;
-                const float y = norm_rope(x, prep->qn, HD, prep->eps, c, sn, rk, red, tid, bar);
-                if (tid < HD) qs[h * HD + tid] = y;
+            const int j = tid % HD, slot = tid / HD;
+            constexpr int SLOTS = NT / HD;             // heads prepared side by side
+            const float c = prep->cs[j], sn = prep->cs[HD + j];
+            for (int h0 = 0; h0 < GRP; h0 += SLOTS) {
+                const int h = h0 + slot;
+                const long long o = (long long)zb * a.nHq * HD + (long long)(hk * GRP + (h < GRP ? h : 0)) * HD;
+                const float x = h < GRP ? __ldcg(prep->q + o + j) : 0.0f;
+                const float y = norm_rope_heads(x, prep->qn, HD, prep->eps, c, sn, rk, red, tid, bar, NT);
+                if (h < GRP) qs[h * HD + j] = y;
             }
             ts(1);
             const int last = S - 1;
             // the warp whose FIRST tile holds row S-1 gets it straight into its stage
-            const int wl = S > 0 ? (last - c0) >> 5 : ATT_WARPS;
-            const bool into_stage = inject && early && S > 0 && c0 <= last && last < c1 && wl < ATT_WARPS;
+            const int wl = S > 0 ? (last - c0) >> 5 : W;
+            const bool into_stage = inject && early && S > 0 && c0 <= last && last < c1 && wl < W;
             if (S > 0 && c0 <= last && last < c1) {
+                // k (norm + RoPE) in head slot 0, v in slot 1 (or after k with one slot)
                 const long long o = (long long)zb * a.nKv * HD + (long long)hk * HD;
                 const long long row = (long long)last * row_elems + (long long)hk * HD;
-                const float kx = tid < HD ? __ldcg(prep->k + o + tid) : 0.0f;
-                const float vx = tid < HD ? __ldcg(prep->v + o + tid) : 0.0f;
-                const float kr = norm_rope(kx, prep->kn, HD, prep->eps, c, sn, rk, red, tid, bar);
-                // quant_row's values, into the cache and (into_stage) the stage of warp wl
-                const float km = fmaxf(1e-12f, warp_max(fabsf(kr))), vm = fmaxf(1e-12f, warp_max(fabsf(vx)));
-                const int8_t kq = snorm8(__fdiv_rn(kr, km)), vq = snorm8(__fdiv_rn(vx, vm));
-                if (tid < HD) {
-                    const_cast<int8_t*>(Kq)[row + tid] = kq;
-                    const_cast<int8_t*>(Vq)[row + tid] = vq;
-                    if (lane == 0) {
-                        const_cast<float*>(Ks)[row / 32 + (tid >> 5)] = km;
-                        const_cast<float*>(Vs)[row / 32 + (tid >> 5)] = vm;
-                    }
-                    if (into_stage) {
-                        uint8_t* st = smem + L::OFF_ST + wl * NST * L::STAGE;
-                        const int kr_ = last - (c0 + wl * 32), ch = tid >> 4;
-                        const int off = (kr_ * KV16 + (ch ^ (kr_ & (KV16 - 1)))) * 16 + (tid & 15);
-                        st[L::ST_K + off] = (uint8_t)kq;
-                        st[L::ST_V + off] = (uint8_t)vq;
-                        if (lane == 0) {
-                            reinterpret_cast<float*>(st + L::ST_KS)[kr_ * NG + (tid >> 5)] = km;
-                            reinterpret_cast<float*>(st + L::ST_VS)[kr_ * NG + (tid >> 5)] = vm;
+                for (int part = 0; part < 2; part += SLOTS) {
+                    const int which = part + slot;       // 0: k, 1: v
+                    const float x = which < 2 ? __ldcg((which ? prep->v : prep->k) + o + j) : 0.0f;
+                    const float kr = norm_rope_heads(x, prep->kn, HD, prep->eps, c, sn, rk, red, tid, bar, NT);
+                    const float val = which == 0 ? kr : x;
+                    // quant_row's values, into the cache and (into_stage) the stage of warp wl
+                    const float m = fmaxf(1e-12f, warp_max(fabsf(val)));
+                    const int8_t q8 = snorm8(__fdiv_rn(val, m));
+                    if (which < 2) {
+                        const_cast<int8_t*>(which ? Vq : Kq)[row + j] = q8;
+                        if (lane == 0) const_cast<float*>(which ? Vs : Ks)[row / 32 + (j >> 5)] = m;
+                        if (into_stage) {
+                            uint8_t* st = smem + L::OFF_ST + wl * NST * L::STAGE;
+                            const int kr_ = last - (c0 + wl * 32), ch = j >> 4;
+                            const int off = (kr_ * KV16 + (ch ^ (kr_ & (KV16 - 1)))) * 16 + (j & 15);
+                            st[(which ? L::ST_V : L::ST_K) + off] = (uint8_t)q8;
+                            if (lane == 0)
+                                reinterpret_cast<float*>(st + (which ? L::ST_VS : L::ST_KS))[kr_ * NG + (j >> 5)] = m;
                         }
                     }
                 }
                 if (!into_stage) __threadfence();    // the row reaches L2 before a warp's cp.async reads it
             }
-            unit_sync(bar);
+            unit_sync(bar, NT);
             ts(2);
             if (early && first_new() && !inject) issue(0, 0);
         } else {
             if (early && first_new()) issue(0, 0);
-            for (int i = tid; i < GRP * HD; i += ATT_THREADS) qs[i] = __ldcg(qrow + (long long)hk * GRP * HD + i);
-            unit_sync(bar);
+            for (int i = tid; i < GRP * HD; i += NT) qs[i] = __ldcg(qrow + (long long)hk * GRP * HD + i);
+            unit_sync(bar, NT);
         }
 
         float m[GRP], l[GRP];
@@ -360,7 +383,7 @@ struct DecUnit {
             cp_async_wait<NST - 1>();
             __syncwarp();
             const uint8_t* st = stg + (j % NST) * L::STAGE;
-            const int t0 = c0 + (wid + ATT_WARPS * j) * 32;
+            const int t0 = c0 + (wid + W * j) * 32;
             const bool valid = t0 + lane < c1;
             const int nk = min(32, c1 - t0);
 
@@ -449,7 +472,7 @@ struct DecUnit {
             }
         }
         cp_async_wait<0>();
-        unit_sync(bar);    // every warp is done with its stages: reuse them for the merge
+        unit_sync(bar, NT);    // every warp is done with its stages: reuse them for the merge
         ts(3);
 
         // ---- merge warps
@@ -462,15 +485,15 @@ struct DecUnit {
             for (int i = 0; i < DPL / 2; i++)
                 *reinterpret_cast<float2*>(wo + (wid * GRP + h) * HD + lane * DPL + 2 * i) = o[h][i];
         }
-        unit_sync(bar);
-        for (int i = tid; i < GRP * HD; i += ATT_THREADS) {
+        unit_sync(bar, NT);
+        for (int i = tid; i < GRP * HD; i += NT) {
             const int h = i / HD, d = i - h * HD;
             float M = NEG_BIG;
 #pragma unroll
-            for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, wm[w * GRP + h]);
+            for (int w = 0; w < W; w++) M = fmaxf(M, wm[w * GRP + h]);
             float Ls = 0.0f, O = 0.0f;
 #pragma unroll
-            for (int w = 0; w < ATT_WARPS; w++) {
+            for (int w = 0; w < W; w++) {
                 const float e = __expf(wm[w * GRP + h] - M);
                 Ls = fmaf(wl[w * GRP + h], e, Ls);
                 O = fmaf(wo[(w * GRP + h) * HD + d], e, O);
@@ -490,17 +513,17 @@ struct DecUnit {
         //      (ATTN_DEC_COMBINE, qwen3.js:2048-2069): out = sum_i e_i O_i / sum_i e_i l_i,
         //      e_i = exp(m_i - max m).  Partials are read through L2 (ld.cg).
         __threadfence();
-        unit_sync(bar);
+        unit_sync(bar, NT);
         int* last = reinterpret_cast<int*>(wm);          // wm/wl are free again after the loop above
         if (tid == 0) *last = atomicAdd(counter, 1u) == (unsigned)(a.nsplit - 1);
-        unit_sync(bar);
+        unit_sync(bar, NT);
         ts(5);
         if (tr && tid == 0) tr[7] = *last;
         if (!*last) return;
         __threadfence();
         float* wts = reinterpret_cast<float*>(smem + L::OFF_ST);    // [GRP][nsplit]
         float* lsum = wl;                                            // [GRP]
-        for (int h = wid; h < GRP; h += ATT_WARPS) {
+        for (int h = wid; h < GRP; h += W) {
             const float* pml = PML + (long long)(hk * GRP + h) * a.nsplit * 2;
             float M = NEG_BIG;
             for (int i = lane; i < a.nsplit; i += 32) M = fmaxf(M, __ldcg(pml + 2 * i));
@@ -514,14 +537,14 @@ struct DecUnit {
             Ls = warp_sum(Ls);
             if (lane == 0) lsum[h] = Ls;
         }
-        unit_sync(bar);
+        unit_sync(bar, NT);
         // float4 columns (head h, dims 4c..4c+3); when there are fewer columns than
         // threads, P threads share a column, each summing every P-th split with 8
         // loads in flight, and the P partials are added in part order.
         constexpr int NCOL = GRP * HD / 4;
-        constexpr int P = NCOL >= ATT_THREADS ? 1 : ATT_THREADS / NCOL;
+        constexpr int P = NCOL >= NT ? 1 : NT / NCOL;
         float4* part = reinterpret_cast<float4*>(wts + GRP * L::MAXSPLIT);     // [P][NCOL]
-        for (int i = tid; i < NCOL * P; i += ATT_THREADS) {
+        for (int i = tid; i < NCOL * P; i += NT) {
             const int col = i % NCOL, pp = i / NCOL;
             const int h = col / (HD / 4), c4 = col - h * (HD / 4);
             const float4* po = reinterpret_cast<const float4*>(PO + (long long)(hk * GRP + h) * a.nsplit * HD) + c4;
@@ -547,8 +570,8 @@ struct DecUnit {
             }
             part[pp * NCOL + col] = acc;
         }
-        unit_sync(bar);
-        for (int col = tid; col < NCOL; col += ATT_THREADS) {
+        unit_sync(bar, NT);
+        for (int col = tid; col < NCOL; col += NT) {
             const int h = col / (HD / 4), c4 = col - h * (HD / 4);
             float4 O = part[col];
             for (int pp = 1; pp < P; pp++) {

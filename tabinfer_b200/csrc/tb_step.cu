@@ -71,7 +71,7 @@ struct StepArgs {
     // written, arrival counted, end, last-split flag)
     unsigned long long* trace;
     // shared-memory layout (bytes)
-    int off_P, off_Q, off_R, off_act, off_misc;
+    int off_P, off_Q, off_R, off_act, off_misc, off_layers;
     int rpC, rpD;            // rows per CTA of o / down (rpC) and gate / up (rpD)
 };
 
@@ -177,7 +177,7 @@ __device__ __forceinline__ BlockA block_a(const StepArgs& a)
 // Thread 0: request a phase's rows into a buffer (after the CTA finished reading it).
 __device__ void request(const StepArgs& a, Ctl* ctl, int buf, int phase, int l, unsigned char* smem, uint64_t* bars)
 {
-    const StepLayer& Ly = a.layers[l];
+    const StepLayer& Ly = reinterpret_cast<const StepLayer*>(smem + a.off_layers)[l];
     uint64_t* bar = bars + buf;
     unsigned char* dst = smem + (buf == BUF_P ? a.off_P : buf == BUF_Q ? a.off_Q : a.off_R);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -380,53 +380,47 @@ __device__ __forceinline__ int unit_rot(const StepArgs& a, int u)
     return N > G ? (u + N - G) % N : u;
 }
 
-// attention units of this CTA: unit u = blockIdx.x + gridDim.x * (NG i + group).
-// UNST = 2: at most one unit per CTA (group 0, two-stage tile pipeline); UNST = 1:
-// two groups, one stage each.
-template <int GRP, int UNST>
-__device__ void attn_prefetch(const StepArgs& a, int l, unsigned char* smem)
+// attention units: one 8-warp unit (the whole CTA) per CTA, unit u of CTA
+// blockIdx.x + gridDim.x * i; one 32-key tile per warp (the plan checks it)
+constexpr int UW = 8;
+
+template <int GRP>
+__device__ void attn_prefetch(const StepArgs& a, const StepLayer& Ly, unsigned char* smem)
 {
-    using U = DecUnit<STEP_HD, GRP, UNST>;
-    constexpr int NGR = UNST == 2 ? 1 : 2;
-    const int grp = threadIdx.x >> 7, gtid = threadIdx.x & 127;
-    if (grp >= NGR) return;
-    const int u = blockIdx.x + gridDim.x * grp;
+    using U = DecUnit<STEP_HD, GRP, 1, UW>;
+    const int u = blockIdx.x;
     if (u >= a.nKv * a.nsplit) return;
-    const AttnArgs t = attn_args(a, a.layers[l]);
+    const AttnArgs t = attn_args(a, Ly);
     const int r = unit_rot(a, u);
-    U unit(t, smem + a.off_P + grp * U::L::BYTES, r % a.nKv, r / a.nKv, 0, gtid, 1 + grp);
+    U unit(t, smem + a.off_P, r % a.nKv, r / a.nKv, 0, threadIdx.x, 0);
     unit.inject = true;
     unit.prefetch(true);
 }
 
-template <int GRP, int UNST>
-__device__ void attn_run(const StepArgs& a, int l, unsigned char* smem, const float* cs)
+template <int GRP>
+__device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned char* smem, const float* cs)
 {
-    using U = DecUnit<STEP_HD, GRP, UNST>;
-    constexpr int NGR = UNST == 2 ? 1 : 2;
-    const int grp = threadIdx.x >> 7, gtid = threadIdx.x & 127;
-    if (grp >= NGR) return;
-    const StepLayer& Ly = a.layers[l];
+    using U = DecUnit<STEP_HD, GRP, 1, UW>;
     const AttnArgs t = attn_args(a, Ly);
     const PrepIn pin{a.q, a.k, a.v, Ly.qn, Ly.kn, cs, a.eps};
     for (int i = 0;; i++) {
-        const int u = blockIdx.x + gridDim.x * (NGR * i + grp);
+        const int u = blockIdx.x + gridDim.x * i;
         if (u >= a.nKv * a.nsplit) break;
         const int r = unit_rot(a, u);
-        U unit(t, smem + a.off_P + grp * U::L::BYTES, r % a.nKv, r / a.nKv, 0, gtid, 1 + grp);
+        U unit(t, smem + a.off_P, r % a.nKv, r / a.nKv, 0, threadIdx.x, 0);
         unit.prep = &pin;
-        if (a.trace && i == 0 && grp == 0)
-            unit.tr = a.trace + (size_t)blockIdx.x * (1 + 33 * a.L) + 1 + 25 * a.L + 8 * l;
+        if (a.trace && i == 0) unit.tr = a.trace + (size_t)blockIdx.x * (1 + 33 * a.L) + 1 + 25 * a.L + 8 * l;
         // the first unit's tiles were requested in an earlier phase (row pos is
         // written into its stage by the prep); a later unit requests them now,
         // the tile holding row pos only after the prep wrote that row
         unit.inject = i == 0;
         if (i > 0) unit.prefetch(true);
         unit.run(true);
+        __syncthreads();
     }
 }
 
-template <int GRP, int UNST>
+template <int GRP>
 __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
 {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -462,12 +456,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
         cs[tid] = c;
         cs[STEP_HD + tid] = s;
     }
+    // the per-layer pointer records, on chip for the whole launch
+    StepLayer* sl = reinterpret_cast<StepLayer*>(smem + a.off_layers);
+    for (int i = tid; i < a.L * (int)(sizeof(StepLayer) / 8); i += THREADS)
+        reinterpret_cast<unsigned long long*>(sl)[i] = reinterpret_cast<const unsigned long long*>(a.layers)[i];
     __syncthreads();
     if (tid == 0) {
         request(a, ctl, BUF_R, 0, 0, smem, bars);
         request(a, ctl, BUF_Q, 4, 0, smem, bars);
     }
-    attn_prefetch<GRP, UNST>(a, 0, smem);
+    attn_prefetch<GRP>(a, sl[0], smem);
     // embed: this CTA's rows of x (the o / down row slice)
     {
         const int r0 = rowsC0(a), n = rowsC(a);
@@ -481,7 +479,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
     if (!grid_sync(a, ctl)) goto drain;
 
     for (int l = 0; l < a.L; l++) {
-        const StepLayer& Ly = a.layers[l];
+        const StepLayer& Ly = sl[l];
         const bool more = l + 1 < a.L;
         // ---- A: rmsnorm + quant of x, q/k/v rows, prep of completed heads
         {
@@ -504,7 +502,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
         // ---- B: attention (prep'd q, cache row pos written in A)
         {
             STAMP(1, 0);
-            attn_run<GRP, UNST>(a, l, smem, cs);
+            attn_run<GRP>(a, Ly, l, smem, cs);
             __syncthreads();
             if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
             STAMP(1, 3);
@@ -538,7 +536,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                 gemv_rows<2>(smem + a.off_act, wP, wP + mat_bytes(n, a.H), n, a.H / 32, a.swi, rowsD0(a), nullptr);
             }
             __syncthreads();
-            if (more) attn_prefetch<GRP, UNST>(a, l + 1, smem);
+            if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
             STAMP(3, 3);
             if (!grid_sync(a, ctl)) goto drain;
             STAMP(3, 4);
@@ -574,7 +572,7 @@ drain:
 // ---- host side ---------------------------------------------------------------------
 struct tb_step_plan {
     StepArgs a;
-    int smem = 0, grid = 0, grp = 0, unst = 1;
+    int smem = 0, grid = 0, grp = 0;
 };
 
 // Layout and feasibility of the persistent step for these sizes on this device;
@@ -599,15 +597,15 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     a.rpD = (I + G - 1) / G;
     if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
     auto mb = [](int n, int K) { return (size_t)n * (K / 2 + K / 16); };
-    // one unit per CTA (two-stage tiles) when the units fit the grid, else two
-    // one-stage units per CTA
-    const int unst = nKv * nsplit <= G ? 2 : 1;
+    // one 8-warp unit per CTA with one 32-key tile per warp at the longest context
+    const int per = (max_seq + nsplit - 1) / nsplit;
+    if (nKv * nsplit > G || per > UW * 32) return TB_ERR_UNSUPPORTED;
     size_t unit_bytes = 0;
     switch (grp) {
-    case 1: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 1, 2>::BYTES : 2 * DecLayout<STEP_HD, 1, 1>::BYTES; break;
-    case 2: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 2, 2>::BYTES : 2 * DecLayout<STEP_HD, 2, 1>::BYTES; break;
-    case 4: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 4, 2>::BYTES : 2 * DecLayout<STEP_HD, 4, 1>::BYTES; break;
-    default: unit_bytes = unst == 2 ? DecLayout<STEP_HD, 8, 2>::BYTES : 2 * DecLayout<STEP_HD, 8, 1>::BYTES; break;
+    case 1: unit_bytes = DecLayout<STEP_HD, 1, 1, UW>::BYTES; break;
+    case 2: unit_bytes = DecLayout<STEP_HD, 2, 1, UW>::BYTES; break;
+    case 4: unit_bytes = DecLayout<STEP_HD, 4, 1, UW>::BYTES; break;
+    default: unit_bytes = DecLayout<STEP_HD, 8, 1, UW>::BYTES; break;
     }
     auto up = [](size_t v) { return (v + 127) & ~size_t(127); };
     const size_t bP = up(std::max(unit_bytes, 2 * mb(a.rpD, H) + (size_t)H * 2));
@@ -621,7 +619,8 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     a.off_R = (int)(bP + bQ);
     a.off_act = (int)(bP + bQ + bR);
     a.off_misc = (int)(bP + bQ + bR + act);
-    const size_t total = (size_t)a.off_misc + misc;
+    a.off_layers = (int)(bP + bQ + bR + act + misc);
+    const size_t total = (size_t)a.off_layers + (size_t)L * sizeof(StepLayer);
     int maxsm = 0;
     cudaDeviceGetAttribute(&maxsm, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device);
     if (total > (size_t)maxsm) return TB_ERR_UNSUPPORTED;
@@ -633,7 +632,6 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     p->smem = (int)total;
     p->grid = G;
     p->grp = grp;
-    p->unst = unst;
     *out = p;
     return TB_OK;
 }
@@ -656,10 +654,10 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.trace = reinterpret_cast<unsigned long long*>(io->trace);
     void (*kern)(const StepArgs) = nullptr;
     switch (p->grp) {
-    case 1: kern = p->unst == 2 ? k_decode_step<1, 2> : k_decode_step<1, 1>; break;
-    case 2: kern = p->unst == 2 ? k_decode_step<2, 2> : k_decode_step<2, 1>; break;
-    case 4: kern = p->unst == 2 ? k_decode_step<4, 2> : k_decode_step<4, 1>; break;
-    default: kern = p->unst == 2 ? k_decode_step<8, 2> : k_decode_step<8, 1>; break;
+    case 1: kern = k_decode_step<1>; break;
+    case 2: kern = k_decode_step<2>; break;
+    case 4: kern = k_decode_step<4>; break;
+    default: kern = k_decode_step<8>; break;
     }
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "decode step attribute: %s", cudaGetErrorString(e));
