@@ -523,6 +523,24 @@ struct DecUnit {
         __threadfence();
         float* wts = reinterpret_cast<float*>(smem + L::OFF_ST);    // [GRP][nsplit]
         float* lsum = wl;                                            // [GRP]
+        // float4 columns (head h, dims 4c..4c+3); when there are fewer columns than
+        // threads, P threads share a column, each summing every P-th split, and the
+        // P partials are added in part order.  With one (column, part) per thread
+        // and at most 8 splits a thread, its partials are requested here, before
+        // the split weights are known (the sums keep their order).
+        constexpr int NCOL = GRP * HD / 4;
+        constexpr int P = NCOL >= NT ? 1 : NT / NCOL;
+        constexpr int PRE = 8;
+        const bool pre = NCOL * P == NT && a.nsplit <= PRE * P;
+        float4 pv[PRE];
+        if (pre) {
+            const int col = tid % NCOL, pp = tid / NCOL;
+            const int h = col / (HD / 4), c4 = col - h * (HD / 4);
+            const float4* po = reinterpret_cast<const float4*>(PO + (long long)(hk * GRP + h) * a.nsplit * HD) + c4;
+#pragma unroll
+            for (int u = 0; u < PRE; u++)
+                if (pp + u * P < a.nsplit) pv[u] = __ldcg(po + (long long)(pp + u * P) * (HD / 4));
+        }
         for (int h = wid; h < GRP; h += W) {
             const float* pml = PML + (long long)(hk * GRP + h) * a.nsplit * 2;
             float M = NEG_BIG;
@@ -538,13 +556,24 @@ struct DecUnit {
             if (lane == 0) lsum[h] = Ls;
         }
         unit_sync(bar, NT);
-        // float4 columns (head h, dims 4c..4c+3); when there are fewer columns than
-        // threads, P threads share a column, each summing every P-th split with 8
-        // loads in flight, and the P partials are added in part order.
-        constexpr int NCOL = GRP * HD / 4;
-        constexpr int P = NCOL >= NT ? 1 : NT / NCOL;
         float4* part = reinterpret_cast<float4*>(wts + GRP * L::MAXSPLIT);     // [P][NCOL]
-        for (int i = tid; i < NCOL * P; i += NT) {
+        if (pre) {
+            const int col = tid % NCOL, pp = tid / NCOL;
+            const int h = col / (HD / 4);
+            const float* w = wts + h * a.nsplit;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int u = 0; u < PRE; u++) {
+                const int k = pp + u * P;
+                if (k < a.nsplit) {
+                    const float e = w[k];
+                    acc.x = fmaf(pv[u].x, e, acc.x); acc.y = fmaf(pv[u].y, e, acc.y);
+                    acc.z = fmaf(pv[u].z, e, acc.z); acc.w = fmaf(pv[u].w, e, acc.w);
+                }
+            }
+            part[pp * NCOL + col] = acc;
+        }
+        for (int i = pre ? NCOL * P : tid; i < NCOL * P; i += NT) {
             const int col = i % NCOL, pp = i / NCOL;
             const int h = col / (HD / 4), c4 = col - h * (HD / 4);
             const float4* po = reinterpret_cast<const float4*>(PO + (long long)(hk * GRP + h) * a.nsplit * HD) + c4;

@@ -20,11 +20,12 @@
 //   C  QUANTQ8 of the attention output, o rows, += residual
 //   D  RMSNorm + QUANTQ8 of x, gate/up rows, SwiGLU
 //   E  QUANTQ8 of swi, down rows, += residual
-// Shared-memory buffers and what they hold, requested as soon as they are free:
-//   R  A(l) -> C(l) -> A(l+1)   (requested at the end of A(l) / C(l))
-//   P  B(l) key/value tiles (cp.async) -> D(l) gate/up (requested at the end of
-//      B(l)) -> B(l+1) tiles (requested at the end of D(l))
-//   Q  E(l) -> E(l+1)           (requested at the end of E(l))
+// Shared-memory buffers and what they hold; each is requested once it is free,
+// right after the next phase's own activation loads (so neither those loads nor
+// the barriers queue behind the bulk copies), at least one phase ahead:
+//   R  A(l) -> C(l) (requested at the start of B(l)) -> A(l+1) (during D(l))
+//   P  B(l) key/value tiles (cp.async, during E(l-1)) -> D(l) gate/up (during C(l))
+//   Q  E(l) (during A(l))
 // Every phase uses the standalone kernels' device code (tb_gemv_dev.cuh,
 // tb_attn_dev.cuh) with the same split count, so the step is bit-identical to
 // the multi-kernel step.  Barrier and copy waits are bounded; a CTA that gives up
@@ -235,11 +236,11 @@ __device__ bool await_buf(const StepArgs& a, Ctl* ctl, int buf, uint64_t* bars)
 // w_s: [n][G] 16-byte weight groups, then [n][G] f16 scales
 // own: this CTA's rows of the residual x kept in shared memory (their only
 // writer is this CTA), so y = own + W.a needs no read of y from memory
-template <int NM>
-__device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
-                          float* y, int row0, float* own)
+template <int NM, int RPW>
+__device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
+                            float* y, int row0, float* own)
 {
-    constexpr int RPW = 4, NW = THREADS / 32;
+    constexpr int NW = THREADS / 32;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     for (int r0 = wid; r0 < n; r0 += NW * RPW) {
         float acc[RPW][NM];
@@ -285,6 +286,19 @@ __device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, con
             }
         }
     }
+}
+
+// rows per warp chosen so the CTA's rows take one pass (a row's sum does not
+// depend on which warp computes it)
+template <int NM>
+__device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
+                          float* y, int row0, float* own)
+{
+    const int rpw = (n + THREADS / 32 - 1) / (THREADS / 32);
+    if (rpw <= 2) gemv_rows_r<NM, 2>(act, w0, w1, n, G, y, row0, own);
+    else if (rpw <= 4) gemv_rows_r<NM, 4>(act, w0, w1, n, G, y, row0, own);
+    else if (rpw <= 6) gemv_rows_r<NM, 6>(act, w0, w1, n, G, y, row0, own);
+    else gemv_rows_r<NM, 8>(act, w0, w1, n, G, y, row0, own);
 }
 
 // QUANTQ8 (optionally RMSNorm first) of a whole f32 row written by other CTAs,
@@ -488,13 +502,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const BlockA b = block_a(a);
             const unsigned char* wR = smem + a.off_R;
             const uint16_t* nws = reinterpret_cast<const uint16_t*>(wR + (b.live ? mat_bytes(RBA, a.H) : 0));
+            if (b.live) stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
+            if (tid == 0 && l > 0) request(a, ctl, BUF_Q, 4, l, smem, bars);   // Q held E(l-1)
             if (b.live) {
-                stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
                 float* y = b.mat == WQ ? a.q : (b.mat == WK ? a.k : a.v);
                 gemv_rows<1>(smem + a.off_act, wR, nullptr, RBA, a.H / 32, y, b.row0, nullptr);
             }
             __syncthreads();
-            if (tid == 0) request(a, ctl, BUF_R, 2, l, smem, bars);
             STAMP(0, 3);
             if (!grid_sync(a, ctl)) goto drain;
             STAMP(0, 4);
@@ -502,9 +516,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
         // ---- B: attention (prep'd q, cache row pos written in A)
         {
             STAMP(1, 0);
+            // (requests are issued after the phase's own critical loads, so the
+            // barrier and the activation loads do not queue behind them)
+            if (tid == 0) request(a, ctl, BUF_R, 2, l, smem, bars);
             attn_run<GRP>(a, Ly, l, smem, cs);
             __syncthreads();
-            if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
             STAMP(1, 3);
             if (!grid_sync(a, ctl)) goto drain;
             STAMP(1, 4);
@@ -514,12 +530,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (!await_buf(a, ctl, BUF_R, bars)) goto drain;
             STAMP(2, 0);
             const int n = rowsC(a);
+            if (n > 0) stage(a, smem, a.attn, a.nHq * STEP_HD, false, nullptr, red, 1 + 25 * l + 5 * 2 + 1);
+            if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
             if (n > 0) {
-                stage(a, smem, a.attn, a.nHq * STEP_HD, false, nullptr, red, 1 + 25 * l + 5 * 2 + 1);
                 gemv_rows<1>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
-            if (tid == 0 && more) request(a, ctl, BUF_R, 0, l + 1, smem, bars);
             STAMP(2, 3);
             if (!grid_sync(a, ctl)) goto drain;
             STAMP(2, 4);
@@ -533,10 +549,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (n > 0) {
                 const uint16_t* nws = reinterpret_cast<const uint16_t*>(wP + 2 * mat_bytes(n, a.H));
                 stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 3 + 1);
+            }
+            if (tid == 0 && more) request(a, ctl, BUF_R, 0, l + 1, smem, bars);
+            if (n > 0) {
                 gemv_rows<2>(smem + a.off_act, wP, wP + mat_bytes(n, a.H), n, a.H / 32, a.swi, rowsD0(a), nullptr);
             }
             __syncthreads();
-            if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
             STAMP(3, 3);
             if (!grid_sync(a, ctl)) goto drain;
             STAMP(3, 4);
@@ -546,12 +564,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (!await_buf(a, ctl, BUF_Q, bars)) goto drain;
             STAMP(4, 0);
             const int n = rowsC(a);
+            if (n > 0) stage(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
+            if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
             if (n > 0) {
-                stage(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
                 gemv_rows<1>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
-            if (tid == 0 && more) request(a, ctl, BUF_Q, 4, l + 1, smem, bars);
             STAMP(4, 3);
             if (more && !grid_sync(a, ctl)) goto drain;
             STAMP(4, 4);
