@@ -788,12 +788,16 @@ def bonsai_extra(dev, peak_gbs, stream, context=4096):
     lm_head, loaded as ternary WebGPU-layout records) through the recorded
     decode step: tok/s at batch 1, context 4096."""
     import torch
-    m = build_model(Q17, dev, 1, context, 16, 1, 0, seed=77, ternary=True)
-    m.set_tokens([1000], [context - 1])
+    steps = 50
+    m = build_model(Q17, dev, 1, context, steps + 16, 1, 0, seed=77, ternary=True)
     for _ in range(5):
+        m.set_tokens([1000], [context - 1])
         m.step()
+    m.set_tokens([1000], [context - 1])        # every timed step inside the cache
     torch.cuda.synchronize(dev)
-    ms = time_steps(m, 50, stream) / 50
+    ms = time_steps(m, steps, stream) / steps
+    err = m.ctx.device_error()
+    assert err == 0, "bonsai decode device error 0x%x" % err
     nb = step_bytes(Q17, 1, 1, context, tern=True)
     kinds = sorted({m.weight_format(n) for n in ("lm_head.weight", "model.layers.0.mlp.down_proj.weight")})
     m.close()
@@ -1224,6 +1228,8 @@ def main():
                 mx.step()
             torch.cuda.synchronize(dev)
             msx = time_steps(mx, 50, stream) / 50
+            errx = mx.ctx.device_error()
+            assert errx == 0, "decode extra device error 0x%x" % errx
             extras["batch%d_context%d" % (Bx, Sx)] = {
                 "tok_per_s": round(Bx * 1e3 / msx, 1), "ms_per_step": round(msx, 4),
                 "step_hbm_gbs": round(step_bytes(Q17, 1, Bx, Sx) / (msx * 1e-3) / 1e9, 1)}

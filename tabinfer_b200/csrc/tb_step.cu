@@ -375,14 +375,17 @@ __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, i
     stamp(sa, slot + 1);
 }
 
-__device__ __forceinline__ AttnArgs attn_args(const StepArgs& a, const StepLayer& Ly)
+// the context S = pos + 1 was read and checked at the kernel's start (0 when pos
+// is outside the cache: every split empty), so the units read no position
+__device__ __forceinline__ AttnArgs attn_args(const StepArgs& a, const StepLayer& Ly, int S)
 {
     AttnArgs t{};
     t.qr = a.qr; t.Kq = Ly.Kq; t.Ks = Ly.Ks; t.Vq = Ly.Vq; t.Vs = Ly.Vs;
-    t.PO = a.PO; t.PML = a.PML; t.out = a.attn; t.counters = a.counters; t.dpos = a.pos; t.err = a.err;
-    t.cache_rows = a.max_seq; t.S = 0; t.nHq = a.nHq; t.nKv = a.nKv; t.nsplit = a.nsplit; t.grid_z = 1;
+    t.PO = a.PO; t.PML = a.PML; t.out = a.attn; t.counters = a.counters; t.dpos = nullptr; t.err = a.err;
+    t.cache_rows = a.max_seq; t.S = S; t.nHq = a.nHq; t.nKv = a.nKv; t.nsplit = a.nsplit; t.grid_z = 1;
     return t;
 }
+__device__ __forceinline__ int step_S(const StepArgs& a, int pos) { return pos >= 0 && pos < a.max_seq ? pos + 1 : 0; }
 
 // Units on CTAs: slot u = blockIdx.x + gridDim.x * (2 i + group).  The (kv head,
 // split) of slot u is rotated so the last splits (they hold row pos: prep of the
@@ -404,7 +407,7 @@ __device__ void attn_prefetch(const StepArgs& a, const StepLayer& Ly, unsigned c
     using U = DecUnit<STEP_HD, GRP, 1, UW>;
     const int u = blockIdx.x;
     if (u >= a.nKv * a.nsplit) return;
-    const AttnArgs t = attn_args(a, Ly);
+    const AttnArgs t = attn_args(a, Ly, step_S(a, a.pos[0]));
     const int r = unit_rot(a, u);
     U unit(t, smem + a.off_P, r % a.nKv, r / a.nKv, 0, threadIdx.x, 0);
     unit.inject = true;
@@ -412,10 +415,10 @@ __device__ void attn_prefetch(const StepArgs& a, const StepLayer& Ly, unsigned c
 }
 
 template <int GRP>
-__device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned char* smem, const float* cs)
+__device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned char* smem, const float* cs, int pos)
 {
     using U = DecUnit<STEP_HD, GRP, 1, UW>;
-    const AttnArgs t = attn_args(a, Ly);
+    const AttnArgs t = attn_args(a, Ly, step_S(a, pos));
     const PrepIn pin{a.q, a.k, a.v, Ly.qn, Ly.kn, cs, a.eps};
     for (int i = 0;; i++) {
         const int u = blockIdx.x + gridDim.x * i;
@@ -448,6 +451,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
     float* xo = reinterpret_cast<float*>(misc + 2112);               // this CTA's rows of x [rpC <= 64]
     const int tid = threadIdx.x;
     const int pos = a.pos[0];
+    if (tid == 0 && blockIdx.x == 0 && step_S(a, pos) == 0) atomicExch(a.err, ERR_ATTN_POS);
     stamp(a, 0);
 
     if (tid == 0) {
@@ -519,7 +523,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             // (requests are issued after the phase's own critical loads, so the
             // barrier and the activation loads do not queue behind them)
             if (tid == 0) request(a, ctl, BUF_R, 2, l, smem, bars);
-            attn_run<GRP>(a, Ly, l, smem, cs);
+            attn_run<GRP>(a, Ly, l, smem, cs, pos);
             __syncthreads();
             STAMP(1, 3);
             if (!grid_sync(a, ctl)) goto drain;

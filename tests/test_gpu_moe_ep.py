@@ -5,9 +5,10 @@ bit-identical outputs, since the owner ranks run the same grouped GEMVs per
 
 * P = 1 on one GPU: the whole exchange path (dispatch into the arena, plan,
   GEMVs writing into the return slots, signal, combine) with all 32 experts.
-* P = 2 on two GPUs (skipped on one): config-5 shapes, each rank routing its
-  own tokens, one rank's routing skewed onto the other rank's experts, several
-  forwards with different token counts (epochs), no device errors."""
+* P = every visible GPU up to 8 (skipped on one; 8 GPUs is config 5's 4 experts
+  per GPU): each rank routing its own tokens, rank 1's routing skewed onto rank
+  0's experts, several forwards with different token counts (epochs), no device
+  errors."""
 import os
 
 import numpy as np
@@ -61,7 +62,9 @@ def _single(ws, logits, a, x0):
     return host(x)
 
 
-RUNS = {0: [64, 1, 37], 1: [50, 8, 64]}     # tokens per forward, per rank
+def _runs(rank):
+    """tokens per forward of a rank"""
+    return [[64, 1, 37], [50, 8, 64]][rank] if rank < 2 else [1 + 9 * rank, 64, 3 + rank]
 
 
 def _ep_run(rank, P, ws, exchange=None):
@@ -74,7 +77,7 @@ def _ep_run(rank, P, ws, exchange=None):
         ep.connect(mine.get(timeout=120))
     ep.set_experts(*_local(ws, P, rank))
     outs = []
-    for it, T in enumerate(RUNS[rank]):
+    for it, T in enumerate(_runs(rank)):
         logits, a, x0 = _tokens(rank, it, T, dev)
         idx, wt = tb.moe_router(logits, torch.zeros(NE, device=dev), K)
         x = x0.clone()
@@ -89,7 +92,7 @@ def test_ep1_matches_single_device(cuda):
     ws = _experts(torch.device("cuda", 0))
     outs, err = _ep_run(0, 1, ws)
     assert err == 0
-    for it, T in enumerate(RUNS[0]):
+    for it, T in enumerate(_runs(0)):
         ref = _single(ws, *_tokens(0, it, T, torch.device("cuda", 0)))
         np.testing.assert_array_equal(outs[it], ref)
 
@@ -104,26 +107,28 @@ def _rank(rank, P, q, exchange):
         q.put((rank, repr(e)))
 
 
-def test_ep2_matches_single_device(cuda):
-    if torch.cuda.device_count() < 2:
+def test_ep_matches_single_device(cuda):
+    n = min(8, torch.cuda.device_count())
+    P = 1 << (n.bit_length() - 1) if n > 0 else 0      # 32 experts split evenly: 2, 4 or 8 ranks
+    if P < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q, hq = ctx.Queue(), ctx.Queue()
-    mine = [ctx.Queue() for _ in range(2)]
-    procs = [ctx.Process(target=_rank, args=(r, 2, q, (hq, mine[r]))) for r in range(2)]
+    mine = [ctx.Queue() for _ in range(P)]
+    procs = [ctx.Process(target=_rank, args=(r, P, q, (hq, mine[r]))) for r in range(P)]
     for p in procs:
         p.start()
-    hs = dict(hq.get(timeout=300) for _ in range(2))
+    hs = dict(hq.get(timeout=300) for _ in range(P))
     for m in mine:
-        m.put([hs[0], hs[1]])
-    res = dict(q.get(timeout=300) for _ in range(2))
+        m.put([hs[r] for r in range(P)])
+    res = dict(q.get(timeout=300) for _ in range(P))
     for p in procs:
         p.join(timeout=60)
-    for r in range(2):
+    for r in range(P):
         assert not isinstance(res[r], str), res[r]
         assert res[r][1] == 0, "rank %d device error %#x" % (r, res[r][1])
     ws = _experts(torch.device("cuda", 0))
-    for r in range(2):
-        for it, T in enumerate(RUNS[r]):
+    for r in range(P):
+        for it, T in enumerate(_runs(r)):
             ref = _single(ws, *_tokens(r, it, T, torch.device("cuda", 0)))
             np.testing.assert_array_equal(res[r][0][it], ref, err_msg="rank %d forward %d" % (r, it))
