@@ -23,7 +23,7 @@ constexpr int MOE_THREADS = 256;
 template <int KIND> constexpr int moe_rpw() { return KIND == 0 ? 1 : 2; }
 template <int KIND> constexpr int moe_rb() { return moe_rpw<KIND>() * MOE_THREADS / 32; }
 constexpr int MOE_GPL = 2;     // 32-groups per lane and row (K <= 2048)
-constexpr int MOE_BPC = 4;     // row blocks per CTA (weights of the next one in flight)
+constexpr int MOE_BPC = 4;     // row blocks per CTA (weights of the next one in flight) with many pairs
 constexpr int XS_PAD = 36;     // floats per staged 32-group (4 of padding: conflict-free 16-byte reads)
 
 // ---- _requant43 -------------------------------------------------------------
@@ -176,6 +176,7 @@ struct MoeArgs {
     const int* offsets;
     int N, Kc, G;
     const int* xrow = nullptr;   // when set, pair p reads activation row xrow[p]
+    int bpc = MOE_BPC;           // row blocks per CTA
     // when set (expert parallel), pair p's output row goes to another rank's
     // memory: c = ydst[p], row (c & 0xffffff) of ypeer[c >> 24]
     const uint32_t* ydst = nullptr;
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
         float s[RPW][MOE_GPL][NM];
     };
     auto fetch = [&](int blk, W& d) {
-        const int rw0 = (blockIdx.x * MOE_BPC + blk) * moe_rb<KIND>() + wid * RPW;
+        const int rw0 = (blockIdx.x * a.bpc + blk) * moe_rb<KIND>() + wid * RPW;
 #pragma unroll
         for (int j = 0; j < RPW; j++)
 #pragma unroll
@@ -246,9 +247,9 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
                 xs[(b * G + (k >> 5)) * XS_PAD + (k & 31)] = src[k];
         }
         __syncthreads();
-        for (int blk = 0; blk < MOE_BPC; blk++) {
-            if (blk + 1 < MOE_BPC) fetch(blk + 1, nxt);
-            const int rw0 = (blockIdx.x * MOE_BPC + blk) * moe_rb<KIND>() + wid * RPW;
+        for (int blk = 0; blk < a.bpc; blk++) {
+            if (blk + 1 < a.bpc) fetch(blk + 1, nxt);
+            const int rw0 = (blockIdx.x * a.bpc + blk) * moe_rb<KIND>() + wid * RPW;
             float acc[NM][RPW][MB];
 #pragma unroll
             for (int m = 0; m < NM; m++)
@@ -343,7 +344,7 @@ int launch_moe(tb_ctx* ctx, const MoeArgs& a, int nE)
     TB_REQUIRE(ctx, smem <= 200 * 1024, "moe: K = %d too large for the staged activations", a.Kc);
     cudaError_t e = cudaFuncSetAttribute(k_moe_gemv3<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
-        e = tb_launch(ctx, k_moe_gemv3<KIND>, dim3((unsigned)tb_cdiv(a.N, moe_rb<KIND>() * MOE_BPC), (unsigned)nE),
+        e = tb_launch(ctx, k_moe_gemv3<KIND>, dim3((unsigned)tb_cdiv(a.N, moe_rb<KIND>() * a.bpc), (unsigned)nE),
                       dim3(MOE_THREADS),
                       smem, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe gemv launch: %s", cudaGetErrorString(e));
@@ -406,9 +407,13 @@ TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const u
                               ctx->dev_error);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe group launch: %s", cudaGetErrorString(e));
     MoeArgs g{x_in, H, (int)K, {w1p, w3p}, {w1s, w3s}, swi, order, offsets, (int)I, (int)H, (int)(H / 32)};
+    // fewer pairs than experts (decode): each routed expert's rows spread over
+    // more CTAs, one row block each, for more weight bytes in flight
+    g.bpc = P < nE ? 1 : MOE_BPC;
     int rc = launch_moe<MOE_GATEUP>(ctx, g, (int)nE);
     if (rc) return rc;
     MoeArgs d{swi, I, 1, {w2p, w2p}, {w2s, w2s}, o, order, offsets, (int)H, (int)I, (int)(I / 32)};
+    d.bpc = g.bpc;
     rc = launch_moe<MOE_DOWN>(ctx, d, (int)nE);
     if (rc) return rc;
     const long long total = T * H;
@@ -864,10 +869,12 @@ TB_API int tb_moe_ep_forward(tb_moe_ep* m, float* x_out, const float* x_in, cons
     MoeArgs g{reinterpret_cast<const float*>(m->arena + m->L.rows), H, 1, {m->wp[0], m->wp[1]}, {m->ws[0], m->ws[1]},
               m->swi, nullptr, m->offsets, I, H, H / 32};
     g.xrow = m->xrow;
+    g.bpc = T * m->K < m->nE ? 1 : MOE_BPC;
     int rc = launch_moe<MOE_GATEUP>(ctx, g, (int)m->El);
     if (rc) return rc;
     MoeArgs dn{m->swi, I, 1, {m->wp[2], m->wp[2]}, {m->ws[2], m->ws[2]}, nullptr, nullptr, m->offsets, H, I, I / 32};
     dn.ydst = m->ydst;
+    dn.bpc = g.bpc;
     for (int s = 0; s < P; s++) dn.ypeer[s] = reinterpret_cast<float*>(m->peer[s] + m->L.ret);
     rc = launch_moe<MOE_DOWN>(ctx, dn, (int)m->El);
     if (rc) return rc;
