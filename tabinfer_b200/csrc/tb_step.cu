@@ -236,21 +236,16 @@ __device__ bool await_buf(const StepArgs& a, Ctl* ctl, int buf, uint64_t* bars)
 // w_s: [n][G] 16-byte weight groups, then [n][G] f16 scales
 // own: this CTA's rows of the residual x kept in shared memory (their only
 // writer is this CTA), so y = own + W.a needs no read of y from memory
-// Rows per warp rpw <= RMAX chosen at run time so the CTA's rows take one pass
-// (a row's sum does not depend on which warp computes it); one copy of the
-// loop per NM keeps the kernel's code small.
-constexpr int RMAX = 8;
-template <int NM>
-__device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
-                          float* y, int row0, float* own)
+template <int NM, int RPW>
+__device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
+                            float* y, int row0, float* own)
 {
     constexpr int NW = THREADS / 32;
-    const int rpw = min(RMAX, (n + NW - 1) / NW);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int r0 = wid; r0 < n; r0 += NW * rpw) {
-        float acc[RMAX][NM];
+    for (int r0 = wid; r0 < n; r0 += NW * RPW) {
+        float acc[RPW][NM];
 #pragma unroll
-        for (int q = 0; q < RMAX; q++)
+        for (int q = 0; q < RPW; q++)
 #pragma unroll
             for (int s = 0; s < NM; s++) acc[q][s] = 0.0f;
 #pragma unroll
@@ -262,22 +257,21 @@ __device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, con
                 XQ<1> xg;
                 load_xq<1>(xg, act, G, g);
 #pragma unroll
-                for (int q = 0; q < RMAX; q++) {
+                for (int q = 0; q < RPW; q++) {
                     const int r = r0 + q * NW;
-                    if (q < rpw && r < n) item_q8x<1>(wq[r * G + g], tb_h2f(sbase[r * G + g]), xg, &acc[q][s]);
+                    if (r < n) item_q8x<1>(wq[r * G + g], tb_h2f(sbase[r * G + g]), xg, &acc[q][s]);
                 }
             }
         }
 #pragma unroll
-        for (int q = 0; q < RMAX; q++)
+        for (int q = 0; q < RPW; q++)
 #pragma unroll
-            for (int s = 0; s < NM; s++)
-                if (q < rpw) acc[q][s] = warp_sum(acc[q][s]);
+            for (int s = 0; s < NM; s++) acc[q][s] = warp_sum(acc[q][s]);
         if (lane == 0) {
 #pragma unroll
-            for (int q = 0; q < RMAX; q++) {
+            for (int q = 0; q < RPW; q++) {
                 const int r = r0 + q * NW;
-                if (q >= rpw || r >= n) continue;
+                if (r >= n) continue;
                 float* yp = y + row0 + r;
                 if (NM == 2) {
                     const float g = acc[q][0], u = acc[q][NM - 1];
@@ -294,6 +288,18 @@ __device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, con
     }
 }
 
+// rows per warp chosen so the CTA's rows take one pass (a row's sum does not
+// depend on which warp computes it)
+template <int NM>
+__device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
+                          float* y, int row0, float* own)
+{
+    const int rpw = (n + THREADS / 32 - 1) / (THREADS / 32);
+    if (rpw <= 2) gemv_rows_r<NM, 2>(act, w0, w1, n, G, y, row0, own);
+    else if (rpw <= 4) gemv_rows_r<NM, 4>(act, w0, w1, n, G, y, row0, own);
+    else if (rpw <= 6) gemv_rows_r<NM, 6>(act, w0, w1, n, G, y, row0, own);
+    else gemv_rows_r<NM, 8>(act, w0, w1, n, G, y, row0, own);
+}
 
 // QUANTQ8 (optionally RMSNorm first) of a whole f32 row written by other CTAs,
 // into the permuted int8 layout of stage_q8<1, false> with the same bits: thread
