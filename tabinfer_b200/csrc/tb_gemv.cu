@@ -289,7 +289,10 @@ int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count,
         const int fixed = SMEM_HDR + p.act_bytes + p.xbuf_bytes + p.nw_bytes;
         while (nst > 1 && fixed + nst * per_stage > budget) nst--;
         p.smem = fixed + nst * per_stage;
-        if (p.smem <= 200 * 1024 || RB == 8) {
+        // a CTA that streams several row blocks keeps at least two stages, so a
+        // copy is in flight while it computes (smaller blocks rather than one stage)
+        const bool deep_enough = nst >= 2 || blocks_per_cta < 2;
+        if ((p.smem <= 200 * 1024 && deep_enough) || RB == 8) {
             p.RB = RB;
             p.nst = nst;
             p.nrb = nrb;
