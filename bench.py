@@ -762,6 +762,32 @@ def profile_step(layers):
     print("profile step done", flush=True)
 
 
+def profile_moe(T):
+    """Three int3 MoE layers (config 5 shapes: router, grouping, grouped gate/up
+    and down GEMVs, combine) over T tokens, for an ncu launch list."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    H, I, NE, K = 2048, 1792, 32, 4
+    ws = []
+    for j, (rows, cols) in enumerate(((NE * I, H), (NE * I, H), (NE * H, I))):
+        g = torch.Generator(device=dev).manual_seed(11 + j)
+        w = (torch.randn(rows, cols, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        pk, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+        del w
+        ws.append(tb.requant_int3(pk, sc))
+    g = torch.Generator(device=dev).manual_seed(5)
+    logits = torch.randn(T, NE, device=dev, generator=g)
+    bias = torch.zeros(NE, device=dev)
+    a = torch.randn(T, H, device=dev, generator=g)
+    x = torch.zeros(T, H, device=dev)
+    for _ in range(3):
+        idx, wt = tb.moe_router(logits, bias, K)
+        tb.moe_ffn_int3(x, a, idx, wt, ws[0], ws[1], ws[2], NE, H, I)
+    torch.cuda.synchronize()
+    print("profile moe done", flush=True)
+
+
 def profile_gemm(M, N, K):
     """Three cold-L2 launches of the tcgen05 prefill GEMM (bf16 activations) at
     M x N x K (config 4: M in {512, 2048, 8192}), for an ncu capture of one."""
@@ -1041,11 +1067,16 @@ def main():
                     help="decode step as one persistent kernel (auto: where it applies) or one kernel per op")
     ap.add_argument("--profile-step", type=int, default=0, metavar="LAYERS",
                     help="persistent decode step of a LAYERS-layer 1.7B-width model, launched alone (for ncu)")
+    ap.add_argument("--profile-moe", type=int, default=0, metavar="T",
+                    help="three int3 MoE layers over T tokens (for an ncu launch list), then exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
     args = ap.parse_args()
     if args.profile_decode:
         profile_decode(args.profile_decode)
+        return
+    if args.profile_moe:
+        profile_moe(args.profile_moe)
         return
     if args.profile_step:
         profile_step(args.profile_step)

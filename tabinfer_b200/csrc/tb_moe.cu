@@ -134,9 +134,12 @@ __global__ void __launch_bounds__(64) k_moe_router(const float* __restrict__ log
 }
 
 // ---- grouping: the pairs (t, k) = t*K + k sorted by expert, stable ------------
-// one CTA: offsets[e] = first position of expert e in `order`, offsets[nE] = P
+// one CTA: offsets[e] = first position of expert e in `order`, offsets[nE] = P;
+// active[0 .. *nactive) = the experts with pairs, in order (the GEMVs launch
+// one expert slot per pair at most and read their expert from this list)
 __global__ void __launch_bounds__(256) k_moe_group(const uint32_t* __restrict__ idx, int P, int nE,
-                                                   int* __restrict__ order, int* __restrict__ offsets, int* err)
+                                                   int* __restrict__ order, int* __restrict__ offsets,
+                                                   int* __restrict__ active, int* __restrict__ nactive, int* err)
 {
     __shared__ int cnt[257];
     tb_pdl_wait();
@@ -150,7 +153,12 @@ __global__ void __launch_bounds__(256) k_moe_group(const uint32_t* __restrict__ 
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int e = 0; e < nE; e++) cnt[e + 1] += cnt[e];
+        int na = 0;
+        for (int e = 0; e < nE; e++) {
+            if (cnt[e + 1] > 0) active[na++] = e;
+            cnt[e + 1] += cnt[e];
+        }
+        *nactive = na;
         for (int e = 0; e <= nE; e++) offsets[e] = cnt[e];
         // stable placement in pair order
         for (int p = 0; p < P; p++) {
@@ -177,6 +185,11 @@ struct MoeArgs {
     int N, Kc, G;
     const int* xrow = nullptr;   // when set, pair p reads activation row xrow[p]
     int bpc = MOE_BPC;           // row blocks per CTA
+    int mb = MB;                 // pairs per chunk (<= MB): the staged activations' rows
+    // when set, expert slot blockIdx.y runs expert active[blockIdx.y] (slots past
+    // *nactive return); else slot = expert
+    const int* active = nullptr;
+    const int* nactive = nullptr;
     // when set (expert parallel), pair p's output row goes to another rank's
     // memory: c = ydst[p], row (c & 0xffffff) of ypeer[c >> 24]
     const uint32_t* ydst = nullptr;
@@ -207,7 +220,11 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
     extern __shared__ __align__(16) float xs[];   // [MB][G][XS_PAD]: xs[b][g][i] = x_b[32 g + i]
     tb_pdl_wait();
     tb_pdl_trigger();
-    const int e = blockIdx.y;
+    int e = blockIdx.y;
+    if (a.active) {
+        if ((int)blockIdx.y >= *a.nactive) return;
+        e = a.active[blockIdx.y];
+    }
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int G = a.G;
     const int p0 = a.offsets[e], np = a.offsets[e + 1] - p0;
@@ -235,8 +252,8 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
                     d.s[j][t][m] = ok ? tb_h2f(__ldg(a.s3[m] + row * G + (ok ? g : 0))) : 0.0f;
                 }
     };
-    for (int c0 = 0; c0 < np; c0 += MB) {
-        const int nb = min(MB, np - c0);
+    for (int c0 = 0; c0 < np; c0 += a.mb) {
+        const int nb = min(a.mb, np - c0);
         W cur, nxt;
         fetch(0, cur);                       // in flight while the activations are staged
         __syncthreads();                     // the previous chunk's reads are done
@@ -334,17 +351,18 @@ __global__ void __launch_bounds__(256) k_moe_combine(float* __restrict__ x, cons
     }
 }
 
-size_t moe_smem(int Kc) { return (size_t)MB * (Kc / 32) * XS_PAD * sizeof(float); }
+size_t moe_smem(int Kc, int mb) { return (size_t)mb * (Kc / 32) * XS_PAD * sizeof(float); }
 
+// nslots: expert slots of the grid (nE, or at most the pair count with a.active)
 template <int KIND>
-int launch_moe(tb_ctx* ctx, const MoeArgs& a, int nE)
+int launch_moe(tb_ctx* ctx, const MoeArgs& a, int nslots)
 {
-    const size_t smem = moe_smem(a.Kc);
+    const size_t smem = moe_smem(a.Kc, a.mb);
     TB_REQUIRE(ctx, a.G <= 32 * MOE_GPL, "moe: K = %d above %d", a.Kc, 32 * 32 * MOE_GPL);
     TB_REQUIRE(ctx, smem <= 200 * 1024, "moe: K = %d too large for the staged activations", a.Kc);
     cudaError_t e = cudaFuncSetAttribute(k_moe_gemv3<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess)
-        e = tb_launch(ctx, k_moe_gemv3<KIND>, dim3((unsigned)tb_cdiv(a.N, moe_rb<KIND>() * a.bpc), (unsigned)nE),
+        e = tb_launch(ctx, k_moe_gemv3<KIND>, dim3((unsigned)tb_cdiv(a.N, moe_rb<KIND>() * a.bpc), (unsigned)nslots),
                       dim3(MOE_THREADS),
                       smem, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe gemv launch: %s", cudaGetErrorString(e));
@@ -396,25 +414,37 @@ TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const u
     const int64_t P = T * K;
     TB_REQUIRE(ctx, P <= (1 << 20), "too many (token, expert) pairs");
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
-    const size_t b_order = up(P * 4), b_off = up((nE + 1) * 4), b_swi = up(P * I * 4), b_o = up(P * H * 4);
-    char* scr = static_cast<char*>(tb_ctx_scratch(ctx, b_order + b_off + b_swi + b_o));
+    const size_t b_order = up(P * 4), b_off = up((nE + 1) * 4), b_act = up((nE + 1) * 4), b_swi = up(P * I * 4),
+                 b_o = up(P * H * 4);
+    char* scr = static_cast<char*>(tb_ctx_scratch(ctx, b_order + b_off + b_act + b_swi + b_o));
     if (!scr) return TB_ERR_NOMEM;
     int* order = reinterpret_cast<int*>(scr);
     int* offsets = reinterpret_cast<int*>(scr + b_order);
-    float* swi = reinterpret_cast<float*>(scr + b_order + b_off);
-    float* o = reinterpret_cast<float*>(scr + b_order + b_off + b_swi);
-    cudaError_t e = tb_launch(ctx, k_moe_group, dim3(1), dim3(256), 0, idx, (int)P, (int)nE, order, offsets,
-                              ctx->dev_error);
+    int* active = reinterpret_cast<int*>(scr + b_order + b_off);     // [nE] then the count
+    float* swi = reinterpret_cast<float*>(scr + b_order + b_off + b_act);
+    float* o = reinterpret_cast<float*>(scr + b_order + b_off + b_act + b_swi);
+    cudaError_t e = tb_launch(ctx, k_moe_group, dim3(1), dim3(256), 0, idx, (int)P, (int)nE, order, offsets, active,
+                              active + nE, ctx->dev_error);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe group launch: %s", cudaGetErrorString(e));
     MoeArgs g{x_in, H, (int)K, {w1p, w3p}, {w1s, w3s}, swi, order, offsets, (int)I, (int)H, (int)(H / 32)};
     // fewer pairs than experts (decode): each routed expert's rows spread over
     // more CTAs, one row block each, for more weight bytes in flight
     g.bpc = P < nE ? 1 : MOE_BPC;
-    int rc = launch_moe<MOE_GATEUP>(ctx, g, (int)nE);
+    // only the routed experts get CTAs (at most one slot per pair), and an expert
+    // has at most T pairs (a token's top-k experts are distinct), which sizes the
+    // staged activations
+    g.active = active;
+    g.nactive = active + nE;
+    g.mb = (int)std::min<int64_t>(MB, T);
+    const int nslots = (int)std::min<int64_t>(nE, P);
+    int rc = launch_moe<MOE_GATEUP>(ctx, g, nslots);
     if (rc) return rc;
     MoeArgs d{swi, I, 1, {w2p, w2p}, {w2s, w2s}, o, order, offsets, (int)H, (int)I, (int)(I / 32)};
     d.bpc = g.bpc;
-    rc = launch_moe<MOE_DOWN>(ctx, d, (int)nE);
+    d.active = g.active;
+    d.nactive = g.nactive;
+    d.mb = g.mb;
+    rc = launch_moe<MOE_DOWN>(ctx, d, nslots);
     if (rc) return rc;
     const long long total = T * H;
     const int grid = (int)std::min<long long>((total + 255) / 256, (long long)ctx->num_sms * 8);
