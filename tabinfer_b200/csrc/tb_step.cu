@@ -61,7 +61,6 @@ struct StepArgs {
     const uint16_t* embed;
     float *x, *q, *k, *v, *qr, *attn, *swi, *PO, *PML;
     unsigned* counters;      // [nKv] split arrivals (zero between steps)
-    unsigned* head_ctr;      // [nHq + 2 nKv] phase-A block arrivals (zero between steps)
     unsigned long long* bar_count;   // grid barrier: arrivals since the model was made (monotonic)
     unsigned* abort_word;    // == this launch's tag: a CTA gave up in this launch
     int* err;
@@ -446,8 +445,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
     Ctl* ctl = reinterpret_cast<Ctl*>(misc + 64);
     float* red = reinterpret_cast<float*>(misc + 128);               // >= 72 floats
     float* cs = reinterpret_cast<float*>(misc + 512);                // cos [hd], sin [hd]
-    float* rk = cs + 2 * STEP_HD;                                    // [hd]
-    int* flag = reinterpret_cast<int*>(rk + STEP_HD);
     float* xo = reinterpret_cast<float*>(misc + 2112);               // this CTA's rows of x [rpC <= 64]
     const int tid = threadIdx.x;
     const int pos = a.pos[0];
@@ -635,7 +632,7 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     const size_t bR = up(std::max(mb(RBA, H) + (size_t)H * 2, mb(a.rpC, nHq * hd)));
     const int Kmax = std::max(std::max(H, I), nHq * hd);
     const size_t act = up((size_t)(Kmax / 32) * 40);
-    const size_t misc = 2112 + 64 * 4;     // barriers, control, reduction, rope, prep row, flag, own x rows
+    const size_t misc = 2112 + 64 * 4;     // barriers, control, reduction, rope table, own rows of x
     a.off_P = 0;
     a.off_Q = (int)bP;
     a.off_R = (int)(bP + bQ);
@@ -670,7 +667,7 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.eps = io->eps; a.theta = io->theta;
     a.ids = io->ids; a.pos = io->pos; a.embed = io->embed;
     a.x = io->x; a.q = io->q; a.k = io->k; a.v = io->v; a.qr = io->qr; a.attn = io->attn; a.swi = io->swi;
-    a.PO = io->PO; a.PML = io->PML; a.counters = io->counters; a.head_ctr = io->ctrl;
+    a.PO = io->PO; a.PML = io->PML; a.counters = io->counters;
     a.bar_count = reinterpret_cast<unsigned long long*>(io->ctrl + 64); a.abort_word = io->ctrl + 128;
     a.err = ctx->dev_error;
     a.trace = reinterpret_cast<unsigned long long*>(io->trace);
