@@ -549,12 +549,13 @@ TB_API int tb_qwen3_step_kind(tb_qwen3 *m);
  * Needs a recorded persistent step. */
 TB_API int tb_qwen3_step_layers(tb_qwen3 *m);
 /* Profiling: %globaltimer stamps of the persistent kernel into trace (device,
- * u64 [SM count][1 + 33 * layers]; null turns it off): per CTA the kernel start,
+ * u64 [SM count][1 + 38 * layers]; null turns it off): per CTA the kernel start,
  * then per layer and phase (q/k/v, attention, o, gate/up, down) the moments its
  * weights were ready, its activation row arrived, its activation was staged, it
  * finished, and its grid barrier opened; then per layer 8 stamps of the CTA's
  * first attention unit (start, q prep, k/v prep, tiles done, partial written,
- * arrival counted, end, whether it combined). */
+ * arrival counted, end, whether it combined), then per layer and phase the
+ * moment its request for the next weights was issued. */
 TB_API int tb_qwen3_step_trace(tb_qwen3 *m, void *trace);
 /* Host-only: the block of a full [rows][cols] tensor of `kind` that rank
  * cfg->tp_rank keeps (norm vectors count as one row). */

@@ -343,15 +343,17 @@ __device__ __forceinline__ void item_q8(const uint4 w, const float s, const unsi
     for (int b = 0; b < B; b++) {
         const int i = b * G + g;
         const uint4 xl = xlo[i], xh = xhi[i];
-        int d = -xs8[i];
-        d = __dp4a((int)l0, (int)xl.x, d);
-        d = __dp4a((int)h0, (int)xl.y, d);
-        d = __dp4a((int)l1, (int)xl.z, d);
-        d = __dp4a((int)h1, (int)xl.w, d);
-        d = __dp4a((int)l2, (int)xh.x, d);
-        d = __dp4a((int)h2, (int)xh.y, d);
-        d = __dp4a((int)l3, (int)xh.z, d);
-        d = __dp4a((int)h3, (int)xh.w, d);
+        // four independent chains (the integer sum is the same in any order)
+        int d0 = -xs8[i], d1 = 0, d2 = 0, d3 = 0;
+        d0 = __dp4a((int)l0, (int)xl.x, d0);
+        d1 = __dp4a((int)h0, (int)xl.y, d1);
+        d2 = __dp4a((int)l1, (int)xl.z, d2);
+        d3 = __dp4a((int)h1, (int)xl.w, d3);
+        d0 = __dp4a((int)l2, (int)xh.x, d0);
+        d1 = __dp4a((int)h2, (int)xh.y, d1);
+        d2 = __dp4a((int)l3, (int)xh.z, d2);
+        d3 = __dp4a((int)h3, (int)xh.w, d3);
+        const int d = (d0 + d1) + (d2 + d3);
         acc[b] = fmaf(s * xsf[i], (float)d, acc[b]);
     }
 }
@@ -390,15 +392,17 @@ __device__ __forceinline__ void item_q8x(const uint4 w, const float s, const XQ<
     const uint32_t l3 = w.w & 0x0f0f0f0fu, h3 = (w.w >> 4) & 0x0f0f0f0fu;
 #pragma unroll
     for (int b = 0; b < B; b++) {
-        int d = -x.s8[b];
-        d = __dp4a((int)l0, (int)x.lo[b].x, d);
-        d = __dp4a((int)h0, (int)x.lo[b].y, d);
-        d = __dp4a((int)l1, (int)x.lo[b].z, d);
-        d = __dp4a((int)h1, (int)x.lo[b].w, d);
-        d = __dp4a((int)l2, (int)x.hi[b].x, d);
-        d = __dp4a((int)h2, (int)x.hi[b].y, d);
-        d = __dp4a((int)l3, (int)x.hi[b].z, d);
-        d = __dp4a((int)h3, (int)x.hi[b].w, d);
+        // four independent chains (the integer sum is the same in any order)
+        int d0 = -x.s8[b], d1 = 0, d2 = 0, d3 = 0;
+        d0 = __dp4a((int)l0, (int)x.lo[b].x, d0);
+        d1 = __dp4a((int)h0, (int)x.lo[b].y, d1);
+        d2 = __dp4a((int)l1, (int)x.lo[b].z, d2);
+        d3 = __dp4a((int)h1, (int)x.lo[b].w, d3);
+        d0 = __dp4a((int)l2, (int)x.hi[b].x, d0);
+        d1 = __dp4a((int)h2, (int)x.hi[b].y, d1);
+        d2 = __dp4a((int)l3, (int)x.hi[b].z, d2);
+        d3 = __dp4a((int)h3, (int)x.hi[b].w, d3);
+        const int d = (d0 + d1) + (d2 + d3);
         acc[b] = fmaf(s * x.sf[b], (float)d, acc[b]);
     }
 }
@@ -411,15 +415,17 @@ __device__ __forceinline__ void item_ternx(const uint2 w, const float s, const X
     const uint32_t c0 = w.y & M, c1 = (w.y >> 2) & M, c2 = (w.y >> 4) & M, c3 = (w.y >> 6) & M;
 #pragma unroll
     for (int b = 0; b < B; b++) {
-        int d = -x.s8[b];
-        d = __dp4a((int)a0, (int)x.lo[b].x, d);
-        d = __dp4a((int)a1, (int)x.lo[b].y, d);
-        d = __dp4a((int)a2, (int)x.lo[b].z, d);
-        d = __dp4a((int)a3, (int)x.lo[b].w, d);
-        d = __dp4a((int)c0, (int)x.hi[b].x, d);
-        d = __dp4a((int)c1, (int)x.hi[b].y, d);
-        d = __dp4a((int)c2, (int)x.hi[b].z, d);
-        d = __dp4a((int)c3, (int)x.hi[b].w, d);
+        // four independent chains (the integer sum is the same in any order)
+        int d0 = -x.s8[b], d1 = 0, d2 = 0, d3 = 0;
+        d0 = __dp4a((int)a0, (int)x.lo[b].x, d0);
+        d1 = __dp4a((int)a1, (int)x.lo[b].y, d1);
+        d2 = __dp4a((int)a2, (int)x.lo[b].z, d2);
+        d3 = __dp4a((int)a3, (int)x.lo[b].w, d3);
+        d0 = __dp4a((int)c0, (int)x.hi[b].x, d0);
+        d1 = __dp4a((int)c1, (int)x.hi[b].y, d1);
+        d2 = __dp4a((int)c2, (int)x.hi[b].z, d2);
+        d3 = __dp4a((int)c3, (int)x.hi[b].w, d3);
+        const int d = (d0 + d1) + (d2 + d3);
         acc[b] = fmaf(s * x.sf[b], (float)d, acc[b]);
     }
 }
@@ -440,15 +446,17 @@ __device__ __forceinline__ void item_tern(const uint2 w, const float s, const un
     for (int b = 0; b < B; b++) {
         const int i = b * G + g;
         const uint4 xl = xlo[i], xh = xhi[i];
-        int d = -xsum[i];
-        d = __dp4a((int)a0, (int)xl.x, d);
-        d = __dp4a((int)a1, (int)xl.y, d);
-        d = __dp4a((int)a2, (int)xl.z, d);
-        d = __dp4a((int)a3, (int)xl.w, d);
-        d = __dp4a((int)c0, (int)xh.x, d);
-        d = __dp4a((int)c1, (int)xh.y, d);
-        d = __dp4a((int)c2, (int)xh.z, d);
-        d = __dp4a((int)c3, (int)xh.w, d);
+        // four independent chains (the integer sum is the same in any order)
+        int d0 = -xsum[i], d1 = 0, d2 = 0, d3 = 0;
+        d0 = __dp4a((int)a0, (int)xl.x, d0);
+        d1 = __dp4a((int)a1, (int)xl.y, d1);
+        d2 = __dp4a((int)a2, (int)xl.z, d2);
+        d3 = __dp4a((int)a3, (int)xl.w, d3);
+        d0 = __dp4a((int)c0, (int)xh.x, d0);
+        d1 = __dp4a((int)c1, (int)xh.y, d1);
+        d2 = __dp4a((int)c2, (int)xh.z, d2);
+        d3 = __dp4a((int)c3, (int)xh.w, d3);
+        const int d = (d0 + d1) + (d2 + d3);
         acc[b] = fmaf(s * xsf[i], (float)d, acc[b]);
     }
 }

@@ -87,7 +87,7 @@ struct tb_step_io {
     float *x, *q, *k, *v, *qr, *attn, *swi, *PO, *PML;
     unsigned* counters;            // [nKv] attention split arrivals, zero between steps
     unsigned* ctrl;                // [256] zero-initialised: grid barrier counter (u64 at word 64), abort word (128)
-    void* trace;                   // optional: u64 [grid][1 + 33 * layers] %globaltimer stamps
+    void* trace;                   // optional: u64 [grid][1 + 38 * layers] %globaltimer stamps
 };
 int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I, int nsplit, int max_seq,
                       tb_step_plan** out);

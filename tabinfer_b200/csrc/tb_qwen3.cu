@@ -1011,11 +1011,12 @@ TB_API int tb_qwen3_step_kind(tb_qwen3* m)
     return m ? m->step_kind : 0;
 }
 
-// Phase trace of the persistent kernel: trace (device, u64 [SMs][1 + 33 * layers])
+// Phase trace of the persistent kernel: trace (device, u64 [SMs][1 + 38 * layers])
 // receives %globaltimer stamps from every later launch (null: off).  Per CTA:
 // kernel start, then per layer and phase (qkv, attention, o, gate/up, down):
 // weights ready, activation row loaded, activation staged, phase done, barrier
-// passed; then per layer 8 stamps of the CTA's first attention unit.
+// passed; then per layer 8 stamps of the CTA's first attention unit; then per
+// layer and phase the moment its next-buffer request was issued.
 TB_API int tb_qwen3_step_trace(tb_qwen3* m, void* trace)
 {
     if (!m) return TB_ERR_INVALID;

@@ -64,11 +64,12 @@ struct StepArgs {
     unsigned long long* bar_count;   // grid barrier: arrivals since the model was made (monotonic)
     unsigned* abort_word;    // == this launch's tag: a CTA gave up in this launch
     int* err;
-    // optional phase trace: per CTA 1 + 33 * L %globaltimer stamps (kernel start;
+    // optional phase trace: per CTA 1 + 38 * L %globaltimer stamps (kernel start;
     // per layer and phase: weights ready, activation row loaded, activation
     // staged, phase done, barrier passed; then per layer 8 slots of the CTA's
     // first attention unit: start, q prep, k/v prep, tiles done, partial
-    // written, arrival counted, end, last-split flag)
+    // written, arrival counted, end, last-split flag; then per layer and phase
+    // the moment the phase's next-buffer request was issued)
     unsigned long long* trace;
     // shared-memory layout (bytes)
     int off_P, off_Q, off_R, off_act, off_misc, off_layers;
@@ -80,10 +81,11 @@ __device__ __forceinline__ void stamp(const StepArgs& a, int slot)
     if (a.trace && threadIdx.x == 0) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        a.trace[(size_t)blockIdx.x * (1 + 33 * a.L) + slot] = t;
+        a.trace[(size_t)blockIdx.x * (1 + 38 * a.L) + slot] = t;
     }
 }
 #define STAMP(ph, k) stamp(a, 1 + 25 * l + 5 * (ph) + (k))
+#define STAMP_REQ(ph) stamp(a, 1 + 33 * a.L + 5 * l + (ph))
 
 // ---- grid barrier ---------------------------------------------------------------
 __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v)
@@ -425,7 +427,7 @@ __device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned
         const int r = unit_rot(a, u);
         U unit(t, smem + a.off_P, r % a.nKv, r / a.nKv, 0, threadIdx.x, 0);
         unit.prep = &pin;
-        if (a.trace && i == 0) unit.tr = a.trace + (size_t)blockIdx.x * (1 + 33 * a.L) + 1 + 25 * a.L + 8 * l;
+        if (a.trace && i == 0) unit.tr = a.trace + (size_t)blockIdx.x * (1 + 38 * a.L) + 1 + 25 * a.L + 8 * l;
         // the first unit's tiles were requested in an earlier phase (row pos is
         // written into its stage by the prep); a later unit requests them now,
         // the tile holding row pos only after the prep wrote that row
@@ -505,6 +507,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const uint16_t* nws = reinterpret_cast<const uint16_t*>(wR + (b.live ? mat_bytes(RBA, a.H) : 0));
             if (b.live) stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
             if (tid == 0 && l > 0) request(a, ctl, BUF_Q, 4, l, smem, bars);   // Q held E(l-1)
+            STAMP_REQ(0);
             if (b.live) {
                 float* y = b.mat == WQ ? a.q : (b.mat == WK ? a.k : a.v);
                 gemv_rows<1>(smem + a.off_act, wR, nullptr, RBA, a.H / 32, y, b.row0, nullptr);
@@ -520,6 +523,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             // (requests are issued after the phase's own critical loads, so the
             // barrier and the activation loads do not queue behind them)
             if (tid == 0) request(a, ctl, BUF_R, 2, l, smem, bars);
+            STAMP_REQ(1);
             attn_run<GRP>(a, Ly, l, smem, cs, pos);
             __syncthreads();
             STAMP(1, 3);
@@ -533,6 +537,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const int n = rowsC(a);
             if (n > 0) stage(a, smem, a.attn, a.nHq * STEP_HD, false, nullptr, red, 1 + 25 * l + 5 * 2 + 1);
             if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
+            STAMP_REQ(2);
             if (n > 0) {
                 gemv_rows<1>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x, rowsC0(a), xo);
             }
@@ -552,6 +557,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                 stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 3 + 1);
             }
             if (tid == 0 && more) request(a, ctl, BUF_R, 0, l + 1, smem, bars);
+            STAMP_REQ(3);
             if (n > 0) {
                 gemv_rows<2>(smem + a.off_act, wP, wP + mat_bytes(n, a.H), n, a.H / 32, a.swi, rowsD0(a), nullptr);
             }
@@ -567,6 +573,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const int n = rowsC(a);
             if (n > 0) stage(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
             if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
+            STAMP_REQ(4);
             if (n > 0) {
                 gemv_rows<1>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
             }

@@ -203,7 +203,7 @@ class Qwen3:
 
     def step_trace(self, buf):
         """Phase trace of the persistent kernel into buf (int64 CUDA tensor of
-        SMs x (1 + 33 * layers)), or None to stop."""
+        SMs x (1 + 38 * layers)), or None to stop."""
         self.ctx.check(LIB.tb_qwen3_step_trace(self.h, None if buf is None else _p(buf)), "step_trace")
 
     def step_kind(self):
