@@ -77,6 +77,40 @@ __device__ __forceinline__ Q8Group q8_group(float v)
     return Q8Group{q8_quant(v, q8_inv(scale)), scale};
 }
 
+// QUANTQ8 of one 32-group held by 8 consecutive lanes (lane & 7 = j4 holds
+// elements 4*j4 .. 4*j4+3), stored in the permuted dp4a layout of the GEMV
+// activation (act: xlo uint4 [G], xhi uint4 [G], s8 int [G] = 8*sum(q), sf float
+// [G] = scale): the same bits as stage_q8<1, false>.  Every lane of the warp
+// calls it (shuffles); live: this lane's group is real and is stored.
+__device__ __forceinline__ void q8_store_group4(const float e[4], int g, bool live, unsigned char* act, int G)
+{
+    uint4* xlo = reinterpret_cast<uint4*>(act);
+    uint4* xhi = xlo + G;
+    int* xs8 = reinterpret_cast<int*>(xhi + G);
+    float* xsf = reinterpret_cast<float*>(xs8 + G);
+    float mx = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    const float scale = q8_scale(mx), is = q8_inv(scale);
+    const int q0 = q8_quant(e[0], is), q1 = q8_quant(e[1], is), q2 = q8_quant(e[2], is), q3 = q8_quant(e[3], is);
+    // this lane's k = 4*j4 .. 4*j4+3 of the group: weight word j4/2, half j4&1
+    const uint32_t ev = ((uint32_t)q0 & 0xffu) | (((uint32_t)q2 & 0xffu) << 8);
+    const uint32_t od = ((uint32_t)q1 & 0xffu) | (((uint32_t)q3 & 0xffu) << 8);
+    const uint32_t ev_p = __shfl_xor_sync(0xffffffffu, ev, 1), od_p = __shfl_xor_sync(0xffffffffu, od, 1);
+    int sum = q0 + q1 + q2 + q3;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    const int j4 = threadIdx.x & 7;
+    if (live && !(j4 & 1)) {
+        const int w = j4 >> 1;
+        uint32_t* dst = reinterpret_cast<uint32_t*>((w < 2 ? xlo : xhi) + g) + 2 * (w & 1);
+        *reinterpret_cast<uint2*>(dst) = make_uint2(ev | (ev_p << 16), od | (od_p << 16));
+        if (j4 == 0) { xs8[g] = 8 * sum; xsf[g] = scale; }
+    }
+}
+
 // models/qwen3.js:3357-3374: f16 bits of an f32, mantissa rounded half-up.
 __device__ __forceinline__ uint32_t js_f32_to_f16(float val)
 {

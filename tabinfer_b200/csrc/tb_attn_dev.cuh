@@ -5,7 +5,7 @@
 // the combine of ATTN_DEC_COMBINE (qwen3.js:2048-2069).  One copy of this code
 // means the two paths compute bit-identical attention.
 #pragma once
-#include "tb_common.cuh"
+#include "tb_act.cuh"
 
 namespace {
 
@@ -204,6 +204,11 @@ struct DecUnit {
     // written into the stage by the prep instead of copied (inject)
     const PrepIn* prep = nullptr;
     bool inject = false;
+    // persistent step: the combining unit also stores its heads' outputs QUANTQ8'd
+    // in the GEMV activation layout (qG groups), so the o phase copies instead of
+    // quantizing
+    unsigned char* qout = nullptr;
+    int qG = 0;
     unsigned long long* tr = nullptr;   // optional %globaltimer stamps of the unit's stages (8 slots)
 
     __device__ void ts(int k) const
@@ -506,7 +511,19 @@ struct DecUnit {
                 if (d == 0) { PML[pidx * 2] = M; PML[pidx * 2 + 1] = Ls; }
             }
         }
-        if (a.nsplit == 1) return;
+        if (a.nsplit == 1) {
+            if (qout) {     // the heads' outputs, written above by this unit, QUANTQ8'd
+                unit_sync(bar, NT);
+                constexpr int NC = GRP * HD / 4;
+                for (int col = tid; col < NC; col += NT) {
+                    const int h = col / (HD / 4), c4 = col - h * (HD / 4);
+                    const float4 r = __ldcg(reinterpret_cast<const float4*>(outp + (long long)(hk * GRP + h) * HD) + c4);
+                    const float e4[4] = {r.x, r.y, r.z, r.w};
+                    q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG);
+                }
+            }
+            return;
+        }
         ts(4);
 
         // ---- the last split of this kv head to finish combines all of them
@@ -611,6 +628,10 @@ struct DecUnit {
             const float4 res = Ls > 0.0f ? make_float4(O.x / Ls, O.y / Ls, O.z / Ls, O.w / Ls)
                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             reinterpret_cast<float4*>(outp + (long long)(hk * GRP + h) * HD)[c4] = res;
+            if (qout) {     // 8 consecutive columns = one 32-group, 8 consecutive lanes
+                const float e4[4] = {res.x, res.y, res.z, res.w};
+                q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG);
+            }
         }
         if (tid == 0) *counter = 0u;     // ready for the next call
         ts(6);

@@ -85,6 +85,7 @@ struct tb_step_io {
     const int32_t* pos;
     const uint16_t* embed;
     float *x, *q, *k, *v, *qr, *attn, *swi, *PO, *PML;
+    unsigned char* attnq;          // nHq*hd/32 * 40 bytes: the attention output in the GEMV activation layout
     unsigned* counters;            // [nKv] attention split arrivals, zero between steps
     unsigned* ctrl;                // [256] zero-initialised: grid barrier counter (u64 at word 64), abort word (128)
     void* trace;                   // optional: u64 [grid][1 + 38 * layers] %globaltimer stamps

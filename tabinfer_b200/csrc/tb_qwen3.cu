@@ -131,6 +131,7 @@ struct tb_qwen3 {
     tb_step_plan* step = nullptr;
     unsigned char* step_layers = nullptr;        // device per-layer records
     unsigned* step_ctrl = nullptr;               // [256] block arrivals, grid barrier, abort word
+    unsigned char* step_attnq = nullptr;         // quantized attention output of the persistent step
     bool step_direct = false;                    // persistent step launched per call (not capturable)
     void* step_trace = nullptr;                  // optional phase trace of the persistent kernel
 };
@@ -289,7 +290,9 @@ bool persistent_ok(tb_qwen3* m)
             tb_step_layer_fill(host.data() + rec * l, packs, scs, Ly.ln1, Ly.ln2, Ly.qn, Ly.kn, Ly.Kq, Ly.Ks, Ly.Vq,
                                Ly.Vs);
         }
-        if (alloc(m, &m->step_layers, host.size()) || alloc(m, &m->step_ctrl, 256)) return false;
+        if (alloc(m, &m->step_layers, host.size()) || alloc(m, &m->step_ctrl, 256) ||
+            alloc(m, &m->step_attnq, (size_t)m->nHq * m->c.head_dim / 32 * 40))
+            return false;
         if (cudaMemcpy(m->step_layers, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemset(m->step_ctrl, 0, 256 * 4) != cudaSuccess) {
             cudaGetLastError();
@@ -313,6 +316,7 @@ tb_step_io step_io(tb_qwen3* m)
     io.x = m->x[0]; io.q = m->q; io.k = m->k; io.v = m->v; io.qr = m->qr; io.attn = m->attn; io.swi = m->swi;
     io.PO = m->PO; io.PML = m->PML; io.counters = m->counters; io.ctrl = m->step_ctrl;
     io.trace = m->step_trace;
+    io.attnq = m->step_attnq;
     return io;
 }
 

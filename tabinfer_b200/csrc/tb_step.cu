@@ -17,7 +17,7 @@
 //      its own q heads (norm + RoPE) and the unit holding row pos writes that
 //      cache row (k: norm + RoPE + int8, v: int8); the last split of a kv head
 //      combines
-//   C  QUANTQ8 of the attention output, o rows, += residual
+//   C  the attention output (QUANTQ8'd by the combining units), o rows, += residual
 //   D  RMSNorm + QUANTQ8 of x, gate/up rows, SwiGLU
 //   E  QUANTQ8 of swi, down rows, += residual
 // Shared-memory buffers and what they hold; each is requested once it is free,
@@ -60,6 +60,7 @@ struct StepArgs {
     const int32_t* pos;
     const uint16_t* embed;
     float *x, *q, *k, *v, *qr, *attn, *swi, *PO, *PML;
+    unsigned char* attnq;    // the attention output QUANTQ8'd in the GEMV activation layout
     unsigned* counters;      // [nKv] split arrivals (zero between steps)
     unsigned long long* bar_count;   // grid barrier: arrivals since the model was made (monotonic)
     unsigned* abort_word;    // == this launch's tag: a CTA gave up in this launch
@@ -336,10 +337,6 @@ __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, i
         block256_reduce_rows<1>(&ss, red, &tot);
         inv = rms_inv(tot, K, sa.eps);
     }
-    uint4* xlo = reinterpret_cast<uint4*>(smem + sa.off_act);
-    uint4* xhi = xlo + G;
-    int* xs8 = reinterpret_cast<int*>(xhi + G);
-    float* xsf = reinterpret_cast<float*>(xs8 + G);
 #pragma unroll
     for (int i = 0; i < MAXF; i++) {
         if (i >= nf) break;
@@ -350,27 +347,7 @@ __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, i
 #pragma unroll
             for (int j = 0; j < 4; j++) e[j] = __fmul_rn(__fmul_rn(e[j], inv), tb_h2f(nws[4 * f + j]));
         }
-        float mx = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        const float scale = q8_scale(mx), is = q8_inv(scale);
-        const int q0 = q8_quant(e[0], is), q1 = q8_quant(e[1], is), q2 = q8_quant(e[2], is), q3 = q8_quant(e[3], is);
-        // this thread's k = 4*j4 .. 4*j4+3 of the group: weight word j4/2, half j4&1
-        const uint32_t ev = ((uint32_t)q0 & 0xffu) | (((uint32_t)q2 & 0xffu) << 8);
-        const uint32_t od = ((uint32_t)q1 & 0xffu) | (((uint32_t)q3 & 0xffu) << 8);
-        const uint32_t ev_p = __shfl_xor_sync(0xffffffffu, ev, 1), od_p = __shfl_xor_sync(0xffffffffu, od, 1);
-        int sum = q0 + q1 + q2 + q3;
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        const int j4 = f & 7, g = f >> 3;
-        if (live && !(j4 & 1)) {
-            const int w = j4 >> 1;
-            uint32_t* dst = reinterpret_cast<uint32_t*>((w < 2 ? xlo : xhi) + g) + 2 * (w & 1);
-            *reinterpret_cast<uint2*>(dst) = make_uint2(ev | (ev_p << 16), od | (od_p << 16));
-            if (j4 == 0) { xs8[g] = 8 * sum; xsf[g] = scale; }
-        }
+        q8_store_group4(e, f >> 3, live, smem + sa.off_act, G);      // f & 7 == lane & 7
     }
     __syncthreads();
     stamp(sa, slot + 1);
@@ -427,6 +404,8 @@ __device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned
         const int r = unit_rot(a, u);
         U unit(t, smem + a.off_P, r % a.nKv, r / a.nKv, 0, threadIdx.x, 0);
         unit.prep = &pin;
+        unit.qout = a.attnq;
+        unit.qG = a.nHq * STEP_HD / 32;
         if (a.trace && i == 0) unit.tr = a.trace + (size_t)blockIdx.x * (1 + 38 * a.L) + 1 + 25 * a.L + 8 * l;
         // the first unit's tiles were requested in an earlier phase (row pos is
         // written into its stage by the prep); a later unit requests them now,
@@ -535,7 +514,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (!await_buf(a, ctl, BUF_R, bars)) goto drain;
             STAMP(2, 0);
             const int n = rowsC(a);
-            if (n > 0) stage(a, smem, a.attn, a.nHq * STEP_HD, false, nullptr, red, 1 + 25 * l + 5 * 2 + 1);
+            if (n > 0) {    // the combining units stored the quantized attention output
+                const int nq = a.nHq * STEP_HD / 32 * 40 / 16;
+                for (int i = tid; i < nq; i += THREADS)
+                    reinterpret_cast<uint4*>(smem + a.off_act)[i] = __ldcg(reinterpret_cast<const uint4*>(a.attnq) + i);
+                __syncthreads();
+                STAMP(2, 2);
+            }
             if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
             STAMP_REQ(2);
             if (n > 0) {
@@ -674,6 +659,7 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.eps = io->eps; a.theta = io->theta;
     a.ids = io->ids; a.pos = io->pos; a.embed = io->embed;
     a.x = io->x; a.q = io->q; a.k = io->k; a.v = io->v; a.qr = io->qr; a.attn = io->attn; a.swi = io->swi;
+    a.attnq = io->attnq;
     a.PO = io->PO; a.PML = io->PML; a.counters = io->counters;
     a.bar_count = reinterpret_cast<unsigned long long*>(io->ctrl + 64); a.abort_word = io->ctrl + 128;
     a.err = ctx->dev_error;
