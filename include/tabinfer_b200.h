@@ -490,7 +490,9 @@ TB_API int tb_convert_bf16_f16(tb_ctx *ctx, const uint16_t *in_bf16, uint16_t *o
  * written this step and is advanced by one, so consecutive steps need no host
  * work (the reference's GPU token history, :4055-4060).  The first
  * tb_qwen3_decode_step records the step as a CUDA graph; later calls replay it
- * on the context's stream.
+ * on the context's stream.  At batch 1 on one GPU the step is, by default, one
+ * persistent kernel for embed and all layers plus the lm_head and argmax
+ * (tb_qwen3_set_step_mode); elsewhere one kernel per operation.
  *
  * Tensor parallelism (tp_size > 1, one context and process per GPU): each
  * rank keeps q/k/v and gate/up row blocks, o and down column blocks, its
@@ -535,7 +537,7 @@ enum {
  * ONE persistent kernel (one CTA per SM, grid barriers between the phases, each
  * CTA requesting the weights of its next phases into shared memory while the
  * current one runs), then lm_head and argmax; batch 1, one GPU, int4 layer
- * weights.  TB_QW_STEP_KERNELS: one kernel per operation (~170 a step).
+ * weights.  TB_QW_STEP_KERNELS: one kernel per operation (6 per layer + 4).
  * TB_QW_STEP_AUTO (default): persistent where it applies.  Both compute the same
  * bits.  No reference counterpart (the reference dispatches WebGPU passes). */
 #define TB_QW_STEP_AUTO 0
