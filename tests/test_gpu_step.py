@@ -73,3 +73,32 @@ def test_persistent_mode_refused_where_it_does_not_apply(cuda):
     m.step()
     assert m.step_kind() == _lib.QW_STEP_KERNELS
     m.close()
+
+
+def test_phase_trace_stamps_are_ordered(cuda):
+    """tb_qwen3_step_trace: every CTA stamps the kernel start and, for each layer
+    and phase, weights ready <= phase done <= barrier passed, phases in order."""
+    import torch
+    cfg = dict(SMALL, batch=1, layers=2)
+    W, m = _build(cfg, 47, [9])
+    m.set_tokens([3], [9])
+    m.step()
+    assert m.step_kind() == _lib.QW_STEP_PERSISTENT
+    L = cfg["layers"]
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    buf = torch.zeros(G, 1 + 38 * L, dtype=torch.int64, device="cuda")
+    m.step_trace(buf)
+    m.step_layers()
+    t = buf.cpu().numpy()
+    m.step_trace(None)
+    assert (t[:, 0] > 0).all()
+    ph = t[:, 1:1 + 25 * L].reshape(G, L, 5, 5)       # ready, loaded, staged, done, out
+    ready, done, out = ph[:, :, :, 0], ph[:, :, :, 3], ph[:, :, :, 4]
+    last = (slice(None), L - 1, 4)                    # the last phase has no barrier after it
+    assert (ready > 0).all() and (done >= ready).all()
+    out[last] = done[last]
+    assert (out >= done).all()
+    flat_ready = ready.reshape(G, -1)
+    assert (np.diff(flat_ready, axis=1) >= 0).all()
+    assert m.ctx.device_error() == 0
+    m.close()
