@@ -12,11 +12,11 @@
 //
 // Phases of layer l (barrier after each):
 //   A  RMSNorm + QUANTQ8 of x, q/k/v rows (32-row blocks)
-//   B  split-KV attention: (kv head, split) units on 4-warp groups, two per CTA
-//      (DecUnit, the standalone kernel's code); each unit runs attnPrepQ8 for
-//      its own q heads (norm + RoPE) and the unit holding row pos writes that
-//      cache row (k: norm + RoPE + int8, v: int8); the last split of a kv head
-//      combines
+//   B  split-KV attention: one 8-warp (kv head, split) unit per CTA (DecUnit,
+//      the standalone kernel's code); each unit runs attnPrepQ8 for its own q
+//      heads (norm + RoPE) and the unit holding row pos writes that cache row
+//      (k: norm + RoPE + int8, v: int8, also straight into its tile); the last
+//      split of a kv head combines and stores the heads' outputs QUANTQ8'd
 //   C  the attention output (QUANTQ8'd by the combining units), o rows, += residual
 //   D  RMSNorm + QUANTQ8 of x, gate/up rows, SwiGLU
 //   E  QUANTQ8 of swi, down rows, += residual
