@@ -814,6 +814,7 @@ def bonsai_extra(dev, peak_gbs, stream, context=4096):
     lm_head, loaded as ternary WebGPU-layout records) through the recorded
     decode step: tok/s at batch 1, context 4096."""
     import torch
+    from tabinfer_b200 import _lib as _tl
     steps = 50
     m = build_model(Q17, dev, 1, context, steps + 16, 1, 0, seed=77, ternary=True)
     for _ in range(5):
@@ -824,11 +825,23 @@ def bonsai_extra(dev, peak_gbs, stream, context=4096):
     ms = time_steps(m, steps, stream) / steps
     err = m.ctx.device_error()
     assert err == 0, "bonsai decode device error 0x%x" % err
+    kind = {_tl.QW_STEP_KERNELS: "kernels", _tl.QW_STEP_PERSISTENT: "persistent"}.get(m.step_kind(), "?")
+    # the same step as one kernel per operation, for comparison
+    m.set_step_mode(_tl.QW_STEP_KERNELS)
+    for _ in range(3):
+        m.set_tokens([1000], [context - 1])
+        m.step()
+    m.set_tokens([1000], [context - 1])
+    torch.cuda.synchronize(dev)
+    ms_k = time_steps(m, steps, stream) / steps
+    err = m.ctx.device_error()
+    assert err == 0, "bonsai decode (kernels) device error 0x%x" % err
     nb = step_bytes(Q17, 1, 1, context, tern=True)
     kinds = sorted({m.weight_format(n) for n in ("lm_head.weight", "model.layers.0.mlp.down_proj.weight")})
     m.close()
     torch.cuda.synchronize(dev)
-    return {"tok_per_s": round(1e3 / ms, 1), "ms_per_step": round(ms, 4), "bytes_per_step": int(nb),
+    return {"tok_per_s": round(1e3 / ms, 1), "ms_per_step": round(ms, 4), "step_kind": kind,
+            "tok_per_s_one_kernel_per_op": round(1e3 / ms_k, 1), "bytes_per_step": int(nb),
             "step_hbm_gbs": round(nb / (ms * 1e-3) / 1e9, 1), "frac_of_peak": round(nb / (ms * 1e-3) / 1e9 / peak_gbs, 4),
             "weight_formats": kinds, "reference_webgpu_tok_per_s": "21.7 (Iris Xe)"}
 

@@ -80,9 +80,13 @@ __device__ __forceinline__ Q8Group q8_group(float v)
 // QUANTQ8 of one 32-group held by 8 consecutive lanes (lane & 7 = j4 holds
 // elements 4*j4 .. 4*j4+3), stored in the permuted dp4a layout of the GEMV
 // activation (act: xlo uint4 [G], xhi uint4 [G], s8 int [G] = 8*sum(q), sf float
-// [G] = scale): the same bits as stage_q8<1, false>.  Every lane of the warp
-// calls it (shuffles); live: this lane's group is real and is stored.
-__device__ __forceinline__ void q8_store_group4(const float e[4], int g, bool live, unsigned char* act, int G)
+// [G] = scale): the same bits as stage_q8<1, false>.  nat (warp-uniform): the
+// natural-order layout of the ternary GEMVs instead (word j4 of the group holds
+// elements 4*j4 .. 4*j4+3, s8 = sum(q)): the same bits as stage_q8<1, true>.
+// Every lane of the warp calls it (shuffles); live: this lane's group is real
+// and is stored.
+__device__ __forceinline__ void q8_store_group4(const float e[4], int g, bool live, unsigned char* act, int G,
+                                                bool nat = false)
 {
     uint4* xlo = reinterpret_cast<uint4*>(act);
     uint4* xhi = xlo + G;
@@ -94,6 +98,20 @@ __device__ __forceinline__ void q8_store_group4(const float e[4], int g, bool li
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
     const float scale = q8_scale(mx), is = q8_inv(scale);
     const int q0 = q8_quant(e[0], is), q1 = q8_quant(e[1], is), q2 = q8_quant(e[2], is), q3 = q8_quant(e[3], is);
+    if (nat) {
+        int sum = q0 + q1 + q2 + q3;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        const int j4 = threadIdx.x & 7;
+        if (live) {
+            reinterpret_cast<uint32_t*>((j4 < 4 ? xlo : xhi) + g)[j4 & 3] =
+                ((uint32_t)q0 & 0xffu) | (((uint32_t)q1 & 0xffu) << 8) | (((uint32_t)q2 & 0xffu) << 16) |
+                ((uint32_t)q3 << 24);
+            if (j4 == 0) { xs8[g] = sum; xsf[g] = scale; }
+        }
+        return;
+    }
     // this lane's k = 4*j4 .. 4*j4+3 of the group: weight word j4/2, half j4&1
     const uint32_t ev = ((uint32_t)q0 & 0xffu) | (((uint32_t)q2 & 0xffu) << 8);
     const uint32_t od = ((uint32_t)q1 & 0xffu) | (((uint32_t)q3 & 0xffu) << 8);

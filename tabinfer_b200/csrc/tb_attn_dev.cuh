@@ -209,6 +209,7 @@ struct DecUnit {
     // quantizing
     unsigned char* qout = nullptr;
     int qG = 0;
+    bool qnat = false;                  // qout in the ternary GEMVs' natural-order layout
     unsigned long long* tr = nullptr;   // optional %globaltimer stamps of the unit's stages (8 slots)
 
     __device__ void ts(int k) const
@@ -519,7 +520,7 @@ struct DecUnit {
                     const int h = col / (HD / 4), c4 = col - h * (HD / 4);
                     const float4 r = __ldcg(reinterpret_cast<const float4*>(outp + (long long)(hk * GRP + h) * HD) + c4);
                     const float e4[4] = {r.x, r.y, r.z, r.w};
-                    q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG);
+                    q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG, qnat);
                 }
             }
             return;
@@ -630,7 +631,7 @@ struct DecUnit {
             reinterpret_cast<float4*>(outp + (long long)(hk * GRP + h) * HD)[c4] = res;
             if (qout) {     // 8 consecutive columns = one 32-group, 8 consecutive lanes
                 const float e4[4] = {res.x, res.y, res.z, res.w};
-                q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG);
+                q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG, qnat);
             }
         }
         if (tid == 0) *counter = 0u;     // ready for the next call

@@ -90,8 +90,9 @@ struct tb_step_io {
     unsigned* ctrl;                // [256] zero-initialised: grid barrier counter (u64 at word 64), abort word (128)
     void* trace;                   // optional: u64 [grid][1 + 38 * layers] %globaltimer stamps
 };
+// tern: the layer weights are ternary (WebGPU layout) instead of int4 G32
 int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I, int nsplit, int max_seq,
-                      tb_step_plan** out);
+                      int tern, tb_step_plan** out);
 void tb_step_plan_free(tb_step_plan* p);
 size_t tb_step_plan_smem(const tb_step_plan* p);
 int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io);

@@ -130,6 +130,7 @@ struct tb_qwen3 {
     int step_kind = 0;                           // recorded: TB_QW_STEP_KERNELS or TB_QW_STEP_PERSISTENT
     tb_step_plan* step = nullptr;
     unsigned char* step_layers = nullptr;        // device per-layer records
+    int step_tern = -1;                          // weight format the plan was made for (1 ternary)
     unsigned* step_ctrl = nullptr;               // [256] block arrivals, grid barrier, abort word
     unsigned char* step_attnq = nullptr;         // quantized attention output of the persistent step
     bool step_direct = false;                    // persistent step launched per call (not capturable)
@@ -266,17 +267,27 @@ int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w, int xi)
 
 int issue_head(tb_qwen3* m, int cur);
 
-// Can this model's step run as the persistent kernel?  (batch 1, one GPU, int4
-// q/k/v/o/gate/up/down in every layer, sizes tb_step_plan_make accepts)
+// Can this model's step run as the persistent kernel?  (batch 1, one GPU,
+// q/k/v/o/gate/up/down all int4 or all ternary in every layer, sizes
+// tb_step_plan_make accepts)
 bool persistent_ok(tb_qwen3* m)
 {
-    if (m->P != 1 || m->c.batch != 1) return false;
-    for (const Layer& Ly : m->L)
-        if (Ly.q.tern || Ly.k.tern || Ly.v.tern || Ly.o.tern || Ly.gate.tern || Ly.up.tern || Ly.down.tern) return false;
+    if (m->P != 1 || m->c.batch != 1 || m->L.empty()) return false;
+    const bool tern = m->L[0].q.tern;
+    for (const Layer& Ly : m->L) {
+        const Mat* ms[7] = {&Ly.q, &Ly.k, &Ly.v, &Ly.o, &Ly.gate, &Ly.up, &Ly.down};
+        for (const Mat* w : ms)
+            if (w->tern != tern) return false;
+    }
+    if (m->step && m->step_tern != (int)tern) {   // the weights changed format since the plan was made
+        tb_step_plan_free(m->step);
+        m->step = nullptr;
+    }
     if (!m->step) {
         if (tb_step_plan_make(m->ctx, m->c.layers, m->c.hidden, (int)m->nHq, (int)m->nKv, m->c.head_dim, (int)m->I,
-                              m->nsplit, m->c.max_seq, &m->step) != TB_OK)
+                              m->nsplit, m->c.max_seq, (int)tern, &m->step) != TB_OK)
             return false;
+        m->step_tern = (int)tern;
     }
     if (!m->step_layers) {
         const size_t rec = tb_step_layer_bytes();
@@ -943,7 +954,8 @@ TB_API int tb_qwen3_decode_step(tb_qwen3* m)
         const bool pers = m->step_mode != TB_QW_STEP_KERNELS && persistent_ok(m);
         if (m->step_mode == TB_QW_STEP_PERSISTENT && !pers)
             return tb_fail(ctx, TB_ERR_UNSUPPORTED,
-                           "persistent decode step needs batch 1, one GPU, int4 layer weights and sizes it supports");
+                           "persistent decode step needs batch 1, one GPU, layer weights all int4 or all ternary "
+                           "and sizes it supports");
         m->step_kind = pers ? TB_QW_STEP_PERSISTENT : TB_QW_STEP_KERNELS;
         // record the step once on a private stream, after everything queued so far
         cudaStream_t user = ctx->stream;

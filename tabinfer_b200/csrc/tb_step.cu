@@ -28,6 +28,9 @@
 //   Q  E(l) (during A(l))
 // Every phase uses the standalone kernels' device code (tb_gemv_dev.cuh,
 // tb_attn_dev.cuh) with the same split count, so the step is bit-identical to
+// the multi-kernel step.  The layer weights are all int4 G32 or all ternary in
+// the WebGPU layout (TERN: 8 code bytes a 32-group, the activations QUANTQ8'd
+// in natural order, item_ternx instead of item_q8x), as gemvTern / gemvQ8 of
 // the multi-kernel step.  Barrier and copy waits are bounded; a CTA that gives up
 // records the error, raises the launch's abort word, drains its copies and
 // returns, and the others leave at their next barrier.
@@ -75,6 +78,7 @@ struct StepArgs {
     // shared-memory layout (bytes)
     int off_P, off_Q, off_R, off_act, off_misc, off_layers;
     int rpC, rpD;            // rows per CTA of o / down (rpC) and gate / up (rpD)
+    int tern;                // layer weights: 0 int4 G32, 1 ternary in the WebGPU layout
 };
 
 __device__ __forceinline__ void stamp(const StepArgs& a, int slot)
@@ -145,14 +149,20 @@ __device__ bool grid_sync(const StepArgs& a, Ctl* ctl)
 // ---- weight requests ---------------------------------------------------------
 enum { BUF_P = 0, BUF_Q = 1, BUF_R = 2 };
 
-// rows [r0, r0+n) of a matrix with K columns -> dst: packed rows, then their scales
-__device__ __forceinline__ uint32_t mat_bytes(int n, int K) { return (uint32_t)n * (K / 2 + K / 16); }
-__device__ __forceinline__ void req_rows(unsigned char* dst, const uint32_t* pack, const uint16_t* sc, int r0, int n,
-                                         int K, uint64_t* bar)
+// rows [r0, r0+n) of a matrix with K columns -> dst: packed rows (K/2 bytes a
+// row of int4, K/4 of ternary codes), then their f16 scales (one per 32-group)
+__device__ __forceinline__ uint32_t row_bytes(const StepArgs& a, int K) { return (uint32_t)(K >> (a.tern ? 2 : 1)); }
+__device__ __forceinline__ uint32_t mat_bytes(const StepArgs& a, int n, int K)
+{
+    return (uint32_t)n * (row_bytes(a, K) + K / 16);
+}
+__device__ __forceinline__ void req_rows(const StepArgs& a, unsigned char* dst, const uint32_t* pack,
+                                         const uint16_t* sc, int r0, int n, int K, uint64_t* bar)
 {
     if (n <= 0) return;
-    bulk_g2s(dst, reinterpret_cast<const unsigned char*>(pack) + (size_t)r0 * (K / 2), (uint32_t)n * (K / 2), bar);
-    bulk_g2s(dst + (size_t)n * (K / 2), sc + (size_t)r0 * (K / 32), (uint32_t)n * (K / 16), bar);
+    const uint32_t wb = row_bytes(a, K);
+    bulk_g2s(dst, reinterpret_cast<const unsigned char*>(pack) + (size_t)r0 * wb, (uint32_t)n * wb, bar);
+    bulk_g2s(dst + (size_t)n * wb, sc + (size_t)r0 * (K / 32), (uint32_t)n * (K / 16), bar);
 }
 
 __device__ __forceinline__ int rowsC0(const StepArgs& a) { return min(a.H, (int)blockIdx.x * a.rpC); }
@@ -187,30 +197,30 @@ __device__ void request(const StepArgs& a, Ctl* ctl, int buf, int phase, int l, 
     uint32_t bytes = 0;
     if (phase == 0) {          // A: one 32-row block + ln1
         const BlockA b = block_a(a);
-        if (b.live) bytes = mat_bytes(RBA, a.H);
+        if (b.live) bytes = mat_bytes(a, RBA, a.H);
         bytes += (uint32_t)a.H * 2;
         mbar_expect_tx(bar, bytes);
-        if (b.live) req_rows(dst, Ly.p[b.mat], Ly.s[b.mat], b.row0, RBA, a.H, bar);
-        bulk_g2s(dst + (b.live ? mat_bytes(RBA, a.H) : 0u), Ly.ln1, (uint32_t)a.H * 2, bar);
+        if (b.live) req_rows(a, dst, Ly.p[b.mat], Ly.s[b.mat], b.row0, RBA, a.H, bar);
+        bulk_g2s(dst + (b.live ? mat_bytes(a, RBA, a.H) : 0u), Ly.ln1, (uint32_t)a.H * 2, bar);
     } else if (phase == 2) {   // C: o rows
         const int n = rowsC(a), K = a.nHq * STEP_HD;
-        bytes = mat_bytes(n, K);
+        bytes = mat_bytes(a, n, K);
         if (bytes == 0) return;
         mbar_expect_tx(bar, bytes);
-        req_rows(dst, Ly.p[WO], Ly.s[WO], rowsC0(a), n, K, bar);
+        req_rows(a, dst, Ly.p[WO], Ly.s[WO], rowsC0(a), n, K, bar);
     } else if (phase == 3) {   // D: gate rows, up rows, ln2
         const int n = rowsD(a);
-        bytes = 2 * mat_bytes(n, a.H) + (uint32_t)a.H * 2;
+        bytes = 2 * mat_bytes(a, n, a.H) + (uint32_t)a.H * 2;
         mbar_expect_tx(bar, bytes);
-        req_rows(dst, Ly.p[WG], Ly.s[WG], rowsD0(a), n, a.H, bar);
-        req_rows(dst + mat_bytes(n, a.H), Ly.p[WU], Ly.s[WU], rowsD0(a), n, a.H, bar);
-        bulk_g2s(dst + 2 * mat_bytes(n, a.H), Ly.ln2, (uint32_t)a.H * 2, bar);
+        req_rows(a, dst, Ly.p[WG], Ly.s[WG], rowsD0(a), n, a.H, bar);
+        req_rows(a, dst + mat_bytes(a, n, a.H), Ly.p[WU], Ly.s[WU], rowsD0(a), n, a.H, bar);
+        bulk_g2s(dst + 2 * mat_bytes(a, n, a.H), Ly.ln2, (uint32_t)a.H * 2, bar);
     } else {                   // E: down rows
         const int n = rowsC(a);
-        bytes = mat_bytes(n, a.I);
+        bytes = mat_bytes(a, n, a.I);
         if (bytes == 0) return;
         mbar_expect_tx(bar, bytes);
-        req_rows(dst, Ly.p[WD], Ly.s[WD], rowsC0(a), n, a.I, bar);
+        req_rows(a, dst, Ly.p[WD], Ly.s[WD], rowsC0(a), n, a.I, bar);
     }
     ctl->pend |= 1u << buf;
 }
@@ -238,7 +248,7 @@ __device__ bool await_buf(const StepArgs& a, Ctl* ctl, int buf, uint64_t* bars)
 // w_s: [n][G] 16-byte weight groups, then [n][G] f16 scales
 // own: this CTA's rows of the residual x kept in shared memory (their only
 // writer is this CTA), so y = own + W.a needs no read of y from memory
-template <int NM, int RPW>
+template <int NM, int RPW, bool TERN>
 __device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
                             float* y, int row0, float* own)
 {
@@ -253,15 +263,20 @@ __device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, c
 #pragma unroll
         for (int s = 0; s < NM; s++) {
             const unsigned char* slot = s ? w1 : w0;
-            const uint4* wq = reinterpret_cast<const uint4*>(slot);
-            const uint16_t* sbase = reinterpret_cast<const uint16_t*>(slot + (size_t)n * G * 16);
+            const uint16_t* sbase = reinterpret_cast<const uint16_t*>(slot + (size_t)n * G * (TERN ? 8 : 16));
             for (int g = lane; g < G; g += 32) {
                 XQ<1> xg;
                 load_xq<1>(xg, act, G, g);
 #pragma unroll
                 for (int q = 0; q < RPW; q++) {
                     const int r = r0 + q * NW;
-                    if (r < n) item_q8x<1>(wq[r * G + g], tb_h2f(sbase[r * G + g]), xg, &acc[q][s]);
+                    if (r >= n) continue;
+                    if (TERN)
+                        item_ternx<1>(reinterpret_cast<const uint2*>(slot)[r * G + g], tb_h2f(sbase[r * G + g]), xg,
+                                      &acc[q][s]);
+                    else
+                        item_q8x<1>(reinterpret_cast<const uint4*>(slot)[r * G + g], tb_h2f(sbase[r * G + g]), xg,
+                                    &acc[q][s]);
                 }
             }
         }
@@ -292,24 +307,26 @@ __device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, c
 
 // rows per warp chosen so the CTA's rows take one pass (a row's sum does not
 // depend on which warp computes it)
-template <int NM>
+template <int NM, bool TERN>
 __device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
                           float* y, int row0, float* own)
 {
     const int rpw = (n + THREADS / 32 - 1) / (THREADS / 32);
-    if (rpw <= 2) gemv_rows_r<NM, 2>(act, w0, w1, n, G, y, row0, own);
-    else if (rpw <= 4) gemv_rows_r<NM, 4>(act, w0, w1, n, G, y, row0, own);
-    else if (rpw <= 6) gemv_rows_r<NM, 6>(act, w0, w1, n, G, y, row0, own);
-    else gemv_rows_r<NM, 8>(act, w0, w1, n, G, y, row0, own);
+    if (rpw <= 2) gemv_rows_r<NM, 2, TERN>(act, w0, w1, n, G, y, row0, own);
+    else if (rpw <= 4) gemv_rows_r<NM, 4, TERN>(act, w0, w1, n, G, y, row0, own);
+    else if (rpw <= 6) gemv_rows_r<NM, 6, TERN>(act, w0, w1, n, G, y, row0, own);
+    else gemv_rows_r<NM, 8, TERN>(act, w0, w1, n, G, y, row0, own);
 }
 
 // QUANTQ8 (optionally RMSNorm first) of a whole f32 row written by other CTAs,
-// into the permuted int8 layout of stage_q8<1, false> with the same bits: thread
+// into the int8 layout of stage_q8<1, NAT> with the same bits (NAT: the
+// ternary GEMVs' natural order; else the permuted int4 dp4a order): thread
 // t holds float4s f = t, t+256, ... in registers (the canonical sum-of-squares
 // order), 8 consecutive threads (one warp-aligned 32-group) find the group
 // maximum and sum with shuffles, and pairs of threads assemble the even / odd
 // byte words of a weight word.  Every thread is busy and there is one
 // round trip to memory.  K % 32 == 0, K <= 8192.
+template <bool NAT>
 __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, int K, bool norm, const uint16_t* nws,
                       float* red, int slot)
 {
@@ -347,7 +364,7 @@ __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, i
 #pragma unroll
             for (int j = 0; j < 4; j++) e[j] = __fmul_rn(__fmul_rn(e[j], inv), tb_h2f(nws[4 * f + j]));
         }
-        q8_store_group4(e, f >> 3, live, smem + sa.off_act, G);      // f & 7 == lane & 7
+        q8_store_group4(e, f >> 3, live, smem + sa.off_act, G, NAT);      // f & 7 == lane & 7
     }
     __syncthreads();
     stamp(sa, slot + 1);
@@ -392,7 +409,7 @@ __device__ void attn_prefetch(const StepArgs& a, const StepLayer& Ly, unsigned c
     unit.prefetch(true);
 }
 
-template <int GRP>
+template <int GRP, bool TERN>
 __device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned char* smem, const float* cs, int pos)
 {
     using U = DecUnit<STEP_HD, GRP, 1, UW>;
@@ -406,6 +423,7 @@ __device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned
         unit.prep = &pin;
         unit.qout = a.attnq;
         unit.qG = a.nHq * STEP_HD / 32;
+        unit.qnat = TERN;
         if (a.trace && i == 0) unit.tr = a.trace + (size_t)blockIdx.x * (1 + 38 * a.L) + 1 + 25 * a.L + 8 * l;
         // the first unit's tiles were requested in an earlier phase (row pos is
         // written into its stage by the prep); a later unit requests them now,
@@ -417,7 +435,7 @@ __device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned
     }
 }
 
-template <int GRP>
+template <int GRP, bool TERN>
 __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
 {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -483,13 +501,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             STAMP(0, 0);
             const BlockA b = block_a(a);
             const unsigned char* wR = smem + a.off_R;
-            const uint16_t* nws = reinterpret_cast<const uint16_t*>(wR + (b.live ? mat_bytes(RBA, a.H) : 0));
-            if (b.live) stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
+            const uint16_t* nws = reinterpret_cast<const uint16_t*>(wR + (b.live ? mat_bytes(a, RBA, a.H) : 0));
+            if (b.live) stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
             if (tid == 0 && l > 0) request(a, ctl, BUF_Q, 4, l, smem, bars);   // Q held E(l-1)
             STAMP_REQ(0);
             if (b.live) {
                 float* y = b.mat == WQ ? a.q : (b.mat == WK ? a.k : a.v);
-                gemv_rows<1>(smem + a.off_act, wR, nullptr, RBA, a.H / 32, y, b.row0, nullptr);
+                gemv_rows<1, TERN>(smem + a.off_act, wR, nullptr, RBA, a.H / 32, y, b.row0, nullptr);
             }
             __syncthreads();
             STAMP(0, 3);
@@ -503,7 +521,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             // barrier and the activation loads do not queue behind them)
             if (tid == 0) request(a, ctl, BUF_R, 2, l, smem, bars);
             STAMP_REQ(1);
-            attn_run<GRP>(a, Ly, l, smem, cs, pos);
+            attn_run<GRP, TERN>(a, Ly, l, smem, cs, pos);
             __syncthreads();
             STAMP(1, 3);
             if (!grid_sync(a, ctl)) goto drain;
@@ -524,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
             STAMP_REQ(2);
             if (n > 0) {
-                gemv_rows<1>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x, rowsC0(a), xo);
+                gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
             STAMP(2, 3);
@@ -538,13 +556,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const int n = rowsD(a);
             const unsigned char* wP = smem + a.off_P;
             if (n > 0) {
-                const uint16_t* nws = reinterpret_cast<const uint16_t*>(wP + 2 * mat_bytes(n, a.H));
-                stage(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 3 + 1);
+                const uint16_t* nws = reinterpret_cast<const uint16_t*>(wP + 2 * mat_bytes(a, n, a.H));
+                stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 3 + 1);
             }
             if (tid == 0 && more) request(a, ctl, BUF_R, 0, l + 1, smem, bars);
             STAMP_REQ(3);
             if (n > 0) {
-                gemv_rows<2>(smem + a.off_act, wP, wP + mat_bytes(n, a.H), n, a.H / 32, a.swi, rowsD0(a), nullptr);
+                gemv_rows<2, TERN>(smem + a.off_act, wP, wP + mat_bytes(a, n, a.H), n, a.H / 32, a.swi, rowsD0(a), nullptr);
             }
             __syncthreads();
             STAMP(3, 3);
@@ -556,11 +574,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (!await_buf(a, ctl, BUF_Q, bars)) goto drain;
             STAMP(4, 0);
             const int n = rowsC(a);
-            if (n > 0) stage(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
+            if (n > 0) stage<TERN>(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
             if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
             STAMP_REQ(4);
             if (n > 0) {
-                gemv_rows<1>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
+                gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
             STAMP(4, 3);
@@ -590,7 +608,7 @@ struct tb_step_plan {
 // returns TB_ERR_UNSUPPORTED when it does not apply (the caller keeps the
 // multi-kernel step).
 int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I, int nsplit, int max_seq,
-                      tb_step_plan** out)
+                      int tern, tb_step_plan** out)
 {
     *out = nullptr;
     const int G = ctx->num_sms;
@@ -604,10 +622,11 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     if (nsplit < 1 || nsplit > 256) return TB_ERR_UNSUPPORTED;
     StepArgs a{};
     a.L = L; a.H = H; a.nHq = nHq; a.nKv = nKv; a.I = I; a.nsplit = nsplit; a.max_seq = max_seq;
+    a.tern = tern ? 1 : 0;
     a.rpC = (H + G - 1) / G;
     a.rpD = (I + G - 1) / G;
     if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
-    auto mb = [](int n, int K) { return (size_t)n * (K / 2 + K / 16); };
+    auto mb = [&](int n, int K) { return (size_t)n * ((K >> (a.tern ? 2 : 1)) + K / 16); };
     // one 8-warp unit per CTA with one 32-key tile per warp at the longest context
     const int per = (max_seq + nsplit - 1) / nsplit;
     if (nKv * nsplit > G || per > UW * 32) return TB_ERR_UNSUPPORTED;
@@ -665,11 +684,20 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.err = ctx->dev_error;
     a.trace = reinterpret_cast<unsigned long long*>(io->trace);
     void (*kern)(const StepArgs) = nullptr;
-    switch (p->grp) {
-    case 1: kern = k_decode_step<1>; break;
-    case 2: kern = k_decode_step<2>; break;
-    case 4: kern = k_decode_step<4>; break;
-    default: kern = k_decode_step<8>; break;
+    if (a.tern) {
+        switch (p->grp) {
+        case 1: kern = k_decode_step<1, true>; break;
+        case 2: kern = k_decode_step<2, true>; break;
+        case 4: kern = k_decode_step<4, true>; break;
+        default: kern = k_decode_step<8, true>; break;
+        }
+    } else {
+        switch (p->grp) {
+        case 1: kern = k_decode_step<1, false>; break;
+        case 2: kern = k_decode_step<2, false>; break;
+        case 4: kern = k_decode_step<4, false>; break;
+        default: kern = k_decode_step<8, false>; break;
+        }
     }
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p->smem);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "decode step attribute: %s", cudaGetErrorString(e));

@@ -16,9 +16,9 @@ SMALL = dict(hidden=256, layers=2, n_heads=4, n_kv_heads=2, head_dim=128, interm
              rope_theta=1e6, rms_eps=1e-6, max_seq=64)
 
 
-def _build(cfg, seed, prefill):
+def _build(cfg, seed, prefill, ternary=False):
     import tabinfer_b200 as tb
-    W = make_weights(cfg, seed)
+    W = make_weights(cfg, seed, ternary=ternary)
     m = tb.Qwen3(cfg)
     for name, w in W.items():
         assert m.load(name, u16_dev(w))

@@ -2,14 +2,15 @@
 grid barriers between the phases) against the multi-kernel step on identical
 models: logits bit-identical, the same ids, positions and cache rows, over
 several consecutive steps (graph replays), at the small test shapes and at
-Qwen3-1.7B width (context 4096, the bench's attention split), plus the oracle
-check of the persistent path at batch 1."""
+Qwen3-1.7B width (context 4096, the bench's attention split), with int4 and
+with Bonsai-style ternary layer weights, plus the oracle check of the
+persistent path at batch 1."""
 import numpy as np
 import pytest
 
 import tabinfer_b200 as tb
 from tabinfer_b200 import _lib
-from qwen3_oracle import OracleModel
+from qwen3_oracle import OracleModel, make_weights
 from test_gpu_qwen3 import SMALL, _build, _check_step
 
 pytestmark = pytest.mark.gpu
@@ -18,19 +19,26 @@ WIDE = dict(hidden=2048, layers=2, n_heads=16, n_kv_heads=8, head_dim=128, inter
             rope_theta=1e6, rms_eps=1e-6, max_seq=4200, batch=1)
 
 
-def _pair(cfg, seed, prefill):
+def _pair(cfg, seed, prefill, ternary=False):
     out = []
     for mode in (_lib.QW_STEP_KERNELS, _lib.QW_STEP_PERSISTENT):
-        W, m = _build(cfg, seed, prefill)
+        W, m = _build(cfg, seed, prefill, ternary)
         m.set_step_mode(mode)
         out.append(m)
     return out
 
 
-@pytest.mark.parametrize("cfg,prefill", [(dict(SMALL, batch=1), [23]), (dict(SMALL, batch=1, n_heads=8, n_kv_heads=8), [40]),
-                                         (dict(SMALL, batch=1, max_seq=1024, layers=3), [700]), (WIDE, [4095])])
-def test_persistent_step_equals_kernels(cuda, cfg, prefill):
-    mk, mp = _pair(cfg, 31, prefill)
+@pytest.mark.parametrize("cfg,prefill,ternary", [(dict(SMALL, batch=1), [23], False),
+                                                 (dict(SMALL, batch=1, n_heads=8, n_kv_heads=8), [40], False),
+                                                 (dict(SMALL, batch=1, max_seq=1024, layers=3), [700], False),
+                                                 (WIDE, [4095], False),
+                                                 (dict(SMALL, batch=1), [23], True),
+                                                 (dict(SMALL, batch=1, max_seq=1024, layers=3), [700], True),
+                                                 (WIDE, [4095], True)])
+def test_persistent_step_equals_kernels(cuda, cfg, prefill, ternary):
+    mk, mp = _pair(cfg, 31, prefill, ternary)
+    if ternary:
+        assert mp.weight_format("model.layers.0.mlp.down_proj.weight") == _lib.QW_FMT_TERN
     ids = [777 % cfg["vocab"]]
     for m in (mk, mp):
         m.set_tokens(ids, prefill)
@@ -72,6 +80,53 @@ def test_persistent_mode_refused_where_it_does_not_apply(cuda):
     m.set_step_mode(_lib.QW_STEP_AUTO)
     m.step()
     assert m.step_kind() == _lib.QW_STEP_KERNELS
+    m.close()
+
+
+def test_persistent_ternary_step_matches_oracle(cuda):
+    cfg = dict(SMALL, batch=1, layers=2)
+    W, m = _build(cfg, 45, [11], ternary=True)
+    m.set_step_mode(_lib.QW_STEP_PERSISTENT)
+    om = OracleModel(cfg, W)
+    assert all(om.tern.values())
+    m.set_tokens([8], [11])
+    ids, pos = _check_step(m, om, cfg, [8], [11], route_f32=False)
+    _check_step(m, om, cfg, ids, pos, route_f32=False)
+    assert m.step_kind() == _lib.QW_STEP_PERSISTENT
+    m.close()
+
+
+def test_step_follows_weight_format_changes(cuda):
+    """The persistent kernel needs one format for every layer matrix: a ternary
+    model runs it; with one int4 matrix among ternary ones AUTO records the
+    multi-kernel step and PERSISTENT is refused; with every layer matrix int4
+    the persistent step is planned again, for the new format, and still matches
+    the oracle."""
+    from helpers import u16_dev
+    cfg = dict(SMALL, batch=1)
+    W, m = _build(cfg, 49, [6], ternary=True)
+    m.set_tokens([4], [6])
+    m.step()
+    assert m.step_kind() == _lib.QW_STEP_PERSISTENT
+    I4 = make_weights(cfg, 50)
+    layer_mats = [n for n in W if ".layers." in n and n.endswith("proj.weight")]
+    assert len(layer_mats) == 7 * cfg["layers"]
+    m.load(layer_mats[0], u16_dev(I4[layer_mats[0]]))
+    assert m.weight_format(layer_mats[0]) == _lib.QW_FMT_INT4
+    m.step()
+    assert m.step_kind() == _lib.QW_STEP_KERNELS
+    m.set_step_mode(_lib.QW_STEP_PERSISTENT)
+    with pytest.raises(tb.TabInferError):
+        m.step()
+    for n in layer_mats[1:]:
+        m.load(n, u16_dev(I4[n]))
+    W2 = dict(W, **{n: I4[n] for n in layer_mats})
+    om = OracleModel(cfg, W2)
+    ids, pos = m.tokens()
+    ids, pos = _check_step(m, om, cfg, ids, pos, route_f32=False)
+    assert m.step_kind() == _lib.QW_STEP_PERSISTENT
+    _check_step(m, om, cfg, ids, pos, route_f32=False)
+    assert m.ctx.device_error() == 0
     m.close()
 
 
