@@ -196,20 +196,17 @@ struct MoeArgs {
     float* ypeer[EP_MAX] = {};
 };
 
-// 32 weights (q3 + 4 in three bitplanes) of one group as floats q - 4
-__device__ __forceinline__ void decode32(uint32_t b0, uint32_t b1, uint32_t b2, float* q)
+// weights 4j .. 4j+3 (q3 + 4 in three bitplanes) of one 32-group as floats q - 4
+__device__ __forceinline__ void decode4(uint32_t b0, uint32_t b1, uint32_t b2, int j, float* q)
 {
+    // spread the 4 bits of each plane's nibble j into the low bit of 4 bytes
+    const uint32_t n0 = ((b0 >> (4 * j)) & 15u) * 0x00204081u & 0x01010101u;
+    const uint32_t n1 = ((b1 >> (4 * j)) & 15u) * 0x00204081u & 0x01010101u;
+    const uint32_t n2 = ((b2 >> (4 * j)) & 15u) * 0x00204081u & 0x01010101u;
+    const uint32_t v = n0 | (n1 << 1) | (n2 << 2);   // 4 bytes, each q3 + 4 in 0..7
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        // spread the 4 bits of each plane's nibble j into the low bit of 4 bytes
-        const uint32_t n0 = ((b0 >> (4 * j)) & 15u) * 0x00204081u & 0x01010101u;
-        const uint32_t n1 = ((b1 >> (4 * j)) & 15u) * 0x00204081u & 0x01010101u;
-        const uint32_t n2 = ((b2 >> (4 * j)) & 15u) * 0x00204081u & 0x01010101u;
-        const uint32_t v = n0 | (n1 << 1) | (n2 << 2);   // 4 bytes, each q3 + 4 in 0..7
-#pragma unroll
-        for (int k = 0; k < 4; k++)
-            q[4 * j + k] = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540 + k)) - 8388612.0f;   // 2^23 + 4
-    }
+    for (int k = 0; k < 4; k++)
+        q[k] = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540 + k)) - 8388612.0f;   // 2^23 + 4
 }
 
 template <int KIND>
@@ -278,29 +275,52 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
             for (int t = 0; t < MOE_GPL; t++) {
                 const int g = lane + 32 * t;
                 if (g < G) {
+                    // the group nibble by nibble: weights 4 i4 .. 4 i4 + 3 of every (row,
+                    // matrix) of the warp, then each staged activation float4 read from
+                    // shared memory ONCE for all of them (not once per row and matrix);
+                    // every sum still runs over the group's k in order, then one fmaf
+                    // with the group scale, so the results are the same bits
+                    float sum[RPW][NM][MB];
 #pragma unroll
                     for (int j = 0; j < RPW; j++)
 #pragma unroll
-                        for (int m = 0; m < NM; m++) {
-                            float q[32];
-                            decode32(cur.w[j][t][m][0], cur.w[j][t][m][1], cur.w[j][t][m][2], q);
+                        for (int m = 0; m < NM; m++)
+#pragma unroll
+                            for (int b = 0; b < MB; b++) sum[j][m][b] = 0.0f;
+#pragma unroll
+                    for (int i4 = 0; i4 < 8; i4++) {
+                        float q[RPW][NM][4];
+#pragma unroll
+                        for (int j = 0; j < RPW; j++)
+#pragma unroll
+                            for (int m = 0; m < NM; m++)
+                                decode4(cur.w[j][t][m][0], cur.w[j][t][m][1], cur.w[j][t][m][2], i4, q[j][m]);
+#pragma unroll
+                        for (int b = 0; b < MB; b++) {
+                            if (b >= nb) break;      // one failed test per pass, not MB - nb
+                            const float4 xv = reinterpret_cast<const float4*>(xs + (b * G + g) * XS_PAD)[i4];
+#pragma unroll
+                            for (int j = 0; j < RPW; j++)
+#pragma unroll
+                                for (int m = 0; m < NM; m++) {
+                                    float v = sum[j][m][b];
+                                    v = fmaf(q[j][m][0], xv.x, v);
+                                    v = fmaf(q[j][m][1], xv.y, v);
+                                    v = fmaf(q[j][m][2], xv.z, v);
+                                    v = fmaf(q[j][m][3], xv.w, v);
+                                    sum[j][m][b] = v;
+                                }
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < RPW; j++)
+#pragma unroll
+                        for (int m = 0; m < NM; m++)
 #pragma unroll
                             for (int b = 0; b < MB; b++) {
-                                if (b < nb) {
-                                    const float4* xb = reinterpret_cast<const float4*>(xs + (b * G + g) * XS_PAD);
-                                    float sum = 0.0f;
-#pragma unroll
-                                    for (int i4 = 0; i4 < 8; i4++) {
-                                        const float4 xv = xb[i4];
-                                        sum = fmaf(q[4 * i4], xv.x, sum);
-                                        sum = fmaf(q[4 * i4 + 1], xv.y, sum);
-                                        sum = fmaf(q[4 * i4 + 2], xv.z, sum);
-                                        sum = fmaf(q[4 * i4 + 3], xv.w, sum);
-                                    }
-                                    acc[m][j][b] = fmaf(cur.s[j][t][m], sum, acc[m][j][b]);
-                                }
+                                if (b >= nb) break;
+                                acc[m][j][b] = fmaf(cur.s[j][t][m], sum[j][m][b], acc[m][j][b]);
                             }
-                        }
                 }
             }
 #pragma unroll
