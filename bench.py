@@ -1206,15 +1206,17 @@ def main():
         e1.record(stream)
         e1.synchronize()
         pers_us = e0.elapsed_time(e1) * 1e3 / K2
-        if not args.no_extras and world == 1:
-            # the same model as one kernel per operation (identical results), for comparison
+        if not args.no_extras:
+            # the same model as one kernel per operation (identical results), for
+            # comparison; every rank takes the same steps
             m.set_step_mode(_tl.QW_STEP_KERNELS)
             m.set_tokens(ids0, pos0)
             for _ in range(args.warmup):
                 m.step()
             m.set_tokens(ids0, pos0)
             torch.cuda.synchronize(dev)
-            msk = time_steps(m, args.steps, stream) / args.steps
+            barrier()
+            msk = max_over_ranks(time_steps(m, args.steps, stream) / args.steps)
             kernels_alt = {"tok_per_s": round(B * 1e3 / msk, 2), "ms_per_step": round(msk, 4),
                            "launches_per_step": m.launches_per_step()[0]}
     err = ctx.device_error()

@@ -536,10 +536,13 @@ enum {
 /* How the decode step runs.  TB_QW_STEP_PERSISTENT: embed and every layer in
  * ONE persistent kernel (one CTA per SM, grid barriers between the phases, each
  * CTA requesting the weights of its next phases into shared memory while the
- * current one runs), then lm_head and argmax; batch 1, one GPU, layer weights
- * all int4 or all ternary.  TB_QW_STEP_KERNELS: one kernel per operation (6 per layer + 4).
- * TB_QW_STEP_AUTO (default): persistent where it applies.  Both compute the same
- * bits.  No reference counterpart (the reference dispatches WebGPU passes). */
+ * current one runs), then lm_head and argmax; batch 1, layer weights all int4
+ * or all ternary, one GPU or tensor parallel over peer memory (tp_connect: the
+ * o / down rows are exchanged inside the kernel, CTA by CTA, over NVLink).
+ * TB_QW_STEP_KERNELS: one kernel per operation (6 per layer + 4).
+ * TB_QW_STEP_AUTO (default): persistent where it applies on one GPU; the
+ * multi-kernel step under tensor parallelism, where it is the faster of the
+ * two.  Both compute the same bits.  No reference counterpart (the reference dispatches WebGPU passes). */
 #define TB_QW_STEP_AUTO 0
 #define TB_QW_STEP_KERNELS 1
 #define TB_QW_STEP_PERSISTENT 2

@@ -41,6 +41,11 @@ int tb_quant_int4_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint3
 
 // tensor-parallel exchanges over IPC-mapped peer arenas (tb_tp.cu)
 size_t tb_tp_arena_bytes(int P, int64_t n);
+// the persistent decode step's per-CTA exchange flags in an arena: u32
+// [TB_TP_MAX][TB_TP_STEP_CTAS], row s written by rank s's CTAs (zero at creation)
+constexpr int TB_TP_MAX = 8;
+constexpr int TB_TP_STEP_CTAS = 256;
+unsigned* tb_tp_arena_step_flags(char* base, int64_t n);
 void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long** keys, unsigned** flag,
                         unsigned** flag2, unsigned** step);
 int tb_tp_allreduce_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, float* x, int xi, int nx);
@@ -89,10 +94,16 @@ struct tb_step_io {
     unsigned* counters;            // [nKv] attention split arrivals, zero between steps
     unsigned* ctrl;                // [256] zero-initialised: grid barrier counter (u64 at word 64), abort word (128)
     void* trace;                   // optional: u64 [grid][1 + 38 * layers] %globaltimer stamps
+    // tensor parallel over peer memory (P > 1): every rank's exchange-arena part
+    // buffers (f32 [2][hidden]) and step flags, mapped here; this rank's index
+    int P, rank;
+    float* tp_part[TB_TP_MAX];
+    unsigned* tp_flags[TB_TP_MAX];
 };
 // tern: the layer weights are ternary (WebGPU layout) instead of int4 G32
+// P > 1: this rank's shard of a tensor-parallel model (nHq, nKv, I per rank)
 int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I, int nsplit, int max_seq,
-                      int tern, tb_step_plan** out);
+                      int tern, int P, tb_step_plan** out);
 void tb_step_plan_free(tb_step_plan* p);
 size_t tb_step_plan_smem(const tb_step_plan* p);
 int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io);

@@ -267,12 +267,12 @@ int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w, int xi)
 
 int issue_head(tb_qwen3* m, int cur);
 
-// Can this model's step run as the persistent kernel?  (batch 1, one GPU,
-// q/k/v/o/gate/up/down all int4 or all ternary in every layer, sizes
-// tb_step_plan_make accepts)
+// Can this model's step run as the persistent kernel?  (batch 1, one GPU or
+// tensor parallel over the peer-memory exchange arenas, q/k/v/o/gate/up/down
+// all int4 or all ternary in every layer, sizes tb_step_plan_make accepts)
 bool persistent_ok(tb_qwen3* m)
 {
-    if (m->P != 1 || m->c.batch != 1 || m->L.empty()) return false;
+    if (m->c.batch != 1 || m->L.empty() || (m->P > 1 && !m->p2p)) return false;
     const bool tern = m->L[0].q.tern;
     for (const Layer& Ly : m->L) {
         const Mat* ms[7] = {&Ly.q, &Ly.k, &Ly.v, &Ly.o, &Ly.gate, &Ly.up, &Ly.down};
@@ -285,7 +285,7 @@ bool persistent_ok(tb_qwen3* m)
     }
     if (!m->step) {
         if (tb_step_plan_make(m->ctx, m->c.layers, m->c.hidden, (int)m->nHq, (int)m->nKv, m->c.head_dim, (int)m->I,
-                              m->nsplit, m->c.max_seq, (int)tern, &m->step) != TB_OK)
+                              m->nsplit, m->c.max_seq, (int)tern, m->P, &m->step) != TB_OK)
             return false;
         m->step_tern = (int)tern;
     }
@@ -328,6 +328,17 @@ tb_step_io step_io(tb_qwen3* m)
     io.PO = m->PO; io.PML = m->PML; io.counters = m->counters; io.ctrl = m->step_ctrl;
     io.trace = m->step_trace;
     io.attnq = m->step_attnq;
+    io.P = m->P;
+    io.rank = m->r;
+    if (m->P > 1) {
+        const int64_t n = (int64_t)m->c.batch * m->c.hidden;
+        for (int s = 0; s < m->P; s++) {
+            float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
+            tb_tp_arena_layout(m->peer_arena[s], n, &part, &keys, &flag, &flag2, &step);
+            io.tp_part[s] = part;
+            io.tp_flags[s] = tb_tp_arena_step_flags(m->peer_arena[s], n);
+        }
+    }
     return io;
 }
 
@@ -634,7 +645,8 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
     if (B == 1 && m->P == 1) {
         // one sequence on one GPU: one (kv head, split) unit per SM, the split
         // count the persistent step runs best with (both step kinds use it, so
-        // they compute the same bits)
+        // they compute the same bits); under TP both kinds keep the rule above,
+        // and the persistent step applies where it gives one 32-key tile per warp
         const long long by_keys = (c.max_seq + 127) / 128;
         m->nsplit = (int)std::max(1LL, std::min(by_keys, (long long)(ctx->num_sms / m->nKv)));
     }
@@ -951,11 +963,15 @@ TB_API int tb_qwen3_decode_step(tb_qwen3* m)
                    "a projection weight was never set");
     TB_REQUIRE(ctx, m->lm.set, "lm_head weight was never set");
     if (!m->exec && !m->step_direct) {
-        const bool pers = m->step_mode != TB_QW_STEP_KERNELS && persistent_ok(m);
+        // AUTO takes the persistent kernel on one GPU only: under TP its in-kernel
+        // exchanges measured slower than the multi-kernel step (588 vs 806 tok/s at
+        // TP = 2), so there it runs when asked for (TB_QW_STEP_PERSISTENT)
+        const bool want = m->step_mode == TB_QW_STEP_PERSISTENT || (m->step_mode == TB_QW_STEP_AUTO && m->P == 1);
+        const bool pers = want && persistent_ok(m);
         if (m->step_mode == TB_QW_STEP_PERSISTENT && !pers)
             return tb_fail(ctx, TB_ERR_UNSUPPORTED,
-                           "persistent decode step needs batch 1, one GPU, layer weights all int4 or all ternary "
-                           "and sizes it supports");
+                           "persistent decode step needs batch 1, one GPU or tensor parallel over peer memory "
+                           "(tp_connect), layer weights all int4 or all ternary and sizes it supports");
         m->step_kind = pers ? TB_QW_STEP_PERSISTENT : TB_QW_STEP_KERNELS;
         // record the step once on a private stream, after everything queued so far
         cudaStream_t user = ctx->stream;

@@ -28,10 +28,16 @@
 //   Q  E(l) (during A(l))
 // Every phase uses the standalone kernels' device code (tb_gemv_dev.cuh,
 // tb_attn_dev.cuh) with the same split count, so the step is bit-identical to
-// the multi-kernel step.  The layer weights are all int4 G32 or all ternary in
-// the WebGPU layout (TERN: 8 code bytes a 32-group, the activations QUANTQ8'd
-// in natural order, item_ternx instead of item_q8x), as gemvTern / gemvQ8 of
-// the multi-kernel step.  Barrier and copy waits are bounded; a CTA that gives up
+// the multi-kernel step.  Under tensor parallelism over peer memory each rank
+// runs this kernel on its shard: the o and down rows are partial sums, and CTA c
+// exchanges its slice of them with CTA c of every rank inside the kernel (its
+// own arena's part buffer, a system-scope release flag per rank, a bounded
+// acquire wait, then x + part_0 + ... + part_{P-1} in rank order, the sum of the
+// exchange kernel k_tp_allreduce), so the step is one kernel per rank and the
+// same bits as the multi-kernel TP step.  The layer weights are all int4 G32
+// or all ternary in the WebGPU layout (TERN: 8 code bytes a 32-group, the
+// activations QUANTQ8'd in natural order, item_ternx instead of item_q8x), as
+// gemvTern / gemvQ8 of the multi-kernel step.  Barrier and copy waits are bounded; a CTA that gives up
 // records the error, raises the launch's abort word, drains its copies and
 // returns, and the others leave at their next barrier.
 #include "tb_internal.h"
@@ -42,6 +48,7 @@ namespace {
 
 constexpr int ERR_STEP_BARRIER = 0x5101;
 constexpr int ERR_STEP_COPY = 0x5102;
+constexpr int ERR_STEP_TP = 0x5103;
 constexpr long long STEP_WAIT_LIMIT = 1LL << 21;   // barrier polls of ~0.5 us: ~1 s
 constexpr int RBA = 32;                              // rows of a phase-A block (a head has hd/32 blocks)
 constexpr int STEP_HD = 128;
@@ -79,6 +86,14 @@ struct StepArgs {
     int off_P, off_Q, off_R, off_act, off_misc, off_layers;
     int rpC, rpD;            // rows per CTA of o / down (rpC) and gate / up (rpD)
     int tern;                // layer weights: 0 int4 G32, 1 ternary in the WebGPU layout
+    // tensor parallel (P > 1): the o and down rows are partial sums over this rank's
+    // heads / intermediate slice; CTA c exchanges its rows with CTA c of every rank
+    // through the ranks' exchange arenas (peer memory over NVLink)
+    int P, rank;
+    float* xpart;                       // this rank's part[2][H]
+    const float* peer_part[TB_TP_MAX];  // every rank's part[2][H] (own at [rank])
+    unsigned* peer_flag[TB_TP_MAX];     // this rank's row of every rank's step flags
+    const unsigned* my_flag;            // this rank's step flags [TB_TP_MAX][TB_TP_STEP_CTAS]
 };
 
 __device__ __forceinline__ void stamp(const StepArgs& a, int slot)
@@ -370,6 +385,63 @@ __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, i
     stamp(sa, slot + 1);
 }
 
+// ---- tensor-parallel exchange of the o / down rows ----------------------------------
+__device__ __forceinline__ float ld_volatile_f32(const float* p)
+{
+    float v;
+    asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// After this CTA stored its partial rows of exchange xi (rows rowsC0 .. +rowsC)
+// into its own arena's part[xi & 1] and the caller's __syncthreads: publish
+// them to CTA blockIdx.x of every rank (system-scope release of epoch e into
+// this rank's flag slot in every arena), wait for every rank's slot to reach e
+// (acquire, bounded), then own = own + part_0 + ... + part_{P-1} in rank order,
+// the sum k_tp_allreduce forms, into the CTA's residual rows and x.
+// e = (barriers before this launch) + xi + 1: every launch passes 5L barriers
+// and has 2L exchanges, so epochs grow across launches and the flags are never
+// cleared.  part[xi & 1] is rewritten at exchange xi + 2 only after every
+// rank's CTA signalled xi + 1, which it does after reading exchange xi.
+__device__ bool tp_exchange(const StepArgs& a, Ctl* ctl, int xi, float* own)
+{
+    const unsigned e = (unsigned)(ctl->base / gridDim.x) + (unsigned)xi + 1u;
+    const int tid = threadIdx.x;
+    if (tid == 0 && !ctl->abort) {
+        __threadfence_system();
+        for (int s = 0; s < a.P; s++) st_release_sys(a.peer_flag[s] + blockIdx.x, e);
+    }
+    if (tid < a.P && !ctl->abort) {
+        const unsigned* f = a.my_flag + (size_t)tid * TB_TP_STEP_CTAS + blockIdx.x;
+        long long it = 0;
+        while ((int)(ld_acquire_sys(f) - e) < 0) {
+            ++it;
+            if ((it & 255) == 0 && *reinterpret_cast<volatile unsigned*>(a.abort_word) == ctl->tag) {
+                ctl->abort = 1;
+                break;
+            }
+            if (it > STEP_WAIT_LIMIT) {
+                atomicExch(a.err, ERR_STEP_TP);
+                atomicExch(a.abort_word, ctl->tag);
+                ctl->abort = 1;
+                break;
+            }
+            if (it > 2048) __nanosleep(32);
+        }
+    }
+    __syncthreads();
+    if (ctl->abort) return false;
+    const int r0 = rowsC0(a), n = rowsC(a);
+    const float* const* parts = a.peer_part;
+    for (int i = tid; i < n; i += THREADS) {
+        float v = own[i];
+        for (int s = 0; s < a.P; s++) v += ld_volatile_f32(parts[s] + (size_t)(xi & 1) * a.H + r0 + i);
+        own[i] = v;
+        a.x[r0 + i] = v;
+    }
+    return true;
+}
+
 // the context S = pos + 1 was read and checked at the kernel's start (0 when pos
 // is outside the cache: every split empty), so the units read no position
 __device__ __forceinline__ AttnArgs attn_args(const StepArgs& a, const StepLayer& Ly, int S)
@@ -542,9 +614,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (tid == 0) request(a, ctl, BUF_P, 3, l, smem, bars);
             STAMP_REQ(2);
             if (n > 0) {
-                gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x, rowsC0(a), xo);
+                if (a.P > 1)    // this rank's partial rows -> its arena, then the exchange
+                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.xpart,
+                                       rowsC0(a), nullptr);
+                else
+                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x,
+                                       rowsC0(a), xo);
             }
             __syncthreads();
+            if (a.P > 1 && !tp_exchange(a, ctl, 2 * l, xo)) goto drain;
             STAMP(2, 3);
             if (!grid_sync(a, ctl)) goto drain;
             STAMP(2, 4);
@@ -578,9 +656,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
             STAMP_REQ(4);
             if (n > 0) {
-                gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
+                if (a.P > 1)
+                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.xpart + a.H,
+                                       rowsC0(a), nullptr);
+                else
+                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
+            if (a.P > 1 && !tp_exchange(a, ctl, 2 * l + 1, xo)) goto drain;
             STAMP(4, 3);
             if (more && !grid_sync(a, ctl)) goto drain;
             STAMP(4, 4);
@@ -608,7 +691,7 @@ struct tb_step_plan {
 // returns TB_ERR_UNSUPPORTED when it does not apply (the caller keeps the
 // multi-kernel step).
 int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I, int nsplit, int max_seq,
-                      int tern, tb_step_plan** out)
+                      int tern, int P, tb_step_plan** out)
 {
     *out = nullptr;
     const int G = ctx->num_sms;
@@ -623,6 +706,8 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     StepArgs a{};
     a.L = L; a.H = H; a.nHq = nHq; a.nKv = nKv; a.I = I; a.nsplit = nsplit; a.max_seq = max_seq;
     a.tern = tern ? 1 : 0;
+    a.P = P > 1 ? P : 1;
+    if (a.P > TB_TP_MAX || (a.P > 1 && G > TB_TP_STEP_CTAS)) return TB_ERR_UNSUPPORTED;
     a.rpC = (H + G - 1) / G;
     a.rpD = (I + G - 1) / G;
     if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
@@ -683,6 +768,18 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.bar_count = reinterpret_cast<unsigned long long*>(io->ctrl + 64); a.abort_word = io->ctrl + 128;
     a.err = ctx->dev_error;
     a.trace = reinterpret_cast<unsigned long long*>(io->trace);
+    const int P = io->P > 1 ? io->P : 1;
+    TB_REQUIRE(ctx, P == a.P && io->rank >= 0 && io->rank < P, "decode step: tensor-parallel ranks differ from the plan");
+    a.rank = io->rank;
+    if (P > 1) {
+        for (int s = 0; s < P; s++) {
+            TB_REQUIRE(ctx, io->tp_part[s] && io->tp_flags[s], "decode step: exchange arena of rank %d not mapped", s);
+            a.peer_part[s] = io->tp_part[s];
+            a.peer_flag[s] = io->tp_flags[s] + (size_t)a.rank * TB_TP_STEP_CTAS;
+        }
+        a.xpart = io->tp_part[a.rank];
+        a.my_flag = io->tp_flags[a.rank];
+    }
     void (*kern)(const StepArgs) = nullptr;
     if (a.tern) {
         switch (p->grp) {

@@ -9,6 +9,8 @@
 //   flag[P]      u32 epochs written by the peers ("my part for epoch e is ready")
 //   flag2[P]     the same for the argmax keys
 //   step         u32 steps completed (local)
+//   sflag[8][256] u32 epochs of the persistent decode step's per-CTA exchanges
+//                (tb_step.cu): row s, column c written by CTA c of rank s
 // An exchange: after the producing kernel finished (griddepcontrol.wait), rank
 // r stores epoch e into flag[r] of every rank with a system-scope release,
 // waits until its own flag[s] >= e for every s (acquire, bounded), then reads
@@ -107,11 +109,21 @@ __global__ void __launch_bounds__(32) k_tp_argmax_merge(const TpKeyArgs a)
 }  // namespace
 
 // ---- arena layout -----------------------------------------------------------
+static size_t tp_base_bytes(int64_t n)
+{
+    const size_t part = ((size_t)2 * n * 4 + 255) & ~size_t(255);
+    return part + 16 * 8 + 2 * TP_MAX * 4 + 256;
+}
+
 size_t tb_tp_arena_bytes(int P, int64_t n)
 {
     (void)P;
-    const size_t part = ((size_t)2 * n * 4 + 255) & ~size_t(255);
-    return part + 16 * 8 + 2 * TP_MAX * 4 + 256;
+    return ((tp_base_bytes(n) + 255) & ~size_t(255)) + (size_t)TB_TP_MAX * TB_TP_STEP_CTAS * 4;
+}
+
+unsigned* tb_tp_arena_step_flags(char* base, int64_t n)
+{
+    return reinterpret_cast<unsigned*>(base + ((tp_base_bytes(n) + 255) & ~size_t(255)));
 }
 
 void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long** keys, unsigned** flag,

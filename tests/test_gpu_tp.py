@@ -192,3 +192,89 @@ def test_tp2_prefill_matches_single_gpu(cuda):
                     full = _deq(single[1][l][i][b, :n], single[1][l][i + 1][b, :n])[:, r * w:(r + 1) * w]
                     rel = np.max(np.abs(got - full), axis=1) / np.max(np.abs(full), axis=1)
                     assert float(np.max(rel)) < 5e-2, (l, r, i, b)
+
+
+# ---- the persistent decode step under tensor parallelism ---------------------------
+# (the o / down rows' exchange inside the kernel, per CTA over the peer-mapped
+# exchange arenas) against the multi-kernel TP step on the same rank: same bits.
+WIDE1 = dict(hidden=2048, layers=2, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=6144, vocab=20000,
+             rope_theta=1e6, rms_eps=1e-6, max_seq=4200, batch=1)
+KIND_CASES = [(dict(CFG, batch=1), 9, False), (dict(CFG, batch=1, max_seq=1024, layers=3), 700, False),
+              (dict(CFG, batch=1), 9, True), (WIDE1, 4095, False)]
+
+
+def _run_kinds(rank, P, exchange, case):
+    """Rank `rank` of P over peer memory: three steps as one kernel per op,
+    then the same three steps (same start) as the persistent kernel."""
+    import tabinfer_b200 as tb
+    from tabinfer_b200 import _lib
+    cfg, n, ternary = KIND_CASES[case]
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    W = make_weights(cfg, 23, ternary=ternary)
+    m = tb.Qwen3(dict(cfg, tp_size=P, tp_rank=rank), device=rank)
+    for name, w in W.items():
+        m.load(name, torch.from_numpy(np.ascontiguousarray(w).view(np.int16)).to(dev))
+    rng = np.random.default_rng(29)
+    row = cfg["n_kv_heads"] * cfg["head_dim"]
+    w = row // P
+    for l in range(cfg["layers"]):
+        k = rng.standard_normal((n, row)).astype(np.float32)
+        v = rng.standard_normal((n, row)).astype(np.float32)
+        m.kv_fill(l, 0, torch.from_numpy(np.ascontiguousarray(k[:, rank * w:(rank + 1) * w])).to(dev),
+                  torch.from_numpy(np.ascontiguousarray(v[:, rank * w:(rank + 1) * w])).to(dev), 0)
+    hq, allq = exchange
+    hq.put((rank, m.tp_handle()))
+    m.tp_connect(allq.get(timeout=120))
+    out = {}
+    for mode in (_lib.QW_STEP_KERNELS, _lib.QW_STEP_PERSISTENT):
+        m.set_step_mode(mode)
+        m.set_tokens([321 % cfg["vocab"]], [n])
+        runs = []
+        for _ in range(3):
+            m.step()
+            runs.append((m.logits().numpy().copy(), *m.tokens()))
+        out[mode] = (m.step_kind(), runs)
+    err = m.ctx.device_error()
+    m.close()
+    return out, err
+
+
+def _rank_kinds(rank, P, q, exchange, case):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        q.put((rank, _run_kinds(rank, P, exchange, case)))
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", range(len(KIND_CASES)))
+def test_tp2_persistent_step_equals_kernels(cuda, case):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from tabinfer_b200 import _lib
+    ctx = mp.get_context("spawn")
+    q, hq = ctx.Queue(), ctx.Queue()
+    outs = [ctx.Queue() for _ in range(2)]
+    procs = [ctx.Process(target=_rank_kinds, args=(r, 2, q, (hq, outs[r]), case)) for r in range(2)]
+    for p in procs:
+        p.start()
+    hs = dict(hq.get(timeout=300) for _ in range(2))
+    for o in outs:
+        o.put([hs[0], hs[1]])
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+        out, err = res[r]
+        assert err == 0, "rank %d device error 0x%x" % (r, err)
+        kk, runs_k = out[_lib.QW_STEP_KERNELS]
+        kp, runs_p = out[_lib.QW_STEP_PERSISTENT]
+        assert kk == _lib.QW_STEP_KERNELS and kp == _lib.QW_STEP_PERSISTENT
+        for i, (a, b) in enumerate(zip(runs_k, runs_p)):
+            np.testing.assert_array_equal(b[0], a[0], err_msg="rank %d step %d" % (r, i))
+            assert b[1:] == a[1:], (r, i)
+    assert [x[1:] for x in res[0][0][_lib.QW_STEP_PERSISTENT][1]] == \
+        [x[1:] for x in res[1][0][_lib.QW_STEP_PERSISTENT][1]]
