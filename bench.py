@@ -649,6 +649,220 @@ def tern_extra(dev, peak_gbs, peak_tf, stream):
 
 
 # ---------------------------------------------------------------------------
+# ternary Q2_0_g64 decode GEMV: the Bonsai-1.7B layer matrices in the
+# n2-core binfmt layout, on the B200 and on the host cores
+# ---------------------------------------------------------------------------
+BONSAI_MATS = [("qkv", 4096, 2048), ("o", 2048, 2048), ("gate", 6144, 2048), ("up", 6144, 2048),
+               ("down", 2048, 6144)]
+BONSAI_LAYERS = 28
+
+
+def q2g64_bytes(N, K, B=1):
+    """Q2_0_g64 GEMV algorithmic bytes: 2-bit codes (K/4 bytes a row) and one f32
+    scale per 64 read once, B int8 activation rows with their i32 sums per 64 in,
+    B f32 rows out (0.3125 B a weight + activations)."""
+    return N * K // 4 + N * (K // 64) * 4 + B * (K + (K // 64) * 4 + N * 4)
+
+
+def _q2g64_pack(dev, g, N, K):
+    """configs[0] weights: t in {-1, 0, +1} with p = 1/3 each times a per-64-group
+    scale U(0.01, 0.05) rounded to f16, packed by the product's tb_pack_tern_q2g64
+    (tern.rs pack_ternary): codes t + 1, scales s exactly."""
+    import torch
+    import tabinfer_b200 as tb
+    t = torch.randint(0, 3, (N, K), device=dev, generator=g, dtype=torch.int32).float() - 1.0
+    s = (torch.rand(N, K // 64, device=dev, generator=g) * 0.04 + 0.01).half().float()
+    w = t * s.repeat_interleave(64, dim=1)
+    del t
+    return tb.pack_ternary(w)
+
+
+def _record_batch(ctx, dev, fn):
+    """fn's launches recorded once as a replayable tb_batch on the context's own
+    stream (so the timed replays are not bound by Python launch overhead)."""
+    import torch
+    from tabinfer_b200._lib import LIB, P
+    stream = torch.cuda.ExternalStream(ctx.own_stream(), device=dev)
+    with torch.cuda.stream(stream):
+        fn()
+        stream.synchronize()
+        ctx.check(LIB.tb_batch_begin(ctx.h), "batch_begin")
+        fn()
+        h = P()
+        ctx.check(LIB.tb_batch_end(ctx.h, ctypes.byref(h)), "batch_end")
+    return h, stream
+
+
+def _replay_ms(ctx, h, stream, reps):
+    """ms per replay of a recorded batch: CUDA events on its stream around `reps`
+    back-to-back replays, after three untimed ones."""
+    import torch
+    from tabinfer_b200._lib import LIB
+    for _ in range(3):
+        ctx.check(LIB.tb_batch_submit(ctx.h, h), "submit")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        ctx.check(LIB.tb_batch_submit(ctx.h, h), "submit")
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def q2g64_extra(dev, ctx, peak_gbs):
+    """configs[0] on the B200: tb_gemv_tern_q2g64 (batch 1) over the Bonsai-1.7B
+    layer matrices.  28 layer copies (440 MB, > 3x L2) are swept in order, each
+    matrix one launch, recorded once and replayed; a launch therefore reads its
+    weights from HBM, as in decode.  Also the kernel alone on a 151936 x 2048
+    (lm_head-sized) matrix, rotated over three copies."""
+    import torch
+    import tabinfer_b200 as tb
+    from tabinfer_b200._lib import LIB
+    g = torch.Generator(device=dev).manual_seed(31)
+    layers = [{n: _q2g64_pack(dev, g, N, K) for n, N, K in BONSAI_MATS} for _ in range(BONSAI_LAYERS)]
+    acts = {}
+    for K in sorted({K for _, _, K in BONSAI_MATS} | {Q17["hidden"]}):
+        x = torch.randn(1, K, device=dev, generator=g)
+        acts[K] = tb.quantize_act(x)[:2]
+    outs = {n: torch.empty(1, N, device=dev) for n, N, _ in BONSAI_MATS}
+    dims = {n: (N, K) for n, N, K in BONSAI_MATS}
+
+    def gemv(name, L):
+        codes, scales = L[name]
+        act, xsum = acts[dims[name][1]]
+        tb.gemv_tern(codes, scales, act, xsum, out=outs[name])
+
+    res = {}
+    reps = 30
+    h, stream = _record_batch(ctx, dev, lambda: [gemv(n, L) for L in layers for n, _, _ in BONSAI_MATS])
+    ms = _replay_ms(ctx, h, stream, reps)
+    LIB.tb_batch_destroy(h)
+    lb = sum(q2g64_bytes(N, K) for _, N, K in BONSAI_MATS)
+    gbs = lb * BONSAI_LAYERS / (ms * 1e-3) / 1e9
+    macs = sum(N * K for _, N, K in BONSAI_MATS)
+    res["layer_sweep"] = {"us_per_layer": round(ms * 1e3 / BONSAI_LAYERS, 3), "bytes_per_layer": lb,
+                          "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak_gbs, 4),
+                          "gmacs": round(macs * BONSAI_LAYERS / (ms * 1e-3) / 1e9, 1),
+                          "launches_per_layer": len(BONSAI_MATS)}
+    per = {}
+    for n, N, K in BONSAI_MATS:
+        h, stream = _record_batch(ctx, dev, lambda: [gemv(n, L) for L in layers])
+        msn = _replay_ms(ctx, h, stream, reps) / BONSAI_LAYERS
+        LIB.tb_batch_destroy(h)
+        b = q2g64_bytes(N, K)
+        per[n] = {"N": N, "K": K, "us": round(msn * 1e3, 3), "bytes": b, "gbs": round(b / (msn * 1e-3) / 1e9, 1),
+                  "frac_of_peak": round(b / (msn * 1e-3) / 1e9 / peak_gbs, 4),
+                  "gmacs": round(N * K / (msn * 1e-3) / 1e9, 1)}
+    res["per_matrix"] = per
+    del layers
+    torch.cuda.synchronize(dev)
+    V, H = Q17["vocab"], Q17["hidden"]
+    big = [_q2g64_pack(dev, g, V, H) for _ in range(3)]
+    yb = torch.empty(1, V, device=dev)
+    act, xsum = acts[H]
+    h, stream = _record_batch(ctx, dev, lambda: [tb.gemv_tern(c, s, act, xsum, out=yb) for c, s in big])
+    msb = _replay_ms(ctx, h, stream, 20) / 3
+    LIB.tb_batch_destroy(h)
+    b = q2g64_bytes(V, H)
+    res["lm_head_151936x2048"] = {"us": round(msb * 1e3, 2), "bytes": b, "gbs": round(b / (msb * 1e-3) / 1e9, 1),
+                                  "frac_of_peak": round(b / (msb * 1e-3) / 1e9 / peak_gbs, 4)}
+    del big
+    torch.cuda.synchronize(dev)
+    res["timing"] = ("recorded launches replayed back to back (PDL on), CUDA events on the launching stream; weights "
+                     "rotated over > 2x L2 (28 layer copies, 3 lm_head copies); bytes = 0.3125 B a weight + int8 "
+                     "activation, i32 sums and f32 output")
+    return res
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _llc_bytes():
+    try:
+        v = os.sysconf("SC_LEVEL3_CACHE_SIZE")
+        if v and v > 0:
+            return int(v)
+    except (ValueError, OSError):
+        pass
+    return 64 << 20
+
+
+def cpu_q2g64(budget_s=12.0):
+    """configs[0] on the host cores: the reference's ternary GEMV backends,
+    transcribed to C (oracle/tb_cpu_ref.c: tern.rs scalar :100-140 and AVX2
+    :268-338), over the same Bonsai-1.7B layer matrices.  The weight copies
+    together exceed 4x the last-level cache (DRAM-streaming, the regime
+    native/docs/ROADMAP.md:11-27 says predicts decode).  Discipline of
+    n2-kernels/src/timing.rs: warm-up, alternating order every repetition, min
+    over repetitions, and a base-vs-base control whose ratio must read ~1.000."""
+    import itertools
+    import oracle
+    lib = oracle.cpuref()
+    rng = np.random.default_rng(0x9E3779B9)
+    lut = np.array([a | (b << 2) | (c << 4) | (d << 6) for a, b, c, d in itertools.product(range(3), repeat=4)],
+                   np.uint8)
+    layer_b = sum(q2g64_bytes(N, K) for _, N, K in BONSAI_MATS)
+    ws = min(max(256 << 20, 4 * _llc_bytes()), 640 << 20)
+    nl = max(2, -(-ws // layer_b))
+    mats = []
+    for _ in range(nl):
+        for n, N, K in BONSAI_MATS:
+            codes = lut[rng.integers(0, 81, N * K // 4, dtype=np.uint8)]
+            scales = np.float16(rng.uniform(0.01, 0.05, N * (K // 64))).astype(np.float32)
+            mats.append((N, K, codes, scales))
+    acts = {}
+    for K in {K for _, _, K in BONSAI_MATS}:
+        acts[K] = (rng.integers(-127, 128, K).astype(np.int8), rng.integers(-2000, 2000, K // 64).astype(np.int32))
+    outs = {N: np.zeros(N, np.float32) for _, N, _ in BONSAI_MATS}
+    P = ctypes.c_void_p
+    threads_all = os.cpu_count() or 1
+
+    def sweep(fn, threads):
+        t0 = time.perf_counter()
+        for N, K, codes, scales in mats:
+            act, xsum = acts[K]
+            fn(P(outs[N].ctypes.data), P(codes.ctypes.data), P(scales.ctypes.data), P(act.ctypes.data),
+               P(xsum.ctypes.data), ctypes.c_int64(N), ctypes.c_int64(K), ctypes.c_int(threads))
+        return time.perf_counter() - t0
+
+    variants = [("avx2_1t", lib.tbr_gemv_tern_avx2, 1), ("avx2_1t_control", lib.tbr_gemv_tern_avx2, 1),
+                ("scalar_1t", lib.tbr_gemv_tern_scalar, 1), ("avx2_all", lib.tbr_gemv_tern_avx2, threads_all)]
+    for _, fn, th in variants:          # warm-up
+        sweep(fn, th)
+    best = {v[0]: float("inf") for v in variants}
+    reps = 0
+    t0 = time.perf_counter()
+    while reps < 3 or (time.perf_counter() - t0 < budget_s and reps < 50):
+        order = variants if reps % 2 == 0 else variants[::-1]
+        for name, fn, th in order:
+            best[name] = min(best[name], sweep(fn, th))
+        reps += 1
+    macs = sum(N * K for N, K, _, _ in mats)
+    nbytes = sum(q2g64_bytes(N, K) for N, K, _, _ in mats)
+    out = {}
+    for name, _, th in variants:
+        if name == "avx2_1t_control":
+            continue
+        out[name] = {"threads": th, "gmacs": round(macs / best[name] / 1e9, 2),
+                     "gbs": round(nbytes / best[name] / 1e9, 2), "ms_per_layer": round(best[name] * 1e3 / nl, 3)}
+    out["control_ratio"] = round(best["avx2_1t"] / best["avx2_1t_control"], 3)
+    out.update({"kind": "port", "reps": reps, "layer_copies": nl, "working_set_mb": round(nbytes / 2 ** 20, 1),
+                "cpu_model": _cpu_model(), "nproc": threads_all,
+                "reference_published": "AVX2 1 thread DRAM-streaming 15.32 GMAC/s ~ 4.8 GB/s, scalar 2.69 GMAC/s "
+                                       "(i5-1235U, native/docs/ROADMAP.md:17-25)",
+                "sample": "the 5 Bonsai-1.7B layer GEMVs over %d layer copies per repetition, min of %d "
+                          "alternating-order repetitions" % (nl, reps)})
+    return out
+
+
+# ---------------------------------------------------------------------------
 # profiling cases (for ncu on a small case)
 # ---------------------------------------------------------------------------
 
@@ -868,6 +1082,42 @@ def prefill_forward_extra(dev, stream, T=2048):
     return {"tokens": T, "ms": round(ms, 3), "tok_per_s": round(T / (ms * 1e-3), 1)}
 
 
+def prefill_forward_tp_extra(dev, stream, world, rank, dist, T=2048):
+    """forward(ids, 0) at T tokens of Qwen3-1.7B tensor-parallel over the world
+    (column-split q/k/v and gate/up, row-split o/down with an NCCL allreduce of
+    the prompt rows after each, vocab-split lm_head): prompt tokens per second,
+    device time max over ranks.  Every rank runs every step."""
+    import torch
+    from tabinfer_b200.qwen3 import nccl_unique_id
+    m = build_model(Q17, dev, 1, T + 16, 16, world, rank, seed=91)
+    uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        uid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    m.tp_init(bytes(uid.cpu().numpy().tobytes()))
+    ids = list(np.random.default_rng(3).integers(0, Q17["vocab"], T))
+    m.prefill(0, ids, 0)
+    torch.cuda.synchronize(dev)
+    ts = []
+    for _ in range(3):
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m.prefill(0, ids, 0)
+        e1.record(stream)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ts.append(float(t.item()))
+    err = m.ctx.device_error()
+    m.close()
+    del m
+    torch.cuda.synchronize(dev)
+    ms = statistics.median(ts)
+    return {"tokens": T, "tp": world, "ms": round(ms, 3), "tok_per_s": round(T / (ms * 1e-3), 1),
+            "device_error": err, "timing": "CUDA events per rank, max over ranks, median of 3"}
+
+
 def prefill_attn_extra(dev, peak_tf, stream):
     """int8-KV prefill attention of one Qwen3-1.7B layer (16 q / 8 kv heads of
     128) over T = S = 512 / 2048 / 8192: TFLOP/s of the causal 4 * pairs * hd * heads."""
@@ -1041,7 +1291,7 @@ def run_reference(args, rank, world):
     line = {"metric": "Qwen3-1.7B int4 decode tok/s (context %d, batch %d)" % (args.context, args.batch),
             "impl": "reference", "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1e3 * args.batch / v, 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4xint8->int32,f32", "data": "synthetic",
             "config": {"workload": "qwen3-1.7b int4 decode step", "batch": args.batch, "context": args.context},
             "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": sample},
@@ -1298,16 +1548,30 @@ def main():
                          "%.1f s, scaled to the full step; C transcription of the JS linearQ int4 math, 1 thread; "
                          "attention excluded" % (reps, dt)}
 
+    if world == 1 and rank == 0 and not args.no_extras:
+        for Bc in (4, 8):
+            ch = chain_gbs(dev, ctx, Bc, max(100, args.steps))
+            ch["frac_of_peak"] = round(ch["gbs"] / peak, 4)
+            ch["tok_per_s"] = round(Bc * 1e3 / ch["ms_per_step"], 1)
+            extras["gemv_chain_0.6b_batch%d" % Bc] = ch
+        q2 = q2g64_extra(dev, ctx, peak)
+        q2["cpu_baseline"] = cpu_q2g64(12.0)
+        extras["ternary_q2g64_bonsai_1.7b"] = q2
+
     if not args.no_extras:          # every rank: the expert-parallel exchange needs all of them
         ep_out = moe_ep_extra(dev, world, rank, stream, peak, dist)
         if rank == 0:
             extras["moe_ep_lfm2.5"] = ep_out
+        if world > 1:
+            pf = prefill_forward_tp_extra(dev, stream, world, rank, dist)
+            if rank == 0:
+                extras["prefill_forward_1.7b_tp"] = pf
 
     if rank == 0:
         line = {"metric": "Qwen3-1.7B int4 decode tok/s (context %d, batch %d)" % (S, B), "value": round(value, 2),
                 "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+                "vs_baseline": None, "dtype": "int4xint8->int32,f32", "data": "synthetic",
                 "config": {"workload": "qwen3-1.7b int4 decode step (28 layers, int8 KV, tied lm_head)",
                            "batch": B, "context": S, "hidden": Q17["hidden"], "layers": Q17["layers"],
                            "heads": "%d q / %d kv x %d" % (Q17["n_heads"], Q17["n_kv_heads"], Q17["head_dim"]),

@@ -348,8 +348,9 @@ TB_API int tb_attn_decode_q8(tb_ctx *ctx, float *out, const float *qr,
  * own pool at start-up, or a loop that must not let an allocation synchronize
  * the device mid-step).  No counterpart in the reference.  The split partials
  * live in a fixed 1 MiB device array inside the library instead of context
- * scratch: requests with nHq*nsplit*(hd+2) > 262144 floats are rejected with
- * TB_ERR_INVALID.  The first call on a device looks up the array's address
+ * scratch: an explicit nsplit with nHq*nsplit*(hd+2) > 262144 floats is
+ * rejected with TB_ERR_INVALID; nsplit = 0 picks the automatic split count
+ * capped at what fits.  The first call on a device looks up the array's address
  * (make it before any stream capture); calls share the array, so calls that
  * overlap on the GPU race and must be ordered by the caller. */
 TB_API int tb_attn_decode_q8_noalloc(tb_ctx *ctx, float *out, const float *qr,

@@ -298,6 +298,18 @@ def gemv_tern_dequant(codes, scales, act):
     return out
 
 
+def gemv_tern_scalar_timed(codes, scales, act, xsum, threads=1):
+    """The transcribed scalar backend (tern.rs:100-140) of the timed CPU
+    baseline, built -O3; single activation row."""
+    N = codes.shape[0]
+    K = act.shape[-1]
+    out = np.zeros(N, np.float32)
+    cpuref().tbr_gemv_tern_scalar(_ptr(out), _ptr(np.ascontiguousarray(codes)), _ptr(np.ascontiguousarray(scales)),
+                                  _ptr(np.ascontiguousarray(act, np.int8)), _ptr(np.ascontiguousarray(xsum, np.int32)),
+                                  _I(N), _I(K), ctypes.c_int(threads))
+    return out
+
+
 def gemv_tern_avx2(codes, scales, act, xsum, threads=1):
     """The transcribed AVX2 backend (tern.rs:268-338), single activation row."""
     N = codes.shape[0]

@@ -6,6 +6,7 @@
  *
  * The reference's own CPU code cannot run here (no cargo, no node), so these
  * are faithful transcriptions:
+ *   - tbr_gemv_tern_scalar: tern.rs:100-140 (gemv_tern_scalar), plain loops;
  *   - tbr_gemv_tern_avx2: native/crates/n2-kernels/src/tern.rs:268-338, the
  *     same AVX2 intrinsics (vpmaddubsw + vpmaddwd, two 64-blocks per 256-bit
  *     step, scale lanes split per 128-bit half, one horizontal sum per row);
@@ -73,6 +74,33 @@ static void tern_rows_avx2(float *out, const uint8_t *codes, const float *scales
             for (int j = 0; j < 4; j++)
                 for (int i = 0; i < 16; i++)
                     dot += (int32_t)((rc[b * 16 + i] >> (2 * j)) & 3) * (int32_t)act[b * 64 + j * 16 + i];
+            acc += rs[b] * (float)dot;
+            sxs += rs[b] * (float)xsum[b];
+        }
+        out[row] = acc - sxs;
+    }
+}
+
+/* ---------------- ternary Q2_0_g64, scalar (tern.rs:100-140) --------------
+ * Per row: for every 64-block the exact i32 dot of the unsigned codes with the
+ * int8 activations, plane j (bits 2j of each byte) holding codes j*16..j*16+15;
+ * acc += s*dot and sxs += s*xsum in block order, out = acc - sxs. */
+static void tern_rows_scalar(float *out, const uint8_t *codes, const float *scales,
+                             const int8_t *act, const int32_t *xsum,
+                             int64_t r0, int64_t r1, int64_t K)
+{
+    const int64_t nb = K / 64, bpr = K / 4;
+    for (int64_t row = r0; row < r1; row++) {
+        const uint8_t *rc = codes + row * bpr;
+        const float *rs = scales + row * nb;
+        float acc = 0.0f, sxs = 0.0f;
+        for (int64_t b = 0; b < nb; b++) {
+            const uint8_t *blk = rc + b * 16;
+            const int8_t *ab = act + b * 64;
+            int32_t dot = 0;
+            for (int j = 0; j < 4; j++)
+                for (int i = 0; i < 16; i++)
+                    dot += (int32_t)((blk[i] >> (2 * j)) & 3) * (int32_t)ab[j * 16 + i];
             acc += rs[b] * (float)dot;
             sxs += rs[b] * (float)xsum[b];
         }
@@ -150,7 +178,7 @@ static void quant_q8_row(const float *x, int64_t K, int8_t *xq, float *xs)
 
 /* ---------------- row-partitioned worker pool ------------------------------ */
 
-enum { JOB_TERN = 0, JOB_INT4_F32 = 1, JOB_INT4_Q8 = 2 };
+enum { JOB_TERN = 0, JOB_INT4_F32 = 1, JOB_INT4_Q8 = 2, JOB_TERN_SCALAR = 3 };
 #define CHUNK_ROWS 128
 
 typedef struct {
@@ -172,6 +200,10 @@ static void run_rows(job_t *j, int64_t r0, int64_t r1)
     case JOB_TERN:
         tern_rows_avx2(j->out, (const uint8_t *)j->w, (const float *)j->s, (const int8_t *)j->x,
                        j->xsum, r0, r1, j->K);
+        break;
+    case JOB_TERN_SCALAR:
+        tern_rows_scalar(j->out, (const uint8_t *)j->w, (const float *)j->s, (const int8_t *)j->x,
+                         j->xsum, r0, r1, j->K);
         break;
     case JOB_INT4_F32:
         int4_rows_f32(j->out, (const float *)j->x, (const uint32_t *)j->w, (const uint16_t *)j->s,
@@ -214,6 +246,15 @@ TBR_API void tbr_gemv_tern_avx2(float *out, const uint8_t *codes, const float *s
                                 int threads)
 {
     job_t j = {JOB_TERN, N, K, 0, out, codes, scales, act, NULL, xsum, 0};
+    run_job(&j, threads);
+}
+
+/* Ternary GEMV, scalar backend (tern.rs gemv_tern_scalar) over N rows. */
+TBR_API void tbr_gemv_tern_scalar(float *out, const uint8_t *codes, const float *scales,
+                                  const int8_t *act, const int32_t *xsum, int64_t N, int64_t K,
+                                  int threads)
+{
+    job_t j = {JOB_TERN_SCALAR, N, K, 0, out, codes, scales, act, NULL, xsum, 0};
     run_job(&j, threads);
 }
 

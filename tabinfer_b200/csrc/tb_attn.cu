@@ -310,8 +310,10 @@ TB_API int tb_attn_decode_q8_batch(tb_ctx* ctx, float* out, const float* qr, con
 // partials live in the file-scope array below, sized at NOALLOC_SCRATCH_FLOATS
 // floats (1 MiB), which every GPU that loads this library holds until exit.
 //  * Limit: nHq * nsplit * (hd + 2) <= NOALLOC_SCRATCH_FLOATS (Qwen3-1.7B, 16 q
-//    heads x hd 128, fits up to 126 splits); larger requests are rejected with
-//    TB_ERR_INVALID before anything is enqueued.
+//    heads x hd 128, fits up to 126 splits); an explicit split count beyond it is
+//    rejected with TB_ERR_INVALID before anything is enqueued.  With nsplit = 0
+//    the automatic split count is capped at what fits, so wide models (64 q heads
+//    at long context) still run, with fewer splits.
 //  * The device address of the array is looked up once per device, on the first
 //    call made on that device (cudaGetSymbolAddress with the device current); make
 //    that first call before any stream capture.
@@ -366,7 +368,10 @@ extern "C" TB_API int tb_attn_decode_q8_noalloc(tb_ctx* ctx, float* out, const f
     int rc = tb_attn_check(ctx, qr, Kq, Ks, Vq, Vs, S, nHq, nKv, hd, nsplit);
     if (rc) return rc;
     TB_REQUIRE(ctx, out != nullptr && TB_ALIGNED(out, 16), "output must be non-null and 16-byte aligned");
-    if (nsplit == 0) nsplit = tb_attn_auto_nsplit(ctx, S, nKv);
+    if (nsplit == 0) {
+        const int64_t fit = (int64_t)(NOALLOC_SCRATCH_FLOATS / (size_t)(nHq * (hd + 2)));
+        nsplit = (int)std::max<int64_t>(1, std::min<int64_t>(tb_attn_auto_nsplit(ctx, S, nKv), fit));
+    }
     const size_t need = (size_t)nHq * nsplit * (hd + 2);
     if (need > NOALLOC_SCRATCH_FLOATS)
         return tb_fail(ctx, TB_ERR_INVALID,

@@ -62,6 +62,15 @@ def test_avx2_transcription_matches_scalar():
         np.testing.assert_array_equal(b, c)
 
 
+def test_timed_scalar_baseline_is_the_oracle_scalar():
+    """The timed scalar baseline (-O3 build) gives the oracle's gemv_tern_scalar bits."""
+    for n, k in [(1, 64), (5, 192), (64, 2048)]:
+        codes, scales, act, xsum, _, _ = oracle.tern_fixture(n, k, 0xBEEF + k)
+        a = oracle.gemv_tern_scalar(codes, scales, act, xsum)[0]
+        np.testing.assert_array_equal(oracle.gemv_tern_scalar_timed(codes, scales, act, xsum), a)
+        np.testing.assert_array_equal(oracle.gemv_tern_scalar_timed(codes, scales, act, xsum, threads=3), a)
+
+
 def test_selftest_shapes():
     """n2 selftest (main.rs:116-160), seed 0x9E3779B97F4A7C15."""
     for n, k in [(1, 64), (3, 192), (17, 256), (64, 2048)]:
