@@ -616,6 +616,16 @@ TB_API int tb_qwen3_tp_init(tb_qwen3 *m, const void *unique_id128);
  * device error word); the result is identical on every rank. */
 TB_API int tb_qwen3_tp_handle(tb_qwen3 *m, void *out64);
 TB_API int tb_qwen3_tp_connect(tb_qwen3 *m, const void *handles);
+/* After a device-side exchange wait gave up under tensor parallelism (the
+ * device error word reads 0x5103 / 0x7a01, tb_ctx_device_error returns
+ * TB_ERR_TIMEOUT), the ranks' exchange epochs may disagree, so the rank
+ * poisons itself: every later step on it does nothing and reports 0x5104
+ * (persistent step) or 0x7a02 (exchange kernels) until this reset.  It clears
+ * this rank's exchange arena, step control words and attention counters and
+ * synchronizes.  Call it on every rank, with every rank's stream idle and
+ * behind a host barrier, and step again only after every rank returned from it.
+ * No reference counterpart (the reference has no tensor parallelism). */
+TB_API int tb_qwen3_tp_reset(tb_qwen3 *m);
 TB_API int tb_qwen3_decode_step(tb_qwen3 *m);
 /* Kernels of this library in one recorded step, and NCCL collectives. */
 TB_API int tb_qwen3_launches_per_step(tb_qwen3 *m, int *kernels, int *collectives);

@@ -105,6 +105,7 @@ SIGNATURES = {
     "tb_qwen3_step_trace": [P, P],
     "tb_qwen3_tp_handle": [P, P],
     "tb_qwen3_tp_connect": [P, P],
+    "tb_qwen3_tp_reset": [P],
     "tb_qwen3_decode_step": [P],
     "tb_qwen3_launches_per_step": [P, ctypes.POINTER(I32), ctypes.POINTER(I32)],
 }

@@ -41,11 +41,11 @@ int tb_quant_int4_strided_impl(tb_ctx* ctx, const uint16_t* w, int64_t ld, uint3
 
 // tensor-parallel exchanges over IPC-mapped peer arenas (tb_tp.cu)
 size_t tb_tp_arena_bytes(int P, int64_t n);
-// the persistent decode step's per-CTA exchange flags in an arena: u32
-// [TB_TP_MAX][TB_TP_STEP_CTAS], row s written by rank s's CTAs (zero at creation)
+// the persistent decode step's exchange inbox in an arena: u64
+// [TB_TP_MAX][2][n] packets (epoch << 32 | f32 bits), row s written by rank s
+// (zero at creation and after tb_qwen3_tp_reset)
 constexpr int TB_TP_MAX = 8;
-constexpr int TB_TP_STEP_CTAS = 256;
-unsigned* tb_tp_arena_step_flags(char* base, int64_t n);
+unsigned long long* tb_tp_arena_step_inbox(char* base, int64_t n);
 void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long** keys, unsigned** flag,
                         unsigned** flag2, unsigned** step);
 int tb_tp_allreduce_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, float* x, int xi, int nx);
@@ -97,8 +97,9 @@ struct tb_step_io {
     // tensor parallel over peer memory (P > 1): every rank's exchange-arena part
     // buffers (f32 [2][hidden]) and step flags, mapped here; this rank's index
     int P, rank;
-    float* tp_part[TB_TP_MAX];
-    unsigned* tp_flags[TB_TP_MAX];
+    float* xpart;                              // this rank's part[2][hidden]
+    unsigned long long* tp_inbox[TB_TP_MAX];   // every rank's inbox [TB_TP_MAX][2][hidden]
+    unsigned* tp_poison;                       // this rank's poison word (step[1] of its arena)
 };
 // tern: the layer weights are ternary (WebGPU layout) instead of int4 G32
 // P > 1: this rank's shard of a tensor-parallel model (nHq, nKv, I per rank)

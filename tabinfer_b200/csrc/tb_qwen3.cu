@@ -332,12 +332,11 @@ tb_step_io step_io(tb_qwen3* m)
     io.rank = m->r;
     if (m->P > 1) {
         const int64_t n = (int64_t)m->c.batch * m->c.hidden;
-        for (int s = 0; s < m->P; s++) {
-            float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
-            tb_tp_arena_layout(m->peer_arena[s], n, &part, &keys, &flag, &flag2, &step);
-            io.tp_part[s] = part;
-            io.tp_flags[s] = tb_tp_arena_step_flags(m->peer_arena[s], n);
-        }
+        for (int s = 0; s < m->P; s++) io.tp_inbox[s] = tb_tp_arena_step_inbox(m->peer_arena[s], n);
+        float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
+        tb_tp_arena_layout(m->arena, n, &part, &keys, &flag, &flag2, &step);
+        io.xpart = part;
+        io.tp_poison = step + 1;
     }
     return io;
 }
@@ -949,6 +948,29 @@ TB_API int tb_qwen3_tp_connect(tb_qwen3* m, const void* handles)
     }
     release_graph(m);
     m->p2p = true;
+    return TB_OK;
+}
+
+// Recovery after a device-side wait gave up under tensor parallelism: the
+// exchanges' epochs may disagree between the ranks from then on, so the rank
+// poisoned itself and its exchanges refuse to run.  This clears this rank's
+// exchange arena (partials, flags, step counter, poison word, inbox), the
+// persistent step's barrier and abort words and the attention split counters,
+// and waits for it.  Contract: call it on EVERY rank, after every rank's stream
+// is idle (no step in flight anywhere) and behind a host barrier, and let no
+// rank step again until every rank has returned from it (a second barrier).
+TB_API int tb_qwen3_tp_reset(tb_qwen3* m)
+{
+    if (!m) return TB_ERR_INVALID;
+    tb_ctx* ctx = m->ctx;
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e == cudaSuccess && m->arena)
+        e = cudaMemsetAsync(m->arena, 0, tb_tp_arena_bytes(m->P, (int64_t)m->c.batch * m->c.hidden), ctx->stream);
+    if (e == cudaSuccess && m->step_ctrl) e = cudaMemsetAsync(m->step_ctrl, 0, 256 * 4, ctx->stream);
+    if (e == cudaSuccess && m->counters)
+        e = cudaMemsetAsync(m->counters, 0, (size_t)m->c.batch * m->nKv * sizeof(unsigned), ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "tp_reset: %s", cudaGetErrorString(e));
     return TB_OK;
 }
 

@@ -30,11 +30,11 @@
 // tb_attn_dev.cuh) with the same split count, so the step is bit-identical to
 // the multi-kernel step.  Under tensor parallelism over peer memory each rank
 // runs this kernel on its shard: the o and down rows are partial sums, and CTA c
-// exchanges its slice of them with CTA c of every rank inside the kernel (its
-// own arena's part buffer, a system-scope release flag per rank, a bounded
-// acquire wait, then x + part_0 + ... + part_{P-1} in rank order, the sum of the
-// exchange kernel k_tp_allreduce), so the step is one kernel per rank and the
-// same bits as the multi-kernel TP step.  The layer weights are all int4 G32
+// exchanges its slice of them with CTA c of every rank inside the kernel (each
+// row pushed to every peer's inbox as one 8-byte (epoch, value) packet, a
+// bounded wait on local loads, then x + part_0 + ... + part_{P-1} in rank order,
+// the sum of the exchange kernel k_tp_allreduce), so the step is one kernel per
+// rank and the same bits as the multi-kernel TP step.  The layer weights are all int4 G32
 // or all ternary in the WebGPU layout (TERN: 8 code bytes a 32-group, the
 // activations QUANTQ8'd in natural order, item_ternx instead of item_q8x), as
 // gemvTern / gemvQ8 of the multi-kernel step.  Barrier and copy waits are bounded; a CTA that gives up
@@ -49,6 +49,7 @@ namespace {
 constexpr int ERR_STEP_BARRIER = 0x5101;
 constexpr int ERR_STEP_COPY = 0x5102;
 constexpr int ERR_STEP_TP = 0x5103;
+constexpr int ERR_STEP_TP_POISONED = 0x5104;   // refused: an earlier exchange wait of this rank gave up
 constexpr long long STEP_WAIT_LIMIT = 1LL << 21;   // barrier polls of ~0.5 us: ~1 s
 constexpr int RBA = 32;                              // rows of a phase-A block (a head has hd/32 blocks)
 constexpr int STEP_HD = 128;
@@ -90,10 +91,10 @@ struct StepArgs {
     // heads / intermediate slice; CTA c exchanges its rows with CTA c of every rank
     // through the ranks' exchange arenas (peer memory over NVLink)
     int P, rank;
-    float* xpart;                       // this rank's part[2][H]
-    const float* peer_part[TB_TP_MAX];  // every rank's part[2][H] (own at [rank])
-    unsigned* peer_flag[TB_TP_MAX];     // this rank's row of every rank's step flags
-    const unsigned* my_flag;            // this rank's step flags [TB_TP_MAX][TB_TP_STEP_CTAS]
+    float* xpart;                                 // this rank's part[2][H]
+    unsigned long long* peer_inbox[TB_TP_MAX];    // every rank's inbox [TB_TP_MAX][2][H]
+    const unsigned long long* my_inbox;           // this rank's inbox
+    unsigned* poison;                             // this rank's poison word
 };
 
 __device__ __forceinline__ void stamp(const StepArgs& a, int slot)
@@ -386,56 +387,78 @@ __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, i
 }
 
 // ---- tensor-parallel exchange of the o / down rows ----------------------------------
-__device__ __forceinline__ float ld_volatile_f32(const float* p)
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v)
 {
-    float v;
-    asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
 // After this CTA stored its partial rows of exchange xi (rows rowsC0 .. +rowsC)
-// into its own arena's part[xi & 1] and the caller's __syncthreads: publish
-// them to CTA blockIdx.x of every rank (system-scope release of epoch e into
-// this rank's flag slot in every arena), wait for every rank's slot to reach e
-// (acquire, bounded), then own = own + part_0 + ... + part_{P-1} in rank order,
-// the sum k_tp_allreduce forms, into the CTA's residual rows and x.
-// e = (barriers before this launch) + xi + 1: every launch passes 5L barriers
-// and has 2L exchanges, so epochs grow across launches and the flags are never
-// cleared.  part[xi & 1] is rewritten at exchange xi + 2 only after every
-// rank's CTA signalled xi + 1, which it does after reading exchange xi.
-__device__ bool tp_exchange(const StepArgs& a, Ctl* ctl, int xi, float* own)
+// into its own arena's part[xi & 1] and the caller's __syncthreads: push every
+// row to every other rank as one 8-byte packet (e << 32) | f32 bits into that
+// rank's inbox[this rank][xi & 1][row] (plain NVLink stores, no fence: the epoch
+// travels in the same store as the value, so a packet is complete the moment it
+// is seen), then wait (bounded) until this rank's inbox holds epoch e for every
+// other rank's rows of this CTA -- local loads only -- and form
+// x + part_0 + ... + part_{P-1} in rank order, the sum k_tp_allreduce forms,
+// into the CTA's residual rows and x.
+// e = (barriers before this launch) + xi + 1: a launch passes 5L >= 2L + 1
+// barriers and has 2L exchanges, so epochs grow across launches; a slot holds
+// epoch e - 2 or e, never more (a rank sends exchange xi + 2 only after it
+// received every rank's xi + 1, sent after that rank consumed xi), so the wait
+// is for equality.  A wait that gives up aborts the launch; the abort poisons
+// the rank (checked at the start of every launch), because the ranks' epochs
+// may disagree from then on until tb_qwen3_tp_reset.
+__device__ bool tp_exchange(const StepArgs& a, Ctl* ctl, int xi, float* own, float* vals)
 {
     const unsigned e = (unsigned)(ctl->base / gridDim.x) + (unsigned)xi + 1u;
-    const int tid = threadIdx.x;
-    if (tid == 0 && !ctl->abort) {
-        __threadfence_system();
-        for (int s = 0; s < a.P; s++) st_release_sys(a.peer_flag[s] + blockIdx.x, e);
-    }
-    if (tid < a.P && !ctl->abort) {
-        const unsigned* f = a.my_flag + (size_t)tid * TB_TP_STEP_CTAS + blockIdx.x;
-        long long it = 0;
-        while ((int)(ld_acquire_sys(f) - e) < 0) {
-            ++it;
-            if ((it & 255) == 0 && *reinterpret_cast<volatile unsigned*>(a.abort_word) == ctl->tag) {
-                ctl->abort = 1;
-                break;
+    const int tid = threadIdx.x, r0 = rowsC0(a), n = rowsC(a), par = xi & 1;
+    const float* part = a.xpart + (size_t)par * a.H + r0;
+    const int pairs = a.P * n;
+    if (!ctl->abort) {
+        for (int j = tid; j < pairs; j += THREADS) {
+            const int s = j / n, i = j - s * n;
+            const float v = part[i];
+            if (s == a.rank) {
+                vals[s * 64 + i] = v;
+            } else {
+                st_relaxed_sys_u64(a.peer_inbox[s] + ((size_t)a.rank * 2 + par) * a.H + r0 + i,
+                                   ((unsigned long long)e << 32) | __float_as_uint(v));
             }
-            if (it > STEP_WAIT_LIMIT) {
-                atomicExch(a.err, ERR_STEP_TP);
-                atomicExch(a.abort_word, ctl->tag);
-                ctl->abort = 1;
-                break;
+        }
+        for (int j = tid; j < pairs; j += THREADS) {
+            const int s = j / n, i = j - s * n;
+            if (s == a.rank) continue;
+            const unsigned long long* slot = a.my_inbox + ((size_t)s * 2 + par) * a.H + r0 + i;
+            unsigned long long pk;
+            long long it = 0;
+            while ((unsigned)((pk = ld_relaxed_sys_u64(slot)) >> 32) != e) {
+                ++it;
+                if ((it & 255) == 0 && *reinterpret_cast<volatile unsigned*>(a.abort_word) == ctl->tag) {
+                    ctl->abort = 1;
+                    break;
+                }
+                if (it > STEP_WAIT_LIMIT) {
+                    atomicExch(a.err, ERR_STEP_TP);
+                    atomicExch(a.abort_word, ctl->tag);
+                    ctl->abort = 1;
+                    break;
+                }
+                if (it > 2048) __nanosleep(32);
             }
-            if (it > 2048) __nanosleep(32);
+            vals[s * 64 + i] = __uint_as_float((unsigned)pk);
         }
     }
     __syncthreads();
     if (ctl->abort) return false;
-    const int r0 = rowsC0(a), n = rowsC(a);
-    const float* const* parts = a.peer_part;
     for (int i = tid; i < n; i += THREADS) {
         float v = own[i];
-        for (int s = 0; s < a.P; s++) v += ld_volatile_f32(parts[s] + (size_t)(xi & 1) * a.H + r0 + i);
+        for (int s = 0; s < a.P; s++) v += vals[s * 64 + i];
         own[i] = v;
         a.x[r0 + i] = v;
     }
@@ -517,7 +540,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
     float* red = reinterpret_cast<float*>(misc + 128);               // >= 72 floats
     float* cs = reinterpret_cast<float*>(misc + 512);                // cos [hd], sin [hd]
     float* xo = reinterpret_cast<float*>(misc + 2112);               // this CTA's rows of x [rpC <= 64]
+    float* tpv = reinterpret_cast<float*>(misc + 2112 + 256);        // P > 1: exchanged rows [P][64]
     const int tid = threadIdx.x;
+    if (a.P > 1) {
+        // a rank poisoned by an earlier exchange that gave up runs nothing (no
+        // barrier arrival, no copy, no packet) until tb_qwen3_tp_reset
+        if (__syncthreads_or(tid == 0 && *reinterpret_cast<const volatile unsigned*>(a.poison) != 0u)) {
+            if (tid == 0 && blockIdx.x == 0) atomicCAS(a.err, 0, ERR_STEP_TP_POISONED);   // keeps a first error
+            return;
+        }
+    }
     const int pos = a.pos[0];
     if (tid == 0 && blockIdx.x == 0 && step_S(a, pos) == 0) atomicExch(a.err, ERR_ATTN_POS);
     stamp(a, 0);
@@ -622,7 +654,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                                        rowsC0(a), xo);
             }
             __syncthreads();
-            if (a.P > 1 && !tp_exchange(a, ctl, 2 * l, xo)) goto drain;
+            if (a.P > 1 && !tp_exchange(a, ctl, 2 * l, xo, tpv)) goto drain;
             STAMP(2, 3);
             if (!grid_sync(a, ctl)) goto drain;
             STAMP(2, 4);
@@ -663,7 +695,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                     gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
-            if (a.P > 1 && !tp_exchange(a, ctl, 2 * l + 1, xo)) goto drain;
+            if (a.P > 1 && !tp_exchange(a, ctl, 2 * l + 1, xo, tpv)) goto drain;
             STAMP(4, 3);
             if (more && !grid_sync(a, ctl)) goto drain;
             STAMP(4, 4);
@@ -673,6 +705,7 @@ drain:
     // copies still in flight land before the CTA's shared memory is released
     cp_async_wait<0>();
     __syncthreads();
+    if (tid == 0 && a.P > 1 && ctl->abort) atomicExch(a.poison, 1u);   // epochs may disagree from here on
     if (tid == 0) {
         for (int b = 0; b < 3; b++)
             if (ctl->pend & (1u << b)) mbar_wait(&bars[b], (ctl->par >> b) & 1u);
@@ -707,7 +740,10 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     a.L = L; a.H = H; a.nHq = nHq; a.nKv = nKv; a.I = I; a.nsplit = nsplit; a.max_seq = max_seq;
     a.tern = tern ? 1 : 0;
     a.P = P > 1 ? P : 1;
-    if (a.P > TB_TP_MAX || (a.P > 1 && G > TB_TP_STEP_CTAS)) return TB_ERR_UNSUPPORTED;
+    if (a.P > TB_TP_MAX) return TB_ERR_UNSUPPORTED;
+    // the exchange epochs: a launch passes 1 + 4L + (L - 1) = 5L grid barriers and
+    // has 2L exchanges; epochs stay unique across launches while 5L >= 2L + 1
+    if (5 * L < 2 * L + 1) return TB_ERR_UNSUPPORTED;
     a.rpC = (H + G - 1) / G;
     a.rpD = (I + G - 1) / G;
     if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
@@ -728,7 +764,8 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     const size_t bR = up(std::max(mb(RBA, H) + (size_t)H * 2, mb(a.rpC, nHq * hd)));
     const int Kmax = std::max(std::max(H, I), nHq * hd);
     const size_t act = up((size_t)(Kmax / 32) * 40);
-    const size_t misc = 2112 + 64 * 4;     // barriers, control, reduction, rope table, own rows of x
+    // barriers, control, reduction, rope table, own rows of x, exchanged rows (P > 1)
+    const size_t misc = 2112 + 64 * 4 + (a.P > 1 ? (size_t)TB_TP_MAX * 64 * 4 : 0);
     a.off_P = 0;
     a.off_Q = (int)bP;
     a.off_R = (int)(bP + bQ);
@@ -773,12 +810,13 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.rank = io->rank;
     if (P > 1) {
         for (int s = 0; s < P; s++) {
-            TB_REQUIRE(ctx, io->tp_part[s] && io->tp_flags[s], "decode step: exchange arena of rank %d not mapped", s);
-            a.peer_part[s] = io->tp_part[s];
-            a.peer_flag[s] = io->tp_flags[s] + (size_t)a.rank * TB_TP_STEP_CTAS;
+            TB_REQUIRE(ctx, io->tp_inbox[s], "decode step: exchange arena of rank %d not mapped", s);
+            a.peer_inbox[s] = io->tp_inbox[s];
         }
-        a.xpart = io->tp_part[a.rank];
-        a.my_flag = io->tp_flags[a.rank];
+        TB_REQUIRE(ctx, io->xpart && io->tp_poison, "decode step: this rank's exchange arena is not set");
+        a.xpart = io->xpart;
+        a.my_inbox = io->tp_inbox[a.rank];
+        a.poison = io->tp_poison;
     }
     void (*kern)(const StepArgs) = nullptr;
     if (a.tern) {

@@ -9,8 +9,10 @@
 //   flag[P]      u32 epochs written by the peers ("my part for epoch e is ready")
 //   flag2[P]     the same for the argmax keys
 //   step         u32 steps completed (local)
-//   sflag[8][256] u32 epochs of the persistent decode step's per-CTA exchanges
-//                (tb_step.cu): row s, column c written by CTA c of rank s
+//   poison       u32 set when any exchange wait of this rank gave up (see below)
+//   inbox[8][2][n] u64 packets of the persistent decode step's exchanges
+//                (tb_step.cu): (epoch << 32) | f32 bits of row i of rank s's
+//                partial, written by rank s with one 8-byte store, parity 2
 // An exchange: after the producing kernel finished (griddepcontrol.wait), rank
 // r stores epoch e into flag[r] of every rank with a system-scope release,
 // waits until its own flag[s] >= e for every s (acquire, bounded), then reads
@@ -20,6 +22,15 @@
 // replayed.  Reuse is safe with two part buffers: rank r overwrites
 // part[parity(e)] at exchange e+2 only after every peer signalled e+1, which a
 // peer does only after it finished reading exchange e.
+//
+// Poison: epochs stay in step only while every rank ran every exchange.  A wait
+// that gives up (a peer died, or ran more than ~1 s late) leaves the ranks at
+// different epochs, after which a later exchange could accept a stale flag or
+// packet.  So a rank whose wait gave up sets its poison word, and every
+// exchange (these kernels and the persistent step) starts by reading it: when
+// set, the exchange does nothing but record ERR_TP_POISONED in the device error
+// word.  tb_qwen3_tp_reset clears the arena on every rank (all ranks idle,
+// behind a host barrier) and the epochs restart together from zero.
 #include "tb_internal.h"
 
 namespace {
@@ -27,33 +38,48 @@ namespace {
 constexpr int TP_MAX = 8;
 constexpr long long TP_WAIT_LIMIT = 1LL << 22;    // polls (sleeping 64+ ns after the first 4096): ~1 s
 constexpr int ERR_TP_WAIT = 0x7a01;
+constexpr int ERR_TP_POISONED = 0x7a02;
 
 struct TpArgs {
     const float* part[TP_MAX];      // this exchange's part buffer on every rank
     unsigned* peer_flag[TP_MAX];    // &flag[r] on every rank (where this rank signals)
     const unsigned* my_flag;        // flag[0..P) of this rank
     const unsigned* step;           // steps completed
+    unsigned* poison;               // this rank's poison word
     float* x;                       // residual, updated in place: x += sum_s part_s
     int n, P, xi, nx;
     int* err;
 };
 
-// signal flag slot of every rank, then wait for every rank's signal (bounded)
-__device__ __forceinline__ void tp_signal_wait(unsigned* const* peer_flag, const unsigned* my_flag, int P, unsigned e,
-                                               bool signal, int* err)
+// The CTA-wide poison check every exchange starts with: true when an earlier
+// wait of this rank gave up (the error word is set once, by CTA 0).
+__device__ __forceinline__ bool tp_poisoned(const unsigned* poison, int* err)
+{
+    const bool p = __syncthreads_or(threadIdx.x == 0 && *reinterpret_cast<const volatile unsigned*>(poison) != 0u);
+    if (p && blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(err, 0, ERR_TP_POISONED);   // keeps a first error
+    return p;
+}
+
+// signal flag slot of every rank, then wait for every rank's signal (bounded);
+// false (for the whole CTA) when a wait gave up, which poisons this rank
+__device__ __forceinline__ bool tp_signal_wait(unsigned* const* peer_flag, const unsigned* my_flag, int P, unsigned e,
+                                               bool signal, int* err, unsigned* poison)
 {
     if (signal && threadIdx.x < P) st_release_sys(peer_flag[threadIdx.x], e);
+    bool gave_up = false;
     if (threadIdx.x < P) {
         long long it = 0;
         while ((int)(ld_acquire_sys(my_flag + threadIdx.x) - e) < 0) {
             if (++it > TP_WAIT_LIMIT) {
                 atomicExch(err, ERR_TP_WAIT);
+                atomicExch(poison, 1u);
+                gave_up = true;
                 break;
             }
             if (it > 4096) __nanosleep(64);   // a healthy peer answers within the first polls
         }
     }
-    __syncthreads();
+    return !__syncthreads_or(gave_up);
 }
 
 // x[i] += part_0[i] + part_1[i] + ... (rank order), float4 per thread
@@ -61,8 +87,9 @@ __global__ void __launch_bounds__(256) k_tp_allreduce(const TpArgs a)
 {
     tb_pdl_wait();
     tb_pdl_trigger();
+    if (tp_poisoned(a.poison, a.err)) return;
     const unsigned e = *a.step * (unsigned)a.nx + (unsigned)a.xi + 1u;
-    tp_signal_wait(a.peer_flag, a.my_flag, a.P, e, blockIdx.x == 0, a.err);
+    if (!tp_signal_wait(a.peer_flag, a.my_flag, a.P, e, blockIdx.x == 0, a.err, a.poison)) return;
     const int n4 = a.n >> 2;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
         float4 v = reinterpret_cast<const float4*>(a.x)[i];
@@ -79,6 +106,7 @@ struct TpKeyArgs {
     unsigned* peer_flag2[TP_MAX];
     const unsigned* my_flag2;
     unsigned* step;                           // incremented here: the last kernel of a step
+    unsigned* poison;
     uint32_t* ids;
     int32_t* pos;
     int rows, P;
@@ -91,8 +119,9 @@ __global__ void __launch_bounds__(32) k_tp_argmax_merge(const TpKeyArgs a)
 {
     tb_pdl_wait();
     tb_pdl_trigger();
+    if (tp_poisoned(a.poison, a.err)) return;
     const unsigned e = *a.step + 1u;
-    tp_signal_wait(a.peer_flag2, a.my_flag2, a.P, e, true, a.err);
+    if (!tp_signal_wait(a.peer_flag2, a.my_flag2, a.P, e, true, a.err, a.poison)) return;
     for (int row = threadIdx.x; row < a.rows; row += blockDim.x) {
         unsigned long long best = 0ull;
         for (int s = 0; s < a.P; s++) {
@@ -118,12 +147,12 @@ static size_t tp_base_bytes(int64_t n)
 size_t tb_tp_arena_bytes(int P, int64_t n)
 {
     (void)P;
-    return ((tp_base_bytes(n) + 255) & ~size_t(255)) + (size_t)TB_TP_MAX * TB_TP_STEP_CTAS * 4;
+    return ((tp_base_bytes(n) + 255) & ~size_t(255)) + (size_t)TB_TP_MAX * 2 * n * 8;
 }
 
-unsigned* tb_tp_arena_step_flags(char* base, int64_t n)
+unsigned long long* tb_tp_arena_step_inbox(char* base, int64_t n)
 {
-    return reinterpret_cast<unsigned*>(base + ((tp_base_bytes(n) + 255) & ~size_t(255)));
+    return reinterpret_cast<unsigned long long*>(base + ((tp_base_bytes(n) + 255) & ~size_t(255)));
 }
 
 void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long** keys, unsigned** flag,
@@ -134,7 +163,7 @@ void tb_tp_arena_layout(char* base, int64_t n, float** part, unsigned long long*
     *keys = reinterpret_cast<unsigned long long*>(base + part_b);
     *flag = reinterpret_cast<unsigned*>(base + part_b + 16 * 8);
     *flag2 = *flag + TP_MAX;
-    *step = *flag2 + TP_MAX;
+    *step = *flag2 + TP_MAX;      // step[1] is the poison word
 }
 
 // x += sum over ranks of part (exchange xi of nx per step, parity buffer
@@ -148,7 +177,7 @@ int tb_tp_allreduce_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t
         tb_tp_arena_layout(arenas[s], n, &part, &keys, &flag, &flag2, &step);
         a.part[s] = part + (size_t)((xi + 1) & 1) * n;
         a.peer_flag[s] = flag + r;
-        if (s == r) { a.my_flag = flag; a.step = step; }
+        if (s == r) { a.my_flag = flag; a.step = step; a.poison = step + 1; }
     }
     a.x = x; a.n = (int)n; a.P = P; a.xi = xi; a.nx = nx; a.err = ctx->dev_error;
     const int grid = (int)std::min<int64_t>(std::max<int64_t>(1, (n / 4 + 255) / 256), 32);
@@ -167,7 +196,7 @@ int tb_tp_argmax_merge_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int6
         tb_tp_arena_layout(arenas[s], n, &part, &keys, &flag, &flag2, &step);
         a.keys[s] = keys;
         a.peer_flag2[s] = flag2 + r;
-        if (s == r) { a.my_flag2 = flag2; a.step = step; }
+        if (s == r) { a.my_flag2 = flag2; a.step = step; a.poison = step + 1; }
     }
     a.ids = ids; a.pos = pos; a.rows = rows; a.P = P; a.err = ctx->dev_error;
     cudaError_t e = tb_launch(ctx, k_tp_argmax_merge, dim3(1), dim3(32), 0, a);

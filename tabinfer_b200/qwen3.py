@@ -222,6 +222,12 @@ class Qwen3:
         assert len(blob) == 64 * self.cfg["tp_size"]
         self.ctx.check(LIB.tb_qwen3_tp_connect(self.h, ctypes.c_char_p(blob)), "tp_connect")
 
+    def tp_reset(self):
+        """Clear this rank's exchange state after a device-side wait gave up
+        (tb_qwen3_tp_reset): call it on every rank with every rank idle, behind
+        a barrier, and step again only after every rank returned."""
+        self.ctx.check(LIB.tb_qwen3_tp_reset(self.h), "tp_reset")
+
     # ---- cache and I/O ----------------------------------------------------------
     def kv_pointers(self, layer):
         p = [ctypes.c_void_p() for _ in range(4)]

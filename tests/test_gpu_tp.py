@@ -278,3 +278,98 @@ def test_tp2_persistent_step_equals_kernels(cuda, case):
             assert b[1:] == a[1:], (r, i)
     assert [x[1:] for x in res[0][0][_lib.QW_STEP_PERSISTENT][1]] == \
         [x[1:] for x in res[1][0][_lib.QW_STEP_PERSISTENT][1]]
+
+
+# ---- a peer that never arrives: bounded wait, poison, reset -------------------------
+def _run_poison(rank, P, exchange, mine, other):
+    """Rank 0 runs one persistent TP step while rank 1 launches nothing: the
+    in-kernel exchange wait runs out (ERR_STEP_TP), the rank is poisoned and
+    its next step refuses to run.  Then both ranks, idle, reset behind a
+    queue barrier and step together; the persistent steps must equal the
+    multi-kernel TP steps from the same start."""
+    import tabinfer_b200 as tb
+    from tabinfer_b200 import _lib
+    cfg, n = dict(CFG, batch=1), 9
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    W = make_weights(cfg, 23)
+    m = tb.Qwen3(dict(cfg, tp_size=P, tp_rank=rank), device=rank)
+    for name, w in W.items():
+        m.load(name, torch.from_numpy(np.ascontiguousarray(w).view(np.int16)).to(dev))
+    hq, allq = exchange
+    hq.put((rank, m.tp_handle()))
+    m.tp_connect(allq.get(timeout=120))
+    m.set_step_mode(_lib.QW_STEP_PERSISTENT)
+    codes = []
+    if rank == 0:
+        import time
+        t0 = time.time()
+        m.set_tokens([321], [n])
+        m.step()
+        codes.append(m.ctx.device_error())      # synchronizes: the wait gave up
+        codes.append(time.time() - t0)
+        m.step()
+        codes.append(m.ctx.device_error())      # poisoned: refused
+        other.put("alone done")
+    else:
+        assert mine.get(timeout=120) == "alone done"
+    # barrier (both idle), reset, barrier
+    other.put("idle")
+    assert mine.get(timeout=120) == "idle"
+    m.tp_reset()
+    other.put("reset")
+    assert mine.get(timeout=120) == "reset"
+    out = {}
+    for mode in (_lib.QW_STEP_PERSISTENT, _lib.QW_STEP_KERNELS):
+        m.set_step_mode(mode)
+        m.set_tokens([321], [n])
+        runs = []
+        for _ in range(2):
+            m.step()
+            runs.append((m.logits().numpy().copy(), *m.tokens()))
+        out[mode] = runs
+    err = m.ctx.device_error()
+    m.close()
+    return codes, out, err
+
+
+def _rank_poison(rank, P, q, exchange, mine, other):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        q.put((rank, _run_poison(rank, P, exchange, mine, other)))
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.gpu
+def test_tp2_exchange_timeout_poisons_until_reset(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from tabinfer_b200 import _lib
+    ctx = mp.get_context("spawn")
+    q, hq = ctx.Queue(), ctx.Queue()
+    outs = [ctx.Queue() for _ in range(2)]
+    boxes = [ctx.Queue() for _ in range(2)]
+    procs = [ctx.Process(target=_rank_poison, args=(r, 2, q, (hq, outs[r]), boxes[r], boxes[1 - r]))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    hs = dict(hq.get(timeout=300) for _ in range(2))
+    for o in outs:
+        o.put([hs[0], hs[1]])
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+    codes = res[0][0]
+    assert codes[0] == 0x5103, "first step: 0x%x" % codes[0]        # ERR_STEP_TP: the exchange wait ran out
+    assert codes[1] < 20.0, "the bounded wait took %.1f s" % codes[1]
+    assert codes[2] == 0x5104, "poisoned step: 0x%x" % codes[2]     # refused until the reset
+    for r in range(2):
+        _, out, err = res[r]
+        assert err == 0, "rank %d device error 0x%x after the reset" % (r, err)
+        for a, b in zip(out[_lib.QW_STEP_KERNELS], out[_lib.QW_STEP_PERSISTENT]):
+            np.testing.assert_array_equal(b[0], a[0])
+            assert b[1:] == a[1:]
+    assert [x[1:] for x in res[0][1][_lib.QW_STEP_PERSISTENT]] == [x[1:] for x in res[1][1][_lib.QW_STEP_PERSISTENT]]
