@@ -1301,6 +1301,28 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_only(name, steps):
+    """One extra block alone (a development run; not the benchmark line)."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ctx = tb.default_context(0)
+    peak, _ = load_peaks()
+    if name == "q2g64":
+        out = q2g64_extra(dev, ctx, peak)
+    elif name == "chain":
+        out = {}
+        for B in (1, 4, 8):
+            ch = chain_gbs(dev, ctx, B, max(100, steps))
+            ch["frac_of_peak"] = round(ch["gbs"] / peak, 4)
+            out["batch%d" % B] = ch
+    else:
+        out = kernel_kinds(Q17, dev, 1, 4096, peak)
+    assert ctx.device_error() == 0
+    print(json.dumps({"only": name, name: out}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 
 def main():
@@ -1334,7 +1356,12 @@ def main():
                     help="three int3 MoE layers over T tokens (for an ncu launch list), then exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
+    ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds"),
+                    help="run one extra block alone on GPU 0 and print its JSON (development runs)")
     args = ap.parse_args()
+    if args.only:
+        run_only(args.only, args.steps)
+        return
     if args.profile_decode:
         profile_decode(args.profile_decode)
         return

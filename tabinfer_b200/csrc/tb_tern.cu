@@ -14,6 +14,7 @@
 // in block order with separately rounded f32 adds, which reproduces
 // gemv_tern_scalar bit for bit while the HBM stream stays fully parallel.
 #include "tb_common.cuh"
+#include "tb_gemv_dev.cuh"
 
 namespace {
 
@@ -25,8 +26,9 @@ constexpr int TERN_UNROLL = 4;
 __global__ void __launch_bounds__(256) k_pack_ternary(const float* __restrict__ w, uint8_t* __restrict__ codes,
                                                       float* __restrict__ scales, long long ngroups)
 {
+    // no early launch_dependents: a GEMV after it requests these codes before
+    // its own wait, so it may start only once they are all written
     tb_pdl_wait();
-    tb_pdl_trigger();
     const int lane = threadIdx.x & 31;
     for (long long g = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; g < ngroups;
          g += ((long long)gridDim.x * blockDim.x) >> 5) {
@@ -101,7 +103,7 @@ template <int B>
 __global__ void __launch_bounds__(TERN_THREADS) k_gemv_tern(const TernArgs a)
 {
     constexpr int TR = B <= 4 ? 8 : 32 / B;   // rows per warp tile
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     const int nb = a.K >> 6;
     const int ld = nb + 1;                      // padded row stride of the parking area
     uint4* act_s = reinterpret_cast<uint4*>(smem);                       // [B][nb*4]
@@ -188,6 +190,228 @@ __global__ void __launch_bounds__(TERN_THREADS) k_gemv_tern(const TernArgs a)
     }
 }
 
+// ---- ternary GEMV, streaming form ------------------------------------------------
+// The row tiles of a CTA (TR consecutive rows: one contiguous run of codes and
+// one of scales) are staged in shared memory by cp.async.bulk in a ring of NST
+// stages, the first NST requested before the grid waits on its producer (the
+// weights do not depend on it).  Lane l of every warp owns the 64-groups
+// l, l + 32, ... of the row: their int8 activations stay in registers for the
+// whole CTA.  Warp w owns rows w*RW .. w*RW+RW-1 of a tile.  A (row, group) item
+// is the exact i32 dot of the group's unsigned codes with the activations: each
+// code word is split by masks into its four planes, scaled by 1, 4, 16, 64
+// (dp4a.u32.s32 on the masked bytes), and the four sums are shifted back
+// exactly.  The rounded products s*dot and s*xsum are parked in shared memory
+// and one lane per (row, activation row) adds them serially in block order, as
+// gemv_tern_scalar does, so the result is bit for bit the scalar one.
+constexpr int T2_THREADS = 256;
+constexpr int T2_WARPS = T2_THREADS / 32;
+constexpr int T2_ERR_WAIT = 0x6d02;
+
+struct Tern2Args {
+    float* out;
+    const uint8_t* codes;
+    const float* scales;
+    const int8_t* act;
+    const int32_t* xsum;
+    const float* act_scale;   // optional [B]: out *= 1/act_scale
+    int N, K, TR, NST, tiles;
+    int stage_bytes;          // TR * (K/4 + nb*4), a multiple of 16
+    int park_ld;              // floats per parked row (nb rounded up to 4)
+    int* err;
+};
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+template <int B, int NBL>
+__global__ void __launch_bounds__(T2_THREADS, 2) k_gemv_tern2(const Tern2Args a)
+{
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int nb = a.K >> 6, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int RW = a.TR / T2_WARPS, ld = a.park_ld;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                          // [NST]
+    float* park = reinterpret_cast<float*>(smem + 128);                          // per warp [2][B][RW][ld]
+    float* P = park + (size_t)wid * 2 * B * RW * ld;
+    float* Q = P + (size_t)B * RW * ld;
+    unsigned char* stages = smem + 128 + (size_t)T2_WARPS * 2 * B * RW * ld * 4;
+    stages = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(stages) + 127) & ~uintptr_t(127));
+    const int cb = a.K >> 2;                                     // code bytes a row
+    const int my_tiles = a.tiles > (int)blockIdx.x ? (a.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+    auto issue = [&](int k) {                                    // thread 0: tile k of this CTA -> stage k % NST
+        const int t = blockIdx.x + k * gridDim.x;
+        const int row0 = t * a.TR, rows = min(a.TR, a.N - row0);
+        unsigned char* st = stages + (size_t)(k % a.NST) * a.stage_bytes;
+        uint64_t* bar = bars + (k % a.NST);
+        const uint32_t c_bytes = (uint32_t)rows * cb, s_bytes = (uint32_t)rows * nb * 4;
+        const bool sbulk = (s_bytes & 15u) == 0;
+        mbar_expect_tx(bar, c_bytes + (sbulk ? s_bytes : 0u));
+        bulk_g2s(st, a.codes + (size_t)row0 * cb, c_bytes, bar);
+        if (sbulk) bulk_g2s(st + (size_t)a.TR * cb, a.scales + (size_t)row0 * nb, s_bytes, bar);
+    };
+    if (tid == 0) {
+        for (int s = 0; s < a.NST; s++) mbar_init(&bars[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int k = 0; k < min(a.NST, my_tiles); k++) issue(k);
+    }
+    __syncthreads();
+    tb_pdl_wait();
+    tb_pdl_trigger();
+
+    // this lane's activations: group g = lane + 32 i, plane j, word w
+    uint32_t A[B][NBL][4][4];
+    float xs[B][NBL];
+#pragma unroll
+    for (int b = 0; b < B; b++)
+#pragma unroll
+        for (int i = 0; i < NBL; i++) {
+            const int g = lane + 32 * i;
+            const bool ok = g < nb;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint4 v = ok ? __ldg(reinterpret_cast<const uint4*>(a.act + (size_t)b * a.K + g * 64) + j)
+                                   : make_uint4(0, 0, 0, 0);
+                A[b][i][j][0] = v.x; A[b][i][j][1] = v.y; A[b][i][j][2] = v.z; A[b][i][j][3] = v.w;
+            }
+            xs[b][i] = ok ? (float)__ldg(a.xsum + (size_t)b * nb + g) : 0.0f;
+        }
+
+    for (int k = 0; k < my_tiles; k++) {
+        const int t = blockIdx.x + k * gridDim.x;
+        const int row0 = t * a.TR, rows = min(a.TR, a.N - row0);
+        const unsigned char* st = stages + (size_t)(k % a.NST) * a.stage_bytes;
+        const bool ok = mbar_wait(bars + (k % a.NST), (uint32_t)((k / a.NST) & 1));
+        if (__syncthreads_or(!ok)) {
+            // the copies did not land within the bound: record it, then give the
+            // tiles still requested (k .. k + NST - 1) a bounded wait each so no copy
+            // is in flight when the CTA's shared memory is released
+            if (tid == 0) {
+                atomicExch(a.err, T2_ERR_WAIT);
+                for (int kk = k + 1; kk < min(my_tiles, k + a.NST); kk++)
+                    mbar_wait(bars + (kk % a.NST), (uint32_t)((kk / a.NST) & 1));
+            }
+            break;
+        }
+        const float* sc = reinterpret_cast<const float*>(st + (size_t)a.TR * cb);
+        const bool sbulk = (((uint32_t)rows * nb * 4) & 15u) == 0;
+        // items: rows of this warp x groups of this lane
+        for (int q = 0; q < RW; q++) {
+            const int r = wid * RW + q;
+            if (r >= rows) break;
+#pragma unroll
+            for (int i = 0; i < NBL; i++) {
+                const int g = lane + 32 * i;
+                if (g >= nb) break;
+                const uint4 cw = *reinterpret_cast<const uint4*>(st + (size_t)r * cb + g * 16);
+                const float s = sbulk ? sc[r * nb + g] : __ldg(a.scales + (size_t)(row0 + r) * nb + g);
+                const uint32_t c[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+                for (int b = 0; b < B; b++) {
+                    int d0 = 0, d1 = 0, d2 = 0, d3 = 0;
+#pragma unroll
+                    for (int w = 0; w < 4; w++) {
+                        d0 = dp4a_us(c[w] & 0x03030303u, A[b][i][0][w], d0);
+                        d1 = dp4a_us(c[w] & 0x0C0C0C0Cu, A[b][i][1][w], d1);
+                        d2 = dp4a_us(c[w] & 0x30303030u, A[b][i][2][w], d2);
+                        d3 = dp4a_us(c[w] & 0xC0C0C0C0u, A[b][i][3][w], d3);
+                    }
+                    const int dot = d0 + (d1 >> 2) + (d2 >> 4) + (d3 >> 6);   // exact: d_j is a multiple of 4^j
+                    P[(b * RW + q) * ld + g] = __fmul_rn(s, (float)dot);
+                    Q[(b * RW + q) * ld + g] = __fmul_rn(s, xs[b][i]);
+                }
+            }
+        }
+        __syncthreads();                       // every warp is done with the stage
+        if (tid == 0 && k + a.NST < my_tiles) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(k + a.NST);
+        }
+        // serial chains in block order: one lane per (activation row, row)
+        if (lane < B * RW) {
+            const int b = lane / RW, q = lane - b * RW, r = wid * RW + q;
+            if (r < rows) {
+                const float* pr = P + (b * RW + q) * ld;
+                const float* qr = Q + (b * RW + q) * ld;
+                float acc = 0.0f, sxs = 0.0f;
+                int g = 0;
+                for (; g + 4 <= nb; g += 4) {
+                    const float4 p4 = *reinterpret_cast<const float4*>(pr + g);
+                    const float4 q4 = *reinterpret_cast<const float4*>(qr + g);
+                    acc = __fadd_rn(acc, p4.x); sxs = __fadd_rn(sxs, q4.x);
+                    acc = __fadd_rn(acc, p4.y); sxs = __fadd_rn(sxs, q4.y);
+                    acc = __fadd_rn(acc, p4.z); sxs = __fadd_rn(sxs, q4.z);
+                    acc = __fadd_rn(acc, p4.w); sxs = __fadd_rn(sxs, q4.w);
+                }
+                for (; g < nb; g++) {
+                    acc = __fadd_rn(acc, pr[g]);
+                    sxs = __fadd_rn(sxs, qr[g]);
+                }
+                float v = __fsub_rn(acc, sxs);
+                if (a.act_scale) v = __fmul_rn(v, __fdiv_rn(1.0f, a.act_scale[b]));
+                a.out[(size_t)b * a.N + row0 + r] = v;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// Tile rows, stages and shared memory of the streaming form for this shape, or
+// false when it does not apply (the activations would not fit in registers).
+struct T2Plan {
+    int TR, NST, NBL, park_ld, stage_bytes;
+    size_t smem;
+};
+bool tern2_plan(int B, int64_t N, int64_t K, int num_sms, T2Plan* p)
+{
+    const int nb = (int)(K / 64);
+    const int NBL = (nb + 31) / 32;
+    if (NBL > 4 || B * NBL > 4) return false;              // <= 64 activation registers a lane
+    const int rowb = (int)(K / 4) + nb * 4;                // code + scale bytes a row
+    // enough tiles to give every SM two CTAs' worth when the matrix allows it
+    int TR = 32;
+    while (TR > 8 && (N + TR - 1) / TR < 2LL * num_sms) TR /= 2;
+    p->TR = TR;
+    p->NBL = NBL;
+    p->park_ld = ((nb + 3) & ~3) + 4;                      // float4 rows, 4-bank shift between rows
+    p->stage_bytes = (TR * rowb + 127) & ~127;
+    const size_t park = (size_t)T2_WARPS * 2 * B * (TR / T2_WARPS) * p->park_ld * 4;
+    // about 96 KB a CTA (two CTAs an SM), at least 2 and at most 6 stages
+    int nst = (int)((96 * 1024 - 256 - park) / p->stage_bytes);
+    nst = std::max(2, std::min(6, nst));
+    p->NST = nst;
+    p->smem = 128 + park + 128 + (size_t)nst * p->stage_bytes;
+    return p->smem <= 227 * 1024;
+}
+
+template <int B, int NBL>
+int launch_tern2(tb_ctx* ctx, const Tern2Args& a, const T2Plan& p)
+{
+    auto kern = k_gemv_tern2<B, NBL>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    int occ = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, T2_THREADS, p.smem);
+    if (occ < 1) occ = 1;
+    const int grid = std::min(a.tiles, ctx->num_sms * occ);
+    e = tb_launch(ctx, kern, dim3(grid), dim3(T2_THREADS), p.smem, a);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemv_tern launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+int tern2_dispatch(tb_ctx* ctx, Tern2Args& a, const T2Plan& p, int B)
+{
+#define T2_CASE(BB, NN) \
+    if (B == BB && p.NBL == NN) return launch_tern2<BB, NN>(ctx, a, p);
+    T2_CASE(1, 1) T2_CASE(1, 2) T2_CASE(1, 3) T2_CASE(1, 4)
+    T2_CASE(2, 1) T2_CASE(2, 2) T2_CASE(3, 1) T2_CASE(4, 1)
+#undef T2_CASE
+    return TB_ERR_UNSUPPORTED;
+}
+
 size_t tern_smem(int B, int nb)
 {
     const int TR = B <= 4 ? 8 : 32 / B;
@@ -223,6 +447,13 @@ int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float
                "bad shape N=%lld K=%lld (K%%64 must be 0)", (long long)N, (long long)K);
     TB_REQUIRE(ctx, TB_ALIGNED(codes, 16) && TB_ALIGNED(act, 16) && TB_ALIGNED(scales, 4) && TB_ALIGNED(xsum, 4),
                "codes/act must be 16-byte aligned");
+    T2Plan p2;
+    if (batch >= 1 && batch <= 4 && TB_ALIGNED(scales, 16) && tern2_plan(batch, N, K, ctx->num_sms, &p2)) {
+        Tern2Args t{out, codes, scales, act, xsum, act_scale, (int)N, (int)K, p2.TR, p2.NST, tb_cdiv(N, p2.TR),
+                    p2.stage_bytes, p2.park_ld, ctx->dev_error};
+        const int rc = tern2_dispatch(ctx, t, p2, batch);
+        if (rc != TB_ERR_UNSUPPORTED) return rc;
+    }
     TernArgs a{out, codes, scales, act, xsum, act_scale, (int)N, (int)K, 0};
     const int TR = batch <= 4 ? 8 : 32 / batch;
     a.tiles = tb_cdiv(N, TR);

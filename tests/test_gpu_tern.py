@@ -118,3 +118,28 @@ def test_linear_tern_matches_model_linear(cuda, T):
 def test_bad_k_raises(cuda):
     with pytest.raises(tb.TabInferError):
         tb.pack_ternary(torch.zeros(4, 96, device="cuda"))
+
+
+def _random_q2g64(seed, N, K):
+    """valid Q2_0_g64 codes (every 2-bit field in {0,1,2}) and f32 scales, made
+    directly (no f32 weight matrix), for large shapes"""
+    import itertools
+    rng = np.random.default_rng(seed)
+    lut = np.array([a | (b << 2) | (c << 4) | (d << 6) for a, b, c, d in itertools.product(range(3), repeat=4)],
+                   np.uint8)
+    codes = lut[rng.integers(0, 81, (N, K // 4), dtype=np.uint8)]
+    scales = np.float16(rng.uniform(0.01, 0.05, (N, K // 64))).astype(np.float32)
+    return codes, scales
+
+
+# Shapes that make the streaming GEMV wrap its stage ring many times (tens of
+# tiles per CTA), odd tails whose scales cannot travel by bulk copy, every
+# batch its register path takes (1..4) and the largest K it keeps in registers.
+@pytest.mark.parametrize("N,K,B", [(60000, 2048, 1), (30000, 6144, 1), (13, 64, 3), (7, 128, 2), (1000, 4096, 2),
+                                   (777, 8192, 1), (20000, 2048, 4), (5003, 1024, 3), (9001, 8256, 1)])
+def test_gemv_bit_exact_streaming_shapes(cuda, N, K, B):
+    codes, scales = _random_q2g64(N + K + B, N, K)
+    x = np.random.default_rng(B + 11).normal(0, 1, (B, K)).astype(np.float32)
+    act, xsum, _ = oracle.quantize_act(x)
+    out = host(tb.gemv_tern(_dev(codes), _dev(scales), _dev(act), _dev(xsum)))
+    np.testing.assert_array_equal(out, oracle.gemv_tern_scalar(codes, scales, act, xsum))
