@@ -386,6 +386,7 @@ def chain_gbs(dev, ctx, B, steps):
             tb.gemv_dp4a(x, *c.lm_head, norm_w=c.norm, eps=1e-6, y=logits)
         tb.argmax(logits, out=tok)
 
+    torch.cuda.synchronize(dev)     # the context's own stream does not wait for torch's
     stream = torch.cuda.ExternalStream(ctx.own_stream(), device=dev)
     with torch.cuda.stream(stream):
         step()
@@ -682,6 +683,9 @@ def _record_batch(ctx, dev, fn):
     stream (so the timed replays are not bound by Python launch overhead)."""
     import torch
     from tabinfer_b200._lib import LIB, P
+    # the context's own stream does not wait for torch's: inputs made there
+    # (weights, activations) must be complete before anything is recorded or timed
+    torch.cuda.synchronize(dev)
     stream = torch.cuda.ExternalStream(ctx.own_stream(), device=dev)
     with torch.cuda.stream(stream):
         fn()
@@ -726,6 +730,7 @@ def q2g64_extra(dev, ctx, peak_gbs):
         acts[K] = tb.quantize_act(x)[:2]
     outs = {n: torch.empty(1, N, device=dev) for n, N, _ in BONSAI_MATS}
     dims = {n: (N, K) for n, N, K in BONSAI_MATS}
+    torch.cuda.synchronize(dev)
 
     def gemv(name, L):
         codes, scales = L[name]
@@ -760,6 +765,7 @@ def q2g64_extra(dev, ctx, peak_gbs):
     big = [_q2g64_pack(dev, g, V, H) for _ in range(3)]
     yb = torch.empty(1, V, device=dev)
     act, xsum = acts[H]
+    torch.cuda.synchronize(dev)
     h, stream = _record_batch(ctx, dev, lambda: [tb.gemv_tern(c, s, act, xsum, out=yb) for c, s in big])
     msb = _replay_ms(ctx, h, stream, 20) / 3
     LIB.tb_batch_destroy(h)
@@ -1301,6 +1307,25 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def profile_q2g64():
+    """Three tb_gemv_tern_q2g64 launches, batch 1, each on its own 151936 x 2048
+    matrix (117 MB; the three together exceed L2), for an ncu capture of one."""
+    import torch
+    import tabinfer_b200 as tb
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(31)
+    V, H = Q17["vocab"], Q17["hidden"]
+    mats = [_q2g64_pack(dev, g, V, H) for _ in range(3)]
+    act, xsum, _ = tb.quantize_act(torch.randn(1, H, device=dev, generator=g))
+    y = torch.empty(1, V, device=dev)
+    torch.cuda.synchronize(dev)
+    for c, s in mats:
+        tb.gemv_tern(c, s, act, xsum, out=y)
+    torch.cuda.synchronize(dev)
+    assert tb.default_context(0).device_error() == 0
+
+
 def run_only(name, steps):
     """One extra block alone (a development run; not the benchmark line)."""
     import torch
@@ -1356,11 +1381,16 @@ def main():
                     help="three int3 MoE layers over T tokens (for an ncu launch list), then exit")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="S",
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
+    ap.add_argument("--profile-q2g64", action="store_true",
+                    help="three Q2_0_g64 GEMV launches on 151936 x 2048 matrices (for an ncu capture), then exit")
     ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds"),
                     help="run one extra block alone on GPU 0 and print its JSON (development runs)")
     args = ap.parse_args()
     if args.only:
         run_only(args.only, args.steps)
+        return
+    if args.profile_q2g64:
+        profile_q2g64()
         return
     if args.profile_decode:
         profile_decode(args.profile_decode)

@@ -200,9 +200,13 @@ __global__ void __launch_bounds__(TERN_THREADS) k_gemv_tern(const TernArgs a)
 // is the exact i32 dot of the group's unsigned codes with the activations: each
 // code word is split by masks into its four planes, scaled by 1, 4, 16, 64
 // (dp4a.u32.s32 on the masked bytes), and the four sums are shifted back
-// exactly.  The rounded products s*dot and s*xsum are parked in shared memory
-// and one lane per (row, activation row) adds them serially in block order, as
-// gemv_tern_scalar does, so the result is bit for bit the scalar one.
+// exactly.  The rounded pair (s*dot, s*xsum) of every item is parked in a
+// CTA-wide buffer (two of them, alternating by tile), and one warp per tile --
+// warp k % 8 for the CTA's k-th tile, so the chains rotate over the warps --
+// gives each lane one (activation row, row) and adds the pairs serially in
+// block order with one packed f32x2 add (two IEEE round-to-nearest lanes), as
+// gemv_tern_scalar adds its two chains, so the result is bit for bit the
+// scalar one.
 constexpr int T2_THREADS = 256;
 constexpr int T2_WARPS = T2_THREADS / 32;
 constexpr int T2_ERR_WAIT = 0x6d02;
@@ -215,8 +219,8 @@ struct Tern2Args {
     const int32_t* xsum;
     const float* act_scale;   // optional [B]: out *= 1/act_scale
     int N, K, TR, NST, tiles;
-    int stage_bytes;          // TR * (K/4 + nb*4), a multiple of 16
-    int park_ld;              // floats per parked row (nb rounded up to 4)
+    int stage_bytes;          // TR * (K/4 + nb*4) rounded up to 128
+    int park_ld;              // float2 pairs per parked row
     int* err;
 };
 
@@ -227,31 +231,39 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
     return d;
 }
 
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b)
+{
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
+        " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0,%1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 template <int B, int NBL>
 __global__ void __launch_bounds__(T2_THREADS, 2) k_gemv_tern2(const Tern2Args a)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     const int nb = a.K >> 6, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int RW = a.TR / T2_WARPS, ld = a.park_ld;
+    const int TR = a.TR, RW = TR / T2_WARPS, ld = a.park_ld;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                          // [NST]
-    float* park = reinterpret_cast<float*>(smem + 128);                          // per warp [2][B][RW][ld]
-    float* P = park + (size_t)wid * 2 * B * RW * ld;
-    float* Q = P + (size_t)B * RW * ld;
-    unsigned char* stages = smem + 128 + (size_t)T2_WARPS * 2 * B * RW * ld * 4;
+    float2* park = reinterpret_cast<float2*>(smem + 128);                        // [2][B][TR][ld]
+    const size_t park_pairs = (size_t)B * TR * ld;
+    unsigned char* stages = smem + 128 + 2 * park_pairs * sizeof(float2);
     stages = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(stages) + 127) & ~uintptr_t(127));
     const int cb = a.K >> 2;                                     // code bytes a row
     const int my_tiles = a.tiles > (int)blockIdx.x ? (a.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
     auto issue = [&](int k) {                                    // thread 0: tile k of this CTA -> stage k % NST
         const int t = blockIdx.x + k * gridDim.x;
-        const int row0 = t * a.TR, rows = min(a.TR, a.N - row0);
+        const int row0 = t * TR, rows = min(TR, a.N - row0);
         unsigned char* st = stages + (size_t)(k % a.NST) * a.stage_bytes;
         uint64_t* bar = bars + (k % a.NST);
         const uint32_t c_bytes = (uint32_t)rows * cb, s_bytes = (uint32_t)rows * nb * 4;
         const bool sbulk = (s_bytes & 15u) == 0;
         mbar_expect_tx(bar, c_bytes + (sbulk ? s_bytes : 0u));
         bulk_g2s(st, a.codes + (size_t)row0 * cb, c_bytes, bar);
-        if (sbulk) bulk_g2s(st + (size_t)a.TR * cb, a.scales + (size_t)row0 * nb, s_bytes, bar);
+        if (sbulk) bulk_g2s(st + (size_t)TR * cb, a.scales + (size_t)row0 * nb, s_bytes, bar);
     };
     if (tid == 0) {
         for (int s = 0; s < a.NST; s++) mbar_init(&bars[s], 1);
@@ -282,13 +294,14 @@ __global__ void __launch_bounds__(T2_THREADS, 2) k_gemv_tern2(const Tern2Args a)
 
     for (int k = 0; k < my_tiles; k++) {
         const int t = blockIdx.x + k * gridDim.x;
-        const int row0 = t * a.TR, rows = min(a.TR, a.N - row0);
+        const int row0 = t * TR, rows = min(TR, a.N - row0);
         const unsigned char* st = stages + (size_t)(k % a.NST) * a.stage_bytes;
+        float2* pk = park + (size_t)(k & 1) * park_pairs;
         const bool ok = mbar_wait(bars + (k % a.NST), (uint32_t)((k / a.NST) & 1));
         if (__syncthreads_or(!ok)) {
             // the copies did not land within the bound: record it, then give the
-            // tiles still requested (k .. k + NST - 1) a bounded wait each so no copy
-            // is in flight when the CTA's shared memory is released
+            // tiles still requested (k + 1 .. k + NST - 1) a bounded wait each so no
+            // copy is in flight when the CTA's shared memory is released
             if (tid == 0) {
                 atomicExch(a.err, T2_ERR_WAIT);
                 for (int kk = k + 1; kk < min(my_tiles, k + a.NST); kk++)
@@ -296,7 +309,7 @@ __global__ void __launch_bounds__(T2_THREADS, 2) k_gemv_tern2(const Tern2Args a)
             }
             break;
         }
-        const float* sc = reinterpret_cast<const float*>(st + (size_t)a.TR * cb);
+        const float* sc = reinterpret_cast<const float*>(st + (size_t)TR * cb);
         const bool sbulk = (((uint32_t)rows * nb * 4) & 15u) == 0;
         // items: rows of this warp x groups of this lane
         for (int q = 0; q < RW; q++) {
@@ -320,42 +333,33 @@ __global__ void __launch_bounds__(T2_THREADS, 2) k_gemv_tern2(const Tern2Args a)
                         d3 = dp4a_us(c[w] & 0xC0C0C0C0u, A[b][i][3][w], d3);
                     }
                     const int dot = d0 + (d1 >> 2) + (d2 >> 4) + (d3 >> 6);   // exact: d_j is a multiple of 4^j
-                    P[(b * RW + q) * ld + g] = __fmul_rn(s, (float)dot);
-                    Q[(b * RW + q) * ld + g] = __fmul_rn(s, xs[b][i]);
+                    pk[((size_t)b * TR + r) * ld + g] = fmul2(make_float2(s, s), make_float2((float)dot, xs[b][i]));
                 }
             }
         }
-        __syncthreads();                       // every warp is done with the stage
+        __syncthreads();                       // the stage is consumed; this tile's pairs are parked
         if (tid == 0 && k + a.NST < my_tiles) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issue(k + a.NST);
         }
-        // serial chains in block order: one lane per (activation row, row)
-        if (lane < B * RW) {
-            const int b = lane / RW, q = lane - b * RW, r = wid * RW + q;
+        // this tile's serial chains: warp k % 8, one lane per (activation row, row)
+        if (wid == (k & (T2_WARPS - 1)) && lane < B * TR) {
+            const int b = lane / TR, r = lane - b * TR;
             if (r < rows) {
-                const float* pr = P + (b * RW + q) * ld;
-                const float* qr = Q + (b * RW + q) * ld;
-                float acc = 0.0f, sxs = 0.0f;
+                const float2* pr = pk + ((size_t)b * TR + r) * ld;
+                float2 acc = make_float2(0.0f, 0.0f);        // (sum s*dot, sum s*xsum)
                 int g = 0;
-                for (; g + 4 <= nb; g += 4) {
-                    const float4 p4 = *reinterpret_cast<const float4*>(pr + g);
-                    const float4 q4 = *reinterpret_cast<const float4*>(qr + g);
-                    acc = __fadd_rn(acc, p4.x); sxs = __fadd_rn(sxs, q4.x);
-                    acc = __fadd_rn(acc, p4.y); sxs = __fadd_rn(sxs, q4.y);
-                    acc = __fadd_rn(acc, p4.z); sxs = __fadd_rn(sxs, q4.z);
-                    acc = __fadd_rn(acc, p4.w); sxs = __fadd_rn(sxs, q4.w);
+                for (; g + 2 <= nb; g += 2) {
+                    const float4 v = *reinterpret_cast<const float4*>(pr + g);
+                    acc = fadd2(acc, make_float2(v.x, v.y));
+                    acc = fadd2(acc, make_float2(v.z, v.w));
                 }
-                for (; g < nb; g++) {
-                    acc = __fadd_rn(acc, pr[g]);
-                    sxs = __fadd_rn(sxs, qr[g]);
-                }
-                float v = __fsub_rn(acc, sxs);
+                if (g < nb) acc = fadd2(acc, pr[g]);
+                float v = __fsub_rn(acc.x, acc.y);
                 if (a.act_scale) v = __fmul_rn(v, __fdiv_rn(1.0f, a.act_scale[b]));
                 a.out[(size_t)b * a.N + row0 + r] = v;
             }
         }
-        __syncwarp();
     }
 }
 
@@ -371,16 +375,17 @@ bool tern2_plan(int B, int64_t N, int64_t K, int num_sms, T2Plan* p)
     const int NBL = (nb + 31) / 32;
     if (NBL > 4 || B * NBL > 4) return false;              // <= 64 activation registers a lane
     const int rowb = (int)(K / 4) + nb * 4;                // code + scale bytes a row
-    // enough tiles to give every SM two CTAs' worth when the matrix allows it
-    int TR = 32;
-    while (TR > 8 && (N + TR - 1) / TR < 2LL * num_sms) TR /= 2;
+    // one chain lane per (activation row, row); enough tiles to give every SM
+    // two CTAs' worth when the matrix allows it; large K keeps the stages small
+    int TR = 32 / B >= 32 ? 32 : (32 / B >= 16 ? 16 : 8);
+    while (TR > 8 && ((N + TR - 1) / TR < 2LL * num_sms || TR * rowb > 32 * 1024)) TR /= 2;
     p->TR = TR;
     p->NBL = NBL;
-    p->park_ld = ((nb + 3) & ~3) + 4;                      // float4 rows, 4-bank shift between rows
+    p->park_ld = ((nb + 15) & ~15) + 2;                    // float4 rows, 4-bank shift between rows
     p->stage_bytes = (TR * rowb + 127) & ~127;
-    const size_t park = (size_t)T2_WARPS * 2 * B * (TR / T2_WARPS) * p->park_ld * 4;
-    // about 96 KB a CTA (two CTAs an SM), at least 2 and at most 6 stages
-    int nst = (int)((96 * 1024 - 256 - park) / p->stage_bytes);
+    const size_t park = 2 * (size_t)B * TR * p->park_ld * 8;
+    // about 104 KB a CTA (two CTAs an SM), at least 2 and at most 6 stages
+    int nst = (int)((104 * 1024 - 256 - (long long)park) / p->stage_bytes);
     nst = std::max(2, std::min(6, nst));
     p->NST = nst;
     p->smem = 128 + park + 128 + (size_t)nst * p->stage_bytes;
