@@ -176,6 +176,16 @@ TB_API int tb_pack_tern_q2g64(tb_ctx *ctx, const float *w, uint8_t *codes, float
 TB_API int tb_quant_act_q8(tb_ctx *ctx, const float *x, int8_t *act, int32_t *xsum,
                            float *scale, int64_t T, int64_t K);
 
+/* The browser CPU engine's activation quantizer, in its argument order: the
+ * WASM export quantize(dst, xsum, x, k) -> asc, cpu/kernel/src/lib.rs:566-606,
+ * which JS workers call before gemv_tern / gemm_tern_b4
+ * (cpu/cpukern-fwd-worker.js:326-357).  Per row of `rows`: asc = amax/127
+ * (1e-9 when amax == 0), dst = nearest-even(x * (1/asc)) clamped to +-127,
+ * xsum i32 per 64; asc f32 [rows] receives what the export returns (the
+ * factor the GEMV output is multiplied by).  Bit-exact.  k%64==0. */
+TB_API int tb_quantize_wasm(tb_ctx *ctx, int8_t *dst, int32_t *xsum, const float *x, int64_t k,
+                            float *asc, int64_t rows);
+
 /* Ternary GEMV for `batch` activation rows (1..8): out[b,n] =
  * sum_blk s*dot - sum_blk s*xsum, accumulated in block order exactly as
  * gemv_tern_scalar, tern.rs:79-119 (bit-exact).  Replaces tern::gemv_tern

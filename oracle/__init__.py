@@ -277,6 +277,17 @@ def quantize_act(x):
     return act, xsum, sc
 
 
+def quantize_act_wasm(x):
+    """WASM quantize (cpu/kernel/src/lib.rs:566-606): returns (act, xsum, asc)."""
+    x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+    T, K = x.shape
+    act = np.zeros((T, K), np.int8)
+    xsum = np.zeros((T, K // 64), np.int32)
+    asc = np.zeros(T, np.float32)
+    lib().tbo_quantize_act_wasm(_ptr(x), _I(T), _I(K), _ptr(act), _ptr(xsum), _ptr(asc))
+    return act, xsum, asc
+
+
 def gemv_tern_scalar(codes, scales, act, xsum):
     act = np.ascontiguousarray(np.atleast_2d(act), np.int8)
     xsum = np.ascontiguousarray(np.atleast_2d(xsum), np.int32)

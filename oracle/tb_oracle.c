@@ -442,6 +442,34 @@ TBO_API void tbo_quantize_act(const float *x, int64_t T, int64_t K,
     }
 }
 
+/* The WASM CPU engine's quantize (cpu/kernel/src/lib.rs:566-606): per-vector
+ * asc = amax/127 (1e-9 when amax == 0), inv = 1/asc, act = nearest-even(x*inv)
+ * clamped to +-127 (f32x4_nearest then the saturating narrow), xsum per 64.
+ * Returns asc -- the factor the caller multiplies the GEMV output by -- where
+ * tern.rs returns 127/amax.  Applied to each of T rows independently. */
+TBO_API void tbo_quantize_act_wasm(const float *x, int64_t T, int64_t K,
+                                   int8_t *act, int32_t *xsum, float *asc_out)
+{
+    for (int64_t t = 0; t < T; t++) {
+        const float *xr = x + t * K;
+        float amax = 0.0f;
+        for (int64_t i = 0; i < K; i++) { float a = fabsf(xr[i]); amax = a > amax ? a : amax; }
+        const float asc = amax > 0.0f ? amax / 127.0f : 1e-9f;
+        const float inv = 1.0f / asc;
+        for (int64_t i = 0; i < K; i++) {
+            float v = rintf(xr[i] * inv);          /* round to nearest, ties to even */
+            v = v < -127.0f ? -127.0f : (v > 127.0f ? 127.0f : v);
+            act[t * K + i] = (int8_t)v;
+        }
+        for (int64_t b = 0; b < K / 64; b++) {
+            int32_t s = 0;
+            for (int i = 0; i < 64; i++) s += act[t * K + b * 64 + i];
+            xsum[t * (K / 64) + b] = s;
+        }
+        asc_out[t] = asc;
+    }
+}
+
 /* tern.rs:79-119 (gemv_tern_scalar), the portable reference every backend is
  * validated against: per row, acc += s*dot and sxs += s*xsum in block order
  * (f32, separately rounded multiply and add), out = acc - sxs.

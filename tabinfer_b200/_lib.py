@@ -66,6 +66,7 @@ SIGNATURES = {
     "tb_gemm_dp4": [P, P, P, P, P, P, I64, I64, I64, I32, I32],
     "tb_linear_tern_wgsl": [P, P, P, P, P, I64, I64, I64, I32],
     "tb_quant_act_q8": [P, P, P, P, P, I64, I64],
+    "tb_quantize_wasm": [P, P, P, P, I64, P, I64],
     "tb_gemv_tern_q2g64": [P, P, P, P, P, P, I64, I64, I32],
     "tb_linear_tern": [P, P, P, P, P, I64, I64, I64],
     "tb_attn_prep_q8": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, F32, F32],

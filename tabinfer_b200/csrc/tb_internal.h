@@ -12,7 +12,9 @@ int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack
                      int64_t N, int64_t K, int batch, int acc);
 int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,
                       const int32_t* xsum, int64_t N, int64_t K, int batch, const float* act_scale);
-int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K);
+// wasm: the WASM engine's quantize (asc = amax/127, nearest-even, asc stored)
+int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K,
+                      bool wasm = false);
 
 // split-KV decode attention over `batch` sequences; sequence b's cache starts
 // cache_rows rows after sequence b-1's; with dpos, S_b = dpos[b] + 1 is read on

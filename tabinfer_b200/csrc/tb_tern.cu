@@ -46,6 +46,10 @@ __global__ void __launch_bounds__(256) k_pack_ternary(const float* __restrict__ 
 }
 
 // ---- quantize_act_into (tern.rs:206-222): one CTA per activation row -------
+// WASM: the CPU engine's quantize (cpu/kernel/src/lib.rs:566-606) instead:
+// asc = amax/127 (1e-9 for a zero row), x*(1/asc) rounded to nearest-even,
+// and asc stored where tern.rs stores 127/amax.
+template <bool WASM>
 __global__ void __launch_bounds__(256) k_quant_act(const float* __restrict__ x, int8_t* __restrict__ act,
                                                    int32_t* __restrict__ xsum, float* __restrict__ scale_out, int K)
 {
@@ -66,14 +70,22 @@ __global__ void __launch_bounds__(256) k_quant_act(const float* __restrict__ x, 
     }
     __syncthreads();
     const float amax = red[0];
-    const float scale = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 1.0f;
-    if (threadIdx.x == 0) scale_out[row] = scale;
+    float scale;
+    if (WASM) {
+        const float asc = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1e-9f;
+        if (threadIdx.x == 0) scale_out[row] = asc;
+        scale = __fdiv_rn(1.0f, asc);
+    } else {
+        scale = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 1.0f;
+        if (threadIdx.x == 0) scale_out[row] = scale;
+    }
     for (int g = wid; g < K / 64; g += nw) {
         int s = 0;
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             int i = g * 64 + h * 32 + lane;
-            float v = roundf(__fmul_rn(xr[i], scale));   // half away from zero, as f32::round
+            // tern.rs: half away from zero (f32::round); WASM: f32x4_nearest, ties to even
+            float v = WASM ? rintf(__fmul_rn(xr[i], scale)) : roundf(__fmul_rn(xr[i], scale));
             v = fminf(127.0f, fmaxf(-127.0f, v));
             int q = (int)v;
             act[(long long)row * K + i] = (int8_t)q;
@@ -475,11 +487,14 @@ int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float
     return tb_fail(ctx, TB_ERR_INVALID, "batch must be 1..8 (got %d)", batch);
 }
 
-int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K)
+int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K,
+                      bool wasm)
 {
     TB_REQUIRE(ctx, x && act && xsum && scale, "null pointer");
     TB_REQUIRE(ctx, T > 0 && T <= 65535 && K > 0 && K % 64 == 0, "bad shape T=%lld K=%lld", (long long)T, (long long)K);
-    cudaError_t e = tb_launch(ctx, k_quant_act, dim3((unsigned)T), dim3(256), 0, x, act, xsum, scale, (int)K);
+    cudaError_t e = wasm ? tb_launch(ctx, k_quant_act<true>, dim3((unsigned)T), dim3(256), 0, x, act, xsum, scale, (int)K)
+                         : tb_launch(ctx, k_quant_act<false>, dim3((unsigned)T), dim3(256), 0, x, act, xsum, scale,
+                                     (int)K);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_act launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -501,7 +516,14 @@ TB_API int tb_pack_tern_q2g64(tb_ctx* ctx, const float* w, uint8_t* codes, float
 TB_API int tb_quant_act_q8(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, float* scale, int64_t T, int64_t K)
 {
     if (!ctx) return TB_ERR_INVALID;
-    return tb_quant_act_impl(ctx, x, act, xsum, scale, T, K);
+    return tb_quant_act_impl(ctx, x, act, xsum, scale, T, K, false);
+}
+
+TB_API int tb_quantize_wasm(tb_ctx* ctx, int8_t* dst, int32_t* xsum, const float* x, int64_t k, float* asc,
+                            int64_t rows)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    return tb_quant_act_impl(ctx, x, dst, xsum, asc, rows, k, true);
 }
 
 TB_API int tb_gemv_tern_q2g64(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,

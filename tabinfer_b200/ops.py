@@ -495,6 +495,19 @@ def quantize_act(x, act=None, xsum=None, scale=None):
     return act, xsum, scale
 
 
+def quantize_wasm(x, dst=None, xsum=None, asc=None):
+    """WASM quantize(dst, xsum, x, k) -> asc (cpu/kernel/src/lib.rs:566-606), per
+    row of x: returns (dst i8, xsum i32 per 64, asc f32 per row)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    T, K = x2.shape
+    dst = dst if dst is not None else torch.empty((T, K), dtype=torch.int8, device=x.device)
+    xsum = xsum if xsum is not None else torch.empty((T, K // 64), dtype=torch.int32, device=x.device)
+    asc = asc if asc is not None else torch.empty((T,), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    c.check(LIB.tb_quantize_wasm(c.h, _p(dst), _p(xsum), _p(x2), K, _p(asc), T), "quantize_wasm")
+    return dst, xsum, asc
+
+
 def gemv_tern(codes, scales, act, xsum, out=None):
     """tern::gemv_tern (tern.rs:56-71) / WASM gemm_tern_b4 (lib.rs:331): batch = act rows."""
     a2 = act.reshape(-1, act.shape[-1])

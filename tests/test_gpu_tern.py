@@ -22,6 +22,22 @@ def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+@pytest.mark.parametrize("T,K", [(1, 64), (1, 2048), (4, 6144), (3, 128)])
+def test_quantize_wasm_bit_exact(cuda, T, K):
+    """WASM quantize (cpu/kernel/src/lib.rs:566-606): asc = amax/127, nearest-even,
+    asc returned; a zero row gives asc 1e-9 and zero codes."""
+    rng = np.random.default_rng(K + 7 * T)
+    x = rng.normal(0, 1, (T, K)).astype(np.float32)
+    if T > 1:
+        x[1] = 0.0
+    x[0, :4] = [x[0].max() / 127 * 0.5, -x[0].max() / 127 * 1.5, 0.0, x[0].max()]
+    dst, xsum, asc = tb.quantize_wasm(_dev(x))
+    oa, ox, oasc = oracle.quantize_act_wasm(x)
+    np.testing.assert_array_equal(host(dst), oa)
+    np.testing.assert_array_equal(host(xsum), ox)
+    np.testing.assert_array_equal(host(asc), oasc)
+
+
 @pytest.mark.parametrize("tag,base,dims", FIXTURES)
 def test_pack_bit_exact_with_reference_packer(cuda, golden, tag, base, dims):
     for n, k in dims:

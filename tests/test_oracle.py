@@ -412,3 +412,32 @@ def test_tern_wgsl_gemv_oracle_is_dequant_dot():
     ref = xd @ _bf16_val(w).T
     # the only rounding is the f32 product f32(s) * xs of each group (~6e-8)
     np.testing.assert_allclose(y, ref, rtol=0, atol=1e-6 * np.max(np.abs(ref)))
+
+
+def _np_quantize_wasm(x):
+    """numpy restatement of cpu/kernel/src/lib.rs:566-606 in f32 arithmetic"""
+    x = np.asarray(x, np.float32)
+    amax = np.float32(np.max(np.abs(x))) if x.size else np.float32(0)
+    asc = np.float32(amax / np.float32(127.0)) if amax > 0 else np.float32(1e-9)
+    inv = np.float32(np.float32(1.0) / asc)
+    q = np.clip(np.rint((x * inv).astype(np.float32)), -127, 127).astype(np.int8)
+    return q, q.reshape(-1, 64).astype(np.int32).sum(1), asc
+
+
+def test_quantize_wasm_oracle_matches_restatement():
+    rng = np.random.default_rng(5)
+    rows = [rng.normal(0, 1, 2048), np.zeros(128), rng.normal(0, 3, 6144)]
+    r = np.zeros(64, np.float32)
+    r[:4] = [127.0, 0.5, -0.5, 1.5]          # x * (1/asc) lands exactly on .5 ties: nearest-even
+    rows.append(r)
+    for x in rows:
+        x = np.asarray(x, np.float32)
+        act, xsum, asc = oracle.quantize_act_wasm(x)
+        q, s, a = _np_quantize_wasm(x)
+        np.testing.assert_array_equal(act[0], q)
+        np.testing.assert_array_equal(xsum[0], s)
+        assert asc[0] == a
+    act, _, asc = oracle.quantize_act_wasm(rows[-1])
+    assert asc[0] == 1.0 and list(act[0][:4]) == [127, 0, 0, 2]    # ties to even, unlike tern.rs
+    _, _, asc0 = oracle.quantize_act_wasm(np.zeros(64, np.float32))
+    assert asc0[0] == np.float32(1e-9)
