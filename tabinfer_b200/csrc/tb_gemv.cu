@@ -79,8 +79,18 @@ __global__ void __launch_bounds__(THREADS, 2) k_gemv(const Args a)
     tb_pdl_wait();
     tb_pdl_trigger();
     if (KIND == KIND_F32) stage_f32<B>(a, act, red, nws);
+    else if (KIND == KIND_F32D) stage_f32d(a, act, xbuf, red, nws);
     else stage_q8<B, TERN>(a, act, xbuf, a.xbuf_bytes >> 2, red, nws);
     __syncthreads();
+
+    // the two-digit activation of this lane's groups (lane, lane + 32) in registers
+    constexpr bool DREG = KIND == KIND_F32D;
+    const bool dreg = DREG && G <= 64;
+    XD xd0{}, xd1{};
+    if (DREG && dreg) {
+        if (lane < G) load_xd(xd0, act, G, lane);
+        if (lane + 32 < G) load_xd(xd1, act, G, lane + 32);
+    }
 
     // f32 activation of a single row kept in registers (groups lane, lane+32),
     // un-swizzled on the way in so every register index is static
@@ -154,6 +164,18 @@ __global__ void __launch_bounds__(THREADS, 2) k_gemv(const Args a)
                                 }
                             } else {
                                 item_tern<B>(tw[r0 * G + g], tb_h2f(sbase[r0 * G + g]), act, G, g, acc[0][s]);
+                            }
+                        }
+                    } else if (DREG) {
+                        const uint4* wq = reinterpret_cast<const uint4*>(slot);
+                        for (int g = lane; g < G; g += 32) {
+                            XD xg;
+                            if (dreg) xg = g == lane ? xd0 : xd1;
+                            else load_xd(xg, act, G, g);
+#pragma unroll
+                            for (int q = 0; q < RPW; q++) {
+                                const int r = r0 + q * NW;
+                                if (r < bl.nrows) item_f32d(wq[r * G + g], tb_h2f(sbase[r * G + g]), xg, &acc[q][s][0]);
                             }
                         }
                     } else if (XREG && xreg) {
@@ -259,7 +281,10 @@ struct Plan {
     int RB, nst, slot_bytes, act_bytes, xbuf_bytes, nw_bytes, smem, grid, nrb;
 };
 
-int act_bytes_for(int kind, int B, int G) { return kind == KIND_F32 ? B * G * 128 : B * G * 40; }
+int act_bytes_for(int kind, int B, int G)
+{
+    return kind == KIND_F32 ? B * G * 128 : (kind == KIND_F32D ? G * 72 : B * G * 40);
+}
 
 int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count, bool norm, Plan& p)
 {
@@ -395,6 +420,8 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
         }
         return TB_OK;
     }
+    // one f32 row (gemvQ's decode route): the two-digit int8 form on dp4a
+    if (kind == KIND_F32 && batch == 1) kind = KIND_F32D;
     Plan p{};
     int rc = make_plan(ctx, kind, batch, (int)K, Ns, count, in.src == ACT_RMSNORM, p);
     if (rc) return rc;
@@ -417,6 +444,7 @@ int run(tb_ctx* ctx, int kind, int count, float* const* ys, const uint32_t* cons
     a.xbuf_bytes = p.xbuf_bytes;
     a.nw_bytes = p.nw_bytes;
     switch (kind) {
+    case KIND_F32D: return launch_B<1, KIND_F32D>(ctx, a, p);
     case KIND_Q8: return launch_kind<KIND_Q8>(ctx, a, p, batch);
     case KIND_GATEUP: return launch_kind<KIND_GATEUP>(ctx, a, p, batch);
     case KIND_TERN: return launch_kind<KIND_TERN>(ctx, a, p, batch);

@@ -15,7 +15,7 @@ constexpr int SMEM_HDR = 512;   // mbarriers (64 B) + reduction scratch (>= 72 f
 constexpr uint32_t WAIT_TRIES = 1000;
 constexpr int ERR_WAIT_TIMEOUT = 0x6d01;
 
-enum Kind { KIND_Q8 = 0, KIND_GATEUP = 1, KIND_F32 = 2, KIND_TERN = 3, KIND_GATEUP_TERN = 4 };
+enum Kind { KIND_Q8 = 0, KIND_GATEUP = 1, KIND_F32 = 2, KIND_TERN = 3, KIND_GATEUP_TERN = 4, KIND_F32D = 5 };
 __host__ __device__ constexpr bool kind_tern(int k) { return k == KIND_TERN || k == KIND_GATEUP_TERN; }
 __host__ __device__ constexpr bool kind_gateup(int k) { return k == KIND_GATEUP || k == KIND_GATEUP_TERN; }
 enum ActSrc { ACT_PREQ = 0, ACT_F32 = 1, ACT_RMSNORM = 2 };
@@ -301,6 +301,141 @@ __device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbu
         }
         __syncthreads();   // xbuf and red are reused by the next chunk
     }
+}
+
+// One f32 row (gemvQ, batch 1) as two int8 digit vectors, so the int4 dot runs
+// on dp4a instead of a float conversion per weight.  Per 32-group: sc =
+// max|x|/127, d1 = rn(x/sc), d2 = rn((x - sc*d1) * 128/sc), so
+// x = sc*d1 + (sc/128)*d2 within sc/256 (about 3e-5 of the group's largest
+// magnitude).  Both digit vectors are stored in the permuted Q8 layout of
+// stage_q8; corr = 8*(128*sum d1 + sum d2) removes the nibble bias (the weight
+// is nib - 8); xsf = sc/128.  The row dot is then
+// (s16 * xsf) * (128*dot(nib, d1) + dot(nib, d2) - corr).
+// Layout: x1lo[G] x1hi[G] x2lo[G] x2hi[G] (uint4), corr[G] (int), xsf[G] (float).
+__device__ void stage_f32d(const Args& a, unsigned char* act, float* xbuf, float* red, const uint16_t* nws)
+{
+    const int G = a.K >> 5, K4 = a.K >> 2;
+    uint4* x1lo = reinterpret_cast<uint4*>(act);
+    uint4* x1hi = x1lo + G;
+    uint4* x2lo = x1hi + G;
+    uint4* x2hi = x2lo + G;
+    int* corr = reinterpret_cast<int*>(x2hi + G);
+    float* xsf = reinterpret_cast<float*>(corr + G);
+    const int tid = threadIdx.x, h2 = tid & 1;
+    float4* xb4 = reinterpret_cast<float4*>(xbuf);
+    float ss[1], inv[1];
+    load_rows_swz<1>(reinterpret_cast<const float4*>(a.x), 1, K4, xb4, ss);
+    if (a.act_src == ACT_RMSNORM) {
+        block256_reduce_rows<1>(ss, red, inv);   // includes the __syncthreads for xb4
+        inv[0] = rms_inv(inv[0], a.K, a.eps);
+    } else {
+        __syncthreads();
+        inv[0] = 1.0f;
+    }
+    // 2 threads per 32-group: thread h2 of the pair owns k = 16 h2 .. 16 h2 + 15
+    for (int base = 0; base < G * 2; base += THREADS) {
+        const int item = (base + tid) >> 1;
+        const bool live = item < G;
+        const int g = live ? item : 0;
+        float v[16];
+        {
+            const float4* xg = xb4 + g * 8;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 t = xg[(4 * h2 + q) ^ (g & 7)];
+                v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+            }
+        }
+        if (a.act_src == ACT_RMSNORM) {
+            const uint4* wq = reinterpret_cast<const uint4*>(nws + g * 32 + 16 * h2);
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const uint4 wv = wq[q];
+                const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    const int k = 8 * q + 2 * h;
+                    v[k] = __fmul_rn(__fmul_rn(v[k], inv[0]), tb_h2f((uint16_t)(ww[h] & 0xffffu)));
+                    v[k + 1] = __fmul_rn(__fmul_rn(v[k + 1], inv[0]), tb_h2f((uint16_t)(ww[h] >> 16)));
+                }
+            }
+        }
+        float mx = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) mx = fmaxf(mx, fabsf(v[i]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        const float sc = q8_scale(mx), is = q8_inv(sc), is128 = __fmul_rn(is, 128.0f);
+        uint32_t d1w[4], d2w[4];
+        int s1 = 0, s2 = 0;
+#pragma unroll
+        for (int w = 0; w < 2; w++) {
+            uint32_t e1 = 0, o1 = 0, e2 = 0, o2 = 0;
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+#pragma unroll
+                for (int par = 0; par < 2; par++) {
+                    const float x = v[8 * w + 2 * h + par];
+                    const int q1 = q8_quant(x, is);
+                    const float r = __fsub_rn(x, __fmul_rn(sc, (float)q1));
+                    const int q2 = max(-127, min(127, __float2int_rn(__fmul_rn(r, is128))));
+                    s1 += q1;
+                    s2 += q2;
+                    const uint32_t b1 = ((uint32_t)q1 & 0xffu) << (8 * h), b2 = ((uint32_t)q2 & 0xffu) << (8 * h);
+                    if (par) { o1 |= b1; o2 |= b2; } else { e1 |= b1; e2 |= b2; }
+                }
+            }
+            d1w[2 * w] = e1; d1w[2 * w + 1] = o1;
+            d2w[2 * w] = e2; d2w[2 * w + 1] = o2;
+        }
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+        if (live) {
+            (h2 ? x1hi : x1lo)[g] = make_uint4(d1w[0], d1w[1], d1w[2], d1w[3]);
+            (h2 ? x2hi : x2lo)[g] = make_uint4(d2w[0], d2w[1], d2w[2], d2w[3]);
+            if (h2 == 0) {
+                corr[g] = 8 * (128 * s1 + s2);
+                xsf[g] = __fmul_rn(sc, 0.0078125f);   // sc / 128, exact
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// The two-digit activation of one 32-group (stage_f32d).
+struct XD {
+    uint4 a1l, a1h, a2l, a2h;
+    int corr;
+    float sf;
+};
+__device__ __forceinline__ void load_xd(XD& x, const unsigned char* act, int G, int g)
+{
+    const uint4* x1lo = reinterpret_cast<const uint4*>(act);
+    x.a1l = x1lo[g];
+    x.a1h = x1lo[G + g];
+    x.a2l = x1lo[2 * G + g];
+    x.a2h = x1lo[3 * G + g];
+    x.corr = reinterpret_cast<const int*>(x1lo + 4 * G)[g];
+    x.sf = reinterpret_cast<const float*>(x1lo + 4 * G)[G + g];
+}
+// int4 word quadruple (32 nibbles) against the two digit vectors: exact integer
+// sums, one conversion and one FMA a group
+__device__ __forceinline__ void item_f32d(const uint4 w, const float s, const XD& x, float* acc)
+{
+    const uint32_t l0 = w.x & 0x0f0f0f0fu, h0 = (w.x >> 4) & 0x0f0f0f0fu;
+    const uint32_t l1 = w.y & 0x0f0f0f0fu, h1 = (w.y >> 4) & 0x0f0f0f0fu;
+    const uint32_t l2 = w.z & 0x0f0f0f0fu, h2 = (w.z >> 4) & 0x0f0f0f0fu;
+    const uint32_t l3 = w.w & 0x0f0f0f0fu, h3 = (w.w >> 4) & 0x0f0f0f0fu;
+    int p0 = 0, p1 = 0, q0 = 0, q1 = 0;
+    p0 = __dp4a((int)l0, (int)x.a1l.x, p0); q0 = __dp4a((int)l0, (int)x.a2l.x, q0);
+    p1 = __dp4a((int)h0, (int)x.a1l.y, p1); q1 = __dp4a((int)h0, (int)x.a2l.y, q1);
+    p0 = __dp4a((int)l1, (int)x.a1l.z, p0); q0 = __dp4a((int)l1, (int)x.a2l.z, q0);
+    p1 = __dp4a((int)h1, (int)x.a1l.w, p1); q1 = __dp4a((int)h1, (int)x.a2l.w, q1);
+    p0 = __dp4a((int)l2, (int)x.a1h.x, p0); q0 = __dp4a((int)l2, (int)x.a2h.x, q0);
+    p1 = __dp4a((int)h2, (int)x.a1h.y, p1); q1 = __dp4a((int)h2, (int)x.a2h.y, q1);
+    p0 = __dp4a((int)l3, (int)x.a1h.z, p0); q0 = __dp4a((int)l3, (int)x.a2h.z, q0);
+    p1 = __dp4a((int)h3, (int)x.a1h.w, p1); q1 = __dp4a((int)h3, (int)x.a2h.w, q1);
+    const int t = 128 * (p0 + p1) + (q0 + q1) - x.corr;     // |t| < 2^24: exact as a float
+    *acc = fmaf(s * x.sf, (float)t, *acc);
 }
 
 // F32 layout: per (b, g) 8 float4, float4 index XOR-swizzled by (g & 7).

@@ -132,6 +132,7 @@ struct tb_qwen3 {
     unsigned char* step_layers = nullptr;        // device per-layer records
     int step_tern = -1;                          // weight format the plan was made for (1 ternary)
     unsigned* step_ctrl = nullptr;               // [256] block arrivals, grid barrier, abort word
+    unsigned* step_heads = nullptr;              // [layers][kv heads] phase-A arrivals of the persistent step
     unsigned char* step_attnq = nullptr;         // quantized attention output of the persistent step
     bool step_direct = false;                    // persistent step launched per call (not capturable)
     void* step_trace = nullptr;                  // optional phase trace of the persistent kernel
@@ -302,6 +303,7 @@ bool persistent_ok(tb_qwen3* m)
                                Ly.Vs);
         }
         if (alloc(m, &m->step_layers, host.size()) || alloc(m, &m->step_ctrl, 256) ||
+            alloc(m, &m->step_heads, (size_t)m->c.layers * m->nKv) ||
             alloc(m, &m->step_attnq, (size_t)m->nHq * m->c.head_dim / 32 * 40))
             return false;
         if (cudaMemcpy(m->step_layers, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -325,7 +327,7 @@ tb_step_io step_io(tb_qwen3* m)
     io.pos = m->pos;
     io.embed = m->embed;
     io.x = m->x[0]; io.q = m->q; io.k = m->k; io.v = m->v; io.qr = m->qr; io.attn = m->attn; io.swi = m->swi;
-    io.PO = m->PO; io.PML = m->PML; io.counters = m->counters; io.ctrl = m->step_ctrl;
+    io.PO = m->PO; io.PML = m->PML; io.counters = m->counters; io.ctrl = m->step_ctrl; io.head_cnt = m->step_heads;
     io.trace = m->step_trace;
     io.attnq = m->step_attnq;
     io.P = m->P;

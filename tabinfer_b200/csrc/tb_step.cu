@@ -75,6 +75,7 @@ struct StepArgs {
     unsigned* counters;      // [nKv] split arrivals (zero between steps)
     unsigned long long* bar_count;   // grid barrier: arrivals since the model was made (monotonic)
     unsigned* abort_word;    // == this launch's tag: a CTA gave up in this launch
+    unsigned* head_cnt;      // [L][nKv] phase-A blocks of each kv head written (zeroed by every launch)
     int* err;
     // optional phase trace: per CTA 1 + 38 * L %globaltimer stamps (kernel start;
     // per layer and phase: weights ready, activation row loaded, activation
@@ -120,6 +121,17 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     return v;
 }
 
+__device__ __forceinline__ void red_release_add_u32(unsigned* p, unsigned v)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 struct Ctl {
     unsigned long long base; // arrivals before this launch (a multiple of the grid)
     unsigned nb;             // barriers of this launch so far
@@ -136,7 +148,6 @@ __device__ bool grid_sync(const StepArgs& a, Ctl* ctl)
 {
     __syncthreads();          // the CTA's stores of this phase happen before thread 0's release
     if (threadIdx.x == 0 && !ctl->abort) {
-        __threadfence();
         ctl->nb++;
         const unsigned long long target = ctl->base + (unsigned long long)ctl->nb * gridDim.x;
         red_release_add(a.bar_count, 1ull);
@@ -407,7 +418,7 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
 // other rank's rows of this CTA -- local loads only -- and form
 // x + part_0 + ... + part_{P-1} in rank order, the sum k_tp_allreduce forms,
 // into the CTA's residual rows and x.
-// e = (barriers before this launch) + xi + 1: a launch passes 5L >= 2L + 1
+// e = (barriers before this launch) + xi + 1: a launch passes 4L >= 2L + 1
 // barriers and has 2L exchanges, so epochs grow across launches; a slot holds
 // epoch e - 2 or e, never more (a rank sends exchange xi + 2 only after it
 // received every rank's xi + 1, sent after that rank consumed xi), so the wait
@@ -504,8 +515,39 @@ __device__ void attn_prefetch(const StepArgs& a, const StepLayer& Ly, unsigned c
     unit.prefetch(true);
 }
 
+// Phase B of layer l may start for kv head h once the phase-A blocks of its
+// q heads and of its k and v rows are written: (GRP + 2) * hd / RBA arrivals on
+// head_cnt[l][h] (a release add by each block's thread 0 after the block's
+// rows), in place of a grid barrier.  Thread 0 polls (acquire, bounded); the
+// CTA barrier then orders every thread's reads of those rows after it.
+__device__ bool head_ready(const StepArgs& a, Ctl* ctl, int l, int h)
+{
+    if (threadIdx.x == 0 && !ctl->abort) {
+        const unsigned need = (unsigned)(a.nHq / a.nKv + 2) * (STEP_HD / RBA);
+        const unsigned* c = a.head_cnt + (size_t)l * a.nKv + h;
+        long long it = 0;
+        while (ld_acquire_u32(c) < need) {
+            ++it;
+            if ((it & 255) == 0 && *reinterpret_cast<volatile unsigned*>(a.abort_word) == ctl->tag) {
+                ctl->abort = 1;
+                break;
+            }
+            if (it > STEP_WAIT_LIMIT) {
+                atomicExch(a.err, ERR_STEP_BARRIER);
+                atomicExch(a.abort_word, ctl->tag);
+                ctl->abort = 1;
+                break;
+            }
+            if (it > 2048) __nanosleep(32);
+        }
+    }
+    __syncthreads();
+    return !ctl->abort;
+}
+
 template <int GRP, bool TERN>
-__device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned char* smem, const float* cs, int pos)
+__device__ void attn_run(const StepArgs& a, Ctl* ctl, const StepLayer& Ly, int l, unsigned char* smem, const float* cs,
+                         int pos)
 {
     using U = DecUnit<STEP_HD, GRP, 1, UW>;
     const AttnArgs t = attn_args(a, Ly, step_S(a, pos));
@@ -514,6 +556,7 @@ __device__ void attn_run(const StepArgs& a, const StepLayer& Ly, int l, unsigned
         const int u = blockIdx.x + gridDim.x * i;
         if (u >= a.nKv * a.nsplit) break;
         const int r = unit_rot(a, u);
+        if (!head_ready(a, ctl, l, r % a.nKv)) return;
         U unit(t, smem + a.off_P, r % a.nKv, r / a.nKv, 0, threadIdx.x, 0);
         unit.prep = &pin;
         unit.qout = a.attnq;
@@ -584,6 +627,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
         request(a, ctl, BUF_Q, 4, 0, smem, bars);
     }
     attn_prefetch<GRP>(a, sl[0], smem);
+    // this launch's head counters start at zero; the embed barrier below orders
+    // the zeroing before any phase-A arrival
+    for (int i = blockIdx.x * THREADS + tid; i < a.L * a.nKv; i += gridDim.x * THREADS) a.head_cnt[i] = 0u;
     // embed: this CTA's rows of x (the o / down row slice)
     {
         const int r0 = rowsC0(a), n = rowsC(a);
@@ -613,9 +659,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                 float* y = b.mat == WQ ? a.q : (b.mat == WK ? a.k : a.v);
                 gemv_rows<1, TERN>(smem + a.off_act, wR, nullptr, RBA, a.H / 32, y, b.row0, nullptr);
             }
-            __syncthreads();
+            __syncthreads();           // the block's rows are written before thread 0's release
             STAMP(0, 3);
-            if (!grid_sync(a, ctl)) goto drain;
+            if (b.live && tid == 0 && !ctl->abort) {
+                const int kvh = b.mat == WQ ? b.row0 / STEP_HD / (a.nHq / a.nKv) : b.row0 / STEP_HD;
+                red_release_add_u32(a.head_cnt + (size_t)l * a.nKv + kvh, 1u);
+            }
             STAMP(0, 4);
         }
         // ---- B: attention (prep'd q, cache row pos written in A)
@@ -625,7 +674,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             // barrier and the activation loads do not queue behind them)
             if (tid == 0) request(a, ctl, BUF_R, 2, l, smem, bars);
             STAMP_REQ(1);
-            attn_run<GRP, TERN>(a, Ly, l, smem, cs, pos);
+            attn_run<GRP, TERN>(a, ctl, Ly, l, smem, cs, pos);
             __syncthreads();
             STAMP(1, 3);
             if (!grid_sync(a, ctl)) goto drain;
@@ -741,9 +790,10 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     a.tern = tern ? 1 : 0;
     a.P = P > 1 ? P : 1;
     if (a.P > TB_TP_MAX) return TB_ERR_UNSUPPORTED;
-    // the exchange epochs: a launch passes 1 + 4L + (L - 1) = 5L grid barriers and
-    // has 2L exchanges; epochs stay unique across launches while 5L >= 2L + 1
-    if (5 * L < 2 * L + 1) return TB_ERR_UNSUPPORTED;
+    // the exchange epochs: a launch passes 1 + 3L + (L - 1) = 4L grid barriers (the
+    // embed, after attention, o and gate/up, and after down but the last) and has
+    // 2L exchanges; epochs stay unique across launches while 4L >= 2L + 1
+    if (4 * L < 2 * L + 1) return TB_ERR_UNSUPPORTED;
     a.rpC = (H + G - 1) / G;
     a.rpD = (I + G - 1) / G;
     if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
@@ -803,6 +853,8 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.attnq = io->attnq;
     a.PO = io->PO; a.PML = io->PML; a.counters = io->counters;
     a.bar_count = reinterpret_cast<unsigned long long*>(io->ctrl + 64); a.abort_word = io->ctrl + 128;
+    a.head_cnt = io->head_cnt;
+    TB_REQUIRE(ctx, a.head_cnt != nullptr, "decode step: no head counters");
     a.err = ctx->dev_error;
     a.trace = reinterpret_cast<unsigned long long*>(io->trace);
     const int P = io->P > 1 ? io->P : 1;

@@ -252,8 +252,12 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b)
     return d;
 }
 
+// CTAs an SM the streaming form is planned for: four at batch 1 with at most
+// two 64-groups a lane (64 registers), else two
+__host__ __device__ constexpr int t2_ctas(int B, int NBL) { return (B == 1 && NBL <= 2) ? 4 : 2; }
+
 template <int B, int NBL>
-__global__ void __launch_bounds__(T2_THREADS, 2) k_gemv_tern2(const Tern2Args a)
+__global__ void __launch_bounds__(T2_THREADS, t2_ctas(B, NBL)) k_gemv_tern2(const Tern2Args a)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     const int nb = a.K >> 6, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -387,17 +391,20 @@ bool tern2_plan(int B, int64_t N, int64_t K, int num_sms, T2Plan* p)
     const int NBL = (nb + 31) / 32;
     if (NBL > 4 || B * NBL > 4) return false;              // <= 64 activation registers a lane
     const int rowb = (int)(K / 4) + nb * 4;                // code + scale bytes a row
-    // one chain lane per (activation row, row); enough tiles to give every SM
-    // two CTAs' worth when the matrix allows it; large K keeps the stages small
-    int TR = 32 / B >= 32 ? 32 : (32 / B >= 16 ? 16 : 8);
+    // one chain lane per (activation row, row), at most 16 rows a tile (more
+    // CTAs an SM hide the per-tile barrier better than bigger tiles); enough tiles
+    // to give every SM two CTAs' worth when the matrix allows it; large K keeps
+    // the stages small
+    int TR = B == 1 ? 16 : (32 / B >= 16 ? 16 : 8);
     while (TR > 8 && ((N + TR - 1) / TR < 2LL * num_sms || TR * rowb > 32 * 1024)) TR /= 2;
     p->TR = TR;
     p->NBL = NBL;
     p->park_ld = ((nb + 15) & ~15) + 2;                    // float4 rows, 4-bank shift between rows
     p->stage_bytes = (TR * rowb + 127) & ~127;
     const size_t park = 2 * (size_t)B * TR * p->park_ld * 8;
-    // about 104 KB a CTA (two CTAs an SM), at least 2 and at most 6 stages
-    int nst = (int)((104 * 1024 - 256 - (long long)park) / p->stage_bytes);
+    // shared memory for t2_ctas CTAs an SM (~200 KB), at least 2 and at most 6 stages
+    const long long budget = 200LL * 1024 / t2_ctas(B, NBL) - 1024;
+    int nst = (int)((budget - 256 - (long long)park) / p->stage_bytes);
     nst = std::max(2, std::min(6, nst));
     p->NST = nst;
     p->smem = 128 + park + 128 + (size_t)nst * p->stage_bytes;

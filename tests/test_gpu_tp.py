@@ -363,7 +363,10 @@ def test_tp2_exchange_timeout_poisons_until_reset(cuda):
     for r in range(2):
         assert not isinstance(res[r], str), res[r]
     codes = res[0][0]
-    assert codes[0] == 0x5103, "first step: 0x%x" % codes[0]        # ERR_STEP_TP: the exchange wait ran out
+    # the first bounded wait to run out: ERR_STEP_TP (0x5103) in a CTA waiting for the
+    # peer's packets, or ERR_STEP_BARRIER (0x5101) in a CTA that owns no residual rows
+    # (it skips the exchange) waiting at the next grid barrier for the others
+    assert codes[0] in (0x5103, 0x5101), "first step: 0x%x" % codes[0]
     assert codes[1] < 20.0, "the bounded wait took %.1f s" % codes[1]
     assert codes[2] == 0x5104, "poisoned step: 0x%x" % codes[2]     # refused until the reset
     for r in range(2):
