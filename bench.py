@@ -463,11 +463,13 @@ def prefill_extra(dev, peak_tf, stream):
     return out
 
 
-def moe_extra(dev, peak_gbs, stream):
+def moe_extra(dev, peak_gbs, stream, group=32):
     """One LFM2.5-8B-A1B-shaped int3 MoE FFN (hidden 2048, 32 experts, I 1792,
-    top-4, group-32 int3 as the reference's _requant43) over 1 / 8 / 64 tokens:
-    router + grouped expert GEMVs + combine.  Algorithmic bytes = the int3 planes
-    and scales of every expert routed to + activations."""
+    top-4) over 1 / 8 / 64 tokens: router + grouped expert GEMVs + combine.
+    group 32: the reference's _requant43 path (bf16 -> int4 G32 -> int3); group
+    128: the configuration's group-128 int3 quantized from bf16 directly.
+    Algorithmic bytes = the int3 planes and scales of every expert routed to +
+    activations."""
     import torch
     import tabinfer_b200 as tb
     H, I, NE, K = 2048, 1792, 32, 4
@@ -475,13 +477,18 @@ def moe_extra(dev, peak_gbs, stream):
     ws = []
     for rows, cols in ((NE * I, H), (NE * I, H), (NE * H, I)):
         w = (torch.randn(rows, cols, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        pk, sc = tb.quantize_int4_bf16(w.view(torch.int16))
-        del w
-        ws.append(tb.requant_int3(pk, sc))
-        del pk, sc
-    per_expert = (2 * I * H + H * I) * 14 // 32
+        if group == 32:
+            pk, sc = tb.quantize_int4_bf16(w.view(torch.int16))
+            del w
+            ws.append(tb.requant_int3(pk, sc))
+            del pk, sc
+        else:
+            ws.append(tb.quant_int3(w.view(torch.int16), group))
+            del w
+    per_expert = (2 * I * H + H * I) * 12 // 32 + (2 * I * H + H * I) * 2 // group
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    out = {}
+    torch.cuda.synchronize(dev)
+    out = {"group": group}
     for T in (1, 8, 64):
         logits = torch.randn(T, NE, device=dev, generator=g)
         bias = torch.zeros(NE, device=dev)
@@ -490,7 +497,7 @@ def moe_extra(dev, peak_gbs, stream):
 
         def step():
             idx, wt = tb.moe_router(logits, bias, K)
-            tb.moe_ffn_int3(x, a, idx, wt, ws[0], ws[1], ws[2], NE, H, I)
+            tb.moe_ffn_int3(x, a, idx, wt, ws[0], ws[1], ws[2], NE, H, I, group=group)
         step()
         idx, _ = tb.moe_router(logits, bias, K)
         used = len(set(idx.flatten().tolist()))
@@ -1595,6 +1602,7 @@ def main():
         extras["prefill_gemm_1.7b"]["peak"] = "bf16_tflops %s (cuBLAS burst)" % (
             "measured" if peaks else "fallback 1590")
         extras["moe_int3_lfm2.5"] = moe_extra(dev, peak, stream)
+        extras["moe_int3_lfm2.5_group128"] = moe_extra(dev, peak, stream, group=128)
         extras["ternary_wgsl_bonsai_1.7b"] = tern_extra(dev, peak, peaks.get("bf16_tflops", 1590.0), stream)
         extras["ternary_wgsl_bonsai_1.7b"]["decode_step_context4096"] = bonsai_extra(dev, peak, stream)
         extras["prefill_attention_1.7b"] = prefill_attn_extra(dev, peaks.get("bf16_tflops", 1590.0), stream)

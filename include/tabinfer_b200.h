@@ -455,6 +455,22 @@ TB_API int tb_moe_ffn_int3(tb_ctx *ctx, float *x_out, const float *x_in, const u
                            const uint32_t *w1p, const uint16_t *w1s, const uint32_t *w3p, const uint16_t *w3s,
                            const uint32_t *w2p, const uint16_t *w2s, int64_t T, int64_t K, int64_t nE,
                            int64_t H, int64_t I);
+/* The same FFN with one f16 scale per `group` weights (32: the reference's
+ * _requant43 layout, tb_moe_ffn_int3; 128: the group-128 int3 of the LFM2.5
+ * benchmark configuration): planes stay three u32 per 32 weights, scales are
+ * [rows][K/group].  H and I multiples of group. */
+TB_API int tb_moe_ffn_int3_g(tb_ctx *ctx, float *x_out, const float *x_in, const uint32_t *idx, const float *wt,
+                             const uint32_t *w1p, const uint16_t *w1s, const uint32_t *w3p, const uint16_t *w3s,
+                             const uint32_t *w2p, const uint16_t *w2s, int64_t T, int64_t K, int64_t nE,
+                             int64_t H, int64_t I, int group);
+/* bf16 [rows][K] -> int3 planes [rows][K/32][3] (stored q + 4) + f16 scales
+ * [rows][K/group], group 32 or 128: scale = f16(max|w| / 4) (the engine's
+ * f32ToF16 of _requant43, lfm25.js:833-855), q = clamp(rn(w / scale), -4, 3).
+ * No reference counterpart: the reference reaches int3 only from int4 at
+ * group 32 (tb_requant_int4_int3); the benchmark's LFM2.5 configuration names
+ * group-128 int3 from bf16 weights. */
+TB_API int tb_quant_int3_bf16(tb_ctx *ctx, const uint16_t *w_bf16, uint32_t *p3, uint16_t *s3, int64_t rows,
+                              int64_t K, int group);
 
 /* Expert parallelism (no reference counterpart: the reference keeps every
  * expert on one device, lfm25.js:824-830): the MoE FFN of tb_moe_ffn_int3 over

@@ -427,13 +427,27 @@ def moe_router(logits, bias, K):
     return idx, wt
 
 
-def moe_ffn_int3(a, idx, wt, w1, w3, w2, H, I):
-    """sum_k wt * W2_e(silu(W1_e a) * W3_e a) per token (f64); w* = (planes, scales)."""
+def moe_ffn_int3(a, idx, wt, w1, w3, w2, H, I, group=32):
+    """sum_k wt * W2_e(silu(W1_e a) * W3_e a) per token (f64); w* = (planes, scales);
+    group: weights per f16 scale (32 or 128)."""
     a = np.ascontiguousarray(a, np.float32)
     T = a.shape[0]
     K = idx.shape[1]
     out = np.zeros((T, H), np.float64)
-    lib().tbo_moe_ffn_int3(_ptr(a), _ptr(np.ascontiguousarray(idx, np.uint32)), _ptr(np.ascontiguousarray(wt, np.float32)),
-                           _ptr(w1[0]), _ptr(w1[1]), _ptr(w3[0]), _ptr(w3[1]), _ptr(w2[0]), _ptr(w2[1]),
-                           _I(T), _I(K), _I(H), _I(I), _ptr(out))
+    c = lambda t: np.ascontiguousarray(t)  # noqa: E731
+    w1, w3, w2 = [(c(p), c(s)) for p, s in (w1, w3, w2)]
+    lib().tbo_moe_ffn_int3_g(_ptr(a), _ptr(np.ascontiguousarray(idx, np.uint32)),
+                             _ptr(np.ascontiguousarray(wt, np.float32)),
+                             _ptr(w1[0]), _ptr(w1[1]), _ptr(w3[0]), _ptr(w3[1]), _ptr(w2[0]), _ptr(w2[1]),
+                             _I(T), _I(K), _I(H), _I(I), _I(group), _ptr(out))
     return out
+
+
+def quant_int3(w, group):
+    """bf16 bits [rows, K] -> int3 planes [rows][K/32][3], f16 scales [rows][K/group]."""
+    w = np.ascontiguousarray(w, np.uint16)
+    rows, K = w.shape
+    p3 = np.zeros((rows, K // 32, 3), np.uint32)
+    s3 = np.zeros((rows, K // group), np.uint16)
+    lib().tbo_quant_int3(_ptr(w), _I(rows), _I(K), _I(group), _ptr(p3), _ptr(s3))
+    return p3, s3

@@ -228,15 +228,67 @@ static void *worker(void *arg)
     return NULL;
 }
 
+/* Persistent worker pool, as the reference's CPU engines keep their workers
+ * (cpu/kernel/cpuengine-mt.js spawns them once): a call publishes the job under
+ * a new generation number, workers 1 .. threads-1 join the chunk loop with the
+ * caller, and the caller waits until every participant has left it.  Workers
+ * spin briefly on the generation before sleeping on a condition variable. */
+#define POOL_MAX 256
+static struct {
+    pthread_mutex_t mu;
+    pthread_cond_t go, done;
+    pthread_t tid[POOL_MAX];
+    int n;                       /* workers started */
+    volatile unsigned gen;       /* job generation */
+    job_t *volatile job;
+    volatile int want;           /* workers taking part in the current job */
+    int left;                    /* participants still in the job */
+} g_pool = {PTHREAD_MUTEX_INITIALIZER, PTHREAD_COND_INITIALIZER, PTHREAD_COND_INITIALIZER};
+
+static void *pool_worker(void *arg)
+{
+    const int idx = (int)(intptr_t)arg;
+    unsigned seen = 0;
+    for (;;) {
+        unsigned g;
+        int spins = 0;
+        while ((g = __atomic_load_n(&g_pool.gen, __ATOMIC_ACQUIRE)) == seen && spins < 200000) { spins++; }
+        if (g == seen) {
+            pthread_mutex_lock(&g_pool.mu);
+            while ((g = g_pool.gen) == seen) pthread_cond_wait(&g_pool.go, &g_pool.mu);
+            pthread_mutex_unlock(&g_pool.mu);
+        }
+        seen = g;
+        if (idx < g_pool.want) {
+            worker(g_pool.job);
+            pthread_mutex_lock(&g_pool.mu);
+            if (--g_pool.left == 0) pthread_cond_signal(&g_pool.done);
+            pthread_mutex_unlock(&g_pool.mu);
+        }
+    }
+    return NULL;
+}
+
 static void run_job(job_t *j, int threads)
 {
     j->cursor = 0;
     if (threads <= 1) { run_rows(j, 0, j->N); return; }
-    pthread_t tid[256];
-    if (threads > 256) threads = 256;
-    for (int t = 1; t < threads; t++) pthread_create(&tid[t], NULL, worker, j);
+    if (threads > POOL_MAX) threads = POOL_MAX;
+    pthread_mutex_lock(&g_pool.mu);
+    while (g_pool.n < threads - 1) {
+        pthread_create(&g_pool.tid[g_pool.n], NULL, pool_worker, (void *)(intptr_t)g_pool.n);
+        g_pool.n++;
+    }
+    g_pool.job = j;
+    g_pool.want = threads - 1;
+    g_pool.left = threads - 1;
+    __atomic_store_n(&g_pool.gen, g_pool.gen + 1, __ATOMIC_RELEASE);
+    pthread_cond_broadcast(&g_pool.go);
+    pthread_mutex_unlock(&g_pool.mu);
     worker(j);
-    for (int t = 1; t < threads; t++) pthread_join(tid[t], NULL);
+    pthread_mutex_lock(&g_pool.mu);
+    while (g_pool.left > 0) pthread_cond_wait(&g_pool.done, &g_pool.mu);
+    pthread_mutex_unlock(&g_pool.mu);
 }
 
 /* Ternary GEMV (tern.rs gemv_tern, AVX2 backend) over N rows with `threads`

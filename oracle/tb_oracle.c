@@ -739,6 +739,42 @@ TBO_API uint16_t tbo_engine_f32_to_f16(float v)
     return (uint16_t)(sign | ((uint32_t)e << 10) | ((mant + 0x00001000u) >> 13));
 }
 
+/* bf16 -> int3 of the LFM2.5 benchmark configuration (group 32 or 128; no
+ * reference counterpart): per (row, group) scale = f16(max|w|/4) by the
+ * engine's f32ToF16, q = clamp(round-to-nearest-even(w / scale), -4, 3) in f32,
+ * stored q + 4 in the _requant43 bitplanes; max|w| = 0 -> scale 0, q = 0. */
+TBO_API void tbo_quant_int3(const uint16_t *w, int64_t rows, int64_t K, int64_t group, uint32_t *p3, uint16_t *s3)
+{
+    const int64_t ng = rows * (K / group), gp = group / 32;
+    for (int64_t gi = 0; gi < ng; gi++) {
+        const uint16_t *src = w + gi * group;
+        float m = 0.0f;
+        for (int64_t i = 0; i < group; i++) {
+            float a = fabsf(bits_f32((uint32_t)src[i] << 16));
+            m = a > m ? a : m;
+        }
+        const uint16_t sh = tbo_engine_f32_to_f16(m / 4.0f);
+        const float sc = (float)tbo_f16_to_f64(sh);
+        for (int64_t j = 0; j < gp; j++) {
+            uint32_t b0 = 0, b1 = 0, b2 = 0;
+            for (int i = 0; i < 32; i++) {
+                const float v = bits_f32((uint32_t)src[j * 32 + i] << 16);
+                int q = 0;
+                if (sc > 0.0f) {
+                    q = (int)rintf(v / sc);
+                    q = q > 3 ? 3 : (q < -4 ? -4 : q);
+                }
+                const uint32_t st = (uint32_t)(q + 4);
+                b0 |= (st & 1u) << i;
+                b1 |= ((st >> 1) & 1u) << i;
+                b2 |= ((st >> 2) & 1u) << i;
+            }
+            p3[(gi * gp + j) * 3] = b0; p3[(gi * gp + j) * 3 + 1] = b1; p3[(gi * gp + j) * 3 + 2] = b2;
+        }
+        s3[gi] = sh;
+    }
+}
+
 /* _requant43, lfm25.js:833-855: int4 group (nibble q+8) -> int3 bitplanes of
  * stored value q3+4 with q3 = clamp(Math.round(q4 * (4/m)), -4, 3), m = max|q4|;
  * scale = f32(f16(s4) * m / 4) through the engine's f32ToF16; m = 0 -> scale 0
@@ -807,8 +843,8 @@ TBO_API void tbo_moe_router(const float *logits, const float *bias, int64_t T, i
 
 /* idxGemv3 (lfm25.js:1924-1973) for one pair: y[n] = sum_g s[row,g] * sum_i (q_i - 4) x[32g+i],
  * row = e*N + n; f64. */
-static void moe_gemv3_row(const uint32_t *p3, const uint16_t *s3, int64_t e, int64_t N, int64_t Kc, const double *x,
-                          double *y)
+static void moe_gemv3_row_g(const uint32_t *p3, const uint16_t *s3, int64_t e, int64_t N, int64_t Kc, const double *x,
+                            double *y, int64_t sg)
 {
     const int64_t G = Kc / 32;
     for (int64_t n = 0; n < N; n++) {
@@ -821,7 +857,7 @@ static void moe_gemv3_row(const uint32_t *p3, const uint16_t *s3, int64_t e, int
                 int st = (int)(((w[0] >> i) & 1u) | (((w[1] >> i) & 1u) << 1) | (((w[2] >> i) & 1u) << 2));
                 sum += (double)(st - 4) * x[g * 32 + i];
             }
-            acc += tbo_f16_to_f64(s3[row * G + g]) * sum;
+            acc += tbo_f16_to_f64(s3[row * (G / sg) + g / sg]) * sum;
         }
         y[n] = acc;
     }
@@ -829,10 +865,12 @@ static void moe_gemv3_row(const uint32_t *p3, const uint16_t *s3, int64_t e, int
 
 /* MoE FFN (w1/w3 gate+up with SiLU, w2 down, MOECOMBINE lfm25.js:1982-2000):
  * x_out[t] = x_in_res[t] + sum_k wt[t,k] * W2_e(silu(W1_e a_t) * W3_e a_t). */
-TBO_API void tbo_moe_ffn_int3(const float *a, const uint32_t *idx, const float *wt, const uint32_t *w1p,
-                              const uint16_t *w1s, const uint32_t *w3p, const uint16_t *w3s, const uint32_t *w2p,
-                              const uint16_t *w2s, int64_t T, int64_t K, int64_t H, int64_t I, double *out)
+TBO_API void tbo_moe_ffn_int3_g(const float *a, const uint32_t *idx, const float *wt, const uint32_t *w1p,
+                                const uint16_t *w1s, const uint32_t *w3p, const uint16_t *w3s, const uint32_t *w2p,
+                                const uint16_t *w2s, int64_t T, int64_t K, int64_t H, int64_t I, int64_t group,
+                                double *out)
 {
+    const int64_t sg = group / 32;
     double *xa = (double *)malloc(sizeof(double) * (size_t)H);
     double *g = (double *)malloc(sizeof(double) * (size_t)I);
     double *u = (double *)malloc(sizeof(double) * (size_t)I);
@@ -841,12 +879,19 @@ TBO_API void tbo_moe_ffn_int3(const float *a, const uint32_t *idx, const float *
         for (int64_t h = 0; h < H; h++) { xa[h] = a[t * H + h]; out[t * H + h] = 0.0; }
         for (int64_t k = 0; k < K; k++) {
             const int64_t e = idx[t * K + k];
-            moe_gemv3_row(w1p, w1s, e, I, H, xa, g);
-            moe_gemv3_row(w3p, w3s, e, I, H, xa, u);
+            moe_gemv3_row_g(w1p, w1s, e, I, H, xa, g, sg);
+            moe_gemv3_row_g(w3p, w3s, e, I, H, xa, u, sg);
             for (int64_t i = 0; i < I; i++) g[i] = g[i] / (1.0 + exp(-g[i])) * u[i];
-            moe_gemv3_row(w2p, w2s, e, H, I, g, o);
+            moe_gemv3_row_g(w2p, w2s, e, H, I, g, o, sg);
             for (int64_t h = 0; h < H; h++) out[t * H + h] += (double)wt[t * K + k] * o[h];
         }
     }
     free(xa); free(g); free(u); free(o);
+}
+
+TBO_API void tbo_moe_ffn_int3(const float *a, const uint32_t *idx, const float *wt, const uint32_t *w1p,
+                              const uint16_t *w1s, const uint32_t *w3p, const uint16_t *w3s, const uint32_t *w2p,
+                              const uint16_t *w2s, int64_t T, int64_t K, int64_t H, int64_t I, double *out)
+{
+    tbo_moe_ffn_int3_g(a, idx, wt, w1p, w1s, w3p, w3s, w2p, w2s, T, K, H, I, 32, out);
 }

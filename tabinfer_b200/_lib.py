@@ -83,6 +83,8 @@ SIGNATURES = {
     "tb_requant_int4_int3": [P, P, P, P, P, I64, I64],
     "tb_moe_router": [P, P, P, P, P, I64, I64, I64],
     "tb_moe_ffn_int3": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64],
+    "tb_moe_ffn_int3_g": [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I32],
+    "tb_quant_int3_bf16": [P, P, P, P, I64, I64, I32],
     "tb_moe_ep_create": [P, ctypes.c_int, ctypes.c_int, I64, I64, I64, I64, I64, P],
     "tb_moe_ep_destroy": [P],
     "tb_moe_ep_handle": [P, P],

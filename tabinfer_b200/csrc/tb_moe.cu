@@ -168,6 +168,41 @@ __global__ void __launch_bounds__(256) k_moe_group(const uint32_t* __restrict__ 
     }
 }
 
+// ---- bf16 -> int3 at group 32 or 128 (config 5's format; not in the reference) ----
+// One warp per (row, group): scale = f16(max|w| / 4) through the engine's
+// f32ToF16 (the conversion _requant43 uses for its scales), q = clamp(rn(w /
+// scale), -4, 3) in f32, stored q + 4 in the three bitplanes of every 32-group
+// of the group (the same planes as _requant43's); max|w| == 0 gives scale 0 and
+// q = 0.  GP = 32-groups per scale group.
+__global__ void __launch_bounds__(256) k_quant_int3(const uint16_t* __restrict__ w, uint32_t* __restrict__ p3,
+                                                    uint16_t* __restrict__ s3, long long ngroups, int GP)
+{
+    // weights are inputs only; a dependent GEMV may start once they are all written
+    tb_pdl_wait();
+    const int lane = threadIdx.x & 31;
+    for (long long gi = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; gi < ngroups;
+         gi += ((long long)gridDim.x * blockDim.x) >> 5) {
+        const uint16_t* src = w + gi * 32 * GP;
+        float m = 0.0f;
+        for (int j = 0; j < GP; j++) m = fmaxf(m, fabsf(__uint_as_float((uint32_t)src[j * 32 + lane] << 16)));
+        m = warp_max(m);
+        const uint32_t sh = engine_f32_to_f16(__fdiv_rn(m, 4.0f));
+        const float sc = __half2float(__ushort_as_half((unsigned short)sh));
+        for (int j = 0; j < GP; j++) {
+            const float v = __uint_as_float((uint32_t)src[j * 32 + lane] << 16);
+            const int q = sc > 0.0f ? max(-4, min(3, __float2int_rn(__fdiv_rn(v, sc)))) : 0;
+            const uint32_t st = (uint32_t)(q + 4);
+            const uint32_t b0 = __ballot_sync(0xffffffffu, st & 1u), b1 = __ballot_sync(0xffffffffu, (st >> 1) & 1u),
+                           b2 = __ballot_sync(0xffffffffu, (st >> 2) & 1u);
+            if (lane == 0) {
+                uint32_t* d = p3 + (gi * GP + j) * 3;
+                d[0] = b0; d[1] = b1; d[2] = b2;
+            }
+        }
+        if (lane == 0) s3[gi] = (uint16_t)sh;
+    }
+}
+
 // ---- grouped int3 expert GEMV ---------------------------------------------------
 enum { MOE_GATEUP = 0, MOE_DOWN = 1 };
 
@@ -183,6 +218,7 @@ struct MoeArgs {
     const int* order;            // position -> pair; null: the identity
     const int* offsets;
     int N, Kc, G;
+    int sg = 1;                  // 32-groups per scale: 1 (group 32, the reference's) or 4 (group 128)
     const int* xrow = nullptr;   // when set, pair p reads activation row xrow[p]
     int bpc = MOE_BPC;           // row blocks per CTA
     int mb = MB;                 // pairs per chunk (<= MB): the staged activations' rows
@@ -246,7 +282,7 @@ __global__ void __launch_bounds__(MOE_THREADS) k_moe_gemv3(const MoeArgs a)
                     d.w[j][t][m][0] = ok ? __ldg(w) : 0u;
                     d.w[j][t][m][1] = ok ? __ldg(w + 1) : 0u;
                     d.w[j][t][m][2] = ok ? __ldg(w + 2) : 0u;
-                    d.s[j][t][m] = ok ? tb_h2f(__ldg(a.s3[m] + row * G + (ok ? g : 0))) : 0.0f;
+                    d.s[j][t][m] = ok ? tb_h2f(__ldg(a.s3[m] + row * (G / a.sg) + (ok ? g : 0) / a.sg)) : 0.0f;
                 }
     };
     for (int c0 = 0; c0 < np; c0 += a.mb) {
@@ -421,13 +457,15 @@ TB_API int tb_moe_router(tb_ctx* ctx, uint32_t* idx, float* wt, const float* log
 // The MoE FFN of T tokens: x_out[t] += sum_k wt[t,k] * W2_e (silu(W1_e a_t) * (W3_e a_t)),
 // e = idx[t,k], a_t = x_in row t.  w1/w3: [nE*I][H/32][3] planes + [nE*I][H/32]
 // scales; w2: [nE*H][I/32][3] + [nE*H][I/32].  Scratch: context-owned.
-TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const uint32_t* idx, const float* wt,
-                           const uint32_t* w1p, const uint16_t* w1s, const uint32_t* w3p, const uint16_t* w3s,
-                           const uint32_t* w2p, const uint16_t* w2s, int64_t T, int64_t K, int64_t nE, int64_t H,
-                           int64_t I)
+TB_API int tb_moe_ffn_int3_g(tb_ctx* ctx, float* x_out, const float* x_in, const uint32_t* idx, const float* wt,
+                             const uint32_t* w1p, const uint16_t* w1s, const uint32_t* w3p, const uint16_t* w3s,
+                             const uint32_t* w2p, const uint16_t* w2s, int64_t T, int64_t K, int64_t nE, int64_t H,
+                             int64_t I, int group)
 {
     if (!ctx) return TB_ERR_INVALID;
     TB_REQUIRE(ctx, x_out && x_in && idx && wt && w1p && w1s && w3p && w3s && w2p && w2s, "null pointer");
+    TB_REQUIRE(ctx, group == 32 || group == 128, "int3 scale group must be 32 or 128 (got %d)", group);
+    TB_REQUIRE(ctx, H % group == 0 && I % group == 0, "H and I must be multiples of the scale group");
     TB_REQUIRE(ctx, T > 0 && K > 0 && nE > 0 && nE <= 256 && H % 32 == 0 && I % 32 == 0 && H > 0 && I > 0 &&
                         H <= 2048 && I <= 2048,
                "bad MoE shape (H, I multiples of 32 up to 2048, nE <= 256)");
@@ -447,6 +485,7 @@ TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const u
                               active + nE, ctx->dev_error);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe group launch: %s", cudaGetErrorString(e));
     MoeArgs g{x_in, H, (int)K, {w1p, w3p}, {w1s, w3s}, swi, order, offsets, (int)I, (int)H, (int)(H / 32)};
+    g.sg = group / 32;
     // fewer pairs than experts (decode): each routed expert's rows spread over
     // more CTAs, one row block each, for more weight bytes in flight
     g.bpc = P < nE ? 1 : MOE_BPC;
@@ -460,6 +499,7 @@ TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const u
     int rc = launch_moe<MOE_GATEUP>(ctx, g, nslots);
     if (rc) return rc;
     MoeArgs d{swi, I, 1, {w2p, w2p}, {w2s, w2s}, o, order, offsets, (int)H, (int)I, (int)(I / 32)};
+    d.sg = g.sg;
     d.bpc = g.bpc;
     d.active = g.active;
     d.nactive = g.nactive;
@@ -470,6 +510,28 @@ TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const u
     const int grid = (int)std::min<long long>((total + 255) / 256, (long long)ctx->num_sms * 8);
     e = tb_launch(ctx, k_moe_combine, dim3(grid), dim3(256), 0, x_out, (const float*)o, wt, (int)H, (int)K, total);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "moe combine launch: %s", cudaGetErrorString(e));
+    return TB_OK;
+}
+
+TB_API int tb_moe_ffn_int3(tb_ctx* ctx, float* x_out, const float* x_in, const uint32_t* idx, const float* wt,
+                           const uint32_t* w1p, const uint16_t* w1s, const uint32_t* w3p, const uint16_t* w3s,
+                           const uint32_t* w2p, const uint16_t* w2s, int64_t T, int64_t K, int64_t nE, int64_t H,
+                           int64_t I)
+{
+    return tb_moe_ffn_int3_g(ctx, x_out, x_in, idx, wt, w1p, w1s, w3p, w3s, w2p, w2s, T, K, nE, H, I, 32);
+}
+
+TB_API int tb_quant_int3_bf16(tb_ctx* ctx, const uint16_t* w_bf16, uint32_t* p3, uint16_t* s3, int64_t rows,
+                              int64_t K, int group)
+{
+    if (!ctx) return TB_ERR_INVALID;
+    TB_REQUIRE(ctx, w_bf16 && p3 && s3, "null pointer");
+    TB_REQUIRE(ctx, group == 32 || group == 128, "int3 scale group must be 32 or 128 (got %d)", group);
+    TB_REQUIRE(ctx, rows > 0 && K > 0 && K % group == 0, "bad shape (K %% group must be 0)");
+    const long long ng = rows * (K / group);
+    const int grid = (int)std::min<long long>((ng * 32 + 255) / 256, (long long)ctx->num_sms * 16);
+    cudaError_t e = tb_launch(ctx, k_quant_int3, dim3(grid), dim3(256), 0, w_bf16, p3, s3, ng, group / 32);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_int3 launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
 

@@ -267,13 +267,26 @@ def moe_router(logits, bias, K):
     return idx, wt
 
 
-def moe_ffn_int3(x_out, x_in, idx, wt, w1, w3, w2, n_experts, hidden, inter):
-    """x_out += sum_k wt * W2_e(silu(W1_e x_in) * W3_e x_in); w* = (planes, scales)."""
+def moe_ffn_int3(x_out, x_in, idx, wt, w1, w3, w2, n_experts, hidden, inter, group=32):
+    """x_out += sum_k wt * W2_e(silu(W1_e x_in) * W3_e x_in); w* = (planes, scales);
+    group: weights per f16 scale (32, the reference's layout, or 128)."""
     T, K = idx.shape
     c = _ctx(x_in)
-    c.check(LIB.tb_moe_ffn_int3(c.h, _p(x_out), _p(x_in), _p(idx), _p(wt), _p(w1[0]), _p(w1[1]), _p(w3[0]),
-                                _p(w3[1]), _p(w2[0]), _p(w2[1]), T, K, n_experts, hidden, inter), "moe_ffn_int3")
+    c.check(LIB.tb_moe_ffn_int3_g(c.h, _p(x_out), _p(x_in), _p(idx), _p(wt), _p(w1[0]), _p(w1[1]), _p(w3[0]),
+                                  _p(w3[1]), _p(w2[0]), _p(w2[1]), T, K, n_experts, hidden, inter, int(group)),
+            "moe_ffn_int3")
     return x_out
+
+
+def quant_int3(w, group=128):
+    """bf16 [rows, K] -> int3 planes [rows][K/32][3] + f16 scales [rows][K/group]
+    (scale = f16(max|w|/4), q = clamp(rn(w/scale), -4, 3))."""
+    rows, K = w.shape
+    p3 = torch.empty((rows, K // 32, 3), dtype=torch.int32, device=w.device)
+    s3 = torch.empty((rows, K // group), dtype=torch.int16, device=w.device)
+    c = _ctx(w)
+    c.check(LIB.tb_quant_int3_bf16(c.h, _p(w), _p(p3), _p(s3), rows, K, int(group)), "quant_int3_bf16")
+    return p3, s3
 
 
 def gemv_q_norm(x, norm_w, eps, pack, scales, y=None, acc=False):

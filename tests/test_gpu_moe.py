@@ -105,3 +105,46 @@ def test_moe_many_pairs_one_expert(cuda, experts):
                               _host_planes(w3), _host_planes(w2), H, I)
     err = np.max(np.abs(host(x)[rows] - ref), axis=1) / np.max(np.abs(ref), axis=1)
     assert float(np.max(err)) < 1e-3, err
+
+
+# ---- group-128 int3 (the LFM2.5 benchmark configuration's format) -------------------
+def _bf16_normal(rows, cols, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).to(torch.bfloat16).view(torch.int16)
+
+
+@pytest.mark.parametrize("group", [32, 128])
+def test_quant_int3_bit_exact(cuda, group):
+    w = _bf16_normal(96, 1024, 11 + group)
+    w[0, :group] = 0                             # an all-zero group: scale 0, q = 0
+    wh = host(w).view(np.uint16)
+    p3, s3 = tb.quant_int3(w, group)
+    rp3, rs3 = oracle.quant_int3(wh, group)
+    np.testing.assert_array_equal(host(p3).view(np.uint32), rp3)
+    np.testing.assert_array_equal(host(s3).view(np.uint16), rs3)
+    assert rs3[0, 0] == 0 and rp3[0, 0, 2] == 0xFFFFFFFF and rp3[0, 0, 0] == 0
+
+
+@pytest.fixture(scope="module")
+def experts128():
+    """config 5 experts as the configuration states them: N(0, 0.02) -> int3, group 128."""
+    ws = [tb.quant_int3(_bf16_normal(rows, cols, 200 + j), 128)
+          for j, (rows, cols) in enumerate(((NE * I, H), (NE * I, H), (NE * H, I)))]
+    torch.cuda.synchronize()
+    return ws
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_moe_ffn_group128_matches_oracle(cuda, experts128, T):
+    rng = np.random.default_rng(T + 40)
+    logits = rng.standard_normal((T, NE)).astype(np.float32)
+    a = rng.standard_normal((T, H)).astype(np.float32)
+    idx, wt = tb.moe_router(torch.from_numpy(logits).cuda(), torch.zeros(NE, device="cuda"), K)
+    x = torch.zeros(T, H, device="cuda")
+    w1, w3, w2 = experts128
+    tb.moe_ffn_int3(x, torch.from_numpy(a).cuda(), idx, wt, w1, w3, w2, NE, H, I, group=128)
+    rows = np.arange(T) if T <= 8 else np.sort(rng.choice(T, 6, replace=False))
+    ref = oracle.moe_ffn_int3(a[rows], host(idx).view(np.uint32)[rows], host(wt)[rows], _host_planes(w1),
+                              _host_planes(w3), _host_planes(w2), H, I, group=128)
+    err = np.max(np.abs(host(x)[rows] - ref), axis=1) / np.max(np.abs(ref), axis=1)
+    assert float(np.max(err)) < 1e-3, err

@@ -441,3 +441,25 @@ def test_quantize_wasm_oracle_matches_restatement():
     assert asc[0] == 1.0 and list(act[0][:4]) == [127, 0, 0, 2]    # ties to even, unlike tern.rs
     _, _, asc0 = oracle.quantize_act_wasm(np.zeros(64, np.float32))
     assert asc0[0] == np.float32(1e-9)
+
+
+def test_quant_int3_oracle_matches_restatement():
+    """bf16 -> int3 (group 32 / 128): scale = engine f16(max|w|/4), q = clamp(rn(w/scale), -4, 3)."""
+    rng = np.random.default_rng(8)
+    w = (rng.normal(0, 0.02, (6, 256)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    w[0, :128] = 0
+    for group in (32, 128):
+        p3, s3 = oracle.quant_int3(w, group)
+        wf = (w.astype(np.uint32) << 16).view(np.float32).reshape(6, -1, group)
+        for r in range(6):
+            for gi in range(256 // group):
+                m = np.float32(np.max(np.abs(wf[r, gi])))
+                sh = oracle.engine_f32_to_f16(float(np.float32(m / np.float32(4.0))))
+                assert s3[r, gi] == sh
+                sc = np.float32(oracle.f16_to_f64(int(sh)))
+                q = np.zeros(group, np.int64) if sc == 0 else np.clip(np.rint(wf[r, gi] / sc), -4, 3).astype(np.int64)
+                st = (q + 4).reshape(-1, 32)
+                for j in range(group // 32):
+                    for p in range(3):
+                        want = int(sum(((int(st[j, i]) >> p) & 1) << i for i in range(32)))
+                        assert int(p3[r, gi * (group // 32) + j, p]) == want
