@@ -283,7 +283,7 @@ struct Plan {
 
 int act_bytes_for(int kind, int B, int G)
 {
-    return kind == KIND_F32 ? B * G * 128 : (kind == KIND_F32D ? G * 72 : B * G * 40);
+    return kind == KIND_F32 ? B * G * 128 : (kind == KIND_F32D ? G * F32D_BYTES_PER_GROUP : B * G * 40);
 }
 
 int make_plan(tb_ctx* ctx, int kind, int B, int K, const int64_t* Ns, int count, bool norm, Plan& p)

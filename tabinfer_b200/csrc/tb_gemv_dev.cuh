@@ -303,24 +303,25 @@ __device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbu
     }
 }
 
-// One f32 row (gemvQ, batch 1) as two int8 digit vectors, so the int4 dot runs
-// on dp4a instead of a float conversion per weight.  Per 32-group: sc =
-// max|x|/127, d1 = rn(x/sc), d2 = rn((x - sc*d1) * 128/sc), so
-// x = sc*d1 + (sc/128)*d2 within sc/256 (about 3e-5 of the group's largest
-// magnitude).  Both digit vectors are stored in the permuted Q8 layout of
-// stage_q8; corr = 8*(128*sum d1 + sum d2) removes the nibble bias (the weight
-// is nib - 8); xsf = sc/128.  The row dot is then
-// (s16 * xsf) * (128*dot(nib, d1) + dot(nib, d2) - corr).
-// Layout: x1lo[G] x1hi[G] x2lo[G] x2hi[G] (uint4), corr[G] (int), xsf[G] (float).
+// One f32 row (gemvQ, batch 1) as three int8 digit vectors, so the int4 dot
+// runs on dp4a instead of a float conversion per weight.  Per 32-group: sc =
+// max|x|/127, d1 = rn(x/sc), d2 = rn((x - sc*d1) * 128/sc), d3 = rn((x - sc*d1
+// - sc/128*d2) * 16384/sc), so x = sc*d1 + sc/128*d2 + sc/16384*d3 within
+// sc/32768 (2.4e-7 of the group's largest magnitude, the size of f32 rounding).
+// The digit vectors are stored in the permuted Q8 layout of stage_q8; c1 =
+// 8*sum d1 and c23 = 8*(128*sum d2 + sum d3) remove the nibble bias (the weight
+// is nib - 8); xsf = sc/16384.  The group dot is then, in exact integers,
+// t1 = dot(nib, d1) - c1 and t23 = 128*dot(nib, d2) + dot(nib, d3) - c23, and
+// (s16 * xsf) * (16384*t1 + t23) with one f32 rounding for the bracket.
+// Layout: x1lo x1hi x2lo x2hi x3lo x3hi [G] (uint4), c1 [G], c23 [G] (int), xsf [G].
+constexpr int F32D_BYTES_PER_GROUP = 6 * 16 + 3 * 4;
 __device__ void stage_f32d(const Args& a, unsigned char* act, float* xbuf, float* red, const uint16_t* nws)
 {
     const int G = a.K >> 5, K4 = a.K >> 2;
-    uint4* x1lo = reinterpret_cast<uint4*>(act);
-    uint4* x1hi = x1lo + G;
-    uint4* x2lo = x1hi + G;
-    uint4* x2hi = x2lo + G;
-    int* corr = reinterpret_cast<int*>(x2hi + G);
-    float* xsf = reinterpret_cast<float*>(corr + G);
+    uint4* xd = reinterpret_cast<uint4*>(act);       // [6][G]
+    int* c1 = reinterpret_cast<int*>(xd + 6 * G);
+    int* c23 = c1 + G;
+    float* xsf = reinterpret_cast<float*>(c23 + G);
     const int tid = threadIdx.x, h2 = tid & 1;
     float4* xb4 = reinterpret_cast<float4*>(xbuf);
     float ss[1], inv[1];
@@ -364,78 +365,98 @@ __device__ void stage_f32d(const Args& a, unsigned char* act, float* xbuf, float
 #pragma unroll
         for (int i = 0; i < 16; i++) mx = fmaxf(mx, fabsf(v[i]));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        const float sc = q8_scale(mx), is = q8_inv(sc), is128 = __fmul_rn(is, 128.0f);
-        uint32_t d1w[4], d2w[4];
-        int s1 = 0, s2 = 0;
+        const float sc = q8_scale(mx), is = q8_inv(sc);
+        const float sc2 = __fmul_rn(sc, 0.0078125f), is2 = __fmul_rn(is, 128.0f);       // sc/128, 128/sc
+        const float sc3 = __fmul_rn(sc, 6.103515625e-05f), is3 = __fmul_rn(is, 16384.0f);  // sc/16384, 16384/sc
+        uint32_t dw[3][4];
+        int s1 = 0, s2 = 0, s3 = 0;
 #pragma unroll
         for (int w = 0; w < 2; w++) {
-            uint32_t e1 = 0, o1 = 0, e2 = 0, o2 = 0;
+            uint32_t e[3] = {0, 0, 0}, o[3] = {0, 0, 0};
 #pragma unroll
             for (int h = 0; h < 4; h++) {
 #pragma unroll
                 for (int par = 0; par < 2; par++) {
                     const float x = v[8 * w + 2 * h + par];
                     const int q1 = q8_quant(x, is);
-                    const float r = __fsub_rn(x, __fmul_rn(sc, (float)q1));
-                    const int q2 = max(-127, min(127, __float2int_rn(__fmul_rn(r, is128))));
-                    s1 += q1;
-                    s2 += q2;
-                    const uint32_t b1 = ((uint32_t)q1 & 0xffu) << (8 * h), b2 = ((uint32_t)q2 & 0xffu) << (8 * h);
-                    if (par) { o1 |= b1; o2 |= b2; } else { e1 |= b1; e2 |= b2; }
+                    const float r1 = __fsub_rn(x, __fmul_rn(sc, (float)q1));
+                    const int q2 = max(-127, min(127, __float2int_rn(__fmul_rn(r1, is2))));
+                    const float r2 = __fsub_rn(r1, __fmul_rn(sc2, (float)q2));
+                    const int q3 = max(-127, min(127, __float2int_rn(__fmul_rn(r2, is3))));
+                    s1 += q1; s2 += q2; s3 += q3;
+                    const int qq[3] = {q1, q2, q3};
+#pragma unroll
+                    for (int d = 0; d < 3; d++) {
+                        const uint32_t b = ((uint32_t)qq[d] & 0xffu) << (8 * h);
+                        if (par) o[d] |= b; else e[d] |= b;
+                    }
                 }
             }
-            d1w[2 * w] = e1; d1w[2 * w + 1] = o1;
-            d2w[2 * w] = e2; d2w[2 * w + 1] = o2;
+#pragma unroll
+            for (int d = 0; d < 3; d++) { dw[d][2 * w] = e[d]; dw[d][2 * w + 1] = o[d]; }
         }
+        (void)sc3;
         s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
         s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+        s3 += __shfl_xor_sync(0xffffffffu, s3, 1);
         if (live) {
-            (h2 ? x1hi : x1lo)[g] = make_uint4(d1w[0], d1w[1], d1w[2], d1w[3]);
-            (h2 ? x2hi : x2lo)[g] = make_uint4(d2w[0], d2w[1], d2w[2], d2w[3]);
+#pragma unroll
+            for (int d = 0; d < 3; d++) xd[(2 * d + h2) * G + g] = make_uint4(dw[d][0], dw[d][1], dw[d][2], dw[d][3]);
             if (h2 == 0) {
-                corr[g] = 8 * (128 * s1 + s2);
-                xsf[g] = __fmul_rn(sc, 0.0078125f);   // sc / 128, exact
+                c1[g] = 8 * s1;
+                c23[g] = 8 * (128 * s2 + s3);
+                xsf[g] = sc3;
             }
         }
     }
     __syncthreads();
 }
 
-// The two-digit activation of one 32-group (stage_f32d).
+// The three-digit activation of one 32-group (stage_f32d).
 struct XD {
-    uint4 a1l, a1h, a2l, a2h;
-    int corr;
+    uint4 d[3][2];      // digit vector, lo / hi half of the permuted layout
+    int c1, c23;
     float sf;
 };
 __device__ __forceinline__ void load_xd(XD& x, const unsigned char* act, int G, int g)
 {
-    const uint4* x1lo = reinterpret_cast<const uint4*>(act);
-    x.a1l = x1lo[g];
-    x.a1h = x1lo[G + g];
-    x.a2l = x1lo[2 * G + g];
-    x.a2h = x1lo[3 * G + g];
-    x.corr = reinterpret_cast<const int*>(x1lo + 4 * G)[g];
-    x.sf = reinterpret_cast<const float*>(x1lo + 4 * G)[G + g];
+    const uint4* xd = reinterpret_cast<const uint4*>(act);
+#pragma unroll
+    for (int d = 0; d < 3; d++) {
+        x.d[d][0] = xd[(2 * d) * G + g];
+        x.d[d][1] = xd[(2 * d + 1) * G + g];
+    }
+    const int* c1 = reinterpret_cast<const int*>(xd + 6 * G);
+    x.c1 = c1[g];
+    x.c23 = c1[G + g];
+    x.sf = reinterpret_cast<const float*>(c1 + 2 * G)[g];
 }
-// int4 word quadruple (32 nibbles) against the two digit vectors: exact integer
-// sums, one conversion and one FMA a group
+// int4 word quadruple (32 nibbles) against the three digit vectors: exact
+// integer sums, one f32 rounding, one FMA a group
 __device__ __forceinline__ void item_f32d(const uint4 w, const float s, const XD& x, float* acc)
 {
-    const uint32_t l0 = w.x & 0x0f0f0f0fu, h0 = (w.x >> 4) & 0x0f0f0f0fu;
-    const uint32_t l1 = w.y & 0x0f0f0f0fu, h1 = (w.y >> 4) & 0x0f0f0f0fu;
-    const uint32_t l2 = w.z & 0x0f0f0f0fu, h2 = (w.z >> 4) & 0x0f0f0f0fu;
-    const uint32_t l3 = w.w & 0x0f0f0f0fu, h3 = (w.w >> 4) & 0x0f0f0f0fu;
-    int p0 = 0, p1 = 0, q0 = 0, q1 = 0;
-    p0 = __dp4a((int)l0, (int)x.a1l.x, p0); q0 = __dp4a((int)l0, (int)x.a2l.x, q0);
-    p1 = __dp4a((int)h0, (int)x.a1l.y, p1); q1 = __dp4a((int)h0, (int)x.a2l.y, q1);
-    p0 = __dp4a((int)l1, (int)x.a1l.z, p0); q0 = __dp4a((int)l1, (int)x.a2l.z, q0);
-    p1 = __dp4a((int)h1, (int)x.a1l.w, p1); q1 = __dp4a((int)h1, (int)x.a2l.w, q1);
-    p0 = __dp4a((int)l2, (int)x.a1h.x, p0); q0 = __dp4a((int)l2, (int)x.a2h.x, q0);
-    p1 = __dp4a((int)h2, (int)x.a1h.y, p1); q1 = __dp4a((int)h2, (int)x.a2h.y, q1);
-    p0 = __dp4a((int)l3, (int)x.a1h.z, p0); q0 = __dp4a((int)l3, (int)x.a2h.z, q0);
-    p1 = __dp4a((int)h3, (int)x.a1h.w, p1); q1 = __dp4a((int)h3, (int)x.a2h.w, q1);
-    const int t = 128 * (p0 + p1) + (q0 + q1) - x.corr;     // |t| < 2^24: exact as a float
-    *acc = fmaf(s * x.sf, (float)t, *acc);
+    const uint32_t nl[4] = {w.x & 0x0f0f0f0fu, w.y & 0x0f0f0f0fu, w.z & 0x0f0f0f0fu, w.w & 0x0f0f0f0fu};
+    const uint32_t nh[4] = {(w.x >> 4) & 0x0f0f0f0fu, (w.y >> 4) & 0x0f0f0f0fu, (w.z >> 4) & 0x0f0f0f0fu,
+                            (w.w >> 4) & 0x0f0f0f0fu};
+    int dd[3];
+#pragma unroll
+    for (int d = 0; d < 3; d++) {
+        const uint4 lo = x.d[d][0], hi = x.d[d][1];
+        int p0 = 0, p1 = 0;
+        p0 = __dp4a((int)nl[0], (int)lo.x, p0);
+        p1 = __dp4a((int)nh[0], (int)lo.y, p1);
+        p0 = __dp4a((int)nl[1], (int)lo.z, p0);
+        p1 = __dp4a((int)nh[1], (int)lo.w, p1);
+        p0 = __dp4a((int)nl[2], (int)hi.x, p0);
+        p1 = __dp4a((int)nh[2], (int)hi.y, p1);
+        p0 = __dp4a((int)nl[3], (int)hi.z, p0);
+        p1 = __dp4a((int)nh[3], (int)hi.w, p1);
+        dd[d] = p0 + p1;
+    }
+    const int t1 = dd[0] - x.c1;                           // |t1| < 2^17: 16384 * t1 exact as a float
+    const int t23 = 128 * dd[1] + dd[2] - x.c23;           // |t23| < 2^24: exact as a float
+    const float t = fmaf((float)t1, 16384.0f, (float)t23);
+    *acc = fmaf(s * x.sf, t, *acc);
 }
 
 // F32 layout: per (b, g) 8 float4, float4 index XOR-swizzled by (g & 7).

@@ -252,9 +252,9 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b)
     return d;
 }
 
-// CTAs an SM the streaming form is planned for: four at batch 1 with at most
-// two 64-groups a lane (64 registers), else two
-__host__ __device__ constexpr int t2_ctas(int B, int NBL) { return (B == 1 && NBL <= 2) ? 4 : 2; }
+// CTAs an SM the streaming form is planned for: three at batch 1 with at most
+// two 64-groups a lane (85 registers), else two
+__host__ __device__ constexpr int t2_ctas(int B, int NBL) { return (B == 1 && NBL <= 2) ? 3 : 2; }
 
 template <int B, int NBL>
 __global__ void __launch_bounds__(T2_THREADS, t2_ctas(B, NBL)) k_gemv_tern2(const Tern2Args a)
@@ -391,11 +391,9 @@ bool tern2_plan(int B, int64_t N, int64_t K, int num_sms, T2Plan* p)
     const int NBL = (nb + 31) / 32;
     if (NBL > 4 || B * NBL > 4) return false;              // <= 64 activation registers a lane
     const int rowb = (int)(K / 4) + nb * 4;                // code + scale bytes a row
-    // one chain lane per (activation row, row), at most 16 rows a tile (more
-    // CTAs an SM hide the per-tile barrier better than bigger tiles); enough tiles
-    // to give every SM two CTAs' worth when the matrix allows it; large K keeps
-    // the stages small
-    int TR = B == 1 ? 16 : (32 / B >= 16 ? 16 : 8);
+    // one chain lane per (activation row, row); enough tiles to give every SM two
+    // CTAs' worth when the matrix allows it; large K keeps the stages small
+    int TR = 32 / B >= 32 ? 32 : (32 / B >= 16 ? 16 : 8);
     while (TR > 8 && ((N + TR - 1) / TR < 2LL * num_sms || TR * rowb > 32 * 1024)) TR /= 2;
     p->TR = TR;
     p->NBL = NBL;
