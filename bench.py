@@ -951,14 +951,14 @@ def profile_attn(S):
     print("profile attn done", flush=True)
 
 
-def profile_decode(context):
-    """Three recorded Qwen3-1.7B decode steps (batch 1) at the given context on
-    one GPU, for an ncu launch list of one step (172 kernels)."""
+def profile_decode(context, batch=1):
+    """Three recorded Qwen3-1.7B decode steps (`batch` sequences) at the given
+    context on one GPU, for an ncu launch list of one step."""
     import torch
     import tabinfer_b200 as tb
     dev = torch.device("cuda", 0)
-    m = build_model(Q17, dev, 1, context, 16, 1, 0)
-    m.set_tokens([1000], [context - 1])
+    m = build_model(Q17, dev, batch, context, 16, 1, 0)
+    m.set_tokens([(1000 + 7919 * b) % Q17["vocab"] for b in range(batch)], [context - 1] * batch)
     for _ in range(3):
         m.step()
     torch.cuda.synchronize()
@@ -1400,7 +1400,7 @@ def main():
         profile_q2g64()
         return
     if args.profile_decode:
-        profile_decode(args.profile_decode)
+        profile_decode(args.profile_decode, args.batch)
         return
     if args.profile_moe:
         profile_moe(args.profile_moe)

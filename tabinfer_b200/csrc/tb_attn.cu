@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) k_kv_quant_write(const float* __restrict_
 
 // hd fixed at compile time (64 or 128); GRP = q heads per kv head.  One CTA
 // (W warps) per (kv head, split); the split's work is DecUnit (tb_attn_dev.cuh).
-template <int HD, int GRP, bool EARLY, int W>
+template <int HD, int GRP, bool EARLY, int W, int NST>
 __global__ void __launch_bounds__(32 * W) k_attn_decode(const AttnArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(32 * W) k_attn_decode(const AttnArgs a)
         // the position and every cache row below S-1 come from earlier steps: a
         // warp's first tile is fetched before griddepcontrol.wait unless it holds
         // row S-1, which the preceding prep kernel writes
-        DecUnit<HD, GRP, 2, W> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
+        DecUnit<HD, GRP, NST, W> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
         u.prefetch(true);
         tb_pdl_wait();
         tb_pdl_trigger();
@@ -104,17 +104,17 @@ __global__ void __launch_bounds__(32 * W) k_attn_decode(const AttnArgs a)
     } else {
         tb_pdl_wait();
         tb_pdl_trigger();
-        DecUnit<HD, GRP, 2, W> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
+        DecUnit<HD, GRP, NST, W> u(a, smem, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, 0);
         u.prefetch(false);
         u.run(false);
     }
 }
 
-template <int HD, int GRP, bool EARLY, int W>
+template <int HD, int GRP, bool EARLY, int W, int NST>
 int launch_decode_w(tb_ctx* ctx, const AttnArgs& a)
 {
-    constexpr int bytes = DecLayout<HD, GRP, 2, W>::BYTES;
-    auto kern = k_attn_decode<HD, GRP, EARLY, W>;
+    constexpr int bytes = DecLayout<HD, GRP, NST, W>::BYTES;
+    auto kern = k_attn_decode<HD, GRP, EARLY, W, NST>;
     static bool attr_set[64] = {};   // per device and instantiation; setting it twice is harmless
     if (ctx->device >= 64 || !attr_set[ctx->device]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -127,11 +127,19 @@ int launch_decode_w(tb_ctx* ctx, const AttnArgs& a)
 }
 
 // one sequence (the decode step at batch 1, ~one split per SM): 8-warp splits,
-// as the persistent decode step runs them; several sequences: 4-warp splits
+// as the persistent decode step runs them; several sequences: 4-warp splits.
+// A grid of at most one CTA an SM keeps two tile stages a warp (a tile in
+// flight while one is scored); a larger grid takes one stage, which halves the
+// shared memory so several CTAs share an SM (4-warp units: 41 KB, five an SM)
+// and their warps hide each other's copies.
 template <int HD, int GRP, bool EARLY>
 int launch_decode(tb_ctx* ctx, const AttnArgs& a)
 {
-    return a.grid_z == 1 ? launch_decode_w<HD, GRP, EARLY, 8>(ctx, a) : launch_decode_w<HD, GRP, EARLY, 4>(ctx, a);
+    const long long ctas = (long long)a.nKv * a.nsplit * a.grid_z;
+    const bool one_stage = ctas > ctx->num_sms;
+    if (a.grid_z == 1)
+        return one_stage ? launch_decode_w<HD, GRP, EARLY, 8, 1>(ctx, a) : launch_decode_w<HD, GRP, EARLY, 8, 2>(ctx, a);
+    return one_stage ? launch_decode_w<HD, GRP, EARLY, 4, 1>(ctx, a) : launch_decode_w<HD, GRP, EARLY, 4, 2>(ctx, a);
 }
 
 template <bool EARLY>
@@ -160,14 +168,15 @@ int decode_dispatch(tb_ctx* ctx, const AttnArgs& a, int64_t hd, int grp)
 }  // namespace
 
 // Split count used when the caller passes nsplit = 0: at least 128 keys per
-// CTA, and enough CTAs (nKv * nsplit) for ~2 per SM (the decode kernel's
-// shared-memory occupancy) at long context.
+// CTA, and at long context as many (kv head, split) CTAs as fit in one wave of
+// single-stage 4-warp units (five an SM), rounded down so no second, partial
+// wave follows; a unit's combine weighs at most 256 splits.
 int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv)
 {
     long long by_keys = (S + 127) / 128;
-    long long by_fill = (2LL * ctx->num_sms + nKv - 1) / nKv;
+    long long by_fill = std::max(1LL, 5LL * ctx->num_sms / nKv);
     long long n = std::min(by_keys, by_fill);
-    return (int)std::max(1LL, std::min(n, 1024LL));
+    return (int)std::max(1LL, std::min(n, 256LL));
 }
 
 // batch sequences (grid.z); sequence b's cache starts cache_rows rows after

@@ -83,14 +83,7 @@ __global__ void __launch_bounds__(THREADS, 2) k_gemv(const Args a)
     else stage_q8<B, TERN>(a, act, xbuf, a.xbuf_bytes >> 2, red, nws);
     __syncthreads();
 
-    // the two-digit activation of this lane's groups (lane, lane + 32) in registers
-    constexpr bool DREG = KIND == KIND_F32D;
-    const bool dreg = DREG && G <= 64;
-    XD xd0{}, xd1{};
-    if (DREG && dreg) {
-        if (lane < G) load_xd(xd0, act, G, lane);
-        if (lane + 32 < G) load_xd(xd1, act, G, lane + 32);
-    }
+    constexpr bool DREG = KIND == KIND_F32D;   // the digit form of one f32 row
 
     // f32 activation of a single row kept in registers (groups lane, lane+32),
     // un-swizzled on the way in so every register index is static
@@ -168,14 +161,15 @@ __global__ void __launch_bounds__(THREADS, 2) k_gemv(const Args a)
                         }
                     } else if (DREG) {
                         const uint4* wq = reinterpret_cast<const uint4*>(slot);
+                        // a group's digits are read once for the warp's RPW rows
                         for (int g = lane; g < G; g += 32) {
                             XD xg;
-                            if (dreg) xg = g == lane ? xd0 : xd1;
-                            else load_xd(xg, act, G, g);
+                            load_xd(xg, act, G, g);
 #pragma unroll
                             for (int q = 0; q < RPW; q++) {
                                 const int r = r0 + q * NW;
-                                if (r < bl.nrows) item_f32d(wq[r * G + g], tb_h2f(sbase[r * G + g]), xg, &acc[q][s][0]);
+                                if (r < bl.nrows)
+                                    item_f32d(wq[r * G + g], tb_h2f(sbase[r * G + g]), xg, &acc[q][s][0]);
                             }
                         }
                     } else if (XREG && xreg) {

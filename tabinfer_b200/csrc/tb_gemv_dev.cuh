@@ -303,25 +303,26 @@ __device__ void stage_q8(const Args& a, unsigned char* act, float* xbuf, int xbu
     }
 }
 
-// One f32 row (gemvQ, batch 1) as three int8 digit vectors, so the int4 dot
+// One f32 row (gemvQ, batch 1) as four int8 digit vectors, so the int4 dot
 // runs on dp4a instead of a float conversion per weight.  Per 32-group: sc =
-// max|x|/127, d1 = rn(x/sc), d2 = rn((x - sc*d1) * 128/sc), d3 = rn((x - sc*d1
-// - sc/128*d2) * 16384/sc), so x = sc*d1 + sc/128*d2 + sc/16384*d3 within
-// sc/32768 (2.4e-7 of the group's largest magnitude, the size of f32 rounding).
-// The digit vectors are stored in the permuted Q8 layout of stage_q8; c1 =
-// 8*sum d1 and c23 = 8*(128*sum d2 + sum d3) remove the nibble bias (the weight
-// is nib - 8); xsf = sc/16384.  The group dot is then, in exact integers,
-// t1 = dot(nib, d1) - c1 and t23 = 128*dot(nib, d2) + dot(nib, d3) - c23, and
-// (s16 * xsf) * (16384*t1 + t23) with one f32 rounding for the bracket.
-// Layout: x1lo x1hi x2lo x2hi x3lo x3hi [G] (uint4), c1 [G], c23 [G] (int), xsf [G].
-constexpr int F32D_BYTES_PER_GROUP = 6 * 16 + 3 * 4;
+// max|x|/127, d1 = rn(x/sc), then each next digit rounds the remaining residual
+// at 128 times finer steps: x = sc*(d1 + d2/128 + d3/128^2 + d4/128^3) within
+// sc/2^22 (1.9e-9 of the group's largest magnitude, below f32 rounding).  The
+// digit vectors are stored in the permuted Q8 layout of stage_q8; c1 = 8*sum d1
+// and c234 = 8*(16384*sum d2 + 128*sum d3 + sum d4) remove the nibble bias (the
+// weight is nib - 8); xsf = sc/2^21.  The group dot is then, in exact integers,
+// t1 = dot(nib, d1) - c1 and t234 = 16384*dot(nib, d2) + 128*dot(nib, d3) +
+// dot(nib, d4) - c234, and (s16 * xsf) * (2^21*t1 + t234) with two f32 roundings.
+// Layout: per digit d a lo and a hi uint4 plane [8][G], c1 [G], c234 [G] (int), xsf [G].
+constexpr int F32D_ND = 4;
+constexpr int F32D_BYTES_PER_GROUP = 2 * F32D_ND * 16 + 3 * 4;
 __device__ void stage_f32d(const Args& a, unsigned char* act, float* xbuf, float* red, const uint16_t* nws)
 {
     const int G = a.K >> 5, K4 = a.K >> 2;
-    uint4* xd = reinterpret_cast<uint4*>(act);       // [6][G]
-    int* c1 = reinterpret_cast<int*>(xd + 6 * G);
-    int* c23 = c1 + G;
-    float* xsf = reinterpret_cast<float*>(c23 + G);
+    uint4* xd = reinterpret_cast<uint4*>(act);       // [2*ND][G]
+    int* c1 = reinterpret_cast<int*>(xd + 2 * F32D_ND * G);
+    int* c234 = c1 + G;
+    float* xsf = reinterpret_cast<float*>(c234 + G);
     const int tid = threadIdx.x, h2 = tid & 1;
     float4* xb4 = reinterpret_cast<float4*>(xbuf);
     float ss[1], inv[1];
@@ -365,82 +366,83 @@ __device__ void stage_f32d(const Args& a, unsigned char* act, float* xbuf, float
 #pragma unroll
         for (int i = 0; i < 16; i++) mx = fmaxf(mx, fabsf(v[i]));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        const float sc = q8_scale(mx), is = q8_inv(sc);
-        const float sc2 = __fmul_rn(sc, 0.0078125f), is2 = __fmul_rn(is, 128.0f);       // sc/128, 128/sc
-        const float sc3 = __fmul_rn(sc, 6.103515625e-05f), is3 = __fmul_rn(is, 16384.0f);  // sc/16384, 16384/sc
-        uint32_t dw[3][4];
-        int s1 = 0, s2 = 0, s3 = 0;
+        // digit d: step sc / 128^d and its inverse (exact power-of-two scalings)
+        float stp[F32D_ND], istp[F32D_ND];
+        stp[0] = q8_scale(mx);
+        istp[0] = q8_inv(stp[0]);
+#pragma unroll
+        for (int d = 1; d < F32D_ND; d++) {
+            stp[d] = __fmul_rn(stp[d - 1], 0.0078125f);
+            istp[d] = __fmul_rn(istp[d - 1], 128.0f);
+        }
+        uint32_t dw[F32D_ND][4];
+        int sums[F32D_ND] = {};
 #pragma unroll
         for (int w = 0; w < 2; w++) {
-            uint32_t e[3] = {0, 0, 0}, o[3] = {0, 0, 0};
+            uint32_t e[F32D_ND] = {}, o[F32D_ND] = {};
 #pragma unroll
             for (int h = 0; h < 4; h++) {
 #pragma unroll
                 for (int par = 0; par < 2; par++) {
-                    const float x = v[8 * w + 2 * h + par];
-                    const int q1 = q8_quant(x, is);
-                    const float r1 = __fsub_rn(x, __fmul_rn(sc, (float)q1));
-                    const int q2 = max(-127, min(127, __float2int_rn(__fmul_rn(r1, is2))));
-                    const float r2 = __fsub_rn(r1, __fmul_rn(sc2, (float)q2));
-                    const int q3 = max(-127, min(127, __float2int_rn(__fmul_rn(r2, is3))));
-                    s1 += q1; s2 += q2; s3 += q3;
-                    const int qq[3] = {q1, q2, q3};
+                    float r = v[8 * w + 2 * h + par];
 #pragma unroll
-                    for (int d = 0; d < 3; d++) {
-                        const uint32_t b = ((uint32_t)qq[d] & 0xffu) << (8 * h);
+                    for (int d = 0; d < F32D_ND; d++) {
+                        const int q = max(-127, min(127, __float2int_rn(__fmul_rn(r, istp[d]))));
+                        r = __fsub_rn(r, __fmul_rn(stp[d], (float)q));
+                        sums[d] += q;
+                        const uint32_t b = ((uint32_t)q & 0xffu) << (8 * h);
                         if (par) o[d] |= b; else e[d] |= b;
                     }
                 }
             }
 #pragma unroll
-            for (int d = 0; d < 3; d++) { dw[d][2 * w] = e[d]; dw[d][2 * w + 1] = o[d]; }
+            for (int d = 0; d < F32D_ND; d++) { dw[d][2 * w] = e[d]; dw[d][2 * w + 1] = o[d]; }
         }
-        (void)sc3;
-        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
-        s3 += __shfl_xor_sync(0xffffffffu, s3, 1);
+#pragma unroll
+        for (int d = 0; d < F32D_ND; d++) sums[d] += __shfl_xor_sync(0xffffffffu, sums[d], 1);
         if (live) {
 #pragma unroll
-            for (int d = 0; d < 3; d++) xd[(2 * d + h2) * G + g] = make_uint4(dw[d][0], dw[d][1], dw[d][2], dw[d][3]);
+            for (int d = 0; d < F32D_ND; d++)
+                xd[(2 * d + h2) * G + g] = make_uint4(dw[d][0], dw[d][1], dw[d][2], dw[d][3]);
             if (h2 == 0) {
-                c1[g] = 8 * s1;
-                c23[g] = 8 * (128 * s2 + s3);
-                xsf[g] = sc3;
+                c1[g] = 8 * sums[0];
+                c234[g] = 8 * (16384 * sums[1] + 128 * sums[2] + sums[3]);
+                xsf[g] = stp[F32D_ND - 1];   // sc / 128^3 = sc / 2^21
             }
         }
     }
     __syncthreads();
 }
 
-// The three-digit activation of one 32-group (stage_f32d).
+// The four-digit activation of one 32-group (stage_f32d).
 struct XD {
-    uint4 d[3][2];      // digit vector, lo / hi half of the permuted layout
-    int c1, c23;
+    uint4 d[F32D_ND][2];     // digit vector, lo / hi half of the permuted layout
+    int c1, c234;
     float sf;
 };
 __device__ __forceinline__ void load_xd(XD& x, const unsigned char* act, int G, int g)
 {
     const uint4* xd = reinterpret_cast<const uint4*>(act);
 #pragma unroll
-    for (int d = 0; d < 3; d++) {
+    for (int d = 0; d < F32D_ND; d++) {
         x.d[d][0] = xd[(2 * d) * G + g];
         x.d[d][1] = xd[(2 * d + 1) * G + g];
     }
-    const int* c1 = reinterpret_cast<const int*>(xd + 6 * G);
+    const int* c1 = reinterpret_cast<const int*>(xd + 2 * F32D_ND * G);
     x.c1 = c1[g];
-    x.c23 = c1[G + g];
+    x.c234 = c1[G + g];
     x.sf = reinterpret_cast<const float*>(c1 + 2 * G)[g];
 }
-// int4 word quadruple (32 nibbles) against the three digit vectors: exact
-// integer sums, one f32 rounding, one FMA a group
+// int4 word quadruple (32 nibbles) against the four digit vectors: exact
+// integer sums, two f32 roundings, one FMA a group
 __device__ __forceinline__ void item_f32d(const uint4 w, const float s, const XD& x, float* acc)
 {
     const uint32_t nl[4] = {w.x & 0x0f0f0f0fu, w.y & 0x0f0f0f0fu, w.z & 0x0f0f0f0fu, w.w & 0x0f0f0f0fu};
     const uint32_t nh[4] = {(w.x >> 4) & 0x0f0f0f0fu, (w.y >> 4) & 0x0f0f0f0fu, (w.z >> 4) & 0x0f0f0f0fu,
                             (w.w >> 4) & 0x0f0f0f0fu};
-    int dd[3];
+    int dd[F32D_ND];
 #pragma unroll
-    for (int d = 0; d < 3; d++) {
+    for (int d = 0; d < F32D_ND; d++) {
         const uint4 lo = x.d[d][0], hi = x.d[d][1];
         int p0 = 0, p1 = 0;
         p0 = __dp4a((int)nl[0], (int)lo.x, p0);
@@ -453,9 +455,10 @@ __device__ __forceinline__ void item_f32d(const uint4 w, const float s, const XD
         p1 = __dp4a((int)nh[3], (int)hi.w, p1);
         dd[d] = p0 + p1;
     }
-    const int t1 = dd[0] - x.c1;                           // |t1| < 2^17: 16384 * t1 exact as a float
-    const int t23 = 128 * dd[1] + dd[2] - x.c23;           // |t23| < 2^24: exact as a float
-    const float t = fmaf((float)t1, 16384.0f, (float)t23);
+    // |dd| <= 32*15*127 = 60960: t234 < 2^31, 2^21 * t1 exact as a float
+    const int t1 = dd[0] - x.c1;
+    const int t234 = 16384 * dd[1] + 128 * dd[2] + dd[3] - x.c234;
+    const float t = fmaf((float)t1, 2097152.0f, (float)t234);
     *acc = fmaf(s * x.sf, t, *acc);
 }
 

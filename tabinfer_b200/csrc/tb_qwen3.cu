@@ -649,7 +649,12 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
         // they compute the same bits); under TP both kinds keep the rule above,
         // and the persistent step applies where it gives one 32-key tile per warp
         const long long by_keys = (c.max_seq + 127) / 128;
-        m->nsplit = (int)std::max(1LL, std::min(by_keys, (long long)(ctx->num_sms / m->nKv)));
+        const long long per_sm = ctx->num_sms / m->nKv;
+        m->nsplit = (int)std::max(1LL, std::min(by_keys, per_sm));
+        // a context too long for the persistent step's one 32-key tile a warp
+        // (256 keys a split) runs the multi-kernel step only: three single-stage
+        // 8-warp units an SM
+        if ((c.max_seq + m->nsplit - 1) / m->nsplit > 256) m->nsplit = (int)std::max(1LL, std::min(by_keys, 3 * per_sm));
     }
     if (!rc) rc = alloc(m, &m->qr, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->PO, (size_t)B * m->nHq * m->nsplit * hd);
