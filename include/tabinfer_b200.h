@@ -567,9 +567,9 @@ enum {
  * or all ternary, one GPU or tensor parallel over peer memory (tp_connect: the
  * o / down rows are exchanged inside the kernel, CTA by CTA, over NVLink).
  * TB_QW_STEP_KERNELS: one kernel per operation (6 per layer + 4).
- * TB_QW_STEP_AUTO (default): persistent where it applies on one GPU; the
- * multi-kernel step under tensor parallelism, where it is the faster of the
- * two.  Both compute the same bits.  No reference counterpart (the reference dispatches WebGPU passes). */
+ * TB_QW_STEP_AUTO (default): persistent wherever it applies (one GPU, or
+ * tensor parallel over the peer-memory exchange of tb_qwen3_tp_connect), else
+ * the multi-kernel step.  Both compute the same bits.  No reference counterpart (the reference dispatches WebGPU passes). */
 #define TB_QW_STEP_AUTO 0
 #define TB_QW_STEP_KERNELS 1
 #define TB_QW_STEP_PERSISTENT 2

@@ -133,6 +133,7 @@ struct tb_qwen3 {
     int step_tern = -1;                          // weight format the plan was made for (1 ternary)
     unsigned* step_ctrl = nullptr;               // [256] block arrivals, grid barrier, abort word
     unsigned* step_heads = nullptr;              // [layers][kv heads] phase-A arrivals of the persistent step
+    unsigned long long* step_pk = nullptr;       // [hidden + intermediate] phase-boundary packets
     unsigned char* step_attnq = nullptr;         // quantized attention output of the persistent step
     bool step_direct = false;                    // persistent step launched per call (not capturable)
     void* step_trace = nullptr;                  // optional phase trace of the persistent kernel
@@ -304,10 +305,12 @@ bool persistent_ok(tb_qwen3* m)
         }
         if (alloc(m, &m->step_layers, host.size()) || alloc(m, &m->step_ctrl, 256) ||
             alloc(m, &m->step_heads, (size_t)m->c.layers * m->nKv) ||
+            alloc(m, &m->step_pk, (size_t)m->c.hidden + (size_t)m->I) ||
             alloc(m, &m->step_attnq, (size_t)m->nHq * m->c.head_dim / 32 * 40))
             return false;
         if (cudaMemcpy(m->step_layers, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
-            cudaMemset(m->step_ctrl, 0, 256 * 4) != cudaSuccess) {
+            cudaMemset(m->step_ctrl, 0, 256 * 4) != cudaSuccess ||
+            cudaMemset(m->step_pk, 0, ((size_t)m->c.hidden + (size_t)m->I) * 8) != cudaSuccess) {
             cudaGetLastError();
             m->step_layers = nullptr;
             return false;
@@ -328,6 +331,7 @@ tb_step_io step_io(tb_qwen3* m)
     io.embed = m->embed;
     io.x = m->x[0]; io.q = m->q; io.k = m->k; io.v = m->v; io.qr = m->qr; io.attn = m->attn; io.swi = m->swi;
     io.PO = m->PO; io.PML = m->PML; io.counters = m->counters; io.ctrl = m->step_ctrl; io.head_cnt = m->step_heads;
+    io.pk = m->step_pk;
     io.trace = m->step_trace;
     io.attnq = m->step_attnq;
     io.P = m->P;
@@ -992,10 +996,10 @@ TB_API int tb_qwen3_decode_step(tb_qwen3* m)
                    "a projection weight was never set");
     TB_REQUIRE(ctx, m->lm.set, "lm_head weight was never set");
     if (!m->exec && !m->step_direct) {
-        // AUTO takes the persistent kernel on one GPU only: under TP its in-kernel
-        // exchanges measured slower than the multi-kernel step (588 vs 806 tok/s at
-        // TP = 2), so there it runs when asked for (TB_QW_STEP_PERSISTENT)
-        const bool want = m->step_mode == TB_QW_STEP_PERSISTENT || (m->step_mode == TB_QW_STEP_AUTO && m->P == 1);
+        // AUTO takes the persistent kernel wherever it applies: on one GPU, and under
+        // TP over peer memory, where its in-kernel packet exchange measured faster
+        // than the multi-kernel step (1016 vs 841 tok/s at TP = 2)
+        const bool want = m->step_mode == TB_QW_STEP_PERSISTENT || m->step_mode == TB_QW_STEP_AUTO;
         const bool pers = want && persistent_ok(m);
         if (m->step_mode == TB_QW_STEP_PERSISTENT && !pers)
             return tb_fail(ctx, TB_ERR_UNSUPPORTED,

@@ -50,6 +50,7 @@ constexpr int ERR_STEP_BARRIER = 0x5101;
 constexpr int ERR_STEP_COPY = 0x5102;
 constexpr int ERR_STEP_TP = 0x5103;
 constexpr int ERR_STEP_TP_POISONED = 0x5104;   // refused: an earlier exchange wait of this rank gave up
+constexpr int ERR_STEP_PACKET = 0x5105;        // a phase-boundary packet wait gave up
 constexpr long long STEP_WAIT_LIMIT = 1LL << 21;   // barrier polls of ~0.5 us: ~1 s
 constexpr int RBA = 32;                              // rows of a phase-A block (a head has hd/32 blocks)
 constexpr int STEP_HD = 128;
@@ -76,6 +77,10 @@ struct StepArgs {
     unsigned long long* bar_count;   // grid barrier: arrivals since the model was made (monotonic)
     unsigned* abort_word;    // == this launch's tag: a CTA gave up in this launch
     unsigned* head_cnt;      // [L][nKv] phase-A blocks of each kv head written (zeroed by every launch)
+    // phase-boundary packets (epoch << 32 | f32 bits): x rows after o and after
+    // down (one GPU), swi rows after gate/up (every rank)
+    unsigned long long* xpk; // [H]
+    unsigned long long* spk; // [I]
     int* err;
     // optional phase trace: per CTA 1 + 38 * L %globaltimer stamps (kernel start;
     // per layer and phase: weights ready, activation row loaded, activation
@@ -130,6 +135,19 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+// Phase-boundary packets: (epoch << 32) | f32 bits, one 8-byte store a value.  A
+// reader polls until the epoch is the one it expects, so a value and the news
+// that it is ready arrive in the same load (no barrier, no second round trip).
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v)
+{
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ld_relaxed_gpu_v2u64(const unsigned long long* p, unsigned long long& a,
+                                                     unsigned long long& b)
+{
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 struct Ctl {
@@ -277,7 +295,7 @@ __device__ bool await_buf(const StepArgs& a, Ctl* ctl, int buf, uint64_t* bars)
 // writer is this CTA), so y = own + W.a needs no read of y from memory
 template <int NM, int RPW, bool TERN>
 __device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
-                            float* y, int row0, float* own)
+                            float* y, int row0, float* own, unsigned long long* pk, unsigned pe)
 {
     constexpr int NW = THREADS / 32;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -317,16 +335,19 @@ __device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, c
                 const int r = r0 + q * NW;
                 if (r >= n) continue;
                 float* yp = y + row0 + r;
+                float v;
                 if (NM == 2) {
                     const float g = acc[q][0], u = acc[q][NM - 1];
-                    *yp = __fdiv_rn(g, 1.0f + expf(-g)) * u;
+                    v = __fdiv_rn(g, 1.0f + expf(-g)) * u;
                 } else if (own) {
-                    const float v = own[r] + acc[q][0];
+                    v = own[r] + acc[q][0];
                     own[r] = v;
-                    *yp = v;
                 } else {
-                    *yp = 0.0f + acc[q][0];
+                    v = 0.0f + acc[q][0];
                 }
+                *yp = v;
+                // the same value as an epoch-tagged packet for the next phase's readers
+                if (pk) st_relaxed_gpu_u64(pk + row0 + r, ((unsigned long long)pe << 32) | __float_as_uint(v));
             }
         }
     }
@@ -336,13 +357,13 @@ __device__ void gemv_rows_r(const unsigned char* act, const unsigned char* w0, c
 // depend on which warp computes it)
 template <int NM, bool TERN>
 __device__ void gemv_rows(const unsigned char* act, const unsigned char* w0, const unsigned char* w1, int n, int G,
-                          float* y, int row0, float* own)
+                          float* y, int row0, float* own, unsigned long long* pk = nullptr, unsigned pe = 0)
 {
     const int rpw = (n + THREADS / 32 - 1) / (THREADS / 32);
-    if (rpw <= 2) gemv_rows_r<NM, 2, TERN>(act, w0, w1, n, G, y, row0, own);
-    else if (rpw <= 4) gemv_rows_r<NM, 4, TERN>(act, w0, w1, n, G, y, row0, own);
-    else if (rpw <= 6) gemv_rows_r<NM, 6, TERN>(act, w0, w1, n, G, y, row0, own);
-    else gemv_rows_r<NM, 8, TERN>(act, w0, w1, n, G, y, row0, own);
+    if (rpw <= 2) gemv_rows_r<NM, 2, TERN>(act, w0, w1, n, G, y, row0, own, pk, pe);
+    else if (rpw <= 4) gemv_rows_r<NM, 4, TERN>(act, w0, w1, n, G, y, row0, own, pk, pe);
+    else if (rpw <= 6) gemv_rows_r<NM, 6, TERN>(act, w0, w1, n, G, y, row0, own, pk, pe);
+    else gemv_rows_r<NM, 8, TERN>(act, w0, w1, n, G, y, row0, own, pk, pe);
 }
 
 // QUANTQ8 (optionally RMSNorm first) of a whole f32 row written by other CTAs,
@@ -397,6 +418,87 @@ __device__ void stage(const StepArgs& sa, unsigned char* smem, const float* x, i
     stamp(sa, slot + 1);
 }
 
+// stage() for a row that arrives as packets (pk[k] = (e << 32) | bits of x[k],
+// written by other CTAs in the previous phase with no barrier in between): each
+// thread polls its own float4s' packets (relaxed loads at gpu scope, two packets
+// a 16-byte load) until all carry epoch e, bounded, then stages exactly as
+// stage() does.  false: this CTA gave up (or saw another CTA give up); the
+// launch is abandoned.
+template <bool NAT>
+__device__ bool stage_pk(const StepArgs& sa, Ctl* ctl, unsigned char* smem, const unsigned long long* pk, unsigned e,
+                         int K, bool norm, const uint16_t* nws, float* red, int slot)
+{
+    constexpr int MAXF = 8;
+    const int tid = threadIdx.x, G = K >> 5, K4 = K >> 2;
+    const int nf = (K4 + THREADS - 1) / THREADS;
+    float4 v[MAXF];
+    unsigned pending = 0;
+#pragma unroll
+    for (int i = 0; i < MAXF; i++) {
+        v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < nf && i * THREADS + tid < K4) pending |= 1u << i;
+    }
+    long long it = 0;
+    while (pending && !*reinterpret_cast<volatile int*>(&ctl->abort)) {
+#pragma unroll
+        for (int i = 0; i < MAXF; i++) {
+            if (!((pending >> i) & 1u)) continue;
+            const unsigned long long* q = pk + 4 * (i * THREADS + tid);
+            unsigned long long p0, p1, p2, p3;
+            ld_relaxed_gpu_v2u64(q, p0, p1);
+            ld_relaxed_gpu_v2u64(q + 2, p2, p3);
+            if ((unsigned)(p0 >> 32) == e && (unsigned)(p1 >> 32) == e && (unsigned)(p2 >> 32) == e &&
+                (unsigned)(p3 >> 32) == e) {
+                v[i] = make_float4(__uint_as_float((unsigned)p0), __uint_as_float((unsigned)p1),
+                                   __uint_as_float((unsigned)p2), __uint_as_float((unsigned)p3));
+                pending &= ~(1u << i);
+            }
+        }
+        if (!pending) break;
+        ++it;
+        if ((it & 255) == 0 && *reinterpret_cast<volatile unsigned*>(sa.abort_word) == ctl->tag) {
+            ctl->abort = 1;
+            break;
+        }
+        if (it > STEP_WAIT_LIMIT) {
+            atomicExch(sa.err, ERR_STEP_PACKET);
+            atomicExch(sa.abort_word, ctl->tag);
+            ctl->abort = 1;
+            break;
+        }
+        if (it > 64) __nanosleep(32);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXF; i++)
+        if (i < nf && i * THREADS + tid < K4) ss = sumsq_f4(v[i], ss);
+    if (sa.trace && tid == 0) {   // the row has arrived in thread 0's registers
+        asm volatile("" ::"f"(ss));
+        stamp(sa, slot);
+    }
+    float inv = 1.0f;
+    if (norm) {
+        float tot;
+        block256_reduce_rows<1>(&ss, red, &tot);
+        inv = rms_inv(tot, K, sa.eps);
+    }
+#pragma unroll
+    for (int i = 0; i < MAXF; i++) {
+        if (i >= nf) break;
+        const int f = i * THREADS + tid;
+        const bool live = f < K4;              // whole 32-groups (8 consecutive f) are live or not
+        float e4[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        if (norm && live) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) e4[j] = __fmul_rn(__fmul_rn(e4[j], inv), tb_h2f(nws[4 * f + j]));
+        }
+        q8_store_group4(e4, f >> 3, live, smem + sa.off_act, G, NAT);      // f & 7 == lane & 7
+    }
+    __syncthreads();
+    stamp(sa, slot + 1);
+    return !ctl->abort;
+}
+
 // ---- tensor-parallel exchange of the o / down rows ----------------------------------
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v)
 {
@@ -418,7 +520,7 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
 // other rank's rows of this CTA -- local loads only -- and form
 // x + part_0 + ... + part_{P-1} in rank order, the sum k_tp_allreduce forms,
 // into the CTA's residual rows and x.
-// e = (barriers before this launch) + xi + 1: a launch passes 4L >= 2L + 1
+// e = (barriers before this launch) + xi + 1: a launch passes 3L >= 2L + 1
 // barriers and has 2L exchanges, so epochs grow across launches; a slot holds
 // epoch e - 2 or e, never more (a rank sends exchange xi + 2 only after it
 // received every rank's xi + 1, sent after that rank consumed xi), so the wait
@@ -642,6 +744,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
     }
     if (!grid_sync(a, ctl)) goto drain;
 
+    // epochs of this launch's phase-boundary packets: ebase + 3l + {1 (x after o),
+    // 2 (swi), 3 (x after down)}.  Every launch that writes packets has passed the
+    // embed barrier, so its base (grid barriers before it) exceeds an earlier
+    // one's and the epoch ranges of two launches never meet; a reader waits for
+    // equality, and the earlier writers of a slot (the phase before, the launch
+    // before) carry other epochs.
+    {
+    const unsigned ebase = (unsigned)(ctl->base / gridDim.x) * (unsigned)(3 * a.L);
     for (int l = 0; l < a.L; l++) {
         const StepLayer& Ly = sl[l];
         const bool more = l + 1 < a.L;
@@ -652,7 +762,15 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const BlockA b = block_a(a);
             const unsigned char* wR = smem + a.off_R;
             const uint16_t* nws = reinterpret_cast<const uint16_t*>(wR + (b.live ? mat_bytes(a, RBA, a.H) : 0));
-            if (b.live) stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
+            if (b.live) {
+                if (l > 0 && a.P == 1) {
+                    if (!stage_pk<TERN>(a, ctl, smem, a.xpk, ebase + 3 * (l - 1) + 3, a.H, true, nws, red,
+                                        1 + 25 * l + 5 * 0 + 1))
+                        goto drain;
+                } else {
+                    stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
+                }
+            }
             if (tid == 0 && l > 0) request(a, ctl, BUF_Q, 4, l, smem, bars);   // Q held E(l-1)
             STAMP_REQ(0);
             if (b.live) {
@@ -700,12 +818,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                                        rowsC0(a), nullptr);
                 else
                     gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_R, nullptr, n, a.nHq * STEP_HD / 32, a.x,
-                                       rowsC0(a), xo);
+                                       rowsC0(a), xo, a.xpk, ebase + 3 * l + 1);
             }
             __syncthreads();
             if (a.P > 1 && !tp_exchange(a, ctl, 2 * l, xo, tpv)) goto drain;
             STAMP(2, 3);
-            if (!grid_sync(a, ctl)) goto drain;
+            // one GPU: phase D reads x as packets, no barrier; under TP, after the exchange
+            if (a.P > 1 && !grid_sync(a, ctl)) goto drain;
             STAMP(2, 4);
         }
         // ---- D: rmsnorm + quant of x, gate/up rows, swiglu
@@ -716,24 +835,32 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const unsigned char* wP = smem + a.off_P;
             if (n > 0) {
                 const uint16_t* nws = reinterpret_cast<const uint16_t*>(wP + 2 * mat_bytes(a, n, a.H));
-                stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 3 + 1);
+                if (a.P == 1) {
+                    if (!stage_pk<TERN>(a, ctl, smem, a.xpk, ebase + 3 * l + 1, a.H, true, nws, red,
+                                        1 + 25 * l + 5 * 3 + 1))
+                        goto drain;
+                } else {
+                    stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 3 + 1);
+                }
             }
             if (tid == 0 && more) request(a, ctl, BUF_R, 0, l + 1, smem, bars);
             STAMP_REQ(3);
             if (n > 0) {
-                gemv_rows<2, TERN>(smem + a.off_act, wP, wP + mat_bytes(a, n, a.H), n, a.H / 32, a.swi, rowsD0(a), nullptr);
+                gemv_rows<2, TERN>(smem + a.off_act, wP, wP + mat_bytes(a, n, a.H), n, a.H / 32, a.swi, rowsD0(a),
+                                   nullptr, a.spk, ebase + 3 * l + 2);
             }
             __syncthreads();
             STAMP(3, 3);
-            if (!grid_sync(a, ctl)) goto drain;
-            STAMP(3, 4);
+            STAMP(3, 4);      // phase E reads swi as packets, no barrier
         }
         // ---- E: quant of swi, down rows += x
         {
             if (!await_buf(a, ctl, BUF_Q, bars)) goto drain;
             STAMP(4, 0);
             const int n = rowsC(a);
-            if (n > 0) stage<TERN>(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
+            if (n > 0 && !stage_pk<TERN>(a, ctl, smem, a.spk, ebase + 3 * l + 2, a.I, false, nullptr, red,
+                                         1 + 25 * l + 5 * 4 + 1))
+                goto drain;
             if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
             STAMP_REQ(4);
             if (n > 0) {
@@ -741,14 +868,17 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                     gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.xpart + a.H,
                                        rowsC0(a), nullptr);
                 else
-                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
+                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo,
+                                       a.xpk, ebase + 3 * l + 3);
             }
             __syncthreads();
             if (a.P > 1 && !tp_exchange(a, ctl, 2 * l + 1, xo, tpv)) goto drain;
             STAMP(4, 3);
-            if (more && !grid_sync(a, ctl)) goto drain;
+            // one GPU: the next layer's phase A reads x as packets, no barrier
+            if (a.P > 1 && more && !grid_sync(a, ctl)) goto drain;
             STAMP(4, 4);
         }
+    }
     }
 drain:
     // copies still in flight land before the CTA's shared memory is released
@@ -790,10 +920,11 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     a.tern = tern ? 1 : 0;
     a.P = P > 1 ? P : 1;
     if (a.P > TB_TP_MAX) return TB_ERR_UNSUPPORTED;
-    // the exchange epochs: a launch passes 1 + 3L + (L - 1) = 4L grid barriers (the
-    // embed, after attention, o and gate/up, and after down but the last) and has
-    // 2L exchanges; epochs stay unique across launches while 4L >= 2L + 1
-    if (4 * L < 2 * L + 1) return TB_ERR_UNSUPPORTED;
+    // the exchange epochs (P > 1): a launch passes 1 + L + L + (L - 1) = 3L grid
+    // barriers (the embed, after attention, after o's exchange, after down's but
+    // the last) and has 2L exchanges; epochs stay unique across launches while
+    // 3L >= 2L + 1.  One GPU passes L + 1 (the embed, after attention).
+    if (3 * L < 2 * L + 1) return TB_ERR_UNSUPPORTED;
     a.rpC = (H + G - 1) / G;
     a.rpD = (I + G - 1) / G;
     if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
@@ -854,7 +985,9 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.PO = io->PO; a.PML = io->PML; a.counters = io->counters;
     a.bar_count = reinterpret_cast<unsigned long long*>(io->ctrl + 64); a.abort_word = io->ctrl + 128;
     a.head_cnt = io->head_cnt;
-    TB_REQUIRE(ctx, a.head_cnt != nullptr, "decode step: no head counters");
+    a.xpk = io->pk;
+    a.spk = io->pk ? io->pk + a.H : nullptr;
+    TB_REQUIRE(ctx, a.head_cnt != nullptr && a.xpk != nullptr, "decode step: no head counters / packet buffers");
     a.err = ctx->dev_error;
     a.trace = reinterpret_cast<unsigned long long*>(io->trace);
     const int P = io->P > 1 ? io->P : 1;
