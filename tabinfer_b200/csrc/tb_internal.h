@@ -96,7 +96,7 @@ struct tb_step_io {
     unsigned* counters;            // [nKv] attention split arrivals, zero between steps
     unsigned* ctrl;                // [256] zero-initialised: grid barrier counter (u64 at word 64), abort word (128)
     unsigned* head_cnt;            // [layers][kv heads] phase-A arrival counters (every launch zeroes them)
-    unsigned long long* pk;        // [hidden + intermediate] phase-boundary packets (zeroed at creation)
+    unsigned long long* pk;        // [hidden] phase-boundary packets of x after o (zeroed at creation)
     void* trace;                   // optional: u64 [grid][1 + 38 * layers] %globaltimer stamps
     // tensor parallel over peer memory (P > 1): every rank's exchange-arena part
     // buffers (f32 [2][hidden]) and step flags, mapped here; this rank's index

@@ -133,7 +133,7 @@ struct tb_qwen3 {
     int step_tern = -1;                          // weight format the plan was made for (1 ternary)
     unsigned* step_ctrl = nullptr;               // [256] block arrivals, grid barrier, abort word
     unsigned* step_heads = nullptr;              // [layers][kv heads] phase-A arrivals of the persistent step
-    unsigned long long* step_pk = nullptr;       // [hidden + intermediate] phase-boundary packets
+    unsigned long long* step_pk = nullptr;       // [hidden] phase-boundary packets of x after o
     unsigned char* step_attnq = nullptr;         // quantized attention output of the persistent step
     bool step_direct = false;                    // persistent step launched per call (not capturable)
     void* step_trace = nullptr;                  // optional phase trace of the persistent kernel
@@ -305,12 +305,12 @@ bool persistent_ok(tb_qwen3* m)
         }
         if (alloc(m, &m->step_layers, host.size()) || alloc(m, &m->step_ctrl, 256) ||
             alloc(m, &m->step_heads, (size_t)m->c.layers * m->nKv) ||
-            alloc(m, &m->step_pk, (size_t)m->c.hidden + (size_t)m->I) ||
+            alloc(m, &m->step_pk, (size_t)m->c.hidden) ||
             alloc(m, &m->step_attnq, (size_t)m->nHq * m->c.head_dim / 32 * 40))
             return false;
         if (cudaMemcpy(m->step_layers, host.data(), host.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemset(m->step_ctrl, 0, 256 * 4) != cudaSuccess ||
-            cudaMemset(m->step_pk, 0, ((size_t)m->c.hidden + (size_t)m->I) * 8) != cudaSuccess) {
+            cudaMemset(m->step_pk, 0, (size_t)m->c.hidden * 8) != cudaSuccess) {
             cudaGetLastError();
             m->step_layers = nullptr;
             return false;
@@ -653,12 +653,10 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
         // they compute the same bits); under TP both kinds keep the rule above,
         // and the persistent step applies where it gives one 32-key tile per warp
         const long long by_keys = (c.max_seq + 127) / 128;
-        const long long per_sm = ctx->num_sms / m->nKv;
-        m->nsplit = (int)std::max(1LL, std::min(by_keys, per_sm));
-        // a context too long for the persistent step's one 32-key tile a warp
-        // (256 keys a split) runs the multi-kernel step only: three single-stage
-        // 8-warp units an SM
-        if ((c.max_seq + m->nsplit - 1) / m->nsplit > 256) m->nsplit = (int)std::max(1LL, std::min(by_keys, 3 * per_sm));
+        // (a long context past the persistent step keeps this count too: three
+        // single-stage units an SM with three times the splits measured slower at
+        // 32k than one two-stage unit an SM, 571 vs 633 tok/s)
+        m->nsplit = (int)std::max(1LL, std::min(by_keys, (long long)(ctx->num_sms / m->nKv)));
     }
     if (!rc) rc = alloc(m, &m->qr, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->PO, (size_t)B * m->nHq * m->nsplit * hd);

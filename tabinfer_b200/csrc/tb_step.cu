@@ -77,10 +77,8 @@ struct StepArgs {
     unsigned long long* bar_count;   // grid barrier: arrivals since the model was made (monotonic)
     unsigned* abort_word;    // == this launch's tag: a CTA gave up in this launch
     unsigned* head_cnt;      // [L][nKv] phase-A blocks of each kv head written (zeroed by every launch)
-    // phase-boundary packets (epoch << 32 | f32 bits): x rows after o and after
-    // down (one GPU), swi rows after gate/up (every rank)
+    // phase-boundary packets (epoch << 32 | f32 bits): x rows after o (one GPU)
     unsigned long long* xpk; // [H]
-    unsigned long long* spk; // [I]
     int* err;
     // optional phase trace: per CTA 1 + 38 * L %globaltimer stamps (kernel start;
     // per layer and phase: weights ready, activation row loaded, activation
@@ -520,7 +518,7 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
 // other rank's rows of this CTA -- local loads only -- and form
 // x + part_0 + ... + part_{P-1} in rank order, the sum k_tp_allreduce forms,
 // into the CTA's residual rows and x.
-// e = (barriers before this launch) + xi + 1: a launch passes 3L >= 2L + 1
+// e = (barriers before this launch) + xi + 1: a launch passes 4L >= 2L + 1
 // barriers and has 2L exchanges, so epochs grow across launches; a slot holds
 // epoch e - 2 or e, never more (a rank sends exchange xi + 2 only after it
 // received every rank's xi + 1, sent after that rank consumed xi), so the wait
@@ -744,12 +742,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
     }
     if (!grid_sync(a, ctl)) goto drain;
 
-    // epochs of this launch's phase-boundary packets: ebase + 3l + {1 (x after o),
-    // 2 (swi), 3 (x after down)}.  Every launch that writes packets has passed the
-    // embed barrier, so its base (grid barriers before it) exceeds an earlier
-    // one's and the epoch ranges of two launches never meet; a reader waits for
-    // equality, and the earlier writers of a slot (the phase before, the launch
-    // before) carry other epochs.
+    // epochs of this launch's phase-boundary packets (x after o, one GPU): ebase +
+    // 3l + 1.  Every launch that writes packets has passed the embed barrier, so its
+    // base (grid barriers before it) exceeds an earlier one's and the epoch ranges
+    // of two launches never meet; a reader waits for equality, and the earlier
+    // writer of a slot (the layer before, the launch before) carries another epoch.
+    // (Packets at the gate/up -> down and down -> q/k/v boundaries measured slower
+    // than the barriers there: every CTA polling all 6144 swi / 2048 x values
+    // loads L2 harder than one counter, and those boundaries stay barriers.)
     {
     const unsigned ebase = (unsigned)(ctl->base / gridDim.x) * (unsigned)(3 * a.L);
     for (int l = 0; l < a.L; l++) {
@@ -762,15 +762,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             const BlockA b = block_a(a);
             const unsigned char* wR = smem + a.off_R;
             const uint16_t* nws = reinterpret_cast<const uint16_t*>(wR + (b.live ? mat_bytes(a, RBA, a.H) : 0));
-            if (b.live) {
-                if (l > 0 && a.P == 1) {
-                    if (!stage_pk<TERN>(a, ctl, smem, a.xpk, ebase + 3 * (l - 1) + 3, a.H, true, nws, red,
-                                        1 + 25 * l + 5 * 0 + 1))
-                        goto drain;
-                } else {
-                    stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
-                }
-            }
+            if (b.live) stage<TERN>(a, smem, a.x, a.H, true, nws, red, 1 + 25 * l + 5 * 0 + 1);
             if (tid == 0 && l > 0) request(a, ctl, BUF_Q, 4, l, smem, bars);   // Q held E(l-1)
             STAMP_REQ(0);
             if (b.live) {
@@ -847,20 +839,19 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
             STAMP_REQ(3);
             if (n > 0) {
                 gemv_rows<2, TERN>(smem + a.off_act, wP, wP + mat_bytes(a, n, a.H), n, a.H / 32, a.swi, rowsD0(a),
-                                   nullptr, a.spk, ebase + 3 * l + 2);
+                                   nullptr);
             }
             __syncthreads();
             STAMP(3, 3);
-            STAMP(3, 4);      // phase E reads swi as packets, no barrier
+            if (!grid_sync(a, ctl)) goto drain;
+            STAMP(3, 4);
         }
         // ---- E: quant of swi, down rows += x
         {
             if (!await_buf(a, ctl, BUF_Q, bars)) goto drain;
             STAMP(4, 0);
             const int n = rowsC(a);
-            if (n > 0 && !stage_pk<TERN>(a, ctl, smem, a.spk, ebase + 3 * l + 2, a.I, false, nullptr, red,
-                                         1 + 25 * l + 5 * 4 + 1))
-                goto drain;
+            if (n > 0) stage<TERN>(a, smem, a.swi, a.I, false, nullptr, red, 1 + 25 * l + 5 * 4 + 1);
             if (more) attn_prefetch<GRP>(a, sl[l + 1], smem);
             STAMP_REQ(4);
             if (n > 0) {
@@ -868,14 +859,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_decode_step(const StepArgs a)
                     gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.xpart + a.H,
                                        rowsC0(a), nullptr);
                 else
-                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo,
-                                       a.xpk, ebase + 3 * l + 3);
+                    gemv_rows<1, TERN>(smem + a.off_act, smem + a.off_Q, nullptr, n, a.I / 32, a.x, rowsC0(a), xo);
             }
             __syncthreads();
             if (a.P > 1 && !tp_exchange(a, ctl, 2 * l + 1, xo, tpv)) goto drain;
             STAMP(4, 3);
-            // one GPU: the next layer's phase A reads x as packets, no barrier
-            if (a.P > 1 && more && !grid_sync(a, ctl)) goto drain;
+            if (more && !grid_sync(a, ctl)) goto drain;
             STAMP(4, 4);
         }
     }
@@ -920,11 +909,11 @@ int tb_step_plan_make(tb_ctx* ctx, int L, int H, int nHq, int nKv, int hd, int I
     a.tern = tern ? 1 : 0;
     a.P = P > 1 ? P : 1;
     if (a.P > TB_TP_MAX) return TB_ERR_UNSUPPORTED;
-    // the exchange epochs (P > 1): a launch passes 1 + L + L + (L - 1) = 3L grid
-    // barriers (the embed, after attention, after o's exchange, after down's but
-    // the last) and has 2L exchanges; epochs stay unique across launches while
-    // 3L >= 2L + 1.  One GPU passes L + 1 (the embed, after attention).
-    if (3 * L < 2 * L + 1) return TB_ERR_UNSUPPORTED;
+    // the exchange epochs (P > 1): a launch passes 1 + 3L + (L - 1) = 4L grid
+    // barriers (the embed, after attention, after o's exchange, after gate/up,
+    // after down's exchange but the last) and has 2L exchanges; epochs stay unique
+    // across launches while 4L >= 2L + 1.  One GPU passes 3L (no barrier after o).
+    if (4 * L < 2 * L + 1) return TB_ERR_UNSUPPORTED;
     a.rpC = (H + G - 1) / G;
     a.rpD = (I + G - 1) / G;
     if (a.rpC > 64) return TB_ERR_UNSUPPORTED;      // own rows of x kept in shared memory
@@ -986,7 +975,6 @@ int tb_step_launch(tb_ctx* ctx, tb_step_plan* p, const tb_step_io* io)
     a.bar_count = reinterpret_cast<unsigned long long*>(io->ctrl + 64); a.abort_word = io->ctrl + 128;
     a.head_cnt = io->head_cnt;
     a.xpk = io->pk;
-    a.spk = io->pk ? io->pk + a.H : nullptr;
     TB_REQUIRE(ctx, a.head_cnt != nullptr && a.xpk != nullptr, "decode step: no head counters / packet buffers");
     a.err = ctx->dev_error;
     a.trace = reinterpret_cast<unsigned long long*>(io->trace);
