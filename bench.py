@@ -374,14 +374,26 @@ def chain_gbs(dev, ctx, B, steps):
     x, q, k, v, swi, logits = z(B, H6), z(B, NHQ6 * HD6), z(B, NKV6 * HD6), z(B, NKV6 * HD6), z(B, INTER6), z(B, VOCAB6)
     tok = torch.zeros(B, dtype=torch.int32, device=dev)
 
+    # batch >= 2: the tensor-core GEMVs (one weight read for all rows; a
+    # quantization launch before each), the route the decode step takes
+    mma = B >= 2
+
     def step():
         for L in c.layers:
-            tb.gemv_dp4a_multi(x, [L["q"], L["k"], L["v"]], norm_w=L["ln1"], eps=1e-6, ys=[q, k, v])
-            tb.gemv_dp4a(q, *L["o"], y=x, acc=True)
-            tb.gate_up_silu_dp4a(x, *L["gate"], *L["up"], norm_w=L["ln2"], eps=1e-6, swi=swi)
-            tb.gemv_dp4a(swi, *L["down"], y=x, acc=True)
+            if mma:
+                tb.gemv_mma_multi(x, [L["q"], L["k"], L["v"]], norm_w=L["ln1"], eps=1e-6, ys=[q, k, v])
+                tb.gemv_mma(q, *L["o"], y=x, acc=True)
+                tb.gate_up_silu_mma(x, *L["gate"], *L["up"], norm_w=L["ln2"], eps=1e-6, swi=swi)
+                tb.gemv_mma(swi, *L["down"], y=x, acc=True)
+            else:
+                tb.gemv_dp4a_multi(x, [L["q"], L["k"], L["v"]], norm_w=L["ln1"], eps=1e-6, ys=[q, k, v])
+                tb.gemv_dp4a(q, *L["o"], y=x, acc=True)
+                tb.gate_up_silu_dp4a(x, *L["gate"], *L["up"], norm_w=L["ln2"], eps=1e-6, swi=swi)
+                tb.gemv_dp4a(swi, *L["down"], y=x, acc=True)
         if B == 1:
             tb.gemv_q_norm(x, c.norm, 1e-6, *c.lm_head, y=logits)
+        elif mma:
+            tb.gemv_mma(x, *c.lm_head, norm_w=c.norm, eps=1e-6, y=logits)
         else:
             tb.gemv_dp4a(x, *c.lm_head, norm_w=c.norm, eps=1e-6, y=logits)
         tb.argmax(logits, out=tok)
@@ -408,7 +420,8 @@ def chain_gbs(dev, ctx, B, steps):
     del c
     torch.cuda.synchronize(dev)
     return {"gbs": round(chain_bytes(B) / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4), "batch": B,
-            "bytes_per_step": chain_bytes(B), "launches_per_step": 4 * LAYERS6 + 3}
+            "bytes_per_step": chain_bytes(B), "launches_per_step": (8 * LAYERS6 + 4) if mma else (4 * LAYERS6 + 3),
+            "gemv": "mma_s8u8" if mma else "dp4a"}
 
 
 # ---------------------------------------------------------------------------
@@ -1333,6 +1346,26 @@ def profile_q2g64():
     assert tb.default_context(0).device_error() == 0
 
 
+def decode_extra(dev, stream, B, S):
+    """Qwen3-1.7B decode steps of B sequences at context S (recorded step, 50 timed)."""
+    import torch
+    mx = build_model(Q17, dev, B, S, 64 + 16, 1, 0)
+    mx.set_tokens([(3 + 101 * b) % Q17["vocab"] for b in range(B)], [S - 1] * B)
+    for _ in range(5):
+        mx.step()
+    torch.cuda.synchronize(dev)
+    msx = time_steps(mx, 50, stream) / 50
+    errx = mx.ctx.device_error()
+    assert errx == 0, "decode extra device error 0x%x" % errx
+    out = {"tok_per_s": round(B * 1e3 / msx, 1), "ms_per_step": round(msx, 4),
+           "step_hbm_gbs": round(step_bytes(Q17, 1, B, S) / (msx * 1e-3) / 1e9, 1),
+           "kernels_per_step": mx.launches_per_step()[0]}
+    mx.close()
+    del mx
+    torch.cuda.synchronize(dev)
+    return out
+
+
 def run_only(name, steps):
     """One extra block alone (a development run; not the benchmark line)."""
     import torch
@@ -1343,6 +1376,10 @@ def run_only(name, steps):
     peak, _ = load_peaks()
     if name == "q2g64":
         out = q2g64_extra(dev, ctx, peak)
+    elif name == "decode":
+        stream = torch.cuda.current_stream(dev)     # the stream main() times the model steps on
+        out = {"batch%d_context%d" % (B, S): decode_extra(dev, stream, B, S)
+               for B, S in ((16, 4096), (4, 4096), (8, 4096))}
     elif name == "chain":
         out = {}
         for B in (1, 4, 8):
@@ -1390,7 +1427,7 @@ def main():
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
     ap.add_argument("--profile-q2g64", action="store_true",
                     help="three Q2_0_g64 GEMV launches on 151936 x 2048 matrices (for an ncu capture), then exit")
-    ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds"),
+    ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds", "decode"),
                     help="run one extra block alone on GPU 0 and print its JSON (development runs)")
     args = ap.parse_args()
     if args.only:
@@ -1582,20 +1619,7 @@ def main():
         for (Bx, Sx) in ((16, 4096), (1, 32768)):
             if (Bx, Sx) == (B, S):
                 continue
-            mx = build_model(Q17, dev, Bx, Sx, 64 + 16, 1, 0)
-            mx.set_tokens([(3 + 101 * b) % Q17["vocab"] for b in range(Bx)], [Sx - 1] * Bx)
-            for _ in range(5):
-                mx.step()
-            torch.cuda.synchronize(dev)
-            msx = time_steps(mx, 50, stream) / 50
-            errx = mx.ctx.device_error()
-            assert errx == 0, "decode extra device error 0x%x" % errx
-            extras["batch%d_context%d" % (Bx, Sx)] = {
-                "tok_per_s": round(Bx * 1e3 / msx, 1), "ms_per_step": round(msx, 4),
-                "step_hbm_gbs": round(step_bytes(Q17, 1, Bx, Sx) / (msx * 1e-3) / 1e9, 1)}
-            mx.close()
-            del mx
-            torch.cuda.synchronize(dev)
+            extras["batch%d_context%d" % (Bx, Sx)] = decode_extra(dev, stream, Bx, Sx)
         peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if os.path.exists(
             os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
         extras["prefill_gemm_1.7b"] = prefill_extra(dev, peaks.get("bf16_tflops", 1590.0), stream)

@@ -114,8 +114,10 @@ TB_API int tb_gemv_int4_f32(tb_ctx *ctx, float *y, const float *x, const uint32_
 
 /* The linearQ router for one int4 matrix, models/qwen3.js:1588-1608:
  * T==1 and N<16384 -> quantQ8 + gemvDP4; T==1 and N>=16384 -> gemvQ;
- * 1<T<=8 -> per-token int8 (QUANTQ8T) x int4 math of gemmDP4A (:1397-1407);
- * T>8 -> QUANTQ8T into context scratch + gemmDP4A with exact group sums
+ * 2<=T<=16 with K%256==0 and N%8==0 -> QUANTQ8T into context scratch + the
+ * gemmDP4A group-sum math on the tensor cores, one weight read (tb_gemv_int4_mma);
+ * other 1<T<=8 -> per-token int8 (QUANTQ8T) x int4 math of gemmDP4A (:1397-1407);
+ * T>16 -> QUANTQ8T into context scratch + gemmDP4A with exact group sums
  * (tb_gemm_dp4, the reference's default; its __noDp4Gemm f16 route is
  * tb_gemm_int4_g32) when T, N and K are multiples of 128, else
  * TB_ERR_UNSUPPORTED. */
@@ -161,6 +163,33 @@ TB_API int tb_gateup_silu_int4_dp4a(tb_ctx *ctx, float *swi, const float *x, con
 TB_API int tb_gemv_int4_f32_norm(tb_ctx *ctx, float *y, const float *x, const uint16_t *norm_w16,
                                  float eps, const uint32_t *pack, const uint16_t *scales,
                                  int64_t N, int64_t K, int batch, int acc);
+
+/* linearQ's T > 1 route, the DP4A GEMM math (models/qwen3.js:1600-1607,
+ * gemmdp4Wgsl :1321-1407, gemmTern :1410-1420), at T = 2..16 rows with every
+ * weight read once: QUANTQ8T of x (RMSNORMQ first when norm_w16 is non-null)
+ * into context scratch, then per 32-group the exact int32 sum of int8 x times
+ * (nib - 8) (or the ternary WebGPU code - 1) on the tensor cores, scaled by
+ * xs * s in f32.  K % 256 == 0, N % 8 == 0; x, weights 16-byte aligned.
+ *   tb_gemv_int4_mma / tb_gemv_tern_wgsl_mma: y [T,N] (+= with acc)
+ *   tb_gemv_int4_mma_multi: the q/k/v triple (count <= 3) from one quantization
+ *   tb_gateup_silu_*_mma: swi [T,I] = silu(W_g . a) * (W_u . a) (gateUpSiluDP4) */
+TB_API int tb_gemv_int4_mma(tb_ctx *ctx, float *y, const float *x, const uint16_t *norm_w16, float eps,
+                            const uint32_t *pack, const uint16_t *scales, int64_t N, int64_t K, int T,
+                            int acc);
+TB_API int tb_gemv_int4_mma_multi(tb_ctx *ctx, int count, float *const *ys, const uint32_t *const *packs,
+                                  const uint16_t *const *scales, const int64_t *Ns, const float *x,
+                                  const uint16_t *norm_w16, float eps, int64_t K, int T, int acc);
+TB_API int tb_gateup_silu_int4_mma(tb_ctx *ctx, float *swi, const float *x, const uint16_t *norm_w16,
+                                   float eps, const uint32_t *gpack, const uint16_t *gscales,
+                                   const uint32_t *upack, const uint16_t *uscales, int64_t I, int64_t K,
+                                   int T);
+TB_API int tb_gemv_tern_wgsl_mma(tb_ctx *ctx, float *y, const float *x, const uint16_t *norm_w16, float eps,
+                                 const uint32_t *pack, const uint16_t *scales, int64_t N, int64_t K, int T,
+                                 int acc);
+TB_API int tb_gateup_silu_tern_wgsl_mma(tb_ctx *ctx, float *swi, const float *x, const uint16_t *norm_w16,
+                                        float eps, const uint32_t *gpack, const uint16_t *gscales,
+                                        const uint32_t *upack, const uint16_t *uscales, int64_t I,
+                                        int64_t K, int T);
 
 /* ---- ternary Q2_0_g64 path (native/crates/n2-kernels) -------------------- */
 
@@ -251,9 +280,10 @@ TB_API int tb_gemm_tern_wgsl(tb_ctx *ctx, float *y, const int8_t *xq, const floa
                              const uint32_t *pack, const uint16_t *scales, int64_t M, int64_t N,
                              int64_t K, int acc);
 
-/* linearQ for a ternary weight record (qwen3.js:1594-1598): T <= 8 rows run the
- * ternary GEMV (quantQ8 fused), T > 8 quantize (QUANTQ8T) into context scratch
- * and run tb_gemm_tern_wgsl (T % 128 == 0, N % 256 == 0). */
+/* linearQ for a ternary weight record (qwen3.js:1594-1598): 2 <= T <= 16 rows
+ * with K % 256 == 0 and N % 8 == 0 run the tensor-core GEMV (tb_gemv_tern_wgsl_mma),
+ * other T <= 8 the ternary GEMV (quantQ8 fused), T > 16 quantize (QUANTQ8T) into
+ * context scratch and run tb_gemm_tern_wgsl (T % 128 == 0, N % 256 == 0). */
 TB_API int tb_linear_tern_wgsl(tb_ctx *ctx, float *y, const float *x, const uint32_t *pack,
                                const uint16_t *scales, int64_t T, int64_t N, int64_t K, int acc);
 

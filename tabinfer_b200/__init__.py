@@ -12,7 +12,7 @@ Errors raise TabInferError, as the reference throws.
 from .ops import (  # noqa: F401
     TabInferError, Context, default_context,
     quantize_int4_bf16, convert_bf16_f16, quant_q8, rmsnorm_q8, gemv_q, gemv_dp4, gemv_dp4_multi, linear_q,
-    gemv_dp4a, gemv_dp4a_multi, gate_up_silu_dp4a, gemv_q_norm, gemm_q,
+    gemv_dp4a, gemv_dp4a_multi, gate_up_silu_dp4a, gemv_mma, gemv_mma_multi, gate_up_silu_mma, gemv_q_norm, gemm_q,
     requant_int3, quant_int3, moe_router, moe_ffn_int3,
     gate_up_silu_dp4, pack_ternary, quantize_act, quantize_wasm, gemv_tern, linear_tern,
     quantize_tern_bf16, gemv_tern_wgsl, gemv_tern_wgsl_dp4a_multi, gate_up_silu_tern, gate_up_silu_tern_dp4a,

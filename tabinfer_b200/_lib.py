@@ -53,6 +53,11 @@ SIGNATURES = {
     "tb_gemv_int4_q8_multi": [P, I32, P, P, P, P, P, P, I64, I32, I32],
     "tb_gemv_int4_dp4a": [P, P, P, P, F32, P, P, I64, I64, I32, I32],
     "tb_gemv_int4_dp4a_multi": [P, I32, P, P, P, P, P, P, F32, I64, I32, I32],
+    "tb_gemv_int4_mma": [P, P, P, P, F32, P, P, I64, I64, I32, I32],
+    "tb_gemv_int4_mma_multi": [P, I32, P, P, P, P, P, P, F32, I64, I32, I32],
+    "tb_gateup_silu_int4_mma": [P, P, P, P, F32, P, P, P, P, I64, I64, I32],
+    "tb_gemv_tern_wgsl_mma": [P, P, P, P, F32, P, P, I64, I64, I32, I32],
+    "tb_gateup_silu_tern_wgsl_mma": [P, P, P, P, F32, P, P, P, P, I64, I64, I32],
     "tb_gateup_silu_int4_dp4a": [P, P, P, P, F32, P, P, P, P, I64, I64, I32],
     "tb_gemv_int4_f32_norm": [P, P, P, P, F32, P, P, I64, I64, I32, I32],
     "tb_pack_tern_q2g64": [P, P, P, P, I64, I64],

@@ -8,6 +8,14 @@
 int tb_gemv_dp4a_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
                       const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
                       float eps, int64_t K, int batch, int acc);
+// decode GEMVs over 2..16 rows on the tensor cores (one weight read): quantize
+// x into buf (tb_gemv_mma_act_bytes bytes) and run `count` matrices, or gate/up
+// with silu when gateup (count 2, ys[0] the output)
+size_t tb_gemv_mma_act_bytes(int64_t K, int batch);
+bool tb_gemv_mma_fits(int64_t K, const int64_t* Ns, int count, int batch);
+int tb_gemv_mma_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
+                     const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
+                     float eps, int64_t K, int batch, int acc, bool tern, bool gateup, void* buf);
 int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
                      int64_t N, int64_t K, int batch, int acc);
 int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,

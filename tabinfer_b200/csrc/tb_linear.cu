@@ -15,6 +15,12 @@ TB_API int tb_linear_int4(tb_ctx* ctx, float* y, const float* x, const uint32_t*
     TB_REQUIRE(ctx, T >= 1, "T must be >= 1");
     TB_REQUIRE(ctx, K > 0 && K % 32 == 0, "K must be a positive multiple of 32");
     if (T == 1 && N >= 16384) return tb_gemv_f32_impl(ctx, y, x, pack, scales, N, K, 1, acc);
+    if (T >= 2 && T <= 16 && tb_gemv_mma_fits(K, &N, 1, (int)T)) {
+        // the DP4A math on the tensor cores, every weight read once for all rows
+        void* buf = tb_ctx_scratch(ctx, tb_gemv_mma_act_bytes(K, (int)T));
+        if (!buf) return TB_ERR_NOMEM;
+        return tb_gemv_mma_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc, false, false, buf);
+    }
     if (T > 8) {
         // prefill: linearQ's default gemmDP4A (qwen3.js:1605-1607) -- QUANTQ8T rows
         // into context scratch, then the tensor-core GEMM on them
@@ -34,7 +40,9 @@ TB_API int tb_linear_int4(tb_ctx* ctx, float* y, const float* x, const uint32_t*
     return tb_gemv_dp4a_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
 }
 
-// linearQ's ternary branch (qwen3.js:1594-1598).  T <= 8 runs the ternary GEMV
+// linearQ's ternary branch (qwen3.js:1594-1598).  T = 2..16 (K % 256 == 0, N % 8
+// == 0) runs the tensor-core GEMV with the same exact group sums; other T <= 8 the
+// ternary GEMV
 // with quantQ8 in its prologue: per 32-group the same exact int32 sum and f32
 // scaling as the reference's gemvTern (T = 1) and gemmTern tiles (T > 1).
 // T > 8 quantizes the rows (QUANTQ8T) into context scratch and runs gemmTern
@@ -45,6 +53,11 @@ TB_API int tb_linear_tern_wgsl(tb_ctx* ctx, float* y, const float* x, const uint
     if (!ctx) return TB_ERR_INVALID;
     TB_REQUIRE(ctx, T >= 1, "T must be >= 1");
     TB_REQUIRE(ctx, K > 0 && K % 64 == 0, "K must be a positive multiple of 64");
+    if (T >= 2 && T <= 16 && tb_gemv_mma_fits(K, &N, 1, (int)T)) {
+        void* buf = tb_ctx_scratch(ctx, tb_gemv_mma_act_bytes(K, (int)T));
+        if (!buf) return TB_ERR_NOMEM;
+        return tb_gemv_mma_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc, true, false, buf);
+    }
     if (T <= 8) return tb_gemv_tern_wgsl_impl(ctx, 1, &y, &pack, &scales, &N, x, nullptr, 0.0f, K, (int)T, acc);
     if (T % 128 != 0 || N % 128 != 0 || K % 128 != 0)
         return tb_fail(ctx, TB_ERR_UNSUPPORTED,

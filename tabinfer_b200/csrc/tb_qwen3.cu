@@ -32,7 +32,9 @@
 
 namespace {
 
-constexpr int GEMV_MAX_B = 8;      // rows per fused-GEMV launch
+constexpr int GEMV_MAX_B = 8;      // rows per fused-GEMV launch (dp4a GEMV)
+constexpr int MMA_MIN_B = 2;       // rows from which the tensor-core GEMV reads each weight once
+constexpr int MMA_MAX_B = 16;      // rows per tensor-core GEMV launch
 
 // NCCL entry points, resolved from the process's libnccl.so.2 (the one the
 // framework that created the ranks already loaded, when there is one).
@@ -135,6 +137,7 @@ struct tb_qwen3 {
     unsigned* step_heads = nullptr;              // [layers][kv heads] phase-A arrivals of the persistent step
     unsigned long long* step_pk = nullptr;       // [hidden] phase-boundary packets of x after o
     unsigned char* step_attnq = nullptr;         // quantized attention output of the persistent step
+    unsigned char* mma_act = nullptr;            // fragment-ordered int8 rows of the tensor-core GEMVs
     bool step_direct = false;                    // persistent step launched per call (not capturable)
     void* step_trace = nullptr;                  // optional phase trace of the persistent kernel
 };
@@ -220,16 +223,29 @@ int nccl_check(tb_qwen3* m, ncclResult_t r, const char* what)
     return tb_fail(m->ctx, TB_ERR_CUDA, "%s: %s", what, nccl().GetErrorString(r));
 }
 
+// The tensor-core GEMV (every weight read once for up to MMA_MAX_B rows) runs
+// the matrices of a call when the batch has at least MMA_MIN_B rows and their
+// shapes fit it; otherwise the dp4a GEMV in launches of GEMV_MAX_B rows.
+bool use_mma(const tb_qwen3* m, const int64_t* Ns, int count, int64_t K)
+{
+    return m->mma_act && m->c.batch >= MMA_MIN_B && tb_gemv_mma_fits(K, Ns, count, MMA_MIN_B);
+}
+
 // y (+)= W . x over B rows, in launches of at most GEMV_MAX_B rows (fused int8
 // quantization of x, optional fused RMSNorm with norm_w)
 int gemv_rows(tb_qwen3* m, float* y, const float* x, const Mat& w, const uint16_t* norm_w, int acc)
 {
     const int B = m->c.batch;
-    for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
-        const int nb = std::min(GEMV_MAX_B, B - b0);
+    const bool mma = use_mma(m, &w.N, 1, w.K);
+    const int chunk = mma ? MMA_MAX_B : GEMV_MAX_B;
+    for (int b0 = 0; b0 < B; b0 += chunk) {
+        const int nb = std::min(chunk, B - b0);
         float* yb = y + (int64_t)b0 * w.N;
         const float* xb = x + (int64_t)b0 * w.K;
-        if (w.tern)
+        if (mma && nb >= MMA_MIN_B)
+            TRY(tb_gemv_mma_impl(m->ctx, 1, &yb, &w.pack, &w.scales, &w.N, xb, norm_w, m->c.rms_eps, w.K, nb, acc,
+                                 w.tern, false, m->mma_act));
+        else if (w.tern)
             TRY(tb_gemv_tern_wgsl_impl(m->ctx, 1, &yb, &w.pack, &w.scales, &w.N, xb, norm_w, m->c.rms_eps, w.K, nb,
                                        acc));
         else
@@ -364,15 +380,23 @@ int issue_step(tb_qwen3* m)
     TRY(tb_embed_gather(ctx, m->ids, 0, m->embed, m->x[cur], B, H));
     for (int l = 0; l < c.layers; l++) {
         Layer& Ly = m->L[l];
-        // fused rmsnormQ + q/k/v (one launch per <= 8 rows)
-        for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
-            const int nb = std::min(GEMV_MAX_B, B - b0);
+        // fused rmsnormQ + q/k/v (one launch per <= 8 rows, or per <= 16 rows on
+        // the tensor cores)
+        const bool same_kind = Ly.q.tern == Ly.k.tern && Ly.k.tern == Ly.v.tern;
+        const int64_t qkvN[3] = {Ly.q.N, Ly.k.N, Ly.v.N};
+        const bool qkv_mma = same_kind && use_mma(m, qkvN, 3, H);
+        const int qkv_chunk = qkv_mma ? MMA_MAX_B : GEMV_MAX_B;
+        for (int b0 = 0; b0 < B; b0 += qkv_chunk) {
+            const int nb = std::min(qkv_chunk, B - b0);
             float* ys[3] = {m->q + (int64_t)b0 * Ly.q.N, m->k + (int64_t)b0 * Ly.k.N, m->v + (int64_t)b0 * Ly.v.N};
             const uint32_t* packs[3] = {Ly.q.pack, Ly.k.pack, Ly.v.pack};
             const uint16_t* scs[3] = {Ly.q.scales, Ly.k.scales, Ly.v.scales};
-            const int64_t Ns[3] = {Ly.q.N, Ly.k.N, Ly.v.N};
+            const int64_t* Ns = qkvN;
             const float* xb = m->x[cur] + (int64_t)b0 * H;
-            if (Ly.q.tern == Ly.k.tern && Ly.k.tern == Ly.v.tern) {
+            if (qkv_mma && nb >= MMA_MIN_B) {
+                TRY(tb_gemv_mma_impl(ctx, 3, ys, packs, scs, Ns, xb, Ly.ln1, c.rms_eps, H, nb, 0, Ly.q.tern, false,
+                                     m->mma_act));
+            } else if (same_kind) {
                 if (Ly.q.tern) TRY(tb_gemv_tern_wgsl_impl(ctx, 3, ys, packs, scs, Ns, xb, Ly.ln1, c.rms_eps, H, nb, 0));
                 else TRY(tb_gemv_int4_dp4a_multi(ctx, 3, ys, packs, scs, Ns, xb, Ly.ln1, c.rms_eps, H, nb, 0));
             } else {   // mixed weight kinds: one launch per matrix
@@ -391,9 +415,18 @@ int issue_step(tb_qwen3* m)
         TRY(tb_attn_decode_impl(ctx, m->attn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, c.max_seq, m->nHq, m->nKv, hd,
                                 m->nsplit, m->PO, m->PML, m->counters, B, c.max_seq, m->pos, true));
         TRY(proj_residual(m, cur, m->attn, Ly.o, 2 * l));
-        for (int b0 = 0; b0 < B; b0 += GEMV_MAX_B) {
-            const int nb = std::min(GEMV_MAX_B, B - b0);
-            if (Ly.gate.tern)   // gateUpSiluQ's ternary branch (qwen3.js:730)
+        const int64_t guN[2] = {m->I, m->I};
+        const bool gu_mma = Ly.gate.tern == Ly.up.tern && use_mma(m, guN, 2, H);
+        const int gu_chunk = gu_mma ? MMA_MAX_B : GEMV_MAX_B;
+        for (int b0 = 0; b0 < B; b0 += gu_chunk) {
+            const int nb = std::min(gu_chunk, B - b0);
+            if (gu_mma && nb >= MMA_MIN_B) {
+                float* ys[2] = {m->swi + (int64_t)b0 * m->I, m->swi + (int64_t)b0 * m->I};
+                const uint32_t* packs[2] = {Ly.gate.pack, Ly.up.pack};
+                const uint16_t* scs[2] = {Ly.gate.scales, Ly.up.scales};
+                TRY(tb_gemv_mma_impl(ctx, 2, ys, packs, scs, guN, m->x[cur] + (int64_t)b0 * H, Ly.ln2, c.rms_eps, H,
+                                     nb, 0, Ly.gate.tern, true, m->mma_act));
+            } else if (Ly.gate.tern)   // gateUpSiluQ's ternary branch (qwen3.js:730)
                 TRY(tb_gateup_silu_tern_wgsl_dp4a(ctx, m->swi + (int64_t)b0 * m->I, m->x[cur] + (int64_t)b0 * H,
                                                   Ly.ln2, c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack,
                                                   Ly.up.scales, m->I, H, nb));
@@ -646,6 +679,10 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
     if (!rc) rc = alloc(m, &m->attn, B * m->nHq * hd);
     if (!rc) rc = alloc(m, &m->swi, B * m->I);
     if (!rc) rc = alloc(m, &m->logits, B * m->V);
+    if (!rc && B >= MMA_MIN_B) {
+        const int64_t kmax = std::max<int64_t>({(int64_t)H, m->nHq * hd, m->I});
+        rc = alloc(m, &m->mma_act, tb_gemv_mma_act_bytes(kmax, (int)std::min<int64_t>(B, MMA_MAX_B)));
+    }
     m->nsplit = tb_attn_auto_nsplit(ctx, c.max_seq, m->nKv * B);
     if (B == 1 && m->P == 1) {
         // one sequence on one GPU: one (kv head, split) unit per SM, the split

@@ -234,6 +234,55 @@ def gate_up_silu_dp4a(x, gpack, gscales, upack, uscales, norm_w=None, eps=1e-6, 
     return swi
 
 
+def gemv_mma(x, pack, scales, norm_w=None, eps=1e-6, y=None, acc=False, tern=False):
+    """linearQ's T > 1 DP4A route (qwen3.js:1600-1607) at 2..16 rows on the tensor
+    cores, every weight read once: y (+)= W . quantQ8(rmsnorm?(x)); int4 G32 weights,
+    or the ternary WebGPU layout with tern=True."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    N = pack.shape[0]
+    if y is None:
+        y = torch.zeros((B, N), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    fn = LIB.tb_gemv_tern_wgsl_mma if tern else LIB.tb_gemv_int4_mma
+    c.check(fn(c.h, _p(y), _p(x2), _p(norm_w), float(eps), _p(pack), _p(scales), N, K, B, 1 if acc else 0),
+            "gemv_mma")
+    return y
+
+
+def gemv_mma_multi(x, mats, norm_w=None, eps=1e-6, ys=None, acc=False):
+    """rmsnormQ + the q/k/v projGemv triple (qwen3.js:3981-3984) at 2..16 rows on the
+    tensor cores: one quantization, one launch.  mats: [(pack, scales)] (<= 3)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, K = x2.shape
+    n = len(mats)
+    if ys is None:
+        ys = [torch.zeros((B, p.shape[0]), dtype=torch.float32, device=x.device) for p, _ in mats]
+    arr_y = (P * n)(*[y.data_ptr() for y in ys])
+    arr_p = (P * n)(*[p.data_ptr() for p, _ in mats])
+    arr_s = (P * n)(*[s.data_ptr() for _, s in mats])
+    arr_n = (ctypes.c_int64 * n)(*[p.shape[0] for p, _ in mats])
+    c = _ctx(x)
+    c.check(LIB.tb_gemv_int4_mma_multi(c.h, n, ctypes.cast(arr_y, P), ctypes.cast(arr_p, P), ctypes.cast(arr_s, P),
+                                       ctypes.cast(arr_n, P), _p(x2), _p(norm_w), float(eps), K, B,
+                                       1 if acc else 0), "gemv_mma_multi")
+    return ys
+
+
+def gate_up_silu_mma(x, gpack, gscales, upack, uscales, norm_w=None, eps=1e-6, swi=None, tern=False):
+    """rmsnormQ + gate/up + silu(gate) * up at 2..16 rows on the tensor cores."""
+    x2 = x.reshape(-1, x.shape[-1])
+    B, Hd = x2.shape
+    I = gpack.shape[0]
+    if swi is None:
+        swi = torch.empty((B, I), dtype=torch.float32, device=x.device)
+    c = _ctx(x)
+    fn = LIB.tb_gateup_silu_tern_wgsl_mma if tern else LIB.tb_gateup_silu_int4_mma
+    c.check(fn(c.h, _p(swi), _p(x2), _p(norm_w), float(eps), _p(gpack), _p(gscales), _p(upack), _p(uscales), I, Hd,
+               B), "gateup_silu_mma")
+    return swi
+
+
 def gemm_q(x, pack, scales, y=None, acc=False):
     """Prefill GEMM on the tensor cores: y[M,N] (+)= f16(x) . f16(deq(W))^T
     (gemmQ, qwen3.js:964-1026).  x [M,K] f32 or bf16."""

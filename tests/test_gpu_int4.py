@@ -226,9 +226,10 @@ def test_fused_norm_lm_head(cuda, B):
     assert row_rel_err(host(y_fused), oracle.gemv_int4_f32act(host(normed), pack, sc)) < TOL
 
 
-@pytest.mark.parametrize("T,N", [(1, 1024), (1, 20000), (4, 3072), (8, 1024)])
+@pytest.mark.parametrize("T,N", [(1, 1024), (1, 20000), (4, 3072), (8, 1024), (12, 1024), (16, 4096), (5, 1001)])
 def test_linear_router(cuda, T, N):
-    """linearQ routing (qwen3.js:1597-1608): T=1 N<16384 int8; T=1 N>=16384 f32; T>1 per-token int8."""
+    """linearQ routing (qwen3.js:1597-1608): T=1 N<16384 int8; T=1 N>=16384 f32; T>1 per-token
+    int8 (the tensor-core GEMV at 2..16 rows, the dp4a GEMV where the rows are not a multiple of 8)."""
     K = 1024
     pack, sc = _mat(T + N, N, K)
     rng = np.random.default_rng(T)

@@ -2,7 +2,7 @@
 models/qwen3.js forward (T = 1, int8 KV): logits within 2e-2 max-abs, argmax
 ids equal wherever the top-2 margin exceeds that tolerance, positions advanced,
 the cache rows the step wrote equal to the oracle's (int8 within 1, scales
-1e-5 rel), and a replay of the recorded step continuing from the GPU's state."""
+2e-3 rel: one RMSNorm tie flip), and a replay of the recorded step continuing from the GPU's state."""
 import numpy as np
 import pytest
 import torch
@@ -55,14 +55,18 @@ def _check_step(m, om, cfg, ids, pos, route_f32):
                 if i in (0, 2):
                     assert np.max(np.abs(g.astype(np.int32) - r.astype(np.int32))) <= 1, "layer %d int8 row" % l
                 else:
-                    np.testing.assert_allclose(g, r, rtol=1e-5)
+                    # f32 scales of the row: a one-LSB RMSNorm tie flip in the int8
+                    # activation (the quantizers agree up to ties) moves every output
+                    # of a 256-wide dot product by about 1/(127*16)
+                    np.testing.assert_allclose(g, r, rtol=2e-3)
     return new_ids, new_pos
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("batch,hd,heads,max_seq,layers", [(2, 128, (4, 2), 64, 2), (9, 64, (8, 2), 64, 2),
                                                            (1, 128, (8, 8), 64, 2), (2, 128, (4, 2), 1024, 1),
-                                                           (3, 128, (16, 8), 4096, 1), (1, 64, (8, 1), 2000, 1)])
+                                                           (3, 128, (16, 8), 4096, 1), (1, 64, (8, 1), 2000, 1),
+                                                           (16, 128, (4, 2), 64, 1)])
 def test_decode_step_matches_oracle(cuda, batch, hd, heads, max_seq, layers):
     """max_seq sets the attention's split count (the automatic rule at S_max =
     max_seq), so the larger cases combine many splits."""

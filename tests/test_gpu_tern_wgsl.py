@@ -142,19 +142,20 @@ def test_gemm_tern(cuda, M, N, K):
 
 
 def test_linear_router(cuda):
-    """linearQ's ternary branch: T <= 8 takes the GEMV (exact group sums), T > 8
-    quantizes (QUANTQ8T) and takes the GEMM; acc adds."""
+    """linearQ's ternary branch: T <= 16 takes a GEMV (exact group sums; the
+    tensor-core one at 2..16 rows), T > 16 quantizes (QUANTQ8T) and takes the GEMM;
+    acc adds."""
     N, K = 512, 2048
     _, pack, sc = _tern(77, N, K)
     rng = np.random.default_rng(77)
-    for T in (1, 5, 256):
+    for T in (1, 5, 12, 256):
         x = rng.normal(0, 1, (T, K)).astype(np.float32)
         y0 = rng.normal(0, 1, (T, N)).astype(np.float32)
         y = torch.from_numpy(y0.copy()).cuda()
         tb.linear_tern_wgsl(torch.from_numpy(x).cuda(), u32_dev(pack), u16_dev(sc), y=y, acc=True)
         xq, xs, _ = oracle.quant_q8(x)
         ref = oracle.gemv_tern_wgsl_q8act(xq, xs, pack, sc)
-        if T <= 8:
+        if T <= 16:
             assert row_rel_err(host(y) - y0, ref) < TOL
         else:
             rel, _ = _gemm_errs(host(y) - y0, ref, xq, xs, pack, sc)
