@@ -64,8 +64,6 @@ constexpr int ERR_MMA_WAIT = 0x6d03;
 __host__ __device__ constexpr int mm_wg(bool tern) { return tern ? 8 : 16; }
 // 128-byte boxes a stage row spans (16 groups): 2 (int4) or 1 (ternary)
 __host__ __device__ constexpr int mm_nbox(bool tern) { return tern ? 1 : 2; }
-// rows of one weight box: a 64-row item, or 32 rows of each of gate and up
-__host__ __device__ constexpr int mm_box_rows(bool gu) { return gu ? 32 : 64; }
 __host__ __device__ constexpr int mm_w_bytes(bool tern) { return mm_nbox(tern) * 64 * 128; }
 constexpr int MM_S_BYTES = 64 * MM_KS * 2;   // f16 scales of the stage's rows
 __host__ __device__ constexpr int mm_stage_bytes(bool tern, int ts)
@@ -92,9 +90,11 @@ struct MmArgs {
     MmMat m[3];
     int count;         // matrices (gate/up: m[0] gate, m[1] up, one unit = a tile of each)
     int units;         // tiles, or tile pairs for gate/up
+    int nu;            // units per work item (<= 8 tiles, <= 4 pairs): the boxes are 8 * nu rows
     int K, G, B, acc;
     const unsigned char* xa;   // [G][TS][32] activation slots
     const uint2* xk;           // [G][TS] {xs bits, kc}
+    int grid;          // CTAs: ceil(units / units per CTA)
     int* err;
 };
 
@@ -167,14 +167,14 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x,
                  : "memory");
 }
 
-// A work item: up to NU consecutive units of one matrix (gate/up: of the pair list)
+// A work item: up to a.nu consecutive units of one matrix (gate/up: of the pair list)
 struct MmItem {
     int ub, n, mi;
 };
 template <bool GU>
 __device__ __forceinline__ MmItem mm_item(const MmArgs& a, int u, int u1)
 {
-    constexpr int NU = GU ? MM_MAXT / 2 : MM_MAXT;
+    const int NU = a.nu;
     int mi = 0, end = u1;
     if (!GU) {
 #pragma unroll
@@ -188,7 +188,7 @@ template <bool TERN, bool GU, bool M16>
 __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constant__ MmArgs a)
 {
     constexpr int TS = M16 ? 16 : 8;
-    constexpr int WG = mm_wg(TERN), NBOX = mm_nbox(TERN), BR = mm_box_rows(GU), NM = GU ? 2 : 1;
+    constexpr int WG = mm_wg(TERN), NBOX = mm_nbox(TERN), NM = GU ? 2 : 1;
     constexpr int SB = mm_stage_bytes(TERN, TS);
     constexpr int W_BYTES = mm_w_bytes(TERN), A_BYTES = MM_KS * TS * 32;
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -199,6 +199,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int G = a.G;
     const int nks = (G + MM_KS - 1) / MM_KS;
+    const int BR = 8 * a.nu;              // rows of a weight / scale box (one item)
     const int u0 = (int)((long long)blockIdx.x * a.units / gridDim.x);
     const int u1 = (int)((long long)(blockIdx.x + 1) * a.units / gridDim.x);
     int nitems = 0;
@@ -395,8 +396,7 @@ int launch_mma(tb_ctx* ctx, const MmArgs& a)
     auto kern = k_gemv_mma<TERN, GU, M16>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    const int grid = std::min(a.units, ctx->num_sms);
-    e = tb_launch(ctx, kern, dim3(grid), dim3(MM_THREADS), (size_t)smem, a);
+    e = tb_launch(ctx, kern, dim3(a.grid), dim3(MM_THREADS), (size_t)smem, a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemv_mma launch: %s", cudaGetErrorString(e));
     return TB_OK;
 }
@@ -491,7 +491,18 @@ int tb_gemv_mma_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* c
     a.xk = xk;
     a.err = ctx->dev_error;
     int tiles = 0;
-    const int box_rows = mm_box_rows(gateup);
+    // the even split of the units over the grid, in items whose boxes (8 * nu rows)
+    // hold no row past the item: each CTA takes tpc units, in as few items of
+    // equal size as fit the stage (8 tiles; gate/up 4 pairs)
+    int units = 0;
+    for (int i = 0; i < count; i++) units += gateup ? 0 : (int)(Ns[i] / 8);
+    if (gateup) units = (int)(Ns[0] / 8);
+    const int maxnu = gateup ? MM_MAXT / 2 : MM_MAXT;
+    const int tpc = (units + ctx->num_sms - 1) / ctx->num_sms;
+    const int nitem = (tpc + maxnu - 1) / maxnu;
+    a.nu = (tpc + nitem - 1) / nitem;
+    a.grid = (units + tpc - 1) / tpc;
+    const int box_rows = 8 * a.nu;
     const int64_t wrow = tern ? K / 4 : K / 2;
     for (int i = 0; i < 3; i++) {
         if (i < count) {
