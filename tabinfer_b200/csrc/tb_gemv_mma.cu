@@ -38,12 +38,11 @@
 //    rows of a tile hit eight different bank groups.  The weight copies of the
 //    first stages are issued before griddepcontrol.wait, so they overlap the
 //    previous kernel.
-//  * The 8 warps split a stage's groups (warp w: groups 2w, 2w+1, one scale
-//    word per row for both); every warp covers all tiles of the item, with the
-//    two groups' A fragments in registers.  Tiles sit at fixed places of the
+//  * The 16 warps split a stage's 16 groups (warp w: group w); every warp
+//    covers all tiles of the item with its group's A fragment in registers.  Tiles sit at fixed places of the
 //    stage (gate/up: gate tiles 0-3, up tiles 4-7), so every shared address is
 //    the stage base plus a compile-time and a per-thread constant.
-//    At the item's end the 8 partial tiles meet in shared memory in warp order
+//    At the item's end the 16 partial tiles meet in shared memory in warp order
 //    (deterministic, independent of the grid) and the epilogue stores, adds
 //    the residual, or applies silu(gate) * up.
 #include <cuda.h>
@@ -52,7 +51,7 @@
 
 namespace {
 
-constexpr int MM_THREADS = 256, MM_WARPS = 8;
+constexpr int MM_THREADS = 512, MM_WARPS = 16;
 constexpr int MM_KS = 16;          // 32-groups per stage
 constexpr int MM_MAXT = 8;         // 8-row tiles per work item
 constexpr int MM_NST = 4;          // stages in the ring
@@ -98,14 +97,6 @@ struct MmArgs {
     int* err;
 };
 
-__device__ __forceinline__ void mma_s8u8(int* c, const uint32_t* a, uint32_t b0, uint32_t b1)
-{
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                 "{%0,%1,%2,%3};"
-                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 __device__ __forceinline__ float2 fmul2(float2 a, float2 b)
 {
     float2 d;
@@ -114,6 +105,60 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b)
         : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
     return d;
 }
+
+// d = a . b + c (c: the token rows' kc, so d is the biased sum; c and d are
+// separate register quads, so the seed is built once per group)
+__device__ __forceinline__ void mma_s8u8(int* d, const uint32_t* a, uint32_t b0, uint32_t b1, const int* c)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c[0]), "r"(c[1]), "r"(c[2]),
+          "r"(c[3]));
+}
+
+// One group of one stage for the first NT tiles of the item (gate/up: NT pairs,
+// gate tiles at slots 0..NT-1, up tiles at 4..4+NT-1): NT is a compile-time count,
+// so every tile's MMA runs unconditionally.
+template <bool TERN, bool GU, bool M16, int NT>
+__device__ __forceinline__ void mm_group(float2 (&acc)[MM_MAXT][2], const unsigned char* W, const uint16_t* S,
+                                         int BR, int wofs, int sh, int g, int t, int gl, const uint32_t* af,
+                                         const int* cq, float2 xslo, float2 xshi)
+{
+    constexpr int NBOX = mm_nbox(TERN);
+    constexpr uint32_t mask = TERN ? 0x03030303u : 0x0f0f0f0fu;
+    const float2 nmagic = make_float2(-MM_MAGIC_F, -MM_MAGIC_F);
+#pragma unroll
+    for (int i = 0; i < MM_MAXT; i++) {
+        if (GU ? (i & 3) < NT : i < NT) {
+            const int sm = GU ? (i >> 2) : 0;              // gate or up
+            const int rt = GU ? (i & 3) * 8 : i * 8;       // tile's first row within the box
+            const unsigned char* wb = W + sm * NBOX * BR * 128 + (rt + g) * 128 + wofs;
+            uint32_t b0, b1;
+            if (TERN) {
+                const uint2 v = *reinterpret_cast<const uint2*>(wb);
+                b0 = (v.x >> sh) & mask;
+                b1 = (v.y >> sh) & mask;
+            } else {
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(wb);
+                b0 = w & mask;
+                b1 = (w >> 4) & mask;
+            }
+            // f16 scales of rows rt + 2t, rt + 2t + 1
+            const uint16_t* sb = S + sm * BR * MM_KS + (rt + 2 * t) * MM_KS + gl;
+            const float2 ws = make_float2(tb_h2f(sb[0]), tb_h2f(sb[MM_KS]));
+            int d[4];
+            mma_s8u8(d, af, b0, b1, cq);
+            const float2 vlo = fadd2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), nmagic);
+            acc[i][0] = ffma2(vlo, fmul2(xslo, ws), acc[i][0]);
+            if (M16) {
+                const float2 vhi = fadd2(make_float2(__int_as_float(d[2]), __int_as_float(d[3])), nmagic);
+                acc[i][1] = ffma2(vhi, fmul2(xshi, ws), acc[i][1]);
+            }
+        }
+    }
+}
+
 
 // ---- activation quantizer ---------------------------------------------------
 // One 256-thread CTA per (token slot, group range); token slots >= B are zero
@@ -258,14 +303,12 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
         }
     }
 
-    const uint32_t mask = TERN ? 0x03030303u : 0x0f0f0f0fu;
-    const float2 nmagic = make_float2(-MM_MAGIC_F, -MM_MAGIC_F);
-    // this warp's two groups of every stage (gl0, gl0 + 1) and this thread's byte
-    // offsets of its weight words of each within a box row (row & 7 == g: the
-    // 128-byte swizzle puts chunk c of the row at c ^ g)
-    const int gl0 = 2 * warp;
-    const int wofs0 = TERN ? (((gl0 >> 1) ^ g) << 4) : (gl0 >> 3) * BR * 128 + (((gl0 & 7) ^ g) << 4) + 4 * t;
-    const int wofs1 = TERN ? wofs0 : (gl0 >> 3) * BR * 128 + ((((gl0 & 7) + 1) ^ g) << 4) + 4 * t;
+    // this warp's group of every stage and this thread's byte offset of its weight
+    // word(s) within a box row (row & 7 == g: the 128-byte swizzle puts chunk c of
+    // the row at c ^ g)
+    const int gl = warp;
+    const int wofs = TERN ? ((((gl >> 1) ^ g) << 4) + (gl & 1) * 8)
+                          : (gl >> 3) * BR * 128 + (((gl & 7) ^ g) << 4) + 4 * t;
     const int sh = TERN ? 2 * t : 0;
 
     float2 acc[MM_MAXT][2];
@@ -279,66 +322,34 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
             for (int i = 0; i < MM_MAXT; i++) acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
         }
         const bool ok = mbar_wait(&full[slot], (uint32_t)((it / MM_NST) & 1));
-        if (ok && gl0 < kg) {
+        if (ok && gl < kg) {
             const unsigned char* W = stages + slot * SB;
             const uint16_t* S = reinterpret_cast<const uint16_t*>(W + W_BYTES);
             const unsigned char* A = W + W_BYTES + MM_S_BYTES;
             const uint2* X = reinterpret_cast<const uint2*>(A + A_BYTES);
-            uint32_t af[2][4];
-            int kclo[2], kchi[2];
-            float2 xslo[2], xshi[2];
-#pragma unroll
-            for (int q = 0; q < 2; q++) {
-                const int gl = gl0 + q;
-                const uint2 alo = *reinterpret_cast<const uint2*>(A + (gl * TS + g) * 32 + 8 * t);
-                const uint2 xlo = X[gl * TS + g];
-                uint2 ahi = make_uint2(0u, 0u), xhi = make_uint2(0u, MM_MAGIC);
-                if (M16) {
-                    ahi = *reinterpret_cast<const uint2*>(A + (gl * TS + g + 8) * 32 + 8 * t);
-                    xhi = X[gl * TS + g + 8];
-                }
-                af[q][0] = alo.x; af[q][1] = ahi.x; af[q][2] = alo.y; af[q][3] = ahi.y;
-                kclo[q] = (int)xlo.y;
-                kchi[q] = (int)xhi.y;
-                xslo[q] = make_float2(__uint_as_float(xlo.x), __uint_as_float(xlo.x));
-                xshi[q] = make_float2(__uint_as_float(xhi.x), __uint_as_float(xhi.x));
+            const uint2 alo = *reinterpret_cast<const uint2*>(A + (gl * TS + g) * 32 + 8 * t);
+            const uint2 xlo = X[gl * TS + g];
+            uint2 ahi = make_uint2(0u, 0u), xhi = make_uint2(0u, MM_MAGIC);
+            if (M16) {
+                ahi = *reinterpret_cast<const uint2*>(A + (gl * TS + g + 8) * 32 + 8 * t);
+                xhi = X[gl * TS + g + 8];
             }
-#pragma unroll
-            for (int i = 0; i < MM_MAXT; i++) {
-                if (GU ? (i & 3) < ci.n : i < ci.n) {
-                    const int sm = GU ? (i >> 2) : 0;              // gate or up
-                    const int rt = GU ? (i & 3) * 8 : i * 8;       // tile's first row within the box
-                    const unsigned char* wb = W + sm * NBOX * BR * 128 + (rt + g) * 128;
-                    // f16 scales of rows rt + 2t, rt + 2t + 1 at both groups (one word each)
-                    const uint16_t* sb = S + sm * BR * MM_KS + (rt + 2 * t) * MM_KS + gl0;
-                    const uint32_t sp0 = *reinterpret_cast<const uint32_t*>(sb);
-                    const uint32_t sp1 = *reinterpret_cast<const uint32_t*>(sb + MM_KS);
-                    uint32_t bw[2][2];
-                    if (TERN) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(wb + wofs0);   // both groups' words
-                        bw[0][0] = (v.x >> sh) & mask; bw[0][1] = (v.y >> sh) & mask;
-                        bw[1][0] = (v.z >> sh) & mask; bw[1][1] = (v.w >> sh) & mask;
-                    } else {
-                        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(wb + wofs0);
-                        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(wb + wofs1);
-                        bw[0][0] = w0 & mask; bw[0][1] = (w0 >> 4) & mask;
-                        bw[1][0] = w1 & mask; bw[1][1] = (w1 >> 4) & mask;
-                    }
-#pragma unroll
-                    for (int q = 0; q < 2; q++) {
-                        int c[4] = {kclo[q], kclo[q], kchi[q], kchi[q]};
-                        mma_s8u8(c, af[q], bw[q][0], bw[q][1]);
-                        const float2 ws = make_float2(tb_h2f((uint16_t)(q ? sp0 >> 16 : sp0 & 0xffffu)),
-                                                      tb_h2f((uint16_t)(q ? sp1 >> 16 : sp1 & 0xffffu)));
-                        const float2 vlo = fadd2(make_float2(__int_as_float(c[0]), __int_as_float(c[1])), nmagic);
-                        acc[i][0] = ffma2(vlo, fmul2(xslo[q], ws), acc[i][0]);
-                        if (M16) {
-                            const float2 vhi = fadd2(make_float2(__int_as_float(c[2]), __int_as_float(c[3])), nmagic);
-                            acc[i][1] = ffma2(vhi, fmul2(xshi[q], ws), acc[i][1]);
-                        }
-                    }
-                }
+            const uint32_t af[4] = {alo.x, ahi.x, alo.y, ahi.y};
+            const int cq[4] = {(int)xlo.y, (int)xlo.y, (int)xhi.y, (int)xhi.y};
+            const float2 xslo = make_float2(__uint_as_float(xlo.x), __uint_as_float(xlo.x));
+            const float2 xshi = make_float2(__uint_as_float(xhi.x), __uint_as_float(xhi.x));
+#define MM_GROUP(N) mm_group<TERN, GU, M16, N>(acc, W, S, BR, wofs, sh, g, t, gl, af, cq, xslo, xshi)
+            switch (ci.n) {   // warp-uniform: one branch a group
+            case 1: MM_GROUP(1); break;
+            case 2: MM_GROUP(2); break;
+            case 3: MM_GROUP(3); break;
+            case 4: MM_GROUP(4); break;
+            case 5: if (!GU) MM_GROUP(5); break;
+            case 6: if (!GU) MM_GROUP(6); break;
+            case 7: if (!GU) MM_GROUP(7); break;
+            default: if (!GU) MM_GROUP(8); break;
             }
+#undef MM_GROUP
         }
         const bool last = cks == nks - 1;
         if (last && ok) {
@@ -355,6 +366,12 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
             if (tid == 0 && a.err) atomicExch(a.err, ERR_MMA_WAIT);
             for (int j = it; j < min(total, it + MM_NST); j++) mbar_wait(&full[j % MM_NST], (uint32_t)((j / MM_NST) & 1));
             return;
+        }
+        // every warp is past stage it: refill its slot with stage it + NST before the
+        // item's epilogue, so the stream does not pause at item ends
+        if (tid == 0 && it + MM_NST < total) {
+            issue(it + MM_NST, pi, pks, true, true);
+            if (++pks == nks) { pks = 0; pi = mm_item<GU>(a, pi.ub + pi.n, u1); }
         }
         if (last) {
             const int nout = ci.n * 128;
@@ -380,11 +397,6 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
             __syncthreads();   // red is rewritten by the next item
         }
         if (++cks == nks) { cks = 0; ci = mm_item<GU>(a, ci.ub + ci.n, u1); }
-        // the slot is free: refill it with stage it + NST
-        if (tid == 0 && it + MM_NST < total) {
-            issue(it + MM_NST, pi, pks, true, true);
-            if (++pks == nks) { pks = 0; pi = mm_item<GU>(a, pi.ub + pi.n, u1); }
-        }
     }
 }
 
