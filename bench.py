@@ -1214,9 +1214,10 @@ def profile_gemm_dp4(M, N, K):
 
 
 def profile_lm_head(kind):
-    """Three cold-L2 batch-1 lm_head GEMVs (151936 x 2048, RMSNorm fused) of one
-    weight kind -- int4_f32 (gemvQ), int4_dp4a (rmsnormQ + gemvDP4) or tern
-    (ternary WebGPU layout) -- for an ncu capture of one."""
+    """Three cold-L2 lm_head GEMVs (151936 x 2048, RMSNorm fused) of one weight
+    kind -- int4_f32 (gemvQ, batch 1), int4_dp4a (rmsnormQ + gemvDP4, batch 1),
+    tern (ternary WebGPU layout, batch 1) or int4_mma16 (16 rows on the tensor
+    cores: one quantization launch, then the GEMV) -- for an ncu capture of one."""
     import torch
     import tabinfer_b200 as tb
     dev = torch.device("cuda", 0)
@@ -1229,8 +1230,9 @@ def profile_lm_head(kind):
         pack, sc = tb.quantize_int4_bf16(w.view(torch.int16))
         del w
     nw = (1 + 0.1 * torch.randn(K, device=dev, generator=g)).half().view(torch.int16)
-    x = torch.randn(1, K, device=dev, generator=g)
-    y = torch.empty(1, N, device=dev)
+    B = 16 if kind == "int4_mma16" else 1
+    x = torch.randn(B, K, device=dev, generator=g)
+    y = torch.empty(B, N, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for it in range(3):
         flush.fill_(it)
@@ -1238,6 +1240,8 @@ def profile_lm_head(kind):
             tb.gemv_q_norm(x, nw, 1e-6, pack, sc, y=y)
         elif kind == "int4_dp4a":
             tb.gemv_dp4a(x, pack, sc, norm_w=nw, y=y)
+        elif kind == "int4_mma16":
+            tb.gemv_mma(x, pack, sc, norm_w=nw, y=y)
         else:
             tb.gemv_tern_wgsl_dp4a_multi(x, [(pack, sc)], norm_w=nw, ys=[y])
     torch.cuda.synchronize()
@@ -1415,7 +1419,7 @@ def main():
                     help="three cold-L2 prefill-attention launches at T = S tokens (for ncu), then exit")
     ap.add_argument("--profile-gemm-dp4", type=int, nargs=3, default=None, metavar=("M", "N", "K"),
                     help="three cold-L2 exact-sum prefill GEMM launches (for ncu), then exit")
-    ap.add_argument("--profile-lm-head", default=None, choices=("int4_f32", "int4_dp4a", "tern"),
+    ap.add_argument("--profile-lm-head", default=None, choices=("int4_f32", "int4_dp4a", "tern", "int4_mma16"),
                     help="three cold-L2 batch-1 lm_head GEMVs of one weight kind (for ncu), then exit")
     ap.add_argument("--step-mode", default="auto", choices=("auto", "kernels", "persistent"),
                     help="decode step as one persistent kernel (auto: where it applies) or one kernel per op")
