@@ -1383,7 +1383,7 @@ def run_only(name, steps):
     elif name == "decode":
         stream = torch.cuda.current_stream(dev)     # the stream main() times the model steps on
         out = {"batch%d_context%d" % (B, S): decode_extra(dev, stream, B, S)
-               for B, S in ((16, 4096), (4, 4096), (8, 4096))}
+               for B, S in ((16, 4096), (4, 4096), (8, 4096), (1, 32768))}
     elif name == "chain":
         out = {}
         for B in (1, 4, 8):

@@ -88,8 +88,10 @@ __global__ void __launch_bounds__(256) k_kv_quant_write(const float* __restrict_
 
 // hd fixed at compile time (64 or 128); GRP = q heads per kv head.  One CTA
 // (W warps) per (kv head, split); the split's work is DecUnit (tb_attn_dev.cuh).
+// 4-warp single-stage units of up to 2 q heads run five CTAs an SM (shared memory
+// allows five): registers are held to that (wider groups would spill).
 template <int HD, int GRP, bool EARLY, int W, int NST>
-__global__ void __launch_bounds__(32 * W) k_attn_decode(const AttnArgs a)
+__global__ void __launch_bounds__(32 * W, (W == 4 && NST == 1 && GRP <= 2) ? 5 : 1) k_attn_decode(const AttnArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     if constexpr (EARLY) {

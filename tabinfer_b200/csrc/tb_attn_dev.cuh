@@ -158,6 +158,9 @@ struct DecLayout {
     static constexpr int OFF_WM = OFF_PS + W * 32 * NG * GRP * 4;   // float [W][GRP]
     static constexpr int OFF_WL = OFF_WM + W * GRP * 4;       // float [W][GRP]
     static constexpr int OFF_ST = (OFF_WL + W * GRP * 4 + 127) / 128 * 128;
+    // q's four int8 digits [GRP][4][HD] replace q itself (OFF_QS) once it is split, and
+    // their steps [GRP][NG] sit in the merge scratch (OFF_WM, unused until the merge)
+    static_assert(GRP * 4 * HD <= GRP * HD * 4 && GRP * NG <= 2 * W * GRP, "q digits must fit");
     static constexpr int BYTES = OFF_ST + W * NST * STAGE;
     // after the key loop the stages are reused for the warps' outputs, float [W][GRP][HD]
     static_assert(W * GRP * HD * 4 <= W * NST * STAGE, "merge buffer must fit in the stages");
@@ -373,6 +376,59 @@ struct DecUnit {
             unit_sync(bar, NT);
         }
 
+        // ---- q as four int8 digits per (head, 32-group): q = sc (d1 + d2/128 + d3/128^2 +
+        // d4/128^3), sc = max|q|/127, each digit the rounded residual (below f32 rounding).
+        // The scores then run on the tensor cores with K as the raw int8 operand.
+        constexpr int NN8 = (GRP * 4 + 7) / 8;            // 8-column tiles of (head, digit)
+        uint32_t qb[NN8][NG][2];                          // B fragments: column g, dims 4t.. / 16+4t..
+        float qst[NN8][NG][2];                            // digit steps of this thread's two columns
+        {
+            int8_t* qd = reinterpret_cast<int8_t*>(smem + L::OFF_QS);   // overwrites q
+            float* qsc = wm;
+            constexpr int PPW = (GRP * NG + W - 1) / W;                  // (head, group) pairs a warp
+            float qv[PPW];
+#pragma unroll
+            for (int i = 0; i < PPW; i++) {
+                const int pr = wid + i * W;
+                qv[i] = pr < GRP * NG ? qs[(pr / NG) * HD + 32 * (pr % NG) + lane] : 0.0f;
+            }
+            unit_sync(bar, NT);          // every q value is in registers: q's area takes the digits
+#pragma unroll
+            for (int i = 0; i < PPW; i++) {
+                const int pr = wid + i * W;
+                if (pr >= GRP * NG) break;
+                const int h = pr / NG, G = pr - h * NG;
+                float r = qv[i];
+                float stp = q8_scale(warp_max(fabsf(r))), istp = q8_inv(stp);
+                if (lane == 0) qsc[h * NG + G] = stp;
+#pragma unroll
+                for (int d = 0; d < 4; d++) {
+                    const int q = max(-127, min(127, __float2int_rn(__fmul_rn(r, istp))));
+                    r = __fsub_rn(r, __fmul_rn(stp, (float)q));
+                    qd[(h * 4 + d) * HD + 32 * G + lane] = (int8_t)q;
+                    stp = __fmul_rn(stp, 0.0078125f);
+                    istp = __fmul_rn(istp, 128.0f);
+                }
+            }
+            unit_sync(bar, NT);
+            const int g8 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+            for (int nt = 0; nt < NN8; nt++) {
+                const int hb = (8 * nt + g8) >> 2, db = (8 * nt + g8) & 3;     // this thread's B column
+                const int hc = 2 * nt + (t4 >> 1);                              // its D columns' head
+#pragma unroll
+                for (int G = 0; G < NG; G++) {
+                    const int8_t* src = qd + (hb * 4 + db) * HD + 32 * G + 4 * t4;
+                    qb[nt][G][0] = hb < GRP ? *reinterpret_cast<const uint32_t*>(src) : 0u;
+                    qb[nt][G][1] = hb < GRP ? *reinterpret_cast<const uint32_t*>(src + 16) : 0u;
+                    const float sc = hc < GRP ? qsc[hc * NG + G] : 0.0f;
+                    // digits 2(t&1) and 2(t&1)+1: sc / 128^d (exact power-of-two steps)
+                    qst[nt][G][0] = (t4 & 1) ? __fmul_rn(sc, 1.0f / 16384.0f) : sc;
+                    qst[nt][G][1] = (t4 & 1) ? __fmul_rn(sc, 1.0f / 2097152.0f) : __fmul_rn(sc, 0.0078125f);
+                }
+            }
+        }
+
         float m[GRP], l[GRP];
         float2 o[GRP][DPL / 2];
 #pragma unroll
@@ -393,39 +449,69 @@ struct DecUnit {
             const bool valid = t0 + lane < c1;
             const int nk = min(32, c1 - t0);
 
-            // ---- scores: lane = key
+            // ---- scores on the tensor cores: D[key][(head, digit)] = sum_32 K * digit per
+            // group (mma m16n8k32, K the int8 A operand straight from the swizzled tile,
+            // seeded with 2^23 + 2^22 so the int32 sum converts exactly), scaled by the
+            // digit steps and the key's group scale; the two digit pairs of a head meet by
+            // one shuffle, and lane = key picks its scores up from shared memory
             float s[GRP];
+            {
+                const int g8 = lane >> 2, t4 = lane & 3;
+                const uint8_t* kb = st + L::ST_K;
+                const float* ksd = reinterpret_cast<const float*>(st + L::ST_KS);
+                float part[2][NN8][2];
 #pragma unroll
-            for (int h = 0; h < GRP; h++) s[h] = 0.0f;
-            if (valid) {
-                const uint4* kd = reinterpret_cast<const uint4*>(st + L::ST_K) + lane * KV16;
-                const float* ksd = reinterpret_cast<const float*>(st + L::ST_KS) + lane * NG;
+                for (int mt = 0; mt < 2; mt++)
 #pragma unroll
-                for (int g = 0; g < NG; g++) {
-                    float2 acc[GRP];
+                    for (int nt = 0; nt < NN8; nt++) part[mt][nt][0] = part[mt][nt][1] = 0.0f;
 #pragma unroll
-                    for (int h = 0; h < GRP; h++) acc[h] = make_float2(0.0f, 0.0f);
+                for (int G = 0; G < NG; G++) {
 #pragma unroll
-                    for (int i2 = 0; i2 < 2; i2++) {
-                        const int i = g * 2 + i2;
-                        const uint4 w4 = kd[i ^ (lane & (KV16 - 1))];
-                        const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+                    for (int mt = 0; mt < 2; mt++) {
+                        const int k0 = 16 * mt + g8, k1 = k0 + 8;
+                        const int c0 = 2 * G, c1 = 2 * G + 1;
+                        uint32_t af[4];
+                        af[0] = *reinterpret_cast<const uint32_t*>(kb + k0 * HD + ((c0 ^ (k0 & (KV16 - 1))) << 4) + 4 * t4);
+                        af[1] = *reinterpret_cast<const uint32_t*>(kb + k1 * HD + ((c0 ^ (k1 & (KV16 - 1))) << 4) + 4 * t4);
+                        af[2] = *reinterpret_cast<const uint32_t*>(kb + k0 * HD + ((c1 ^ (k0 & (KV16 - 1))) << 4) + 4 * t4);
+                        af[3] = *reinterpret_cast<const uint32_t*>(kb + k1 * HD + ((c1 ^ (k1 & (KV16 - 1))) << 4) + 4 * t4);
+                        const float ks0 = ksd[k0 * NG + G], ks1 = ksd[k1 * NG + G];
 #pragma unroll
-                        for (int wq = 0; wq < 4; wq++) {
-                            const float2 k01 = sbytes_f2(ww[wq], 0), k23 = sbytes_f2(ww[wq], 1);
-                            const int d = i * 16 + wq * 4;
-#pragma unroll
-                            for (int h = 0; h < GRP; h++) {
-                                const float4 q4 = *reinterpret_cast<const float4*>(qs + h * HD + d);
-                                acc[h] = ffma2(make_float2(q4.x, q4.y), k01, acc[h]);
-                                acc[h] = ffma2(make_float2(q4.z, q4.w), k23, acc[h]);
-                            }
+                        for (int nt = 0; nt < NN8; nt++) {
+                            int dd[4];
+                            asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+                                "{%8,%9}, {%10,%10,%10,%10};"
+                                : "=r"(dd[0]), "=r"(dd[1]), "=r"(dd[2]), "=r"(dd[3])
+                                : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(qb[nt][G][0]),
+                                  "r"(qb[nt][G][1]), "r"(0x4B400000));
+                            const float2 v0 = fadd2(make_float2(__int_as_float(dd[0]), __int_as_float(dd[1])),
+                                                    make_float2(-12582912.0f, -12582912.0f));
+                            const float2 v1 = fadd2(make_float2(__int_as_float(dd[2]), __int_as_float(dd[3])),
+                                                    make_float2(-12582912.0f, -12582912.0f));
+                            const float w0 = fmaf(v0.y, qst[nt][G][1], v0.x * qst[nt][G][0]);
+                            const float w1 = fmaf(v1.y, qst[nt][G][1], v1.x * qst[nt][G][0]);
+                            part[mt][nt][0] = fmaf(ks0, w0, part[mt][nt][0]);
+                            part[mt][nt][1] = fmaf(ks1, w1, part[mt][nt][1]);
                         }
                     }
-                    const float ksc = ksd[g];
-#pragma unroll
-                    for (int h = 0; h < GRP; h++) s[h] = fmaf(acc[h].x + acc[h].y, ksc, s[h]);
                 }
+                float* scs = ps;      // [32 keys][GRP] scores, before ps holds the V weights
+#pragma unroll
+                for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+                    for (int nt = 0; nt < NN8; nt++) {
+                        const float p0 = part[mt][nt][0] + __shfl_xor_sync(0xffffffffu, part[mt][nt][0], 1);
+                        const float p1 = part[mt][nt][1] + __shfl_xor_sync(0xffffffffu, part[mt][nt][1], 1);
+                        const int h = 2 * nt + (t4 >> 1);
+                        if ((t4 & 1) == 0 && h < GRP) {
+                            scs[(16 * mt + g8) * GRP + h] = p0;
+                            scs[(16 * mt + g8 + 8) * GRP + h] = p1;
+                        }
+                    }
+                __syncwarp();
+#pragma unroll
+                for (int h = 0; h < GRP; h++) s[h] = scs[lane * GRP + h];
+                __syncwarp();         // ps is rewritten below
             }
             // ---- online softmax (per lane partial l; m warp-uniform)
             float pr[GRP];
