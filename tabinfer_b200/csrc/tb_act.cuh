@@ -146,3 +146,43 @@ __device__ __forceinline__ uint32_t js_f32_to_f16(float val)
     }
     return sign | ((((uint32_t)e << 10) | (mant >> 13)) + ((mant >> 12) & 1u));
 }
+
+// ---- fragment-order activation of the tensor-core GEMVs (tb_gemv_mma.cu) ----
+// Per 32-group and row slot, 32 bytes holding the k-slots t and 4+t of MMA thread
+// t side by side: int4 slot i = k 8i+{0,2,4,6} (the low nibbles of word i), slot
+// 4+i = k 8i+{1,3,5,7}; ternary slot s = k 4s..4s+3.  Beside it per (group, row)
+// {scale bits, kc}, kc = 2^23 + 2^22 - F * sum(q) (F = 8 int4, 1 ternary): the
+// accumulator seed that removes the weights' bias and converts the sum exactly.
+constexpr uint32_t MMA_KC_MAGIC = 0x4B400000u;
+__device__ __forceinline__ int mma_slot_pos(int k, bool tern)
+{
+    const int slot = tern ? (k >> 2) : ((k >> 3) + 4 * (k & 1));
+    const int byte = tern ? (k & 3) : ((k & 7) >> 1);
+    return 8 * (slot & 3) + 4 * (slot >> 2) + byte;
+}
+// QUANTQ8 of one 32-group held by 8 consecutive lanes (lane & 7 = j4 holds elements
+// 4 j4 .. 4 j4 + 3; every lane of the warp calls it), stored in fragment order at row
+// slot m of group g: the same int8 values and scale as q8_group on the elements.
+__device__ __forceinline__ void mma_store_group4(const float e[4], int g, int m, int ts, bool tern,
+                                                 unsigned char* xa, uint2* xk)
+{
+    float mx = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    const float scale = q8_scale(mx), is = q8_inv(scale);
+    const int j4 = threadIdx.x & 7;
+    unsigned char* row = xa + ((size_t)g * ts + m) * 32;
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int q = q8_quant(e[i], is);
+        sum += q;
+        row[mma_slot_pos(4 * j4 + i, tern)] = (unsigned char)(q & 0xff);
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (j4 == 0) xk[(size_t)g * ts + m] = make_uint2(__float_as_uint(scale), MMA_KC_MAGIC - (tern ? 1u : 8u) * (uint32_t)sum);
+}
+

@@ -186,11 +186,20 @@ int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv)
 int tb_attn_decode_impl(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
                         const int8_t* Vq, const float* Vs, int64_t S, int64_t nHq, int64_t nKv, int64_t hd,
                         int nsplit, float* PO, float* PML, unsigned* counters, int64_t batch,
-                        int64_t cache_rows, const int32_t* dpos, bool early)
+                        int64_t cache_rows, const int32_t* dpos, bool early, unsigned char* mxa, uint2* mxk,
+                        int mts, bool mtern)
 {
     AttnArgs a{qr, Kq, Ks, Vq, Vs, PO, PML, out, counters, (const int*)dpos, ctx->dev_error,
                (long long)(cache_rows > 0 ? cache_rows : S), (int)S, (int)nHq, (int)nKv, nsplit};
     a.grid_z = (int)batch;
+    if (mxa) {
+        TB_REQUIRE(ctx, mxk && batch <= mts && ((nHq / nKv) * hd) % 128 == 0,
+                   "attention: a fragment-order output needs its row slots and whole warps of groups");
+        a.mxa = mxa;
+        a.mxk = mxk;
+        a.mts = mts;
+        a.mtern = mtern ? 1 : 0;
+    }
     return early ? decode_dispatch<true>(ctx, a, hd, (int)(nHq / nKv))
                  : decode_dispatch<false>(ctx, a, hd, (int)(nHq / nKv));
 }

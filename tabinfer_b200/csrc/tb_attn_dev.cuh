@@ -124,6 +124,11 @@ struct AttnArgs {
     long long cache_rows;  // rows of each sequence's cache
     int S, nHq, nKv, nsplit;
     int grid_z;            // sequences
+    // optional: the heads' outputs also QUANTQ8'd in the tensor-core GEMVs' fragment
+    // order (row slot = sequence, ts slots), for the o projection that follows
+    unsigned char* mxa;
+    uint2* mxk;
+    int mts, mtern;
 };
 
 // ---- cp.async (16-byte and 8-byte global -> shared copies, per thread) -----
@@ -213,6 +218,8 @@ struct DecUnit {
     unsigned char* qout = nullptr;
     int qG = 0;
     bool qnat = false;                  // qout in the ternary GEMVs' natural-order layout
+    // the multi-kernel batched step: the outputs also in the tensor-core GEMVs' fragment
+    // order (a.mxa; groups of 8 lanes, so GRP * HD / 4 is a multiple of 32)
     unsigned long long* tr = nullptr;   // optional %globaltimer stamps of the unit's stages (8 slots)
 
     __device__ void ts(int k) const
@@ -599,14 +606,16 @@ struct DecUnit {
             }
         }
         if (a.nsplit == 1) {
-            if (qout) {     // the heads' outputs, written above by this unit, QUANTQ8'd
+            if (qout || a.mxa) {     // the heads' outputs, written above by this unit, QUANTQ8'd
                 unit_sync(bar, NT);
                 constexpr int NC = GRP * HD / 4;
                 for (int col = tid; col < NC; col += NT) {
                     const int h = col / (HD / 4), c4 = col - h * (HD / 4);
                     const float4 r = __ldcg(reinterpret_cast<const float4*>(outp + (long long)(hk * GRP + h) * HD) + c4);
                     const float e4[4] = {r.x, r.y, r.z, r.w};
-                    q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG, qnat);
+                    const int gq = ((hk * GRP + h) * (HD / 4) + c4) >> 3;
+                    if (qout) q8_store_group4(e4, gq, true, qout, qG, qnat);
+                    else mma_store_group4(e4, gq, zb, a.mts, a.mtern != 0, a.mxa, a.mxk);
                 }
             }
             return;
@@ -715,9 +724,11 @@ struct DecUnit {
             const float4 res = Ls > 0.0f ? make_float4(O.x / Ls, O.y / Ls, O.z / Ls, O.w / Ls)
                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             reinterpret_cast<float4*>(outp + (long long)(hk * GRP + h) * HD)[c4] = res;
-            if (qout) {     // 8 consecutive columns = one 32-group, 8 consecutive lanes
+            if (qout || a.mxa) {     // 8 consecutive columns = one 32-group, 8 consecutive lanes
                 const float e4[4] = {res.x, res.y, res.z, res.w};
-                q8_store_group4(e4, ((hk * GRP + h) * (HD / 4) + c4) >> 3, true, qout, qG, qnat);
+                const int gq = ((hk * GRP + h) * (HD / 4) + c4) >> 3;
+                if (qout) q8_store_group4(e4, gq, true, qout, qG, qnat);
+                else mma_store_group4(e4, gq, zb, a.mts, a.mtern != 0, a.mxa, a.mxk);
             }
         }
         if (tid == 0) *counter = 0u;     // ready for the next call

@@ -48,6 +48,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include "tb_gemv_dev.cuh"
+#include "tb_internal.h"
 
 namespace {
 
@@ -55,7 +56,7 @@ constexpr int MM_THREADS = 512, MM_WARPS = 16;
 constexpr int MM_KS = 16;          // 32-groups per stage
 constexpr int MM_MAXT = 8;         // 8-row tiles per work item
 constexpr int MM_NST = 4;          // stages in the ring
-constexpr uint32_t MM_MAGIC = 0x4B400000u;   // bits of 12582912.0f = 2^23 + 2^22
+constexpr uint32_t MM_MAGIC = MMA_KC_MAGIC;   // bits of 12582912.0f = 2^23 + 2^22
 constexpr float MM_MAGIC_F = 12582912.0f;
 constexpr int ERR_MMA_WAIT = 0x6d03;
 
@@ -90,9 +91,15 @@ struct MmArgs {
     int count;         // matrices (gate/up: m[0] gate, m[1] up, one unit = a tile of each)
     int units;         // tiles, or tile pairs for gate/up
     int nu;            // units per work item (<= 8 tiles, <= 4 pairs): the boxes are 8 * nu rows
+    int ualign;        // a CTA's unit range starts on a multiple of this (4 pairs: one swi group)
     int K, G, B, acc;
     const unsigned char* xa;   // [G][TS][32] activation slots
     const uint2* xk;           // [G][TS] {xs bits, kc}
+    // gate/up only: swi written QUANTQ8'd in the same fragment order for the next
+    // GEMV ([I/32][TS][32] + [I/32][TS]; items are whole 32-row groups), instead of f32
+    unsigned char* oxa;
+    uint2* oxk;
+    int otern;                 // the next GEMV's weights are ternary (natural k order, kc factor 1)
     int grid;          // CTAs: ceil(units / units per CTA)
     int* err;
 };
@@ -115,6 +122,20 @@ __device__ __forceinline__ void mma_s8u8(int* d, const uint32_t* a, uint32_t b0,
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c[0]), "r"(c[1]), "r"(c[2]),
           "r"(c[3]));
+}
+
+// QUANTQ8 of one 32-group held one element per lane (the whole warp), stored in
+// fragment order at row slot m of group g
+__device__ __forceinline__ void mm_store_group(float v, int g, int m, int ts, bool tern, unsigned char* xa,
+                                               uint2* xk)
+{
+    const int lane = threadIdx.x & 31;
+    const Q8Group qg = q8_group(v);
+    int sum = qg.q;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    xa[((size_t)g * ts + m) * 32 + mma_slot_pos(lane, tern)] = (unsigned char)(qg.q & 0xff);
+    if (lane == 0) xk[(size_t)g * ts + m] = make_uint2(__float_as_uint(qg.scale), MM_MAGIC - (tern ? 1u : 8u) * (uint32_t)sum);
 }
 
 // One group of one stage for the first NT tiles of the item (gate/up: NT pairs,
@@ -176,11 +197,6 @@ __global__ void __launch_bounds__(256) k_quant_mma(const float* __restrict__ x, 
     const int b = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int G = K >> 5;
     const int g0 = (int)((long long)blockIdx.y * G / gridDim.y), g1 = (int)((long long)(blockIdx.y + 1) * G / gridDim.y);
-    // this lane's byte within the group's 32 fragment-ordered bytes
-    int slot, byte;
-    if (TERN) { slot = lane >> 2; byte = lane & 3; }
-    else { slot = (lane >> 3) + 4 * (lane & 1); byte = (lane & 7) >> 1; }
-    const int pos = 8 * (slot & 3) + 4 * (slot >> 2) + byte;
     if (b >= B) {
         for (int g = g0 + wid; g < g1; g += 8) {
             xa[((size_t)g * ts + b) * 32 + lane] = 0;
@@ -195,12 +211,7 @@ __global__ void __launch_bounds__(256) k_quant_mma(const float* __restrict__ x, 
         const int k = g * 32 + lane;
         float v = xr[k];
         if (w16) v = __fmul_rn(__fmul_rn(v, inv), tb_h2f(w16[k]));
-        const Q8Group qg = q8_group(v);
-        int s = qg.q;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        xa[((size_t)g * ts + b) * 32 + pos] = (unsigned char)(qg.q & 0xff);
-        if (lane == 0) xk[(size_t)g * ts + b] = make_uint2(__float_as_uint(qg.scale), MM_MAGIC - (TERN ? 1u : 8u) * (uint32_t)s);
+        mm_store_group(v, g, b, ts, TERN, xa, xk);
     }
 }
 
@@ -238,6 +249,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
     constexpr int W_BYTES = mm_w_bytes(TERN), A_BYTES = MM_KS * TS * 32;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[MM_NST];
+    __shared__ float swq[GU ? 16 * 33 : 1];      // gate/up with a quantized output: one group of swi
     unsigned char* stages = smem_raw + ((1024 - (saddr(smem_raw) & 1023)) & 1023);
     float* red = reinterpret_cast<float*>(stages + MM_NST * SB);
 
@@ -245,8 +257,9 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
     const int G = a.G;
     const int nks = (G + MM_KS - 1) / MM_KS;
     const int BR = 8 * a.nu;              // rows of a weight / scale box (one item)
-    const int u0 = (int)((long long)blockIdx.x * a.units / gridDim.x);
-    const int u1 = (int)((long long)(blockIdx.x + 1) * a.units / gridDim.x);
+    const int nq = a.units / a.ualign;
+    const int u0 = (int)((long long)blockIdx.x * nq / gridDim.x) * a.ualign;
+    const int u1 = blockIdx.x + 1 == (int)gridDim.x ? a.units : (int)((long long)(blockIdx.x + 1) * nq / gridDim.x) * a.ualign;
     int nitems = 0;
     for (int u = u0; u < u1; nitems++) u += mm_item<GU>(a, u, u1).n;
     const int total = nitems * nks;
@@ -386,8 +399,9 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
                     float u = red[((i + 4) * 32 + l) * 4 + e];          // up tiles sit at slots 4..7
 #pragma unroll
                     for (int w = 1; w < MM_WARPS; w++) u += red[((w * MM_MAXT + i + 4) * 32 + l) * 4 + e];
-                    const int row = (ci.ub + i) * 8 + col;
-                    a.m[0].y[(size_t)m * a.m[0].N + row] = __fdiv_rn(v, 1.0f + expf(-v)) * u;
+                    const float sw = __fdiv_rn(v, 1.0f + expf(-v)) * u;
+                    if (a.oxa) swq[m * 33 + i * 8 + col] = sw;           // the item is one 32-row group
+                    else a.m[0].y[(size_t)m * a.m[0].N + (ci.ub + i) * 8 + col] = sw;
                 } else {
                     const MmMat& M = a.m[ci.mi];
                     float* y = M.y + (size_t)m * M.N + (ci.ub - M.tile_begin + i) * 8 + col;
@@ -395,6 +409,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1) k_gemv_mma(const __grid_constan
                 }
             }
             __syncthreads();   // red is rewritten by the next item
+            if (GU && a.oxa) {
+                // swi group ci.ub / 4 of every row, QUANTQ8'd for the down GEMV: warp = row
+                if (warp < a.B) mm_store_group(swq[warp * 33 + lane], ci.ub >> 2, warp, TS, a.otern, a.oxa, a.oxk);
+                __syncthreads();   // swq is rewritten by the next item
+            }
         }
         if (++cks == nks) { cks = 0; ci = mm_item<GU>(a, ci.ub + ci.n, u1); }
     }
@@ -472,12 +491,16 @@ bool tb_gemv_mma_fits(int64_t K, const int64_t* Ns, int count, int batch)
 // y_i (+)= W_i . x for `count` matrices (gateup: swi = silu(W_0 . x) * (W_1 . x)).
 int tb_gemv_mma_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
                      const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
-                     float eps, int64_t K, int batch, int acc, bool tern, bool gateup, void* buf)
+                     float eps, int64_t K, int batch, int acc, bool tern, bool gateup, void* buf, bool quantize,
+                     void* obuf, bool otern)
 {
     TB_REQUIRE(ctx, count >= 1 && count <= 3 && (!gateup || count == 2), "bad matrix count %d", count);
     TB_REQUIRE(ctx, tb_gemv_mma_fits(K, Ns, count, batch),
                "gemv_mma: needs batch 2..16, K %% 256 == 0 and rows %% 8 == 0 (batch=%d K=%lld)", batch, (long long)K);
-    TB_REQUIRE(ctx, x && TB_ALIGNED(x, 16) && buf && TB_ALIGNED(buf, 16), "x and buf must be 16-byte aligned");
+    TB_REQUIRE(ctx, (!quantize || (x && TB_ALIGNED(x, 16))) && buf && TB_ALIGNED(buf, 16),
+               "x and buf must be 16-byte aligned");
+    TB_REQUIRE(ctx, !obuf || (gateup && Ns[0] % 32 == 0 && TB_ALIGNED(obuf, 16)),
+               "a quantized output needs gate/up rows in whole 32-groups");
     TB_REQUIRE(ctx, !normw || TB_ALIGNED(normw, 16), "norm weight must be 16-byte aligned");
     for (int i = 0; i < count; i++) {
         TB_REQUIRE(ctx, packs[i] && scales[i] && ys[i], "null weight or output pointer");
@@ -487,12 +510,14 @@ int tb_gemv_mma_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* c
     const int ts = batch > 8 ? 16 : 8, G = (int)(K / 32);
     unsigned char* xa = static_cast<unsigned char*>(buf);
     uint2* xk = reinterpret_cast<uint2*>(xa + (size_t)G * ts * 32);
-    const int gsplit = std::max(1, std::min(G / 8, std::max(1, 2 * ctx->num_sms / ts)));
-    cudaError_t e = tern ? tb_launch(ctx, k_quant_mma<true>, dim3(ts, gsplit), dim3(256), 0, x, normw, eps, (int)K,
-                                     batch, ts, xa, xk)
-                         : tb_launch(ctx, k_quant_mma<false>, dim3(ts, gsplit), dim3(256), 0, x, normw, eps, (int)K,
-                                     batch, ts, xa, xk);
-    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_mma launch: %s", cudaGetErrorString(e));
+    if (quantize) {
+        const int gsplit = std::max(1, std::min(G / 8, std::max(1, 2 * ctx->num_sms / ts)));
+        cudaError_t e = tern ? tb_launch(ctx, k_quant_mma<true>, dim3(ts, gsplit), dim3(256), 0, x, normw, eps,
+                                         (int)K, batch, ts, xa, xk)
+                             : tb_launch(ctx, k_quant_mma<false>, dim3(ts, gsplit), dim3(256), 0, x, normw, eps,
+                                         (int)K, batch, ts, xa, xk);
+        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "quant_mma launch: %s", cudaGetErrorString(e));
+    }
     MmArgs a{};
     a.count = count;
     a.K = (int)K;
@@ -510,10 +535,18 @@ int tb_gemv_mma_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* c
     for (int i = 0; i < count; i++) units += gateup ? 0 : (int)(Ns[i] / 8);
     if (gateup) units = (int)(Ns[0] / 8);
     const int maxnu = gateup ? MM_MAXT / 2 : MM_MAXT;
-    const int tpc = (units + ctx->num_sms - 1) / ctx->num_sms;
+    // a quantized swi output: every item is one whole 32-row group (4 pairs)
+    a.ualign = obuf ? 4 : 1;
+    const int quanta = units / a.ualign;
+    const int tpc = ((quanta + ctx->num_sms - 1) / ctx->num_sms) * a.ualign;
     const int nitem = (tpc + maxnu - 1) / maxnu;
     a.nu = (tpc + nitem - 1) / nitem;
-    a.grid = (units + tpc - 1) / tpc;
+    a.grid = (quanta + tpc / a.ualign - 1) / (tpc / a.ualign);
+    if (obuf) {
+        a.oxa = static_cast<unsigned char*>(obuf);
+        a.oxk = reinterpret_cast<uint2*>(a.oxa + (size_t)(Ns[0] / 32) * ts * 32);
+        a.otern = otern ? 1 : 0;
+    }
     const int box_rows = 8 * a.nu;
     const int64_t wrow = tern ? K / 4 : K / 2;
     for (int i = 0; i < 3; i++) {

@@ -9,13 +9,16 @@ int tb_gemv_dp4a_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* 
                       const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
                       float eps, int64_t K, int batch, int acc);
 // decode GEMVs over 2..16 rows on the tensor cores (one weight read): quantize
-// x into buf (tb_gemv_mma_act_bytes bytes) and run `count` matrices, or gate/up
-// with silu when gateup (count 2, ys[0] the output)
+// x into buf (tb_gemv_mma_act_bytes bytes; quantize = false: buf already holds the
+// rows, written by their producer) and run `count` matrices, or gate/up with silu
+// when gateup (count 2, ys[0] the output; with obuf, swi is written QUANTQ8'd into
+// obuf for a next GEMV of kind otern instead of as f32)
 size_t tb_gemv_mma_act_bytes(int64_t K, int batch);
 bool tb_gemv_mma_fits(int64_t K, const int64_t* Ns, int count, int batch);
 int tb_gemv_mma_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
                      const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
-                     float eps, int64_t K, int batch, int acc, bool tern, bool gateup, void* buf);
+                     float eps, int64_t K, int batch, int acc, bool tern, bool gateup, void* buf,
+                     bool quantize = true, void* obuf = nullptr, bool otern = false);
 int tb_gemv_f32_impl(tb_ctx* ctx, float* y, const float* x, const uint32_t* pack, const uint16_t* scales,
                      int64_t N, int64_t K, int batch, int acc);
 int tb_gemv_tern_impl(tb_ctx* ctx, float* out, const uint8_t* codes, const float* scales, const int8_t* act,
@@ -31,10 +34,14 @@ int tb_quant_act_impl(tb_ctx* ctx, const float* x, int8_t* act, int32_t* xsum, f
 // S_b - 1 are complete before the preceding kernel in the stream runs (only
 // that kernel may write row S_b - 1), so the first tiles are fetched before
 // griddepcontrol.wait.
+// mxa / mxk (optional): the outputs also QUANTQ8'd in the tensor-core GEMVs' fragment
+// order, mts row slots (sequence = slot), for int4 or (mtern) ternary weights; needs
+// (nHq/nKv)·hd a multiple of 128.
 int tb_attn_decode_impl(tb_ctx* ctx, float* out, const float* qr, const int8_t* Kq, const float* Ks,
                         const int8_t* Vq, const float* Vs, int64_t S, int64_t nHq, int64_t nKv, int64_t hd,
                         int nsplit, float* PO, float* PML, unsigned* counters, int64_t batch = 1,
-                        int64_t cache_rows = 0, const int32_t* dpos = nullptr, bool early = false);
+                        int64_t cache_rows = 0, const int32_t* dpos = nullptr, bool early = false,
+                        unsigned char* mxa = nullptr, uint2* mxk = nullptr, int mts = 0, bool mtern = false);
 int tb_attn_auto_nsplit(tb_ctx* ctx, int64_t S, int64_t nKv);
 // two-stage argmax of `rows` rows of n; part holds rows*nparts keys.  out gets
 // the index + idx_base, out_key the ordered key (for tb_argmax_merge_impl),

@@ -138,6 +138,7 @@ struct tb_qwen3 {
     unsigned long long* step_pk = nullptr;       // [hidden] phase-boundary packets of x after o
     unsigned char* step_attnq = nullptr;         // quantized attention output of the persistent step
     unsigned char* mma_act = nullptr;            // fragment-ordered int8 rows of the tensor-core GEMVs
+    unsigned char* mma_act2 = nullptr;           // ... of the down GEMV, written by the gate/up epilogue
     bool step_direct = false;                    // persistent step launched per call (not capturable)
     void* step_trace = nullptr;                  // optional phase trace of the persistent kernel
 };
@@ -232,11 +233,17 @@ bool use_mma(const tb_qwen3* m, const int64_t* Ns, int count, int64_t K)
 }
 
 // y (+)= W . x over B rows, in launches of at most GEMV_MAX_B rows (fused int8
-// quantization of x, optional fused RMSNorm with norm_w)
-int gemv_rows(tb_qwen3* m, float* y, const float* x, const Mat& w, const uint16_t* norm_w, int acc)
+// quantization of x, optional fused RMSNorm with norm_w); with preq, x's rows are
+// already in the tensor-core GEMV's fragment order there (one launch)
+int gemv_rows(tb_qwen3* m, float* y, const float* x, const Mat& w, const uint16_t* norm_w, int acc,
+              void* preq = nullptr)
 {
     const int B = m->c.batch;
     const bool mma = use_mma(m, &w.N, 1, w.K);
+    if (preq) {   // the rows are already quantized by their producer (all B in one launch)
+        return tb_gemv_mma_impl(m->ctx, 1, &y, &w.pack, &w.scales, &w.N, x, nullptr, m->c.rms_eps, w.K, B, acc,
+                                w.tern, false, preq, false);
+    }
     const int chunk = mma ? MMA_MAX_B : GEMV_MAX_B;
     for (int b0 = 0; b0 < B; b0 += chunk) {
         const int nb = std::min(chunk, B - b0);
@@ -256,14 +263,14 @@ int gemv_rows(tb_qwen3* m, float* y, const float* x, const Mat& w, const uint16_
 
 // x_next = x + sum over ranks of (W_r . a_r); `cur` names the buffer holding
 // x_next afterwards.  xi: index of this exchange within the step.
-int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w, int xi)
+int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w, int xi, void* preq = nullptr)
 {
-    if (m->P == 1) return gemv_rows(m, m->x[cur], a, w, nullptr, 1);
+    if (m->P == 1) return gemv_rows(m, m->x[cur], a, w, nullptr, 1, preq);
     if (m->p2p) {
         const int64_t n = (int64_t)m->c.batch * m->c.hidden;
         float* part; unsigned long long* keys; unsigned *flag, *flag2, *step;
         tb_tp_arena_layout(m->arena, n, &part, &keys, &flag, &flag2, &step);
-        TRY(gemv_rows(m, part + (size_t)((xi + 1) & 1) * n, a, w, nullptr, 0));
+        TRY(gemv_rows(m, part + (size_t)((xi + 1) & 1) * n, a, w, nullptr, 0, preq));
         return tb_tp_allreduce_impl(m->ctx, m->peer_arena, m->P, m->r, n, m->x[cur], xi, 2 * m->c.layers);
     }
     const int nxt = cur ^ 1;
@@ -272,9 +279,9 @@ int proj_residual(tb_qwen3* m, int& cur, const float* a, const Mat& w, int xi)
         // rank 0 carries the residual into the sum
         cudaError_t e = cudaMemcpyAsync(m->x[nxt], m->x[cur], bytes, cudaMemcpyDeviceToDevice, m->ctx->stream);
         if (e != cudaSuccess) return tb_fail(m->ctx, TB_ERR_CUDA, "residual copy: %s", cudaGetErrorString(e));
-        TRY(gemv_rows(m, m->x[nxt], a, w, nullptr, 1));
+        TRY(gemv_rows(m, m->x[nxt], a, w, nullptr, 1, preq));
     } else {
-        TRY(gemv_rows(m, m->x[nxt], a, w, nullptr, 0));
+        TRY(gemv_rows(m, m->x[nxt], a, w, nullptr, 0, preq));
     }
     TRY(nccl_check(m, nccl().AllReduce(m->x[nxt], m->x[nxt], (size_t)m->c.batch * m->c.hidden, ncclFloat32, ncclSum,
                                        m->comm, m->ctx->stream), "allreduce"));
@@ -412,11 +419,20 @@ int issue_step(tb_qwen3* m)
         }
         TRY(tb_attn_prep_q8_batch(ctx, m->q, m->k, m->v, Ly.qn, Ly.kn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, m->nHq,
                                   m->nKv, hd, B, c.max_seq, m->pos, c.rope_theta, c.rms_eps));
+        // the whole batch in one tensor-core launch: the attention writes the o GEMV's
+        // rows already quantized, and the gate/up epilogue the down GEMV's
+        const bool one_mma = m->mma_act2 && B <= MMA_MAX_B;
+        const bool o_fused = one_mma && use_mma(m, &Ly.o.N, 1, Ly.o.K) && (m->nHq / m->nKv * hd) % 128 == 0;
+        const int ts = B > 8 ? 16 : 8;
+        unsigned char* oxa = o_fused ? m->mma_act : nullptr;
+        uint2* oxk = o_fused ? reinterpret_cast<uint2*>(m->mma_act + (size_t)(Ly.o.K / 32) * ts * 32) : nullptr;
         TRY(tb_attn_decode_impl(ctx, m->attn, m->qr, Ly.Kq, Ly.Ks, Ly.Vq, Ly.Vs, c.max_seq, m->nHq, m->nKv, hd,
-                                m->nsplit, m->PO, m->PML, m->counters, B, c.max_seq, m->pos, true));
-        TRY(proj_residual(m, cur, m->attn, Ly.o, 2 * l));
+                                m->nsplit, m->PO, m->PML, m->counters, B, c.max_seq, m->pos, true, oxa, oxk, ts,
+                                Ly.o.tern));
+        TRY(proj_residual(m, cur, m->attn, Ly.o, 2 * l, oxa));
         const int64_t guN[2] = {m->I, m->I};
         const bool gu_mma = Ly.gate.tern == Ly.up.tern && use_mma(m, guN, 2, H);
+        const bool down_fused = one_mma && gu_mma && m->I % 32 == 0 && use_mma(m, &Ly.down.N, 1, Ly.down.K);
         const int gu_chunk = gu_mma ? MMA_MAX_B : GEMV_MAX_B;
         for (int b0 = 0; b0 < B; b0 += gu_chunk) {
             const int nb = std::min(gu_chunk, B - b0);
@@ -425,7 +441,8 @@ int issue_step(tb_qwen3* m)
                 const uint32_t* packs[2] = {Ly.gate.pack, Ly.up.pack};
                 const uint16_t* scs[2] = {Ly.gate.scales, Ly.up.scales};
                 TRY(tb_gemv_mma_impl(ctx, 2, ys, packs, scs, guN, m->x[cur] + (int64_t)b0 * H, Ly.ln2, c.rms_eps, H,
-                                     nb, 0, Ly.gate.tern, true, m->mma_act));
+                                     nb, 0, Ly.gate.tern, true, m->mma_act, true,
+                                     down_fused ? m->mma_act2 : nullptr, Ly.down.tern));
             } else if (Ly.gate.tern)   // gateUpSiluQ's ternary branch (qwen3.js:730)
                 TRY(tb_gateup_silu_tern_wgsl_dp4a(ctx, m->swi + (int64_t)b0 * m->I, m->x[cur] + (int64_t)b0 * H,
                                                   Ly.ln2, c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack,
@@ -435,7 +452,7 @@ int issue_step(tb_qwen3* m)
                                              c.rms_eps, Ly.gate.pack, Ly.gate.scales, Ly.up.pack, Ly.up.scales, m->I,
                                              H, nb));
         }
-        TRY(proj_residual(m, cur, m->swi, Ly.down, 2 * l + 1));
+        TRY(proj_residual(m, cur, m->swi, Ly.down, 2 * l + 1, down_fused ? m->mma_act2 : nullptr));
     }
     return issue_head(m, cur);
 }
@@ -682,6 +699,13 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
     if (!rc && B >= MMA_MIN_B) {
         const int64_t kmax = std::max<int64_t>({(int64_t)H, m->nHq * hd, m->I});
         rc = alloc(m, &m->mma_act, tb_gemv_mma_act_bytes(kmax, (int)std::min<int64_t>(B, MMA_MAX_B)));
+        if (!rc) rc = alloc(m, &m->mma_act2, tb_gemv_mma_act_bytes(m->I, (int)std::min<int64_t>(B, MMA_MAX_B)));
+        // row slots past the batch stay zero: producers write only the batch's rows
+        if (!rc && (cudaMemsetAsync(m->mma_act, 0, tb_gemv_mma_act_bytes(kmax, (int)std::min<int64_t>(B, MMA_MAX_B)),
+                                    ctx->stream) != cudaSuccess ||
+                    cudaMemsetAsync(m->mma_act2, 0, tb_gemv_mma_act_bytes(m->I, (int)std::min<int64_t>(B, MMA_MAX_B)),
+                                    ctx->stream) != cudaSuccess))
+            rc = tb_fail(ctx, TB_ERR_CUDA, "qwen3: clearing the activation buffers failed");
     }
     m->nsplit = tb_attn_auto_nsplit(ctx, c.max_seq, m->nKv * B);
     if (B == 1 && m->P == 1) {
