@@ -624,16 +624,21 @@ struct DecUnit {
 
         // ---- the last split of this kv head to finish combines all of them
         //      (ATTN_DEC_COMBINE, qwen3.js:2048-2069): out = sum_i e_i O_i / sum_i e_i l_i,
-        //      e_i = exp(m_i - max m).  Partials are read through L2 (ld.cg).
-        __threadfence();
+        //      e_i = exp(m_i - max m).  Partials are read through L2 (ld.cg).  The
+        //      arrival is one acquire-release add by thread 0 after the unit's barrier:
+        //      it publishes the unit's partial (every thread's stores precede the
+        //      barrier) and, in the last unit, makes every other unit's visible.
         unit_sync(bar, NT);
         int* last = reinterpret_cast<int*>(wm);          // wm/wl are free again after the loop above
-        if (tid == 0) *last = atomicAdd(counter, 1u) == (unsigned)(a.nsplit - 1);
+        if (tid == 0) {
+            unsigned old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+            *last = old == (unsigned)(a.nsplit - 1);
+        }
         unit_sync(bar, NT);
         ts(5);
         if (tr && tid == 0) tr[7] = *last;
         if (!*last) return;
-        __threadfence();
         float* wts = reinterpret_cast<float*>(smem + L::OFF_ST);    // [GRP][nsplit]
         float* lsum = wl;                                            // [GRP]
         // float4 columns (head h, dims 4c..4c+3); when there are fewer columns than
@@ -654,7 +659,7 @@ struct DecUnit {
             for (int u = 0; u < PRE; u++)
                 if (pp + u * P < a.nsplit) pv[u] = __ldcg(po + (long long)(pp + u * P) * (HD / 4));
         }
-        for (int h = wid; h < GRP; h += W) {
+        for (int h = wid; h < GRP && a.nsplit > 256; h += W) {   // many splits: two passes
             const float* pml = PML + (long long)(hk * GRP + h) * a.nsplit * 2;
             float M = NEG_BIG;
             for (int i = lane; i < a.nsplit; i += 32) M = fmaxf(M, __ldcg(pml + 2 * i));
@@ -664,6 +669,31 @@ struct DecUnit {
                 const float e = __expf(__ldcg(pml + 2 * i) - M);
                 wts[h * a.nsplit + i] = e;
                 Ls = fmaf(__ldcg(pml + 2 * i + 1), e, Ls);
+            }
+            Ls = warp_sum(Ls);
+            if (lane == 0) lsum[h] = Ls;
+        }
+        for (int h = wid; h < GRP && a.nsplit <= 256; h += W) {
+            // each split's (m, l) pair read once (at most 8 a lane)
+            const float2* pml = reinterpret_cast<const float2*>(PML + (long long)(hk * GRP + h) * a.nsplit * 2);
+            float2 ml[8];
+            float M = NEG_BIG;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = lane + 32 * u;
+                ml[u] = i < a.nsplit ? __ldcg(pml + i) : make_float2(NEG_BIG, 0.0f);
+                M = fmaxf(M, ml[u].x);
+            }
+            M = warp_max(M);
+            float Ls = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = lane + 32 * u;
+                if (i < a.nsplit) {
+                    const float e = __expf(ml[u].x - M);
+                    wts[h * a.nsplit + i] = e;
+                    Ls = fmaf(ml[u].y, e, Ls);
+                }
             }
             Ls = warp_sum(Ls);
             if (lane == 0) lsum[h] = Ls;
