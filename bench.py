@@ -255,76 +255,74 @@ def time_e2e(m, K, stream, ids0, pos0):
 
 
 def kernel_kinds(cfg, dev, P, context, peak):
-    """Per-launch device time of each kernel kind of one rank's step at batch 1,
-    cold L2 (a 256 MB write between launches), CUDA events on the launching
-    stream.  Returns {kind: {...}} with algorithmic bytes and GB/s."""
+    """Per-launch device time of each kernel kind of one rank's multi-kernel step at
+    batch 1: one recorded batch of back-to-back launches of the kind, each on its own
+    copy of the weights (or KV cache), the copies together at least twice the L2, so
+    every launch streams from HBM; CUDA events around replays on the launching
+    stream, divided by the launches.  Returns {kind: {...}} with algorithmic bytes
+    and GB/s."""
+    import math
     import torch
     import tabinfer_b200 as tb
     g = torch.Generator(device=dev).manual_seed(99)
     H, hd, I, V, L = cfg["hidden"], cfg["head_dim"], cfg["intermediate"], cfg["vocab"], cfg["layers"]
     nHq, nKv = cfg["n_heads"] // P, cfg["n_kv_heads"] // P
+    ctx = tb.default_context(dev.index)
 
     def mat(N, K):
         w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         return tb.quantize_int4_bf16(w.view(torch.int16))
 
-    # a few copies of each matrix so back-to-back launches do not hit L2
-    NC = 4
-    qm = [mat(nHq * hd, H) for _ in range(NC)]
-    km = [mat(nKv * hd, H) for _ in range(NC)]
-    vm = [mat(nKv * hd, H) for _ in range(NC)]
-    om = [mat(H, nHq * hd) for _ in range(NC)]
-    gm = [mat(I // P, H) for _ in range(NC)]
-    um = [mat(I // P, H) for _ in range(NC)]
-    dm = [mat(H, I // P) for _ in range(NC)]
-    lm = mat(V // P, H)
     ln = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half().view(torch.int16)
     x = torch.randn(1, H, device=dev, generator=g)
     xa = torch.randn(1, nHq * hd, device=dev, generator=g)
     xs = torch.randn(1, I // P, device=dev, generator=g)
     S = context
     row = nKv * hd
-    Kq = torch.randint(-127, 128, (S, row), device=dev, generator=g, dtype=torch.int8)
-    Vq = torch.randint(-127, 128, (S, row), device=dev, generator=g, dtype=torch.int8)
-    Ks = torch.rand(S, row // 32, device=dev, generator=g) + 0.5
-    Vs = torch.rand(S, row // 32, device=dev, generator=g) + 0.5
     qr = torch.randn(nHq * hd, device=dev, generator=g)
+
+    def kv():
+        return (torch.randint(-127, 128, (S, row), device=dev, generator=g, dtype=torch.int8),
+                torch.rand(S, row // 32, device=dev, generator=g) + 0.5,
+                torch.randint(-127, 128, (S, row), device=dev, generator=g, dtype=torch.int8),
+                torch.rand(S, row // 32, device=dev, generator=g) + 0.5)
+
     outs = {n: torch.zeros(1, N, device=dev) for n, N in (("q", nHq * hd), ("k", nKv * hd), ("v", nKv * hd),
                                                              ("o", H), ("swi", I // P), ("lm", V // P))}
     att = torch.zeros(nHq * hd, device=dev)
+    # kind: (one copy's tensors, the launch on a copy, algorithmic bytes a launch, launches a step)
     kinds = {
-        "gemv rmsnorm+qkv": (lambda i: tb.gemv_dp4a_multi(x, [qm[i], km[i], vm[i]], norm_w=ln,
-                                                          ys=[outs["q"], outs["k"], outs["v"]]),
+        "gemv rmsnorm+qkv": (lambda: (mat(nHq * hd, H), mat(nKv * hd, H), mat(nKv * hd, H)),
+                             lambda c: tb.gemv_dp4a_multi(x, list(c), norm_w=ln, ys=[outs["q"], outs["k"], outs["v"]]),
                              sum(wbytes(N, H) + N * 4 for N in (nHq * hd, nKv * hd, nKv * hd)) + H * 4, L),
-        "gemv o": (lambda i: tb.gemv_dp4a(xa, *om[i], y=outs["o"], acc=True), gemv_bytes(H, nHq * hd, 1, 4), L),
-        "gemv rmsnorm+gate+up+silu": (lambda i: tb.gate_up_silu_dp4a(x, *gm[i], *um[i], norm_w=ln, swi=outs["swi"]),
+        "gemv o": (lambda: mat(H, nHq * hd), lambda c: tb.gemv_dp4a(xa, *c, y=outs["o"], acc=True),
+                   gemv_bytes(H, nHq * hd, 1, 4), L),
+        "gemv rmsnorm+gate+up+silu": (lambda: (mat(I // P, H), mat(I // P, H)),
+                                      lambda c: tb.gate_up_silu_dp4a(x, *c[0], *c[1], norm_w=ln, swi=outs["swi"]),
                                       2 * wbytes(I // P, H) + H * 4 + (I // P) * 4, L),
-        "gemv down": (lambda i: tb.gemv_dp4a(xs, *dm[i], y=outs["o"], acc=True), gemv_bytes(H, I // P, 1, 4), L),
-        "gemv rmsnorm+lm_head (f32)": (lambda i: tb.gemv_q_norm(x, ln, 1e-6, *lm, y=outs["lm"]),
+        "gemv down": (lambda: mat(H, I // P), lambda c: tb.gemv_dp4a(xs, *c, y=outs["o"], acc=True),
+                      gemv_bytes(H, I // P, 1, 4), L),
+        "gemv rmsnorm+lm_head (f32)": (lambda: mat(V // P, H), lambda c: tb.gemv_q_norm(x, ln, 1e-6, *c, y=outs["lm"]),
                                        gemv_bytes(V // P, H, 1, 4), 1),
-        "attn decode S=%d" % S: (lambda i: tb.attention_decode_q8(qr, (Kq, Ks, Vq, Vs), S, nHq, nKv, hd, out=att),
+        "attn decode S=%d" % S: (kv, lambda c: tb.attention_decode_q8(qr, c, S, nHq, nKv, hd, out=att),
                                  kv_bytes(cfg, P, S) + 2 * nHq * hd * 4, L),
     }
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    from tabinfer_b200._lib import LIB
     res = {}
-    for name, (fn, nbytes, per_step) in kinds.items():
-        fn(0)
-        ts = []
-        for r in range(12):
-            flush.fill_(r & 0xff)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            fn(r % NC)
-            e1.record(stream)
-            e1.synchronize()
-            if r >= 2:
-                ts.append(e0.elapsed_time(e1))
-        us = statistics.median(ts) * 1e3
+    l2 = 126 << 20
+    for name, (make, fn, nbytes, per_step) in kinds.items():
+        nc = max(4, int(math.ceil(2 * l2 / nbytes)))
+        copies = [make() for _ in range(nc)]
+        h, stream = _record_batch(ctx, dev, lambda: [fn(c) for c in copies])
+        ms = _replay_ms(ctx, h, stream, 5)
+        LIB.tb_batch_destroy(h)
+        us = ms * 1e3 / nc
         gbs = nbytes / (us * 1e-6) / 1e9
         res[name] = {"us_per_launch": round(us, 3), "bytes_per_launch": int(nbytes), "launches_per_step": per_step,
-                     "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4), "us_per_step": round(us * per_step, 2)}
-    del flush
+                     "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4), "us_per_step": round(us * per_step, 2),
+                     "timing": "%d back-to-back launches on %d weight copies (> 2x L2), recorded, CUDA events" % (nc, nc)}
+        del copies
+        torch.cuda.synchronize(dev)
     torch.cuda.synchronize(dev)
     return res
 
@@ -1615,7 +1613,7 @@ def main():
                     "frac": d["frac_of_peak"], "traffic": traffic,
                     "peak_source": peak_src + " hbm_gbs (burst copy)",
                     "algorithmic_bytes_per_launch": d["bytes_per_launch"], "us_per_launch": d["us_per_launch"],
-                    "timing": "cold L2 (256 MB write before each launch), CUDA events on the launching stream"}
+                    "timing": d["timing"]}
         extras["kernels"] = kinds
     if world == 1 and rank == 0 and not args.no_extras:
         extras["gemv_chain_0.6b"] = chain_gbs(dev, ctx, 1, max(100, args.steps))
