@@ -17,9 +17,9 @@ from helpers import bf16_normal, host, row_rel_err, tern_bf16, u16_dev, u32_dev
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
-# Qwen3-1.7B projections (q, k/v, gate/up, down), a multi-item row count, and a
-# row count that is not a whole number of items
-SHAPES = [(2048, 2048), (1024, 2048), (6144, 2048), (2048, 6144), (8200, 1024), (40, 256)]
+# Qwen3-1.7B projections (q, k/v, gate/up, down), a multi-item row count, a row
+# count that is not a whole number of items, and K = 768 (a last stage of 8 groups)
+SHAPES = [(2048, 2048), (1024, 2048), (6144, 2048), (2048, 6144), (8200, 1024), (40, 256), (1032, 768)]
 
 
 def _mat(seed, N, K):
@@ -76,7 +76,7 @@ def _tern(seed, N, K):
 
 
 @pytest.mark.parametrize("B", [2, 8, 16])
-@pytest.mark.parametrize("N,K", [(2048, 2048), (2048, 6144), (1000, 1024)])
+@pytest.mark.parametrize("N,K", [(2048, 2048), (2048, 6144), (1000, 1024), (264, 768)])
 def test_gemv_mma_tern_wgsl(cuda, N, K, B):
     pack, sc = _tern(N * 5 + K, N, K)
     x = _x(B + 77, B, K)

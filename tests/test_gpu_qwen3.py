@@ -133,3 +133,21 @@ def test_generate_greedy_tokens_follow_oracle(cuda):
         assert t[0] == int(np.argmax(ref))
         tok, pos = t[0], pos + 1
     m.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch", [4, 12])
+def test_batched_ternary_step_matches_oracle(cuda, batch):
+    """A ternary (WebGPU layout) checkpoint at 2..16 sequences: the tensor-core GEMVs on
+    the ternary codes, with the attention and the gate/up epilogue writing the next
+    GEMV's rows in the ternary fragment order, against the composed oracle."""
+    cfg = dict(SMALL, batch=batch, layers=2)
+    prefill = [(5 + 7 * b) % 40 for b in range(batch)]
+    W, m = _build(cfg, 61 + batch, prefill, ternary=True)
+    om = OracleModel(cfg, W)
+    assert all(om.tern.values())
+    ids = [(17 + 131 * b) % cfg["vocab"] for b in range(batch)]
+    m.set_tokens(ids, prefill)
+    ids2, pos2 = _check_step(m, om, cfg, ids, prefill, route_f32=False)
+    _check_step(m, om, cfg, ids2, pos2, route_f32=False)
+    m.close()
