@@ -716,7 +716,9 @@ TB_API int tb_qwen3_create(tb_ctx* ctx, const tb_qwen3_config* cfg, tb_qwen3** o
         const long long by_keys = (c.max_seq + 127) / 128;
         // (a long context past the persistent step keeps this count too: three
         // single-stage units an SM with three times the splits measured slower at
-        // 32k than one two-stage unit an SM, 571 vs 633 tok/s)
+        // 32k than one two-stage unit an SM, 571 vs 633 tok/s; with the scores on
+        // the tensor cores, five 4-warp single-stage units an SM at 92 splits were
+        // still slower, 675 vs 701 tok/s)
         m->nsplit = (int)std::max(1LL, std::min(by_keys, (long long)(ctx->num_sms / m->nKv)));
     }
     if (!rc) rc = alloc(m, &m->qr, B * m->nHq * hd);
