@@ -1378,6 +1378,9 @@ def run_only(name, steps):
     peak, _ = load_peaks()
     if name == "q2g64":
         out = q2g64_extra(dev, ctx, peak)
+    elif name == "moe":
+        stream = torch.cuda.current_stream(dev)
+        out = {"group32": moe_extra(dev, peak, stream), "group128": moe_extra(dev, peak, stream, group=128)}
     elif name == "decode":
         stream = torch.cuda.current_stream(dev)     # the stream main() times the model steps on
         out = {"batch%d_context%d" % (B, S): decode_extra(dev, stream, B, S)
@@ -1429,7 +1432,7 @@ def main():
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
     ap.add_argument("--profile-q2g64", action="store_true",
                     help="three Q2_0_g64 GEMV launches on 151936 x 2048 matrices (for an ncu capture), then exit")
-    ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds", "decode"),
+    ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds", "decode", "moe"),
                     help="run one extra block alone on GPU 0 and print its JSON (development runs)")
     args = ap.parse_args()
     if args.only:
