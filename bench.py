@@ -474,6 +474,44 @@ def prefill_extra(dev, peak_tf, stream):
     return out
 
 
+def prefill_exact_extra(dev, peak_tf, stream):
+    """The seven Qwen3-1.7B layer matrices as the exact-sum prefill GEMM
+    (gemmDP4A, the product's prefill route) on M = 512 / 2048 / 8192 QUANTQ8T rows:
+    int8 TOP/s of 2*M*N*K for the tcgen05 kind::i8 kernel and for the warp-level
+    mma.sync form of the same arithmetic, cold L2 per launch."""
+    import torch
+    import tabinfer_b200 as tb
+    g = torch.Generator(device=dev).manual_seed(6)
+    H, I = Q17["hidden"], Q17["intermediate"]
+    shapes = [(2048, H), (1024, H), (1024, H), (H, 2048), (I, H), (I, H), (H, I)]
+    mats = []
+    for N, K in shapes:
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        mats.append(tb.quantize_int4_bf16(w.view(torch.int16)))
+        del w
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+    for M in (512, 2048, 8192):
+        row = {}
+        for form, warp in (("tcgen05", False), ("mma_sync", True)):
+            ms = 0.0
+            ops = 0
+            for (N, K), (pk, sc) in zip(shapes, mats):
+                xq = torch.randint(-127, 128, (M, K), device=dev, dtype=torch.int32, generator=g).to(torch.int8)
+                xs = torch.rand(M, K // 32, device=dev, generator=g) * 0.01
+                y = torch.empty(M, N, device=dev)
+                ms += _cold_time(lambda: tb.gemm_dp4(xq, xs, pk, sc, y=y, warp=warp), flush, stream)
+                ops += 2 * M * N * K
+            tops = ops / (ms * 1e-3) / 1e12
+            row[form] = {"us_7_matrices": round(ms * 1e3, 1), "tops": round(tops, 1),
+                         "frac_of_bf16_peak": round(tops / peak_tf, 4)}
+        row["speedup"] = round(row["mma_sync"]["us_7_matrices"] / row["tcgen05"]["us_7_matrices"], 3)
+        out["M%d" % M] = row
+    del flush
+    torch.cuda.synchronize(dev)
+    return out
+
+
 def moe_extra(dev, peak_gbs, stream, group=32):
     """One LFM2.5-8B-A1B-shaped int3 MoE FFN (hidden 2048, 32 experts, I 1792,
     top-4) over 1 / 8 / 64 tokens: router + grouped expert GEMVs + combine.
@@ -1385,6 +1423,11 @@ def run_only(name, steps):
         stream = torch.cuda.current_stream(dev)     # the stream main() times the model steps on
         out = {"batch%d_context%d" % (B, S): decode_extra(dev, stream, B, S)
                for B, S in ((16, 4096), (4, 4096), (8, 4096), (1, 32768))}
+    elif name == "prefill":
+        stream = torch.cuda.current_stream(dev)
+        mp = os.path.join(REPO, "MEASURED_PEAKS.json")
+        bf16 = json.load(open(mp)).get("bf16_tflops", 1590.0) if os.path.exists(mp) else 1590.0
+        out = {"gemm_exact": prefill_exact_extra(dev, bf16, stream), "forward": prefill_forward_extra(dev, stream)}
     elif name == "chain":
         out = {}
         for B in (1, 4, 8):
@@ -1432,7 +1475,7 @@ def main():
                     help="three recorded decode steps at context S (for an ncu launch list), then exit")
     ap.add_argument("--profile-q2g64", action="store_true",
                     help="three Q2_0_g64 GEMV launches on 151936 x 2048 matrices (for an ncu capture), then exit")
-    ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds", "decode", "moe"),
+    ap.add_argument("--only", default=None, choices=("q2g64", "chain", "kinds", "decode", "moe", "prefill"),
                     help="run one extra block alone on GPU 0 and print its JSON (development runs)")
     args = ap.parse_args()
     if args.only:
@@ -1630,6 +1673,7 @@ def main():
         extras["prefill_gemm_1.7b"] = prefill_extra(dev, peaks.get("bf16_tflops", 1590.0), stream)
         extras["prefill_gemm_1.7b"]["peak"] = "bf16_tflops %s (cuBLAS burst)" % (
             "measured" if peaks else "fallback 1590")
+        extras["prefill_gemm_exact_1.7b"] = prefill_exact_extra(dev, peaks.get("bf16_tflops", 1590.0), stream)
         extras["moe_int3_lfm2.5"] = moe_extra(dev, peak, stream)
         extras["moe_int3_lfm2.5_group128"] = moe_extra(dev, peak, stream, group=128)
         extras["ternary_wgsl_bonsai_1.7b"] = tern_extra(dev, peak, peaks.get("bf16_tflops", 1590.0), stream)

@@ -446,12 +446,19 @@ TB_API int tb_gemm_int4_g32(tb_ctx *ctx, float *y, const void *x, int x_bf16, co
 /* The reference's integer prefill GEMMs, gemmDP4A (int4) and gemmTern (ternary
  * WebGPU layout), qwen3.js:1321-1420, with their exact arithmetic: per 32-group
  * the int8 activation (QUANTQ8T xq int8 [M][K], xs f32 [M][K/32]) times the int8
- * weight (nib - 8 or code - 1) summed exactly in int32 on the tensor cores, then
- * y (epilogue)= sum_g f32(s) * xs * sum in f32.  tern selects the weight layout.
- * epilogue: 0 y =, 1 y +=, 2 y = silu(y) * (fused swiglu).  M, N, K % 128 == 0;
- * xq, xs, pack 16-byte, scales and y 8-byte aligned. */
+ * weight (nib - 8 or code - 1) summed exactly in int32 on the tensor cores
+ * (tcgen05.mma kind::i8, one MMA a group into TMEM), then
+ * y (epilogue)= sum_g (f32(s) * xs) * sum in f32, groups in k order.  tern selects
+ * the weight layout.  epilogue: 0 y =, 1 y +=, 2 y = silu(y) * (fused swiglu).
+ * M, N, K % 128 == 0; xq, xs, pack, y 16-byte, scales 8-byte aligned. */
 TB_API int tb_gemm_dp4(tb_ctx *ctx, float *y, const int8_t *xq, const float *xs, const uint32_t *pack,
                        const uint16_t *scales, int64_t M, int64_t N, int64_t K, int epilogue, int tern);
+
+/* The same GEMM on the warp-level MMA (mma.sync m16n8k32 .s8), the same values in
+ * the same order (outputs bit-equal to tb_gemm_dp4): a second implementation for
+ * cross-checks and comparison.  Same arguments and rules, y 8-byte aligned. */
+TB_API int tb_gemm_dp4_warp(tb_ctx *ctx, float *y, const int8_t *xq, const float *xs, const uint32_t *pack,
+                            const uint16_t *scales, int64_t M, int64_t N, int64_t K, int epilogue, int tern);
 
 /* gemmDP4A's data flow on tcgen05 with f16 operands (a faster, rounded form of
  * tb_gemm_dp4 -- linearQ routes to the exact one, qwen3.js:1605-1607): X as QUANTQ8T rows xq int8 [M][K] + xs f32 [M][K/32]

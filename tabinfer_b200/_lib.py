@@ -69,6 +69,7 @@ SIGNATURES = {
     "tb_gemm_tern_wgsl": [P, P, P, P, P, P, I64, I64, I64, I32],
     "tb_gemm_int4_q8": [P, P, P, P, P, P, I64, I64, I64, I32],
     "tb_gemm_dp4": [P, P, P, P, P, P, I64, I64, I64, I32, I32],
+    "tb_gemm_dp4_warp": [P, P, P, P, P, P, I64, I64, I64, I32, I32],
     "tb_linear_tern_wgsl": [P, P, P, P, P, I64, I64, I64, I32],
     "tb_quant_act_q8": [P, P, P, P, P, I64, I64],
     "tb_quantize_wasm": [P, P, P, P, I64, P, I64],

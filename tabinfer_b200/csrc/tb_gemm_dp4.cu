@@ -7,14 +7,15 @@
 // int8 weights (nib - 8, or code - 1) -- exactly as the reference's dot4I8Packed
 // sums, then scaled in f32 once per group.
 //
-// B200 design.  The integer products run on the tensor cores (mma.sync
-// m16n8k32 .s8: one instruction is one 32-group of a 16 x 8 tile, int32
-// accumulators started fresh every group) and each group's int32 tile is scaled
-// and folded into f32 accumulators in registers (packed f32x2 ops; the int32 ->
-// f32 conversion by the exact magic-number add, |sum| < 2^22).  That per-group
-// scaling is what bounds this kernel (2.5 f32 ops per output per 32 MACs), the
-// same on any tensor-core path, so the warp-level MMA is used: no TMEM round
-// trip per group.  CTA tile 128 x 128, 8 warps of 64 x 32, K in stages of 128
+// This file is the warp-level form (tb_gemm_dp4_warp): the integer products run
+// on mma.sync m16n8k32 .s8 (one instruction is one 32-group of a 16 x 8 tile,
+// int32 accumulators started fresh every group) and each group's int32 tile is
+// scaled and folded into f32 accumulators in registers (packed f32x2 ops; the
+// int32 -> f32 conversion by the exact magic-number add, |sum| < 2^22), the MMA
+// and the scaling sharing the same warps' issue slots.  The product path
+// (tb_gemm_dp4) is the tcgen05 form in tb_gemm_i8.cu, which computes the same
+// values in the same order (bit-equal outputs); this one stays as the
+// cross-check.  CTA tile 128 x 128, 8 warps of 64 x 32, K in stages of 128
 // (4 groups): int8 activations arrive by cp.async straight into XOR-swizzled
 // shared rows; packed weights are loaded a stage ahead into registers and
 // widened to int8 (byte permutes + per-byte subtract) while the previous stage
@@ -261,8 +262,8 @@ int launch(tb_ctx* ctx, const DArgs& a)
 
 }  // namespace
 
-int tb_gemm_dp4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
-                     const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue, bool tern)
+int tb_gemm_dp4_warp_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                          const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue, bool tern)
 {
     TB_REQUIRE(ctx, y && xq && xs && pack && scales, "null pointer");
     TB_REQUIRE(ctx, M > 0 && M % BM == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
@@ -277,9 +278,10 @@ int tb_gemm_dp4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, c
     return tern ? launch<true>(ctx, a) : launch<false>(ctx, a);
 }
 
-extern "C" TB_API int tb_gemm_dp4(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
-                                  const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue, int tern)
+extern "C" TB_API int tb_gemm_dp4_warp(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs,
+                                       const uint32_t* pack, const uint16_t* scales, int64_t M, int64_t N, int64_t K,
+                                       int epilogue, int tern)
 {
     if (!ctx) return TB_ERR_INVALID;
-    return tb_gemm_dp4_impl(ctx, y, xq, xs, pack, scales, M, N, K, epilogue, tern != 0);
+    return tb_gemm_dp4_warp_impl(ctx, y, xq, xs, pack, scales, M, N, K, epilogue, tern != 0);
 }

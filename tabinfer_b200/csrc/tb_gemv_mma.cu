@@ -472,6 +472,12 @@ int encode_2d(tb_ctx* ctx, CUtensorMap* map, const void* base, CUtensorMapDataTy
 
 }  // namespace
 
+int tb_encode_2d(tb_ctx* ctx, CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esize, int64_t cols,
+                 int64_t rows, int box_cols, int box_rows, CUtensorMapSwizzle swz)
+{
+    return encode_2d(ctx, map, base, dt, esize, cols, rows, box_cols, box_rows, swz);
+}
+
 size_t tb_gemv_mma_act_bytes(int64_t K, int batch)
 {
     const size_t ts = batch > 8 ? 16 : 8;

@@ -3,7 +3,13 @@
 // calls, for callers that own their buffers (the model runner records them into
 // one CUDA graph, so nothing may allocate).
 #pragma once
+#include <cuda.h>
 #include "tb_common.cuh"
+
+// 2-D TMA tensor map over a row-major [rows][cols] matrix of esize-byte elements,
+// box_cols x box_rows boxes (cuTensorMapEncodeTiled from the driver)
+int tb_encode_2d(tb_ctx* ctx, CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esize, int64_t cols,
+                 int64_t rows, int box_cols, int box_rows, CUtensorMapSwizzle swz);
 
 int tb_gemv_dp4a_impl(tb_ctx* ctx, int count, float* const* ys, const uint32_t* const* packs,
                       const uint16_t* const* scales, const int64_t* Ns, const float* x, const uint16_t* normw,
@@ -97,6 +103,10 @@ int tb_attn_prep_rows_impl(tb_ctx* ctx, const float* q, const float* k, const fl
 // int8 sums (tb_gemm_dp4.cu); M % 128, N % 128, K % 128; epilogue 0 store, 1 add, 2 SwiGLU
 int tb_gemm_dp4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
                      const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue, bool tern);
+// the same GEMM on the warp-level tensor-core MMA (mma.sync), kept as a second
+// implementation of the identical arithmetic (bit-equal outputs)
+int tb_gemm_dp4_warp_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
+                          const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue, bool tern);
 
 // the decode step as one persistent kernel (tb_step.cu): batch 1, one GPU
 struct tb_step_plan;

@@ -480,16 +480,19 @@ def attention_prefill_q8(q, kv, S, nHq, nKv, hd, out=None):
     return out
 
 
-def gemm_dp4(xq, xs, pack, scales, y=None, epilogue=0, tern=False):
+def gemm_dp4(xq, xs, pack, scales, y=None, epilogue=0, tern=False, warp=False):
     """gemmDP4A / gemmTern (qwen3.js:1321-1420) with exact per-group int8 sums, from
-    QUANTQ8T rows.  epilogue 0: y =, 1: y +=, 2: y = silu(y) * (X W^T)."""
+    QUANTQ8T rows.  epilogue 0: y =, 1: y +=, 2: y = silu(y) * (X W^T).  The
+    tcgen05 kind::i8 kernel; warp=True runs the warp-level mma.sync form of the
+    same arithmetic (bit-equal outputs)."""
     xq2 = xq.reshape(-1, xq.shape[-1])
     M, K = xq2.shape
     N = pack.shape[0]
     y = y if y is not None else torch.zeros((M, N), dtype=torch.float32, device=xq.device)
     c = _ctx(xq)
-    c.check(LIB.tb_gemm_dp4(c.h, _p(y), _p(xq2), _p(xs), _p(pack), _p(scales), M, N, K, int(epilogue),
-                            1 if tern else 0), "gemm_dp4")
+    fn = LIB.tb_gemm_dp4_warp if warp else LIB.tb_gemm_dp4
+    c.check(fn(c.h, _p(y), _p(xq2), _p(xs), _p(pack), _p(scales), M, N, K, int(epilogue), 1 if tern else 0),
+            "gemm_dp4_warp" if warp else "gemm_dp4")
     return y
 
 

@@ -121,6 +121,57 @@ def test_gemm_dp4_exact_ternary(cuda, M, N, K):
     assert _rms_err(y, ref) < 1e-5
 
 
+@pytest.mark.parametrize("tern", [False, True])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 1024), (640, 2048, 2048), (2048, 1024, 6144),
+                                   (1280, 1920, 640)])
+def test_gemm_dp4_tcgen05_equals_warp_form(cuda, M, N, K, tern):
+    """The tcgen05 kind::i8 kernel (raw nibbles / codes as unsigned bytes, the offset
+    removed through kc) and the mma.sync kernel (signed widened weights) compute the
+    same group sums and fold them in the same order: every output bit-equal, for
+    every epilogue.  (640, 2048) and (2048, 1024) give more tiles than SMs, so a CTA
+    runs several tiles through the same stage ring and TMEM slots; (1280, 1920, 640)
+    gives 150 tiles, two past one a SM."""
+    from helpers import tern_bf16
+    rng = np.random.default_rng(M + 7 * N + K + tern)
+    pack, sc = oracle.quant_tern_wgsl(tern_bf16(rng, N, K)) if tern else _weights(rng, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x[3, :64] = 0.0                       # zero groups: scale 0
+    x[5] *= 40.0                          # a row of large activations
+    xq, xs, _ = oracle.quant_q8(x)
+    args = (torch.from_numpy(xq).cuda(), torch.from_numpy(xs).cuda(), u32_dev(pack), u16_dev(sc))
+    y0 = rng.standard_normal((M, N)).astype(np.float32)
+    for epi in (0, 1, 2):
+        a = host(tb.gemm_dp4(*args, y=torch.from_numpy(y0.copy()).cuda(), epilogue=epi, tern=tern))
+        b = host(tb.gemm_dp4(*args, y=torch.from_numpy(y0.copy()).cuda(), epilogue=epi, tern=tern, warp=True))
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+    ref = (oracle.gemv_tern_wgsl_q8act if tern else oracle.gemv_int4_q8act)(xq, xs, pack, sc)
+    # each row against its own largest output (row 5's outputs are 40x the others')
+    y = host(tb.gemm_dp4(*args, tern=tern)).astype(np.float64)
+    assert np.max(np.abs(y - ref) / np.max(np.abs(ref), axis=1, keepdims=True)) < 1e-5
+
+
+def test_gemm_dp4_extreme_group_sums(cuda):
+    """Activations and weights at the ends of their ranges (xq = -127/+127, nibbles 0
+    and 15): the largest group sums, 32 * 127 * 8, stay exact through the offset
+    conversion; checked against the exact integer products in double."""
+    M, N, K = 128, 256, 512
+    rng = np.random.default_rng(77)
+    xq = np.where(rng.random((M, K)) < 0.5, -127, 127).astype(np.int8)
+    xq[0] = -127
+    xs = np.full((M, K // 32), 0.5, np.float32)
+    nib = np.where(rng.random((N, K)) < 0.5, 0, 15).astype(np.uint32)
+    nib[0] = 0
+    pack = np.zeros((N, K // 8), np.uint32)
+    for i in range(8):
+        pack |= nib[:, i::8] << (4 * i)
+    sc = np.full((N, K // 32), np.float16(0.25).view(np.uint16), np.uint16)
+    y = host(tb.gemm_dp4(torch.from_numpy(xq).cuda(), torch.from_numpy(xs).cuda(), u32_dev(pack), u16_dev(sc)))
+    w = nib.astype(np.float64) - 8.0
+    ref = (xq.astype(np.float64) @ w.T) * 0.125
+    np.testing.assert_allclose(y, ref, rtol=1e-6, atol=0)
+    assert y[0, 0] == 127 * 8 * K * 0.125
+
+
 def test_gemm_dp4_f16_within_rounding_budget(cuda):
     """The tcgen05 f16-operand form: every output within 2^-10 * sum |w x|."""
     M, N, K = 256, 512, 2048
