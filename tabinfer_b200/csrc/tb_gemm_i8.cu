@@ -12,13 +12,13 @@
 //
 // One kind::i8 MMA has K = 32: exactly one scale group.  Every MMA therefore
 // writes a fresh 128 x 128 int32 tile into one of four TMEM slots (512 columns),
-// and eight epilogue warps turn slot after slot into f32 while the tensor core
+// and sixteen epilogue warps turn slot after slot into f32 while the tensor core
 // fills the next ones.  The weights enter the MMA as raw unsigned nibbles (or
 // ternary codes 0..2) widened to bytes, so the MMA sums xq * nib; the offset is
 // removed in the int32 -> f32 conversion: as_float(S + kc) - 1.5 * 2^23 with
 // kc = 0x4B400000 - 8 * sum_k xq (ternary: - 1 * sum), exact for |S| < 2^22.
 //
-// Warp roles (448 threads, one CTA an SM, persistent over 128 x 128 tiles):
+// Warp roles (704 threads, one CTA an SM, persistent over 128 x 128 tiles):
 //   warp 0      one thread issues the TMA copies of a k-step (128 k): the X tile
 //               (128 rows x 128 int8, 128-byte swizzle, exactly the layout the
 //               MMA descriptor reads) and the raw packed weight tile;
@@ -27,9 +27,11 @@
 //               ones), stage xs and the f16 weight scales as f32;
 //   warp 5      owns TMEM; one thread issues four MMAs a k-step, each into its
 //               group slot, and commits each slot to the epilogue;
-//   warps 6-13  read a slot (32 TMEM lanes = rows x 64 columns per warp), release
-//               it, and fold it into 64 f32 accumulators a thread; after the last
-//               k-step of a tile they apply the epilogue and store the rows.
+//   warps 6-21  read a slot (32 TMEM lanes = rows x 32 columns per warp, one
+//               TMEM load), release it, and fold it into 32 f32 accumulators a
+//               thread; after the last k-step of a tile they apply the epilogue and
+//               store the rows (four of them a scheduler: 1.02x the throughput of
+//               two with 64 columns each).
 // The f32 folding is the bound (2.5 packed-f32 instructions an output per 32
 // MACs), so the MMA and the operand staging run on other warps.
 // Every wait is bounded: a wait that gives up records ERR_I8_WAIT in the context's
@@ -49,8 +51,14 @@ constexpr int STAGE = A_BYTES + B_BYTES + RAW_BYTES + WS_BYTES + XK_BYTES;
 static_assert(STAGE % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
 constexpr int SMEM = 1024 + NST * STAGE + 256;
 static_assert(SMEM <= 227 * 1024, "shared memory");
-constexpr int W_TMA = 0, W_WIDEN = 1, N_WIDEN = 4, W_MMA = 5, W_EPI = 6, N_EPI = 8;
+constexpr int W_TMA = 0, W_WIDEN = 1, N_WIDEN = 4, W_MMA = 5, W_EPI = 6, N_EPI = 16;
 constexpr int THREADS = (W_EPI + N_EPI) * 32;
+constexpr int EPI_COLS = BN * 4 / N_EPI;                      // columns a warp folds (4 lane quarters)
+static_assert(EPI_COLS % 32 == 0, "whole 32-column TMEM loads");
+// registers are allocated per scheduler (16384 each): 22 warps put 6 on some of
+// them, so 6 x 32 x MAX_REGS must fit
+constexpr int MAX_REGS = 80;
+static_assert(((THREADS / 32 + 3) / 4) * 32 * MAX_REGS <= 16384, "registers per scheduler");
 constexpr int NSLOT = NG, TMEM_COLS = NSLOT * BN;             // one 128-column slot a group
 static_assert(TMEM_COLS == 512, "TMEM");
 constexpr int WAIT_TRIES = 1000;       // x a 1 ms suspend hint per try: at most ~1 s a wait
@@ -178,7 +186,7 @@ __device__ __forceinline__ Step step_of(const I8Args& a, int it, int nk)
 }
 
 template <bool TERN>
-__global__ void __launch_bounds__(THREADS, 1) k_gemm_i8(const __grid_constant__ I8Args a)
+__global__ void __maxnreg__(MAX_REGS) k_gemm_i8(const __grid_constant__ I8Args a)
 {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -330,12 +338,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_i8(const __grid_constant__ 
             if (!mbar_wait(done, 0, nullptr)) give_up(abort_flag, a.err);   // no MMA in flight past here
         }
     } else {
-        // ---- epilogue: TMEM lanes 32q.. (tile rows), columns 64h..64h+63
+        // ---- epilogue: TMEM lanes 32q.. (tile rows), columns EPI_COLS*h ..
         const int q = warp & 3, h = (warp - W_EPI) >> 2, rl = 32 * q + lane;
         const float2 M2 = make_float2(-12582912.f, -12582912.f);
-        float2 acc[32];
+        float2 acc[EPI_COLS / 2];
 #pragma unroll
-        for (int i = 0; i < 32; i++) acc[i] = make_float2(0.f, 0.f);
+        for (int i = 0; i < EPI_COLS / 2; i++) acc[i] = make_float2(0.f, 0.f);
         for (int it = 0; it < total; it++) {
             const int s = it % NST;
             const Step st = step_of(a, it, nk);
@@ -359,11 +367,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_i8(const __grid_constant__ 
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                for (int j = 0; j < 2; j++) {
+                for (int j = 0; j < EPI_COLS / 32; j++) {
                     uint32_t r[32];
-                    tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(BN * g + 64 * h + 32 * j), r);
+                    tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(BN * g + EPI_COLS * h + 32 * j), r);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    const float4* wp = reinterpret_cast<const float4*>(WS + g * BN + 64 * h + 32 * j);
+                    const float4* wp = reinterpret_cast<const float4*>(WS + g * BN + EPI_COLS * h + 32 * j);
 #pragma unroll
                     for (int c = 0; c < 8; c++) {
                         const float4 w = wp[c];
@@ -387,9 +395,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_i8(const __grid_constant__ 
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (st.ks == nk - 1) {
-                float4* yp = reinterpret_cast<float4*>(a.y + (size_t)(st.m0 + rl) * a.N + st.n0 + 64 * h);
+                float4* yp = reinterpret_cast<float4*>(a.y + (size_t)(st.m0 + rl) * a.N + st.n0 + EPI_COLS * h);
 #pragma unroll
-                for (int c = 0; c < 16; c++) {
+                for (int c = 0; c < EPI_COLS / 4; c++) {
                     float4 v = make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
                     if (a.epi == 1) {          // fused residual: y += X W^T
                         const float4 o = yp[c];
