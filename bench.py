@@ -1427,7 +1427,8 @@ def run_only(name, steps):
         stream = torch.cuda.current_stream(dev)
         mp = os.path.join(REPO, "MEASURED_PEAKS.json")
         bf16 = json.load(open(mp)).get("bf16_tflops", 1590.0) if os.path.exists(mp) else 1590.0
-        out = {"gemm_exact": prefill_exact_extra(dev, bf16, stream), "forward": prefill_forward_extra(dev, stream)}
+        out = {"gemm_f16": prefill_extra(dev, bf16, stream), "gemm_exact": prefill_exact_extra(dev, bf16, stream),
+               "forward": prefill_forward_extra(dev, stream)}
     elif name == "chain":
         out = {}
         for B in (1, 4, 8):

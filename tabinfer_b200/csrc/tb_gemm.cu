@@ -1,60 +1,57 @@
 // tb_gemm.cu -- prefill GEMM Y[M,N] (+)= f16(X[M,K]) . f16(deq(W[N,K]))^T on the
-// 5th-generation tensor cores (tcgen05.mma kind::f16, f32 accumulator in TMEM).
+// 5th-generation tensor cores (tcgen05.mma kind::f16, f32 accumulators in TMEM).
 //
 // The math is the reference's f16 prefill GEMM (gemmqWgsl / gemmQ,
 // models/qwen3.js:964-1026): every activation is rounded to f16, every weight is
 // dequantized as f16((nib - 8) * f16 scale) (one rounding of the exact product),
 // and the products are summed in f32.
 //
-// CTA tile 128 (M) x 256 (N), K in steps of 64.  Warps 0-15 are producers: each
-// thread cp.asyncs its share of the raw 128 x 64 block of X (f32 or bf16) and of
-// the 256 x 64 block of packed int4 weights + f16 scales a few k-steps ahead,
-// then converts its share to f16 and writes it into shared memory in the
-// 128-byte-swizzled K-major layout the tensor core reads (8-row x 128-byte
-// atoms).  Warp 16 allocates 256 TMEM columns and one of its threads issues four
-// 128x256x16 MMAs per stage; tcgen05.commit frees the stage when they complete.
+// X is rounded to f16 once, by a pre-pass into context scratch (f32 or bf16 rows,
+// or QUANTQ8T rows as f16(xs * q)), padded with zero rows to a whole tile, so the
+// A tiles arrive by TMA in the 128-byte swizzle the MMA descriptor reads, with no
+// conversion work inside the GEMM.  CTA tile 256 (M) x 256 (N), K in steps of 64:
+// each dequantized weight tile (the producer work, fused here) feeds two
+// 128 x 256 x 16 MMAs per k16 -- one per 128-row half of the X tile -- into two
+// 256-column f32 accumulators (all 512 TMEM columns), so a weight is dequantized
+// once per 256 rows of X.  Warps 0-15 are producers: each thread cp.asyncs its
+// share of the raw packed weights + f16 scales NR-1 k-steps ahead and writes it
+// dequantized into the swizzled B tile; warp 16 owns TMEM and one of its threads
+// issues the MMAs; one thread of warp 17 issues the X tile copies.  After the last
+// stage warps 0-15 read the accumulators (warp w: TMEM lanes 32*(w%4).., columns
+// 64*(w/4).. of both) and store f32 rows.
 // Ternary weights in the WebGPU layout (gemmTern, qwen3.js:1410-1420) use the
-// same pipeline with the operands of that GEMM: X arrives as QUANTQ8T int8 rows
-// with per-32 f32 scales and becomes f16(xs * q); a weight becomes the exact
-// f16 (c - 1) * s.  (The reference sums the int8 products of a group exactly
-// and scales once per group; here f16(xs * q) rounds each activation to 11
-// bits, ~1e-4 of a row's scale.)
-// After the last stage warps 0-15 read the accumulator (tcgen05.ld, warp w owns
-// TMEM lanes 32*(w%4)..+31 and columns 64*(w/4)..+63) and store f32 rows.  Waits are bounded: on a timeout the CTA records
-// ERR_GEMM_WAIT, stops issuing, and still frees its TMEM.
+// same pipeline with the operands of that GEMM: X as QUANTQ8T int8 rows with
+// per-32 f32 scales becomes f16(xs * q); a weight becomes the exact f16
+// (c - 1) * s.  (The reference sums the int8 products of a group exactly and
+// scales once per group; here f16(xs * q) rounds each activation to 11 bits,
+// ~1e-4 of a row's scale.)  Waits are bounded: on a timeout the CTA records
+// ERR_GEMM_WAIT, stops issuing, waits for its copies, and still frees its TMEM.
 #include "tb_internal.h"
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int PROD_WARPS = 16, PROD = PROD_WARPS * 32, THREADS = PROD + 32;
-constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE = A_BYTES + B_BYTES;
-// raw staging ring, filled with cp.async NR-1 k-steps ahead of the conversion:
-// X as given (bf16 or f32), packed W, W scales; chunk-major (16-byte chunk c of
-// producer thread t at c * PROD + t) so copies and reads are bank-conflict free
-constexpr int RAW_W = PROD * 16, RAW_S = PROD * 4;
-// X operand: f32 / bf16 rows (gemmQ), or QUANTQ8T int8 rows + f32 group scales
-// (gemmDP4A and gemmTern); W: int4, or ternary for X_Q8_TERN
-enum XMode { X_F32 = 0, X_BF16 = 1, X_Q8_TERN = 2, X_Q8_INT4 = 3 };
-template <int MODE> struct Cfg {
-    static constexpr bool TERN = MODE == X_Q8_TERN;
-    static constexpr bool XQ8 = MODE == X_Q8_TERN || MODE == X_Q8_INT4;
-    static constexpr int XC = MODE == X_F32 ? 4 : (MODE == X_BF16 ? 2 : 1);   // raw X chunks per producer thread
-    static constexpr int XS = XQ8 ? PROD * 4 : 0;            // int8 rows: one f32 group scale per thread
-    static constexpr int X = PROD * XC * 16 + XS;
-    static constexpr int WB = TERN ? PROD * 8 : RAW_W;       // raw weight bytes (ternary: 2 words per thread)
-    static constexpr int RSTAGE = X + WB + RAW_S;
-    static constexpr int NST = MODE == X_F32 ? 2 : 3;        // MMA operand stages
-    static constexpr int NR = 3;                             // raw stages
-    static constexpr int SMEM = 1024 + NST * STAGE + NR * RSTAGE + 256;
-};
-constexpr int TMEM_COLS = 256;
+constexpr int BM = 256, BN = 256, BK = 64, MMA_M = 128;   // BM: the largest tile (HM = 2 row halves)
+constexpr int PROD_WARPS = 16, PROD = PROD_WARPS * 32;
+constexpr int W_MMA = PROD_WARPS, W_TMA = PROD_WARPS + 1, THREADS = PROD + 64;
+// per k-step stage: HM row halves of X (16 KB each) + the weight tile (32 KB)
+template <int HM> constexpr int a_bytes() { return HM * MMA_M * BK * 2; }
+constexpr int B_BYTES = BN * BK * 2;
+template <int HM> constexpr int stage_bytes() { return a_bytes<HM>() + B_BYTES; }
+constexpr int NST = 3;   // MMA operand stages
+constexpr int NR = 3;    // raw weight stages, filled NR-1 k-steps ahead of the dequant
+// raw staging, thread-major: packed W (int4 16 bytes = one 32-group a thread;
+// ternary 8 bytes), then the row's two f16 group scales of the k-step (4 bytes)
+constexpr int RAW_W = PROD * 16, RAW_S = PROD * 4, RSTAGE = RAW_W + RAW_S;
+template <int HM> constexpr int smem_bytes() { return 1024 + NST * stage_bytes<HM>() + NR * RSTAGE + 256; }
+static_assert(smem_bytes<2>() <= 227 * 1024, "shared memory");
+constexpr int TMEM_COLS = 512;   // two 256-column f32 accumulators
 constexpr int GEMM_WAIT_TRIES = 1000;      // x a 1 ms suspend bound per try: at most ~1 s
 constexpr int ERR_GEMM_WAIT = 0x6b01;
+// X as given: f32 / bf16 rows (gemmQ), or QUANTQ8T int8 rows + f32 group scales
+enum XMode { X_F32 = 0, X_BF16 = 1, X_Q8 = 2 };
 
 struct GemmArgs {
-    const void* x;          // [M][K] f32, bf16 or int8 (ternary mode)
-    const float* xs;        // [M][K/32] group scales of int8 rows (ternary mode)
+    CUtensorMap tx;         // f16 X [Mpad][K] (the pre-pass output), box 64 x 256, 128-byte swizzle
     const uint32_t* pack;   // [N][K/8] int4, or [N][K/16] ternary codes
     const uint16_t* scales; // [N][K/32] f16
     float* y;               // [M][N]
@@ -95,8 +92,9 @@ __device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr)
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N = BN, M = BM
-constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N = BN, M = 128
+constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(MMA_M >> 4) << 24);
 
 // byte offset of 16-byte chunk c (0..7) of row r in a swizzled K-major tile
 __device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
@@ -182,30 +180,79 @@ __device__ __forceinline__ void q8x4_scaled(uint32_t w, float xs, float2& a, flo
     b = make_float2(__fmul_rn(b.x, S2.x), __fmul_rn(b.y, S2.y));
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes)
 {
-    using R = Cfg<MODE>;
-    constexpr bool XBF16 = MODE == X_BF16, TERN = R::TERN, XQ8 = R::XQ8;
-    constexpr int NST = R::NST;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// X -> f16 rows [Mpad][K], rows M.. zero: 8 elements (16 bytes out) a thread, grid-stride
+template <int MODE>
+__global__ void __launch_bounds__(256) k_x_f16(const void* __restrict__ x, const float* __restrict__ xs,
+                                               uint4* __restrict__ out, long long n8, long long n8_valid)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n8; i += (long long)gridDim.x * 256) {
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+        if (i < n8_valid) {
+            if (MODE == X_F32) {
+                const float4 u = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
+                const float4 v = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+                o = make_uint4(f32x2_to_f16x2(u.x, u.y), f32x2_to_f16x2(u.z, u.w), f32x2_to_f16x2(v.x, v.y),
+                               f32x2_to_f16x2(v.z, v.w));
+            } else if (MODE == X_BF16) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(x) + i);
+                const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+                uint32_t r[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    r[j] = f32x2_to_f16x2(__uint_as_float(in[j] << 16), __uint_as_float(in[j] & 0xFFFF0000u));
+                o = make_uint4(r[0], r[1], r[2], r[3]);
+            } else {
+                const uint2 q = __ldg(reinterpret_cast<const uint2*>(x) + i);
+                const float xsc = __ldg(xs + ((8 * i) >> 5));   // [M][K/32]: element e's group is e / 32
+                float2 p0, p1, p2, p3;
+                q8x4_scaled(q.x, xsc, p0, p1);
+                q8x4_scaled(q.y, xsc, p2, p3);
+                o = make_uint4(f32x2_to_f16x2(p0.x, p0.y), f32x2_to_f16x2(p1.x, p1.y), f32x2_to_f16x2(p2.x, p2.y),
+                               f32x2_to_f16x2(p3.x, p3.y));
+            }
+        }
+        out[i] = o;
+    }
+}
+
+template <bool TERN, int HM>
+__global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__ GemmArgs a)
+{
+    constexpr int A_BYTES = a_bytes<HM>(), STAGE = stage_bytes<HM>();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* base = smem_raw + (((raw + 1023) & ~1023u) - raw);
     uint8_t* rawbase = base + NST * STAGE;
-    uint64_t* full = reinterpret_cast<uint64_t*>(rawbase + R::NR * R::RSTAGE);
-    uint64_t* empty = full + NST;
+    uint64_t* full = reinterpret_cast<uint64_t*>(rawbase + NR * RSTAGE);   // B dequantized + X tile landed
+    uint64_t* empty = full + NST;                                          // stage consumed by the MMAs
     uint64_t* done = empty + NST;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < NST; s++) { mbar_init(&full[s], PROD_WARPS); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < NST; s++) {
+            mbar_init(&full[s], PROD_WARPS + 1);   // the producer warps + the X copy's expect_tx arrival
+            mbar_init(&empty[s], 1);
+        }
         mbar_init(done, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == PROD_WARPS) {
+    if (warp == W_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
                      "r"(TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -217,96 +264,49 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
     tb_pdl_wait();
     tb_pdl_trigger();
 
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN, nk = a.K / BK;
+    const int m0 = blockIdx.y * (MMA_M * HM), n0 = blockIdx.x * BN, nk = a.K / BK;
     if (warp < PROD_WARPS) {
-        // ---- producers: X rows (4 threads a row, 16 k each), W rows (2 threads a
-        // row, one 32-group each).  Each thread copies its own raw bytes
-        // (cp.async, NR-1 k-steps ahead) and converts only those, so no barrier
-        // is needed between copy and convert.
-        const int xr = tid >> 2, xq = tid & 3;
+        // ---- producers: W rows (2 threads a row, one 32-group each).  Each thread
+        // copies its own raw bytes (cp.async, NR-1 k-steps ahead) and dequantizes
+        // only those, so no barrier is needed between copy and dequant.
         const int wr = tid >> 1, wh = tid & 1;
         auto fetch = [&](int i) {
             if (i < nk) {
-                uint8_t* rs = rawbase + (i % R::NR) * R::RSTAGE;
+                uint8_t* rs = rawbase + (i % NR) * RSTAGE;
                 const int k0 = i * BK;
-                const uint8_t* xs = static_cast<const uint8_t*>(a.x) +
-                                    ((size_t)(m0 + xr) * a.K + k0 + 16 * xq) * (MODE == X_F32 ? 4 : (XBF16 ? 2 : 1));
-#pragma unroll
-                for (int c = 0; c < R::XC; c++) cp16(rs + (c * PROD + tid) * 16, xs + 16 * c);
-                if (XQ8) cp4(rs + PROD * 16 + tid * 4, a.xs + (size_t)(m0 + xr) * (a.K / 32) + k0 / 32 + (xq >> 1));
                 if (TERN) {
-                    cp8(rs + R::X + tid * 8, a.pack + (size_t)(n0 + wr) * (a.K / 16) + k0 / 16 + 2 * wh);
+                    cp8(rs + tid * 8, a.pack + (size_t)(n0 + wr) * (a.K / 16) + k0 / 16 + 2 * wh);
                 } else {
-                    cp16(rs + R::X + tid * 16, a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8 + 4 * wh);
+                    cp16(rs + tid * 16, a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8 + 4 * wh);
                 }
-                cp4(rs + R::X + R::WB + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32);
+                cp4(rs + RAW_W + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32);
             }
             cp_commit();   // a group per k-step, empty past the end, keeps the count uniform
         };
-        for (int i = 0; i < R::NR - 1; i++) fetch(i);
+        for (int i = 0; i < NR - 1; i++) fetch(i);
         for (int i = 0; i < nk; i++) {
-            fetch(i + R::NR - 1);
-            cp_wait<R::NR - 1>();        // this thread's raw bytes of k-step i have landed
+            fetch(i + NR - 1);
+            cp_wait<NR - 1>();        // this thread's raw bytes of k-step i have landed
             const int s = i % NST;
             if (!mbar_wait(&empty[s], ((i / NST) & 1) ^ 1)) {
                 *abort_flag = 1;
                 atomicExch(a.err, ERR_GEMM_WAIT);
             }
             if (*abort_flag) break;
-            uint8_t* A = base + s * STAGE;
-            uint8_t* Bt = A + A_BYTES;
-            const uint8_t* rs = rawbase + (i % R::NR) * R::RSTAGE;
-            // X: 16 values of row xr -> f16 chunks 2 xq, 2 xq + 1
-            if (XQ8) {
-                const uint4 v = *reinterpret_cast<const uint4*>(rs + tid * 16);
-                const float xsc = *reinterpret_cast<const float*>(rs + PROD * 16 + tid * 4);
-                const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-                uint32_t o[8];
+            uint8_t* Bt = base + s * STAGE + A_BYTES;
+            const uint8_t* rs = rawbase + (i % NR) * RSTAGE;
+            const uint32_t sc = *reinterpret_cast<const uint32_t*>(rs + RAW_W + tid * 4);
+            const uint32_t s2 = (wh ? (sc >> 16) : (sc & 0xFFFFu)) * 0x10001u;
+            if (TERN) {
+                const uint2 w2 = *reinterpret_cast<const uint2*>(rs + tid * 8);
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    float2 p, q;
-                    q8x4_scaled(in[j], xsc, p, q);
-                    o[2 * j] = f32x2_to_f16x2(p.x, p.y);
-                    o[2 * j + 1] = f32x2_to_f16x2(q.x, q.y);
-                }
-                *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq)) = make_uint4(o[0], o[1], o[2], o[3]);
-                *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-            } else if (XBF16) {
-#pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(rs + (c * PROD + tid) * 16);
-                    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-                    uint32_t o[4];
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        o[j] = f32x2_to_f16x2(__uint_as_float(in[j] << 16), __uint_as_float(in[j] & 0xFFFF0000u));
-                    *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq + c)) = make_uint4(o[0], o[1], o[2], o[3]);
-                }
+                for (int c = 0; c < 4; c++)
+                    *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_tern8(c < 2 ? w2.x : w2.y, c & 1, s2);
             } else {
+                const uint4 w4 = *reinterpret_cast<const uint4*>(rs + tid * 16);
+                const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    const float4 u = *reinterpret_cast<const float4*>(rs + ((2 * c) * PROD + tid) * 16);
-                    const float4 v = *reinterpret_cast<const float4*>(rs + ((2 * c + 1) * PROD + tid) * 16);
-                    *reinterpret_cast<uint4*>(A + sw128(xr, 2 * xq + c)) =
-                        make_uint4(f32x2_to_f16x2(u.x, u.y), f32x2_to_f16x2(u.z, u.w), f32x2_to_f16x2(v.x, v.y),
-                                   f32x2_to_f16x2(v.z, v.w));
-                }
-            }
-            // W: 32 weights of row wr, group wh of the k-step
-            {
-                const uint32_t sc = *reinterpret_cast<const uint32_t*>(rs + R::X + R::WB + tid * 4);
-                const uint32_t s2 = (wh ? (sc >> 16) : (sc & 0xFFFFu)) * 0x10001u;
-                if (TERN) {
-                    const uint2 w2 = *reinterpret_cast<const uint2*>(rs + R::X + tid * 8);
-#pragma unroll
-                    for (int c = 0; c < 4; c++)
-                        *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_tern8(c < 2 ? w2.x : w2.y, c & 1, s2);
-                } else {
-                    const uint4 w4 = *reinterpret_cast<const uint4*>(rs + R::X + tid * 16);
-                    const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-                    for (int c = 0; c < 4; c++) *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_word(ws[c], s2);
-                }
+                for (int c = 0; c < 4; c++) *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_word(ws[c], s2);
             }
             // generic-proxy writes -> visible to the tensor core (async proxy)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -314,8 +314,26 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
             if (lane == 0) mbar_arrive(&full[s]);
         }
         cp_wait<0>();   // no copy in flight when the CTA leaves
+    } else if (warp == W_TMA) {
+        if (lane == 0) {
+            // ---- the X tiles: 128 HM rows x 64 f16 a k-step, one tensor copy
+            int issued = 0;
+            for (int i = 0; i < nk; i++) {
+                const int s = i % NST;
+                if (!mbar_wait(&empty[s], ((i / NST) & 1) ^ 1)) {
+                    *abort_flag = 1;
+                    atomicExch(a.err, ERR_GEMM_WAIT);
+                }
+                if (*abort_flag) break;
+                mbar_expect_tx(&full[s], (uint32_t)A_BYTES);
+                tma_2d(base + s * STAGE, &a.tx, i * BK, m0, &full[s]);
+                issued = i + 1;
+            }
+            // no copy may land after the CTA has left: wait for the last stages issued
+            for (int i = issued > NST ? issued - NST : 0; i < issued; i++) mbar_wait(&full[i % NST], (i / NST) & 1);
+        }
     } else if (lane == 0) {
-        // ---- MMA issuer
+        // ---- MMA issuer: per k16, rows 0-127 into columns 0-255, rows 128-255 into 256-511
         for (int i = 0; i < nk; i++) {
             const int s = i % NST;
             if (!mbar_wait(&full[s], (i / NST) & 1)) {
@@ -327,11 +345,16 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
             const uint32_t A = smem_u32(base + s * STAGE), Bt = A + A_BYTES;
 #pragma unroll
             for (int kk = 0; kk < BK / 16; kk++) {
-                const uint64_t da = kmajor_sw128_desc(A + kk * 32), db = kmajor_sw128_desc(Bt + kk * 32);
+                const uint64_t db = kmajor_sw128_desc(Bt + kk * 32);
                 const uint32_t accum = (i > 0 || kk > 0) ? 1u : 0u;
-                asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                             " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}"
-                             ::"r"(tmem), "l"(da), "l"(db), "r"(IDESC), "r"(accum), "r"(0u) : "memory");
+#pragma unroll
+                for (int hm = 0; hm < HM; hm++) {
+                    const uint64_t da = kmajor_sw128_desc(A + hm * (MMA_M * 128) + kk * 32);
+                    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}"
+                                 ::"r"(tmem + (uint32_t)(hm * BN)), "l"(da), "l"(db), "r"(IDESC), "r"(accum), "r"(0u)
+                                 : "memory");
+                }
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                          ::"r"(smem_u32(&empty[s])) : "memory");
@@ -340,71 +363,111 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_int4(const GemmArgs a)
                      ::"r"(smem_u32(done)) : "memory");
     }
 
+    if (warp == W_MMA && lane == 0) mbar_wait(done, 0);   // every MMA completed before TMEM is freed
     if (warp < PROD_WARPS) {
-        // ---- epilogue: this warp's 32 TMEM lanes (rows) x 128 columns
-        const bool ok = mbar_wait(done, 0) && !*abort_flag;
-        if (!ok) atomicExch(a.err, ERR_GEMM_WAIT);
+        // ---- epilogue: this warp's 32 TMEM lanes x 64 columns of both accumulators
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0) && !*abort_flag);
+        __syncwarp();
+        if (!ok && lane == 0) atomicExch(a.err, ERR_GEMM_WAIT);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok) {
             const int q = warp & 3, h = warp >> 2;      // TMEM lanes 32q.., columns 64h..
-            const int row = m0 + 32 * q + lane;
-            float* yrow = a.y + (size_t)row * a.N + n0 + 64 * h;
 #pragma unroll 1
-            for (int j = 0; j < 2; j++) {
-                uint32_t r[32];
-                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(64 * h + 32 * j);
-                asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-                             "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                               "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-                               "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-                               "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-                               "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                             : "r"(taddr));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                float4* yp = reinterpret_cast<float4*>(yrow + 32 * j);
+            for (int hm = 0; hm < HM; hm++) {
+                const int row = m0 + hm * MMA_M + 32 * q + lane;
+                float* yrow = a.y + (size_t)row * a.N + n0 + 64 * h;
+#pragma unroll 1
+                for (int j = 0; j < 2; j++) {
+                    uint32_t r[32];
+                    const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(hm * BN + 64 * h + 32 * j);
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+                                 "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                                   "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+                                   "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+                                   "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+                                   "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                                 : "r"(taddr));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    if (row >= a.M) continue;   // zero padding rows of the last tile
+                    float4* yp = reinterpret_cast<float4*>(yrow + 32 * j);
 #pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    float4 v = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
-                                           __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
-                    if (a.acc == 1) {          // fused residual: y += X W^T
-                        const float4 o = yp[c];
-                        v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-                    } else if (a.acc == 2) {   // fused SwiGLU: y holds gate, y = silu(gate) * (X W_up^T)
-                        const float4 gt = yp[c];
-                        v.x = __fdiv_rn(gt.x, 1.0f + expf(-gt.x)) * v.x;
-                        v.y = __fdiv_rn(gt.y, 1.0f + expf(-gt.y)) * v.y;
-                        v.z = __fdiv_rn(gt.z, 1.0f + expf(-gt.z)) * v.z;
-                        v.w = __fdiv_rn(gt.w, 1.0f + expf(-gt.w)) * v.w;
+                    for (int c = 0; c < 8; c++) {
+                        float4 v = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                                               __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
+                        if (a.acc == 1) {          // fused residual: y += X W^T
+                            const float4 o = yp[c];
+                            v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+                        } else if (a.acc == 2) {   // fused SwiGLU: y holds gate, y = silu(gate) * (X W_up^T)
+                            const float4 gt = yp[c];
+                            v.x = __fdiv_rn(gt.x, 1.0f + expf(-gt.x)) * v.x;
+                            v.y = __fdiv_rn(gt.y, 1.0f + expf(-gt.y)) * v.y;
+                            v.z = __fdiv_rn(gt.z, 1.0f + expf(-gt.z)) * v.z;
+                            v.w = __fdiv_rn(gt.w, 1.0f + expf(-gt.w)) * v.w;
+                        }
+                        yp[c] = v;
                     }
-                    yp[c] = v;
                 }
             }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == PROD_WARPS) {
+    if (warp == W_MMA) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
     }
 }
 
-template <int MODE>
-int launch_gemm(tb_ctx* ctx, const GemmArgs& a)
+template <bool TERN, int HM>
+int launch_gemm(tb_ctx* ctx, const GemmArgs& a, int64_t M)
 {
     static bool attr_set[64] = {};
     if (ctx->device >= 64 || !attr_set[ctx->device]) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_int4<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg<MODE>::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_f16<TERN, HM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem_bytes<HM>());
         if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm attribute: %s", cudaGetErrorString(e));
         if (ctx->device < 64) attr_set[ctx->device] = true;
     }
-    static_assert(Cfg<MODE>::SMEM <= 227 * 1024, "shared memory");
-    cudaError_t e = tb_launch(ctx, k_gemm_int4<MODE>, dim3(a.N / BN, a.M / BM), dim3(THREADS),
-                              (size_t)Cfg<MODE>::SMEM, a);
+    const unsigned rows = (unsigned)((M + MMA_M * HM - 1) / (MMA_M * HM));
+    cudaError_t e = tb_launch(ctx, k_gemm_f16<TERN, HM>, dim3(a.N / BN, rows), dim3(THREADS),
+                              (size_t)smem_bytes<HM>(), a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
     return TB_OK;
+}
+
+// X rounded to f16 into context scratch ([Mpad][K], zero rows past M), then the GEMM
+int run_gemm(tb_ctx* ctx, float* y, const void* x, int mode, const float* xs, const uint32_t* pack,
+             const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc, bool tern)
+{
+    const int64_t Mpad = (M + BM - 1) / BM * BM;
+    uint4* xf = static_cast<uint4*>(tb_ctx_scratch(ctx, (size_t)(Mpad * K * 2)));
+    if (!xf) return TB_ERR_NOMEM;
+    const long long n8 = Mpad * K / 8, n8v = M * K / 8;
+    const long long want = (n8 + 255) / 256, cap = (long long)ctx->num_sms * 16;
+    const dim3 grid((unsigned)(want < cap ? want : cap));
+    cudaError_t e;
+    if (mode == X_F32) e = tb_launch(ctx, k_x_f16<X_F32>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
+    else if (mode == X_BF16) e = tb_launch(ctx, k_x_f16<X_BF16>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
+    else e = tb_launch(ctx, k_x_f16<X_Q8>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm x pass launch: %s", cudaGetErrorString(e));
+    // two 128-row halves a CTA (each weight tile dequantized once per 256 rows)
+    // unless that leaves SMs idle; then one
+    const int hm = ((M + BM - 1) / BM) * (N / BN) >= ctx->num_sms ? 2 : 1;
+    GemmArgs a{};
+    const int rc = tb_encode_2d(ctx, &a.tx, xf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, Mpad, BK, MMA_M * hm,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    a.pack = pack;
+    a.scales = scales;
+    a.y = y;
+    a.M = (int)M;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.acc = acc;
+    a.err = ctx->dev_error;
+    if (hm == 2) return tern ? launch_gemm<true, 2>(ctx, a, M) : launch_gemm<false, 2>(ctx, a, M);
+    return tern ? launch_gemm<true, 1>(ctx, a, M) : launch_gemm<false, 1>(ctx, a, M);
 }
 
 }  // namespace
@@ -413,14 +476,13 @@ int tb_gemm_int4_impl(tb_ctx* ctx, float* y, const void* x, int x_bf16, const ui
                       int64_t M, int64_t N, int64_t K, int acc)
 {
     TB_REQUIRE(ctx, y && x && pack && scales, "null pointer");
-    TB_REQUIRE(ctx, M > 0 && M % BM == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
-               "gemm_int4: M %% %d, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BM, BN, BK,
+    TB_REQUIRE(ctx, M > 0 && M % 128 == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
+               "gemm_int4: M %% 128, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BN, BK,
                (long long)M, (long long)N, (long long)K);
-    TB_REQUIRE(ctx, M / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_int4: shape too large");
+    TB_REQUIRE(ctx, (M + BM - 1) / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_int4: shape too large");
     TB_REQUIRE(ctx, TB_ALIGNED(x, 16) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) && TB_ALIGNED(y, 16),
                "gemm_int4: x, pack, y 16-byte and scales 4-byte aligned");
-    GemmArgs a{x, nullptr, pack, scales, y, (int)M, (int)N, (int)K, acc ? 1 : 0, ctx->dev_error};
-    return x_bf16 ? launch_gemm<X_BF16>(ctx, a) : launch_gemm<X_F32>(ctx, a);
+    return run_gemm(ctx, y, x, x_bf16 ? X_BF16 : X_F32, nullptr, pack, scales, M, N, K, acc ? 1 : 0, false);
 }
 
 // gemmDP4A (qwen3.js:1232-1400, linearQ's default prefill route) on the tensor
@@ -430,32 +492,30 @@ int tb_gemm_q8_int4_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* x
                          const uint16_t* scales, int64_t M, int64_t N, int64_t K, int epilogue)
 {
     TB_REQUIRE(ctx, y && xq && xs && pack && scales, "null pointer");
-    TB_REQUIRE(ctx, M > 0 && M % BM == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
-               "gemm_q8: M %% %d, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BM, BN, BK,
+    TB_REQUIRE(ctx, M > 0 && M % 128 == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
+               "gemm_q8: M %% 128, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BN, BK,
                (long long)M, (long long)N, (long long)K);
-    TB_REQUIRE(ctx, M / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_q8: shape too large");
+    TB_REQUIRE(ctx, (M + BM - 1) / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_q8: shape too large");
     TB_REQUIRE(ctx, epilogue >= 0 && epilogue <= 2, "gemm_q8: bad epilogue %d", epilogue);
     TB_REQUIRE(ctx, TB_ALIGNED(xq, 16) && TB_ALIGNED(xs, 4) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) &&
                         TB_ALIGNED(y, 16),
                "gemm_q8: xq, pack, y 16-byte and xs, scales 4-byte aligned");
-    GemmArgs a{xq, xs, pack, scales, y, (int)M, (int)N, (int)K, epilogue, ctx->dev_error};
-    return launch_gemm<X_Q8_INT4>(ctx, a);
+    return run_gemm(ctx, y, xq, X_Q8, xs, pack, scales, M, N, K, epilogue, false);
 }
 
 int tb_gemm_tern_wgsl_impl(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
                            const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc)
 {
     TB_REQUIRE(ctx, y && xq && xs && pack && scales, "null pointer");
-    TB_REQUIRE(ctx, M > 0 && M % BM == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
-               "gemm_tern: M %% %d, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BM, BN, BK,
+    TB_REQUIRE(ctx, M > 0 && M % 128 == 0 && N > 0 && N % BN == 0 && K > 0 && K % BK == 0,
+               "gemm_tern: M %% 128, N %% %d and K %% %d must be 0 (got %lld x %lld x %lld)", BN, BK,
                (long long)M, (long long)N, (long long)K);
-    TB_REQUIRE(ctx, M / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_tern: shape too large");
+    TB_REQUIRE(ctx, (M + BM - 1) / BM <= 65535 && K < (1LL << 30) && N * K < (1LL << 40), "gemm_tern: shape too large");
     TB_REQUIRE(ctx, TB_ALIGNED(xq, 16) && TB_ALIGNED(xs, 4) && TB_ALIGNED(pack, 16) && TB_ALIGNED(scales, 4) &&
                         TB_ALIGNED(y, 16),
                "gemm_tern: xq, pack, y 16-byte and xs, scales 4-byte aligned");
     TB_REQUIRE(ctx, acc >= 0 && acc <= 2, "gemm_tern: bad epilogue %d", acc);
-    GemmArgs a{xq, xs, pack, scales, y, (int)M, (int)N, (int)K, acc, ctx->dev_error};
-    return launch_gemm<X_Q8_TERN>(ctx, a);
+    return run_gemm(ctx, y, xq, X_Q8, xs, pack, scales, M, N, K, acc, true);
 }
 
 extern "C" TB_API int tb_gemm_int4_q8(tb_ctx* ctx, float* y, const int8_t* xq, const float* xs, const uint32_t* pack,
