@@ -39,8 +39,10 @@ constexpr int B_BYTES = BN * BK * 2;
 template <int HM> constexpr int stage_bytes() { return a_bytes<HM>() + B_BYTES; }
 constexpr int NST = 3;   // MMA operand stages
 constexpr int NR = 3;    // raw weight stages, filled NR-1 k-steps ahead of the dequant
-// raw staging, thread-major: packed W (int4 16 bytes = one 32-group a thread;
-// ternary 8 bytes), then the row's two f16 group scales of the k-step (4 bytes)
+// raw staging: the packed W tile of a k-step as [256 rows][32 bytes] (ternary 16),
+// copied by TMA -- thread t = 2 row + half reads bytes 16 t .. (ternary 8 t ..),
+// one 32-group -- then the rows' two f16 group scales of the k-step, 4 bytes a
+// thread (cp.async by the thread itself)
 constexpr int RAW_W = PROD * 16, RAW_S = PROD * 4, RSTAGE = RAW_W + RAW_S;
 template <int HM> constexpr int smem_bytes() { return 1024 + NST * stage_bytes<HM>() + NR * RSTAGE + 256; }
 static_assert(smem_bytes<2>() <= 227 * 1024, "shared memory");
@@ -51,7 +53,8 @@ constexpr int ERR_GEMM_WAIT = 0x6b01;
 enum XMode { X_F32 = 0, X_BF16 = 1, X_Q8 = 2 };
 
 struct GemmArgs {
-    CUtensorMap tx;         // f16 X [Mpad][K] (the pre-pass output), box 64 x 256, 128-byte swizzle
+    CUtensorMap tx;         // f16 X [Mpad][K] (the pre-pass output), box 64 x 128 HM, 128-byte swizzle
+    CUtensorMap tw;         // packed weights as bytes [N][K/2] (ternary [N][K/4]), box 32 (16) x 256
     const uint32_t* pack;   // [N][K/8] int4, or [N][K/16] ternary codes
     const uint16_t* scales; // [N][K/32] f16
     float* y;               // [M][N]
@@ -106,14 +109,6 @@ __device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi)
     return r;
 }
 
-__device__ __forceinline__ void cp16(void* sdst, const void* gsrc)
-{
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
-}
-__device__ __forceinline__ void cp8(void* sdst, const void* gsrc)
-{
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
-}
 __device__ __forceinline__ void cp4(void* sdst, const void* gsrc)
 {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
@@ -238,7 +233,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
     uint8_t* rawbase = base + NST * STAGE;
     uint64_t* full = reinterpret_cast<uint64_t*>(rawbase + NR * RSTAGE);   // B dequantized + X tile landed
     uint64_t* empty = full + NST;                                          // stage consumed by the MMAs
-    uint64_t* done = empty + NST;
+    uint64_t* rfull = empty + NST;                                         // raw weight tile landed
+    uint64_t* rempty = rfull + NR;                                         // raw weight tile read
+    uint64_t* done = rempty + NR;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 2);
 
@@ -247,6 +244,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
         for (int s = 0; s < NST; s++) {
             mbar_init(&full[s], PROD_WARPS + 1);   // the producer warps + the X copy's expect_tx arrival
             mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < NR; r++) {
+            mbar_init(&rfull[r], 1);
+            mbar_init(&rempty[r], PROD_WARPS);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -266,20 +267,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
 
     const int m0 = blockIdx.y * (MMA_M * HM), n0 = blockIdx.x * BN, nk = a.K / BK;
     if (warp < PROD_WARPS) {
-        // ---- producers: W rows (2 threads a row, one 32-group each).  Each thread
-        // copies its own raw bytes (cp.async, NR-1 k-steps ahead) and dequantizes
-        // only those, so no barrier is needed between copy and dequant.
+        // ---- producers: W rows (2 threads a row, one 32-group each).  The raw
+        // weight tile arrives by TMA (rfull); each thread copies its own two group
+        // scales (cp.async, NR-1 k-steps ahead).
         const int wr = tid >> 1, wh = tid & 1;
         auto fetch = [&](int i) {
             if (i < nk) {
                 uint8_t* rs = rawbase + (i % NR) * RSTAGE;
-                const int k0 = i * BK;
-                if (TERN) {
-                    cp8(rs + tid * 8, a.pack + (size_t)(n0 + wr) * (a.K / 16) + k0 / 16 + 2 * wh);
-                } else {
-                    cp16(rs + tid * 16, a.pack + (size_t)(n0 + wr) * (a.K / 8) + k0 / 8 + 4 * wh);
-                }
-                cp4(rs + RAW_W + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + k0 / 32);
+                cp4(rs + RAW_W + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + i * BK / 32);
             }
             cp_commit();   // a group per k-step, empty past the end, keeps the count uniform
         };
@@ -293,17 +288,30 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
                 atomicExch(a.err, ERR_GEMM_WAIT);
             }
             if (*abort_flag) break;
+            const int r = i % NR;
+            if (!__all_sync(0xffffffffu, mbar_wait(&rfull[r], (i / NR) & 1))) {
+                *abort_flag = 1;
+                atomicExch(a.err, ERR_GEMM_WAIT);
+                break;
+            }
             uint8_t* Bt = base + s * STAGE + A_BYTES;
-            const uint8_t* rs = rawbase + (i % NR) * RSTAGE;
+            const uint8_t* rs = rawbase + r * RSTAGE;
             const uint32_t sc = *reinterpret_cast<const uint32_t*>(rs + RAW_W + tid * 4);
             const uint32_t s2 = (wh ? (sc >> 16) : (sc & 0xFFFFu)) * 0x10001u;
+            uint4 w4;
             if (TERN) {
                 const uint2 w2 = *reinterpret_cast<const uint2*>(rs + tid * 8);
+                w4 = make_uint4(w2.x, w2.y, 0u, 0u);
+            } else {
+                w4 = *reinterpret_cast<const uint4*>(rs + tid * 16);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&rempty[r]);   // this warp's raw weight bytes are in registers
+            if (TERN) {
 #pragma unroll
                 for (int c = 0; c < 4; c++)
-                    *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_tern8(c < 2 ? w2.x : w2.y, c & 1, s2);
+                    *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_tern8(c < 2 ? w4.x : w4.y, c & 1, s2);
             } else {
-                const uint4 w4 = *reinterpret_cast<const uint4*>(rs + tid * 16);
                 const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
                 for (int c = 0; c < 4; c++) *reinterpret_cast<uint4*>(Bt + sw128(wr, 4 * wh + c)) = dequant_word(ws[c], s2);
@@ -316,10 +324,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
         cp_wait<0>();   // no copy in flight when the CTA leaves
     } else if (warp == W_TMA) {
         if (lane == 0) {
-            // ---- the X tiles: 128 HM rows x 64 f16 a k-step, one tensor copy
-            int issued = 0;
+            // ---- per k-step: the raw weight tile (256 rows x 32 bytes) and the X
+            // tile (128 HM rows x 64 f16), one tensor copy each
+            constexpr uint32_t WBYTES = TERN ? BN * BK / 4 : BN * BK / 2;
+            int issued_w = 0, issued_x = 0;
             for (int i = 0; i < nk; i++) {
-                const int s = i % NST;
+                const int s = i % NST, r = i % NR;
+                if (!mbar_wait(&rempty[r], ((i / NR) & 1) ^ 1)) {
+                    *abort_flag = 1;
+                    atomicExch(a.err, ERR_GEMM_WAIT);
+                }
+                if (*abort_flag) break;
+                mbar_expect_tx(&rfull[r], WBYTES);
+                tma_2d(rawbase + r * RSTAGE, &a.tw, i * (TERN ? BK / 4 : BK / 2), n0, &rfull[r]);
+                issued_w = i + 1;
                 if (!mbar_wait(&empty[s], ((i / NST) & 1) ^ 1)) {
                     *abort_flag = 1;
                     atomicExch(a.err, ERR_GEMM_WAIT);
@@ -327,10 +345,13 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
                 if (*abort_flag) break;
                 mbar_expect_tx(&full[s], (uint32_t)A_BYTES);
                 tma_2d(base + s * STAGE, &a.tx, i * BK, m0, &full[s]);
-                issued = i + 1;
+                issued_x = i + 1;
             }
-            // no copy may land after the CTA has left: wait for the last stages issued
-            for (int i = issued > NST ? issued - NST : 0; i < issued; i++) mbar_wait(&full[i % NST], (i / NST) & 1);
+            // no copy may land after the CTA has left: wait for the last copies issued
+            // (their barriers complete when the bytes land; full also needs the
+            // producers, so on an abort that wait runs to its bound)
+            for (int i = issued_w > NR ? issued_w - NR : 0; i < issued_w; i++) mbar_wait(&rfull[i % NR], (i / NR) & 1);
+            for (int i = issued_x > NST ? issued_x - NST : 0; i < issued_x; i++) mbar_wait(&full[i % NST], (i / NST) & 1);
         }
     } else if (lane == 0) {
         // ---- MMA issuer: per k16, rows 0-127 into columns 0-255, rows 128-255 into 256-511
@@ -451,12 +472,17 @@ int run_gemm(tb_ctx* ctx, float* y, const void* x, int mode, const float* xs, co
     else if (mode == X_BF16) e = tb_launch(ctx, k_x_f16<X_BF16>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
     else e = tb_launch(ctx, k_x_f16<X_Q8>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm x pass launch: %s", cudaGetErrorString(e));
-    // two 128-row halves a CTA (each weight tile dequantized once per 256 rows)
-    // unless that leaves SMs idle; then one
-    const int hm = ((M + BM - 1) / BM) * (N / BN) >= ctx->num_sms ? 2 : 1;
+    // two 128-row halves a CTA (each weight tile dequantized once per 256 rows), or
+    // one when that costs fewer whole waves (a 128-row tile taking ~0.6 of the time)
+    const int64_t t2 = ((M + BM - 1) / BM) * (N / BN), t1 = (M / MMA_M) * (N / BN);
+    const int64_t w2 = (t2 + ctx->num_sms - 1) / ctx->num_sms, w1 = (t1 + ctx->num_sms - 1) / ctx->num_sms;
+    const int hm = 10 * w2 <= 6 * w1 ? 2 : 1;
     GemmArgs a{};
-    const int rc = tb_encode_2d(ctx, &a.tx, xf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, Mpad, BK, MMA_M * hm,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
+    int rc = tb_encode_2d(ctx, &a.tx, xf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, Mpad, BK, MMA_M * hm,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+        rc = tb_encode_2d(ctx, &a.tw, pack, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, tern ? K / 4 : K / 2, N,
+                          tern ? BK / 4 : BK / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     a.pack = pack;
     a.scales = scales;
