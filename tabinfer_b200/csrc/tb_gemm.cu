@@ -117,7 +117,8 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// 8 weights of one packed word -> 8 f16 f16((nib - 8) * s) in k order (16 bytes)
+// 8 weights of one packed word -> 8 f16 f16((nib - 8) * s), in the pair order the
+// magic-number nibbles come out (k 0 4 1 5 2 6 3 7; 16 bytes)
 __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2)
 {
     const uint32_t magic = 0x64006400u;   // f16 1024 + nib in both halves
@@ -134,12 +135,12 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2)
     asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p1) : "r"(s2));
     asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p2) : "r"(s2));
     asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p3) : "r"(s2));
-    return make_uint4(__byte_perm(p0, p1, 0x5410), __byte_perm(p2, p3, 0x5410), __byte_perm(p0, p1, 0x7632),
-                      __byte_perm(p2, p3, 0x7632));
+    return make_uint4(p0, p1, p2, p3);   // k 0 4 1 5 2 6 3 7 (X is written in the same order)
 }
 
 // 8 ternary codes k = 8h..8h+7 of one word (k = 4s+b at bits 8b+2s, s = 2h, 2h+1)
-// -> 8 f16 (c - 1) * s in k order (16 bytes); exact: c - 1 is -1, 0 or 1.
+// -> 8 f16 (c - 1) * s in the pair order they come out (k 0 2 1 3 4 6 5 7 of the
+// 8; 16 bytes); exact: c - 1 is -1, 0 or 1.
 __device__ __forceinline__ uint4 dequant_tern8(uint32_t w, int h, uint32_t s2)
 {
     const uint32_t magic = 0x64006400u;   // f16 1024 + c in both halves
@@ -157,8 +158,7 @@ __device__ __forceinline__ uint4 dequant_tern8(uint32_t w, int h, uint32_t s2)
     asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p1) : "r"(s2));
     asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p2) : "r"(s2));
     asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(p3) : "r"(s2));
-    return make_uint4(__byte_perm(p0, p1, 0x5410), __byte_perm(p0, p1, 0x7632), __byte_perm(p2, p3, 0x5410),
-                      __byte_perm(p2, p3, 0x7632));
+    return make_uint4(p0, p1, p2, p3);   // k 0 2 1 3 4 6 5 7 of the 8 (X is written in the same order)
 }
 
 // 4 int8 (one word) -> 4 floats exactly (2^23 + (q ^ 0x80) - (2^23 + 128)), times xs
@@ -186,8 +186,12 @@ __device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x,
                  : "memory");
 }
 
-// X -> f16 rows [Mpad][K], rows M.. zero: 8 elements (16 bytes out) a thread, grid-stride
-template <int MODE>
+// X -> f16 rows [Mpad][K], rows M.. zero: 8 elements (16 bytes out) a thread, grid-stride.
+// Each 8-group is written in the k order the weight dequant produces without byte
+// permutes (TERN false: k 0 4 1 5 2 6 3 7; true: 0 2 1 3 4 6 5 7), so A and B agree
+// and every product of the GEMM is the same; only the summation order inside an
+// MMA differs from natural k order.
+template <int MODE, bool TERN>
 __global__ void __launch_bounds__(256) k_x_f16(const void* __restrict__ x, const float* __restrict__ xs,
                                                uint4* __restrict__ out, long long n8, long long n8_valid)
 {
@@ -196,28 +200,33 @@ __global__ void __launch_bounds__(256) k_x_f16(const void* __restrict__ x, const
     for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n8; i += (long long)gridDim.x * 256) {
         uint4 o = make_uint4(0u, 0u, 0u, 0u);
         if (i < n8_valid) {
+            float f[8];
             if (MODE == X_F32) {
                 const float4 u = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
                 const float4 v = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
-                o = make_uint4(f32x2_to_f16x2(u.x, u.y), f32x2_to_f16x2(u.z, u.w), f32x2_to_f16x2(v.x, v.y),
-                               f32x2_to_f16x2(v.z, v.w));
+                f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w; f[4] = v.x; f[5] = v.y; f[6] = v.z; f[7] = v.w;
             } else if (MODE == X_BF16) {
                 const uint4 v = __ldg(reinterpret_cast<const uint4*>(x) + i);
                 const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-                uint32_t r[4];
 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    r[j] = f32x2_to_f16x2(__uint_as_float(in[j] << 16), __uint_as_float(in[j] & 0xFFFF0000u));
-                o = make_uint4(r[0], r[1], r[2], r[3]);
+                for (int j = 0; j < 4; j++) {
+                    f[2 * j] = __uint_as_float(in[j] << 16);
+                    f[2 * j + 1] = __uint_as_float(in[j] & 0xFFFF0000u);
+                }
             } else {
                 const uint2 q = __ldg(reinterpret_cast<const uint2*>(x) + i);
                 const float xsc = __ldg(xs + ((8 * i) >> 5));   // [M][K/32]: element e's group is e / 32
                 float2 p0, p1, p2, p3;
                 q8x4_scaled(q.x, xsc, p0, p1);
                 q8x4_scaled(q.y, xsc, p2, p3);
-                o = make_uint4(f32x2_to_f16x2(p0.x, p0.y), f32x2_to_f16x2(p1.x, p1.y), f32x2_to_f16x2(p2.x, p2.y),
-                               f32x2_to_f16x2(p3.x, p3.y));
+                f[0] = p0.x; f[1] = p0.y; f[2] = p1.x; f[3] = p1.y; f[4] = p2.x; f[5] = p2.y; f[6] = p3.x; f[7] = p3.y;
             }
+            if (TERN)
+                o = make_uint4(f32x2_to_f16x2(f[0], f[2]), f32x2_to_f16x2(f[1], f[3]), f32x2_to_f16x2(f[4], f[6]),
+                               f32x2_to_f16x2(f[5], f[7]));
+            else
+                o = make_uint4(f32x2_to_f16x2(f[0], f[4]), f32x2_to_f16x2(f[1], f[5]), f32x2_to_f16x2(f[2], f[6]),
+                               f32x2_to_f16x2(f[3], f[7]));
         }
         out[i] = o;
     }
@@ -468,9 +477,10 @@ int run_gemm(tb_ctx* ctx, float* y, const void* x, int mode, const float* xs, co
     const long long want = (n8 + 255) / 256, cap = (long long)ctx->num_sms * 16;
     const dim3 grid((unsigned)(want < cap ? want : cap));
     cudaError_t e;
-    if (mode == X_F32) e = tb_launch(ctx, k_x_f16<X_F32>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
-    else if (mode == X_BF16) e = tb_launch(ctx, k_x_f16<X_BF16>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
-    else e = tb_launch(ctx, k_x_f16<X_Q8>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
+    if (tern) e = tb_launch(ctx, k_x_f16<X_Q8, true>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
+    else if (mode == X_F32) e = tb_launch(ctx, k_x_f16<X_F32, false>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
+    else if (mode == X_BF16) e = tb_launch(ctx, k_x_f16<X_BF16, false>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
+    else e = tb_launch(ctx, k_x_f16<X_Q8, false>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm x pass launch: %s", cudaGetErrorString(e));
     // two 128-row halves a CTA (each weight tile dequantized once per 256 rows), or
     // one when that costs fewer whole waves (a 128-row tile taking ~0.6 of the time)
