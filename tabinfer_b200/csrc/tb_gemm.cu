@@ -280,10 +280,24 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
         // weight tile arrives by TMA (rfull); each thread copies its own two group
         // scales (cp.async, NR-1 k-steps ahead).
         const int wr = tid >> 1, wh = tid & 1;
+        // scales: with 16-byte aligned scale rows (K % 256 == 0) one 16-byte load
+        // brings 8 groups (4 k-steps) into a 3-deep register ring, 8 k-steps ahead;
+        // otherwise a 4-byte cp.async a k-step, NR-1 k-steps ahead
+        const bool svec = (a.K % 256) == 0;
+        const uint16_t* srow = a.scales + (size_t)(n0 + wr) * (a.K / 32);
+        auto sload = [&](int i) {   // groups 2i .. 2i+7 (k-steps i .. i+3), i % 4 == 0
+            return i < nk ? __ldg(reinterpret_cast<const uint4*>(srow + 2 * i)) : make_uint4(0u, 0u, 0u, 0u);
+        };
+        uint4 sq0 = make_uint4(0u, 0u, 0u, 0u), sq1 = sq0, sq2 = sq0;
+        if (svec) {
+            sq0 = sload(0);
+            sq1 = sload(4);
+            sq2 = sload(8);
+        }
         auto fetch = [&](int i) {
-            if (i < nk) {
+            if (!svec && i < nk) {
                 uint8_t* rs = rawbase + (i % NR) * RSTAGE;
-                cp4(rs + RAW_W + tid * 4, a.scales + (size_t)(n0 + wr) * (a.K / 32) + i * BK / 32);
+                cp4(rs + RAW_W + tid * 4, srow + i * BK / 32);
             }
             cp_commit();   // a group per k-step, empty past the end, keeps the count uniform
         };
@@ -305,7 +319,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
             }
             uint8_t* Bt = base + s * STAGE + A_BYTES;
             const uint8_t* rs = rawbase + r * RSTAGE;
-            const uint32_t sc = *reinterpret_cast<const uint32_t*>(rs + RAW_W + tid * 4);
+            if (svec && i > 0 && (i & 3) == 0) {
+                sq0 = sq1;
+                sq1 = sq2;
+                sq2 = sload(i + 8);
+            }
+            const int iq = i & 3;
+            const uint32_t sc = svec ? (iq == 0 ? sq0.x : iq == 1 ? sq0.y : iq == 2 ? sq0.z : sq0.w)
+                                     : *reinterpret_cast<const uint32_t*>(rs + RAW_W + tid * 4);
             const uint32_t s2 = (wh ? (sc >> 16) : (sc & 0xFFFFu)) * 0x10001u;
             uint4 w4;
             if (TERN) {
