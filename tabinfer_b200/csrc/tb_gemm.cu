@@ -59,6 +59,10 @@ struct GemmArgs {
     const uint16_t* scales; // [N][K/32] f16
     float* y;               // [M][N]
     int M, N, K, acc;
+    // split-K: CTA z of grid.z runs k-steps [z kps, (z + 1) kps) and, with part set,
+    // stores its raw f32 sums into part[z][M][N] for k_splitk_reduce
+    int kps;
+    float* part;
     int* err;
 };
 
@@ -274,7 +278,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
     tb_pdl_wait();
     tb_pdl_trigger();
 
-    const int m0 = blockIdx.y * (MMA_M * HM), n0 = blockIdx.x * BN, nk = a.K / BK;
+    const int m0 = blockIdx.y * (MMA_M * HM), n0 = blockIdx.x * BN;
+    // this CTA's k-steps: kb .. kb + nk - 1 (loops below count i from 0; data at kb + i)
+    const int kb = (int)blockIdx.z * a.kps;
+    const int nk = min(a.K / BK - kb, a.kps);
     if (warp < PROD_WARPS) {
         // ---- producers: W rows (2 threads a row, one 32-group each).  The raw
         // weight tile arrives by TMA (rfull); each thread copies its own two group
@@ -285,8 +292,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
         // otherwise a 4-byte cp.async a k-step, NR-1 k-steps ahead
         const bool svec = (a.K % 256) == 0;
         const uint16_t* srow = a.scales + (size_t)(n0 + wr) * (a.K / 32);
-        auto sload = [&](int i) {   // groups 2i .. 2i+7 (k-steps i .. i+3), i % 4 == 0
-            return i < nk ? __ldg(reinterpret_cast<const uint4*>(srow + 2 * i)) : make_uint4(0u, 0u, 0u, 0u);
+        auto sload = [&](int i) {   // groups 2(kb+i) .. +7 (k-steps kb+i .. +3), kb + i % 4 == 0
+            return i < nk ? __ldg(reinterpret_cast<const uint4*>(srow + 2 * (kb + i))) : make_uint4(0u, 0u, 0u, 0u);
         };
         uint4 sq0 = make_uint4(0u, 0u, 0u, 0u), sq1 = sq0, sq2 = sq0;
         if (svec) {
@@ -297,7 +304,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
         auto fetch = [&](int i) {
             if (!svec && i < nk) {
                 uint8_t* rs = rawbase + (i % NR) * RSTAGE;
-                cp4(rs + RAW_W + tid * 4, srow + i * BK / 32);
+                cp4(rs + RAW_W + tid * 4, srow + (kb + i) * BK / 32);
             }
             cp_commit();   // a group per k-step, empty past the end, keeps the count uniform
         };
@@ -366,7 +373,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
                 }
                 if (*abort_flag) break;
                 mbar_expect_tx(&rfull[r], WBYTES);
-                tma_2d(rawbase + r * RSTAGE, &a.tw, i * (TERN ? BK / 4 : BK / 2), n0, &rfull[r]);
+                tma_2d(rawbase + r * RSTAGE, &a.tw, (kb + i) * (TERN ? BK / 4 : BK / 2), n0, &rfull[r]);
                 issued_w = i + 1;
                 if (!mbar_wait(&empty[s], ((i / NST) & 1) ^ 1)) {
                     *abort_flag = 1;
@@ -374,7 +381,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
                 }
                 if (*abort_flag) break;
                 mbar_expect_tx(&full[s], (uint32_t)A_BYTES);
-                tma_2d(base + s * STAGE, &a.tx, i * BK, m0, &full[s]);
+                tma_2d(base + s * STAGE, &a.tx, (kb + i) * BK, m0, &full[s]);
                 issued_x = i + 1;
             }
             // no copy may land after the CTA has left: wait for the last copies issued
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
 #pragma unroll 1
             for (int hm = 0; hm < HM; hm++) {
                 const int row = m0 + hm * MMA_M + 32 * q + lane;
-                float* yrow = a.y + (size_t)row * a.N + n0 + 64 * h;
+                float* yrow = (a.part ? a.part + (size_t)blockIdx.z * a.M * a.N : a.y) + (size_t)row * a.N + n0 + 64 * h;
 #pragma unroll 1
                 for (int j = 0; j < 2; j++) {
                     uint32_t r[32];
@@ -446,7 +453,8 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
                     for (int c = 0; c < 8; c++) {
                         float4 v = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
                                                __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
-                        if (a.acc == 1) {          // fused residual: y += X W^T
+                        if (a.part) {
+                        } else if (a.acc == 1) {   // fused residual: y += X W^T
                             const float4 o = yp[c];
                             v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
                         } else if (a.acc == 2) {   // fused SwiGLU: y holds gate, y = silu(gate) * (X W_up^T)
@@ -470,6 +478,32 @@ __global__ void __launch_bounds__(THREADS, 1) k_gemm_f16(const __grid_constant__
     }
 }
 
+// y (epilogue)= the sum of the split-K partials in split order: part [nsplit][M][N]
+__global__ void __launch_bounds__(256) k_splitk_reduce(const float4* __restrict__ part, int nsplit, long long n4,
+                                                       float4* __restrict__ y, int acc)
+{
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n4; i += (long long)gridDim.x * 256) {
+        float4 v = part[i];
+        for (int z = 1; z < nsplit; z++) {
+            const float4 p = part[(long long)z * n4 + i];
+            v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+        }
+        if (acc == 1) {
+            const float4 o = y[i];
+            v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+        } else if (acc == 2) {
+            const float4 gt = y[i];
+            v.x = __fdiv_rn(gt.x, 1.0f + expf(-gt.x)) * v.x;
+            v.y = __fdiv_rn(gt.y, 1.0f + expf(-gt.y)) * v.y;
+            v.z = __fdiv_rn(gt.z, 1.0f + expf(-gt.z)) * v.z;
+            v.w = __fdiv_rn(gt.w, 1.0f + expf(-gt.w)) * v.w;
+        }
+        y[i] = v;
+    }
+}
+
 template <bool TERN, int HM>
 int launch_gemm(tb_ctx* ctx, const GemmArgs& a, int64_t M)
 {
@@ -481,7 +515,8 @@ int launch_gemm(tb_ctx* ctx, const GemmArgs& a, int64_t M)
         if (ctx->device < 64) attr_set[ctx->device] = true;
     }
     const unsigned rows = (unsigned)((M + MMA_M * HM - 1) / (MMA_M * HM));
-    cudaError_t e = tb_launch(ctx, k_gemm_f16<TERN, HM>, dim3(a.N / BN, rows), dim3(THREADS),
+    const unsigned splits = (unsigned)((a.K / BK + a.kps - 1) / a.kps);
+    cudaError_t e = tb_launch(ctx, k_gemm_f16<TERN, HM>, dim3(a.N / BN, rows, splits), dim3(THREADS),
                               (size_t)smem_bytes<HM>(), a);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
     return TB_OK;
@@ -492,8 +527,26 @@ int run_gemm(tb_ctx* ctx, float* y, const void* x, int mode, const float* xs, co
              const uint16_t* scales, int64_t M, int64_t N, int64_t K, int acc, bool tern)
 {
     const int64_t Mpad = (M + BM - 1) / BM * BM;
-    uint4* xf = static_cast<uint4*>(tb_ctx_scratch(ctx, (size_t)(Mpad * K * 2)));
-    if (!xf) return TB_ERR_NOMEM;
+    // two 128-row halves a CTA (each weight tile dequantized once per 256 rows), or
+    // one when that costs fewer whole waves (a 128-row tile taking ~0.6 of the time)
+    const int64_t t2 = ((M + BM - 1) / BM) * (N / BN), t1 = (M / MMA_M) * (N / BN);
+    const int64_t w2 = (t2 + ctx->num_sms - 1) / ctx->num_sms, w1 = (t1 + ctx->num_sms - 1) / ctx->num_sms;
+    const int hm = 10 * w2 <= 6 * w1 ? 2 : 1;
+    // split-K when the tiles leave SMs idle: at most 8 splits of at least 4 k-steps,
+    // split boundaries on 4 k-steps (the scale loads' 8-group alignment)
+    const int64_t tiles = hm == 2 ? t2 : t1, nk = K / BK;
+    int64_t sk = ctx->num_sms / tiles;
+    if (sk > 8) sk = 8;
+    if (sk > nk / 4) sk = nk / 4;
+    if (sk < 1) sk = 1;
+    const int64_t kps = ((nk + sk - 1) / sk + 3) / 4 * 4;
+    sk = (nk + kps - 1) / kps;
+    const size_t xbytes = ((size_t)(Mpad * K * 2) + 255) & ~(size_t)255;
+    const size_t pbytes = sk > 1 ? (size_t)(sk * M * N * 4) : 0;
+    unsigned char* scr = static_cast<unsigned char*>(tb_ctx_scratch(ctx, xbytes + pbytes));
+    if (!scr) return TB_ERR_NOMEM;
+    uint4* xf = reinterpret_cast<uint4*>(scr);
+    float* part = sk > 1 ? reinterpret_cast<float*>(scr + xbytes) : nullptr;
     const long long n8 = Mpad * K / 8, n8v = M * K / 8;
     const long long want = (n8 + 255) / 256, cap = (long long)ctx->num_sms * 16;
     const dim3 grid((unsigned)(want < cap ? want : cap));
@@ -503,11 +556,6 @@ int run_gemm(tb_ctx* ctx, float* y, const void* x, int mode, const float* xs, co
     else if (mode == X_BF16) e = tb_launch(ctx, k_x_f16<X_BF16, false>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
     else e = tb_launch(ctx, k_x_f16<X_Q8, false>, grid, dim3(256), 0, x, xs, xf, n8, n8v);
     if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm x pass launch: %s", cudaGetErrorString(e));
-    // two 128-row halves a CTA (each weight tile dequantized once per 256 rows), or
-    // one when that costs fewer whole waves (a 128-row tile taking ~0.6 of the time)
-    const int64_t t2 = ((M + BM - 1) / BM) * (N / BN), t1 = (M / MMA_M) * (N / BN);
-    const int64_t w2 = (t2 + ctx->num_sms - 1) / ctx->num_sms, w1 = (t1 + ctx->num_sms - 1) / ctx->num_sms;
-    const int hm = 10 * w2 <= 6 * w1 ? 2 : 1;
     GemmArgs a{};
     int rc = tb_encode_2d(ctx, &a.tx, xf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, Mpad, BK, MMA_M * hm,
                           CU_TENSOR_MAP_SWIZZLE_128B);
@@ -522,9 +570,17 @@ int run_gemm(tb_ctx* ctx, float* y, const void* x, int mode, const float* xs, co
     a.N = (int)N;
     a.K = (int)K;
     a.acc = acc;
+    a.kps = (int)kps;
+    a.part = part;
     a.err = ctx->dev_error;
-    if (hm == 2) return tern ? launch_gemm<true, 2>(ctx, a, M) : launch_gemm<false, 2>(ctx, a, M);
-    return tern ? launch_gemm<true, 1>(ctx, a, M) : launch_gemm<false, 1>(ctx, a, M);
+    if (hm == 2) rc = tern ? launch_gemm<true, 2>(ctx, a, M) : launch_gemm<false, 2>(ctx, a, M);
+    else rc = tern ? launch_gemm<true, 1>(ctx, a, M) : launch_gemm<false, 1>(ctx, a, M);
+    if (rc || sk == 1) return rc;
+    const long long n4 = M * N / 4, rw = (n4 + 255) / 256;
+    e = tb_launch(ctx, k_splitk_reduce, dim3((unsigned)(rw < cap ? rw : cap)), dim3(256), 0,
+                  reinterpret_cast<const float4*>(part), (int)sk, n4, reinterpret_cast<float4*>(y), acc);
+    if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "gemm split-K reduce launch: %s", cudaGetErrorString(e));
+    return TB_OK;
 }
 
 }  // namespace
