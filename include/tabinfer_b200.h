@@ -440,9 +440,10 @@ TB_API int tb_embed_gather(tb_ctx *ctx, const uint32_t *ids, int64_t idoff,
  * weights in the int4 G=32 layout of tb_quant_int4_g32.  X is f32 (x_bf16 = 0,
  * as linearQ's buffers) or bf16 (x_bf16 = 1).  M % 128 == 0, N % 256 == 0,
  * K % 64 == 0; x, pack, y 16-byte aligned, scales 4-byte aligned.  X is rounded
- * to f16 into context scratch first (M rounded up to 256, x K, x 2 bytes; the
- * scratch grows on demand), as are the inputs of tb_gemm_int4_q8 and
- * tb_gemm_tern_wgsl. */
+ * to f16 into context scratch first (M rounded up to 256, x K, x 2 bytes), as are
+ * the inputs of tb_gemm_int4_q8 and tb_gemm_tern_wgsl; when the output tiles leave
+ * SMs idle the K range is split and the splits' f32 partials (up to 8 x M x N x 4
+ * bytes) also live in that scratch, which grows on demand. */
 TB_API int tb_gemm_int4_g32(tb_ctx *ctx, float *y, const void *x, int x_bf16, const uint32_t *pack,
                             const uint16_t *scales, int64_t M, int64_t N, int64_t K, int acc);
 
