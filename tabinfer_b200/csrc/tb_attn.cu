@@ -66,6 +66,87 @@ __global__ void __launch_bounds__(256) k_attn_prep(const float* __restrict__ q, 
     (void)lane; (void)wid; (void)nw;
 }
 
+// ---- prep of the T rows of one sequence's prefill ----------------------------
+// One CTA per token row: its threads first form the row's rotary (cos, sin) pairs
+// once (rope_cs, the double-precision angles), then each warp takes whole heads
+// (q, k, then v): lane l holds elements l + 32 i, so the split-half rotary
+// partner of every element (i +- hd/64) is in the same lane and no block barrier
+// is needed.  Every value is the one k_attn_prep forms: the same per-32 warp sums
+// added in the same order, the same norm, rotary and quantization arithmetic.
+// HD = 64, 128 or 256.
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_prep_rows(const float* __restrict__ q, const float* __restrict__ k,
+                                                        const float* __restrict__ v, const uint16_t* __restrict__ qw,
+                                                        const uint16_t* __restrict__ kw, float* __restrict__ qr,
+                                                        int8_t* __restrict__ Kq, float* __restrict__ Ks,
+                                                        int8_t* __restrict__ Vq, float* __restrict__ Vs, int nHq,
+                                                        int nKv, float theta, float eps,
+                                                        const int* __restrict__ dpos, long long cache_rows, int* err)
+{
+    __shared__ float cs_c[128], cs_s[128];
+    tb_pdl_wait();
+    tb_pdl_trigger();
+    const int t = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const long long pos = dpos[t];
+    if (pos < 0 || pos >= cache_rows) {
+        if (threadIdx.x == 0) atomicExch(err, ERR_ATTN_POS);
+        return;
+    }
+    constexpr int hd = HD, half = HD / 2, nw = HD / 32;
+    for (int f = threadIdx.x; f < half; f += blockDim.x) rope_cs(f, hd, pos, theta, &cs_c[f], &cs_s[f]);
+    __syncthreads();
+    q += (long long)t * nHq * hd;
+    qr += (long long)t * nHq * hd;
+    k += (long long)t * nKv * hd;
+    v += (long long)t * nKv * hd;
+    const int nroles = nHq + 2 * nKv;
+    for (int role = wid; role < nroles; role += (int)(blockDim.x >> 5)) {
+        const bool isQ = role < nHq, isK = !isQ && role < nHq + nKv;
+        const int head = isQ ? role : (isK ? role - nHq : role - nHq - nKv);
+        const float* src = (isQ ? q : (isK ? k : v)) + (long long)head * hd;
+        float x[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) x[i] = i < nw ? src[32 * i + lane] : 0.0f;
+        if (isQ || isK) {
+            const uint16_t* w16 = isQ ? qw : kw;
+            float tot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (i < nw) tot += warp_sum(x[i] * x[i]);
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)hd), eps)));
+            float rk[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) rk[i] = i < nw ? __fmul_rn(__fmul_rn(x[i], inv), tb_h2f(w16[32 * i + lane])) : 0.0f;
+            constexpr int hw = nw / 2;   // the rotary partner is hw registers away
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                if (i >= nw) break;
+                const int j = 32 * i + lane, fi = j < half ? j : j - half;
+                const float partner = i < hw ? rk[i + hw] : rk[i - hw];
+                const float rot = j < half ? -partner : partner;
+                x[i] = fmaf(rk[i], cs_c[fi], rot * cs_s[fi]);
+            }
+            if (isQ) {
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    if (i < nw) qr[(long long)head * hd + 32 * i + lane] = x[i];
+                continue;
+            }
+        }
+        // snorm int8 of each 32-group (quant_row) into the cache row `pos`
+        const long long row = pos * nKv * hd + (long long)head * hd;
+        int8_t* dq = (isK ? Kq : Vq) + row;
+        float* ds = (isK ? Ks : Vs) + row / 32;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            if (i >= nw) break;
+            const float m = fmaxf(1e-12f, warp_max(fabsf(x[i])));
+            dq[32 * i + lane] = snorm8(__fdiv_rn(x[i], m));
+            if (lane == 0) ds[i] = m;
+        }
+    }
+}
+
 // ---- prefill quant-write of T rows (KVQW) -----------------------------------
 __global__ void __launch_bounds__(256) k_kv_quant_write(const float* __restrict__ kr, const float* __restrict__ v,
                                                         int8_t* __restrict__ Kq, float* __restrict__ Ks,
@@ -226,6 +307,14 @@ int tb_attn_prep_rows_impl(tb_ctx* ctx, const float* q, const float* k, const fl
                            float eps)
 {
     TB_REQUIRE(ctx, hd % 32 == 0 && hd >= 32 && hd <= 256 && T > 0 && T <= 65535, "attn prep rows: bad shape");
+    if ((hd == 64 || hd == 128 || hd == 256) && dpos) {
+        auto kern = hd == 64 ? k_attn_prep_rows<64> : (hd == 128 ? k_attn_prep_rows<128> : k_attn_prep_rows<256>);
+        cudaError_t e = tb_launch(ctx, kern, dim3((unsigned)T), dim3(256), 0, q, k, v, qw16, kw16, qr, Kq, Ks, Vq, Vs,
+                                  (int)nHq, (int)nKv, theta, eps, (const int*)dpos, (long long)cache_rows,
+                                  ctx->dev_error);
+        if (e != cudaSuccess) return tb_fail(ctx, TB_ERR_CUDA, "attn_prep_rows launch: %s", cudaGetErrorString(e));
+        return TB_OK;
+    }
     cudaError_t e = tb_launch(ctx, k_attn_prep, dim3((unsigned)(nHq + 2 * nKv), (unsigned)T), dim3((unsigned)hd), 0,
                               q, k, v, qw16, kw16, qr, Kq, Ks, Vq, Vs, (int)nHq, (int)nKv, (int)hd, 0LL, theta, eps,
                               (const int*)dpos, (long long)cache_rows, 0LL, ctx->dev_error);
