@@ -1265,6 +1265,21 @@ def profile_gemm_dp4(M, N, K):
     print("profile gemm_dp4 done", flush=True)
 
 
+def profile_prefill(T):
+    """Two T-token prefill forwards of Qwen3-1.7B (random int4 weights), for an ncu
+    launch list of the second (the first also sizes every buffer)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    m = build_model(Q17, dev, 1, T + 16, 16, 1, 0, seed=91)
+    ids = list(np.random.default_rng(3).integers(0, Q17["vocab"], T))
+    for _ in range(2):
+        m.prefill(0, ids, 0)
+        torch.cuda.synchronize(dev)
+    m.close()
+    print("profile prefill done", flush=True)
+
+
 def profile_lm_head(kind):
     """Three cold-L2 lm_head GEMVs (151936 x 2048, RMSNorm fused) of one weight
     kind -- int4_f32 (gemvQ, batch 1), int4_dp4a (rmsnormQ + gemvDP4, batch 1),
@@ -1483,6 +1498,8 @@ def main():
                     help="three cold-L2 prefill-GEMM launches at M x N x K (for ncu), then exit")
     ap.add_argument("--profile-prefill-attn", type=int, default=0, metavar="T",
                     help="three cold-L2 prefill-attention launches at T = S tokens (for ncu), then exit")
+    ap.add_argument("--profile-prefill", type=int, default=None, metavar="T",
+                    help="two T-token prefill forwards (for an ncu launch list)")
     ap.add_argument("--profile-gemm-dp4", type=int, nargs=3, default=None, metavar=("M", "N", "K"),
                     help="three cold-L2 exact-sum prefill GEMM launches (for ncu), then exit")
     ap.add_argument("--profile-lm-head", default=None, choices=("int4_f32", "int4_dp4a", "tern", "int4_mma16"),
@@ -1520,6 +1537,9 @@ def main():
         return
     if args.profile_prefill_attn:
         profile_prefill_attn(args.profile_prefill_attn)
+        return
+    if args.profile_prefill:
+        profile_prefill(args.profile_prefill)
         return
     if args.profile_gemm_dp4:
         profile_gemm_dp4(*args.profile_gemm_dp4)
