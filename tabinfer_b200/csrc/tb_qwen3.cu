@@ -122,7 +122,7 @@ struct tb_qwen3 {
     std::vector<void*> allocs;
     // prefill (forward at T > 1): buffers of `pf_cap` rows, grown on demand
     int64_t pf_cap = 0;
-    float *pf_x = nullptr, *pf_norm = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_qr = nullptr,
+    float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_qr = nullptr,
           *pf_attn = nullptr, *pf_gate = nullptr, *pf_xs = nullptr;
     int8_t* pf_xq = nullptr;
     uint32_t* pf_ids = nullptr;
@@ -494,11 +494,11 @@ int issue_head(tb_qwen3* m, int cur)
 
 void free_prefill(tb_qwen3* m)
 {
-    for (void* p : {(void*)m->pf_x, (void*)m->pf_norm, (void*)m->pf_q, (void*)m->pf_k, (void*)m->pf_v,
+    for (void* p : {(void*)m->pf_x, (void*)m->pf_q, (void*)m->pf_k, (void*)m->pf_v,
                     (void*)m->pf_qr, (void*)m->pf_attn, (void*)m->pf_gate, (void*)m->pf_xs, (void*)m->pf_xq,
                     (void*)m->pf_ids, (void*)m->pf_pos})
         if (p) cudaFree(p);
-    m->pf_x = m->pf_norm = m->pf_q = m->pf_k = m->pf_v = m->pf_qr = m->pf_attn = m->pf_gate = m->pf_xs = nullptr;
+    m->pf_x = m->pf_q = m->pf_k = m->pf_v = m->pf_qr = m->pf_attn = m->pf_gate = m->pf_xs = nullptr;
     m->pf_xq = nullptr;
     m->pf_ids = nullptr;
     m->pf_pos = nullptr;
@@ -517,7 +517,7 @@ int prefill_buffers(tb_qwen3* m, int64_t Tp)
     auto get = [&](auto** p, size_t bytes) {
         if (ok && cudaMalloc((void**)p, (bytes + 255) & ~size_t(255)) != cudaSuccess) { cudaGetLastError(); ok = false; }
     };
-    get(&m->pf_x, Tp * H * 4); get(&m->pf_norm, Tp * H * 4);
+    get(&m->pf_x, Tp * H * 4);
     get(&m->pf_q, Tp * qN * 4); get(&m->pf_k, Tp * kvN * 4); get(&m->pf_v, Tp * kvN * 4);
     get(&m->pf_qr, Tp * qN * 4); get(&m->pf_attn, Tp * qN * 4); get(&m->pf_gate, Tp * c.intermediate * 4);
     get(&m->pf_xq, Tp * kmax); get(&m->pf_xs, Tp * (kmax / 32) * 4);
@@ -576,8 +576,9 @@ int prefill(tb_qwen3* m, int seq, const uint32_t* ids_host, int64_t T, int64_t p
     const int64_t crow = (int64_t)seq * c.max_seq * kvN;   // this sequence's cache
     for (int l = 0; l < c.layers; l++) {
         Layer& Ly = m->L[l];
-        TRY(tb_rmsnorm(ctx, m->pf_x, Ly.ln1, m->pf_norm, Tp, H, c.rms_eps));
-        TRY(pf_quant(m, m->pf_norm, Tp, H));
+        // rmsnormQ of the rows straight into the GEMM's int8 input (the same bits
+        // as rmsnorm then QUANTQ8T, without the f32 round trip)
+        TRY(tb_rmsnorm_q8(ctx, m->pf_x, Ly.ln1, c.rms_eps, m->pf_xq, m->pf_xs, nullptr, Tp, H));
         TRY(pf_gemm(m, m->pf_q, Ly.q, Tp, 0));
         TRY(pf_gemm(m, m->pf_k, Ly.k, Tp, 0));
         TRY(pf_gemm(m, m->pf_v, Ly.v, Tp, 0));
@@ -588,8 +589,7 @@ int prefill(tb_qwen3* m, int seq, const uint32_t* ids_host, int64_t T, int64_t p
                                Ly.Vs + crow / 32, T, pos0 + T, m->nHq, m->nKv, hd));
         TRY(pf_quant(m, m->pf_attn, Tp, qN));
         TRY(pf_residual(m, Ly.o, Tp));
-        TRY(tb_rmsnorm(ctx, m->pf_x, Ly.ln2, m->pf_norm, Tp, H, c.rms_eps));
-        TRY(pf_quant(m, m->pf_norm, Tp, H));
+        TRY(tb_rmsnorm_q8(ctx, m->pf_x, Ly.ln2, c.rms_eps, m->pf_xq, m->pf_xs, nullptr, Tp, H));
         TRY(pf_gemm(m, m->pf_gate, Ly.gate, Tp, 0));
         TRY(pf_gemm(m, m->pf_gate, Ly.up, Tp, 2));
         TRY(pf_quant(m, m->pf_gate, Tp, I));
