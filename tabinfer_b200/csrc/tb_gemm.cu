@@ -7,18 +7,24 @@
 // and the products are summed in f32.
 //
 // X is rounded to f16 once, by a pre-pass into context scratch (f32 or bf16 rows,
-// or QUANTQ8T rows as f16(xs * q)), padded with zero rows to a whole tile, so the
-// A tiles arrive by TMA in the 128-byte swizzle the MMA descriptor reads, with no
-// conversion work inside the GEMM.  CTA tile 256 (M) x 256 (N), K in steps of 64:
-// each dequantized weight tile (the producer work, fused here) feeds two
-// 128 x 256 x 16 MMAs per k16 -- one per 128-row half of the X tile -- into two
-// 256-column f32 accumulators (all 512 TMEM columns), so a weight is dequantized
-// once per 256 rows of X.  Warps 0-15 are producers: each thread cp.asyncs its
-// share of the raw packed weights + f16 scales NR-1 k-steps ahead and writes it
-// dequantized into the swizzled B tile; warp 16 owns TMEM and one of its threads
-// issues the MMAs; one thread of warp 17 issues the X tile copies.  After the last
-// stage warps 0-15 read the accumulators (warp w: TMEM lanes 32*(w%4).., columns
-// 64*(w/4).. of both) and store f32 rows.
+// or QUANTQ8T rows as f16(xs * q)), padded with zero rows to 256, so the A tiles
+// arrive by TMA in the 128-byte swizzle the MMA descriptor reads, with no
+// conversion work inside the GEMM; the pre-pass writes each 8-group in the k order
+// the weight dequant produces its f16 pairs (no byte permutes in the producers).
+// CTA tile 256 (M) x 256 (N) -- each dequantized weight tile (the producer work,
+// fused here) feeds two 128 x 256 x 16 MMAs per k16, one per 128-row half of the X
+// tile, into two 256-column f32 accumulators (all 512 TMEM columns) -- or 128 x 256
+// when that costs fewer whole waves; K in steps of 64.  One thread of warp 17
+// issues per k-step two tensor copies: the raw packed weight tile and the X tile.
+// Warps 0-15 are producers: each thread reads its 32-weight group of the raw tile
+// and writes it dequantized into the swizzled B tile; its two group scales come
+// from a register ring filled 8 k-steps ahead (16-byte loads of 8 groups when
+// K % 256 == 0, else a 4-byte cp.async NR-1 k-steps ahead).  Warp 16 owns TMEM
+// and one of its threads issues the MMAs.  After the last stage warps 0-15 read
+// the accumulators (warp w: TMEM lanes 32*(w%4).., columns 64*(w/4).. of both) and
+// store f32 rows.  When the tiles leave SMs idle the K range is split across
+// grid.z: each split stores its raw sums into context scratch and
+// k_splitk_reduce adds them in split order and applies the epilogue.
 // Ternary weights in the WebGPU layout (gemmTern, qwen3.js:1410-1420) use the
 // same pipeline with the operands of that GEMM: X as QUANTQ8T int8 rows with
 // per-32 f32 scales becomes f16(xs * q); a weight becomes the exact f16

@@ -75,7 +75,8 @@ int tb_tp_allreduce_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t
 int tb_tp_argmax_merge_impl(tb_ctx* ctx, char* const* arenas, int P, int r, int64_t n, int rows, uint32_t* ids,
                             int32_t* pos);
 
-// prefill GEMM Y (+)= f16(X) . f16(deq(W))^T on tcgen05 (M % 128, N % 256, K % 64)
+// prefill GEMM Y (+)= f16(X) . f16(deq(W))^T on tcgen05 (M % 128, N % 256, K % 64);
+// X's f16 copy and any split-K partials live in context scratch
 int tb_gemm_int4_impl(tb_ctx* ctx, float* y, const void* x, int x_bf16, const uint32_t* pack, const uint16_t* scales,
                       int64_t M, int64_t N, int64_t K, int acc);
 // the same GEMM for ternary weights (WebGPU layout) against QUANTQ8T int8 rows
